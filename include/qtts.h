@@ -1,0 +1,164 @@
+/*
+ * qtts.h -- C ABI of the B200-native QORA-TTS 1.7B decode loop
+ * (libqtts_b200.so).
+ *
+ * Every entry point returns an int status (QTTS_OK = 0, negative = error;
+ * qtts_last_error() gives the message of the calling thread's last failure).
+ * Host buffers are caller-owned; pointers named *_dev are device pointers.
+ * A model is read-only and may be shared across threads; a session belongs to
+ * one thread at a time.  Reference citations are paths inside the qora-tts
+ * crate (src/...), the Rust functions each entry point replaces.
+ */
+#ifndef QTTS_H
+#define QTTS_H
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define QTTS_API __attribute__((visibility("default")))
+#else
+#define QTTS_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QTTS_OK 0
+#define QTTS_ERR_BADARG (-1)
+#define QTTS_ERR_OOM (-2)
+#define QTTS_ERR_CUDA (-3)
+#define QTTS_ERR_TIMEOUT (-4)
+#define QTTS_ERR_FORMAT (-5)
+#define QTTS_ERR_IO (-6)
+#define QTTS_ERR_STATE (-7)
+#define QTTS_ERR_NODEV (-8)
+#define QTTS_ERR_RANGE (-9)
+
+typedef struct qtts_model qtts_model;
+typedef struct qtts_session qtts_session;
+
+/* Model dimensions as stored in the .qora-tts headers (save.rs:49-59,92-97). */
+typedef struct {
+  int t_layers, t_hidden, t_text_hidden, t_heads, t_kv_heads, t_head_dim;
+  int t_inter, t_vocab, t_text_vocab, t_max_pos;
+  int t_sec[3];
+  int p_layers, p_hidden, p_heads, p_kv_heads, p_head_dim, p_inter, p_vocab;
+  int p_groups, p_max_pos;
+  int fmt; /* save.rs:34 format_id: 1 = Q4, 0 = F16 */
+} qtts_dims;
+
+/* generate_new.rs:38-45 TTSParams (max_codes is a qtts_generate argument). */
+typedef struct {
+  float temperature;
+  int top_k;
+  float repetition_penalty;
+  uint32_t codec_eos_id;
+} qtts_sample_params;
+
+/* One utterance of generate_new.rs:191-202 generate_speech, after
+ * tokenization (tokenizer.rs:16 is out of scope: callers pass token ids). */
+typedef struct {
+  const uint32_t* text; /* token ids */
+  int n_text;
+  uint32_t speaker_id;
+  uint32_t language_id;
+  const float* voice; /* nullable: 2048-d speaker embedding (main.rs:209-217) */
+  uint64_t seed;      /* xorshift64 state, generate_new.rs:233 */
+  qtts_sample_params params;
+} qtts_utterance;
+
+/* qtts_generate flags */
+#define QTTS_IGNORE_EOS 1u /* run all max_frames (benchmarks with random weights) */
+
+QTTS_API const char* qtts_last_error(void);
+QTTS_API int qtts_version(void);
+
+/* ---- .qora-tts file (host only; no GPU needed) ---------------------------- */
+/* Parse and validate the talker + predictor sections: save.rs:262-409. */
+QTTS_API int qtts_file_probe(const char* path, qtts_dims* out);
+/* Write a seeded synthetic model in the save.rs:23-137 byte layout (talker,
+ * predictor and an empty decoder section): Q4 bytes uniform, scales
+ * f16(|N(0,0.02)|), norms 1, biases N(0,0.02), RoPE tables per rope.rs:11-41
+ * and loader.rs:399-408.  Replaces offline compress_model.rs:35-82. */
+QTTS_API int qtts_synth_write(const char* path, const qtts_dims* dims, uint64_t seed);
+QTTS_API void qtts_dims_1p7b(qtts_dims* out);
+QTTS_API void qtts_dims_tiny(qtts_dims* out);
+
+/* ---- model ------------------------------------------------------------------ */
+/* save.rs:262 load_model + one upload to HBM in the on-disk layout. */
+QTTS_API int qtts_model_load(const char* path, int device, qtts_model** out);
+QTTS_API int qtts_model_free(qtts_model* m);
+QTTS_API int qtts_model_dims(const qtts_model* m, qtts_dims* out);
+QTTS_API size_t qtts_model_device_bytes(const qtts_model* m);
+
+/* ---- session: device KV caches + activations for up to max_batch utterances */
+/* gemv.rs:79-86 empty_kv_cache, as paged device KV (16 positions / page). */
+QTTS_API int qtts_session_create(qtts_model* m, int max_batch, int max_positions, qtts_session** out);
+QTTS_API int qtts_session_free(qtts_session* s);
+QTTS_API int qtts_session_reset(qtts_session* s);
+QTTS_API void* qtts_session_stream(qtts_session* s); /* cudaStream_t the session launches on */
+
+/* ---- per-call reference API (slot 0 of the session, batch 1) ------------- */
+QTTS_API int qtts_embed_text(qtts_session* s, uint32_t token, float* out);  /* talker.rs:105 */
+QTTS_API int qtts_embed_codec(qtts_session* s, uint32_t token, float* out); /* talker.rs:152 */
+/* talker.rs:364-462 prefill_talker_raw (+ talker.rs:627 apply_codec_head):
+ * emb [n][H] host; hidden_out [H], logits_out [V] (either may be NULL). */
+QTTS_API int qtts_prefill(qtts_session* s, const float* emb, int n, float* hidden_out, float* logits_out);
+/* talker.rs:263-360 forward_with_embedding: out = normed hidden [H] ++ logits [V]. */
+QTTS_API int qtts_talker_step(qtts_session* s, const float* emb, int position, float* out);
+/* code_predictor.rs:218-273 generate_acoustic_codes -> codes[p_groups]. */
+QTTS_API int qtts_predict_acoustic(qtts_session* s, const float* talker_hidden, const float* semantic_embed,
+                          uint32_t* codes);
+/* code_predictor.rs:280-293 get_acoustic_embeddings_sum. */
+QTTS_API int qtts_acoustic_embed_sum(qtts_session* s, const uint32_t* codes, float* out);
+/* generate_new.rs:329-391 sample_token on the GPU (bit-exact given the same
+ * logits and rng state); *rng is advanced as the reference advances it. */
+QTTS_API int qtts_sample(qtts_session* s, const float* logits, int n, const qtts_sample_params* p,
+                const uint32_t* prev16, uint64_t* rng, uint32_t* out);
+
+/* ---- batched generation (generate_new.rs:191-300 frame loop, one CUDA graph
+ * per frame for all utterances) ------------------------------------------- */
+/* forced: nullable [n_utt][max_frames][16] teacher-forcing codes (they drive
+ * the next steps; the GPU's own choices are still written to codes_out).
+ * codes_out [n_utt][max_frames][16]; frames_out [n_utt]; logits_dump
+ * nullable [n_utt][max_frames][V]; hidden_dump nullable [n_utt][max_frames][H]. */
+QTTS_API int qtts_generate(qtts_session* s, int n_utt, const qtts_utterance* utts, int max_frames,
+                  unsigned flags, const uint32_t* forced, uint32_t* codes_out, int* frames_out,
+                  float* logits_dump, float* hidden_dump);
+/* The same loop split in three for timing: begin = prefill + trailing text;
+ * frames = n_frames graph replays (asynchronous on the session stream);
+ * end = wait and copy results out. */
+QTTS_API int qtts_generate_begin(qtts_session* s, int n_utt, const qtts_utterance* utts, int max_frames,
+                        unsigned flags, const uint32_t* forced);
+QTTS_API int qtts_generate_frames(qtts_session* s, int n_frames);
+QTTS_API int qtts_generate_end(qtts_session* s, uint32_t* codes_out, int* frames_out, float* logits_dump,
+                      float* hidden_dump);
+/* Number of kernels one frame launches (CUDA-graph nodes). */
+QTTS_API int qtts_frame_kernel_count(qtts_session* s);
+
+/* ---- kernels on device pointers (gemv.rs:149 gemv / :157 gemm) ------------ */
+/* y[m][n] = sum_k x[m][k] * W[k][n] for a Q4 g32 weight in the on-disk
+ * [k][n] layout (packed k*n/2 bytes, low nibble = even column; scales
+ * k*n/32 f16).  scratch_dev: split-K partials, qtts_q4_gemv_scratch_bytes(). */
+QTTS_API size_t qtts_q4_gemv_scratch_bytes(int k, int n, int m);
+QTTS_API int qtts_q4_gemv_dev(const uint8_t* packed_dev, const uint16_t* scales_dev, int k, int n,
+                     const float* x_dev, int m, float* y_dev, void* scratch_dev,
+                     size_t scratch_bytes, void* stream);
+/* Same contract with host buffers (copies in, runs, copies out). */
+QTTS_API int qtts_q4_gemv(const uint8_t* packed, const uint16_t* scales, int k, int n, const float* x,
+                 int m, float* y);
+/* The exp the code-0 sampler uses (Rust f32::exp at generate_new.rs:355,
+ * i.e. glibc expf), element-wise on device pointers, for validation. */
+QTTS_API int qtts_expf_dev(const float* x_dev, float* y_dev, int n, void* stream);
+/* gemv.rs:183-196 gemv_f16 on device pointers. */
+QTTS_API int qtts_f16_gemv_dev(const uint16_t* w_dev, int k, int n, const float* x_dev, int m, float* y_dev,
+                      void* stream);
+/* gemv.rs:378-400 dequant of the whole matrix: out[k][n] = f32(scale)*(q-8). */
+QTTS_API int qtts_q4_dequant_dev(const uint8_t* packed_dev, const uint16_t* scales_dev, int k, int n,
+                        float* out_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

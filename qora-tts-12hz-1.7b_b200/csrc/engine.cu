@@ -1,0 +1,1154 @@
+// engine.cu -- model upload, sessions, launch plans and the C ABI.
+//
+// The reference decode loop (generate_new.rs:242-300) is expressed as a list
+// of kernel launches per frame, built once per generation and captured into a
+// CUDA graph; every per-frame quantity (positions, frame index, codes, rng)
+// lives in device memory, so the graph replays unchanged frame after frame
+// with no host round trip.
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <algorithm>
+#include <cmath>
+#include <string>
+#include <vector>
+
+#include "engine.h"
+
+namespace qtts {
+
+static thread_local std::string g_err;
+void set_error(const std::string& msg) { g_err = msg; }
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+#define CK(call)                                                                          \
+  do {                                                                                    \
+    cudaError_t e_ = (call);                                                              \
+    if (e_ != cudaSuccess) return fail(QTTS_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+#define RC(call)                  \
+  do {                            \
+    int r_ = (call);              \
+    if (r_ != QTTS_OK) return r_; \
+  } while (0)
+
+static inline int ceil_div(long a, long b) { return (int)((a + b - 1) / b); }
+
+// generate_new.rs:25-36 token constants
+enum : uint32_t {
+  IM_START = 151644, ASSISTANT = 77091, NEWLINE = 198, TTS_PAD = 151671, TTS_BOS = 151672,
+  TTS_EOS = 151673, CODEC_THINK = 2154, CODEC_THINK_BOS = 2156, CODEC_THINK_EOS = 2157,
+  CODEC_PAD = 2148, CODEC_BOS = 2149
+};
+
+// ---------------------------------------------------------------------------
+// model upload (save.rs:262-409 -> HBM)
+// ---------------------------------------------------------------------------
+namespace {
+struct Piece {
+  uint64_t file_off, bytes;
+  size_t dev_off;
+};
+struct Layout {
+  size_t total = 0;
+  std::vector<Piece> pieces;
+  size_t add(uint64_t file_off, uint64_t bytes) {
+    const size_t at = total;
+    pieces.push_back({file_off, bytes, at});
+    total += (bytes + 255) & ~(size_t)255;
+    return at;
+  }
+};
+struct WOff {
+  size_t a, b;
+  int k, n;
+};
+WOff lay_w(Layout& L, const HWeight& w) { return {L.add(w.off_a, w.bytes_a), L.add(w.off_b, w.bytes_b), (int)w.k, (int)w.n}; }
+size_t lay_v(Layout& L, const HVec& v) { return L.add(v.off, v.bytes); }
+Q4Mat mk(char* base, const WOff& o) {
+  Q4Mat q;
+  q.packed = reinterpret_cast<const uint8_t*>(base + o.a);
+  q.scales = reinterpret_cast<const __half*>(base + o.b);
+  q.k = o.k;
+  q.n = o.n;
+  return q;
+}
+struct LOff {
+  WOff q, k, v, o, gate, up, down;
+  size_t qn, kn, in, post;
+};
+LOff lay_layer(Layout& L, const HLayer& h) {
+  LOff o;
+  o.q = lay_w(L, h.q); o.k = lay_w(L, h.k); o.v = lay_w(L, h.v); o.o = lay_w(L, h.o);
+  o.qn = lay_v(L, h.q_norm); o.kn = lay_v(L, h.k_norm);
+  o.gate = lay_w(L, h.gate); o.up = lay_w(L, h.up); o.down = lay_w(L, h.down);
+  o.in = lay_v(L, h.in_norm); o.post = lay_v(L, h.post_norm);
+  return o;
+}
+DLayer mk_layer(char* base, const LOff& o) {
+  DLayer d;
+  d.q = mk(base, o.q); d.k = mk(base, o.k); d.v = mk(base, o.v); d.o = mk(base, o.o);
+  d.gate = mk(base, o.gate); d.up = mk(base, o.up); d.down = mk(base, o.down);
+  d.q_norm = reinterpret_cast<const __half*>(base + o.qn);
+  d.k_norm = reinterpret_cast<const __half*>(base + o.kn);
+  d.in_norm = reinterpret_cast<const __half*>(base + o.in);
+  d.post_norm = reinterpret_cast<const __half*>(base + o.post);
+  return d;
+}
+}  // namespace
+
+void gemv_init_attributes();
+
+static int model_load(const char* path, int device, Model** out) {
+  HModel hm;
+  std::string err;
+  int rc = parse_model(path, &hm, &err);
+  if (rc != QTTS_OK) return fail(rc, err);
+  if (hm.d.fmt != 1) return fail(QTTS_ERR_FORMAT, "the GPU decode path needs a Q4 model file (format_id 1)");
+  if (!hm.has_proj) return fail(QTTS_ERR_FORMAT, "models without predictor input_proj (0.6B) are not supported");
+  const qtts_dims& d = hm.d;
+  if (d.t_head_dim != kHeadDim || d.p_head_dim != kHeadDim) return fail(QTTS_ERR_FORMAT, "head_dim must be 128");
+  if (d.p_groups + 1 > kMaxGroups || d.t_vocab > 4096) return fail(QTTS_ERR_FORMAT, "unsupported vocabulary / group count");
+  int ndev = 0;
+  CK(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return fail(QTTS_ERR_NODEV, "no such CUDA device");
+  CK(cudaSetDevice(device));
+  Layout L;
+  std::vector<LOff> tl, pl;
+  for (auto& h : hm.tl) tl.push_back(lay_layer(L, h));
+  const WOff codec_emb = lay_w(L, hm.codec_emb), text_emb = lay_w(L, hm.text_emb), fc1 = lay_w(L, hm.fc1);
+  const size_t fc1_b = lay_v(L, hm.fc1_b);
+  const WOff fc2 = lay_w(L, hm.fc2);
+  const size_t fc2_b = lay_v(L, hm.fc2_b);
+  const WOff codec_head = lay_w(L, hm.codec_head);
+  const size_t t_final = lay_v(L, hm.t_final), t_cos = lay_v(L, hm.t_cos), t_sin = lay_v(L, hm.t_sin);
+  const WOff input_proj = lay_w(L, hm.input_proj);
+  const size_t input_proj_b = lay_v(L, hm.input_proj_b);
+  std::vector<WOff> pe, lm;
+  for (auto& w : hm.p_emb) pe.push_back(lay_w(L, w));
+  for (auto& h : hm.pl) pl.push_back(lay_layer(L, h));
+  for (auto& w : hm.lm) lm.push_back(lay_w(L, w));
+  const size_t p_final = lay_v(L, hm.p_final), p_cos = lay_v(L, hm.p_cos), p_sin = lay_v(L, hm.p_sin);
+
+  Model* m = new Model();
+  m->d = d;
+  m->device = device;
+  CK(cudaDeviceGetAttribute(&m->sm_count, cudaDevAttrMultiProcessorCount, device));
+  m->bytes = L.total;
+  if (cudaMalloc(&m->arena, L.total) != cudaSuccess) {
+    delete m;
+    return fail(QTTS_ERR_OOM, "cannot allocate the weight arena");
+  }
+  // stream payloads file -> pinned staging -> HBM (double-buffered)
+  FILE* f = fopen(path, "rb");
+  const size_t chunk = 64u << 20;
+  void* stage[2] = {nullptr, nullptr};
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  cudaStream_t st = nullptr;
+  bool ok = f != nullptr;
+  ok = ok && cudaMallocHost(&stage[0], chunk) == cudaSuccess && cudaMallocHost(&stage[1], chunk) == cudaSuccess;
+  ok = ok && cudaEventCreateWithFlags(&ev[0], cudaEventDisableTiming) == cudaSuccess &&
+       cudaEventCreateWithFlags(&ev[1], cudaEventDisableTiming) == cudaSuccess;
+  ok = ok && cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) == cudaSuccess;
+  int cur = 0;
+  bool used[2] = {false, false};
+  for (size_t i = 0; ok && i < L.pieces.size(); ++i) {
+    const Piece& p = L.pieces[i];
+    uint64_t done = 0;
+    if (fseeko(f, (off_t)p.file_off, SEEK_SET) != 0) ok = false;
+    while (ok && done < p.bytes) {
+      const size_t nb = (size_t)std::min<uint64_t>(chunk, p.bytes - done);
+      if (used[cur]) ok = cudaEventSynchronize(ev[cur]) == cudaSuccess;
+      if (!ok) break;
+      if (fread(stage[cur], 1, nb, f) != nb) { ok = false; break; }
+      ok = cudaMemcpyAsync(m->arena + p.dev_off + done, stage[cur], nb, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+           cudaEventRecord(ev[cur], st) == cudaSuccess;
+      used[cur] = true;
+      done += nb;
+      cur ^= 1;
+    }
+  }
+  if (st) ok = (cudaStreamSynchronize(st) == cudaSuccess) && ok;
+  if (f) fclose(f);
+  for (int i = 0; i < 2; ++i) {
+    if (stage[i]) cudaFreeHost(stage[i]);
+    if (ev[i]) cudaEventDestroy(ev[i]);
+  }
+  if (st) cudaStreamDestroy(st);
+  if (!ok) {
+    cudaFree(m->arena);
+    delete m;
+    return fail(QTTS_ERR_IO, "failed to stream the weights to the device");
+  }
+  char* b = m->arena;
+  for (auto& o : tl) m->tl.push_back(mk_layer(b, o));
+  for (auto& o : pl) m->pl.push_back(mk_layer(b, o));
+  m->codec_emb = mk(b, codec_emb); m->text_emb = mk(b, text_emb); m->fc1 = mk(b, fc1); m->fc2 = mk(b, fc2);
+  m->codec_head = mk(b, codec_head); m->input_proj = mk(b, input_proj);
+  m->fc1_b = reinterpret_cast<const float*>(b + fc1_b);
+  m->fc2_b = reinterpret_cast<const float*>(b + fc2_b);
+  m->input_proj_b = reinterpret_cast<const float*>(b + input_proj_b);
+  m->t_cos = reinterpret_cast<const float*>(b + t_cos);
+  m->t_sin = reinterpret_cast<const float*>(b + t_sin);
+  m->p_cos = reinterpret_cast<const float*>(b + p_cos);
+  m->p_sin = reinterpret_cast<const float*>(b + p_sin);
+  m->t_final = reinterpret_cast<const __half*>(b + t_final);
+  m->p_final = reinterpret_cast<const __half*>(b + p_final);
+  for (auto& o : pe) m->p_emb.push_back(mk(b, o));
+  for (auto& o : lm) m->lm.push_back(mk(b, o));
+  m->has_proj = hm.has_proj;
+  if (cudaMalloc(&m->d_group_emb, sizeof(Q4Mat) * m->p_emb.size()) != cudaSuccess ||
+      cudaMemcpy(m->d_group_emb, m->p_emb.data(), sizeof(Q4Mat) * m->p_emb.size(), cudaMemcpyHostToDevice) !=
+          cudaSuccess) {
+    cudaFree(m->arena);
+    delete m;
+    return fail(QTTS_ERR_CUDA, "cannot upload the embedding table list");
+  }
+  gemv_init_attributes();
+  *out = m;
+  return QTTS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// launch planning
+// ---------------------------------------------------------------------------
+static GemvDesc gemv_base(int epi, std::initializer_list<Q4Mat> mats, bool paired, int M) {
+  GemvDesc g;
+  g.epi_kind = epi;
+  g.nmat = (int)mats.size();
+  g.paired = paired ? 1 : 0;
+  int tiles = 0, cols = 0, i = 0;
+  for (const Q4Mat& q : mats) {
+    g.mat[i] = q;
+    g.tile0[i] = tiles;
+    g.col0[i] = cols;
+    if (!paired) tiles += ceil_div(q.n, kTileN);
+    cols += q.n;
+    ++i;
+  }
+  if (paired) tiles = ceil_div(g.mat[0].n, kTileN);
+  g.tile0[g.nmat] = tiles;
+  g.ntiles = tiles;
+  g.ncols = cols;
+  g.k = g.mat[0].k;
+  g.M = M;
+  return g;
+}
+
+// Split-K choice: about two CTAs per SM, slices of whole 32-row blocks, at
+// most 2048 rows per slice (shared-memory bound of the input slice).
+static void choose_split(int sm_count, GemvDesc& g) {
+  g.mb = g.paired ? (g.M >= 2 ? 2 : 1) : (g.M >= 3 ? 4 : (g.M == 2 ? 2 : 1));
+  const int zb = ceil_div(g.M, g.mb);
+  const int target = 2 * sm_count;
+  int S = (int)std::lround((double)target / (double)(g.ntiles * zb));
+  S = std::max(1, std::min(S, ceil_div(g.k, 32)));
+  int rps = ceil_div(ceil_div(g.k, S), 32) * 32;
+  rps = std::min(rps, 2048);
+  g.rows_per_split = rps;
+  g.S = ceil_div(g.k, rps);
+}
+
+static int plan_gemv(Session& s, GemvDesc& g) {
+  choose_split(s.m->sm_count, g);
+  while (g.S > 1 && (size_t)g.S * g.M * g.ncols > s.part_floats) {
+    g.rows_per_split = std::min(2048, g.rows_per_split * 2);
+    const int S2 = ceil_div(g.k, g.rows_per_split);
+    if (S2 == g.S) break;
+    g.S = S2;
+  }
+  if (g.S > 1) {
+    if ((size_t)g.S * g.M * g.ncols > s.part_floats) return fail(QTTS_ERR_OOM, "split-K scratch too small");
+    g.part = s.part;
+  }
+  const size_t zb = (size_t)ceil_div(g.M, g.mb);
+  if ((size_t)g.ntiles * zb > s.n_counters || zb > 4096) return fail(QTTS_ERR_OOM, "tile counter array too small");
+  g.counters = s.counters;
+  if (g.epi_kind == EPI_ARGMAX) {
+    g.epi.counters2 = s.counters2;
+    g.epi.keys = s.keys;
+  }
+  return QTTS_OK;
+}
+
+static Op gemv_op(const GemvDesc& g, const FrameCodes& fc = FrameCodes{}) {
+  return [g, fc](cudaStream_t st) { return launch_gemv(g, fc, st); };
+}
+
+struct LayerIO {
+  float* X = nullptr;
+  long ldx = 0;
+  int M = 0;
+  RowPos rp;
+  KvDesc kv;
+  const float *cos = nullptr, *sin = nullptr;
+  int rope_rows = 0, skip_oob = 0;
+  int heads = 0, kvh = 0, inter = 0;
+  int nsplit = 1;
+};
+
+// One transformer layer (talker.rs:279-349 / code_predictor.rs:448-502):
+// RMSNorm+QKV+QK-norm+RoPE+KV append | attention | O+residual |
+// RMSNorm+gate/up+SwiGLU | down+residual.
+static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const LayerIO& io) {
+  const int qd = io.heads * kHeadDim;
+  GemvDesc g = gemv_base(EPI_QKV, {L.q, L.k, L.v}, false, io.M);
+  g.X = io.X; g.ldx = io.ldx; g.gamma = L.in_norm;
+  g.epi.q_out = s.q; g.epi.ldq = qd; g.epi.q_norm = L.q_norm; g.epi.k_norm = L.k_norm;
+  g.epi.rope_cos = io.cos; g.epi.rope_sin = io.sin; g.epi.rope_rows = io.rope_rows; g.epi.rope_skip_oob = io.skip_oob;
+  g.epi.heads = io.heads; g.epi.kv_heads = io.kvh; g.epi.kv = io.kv; g.epi.rp = io.rp; g.epi.err_flag = s.err_flag;
+  RC(plan_gemv(s, g));
+  ops.push_back(gemv_op(g));
+
+  AttnDesc a;
+  a.q = s.q; a.ldq = qd; a.out = s.attn; a.ldo = qd; a.kv = io.kv; a.rp = io.rp;
+  a.heads = io.heads; a.kv_heads = io.kvh; a.M = io.M; a.nsplit = io.nsplit;
+  if (a.nsplit > 1) {
+    const size_t need = (size_t)io.M * io.kvh * a.nsplit * (io.heads / io.kvh) * (2 + kHeadDim);
+    if (need > s.apart_floats || (size_t)io.M * io.kvh > s.n_acounters)
+      return fail(QTTS_ERR_OOM, "attention split scratch too small");
+    a.part = s.apart;
+    a.counters = s.acounters;
+  }
+  ops.push_back([a](cudaStream_t st) { return launch_attention(a, st); });
+
+  GemvDesc o = gemv_base(EPI_RESID, {L.o}, false, io.M);
+  o.X = s.attn; o.ldx = qd; o.epi.out = io.X; o.epi.ldo = io.ldx;
+  RC(plan_gemv(s, o));
+  ops.push_back(gemv_op(o));
+
+  GemvDesc gu = gemv_base(EPI_SWIGLU, {L.gate, L.up}, true, io.M);
+  gu.X = io.X; gu.ldx = io.ldx; gu.gamma = L.post_norm; gu.epi.out = s.h; gu.epi.ldo = io.inter;
+  RC(plan_gemv(s, gu));
+  ops.push_back(gemv_op(gu));
+
+  GemvDesc dn = gemv_base(EPI_RESID, {L.down}, false, io.M);
+  dn.X = s.h; dn.ldx = io.inter; dn.epi.out = io.X; dn.epi.ldo = io.ldx;
+  RC(plan_gemv(s, dn));
+  ops.push_back(gemv_op(dn));
+  return QTTS_OK;
+}
+
+static KvDesc talker_kv(Session& s, int layer) {
+  KvDesc k;
+  k.pool = s.kv_pool; k.page_table = s.page_table; k.pages_per_sess = s.pages_per_sess;
+  k.n_layers = s.m->d.t_layers; k.kv_heads = s.m->d.t_kv_heads; k.layer = layer;
+  return k;
+}
+static KvDesc pred_kv(Session& s, int layer) {
+  KvDesc k;
+  k.pool = s.pkv_pool; k.page_table = nullptr; k.pages_per_sess = 1;
+  k.n_layers = s.m->d.p_layers; k.kv_heads = s.m->d.p_kv_heads; k.layer = layer;
+  return k;
+}
+static int talker_nsplit(Session& s, int M) {
+  const int byL = ceil_div(s.maxP, 64);
+  const int byPar = std::max(1, ceil_div(4L * s.m->sm_count, (long)M * s.m->d.t_kv_heads));
+  return std::max(1, std::min(32, std::min(byL, byPar)));
+}
+
+// Talker layers over rows X (decode: one row per session; prefill: seq rows).
+static int add_talker(Session& s, std::vector<Op>& ops, float* X, long ldx, int M, const RowPos& rp, int nsplit) {
+  const Model& m = *s.m;
+  for (int l = 0; l < m.d.t_layers; ++l) {
+    LayerIO io;
+    io.X = X; io.ldx = ldx; io.M = M; io.rp = rp; io.kv = talker_kv(s, l);
+    io.cos = m.t_cos; io.sin = m.t_sin; io.rope_rows = m.d.t_max_pos; io.skip_oob = 0;
+    io.heads = m.d.t_heads; io.kvh = m.d.t_kv_heads; io.inter = m.d.t_inter; io.nsplit = nsplit;
+    RC(add_layer(s, ops, m.tl[l], io));
+  }
+  return QTTS_OK;
+}
+
+// final norm + codec_head (talker.rs:353-354): logits and the normed hidden.
+static int add_codec_head(Session& s, std::vector<Op>& ops, const float* X, long ldx, int M, float* logits,
+                          float* hid, long ldh) {
+  GemvDesc g = gemv_base(EPI_STORE, {s.m->codec_head}, false, M);
+  g.X = X; g.ldx = ldx; g.gamma = s.m->t_final;
+  g.epi.out = logits; g.epi.ldo = s.m->d.t_vocab;
+  g.xnorm_out = hid; g.ld_xnorm = ldh;
+  RC(plan_gemv(s, g));
+  ops.push_back(gemv_op(g));
+  return QTTS_OK;
+}
+
+// Predictor expansion for B sessions (code_predictor.rs:218-273).  Inputs:
+// s.pin rows (2b = talker hidden, 2b+1 = semantic embedding).  Codes go
+// through FrameCodes (generation) or s.codes_plain (per-call API).
+static int add_predictor(Session& s, std::vector<Op>& ops, int B, bool frame_mode, const FrameCodes& fc) {
+  const Model& m = *s.m;
+  const qtts_dims& d = m.d;
+  const int pH = d.p_hidden;
+  // project_input of both prefill rows (code_predictor.rs:235-236)
+  GemvDesc pj = gemv_base(EPI_STORE, {m.input_proj}, false, 2 * B);
+  pj.X = s.pin; pj.ldx = d.t_hidden; pj.epi.out = s.px; pj.epi.ldo = pH; pj.epi.bias = m.input_proj_b;
+  RC(plan_gemv(s, pj));
+  ops.push_back(gemv_op(pj));
+  auto layers = [&](float* X, int M, const RowPos& rp) -> int {
+    for (int l = 0; l < d.p_layers; ++l) {
+      LayerIO io;
+      io.X = X; io.ldx = pH; io.M = M; io.rp = rp; io.kv = pred_kv(s, l);
+      io.cos = m.p_cos; io.sin = m.p_sin; io.rope_rows = d.p_max_pos; io.skip_oob = 1;
+      io.heads = d.p_heads; io.kvh = d.p_kv_heads; io.inter = d.p_inter; io.nsplit = 1;
+      RC(add_layer(s, ops, m.pl[l], io));
+    }
+    return QTTS_OK;
+  };
+  RowPos rp0;
+  rp0.rows_per_sess = 2;  // prefill positions 0, 1 (code_predictor.rs:244, :369)
+  RC(layers(s.px, 2 * B, rp0));
+  auto head = [&](const float* X, long ldx, int g) -> int {  // final norm + lm_heads[g] + argmax
+    GemvDesc h = gemv_base(EPI_ARGMAX, {m.lm[g]}, false, B);
+    h.X = X; h.ldx = ldx; h.gamma = m.p_final;
+    h.epi.group = g + 1; h.epi.frame_codes = frame_mode ? 1 : 0; h.epi.codes_plain = s.codes_plain;
+    RC(plan_gemv(s, h));
+    ops.push_back(gemv_op(h, fc));
+    return QTTS_OK;
+  };
+  RC(head(s.px + pH, 2L * pH, 0));
+  for (int g = 1; g < d.p_groups; ++g) {  // code_predictor.rs:253-270
+    GemvDesc pe = gemv_base(EPI_STORE, {m.input_proj}, false, B);
+    pe.emb = m.p_emb[g - 1];
+    if (frame_mode) {
+      pe.emb_idx = &s.slots[0].cur[g];
+      pe.emb_idx_stride = (int)(sizeof(SlotState) / sizeof(uint32_t));
+    } else {
+      pe.emb_idx = s.codes_plain + g;
+      pe.emb_idx_stride = kMaxGroups;
+    }
+    pe.epi.out = s.px1; pe.epi.ldo = pH; pe.epi.bias = m.input_proj_b;
+    RC(plan_gemv(s, pe));
+    ops.push_back(gemv_op(pe));
+    RowPos rp;
+    rp.pos_const = g + 1;
+    RC(layers(s.px1, B, rp));
+    RC(head(s.px1, pH, g));
+  }
+  return QTTS_OK;
+}
+
+// embed_text_token for rows of token ids (talker.rs:105-116):
+// fc1(emb) + b1 -> silu -> fc2 + b2.
+static int add_text_proj(Session& s, std::vector<Op>& ops, const uint32_t* tok_dev, int n, float* h1, float* out,
+                         long ldo) {
+  const Model& m = *s.m;
+  GemvDesc g1 = gemv_base(EPI_STORE, {m.fc1}, false, n);
+  g1.emb = m.text_emb; g1.emb_idx = tok_dev; g1.emb_idx_stride = 1;
+  g1.epi.out = h1; g1.epi.ldo = m.fc1.n; g1.epi.bias = m.fc1_b; g1.epi.act_silu = 1;
+  RC(plan_gemv(s, g1));
+  ops.push_back(gemv_op(g1));
+  GemvDesc g2 = gemv_base(EPI_STORE, {m.fc2}, false, n);
+  g2.X = h1; g2.ldx = m.fc1.n;
+  g2.epi.out = out; g2.epi.ldo = ldo; g2.epi.bias = m.fc2_b;
+  RC(plan_gemv(s, g2));
+  ops.push_back(gemv_op(g2));
+  return QTTS_OK;
+}
+
+static int run_ops(Session& s, const std::vector<Op>& ops) {
+  for (const Op& op : ops) {
+    const cudaError_t e = op(s.st);
+    if (e != cudaSuccess) return fail(QTTS_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
+  }
+  return QTTS_OK;
+}
+static int sync_check(Session& s) {
+  CK(cudaStreamSynchronize(s.st));
+  int flag = 0;
+  CK(cudaMemcpy(&flag, s.err_flag, sizeof(int), cudaMemcpyDeviceToHost));
+  if (flag) {
+    CK(cudaMemset(s.err_flag, 0, sizeof(int)));
+    return fail(QTTS_ERR_RANGE, "position beyond the talker RoPE table (rope.rs:73 would panic)");
+  }
+  return QTTS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// sessions
+// ---------------------------------------------------------------------------
+template <class T>
+static int dalloc(T** p, size_t count, std::vector<void*>* track = nullptr) {
+  if (count == 0) count = 1;
+  if (cudaMalloc(reinterpret_cast<void**>(p), sizeof(T) * count) != cudaSuccess)
+    return fail(QTTS_ERR_OOM, "device allocation failed");
+  if (cudaMemset(*p, 0, sizeof(T) * count) != cudaSuccess) return fail(QTTS_ERR_CUDA, "cudaMemset failed");
+  if (track) track->push_back(*p);
+  return QTTS_OK;
+}
+
+static void free_generation(Session& s) {
+  if (s.graph_exec) cudaGraphExecDestroy(s.graph_exec);
+  if (s.graph) cudaGraphDestroy(s.graph);
+  s.graph_exec = nullptr;
+  s.graph = nullptr;
+  for (void* p : s.gen_allocs) cudaFree(p);
+  s.gen_allocs.clear();
+  s.codes = nullptr; s.forced = nullptr; s.trail = nullptr; s.tts_pad = nullptr; s.tp = nullptr; s.tp_h1 = nullptr;
+  s.tp_tok = nullptr; s.recipes = nullptr; s.trail_idx = nullptr; s.voices = nullptr;
+  s.dump_logits = nullptr; s.dump_hidden = nullptr;
+  s.generating = false;
+  s.frame_kernels = 0;
+}
+
+static void session_free_all(Session* s) {
+  if (!s) return;
+  cudaSetDevice(s->m->device);
+  if (s->st) cudaStreamSynchronize(s->st);
+  free_generation(*s);
+  void* bufs[] = {s->kv_pool, s->page_table, s->pkv_pool, s->slots, s->x, s->pin, s->q, s->attn, s->h,
+                  s->px, s->px1, s->logits, s->xpre, s->hid1, s->part, s->counters, s->counters2, s->keys,
+                  s->apart, s->acounters, s->err_flag, s->codes_plain, s->io};
+  for (void* p : bufs)
+    if (p) cudaFree(p);
+  if (s->st) cudaStreamDestroy(s->st);
+  delete s;
+}
+
+static int session_create(Model* m, int maxB, int maxP, Session** out) {
+  if (!m || maxB <= 0 || maxB > 4096 || maxP <= 0) return fail(QTTS_ERR_BADARG, "bad session arguments");
+  if (maxP > m->d.t_max_pos) return fail(QTTS_ERR_RANGE, "max_positions exceeds the talker RoPE table");
+  CK(cudaSetDevice(m->device));
+  const qtts_dims& d = m->d;
+  Session* s = new Session();
+  s->m = m;
+  s->maxB = maxB;
+  s->maxP = maxP;
+  s->pages_per_sess = ceil_div(maxP, kPageSize);
+  int rc = QTTS_OK;
+  auto A = [&](auto** p, size_t n) {
+    if (rc == QTTS_OK) rc = dalloc(p, n);
+  };
+  if (cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking) != cudaSuccess) rc = fail(QTTS_ERR_CUDA, "stream");
+  const size_t tpage = (size_t)d.t_layers * 2 * d.t_kv_heads * kPageSize * kHeadDim;
+  const size_t ppage = (size_t)d.p_layers * 2 * d.p_kv_heads * kPageSize * kHeadDim;
+  A(&s->kv_pool, tpage * maxB * s->pages_per_sess);
+  A(&s->page_table, (size_t)maxB * s->pages_per_sess);
+  A(&s->pkv_pool, ppage * maxB);
+  A(&s->slots, (size_t)maxB);
+  s->rows = 10 * maxB;
+  const int qmax = std::max(d.t_heads, d.p_heads) * kHeadDim;
+  const int imax = std::max(d.t_inter, d.p_inter);
+  A(&s->x, (size_t)maxB * d.t_hidden);
+  A(&s->pin, (size_t)maxB * 2 * d.t_hidden);
+  A(&s->q, (size_t)s->rows * qmax);
+  A(&s->attn, (size_t)s->rows * qmax);
+  A(&s->h, (size_t)s->rows * imax);
+  A(&s->px, (size_t)2 * maxB * d.p_hidden);
+  A(&s->px1, (size_t)maxB * d.p_hidden);
+  A(&s->logits, (size_t)maxB * d.t_vocab);
+  A(&s->xpre, (size_t)s->rows * d.t_hidden);
+  A(&s->hid1, (size_t)maxB * d.t_hidden);
+  s->part_floats = (size_t)16 << 20;
+  A(&s->part, s->part_floats);
+  s->n_counters = 1 << 18;
+  A(&s->counters, s->n_counters);
+  A(&s->counters2, (size_t)4096);
+  A(&s->keys, (size_t)std::max(maxB * 10, 4096));
+  s->apart_floats = (size_t)8 << 20;
+  A(&s->apart, s->apart_floats);
+  s->n_acounters = (size_t)s->rows * std::max(d.t_kv_heads, d.p_kv_heads);
+  A(&s->acounters, s->n_acounters);
+  A(&s->err_flag, (size_t)1);
+  A(&s->codes_plain, (size_t)maxB * kMaxGroups);
+  s->io_floats = (size_t)s->rows * d.t_hidden + 2 * d.t_hidden + d.t_vocab + 64;
+  A(&s->io, s->io_floats);
+  if (rc == QTTS_OK) {  // pages: slot b owns pages [b*pps, (b+1)*pps)
+    std::vector<int> pt((size_t)maxB * s->pages_per_sess);
+    for (size_t i = 0; i < pt.size(); ++i) pt[i] = (int)i;
+    if (cudaMemcpy(s->page_table, pt.data(), sizeof(int) * pt.size(), cudaMemcpyHostToDevice) != cudaSuccess)
+      rc = fail(QTTS_ERR_CUDA, "page table upload");
+  }
+  if (rc != QTTS_OK) {
+    std::string msg = g_err;
+    session_free_all(s);
+    return fail(rc, msg);
+  }
+  *out = s;
+  return QTTS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// generation (generate_new.rs:191-300)
+// ---------------------------------------------------------------------------
+static int build_frame_ops(Session& s, std::vector<Op>& ops, bool dumps) {
+  const Model& m = *s.m;
+  const qtts_dims& d = m.d;
+  const int B = s.B, H = d.t_hidden, V = d.t_vocab;
+  FrameCodes fc;
+  fc.slots = s.slots; fc.codes = s.codes; fc.forced = s.forced; fc.max_frames = s.max_frames;
+  SlotState* slots = s.slots;
+  const int F = s.max_frames;
+  if (dumps) {
+    float* dl = s.dump_logits;
+    float* dh = s.dump_hidden;
+    const float* lg = s.logits;
+    const float* pin = s.pin;
+    if (dl) ops.push_back([=](cudaStream_t st) { return launch_dump(slots, B, lg, V, V, dl, F, st); });
+    if (dh) ops.push_back([=](cudaStream_t st) { return launch_dump(slots, B, pin, 2L * H, H, dh, F, st); });
+  }
+  SampleDesc sd;
+  sd.logits = s.logits; sd.ldl = V; sd.V = V; sd.B = B; sd.fc = fc;
+  ops.push_back([sd](cudaStream_t st) { return launch_sample(sd, st); });
+  const Q4Mat ce = m.codec_emb;
+  float* sem = s.pin + H;
+  ops.push_back([=](cudaStream_t st) { return launch_embed_code0(ce, slots, B, sem, 2L * H, st); });
+  RC(add_predictor(s, ops, B, true, fc));
+  FuseDesc fd;
+  fd.x = s.x; fd.ldx = H; fd.codec_emb = m.codec_emb; fd.group_emb = m.d_group_emb; fd.n_groups = d.p_groups;
+  fd.trail = s.trail; fd.max_trail = s.max_trail; fd.tts_pad = s.tts_pad; fd.B = B; fd.H = H; fd.fc = fc;
+  ops.push_back([fd](cudaStream_t st) { return launch_fuse(fd, st); });
+  RowPos rp;
+  rp.pos_base = &s.slots[0].pos;
+  rp.pos_stride = (int)(sizeof(SlotState) / sizeof(int));
+  RC(add_talker(s, ops, s.x, H, B, rp, talker_nsplit(s, B)));
+  RC(add_codec_head(s, ops, s.x, H, B, s.logits, s.pin, 2L * H));
+  ops.push_back([slots, B](cudaStream_t st) { return launch_frame_end(slots, B, st); });
+  return QTTS_OK;
+}
+
+static int generate_begin(Session& s, int n, const qtts_utterance* u, int F, unsigned flags, const uint32_t* forced,
+                          bool dump_logits, bool dump_hidden) {
+  const Model& m = *s.m;
+  const qtts_dims& d = m.d;
+  if (n <= 0 || n > s.maxB || !u || F <= 0) return fail(QTTS_ERR_BADARG, "bad generate arguments");
+  if (10 + F > s.maxP) return fail(QTTS_ERR_RANGE, "prefill + max_frames exceeds the session's max_positions");
+  CK(cudaSetDevice(m.device));
+  CK(cudaStreamSynchronize(s.st));
+  free_generation(s);
+  const int H = d.t_hidden;
+  // token rows: 6 specials then each utterance's text
+  std::vector<uint32_t> tok = {IM_START, ASSISTANT, NEWLINE, TTS_PAD, TTS_BOS, TTS_EOS};
+  std::vector<int> text_row(n);
+  int max_trail = 1, n_voice = 0;
+  for (int b = 0; b < n; ++b) {
+    const qtts_utterance& q = u[b];
+    if (q.n_text < 0 || (q.n_text > 0 && !q.text) || q.n_text > 65536) return fail(QTTS_ERR_BADARG, "bad text");
+    const qtts_sample_params& p = q.params;
+    if (!(p.temperature > 0.0f) || p.top_k < 0 || !std::isfinite(p.repetition_penalty))
+      return fail(QTTS_ERR_BADARG, "temperature must be > 0 (the reference divides by it), top_k >= 0");
+    if ((int)q.language_id >= d.t_vocab || (!q.voice && (int)q.speaker_id >= d.t_vocab))
+      return fail(QTTS_ERR_BADARG, "speaker / language id outside the codec vocabulary");
+    text_row[b] = (int)tok.size();
+    for (int i = 0; i < q.n_text; ++i) {
+      if ((int)q.text[i] >= d.t_text_vocab) return fail(QTTS_ERR_BADARG, "text token outside the text vocabulary");
+      tok.push_back(q.text[i]);
+    }
+    max_trail = std::max(max_trail, std::max(q.n_text - 1, 0) + 1);
+    if (q.voice) ++n_voice;
+  }
+  s.B = n;
+  s.max_frames = F;
+  s.max_trail = max_trail;
+  s.flags = flags;
+  const int Nt = (int)tok.size();
+  std::vector<void*>& T = s.gen_allocs;
+  RC(dalloc(&s.codes, (size_t)n * F * kMaxGroups, &T));
+  if (forced) RC(dalloc(&s.forced, (size_t)n * F * kMaxGroups, &T));
+  RC(dalloc(&s.tp, (size_t)Nt * H, &T));
+  RC(dalloc(&s.tp_h1, (size_t)Nt * m.fc1.n, &T));
+  RC(dalloc(&s.tp_tok, (size_t)Nt, &T));
+  RC(dalloc(&s.recipes, (size_t)n * 10, &T));
+  RC(dalloc(&s.trail, (size_t)n * max_trail * H, &T));
+  RC(dalloc(&s.trail_idx, (size_t)n * max_trail, &T));
+  RC(dalloc(&s.voices, (size_t)std::max(n_voice, 1) * H, &T));
+  if (dump_logits) RC(dalloc(&s.dump_logits, (size_t)n * F * d.t_vocab, &T));
+  if (dump_hidden) RC(dalloc(&s.dump_hidden, (size_t)n * F * H, &T));
+  if (forced) CK(cudaMemcpy(s.forced, forced, sizeof(uint32_t) * n * F * kMaxGroups, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(s.tp_tok, tok.data(), sizeof(uint32_t) * Nt, cudaMemcpyHostToDevice));
+  // prefill recipes (generate_new.rs:94-173) and trailing text rows (:314-326)
+  std::vector<RowRecipe> rec((size_t)n * 10, RowRecipe{-1, -1, -1, 0});
+  std::vector<int> seq(n), row0(n), trail_idx((size_t)n * max_trail, 5);
+  std::vector<SlotState> slots(n);
+  int vi = 0, nrows = 0;
+  for (int b = 0; b < n; ++b) {
+    const qtts_utterance& q = u[b];
+    row0[b] = nrows;
+    RowRecipe* r = &rec[(size_t)nrows];
+    int t = 0;
+    for (int i = 0; i < 3; ++i) r[t++] = {-1, i, -1, 0};  // role prefix
+    const int lang = (int)q.language_id;
+    const int pre[4] = {(int)CODEC_THINK, (int)CODEC_THINK_BOS, lang, (int)CODEC_THINK_EOS};
+    for (int i = 0; i < 4; ++i) r[t++] = {pre[i], 3, -1, 0};  // codec + TTS_PAD
+    if (q.voice) {
+      CK(cudaMemcpy(s.voices + (size_t)vi * H, q.voice, sizeof(float) * H, cudaMemcpyHostToDevice));
+      r[t++] = {-1, -1, vi++, 0};  // raw voice embedding
+    } else {
+      r[t++] = {(int)q.speaker_id, 3, -1, 0};
+    }
+    r[t++] = {(int)CODEC_PAD, 4, -1, 0};  // PAD + TTS_BOS
+    if (q.n_text > 0) r[t++] = {(int)CODEC_BOS, text_row[b], -1, 0};
+    seq[b] = t;
+    nrows += t;
+    const int ntr = std::max(q.n_text - 1, 0) + 1;
+    for (int i = 1; i < q.n_text; ++i) trail_idx[(size_t)b * max_trail + i - 1] = text_row[b] + i;
+    trail_idx[(size_t)b * max_trail + ntr - 1] = 5;  // TTS_EOS
+    SlotState& sl = slots[b];
+    memset(&sl, 0, sizeof(sl));
+    sl.pos = t;  // generate_new.rs:216
+    sl.n_trail = ntr;
+    sl.flags = (flags & QTTS_IGNORE_EOS) ? 1 : 0;
+    sl.temperature = q.params.temperature;
+    sl.rep_pen = q.params.repetition_penalty;
+    sl.top_k = q.params.top_k;
+    sl.eos = q.params.codec_eos_id;
+    sl.rng = q.seed;
+  }
+  CK(cudaMemcpy(s.recipes, rec.data(), sizeof(RowRecipe) * rec.size(), cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(s.trail_idx, trail_idx.data(), sizeof(int) * trail_idx.size(), cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(s.slots, slots.data(), sizeof(SlotState) * n, cudaMemcpyHostToDevice));
+  CK(cudaMemset(s.err_flag, 0, sizeof(int)));
+
+  // prefill
+  std::vector<Op> ops;
+  RC(add_text_proj(s, ops, s.tp_tok, Nt, s.tp_h1, s.tp, H));
+  {
+    const Q4Mat ce = m.codec_emb;
+    const RowRecipe* rc = s.recipes;
+    const float* tp = s.tp;
+    const float* vo = s.voices;
+    float* xp = s.xpre;
+    ops.push_back([=](cudaStream_t st) { return launch_assemble(ce, rc, nrows, tp, H, vo, H, xp, H, H, st); });
+    float* tr = s.trail;
+    const int* ti = s.trail_idx;
+    const int ntr = n * max_trail;
+    ops.push_back([=](cudaStream_t st) { return launch_gather_rows(tp, H, ti, ntr, tr, H, H, st); });
+  }
+  RC(run_ops(s, ops));
+  ops.clear();
+  s.tts_pad = s.tp + 3L * H;  // embed_text_token(TTS_PAD), generate_new.rs:222
+  // prefill runs of consecutive utterances with equal sequence length
+  // (9 without text, 10 with); their rows are contiguous in xpre
+  int b0 = 0;
+  while (b0 < n) {
+    int b1 = b0;
+    while (b1 < n && seq[b1] == seq[b0]) ++b1;
+    const int sq = seq[b0], nb = b1 - b0;
+    float* X = s.xpre + (size_t)row0[b0] * H;
+    RowPos rp;
+    rp.rows_per_sess = sq;
+    rp.sess0 = b0;
+    RC(add_talker(s, ops, X, H, nb * sq, rp, 1));
+    RC(add_codec_head(s, ops, X + (size_t)(sq - 1) * H, (long)sq * H, nb, s.logits + (size_t)b0 * d.t_vocab,
+                      s.pin + (size_t)b0 * 2 * H, 2L * H));
+    RC(run_ops(s, ops));
+    ops.clear();
+    b0 = b1;
+  }
+  RC(sync_check(s));
+
+  // frame plan -> CUDA graph
+  std::vector<Op> fops;
+  RC(build_frame_ops(s, fops, dump_logits || dump_hidden));
+  s.frame_kernels = (int)fops.size();
+  CK(cudaStreamBeginCapture(s.st, cudaStreamCaptureModeThreadLocal));
+  int rc = run_ops(s, fops);
+  cudaGraph_t g = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(s.st, &g);
+  if (rc != QTTS_OK) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (ce != cudaSuccess) return fail(QTTS_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
+  s.graph = g;
+  CK(cudaGraphInstantiate(&s.graph_exec, g, 0));
+  s.generating = true;
+  return QTTS_OK;
+}
+
+static int generate_frames(Session& s, int nf) {
+  if (!s.generating) return fail(QTTS_ERR_STATE, "no generation in progress");
+  for (int i = 0; i < nf; ++i) CK(cudaGraphLaunch(s.graph_exec, s.st));
+  return QTTS_OK;
+}
+
+static int generate_end(Session& s, uint32_t* codes, int* frames_out, float* dl, float* dh) {
+  if (!s.generating) return fail(QTTS_ERR_STATE, "no generation in progress");
+  RC(sync_check(s));
+  const int n = s.B, F = s.max_frames;
+  const qtts_dims& d = s.m->d;
+  if (codes) CK(cudaMemcpy(codes, s.codes, sizeof(uint32_t) * n * F * kMaxGroups, cudaMemcpyDeviceToHost));
+  if (frames_out) {
+    std::vector<SlotState> sl(n);
+    CK(cudaMemcpy(sl.data(), s.slots, sizeof(SlotState) * n, cudaMemcpyDeviceToHost));
+    for (int b = 0; b < n; ++b) frames_out[b] = std::min(sl[b].frames_out, F);
+  }
+  if (dl && s.dump_logits) CK(cudaMemcpy(dl, s.dump_logits, sizeof(float) * n * F * d.t_vocab, cudaMemcpyDeviceToHost));
+  if (dh && s.dump_hidden) CK(cudaMemcpy(dh, s.dump_hidden, sizeof(float) * n * F * d.t_hidden, cudaMemcpyDeviceToHost));
+  return QTTS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// per-call reference API (slot 0)
+// ---------------------------------------------------------------------------
+static int text_embed(Session& s, uint32_t tok, float* out) {
+  const Model& m = *s.m;
+  if ((int)tok >= m.d.t_text_vocab) return fail(QTTS_ERR_BADARG, "token outside the text vocabulary");
+  uint32_t* td = s.codes_plain;  // scratch for one id
+  CK(cudaMemcpyAsync(td, &tok, sizeof(uint32_t), cudaMemcpyHostToDevice, s.st));
+  std::vector<Op> ops;
+  float* h1 = s.h;
+  float* o = s.io;
+  RC(add_text_proj(s, ops, td, 1, h1, o, m.d.t_hidden));
+  RC(run_ops(s, ops));
+  CK(cudaMemcpyAsync(out, o, sizeof(float) * m.d.t_hidden, cudaMemcpyDeviceToHost, s.st));
+  return sync_check(s);
+}
+
+static int codec_embed(Session& s, uint32_t tok, float* out) {
+  const Model& m = *s.m;
+  if ((int)tok >= m.codec_emb.k) return fail(QTTS_ERR_BADARG, "token outside the codec vocabulary");
+  CK(cudaMemcpyAsync(s.codes_plain, &tok, sizeof(uint32_t), cudaMemcpyHostToDevice, s.st));
+  const cudaError_t e = launch_embed_rows(m.codec_emb, s.codes_plain, 1, s.io, m.d.t_hidden, s.st);
+  if (e != cudaSuccess) return fail(QTTS_ERR_CUDA, cudaGetErrorString(e));
+  CK(cudaMemcpyAsync(out, s.io, sizeof(float) * m.d.t_hidden, cudaMemcpyDeviceToHost, s.st));
+  return sync_check(s);
+}
+
+static int prefill_call(Session& s, const float* emb, int n, float* hid, float* logits) {
+  const Model& m = *s.m;
+  const int H = m.d.t_hidden;
+  if (!emb || n <= 0 || n > s.rows || n > s.maxP) return fail(QTTS_ERR_BADARG, "bad prefill length");
+  if (s.kvlen0 != 0) return fail(QTTS_ERR_STATE, "prefill needs an empty cache (qtts_session_reset)");
+  if (s.generating) free_generation(s);
+  CK(cudaMemcpyAsync(s.xpre, emb, sizeof(float) * n * H, cudaMemcpyHostToDevice, s.st));
+  std::vector<Op> ops;
+  RowPos rp;
+  rp.rows_per_sess = n;
+  RC(add_talker(s, ops, s.xpre, H, n, rp, 1));
+  RC(add_codec_head(s, ops, s.xpre + (size_t)(n - 1) * H, H, 1, s.logits, s.hid1, H));
+  RC(run_ops(s, ops));
+  if (hid) CK(cudaMemcpyAsync(hid, s.hid1, sizeof(float) * H, cudaMemcpyDeviceToHost, s.st));
+  if (logits) CK(cudaMemcpyAsync(logits, s.logits, sizeof(float) * m.d.t_vocab, cudaMemcpyDeviceToHost, s.st));
+  RC(sync_check(s));
+  s.kvlen0 = n;
+  return QTTS_OK;
+}
+
+static int talker_step_call(Session& s, const float* emb, int position, float* out) {
+  const Model& m = *s.m;
+  const int H = m.d.t_hidden, V = m.d.t_vocab;
+  if (!emb || !out || position < 0) return fail(QTTS_ERR_BADARG, "bad talker step arguments");
+  if (s.kvlen0 + 1 > s.maxP) return fail(QTTS_ERR_RANGE, "session KV capacity exhausted");
+  if (position >= m.d.t_max_pos) return fail(QTTS_ERR_RANGE, "position beyond the talker RoPE table");
+  if (s.generating) free_generation(s);
+  CK(cudaMemcpyAsync(s.x, emb, sizeof(float) * H, cudaMemcpyHostToDevice, s.st));
+  std::vector<Op> ops;
+  RowPos rp;
+  rp.pos_const = position;
+  rp.kv_const = s.kvlen0;
+  RC(add_talker(s, ops, s.x, H, 1, rp, talker_nsplit(s, 1)));
+  RC(add_codec_head(s, ops, s.x, H, 1, s.logits, s.hid1, H));
+  RC(run_ops(s, ops));
+  CK(cudaMemcpyAsync(out, s.hid1, sizeof(float) * H, cudaMemcpyDeviceToHost, s.st));
+  CK(cudaMemcpyAsync(out + H, s.logits, sizeof(float) * V, cudaMemcpyDeviceToHost, s.st));
+  RC(sync_check(s));
+  s.kvlen0 += 1;
+  return QTTS_OK;
+}
+
+static int predict_call(Session& s, const float* hidden, const float* sem, uint32_t* codes) {
+  const Model& m = *s.m;
+  const int H = m.d.t_hidden;
+  if (!hidden || !sem || !codes) return fail(QTTS_ERR_BADARG, "null argument");
+  if (s.generating) free_generation(s);
+  CK(cudaMemcpyAsync(s.pin, hidden, sizeof(float) * H, cudaMemcpyHostToDevice, s.st));
+  CK(cudaMemcpyAsync(s.pin + H, sem, sizeof(float) * H, cudaMemcpyHostToDevice, s.st));
+  std::vector<Op> ops;
+  RC(add_predictor(s, ops, 1, false, FrameCodes{}));
+  RC(run_ops(s, ops));
+  uint32_t c[kMaxGroups];
+  CK(cudaMemcpyAsync(c, s.codes_plain, sizeof(c), cudaMemcpyDeviceToHost, s.st));
+  RC(sync_check(s));
+  for (int g = 0; g < m.d.p_groups; ++g) codes[g] = c[g + 1];
+  return QTTS_OK;
+}
+
+static int acoustic_sum_call(Session& s, const uint32_t* codes, float* out) {
+  const Model& m = *s.m;
+  if (!codes || !out) return fail(QTTS_ERR_BADARG, "null argument");
+  for (int g = 0; g < m.d.p_groups; ++g)
+    if ((int)codes[g] >= m.p_emb[g].k) return fail(QTTS_ERR_BADARG, "code outside the predictor vocabulary");
+  CK(cudaMemcpyAsync(s.codes_plain, codes, sizeof(uint32_t) * m.d.p_groups, cudaMemcpyHostToDevice, s.st));
+  FuseDesc fd;
+  fd.x = s.io; fd.ldx = m.d.t_hidden; fd.group_emb = m.d_group_emb; fd.n_groups = m.d.p_groups;
+  fd.B = 1; fd.H = m.d.t_hidden; fd.mode = 2; fd.codes_plain = s.codes_plain;
+  const cudaError_t e = launch_fuse(fd, s.st);
+  if (e != cudaSuccess) return fail(QTTS_ERR_CUDA, cudaGetErrorString(e));
+  CK(cudaMemcpyAsync(out, s.io, sizeof(float) * m.d.t_hidden, cudaMemcpyDeviceToHost, s.st));
+  return sync_check(s);
+}
+
+static int sample_call(Session& s, const float* logits, int n, const qtts_sample_params* p, const uint32_t* prev,
+                       uint64_t* rng, uint32_t* out) {
+  if (!logits || !p || !prev || !rng || !out || n <= 0 || n > 4096) return fail(QTTS_ERR_BADARG, "bad sample arguments");
+  if (!(p->temperature > 0.0f) || p->top_k < 0) return fail(QTTS_ERR_BADARG, "temperature must be > 0, top_k >= 0");
+  // io layout: [logits n][prev 16][rng 2][out 1]
+  float* dl = s.io;
+  uint32_t* dprev = reinterpret_cast<uint32_t*>(s.io + n);
+  unsigned long long* drng = reinterpret_cast<unsigned long long*>(s.io + ((n + 16 + 1) & ~1));
+  uint32_t* dout = reinterpret_cast<uint32_t*>(drng + 1);
+  CK(cudaMemcpyAsync(dl, logits, sizeof(float) * n, cudaMemcpyHostToDevice, s.st));
+  CK(cudaMemcpyAsync(dprev, prev, sizeof(uint32_t) * 16, cudaMemcpyHostToDevice, s.st));
+  CK(cudaMemcpyAsync(drng, rng, sizeof(uint64_t), cudaMemcpyHostToDevice, s.st));
+  SampleDesc sd;
+  sd.logits = dl; sd.ldl = n; sd.V = n; sd.B = 1; sd.standalone = 1;
+  sd.temperature = p->temperature; sd.rep_pen = p->repetition_penalty; sd.top_k = p->top_k;
+  sd.prev = dprev; sd.rng = drng; sd.out = dout;
+  const cudaError_t e = launch_sample(sd, s.st);
+  if (e != cudaSuccess) return fail(QTTS_ERR_CUDA, cudaGetErrorString(e));
+  CK(cudaMemcpyAsync(rng, drng, sizeof(uint64_t), cudaMemcpyDeviceToHost, s.st));
+  CK(cudaMemcpyAsync(out, dout, sizeof(uint32_t), cudaMemcpyDeviceToHost, s.st));
+  return sync_check(s);
+}
+
+// ---------------------------------------------------------------------------
+// standalone GEMV entry points
+// ---------------------------------------------------------------------------
+constexpr size_t kCounterBytes = 16384;  // 4096 tile counters at the head of the scratch
+
+static int gemv_plan_standalone(int k, int n, int m, GemvDesc& g) {
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaGetLastError();
+  Q4Mat w;
+  w.k = k;
+  w.n = n;
+  g = gemv_base(EPI_STORE, {w}, false, m);
+  choose_split(sms, g);
+  return QTTS_OK;
+}
+
+static size_t gemv_scratch(int k, int n, int m) {
+  GemvDesc g;
+  gemv_plan_standalone(k, n, m, g);
+  return kCounterBytes + (g.S > 1 ? sizeof(float) * (size_t)g.S * m * n : 0);
+}
+
+static int gemv_dev(const uint8_t* packed, const uint16_t* scales, int k, int n, const float* x, int m, float* y,
+                    void* scratch, size_t scratch_bytes, cudaStream_t st) {
+  if (!packed || !scales || !x || !y || k <= 0 || n <= 0 || m <= 0 || n % 32)
+    return fail(QTTS_ERR_BADARG, "bad gemv arguments (n must be a multiple of 32)");
+  GemvDesc g;
+  gemv_plan_standalone(k, n, m, g);
+  g.mat[0].packed = packed;
+  g.mat[0].scales = reinterpret_cast<const __half*>(scales);
+  g.X = x; g.ldx = k;
+  g.epi.out = y; g.epi.ldo = n;
+  const size_t zb = (size_t)ceil_div(m, g.mb);
+  if (g.ntiles * zb > kCounterBytes / 4) return fail(QTTS_ERR_BADARG, "too many tiles for the counter area");
+  const size_t need = kCounterBytes + (g.S > 1 ? sizeof(float) * (size_t)g.S * m * n : 0);
+  if (!scratch || scratch_bytes < need) return fail(QTTS_ERR_BADARG, "scratch smaller than qtts_q4_gemv_scratch_bytes()");
+  g.counters = reinterpret_cast<unsigned*>(scratch);
+  g.part = reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + kCounterBytes);
+  gemv_init_attributes();
+  const cudaError_t e = launch_gemv(g, FrameCodes{}, st);
+  if (e != cudaSuccess) return fail(QTTS_ERR_CUDA, cudaGetErrorString(e));
+  return QTTS_OK;
+}
+
+}  // namespace qtts
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+using namespace qtts;
+
+struct qtts_model {
+  Model* m;
+};
+struct qtts_session {
+  Session* s;
+};
+
+extern "C" {
+
+const char* qtts_last_error(void) { return g_err.c_str(); }
+int qtts_version(void) { return 1; }
+
+int qtts_file_probe(const char* path, qtts_dims* out) {
+  if (!path || !out) return fail(QTTS_ERR_BADARG, "null argument");
+  HModel hm;
+  std::string err;
+  const int rc = parse_model(path, &hm, &err);
+  if (rc != QTTS_OK) return fail(rc, err);
+  *out = hm.d;
+  return QTTS_OK;
+}
+
+int qtts_synth_write(const char* path, const qtts_dims* dims, uint64_t seed) {
+  if (!path || !dims) return fail(QTTS_ERR_BADARG, "null argument");
+  std::string err;
+  const int rc = synth_write(path, *dims, seed, &err);
+  return rc == QTTS_OK ? rc : fail(rc, err);
+}
+void qtts_dims_1p7b(qtts_dims* out) { dims_1p7b(out); }
+void qtts_dims_tiny(qtts_dims* out) { dims_tiny(out); }
+
+int qtts_model_load(const char* path, int device, qtts_model** out) {
+  if (!path || !out) return fail(QTTS_ERR_BADARG, "null argument");
+  Model* m = nullptr;
+  const int rc = model_load(path, device, &m);
+  if (rc != QTTS_OK) return rc;
+  *out = new qtts_model{m};
+  return QTTS_OK;
+}
+
+int qtts_model_free(qtts_model* h) {
+  if (!h) return QTTS_OK;
+  cudaSetDevice(h->m->device);
+  cudaFree(h->m->arena);
+  cudaFree(h->m->d_group_emb);
+  delete h->m;
+  delete h;
+  return QTTS_OK;
+}
+
+int qtts_model_dims(const qtts_model* h, qtts_dims* out) {
+  if (!h || !out) return fail(QTTS_ERR_BADARG, "null argument");
+  *out = h->m->d;
+  return QTTS_OK;
+}
+size_t qtts_model_device_bytes(const qtts_model* h) { return h ? h->m->bytes : 0; }
+
+int qtts_session_create(qtts_model* h, int max_batch, int max_positions, qtts_session** out) {
+  if (!h || !out) return fail(QTTS_ERR_BADARG, "null argument");
+  Session* s = nullptr;
+  const int rc = session_create(h->m, max_batch, max_positions, &s);
+  if (rc != QTTS_OK) return rc;
+  *out = new qtts_session{s};
+  return QTTS_OK;
+}
+int qtts_session_free(qtts_session* h) {
+  if (!h) return QTTS_OK;
+  session_free_all(h->s);
+  delete h;
+  return QTTS_OK;
+}
+int qtts_session_reset(qtts_session* h) {
+  if (!h) return fail(QTTS_ERR_BADARG, "null argument");
+  Session& s = *h->s;
+  CK(cudaSetDevice(s.m->device));
+  CK(cudaStreamSynchronize(s.st));
+  free_generation(s);
+  s.kvlen0 = 0;
+  return QTTS_OK;
+}
+void* qtts_session_stream(qtts_session* h) { return h ? (void*)h->s->st : nullptr; }
+
+#define SESS(h)                                                      \
+  if (!h) return fail(QTTS_ERR_BADARG, "null session");              \
+  Session& s = *h->s;                                                \
+  if (cudaSetDevice(s.m->device) != cudaSuccess) return fail(QTTS_ERR_CUDA, "cudaSetDevice");
+
+int qtts_embed_text(qtts_session* h, uint32_t token, float* out) {
+  SESS(h);
+  if (!out) return fail(QTTS_ERR_BADARG, "null output");
+  return text_embed(s, token, out);
+}
+int qtts_embed_codec(qtts_session* h, uint32_t token, float* out) {
+  SESS(h);
+  if (!out) return fail(QTTS_ERR_BADARG, "null output");
+  return codec_embed(s, token, out);
+}
+int qtts_prefill(qtts_session* h, const float* emb, int n, float* hidden_out, float* logits_out) {
+  SESS(h);
+  return prefill_call(s, emb, n, hidden_out, logits_out);
+}
+int qtts_talker_step(qtts_session* h, const float* emb, int position, float* out) {
+  SESS(h);
+  return talker_step_call(s, emb, position, out);
+}
+int qtts_predict_acoustic(qtts_session* h, const float* talker_hidden, const float* semantic_embed, uint32_t* codes) {
+  SESS(h);
+  return predict_call(s, talker_hidden, semantic_embed, codes);
+}
+int qtts_acoustic_embed_sum(qtts_session* h, const uint32_t* codes, float* out) {
+  SESS(h);
+  return acoustic_sum_call(s, codes, out);
+}
+int qtts_sample(qtts_session* h, const float* logits, int n, const qtts_sample_params* p, const uint32_t* prev16,
+                uint64_t* rng, uint32_t* out) {
+  SESS(h);
+  return sample_call(s, logits, n, p, prev16, rng, out);
+}
+
+int qtts_generate_begin(qtts_session* h, int n_utt, const qtts_utterance* utts, int max_frames, unsigned flags,
+                        const uint32_t* forced) {
+  SESS(h);
+  return generate_begin(s, n_utt, utts, max_frames, flags, forced, false, false);
+}
+int qtts_generate_frames(qtts_session* h, int n_frames) {
+  SESS(h);
+  return generate_frames(s, n_frames);
+}
+int qtts_generate_end(qtts_session* h, uint32_t* codes_out, int* frames_out, float* logits_dump, float* hidden_dump) {
+  SESS(h);
+  return generate_end(s, codes_out, frames_out, logits_dump, hidden_dump);
+}
+int qtts_generate(qtts_session* h, int n_utt, const qtts_utterance* utts, int max_frames, unsigned flags,
+                  const uint32_t* forced, uint32_t* codes_out, int* frames_out, float* logits_dump,
+                  float* hidden_dump) {
+  SESS(h);
+  RC(generate_begin(s, n_utt, utts, max_frames, flags, forced, logits_dump != nullptr, hidden_dump != nullptr));
+  RC(generate_frames(s, max_frames));
+  return generate_end(s, codes_out, frames_out, logits_dump, hidden_dump);
+}
+int qtts_frame_kernel_count(qtts_session* h) { return h ? h->s->frame_kernels : 0; }
+
+size_t qtts_q4_gemv_scratch_bytes(int k, int n, int m) {
+  if (k <= 0 || n <= 0 || m <= 0) return 0;
+  return gemv_scratch(k, n, m);
+}
+int qtts_q4_gemv_dev(const uint8_t* packed, const uint16_t* scales, int k, int n, const float* x, int m, float* y,
+                     void* scratch, size_t scratch_bytes, void* stream) {
+  return gemv_dev(packed, scales, k, n, x, m, y, scratch, scratch_bytes, (cudaStream_t)stream);
+}
+int qtts_q4_gemv(const uint8_t* packed, const uint16_t* scales, int k, int n, const float* x, int m, float* y) {
+  if (!packed || !scales || !x || !y || k <= 0 || n <= 0 || m <= 0 || n % 32) return fail(QTTS_ERR_BADARG, "bad gemv arguments");
+  const size_t pb = (size_t)k * n / 2, sb = (size_t)k * n / 32 * 2, xb = sizeof(float) * (size_t)m * k,
+               yb = sizeof(float) * (size_t)m * n, scr = gemv_scratch(k, n, m);
+  char* buf = nullptr;
+  const size_t a = (pb + 255) & ~(size_t)255, b2 = (sb + 255) & ~(size_t)255, c = (xb + 255) & ~(size_t)255,
+               dsz = (yb + 255) & ~(size_t)255;
+  if (cudaMalloc(&buf, a + b2 + c + dsz + scr) != cudaSuccess) return fail(QTTS_ERR_OOM, "device allocation failed");
+  int rc = QTTS_OK;
+  if (cudaMemset(buf + a + b2 + c + dsz, 0, scr) != cudaSuccess ||
+      cudaMemcpy(buf, packed, pb, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(buf + a, scales, sb, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(buf + a + b2, x, xb, cudaMemcpyHostToDevice) != cudaSuccess)
+    rc = fail(QTTS_ERR_CUDA, "copy to device failed");
+  if (rc == QTTS_OK)
+    rc = gemv_dev(reinterpret_cast<uint8_t*>(buf), reinterpret_cast<uint16_t*>(buf + a), k, n,
+                  reinterpret_cast<float*>(buf + a + b2), m, reinterpret_cast<float*>(buf + a + b2 + c),
+                  buf + a + b2 + c + dsz, scr, nullptr);
+  if (rc == QTTS_OK && cudaMemcpy(y, buf + a + b2 + c, yb, cudaMemcpyDeviceToHost) != cudaSuccess)
+    rc = fail(QTTS_ERR_CUDA, "copy from device failed");
+  cudaFree(buf);
+  return rc;
+}
+int qtts_expf_dev(const float* x, float* y, int n, void* stream) {
+  if (!x || !y || n < 0) return fail(QTTS_ERR_BADARG, "bad expf arguments");
+  const cudaError_t e = launch_expf(x, y, n, (cudaStream_t)stream);
+  return e == cudaSuccess ? QTTS_OK : fail(QTTS_ERR_CUDA, cudaGetErrorString(e));
+}
+int qtts_f16_gemv_dev(const uint16_t* w, int k, int n, const float* x, int m, float* y, void* stream) {
+  if (!w || !x || !y || k <= 0 || n <= 0 || m <= 0 || n % 2) return fail(QTTS_ERR_BADARG, "bad f16 gemv arguments");
+  const cudaError_t e = launch_f16_gemv(reinterpret_cast<const __half*>(w), k, n, x, m, y, (cudaStream_t)stream);
+  return e == cudaSuccess ? QTTS_OK : fail(QTTS_ERR_CUDA, cudaGetErrorString(e));
+}
+int qtts_q4_dequant_dev(const uint8_t* packed, const uint16_t* scales, int k, int n, float* out, void* stream) {
+  if (!packed || !scales || !out || k <= 0 || n <= 0 || n % 32) return fail(QTTS_ERR_BADARG, "bad dequant arguments");
+  Q4Mat q;
+  q.packed = packed;
+  q.scales = reinterpret_cast<const __half*>(scales);
+  q.k = k;
+  q.n = n;
+  const cudaError_t e = launch_dequant(q, out, (cudaStream_t)stream);
+  return e == cudaSuccess ? QTTS_OK : fail(QTTS_ERR_CUDA, cudaGetErrorString(e));
+}
+
+}  // extern "C"

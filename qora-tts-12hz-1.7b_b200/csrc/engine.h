@@ -1,0 +1,97 @@
+// engine.h -- device model, sessions and per-frame launch plans.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <functional>
+#include <string>
+#include <vector>
+
+#include "../../include/qtts.h"
+#include "format.h"
+#include "kernels.h"
+#include "misc.h"
+
+namespace qtts {
+
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+
+struct DLayer {
+  Q4Mat q, k, v, o, gate, up, down;
+  const __half *q_norm = nullptr, *k_norm = nullptr, *in_norm = nullptr, *post_norm = nullptr;
+};
+
+// The model in HBM: every Weight keeps its on-disk bytes (packed + f16
+// scales), norms stay f16, biases and RoPE tables f32 -- one arena.
+struct Model {
+  qtts_dims d{};
+  int device = 0;
+  int sm_count = 148;
+  char* arena = nullptr;
+  size_t bytes = 0;
+  std::vector<DLayer> tl, pl;
+  Q4Mat codec_emb, text_emb, fc1, fc2, codec_head, input_proj;
+  const float *fc1_b = nullptr, *fc2_b = nullptr, *input_proj_b = nullptr;
+  const float *t_cos = nullptr, *t_sin = nullptr, *p_cos = nullptr, *p_sin = nullptr;
+  const __half *t_final = nullptr, *p_final = nullptr;
+  std::vector<Q4Mat> p_emb, lm;
+  Q4Mat* d_group_emb = nullptr;  // device copy of p_emb for the fusion kernel
+  bool has_proj = false;
+};
+
+using Op = std::function<cudaError_t(cudaStream_t)>;
+
+struct Session {
+  Model* m = nullptr;
+  int maxB = 0, maxP = 0, pages_per_sess = 0;
+  cudaStream_t st = nullptr;
+  // caches
+  float* kv_pool = nullptr;   // talker [pages][layers][2][kvh][16][128]
+  int* page_table = nullptr;  // [maxB][pages_per_sess]
+  float* pkv_pool = nullptr;  // predictor, one page per slot
+  // per-slot state
+  SlotState* slots = nullptr;
+  // activations
+  int rows = 0;  // row capacity of q/attn/h/xpre (10 * maxB)
+  float *x = nullptr, *pin = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr;
+  float *px = nullptr, *px1 = nullptr, *logits = nullptr, *xpre = nullptr, *hid1 = nullptr;
+  // scratch
+  float* part = nullptr;
+  size_t part_floats = 0;
+  unsigned* counters = nullptr;
+  size_t n_counters = 0;
+  unsigned* counters2 = nullptr;
+  unsigned long long* keys = nullptr;
+  float* apart = nullptr;
+  size_t apart_floats = 0;
+  unsigned* acounters = nullptr;
+  size_t n_acounters = 0;
+  int* err_flag = nullptr;
+  uint32_t* codes_plain = nullptr;  // [maxB][16]
+  // per-call API
+  int kvlen0 = 0;
+  float* io = nullptr;  // staging [io_floats]
+  size_t io_floats = 0;
+  // generation
+  int B = 0, max_frames = 0, max_trail = 0;
+  unsigned flags = 0;
+  uint32_t* codes = nullptr;
+  uint32_t* forced = nullptr;
+  float* trail = nullptr;
+  float* tts_pad = nullptr;
+  float* tp = nullptr;
+  float* tp_h1 = nullptr;
+  uint32_t* tp_tok = nullptr;
+  RowRecipe* recipes = nullptr;
+  int* trail_idx = nullptr;
+  float* voices = nullptr;
+  float* dump_logits = nullptr;
+  float* dump_hidden = nullptr;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t graph_exec = nullptr;
+  int frame_kernels = 0;
+  bool generating = false;
+  std::vector<void*> gen_allocs;
+};
+
+}  // namespace qtts

@@ -1,0 +1,221 @@
+// kernels.h -- descriptors and launchers of the QORA-TTS sm_100a kernels.
+// Shared by the kernel translation units and the engine (host C++).
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace qtts {
+
+constexpr int kHeadDim = 128;      // head_dim of talker and predictor (config.json)
+constexpr int kPageSize = 16;      // KV positions per page
+constexpr int kTileN = 256;        // GEMV columns per CTA tile (8 Q4 groups of 32)
+constexpr int kGemvThreads = 256;  // 8 warps
+constexpr int kMaxGroups = 16;     // codes per frame (1 semantic + 15 acoustic)
+
+// One Q4 g32 weight in its on-disk [k][n] layout (gemv.rs:26-31).
+struct Q4Mat {
+  const uint8_t* packed = nullptr;  // k*n/2 bytes, low nibble = even column
+  const __half* scales = nullptr;   // k*n/32 f16, groups of 32 along n
+  int k = 0, n = 0;
+};
+
+// Paged KV addressing.  A page holds kPageSize positions of every layer:
+//   pool[page][layer][K|V][kv_head][pos % 16][128]  (f32)
+// page = page_table[sess * pages_per_sess + pos / 16] (or = sess when
+// page_table is null: one page per session, the predictor cache).
+struct KvDesc {
+  float* pool = nullptr;
+  const int* page_table = nullptr;
+  int pages_per_sess = 0;
+  int n_layers = 0;
+  int kv_heads = 0;
+  int layer = 0;
+};
+
+// Row -> (session, position) mapping shared by the QKV epilogue and the
+// attention kernel: s = m / rows_per_sess, r = m % rows_per_sess,
+// session = sess0 + s, rope position = (pos_base ? pos_base[session *
+// pos_stride] : pos_const) + r, cache index = kv_const + r when kv_const >= 0
+// (talker.rs:277,299: K/V append at cached_len, RoPE at `position`), else the
+// rope position.  A row attends cache entries [0, cache index].
+struct RowPos {
+  int rows_per_sess = 1;
+  const int* pos_base = nullptr;
+  int pos_stride = 1;
+  int pos_const = 0;
+  int kv_const = -1;
+  int sess0 = 0;
+};
+
+__host__ __device__ __forceinline__ void row_pos(const RowPos& rp, int m, int& sess, int& pos, int& kvpos) {
+  const int s = m / rp.rows_per_sess;
+  const int r = m - s * rp.rows_per_sess;
+  sess = rp.sess0 + s;
+  pos = (rp.pos_base ? rp.pos_base[sess * rp.pos_stride] : rp.pos_const) + r;
+  kvpos = rp.kv_const >= 0 ? rp.kv_const + r : pos;
+}
+
+enum EpiKind : int {
+  EPI_STORE = 0,    // out = v (+bias) (optionally silu)
+  EPI_RESID = 1,    // out += v
+  EPI_SWIGLU = 2,   // paired gate/up: out = silu(gate) * up
+  EPI_QKV = 3,      // q|k|v: per-head QK-norm + RoPE; q -> q_out, k/v -> KV cache
+  EPI_ARGMAX = 4,   // argmax over n, last index wins on ties -> code
+};
+
+struct EpiDesc {
+  // STORE / RESID / SWIGLU
+  float* out = nullptr;
+  long ldo = 0;
+  const float* bias = nullptr;
+  int act_silu = 0;
+  // QKV
+  float* q_out = nullptr;
+  long ldq = 0;
+  const __half* q_norm = nullptr;
+  const __half* k_norm = nullptr;
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+  int rope_rows = 0;
+  int rope_skip_oob = 0;  // predictor: rotation skipped past the table (code_predictor.rs:107)
+  int heads = 0, kv_heads = 0;
+  KvDesc kv;
+  RowPos rp;
+  int* err_flag = nullptr;
+  // ARGMAX: keys[m] accumulates (order_key(v) << 32 | col); the last tile
+  // finalises codes (see FrameCodes).
+  unsigned long long* keys = nullptr;
+  unsigned* counters2 = nullptr;
+  int group = 0;         // code slot written (1..15)
+  int frame_codes = 0;   // 1 = write through FrameCodes (generation); 0 = codes_plain
+  uint32_t* codes_plain = nullptr;  // [M][16]
+};
+
+struct GemvDesc {
+  int epi_kind = EPI_STORE;
+  int nmat = 1;     // matrices in this launch (<= 3)
+  int paired = 0;   // 1: both matrices cover the same columns (gate/up)
+  Q4Mat mat[3];
+  int tile0[4] = {0, 0, 0, 0};  // first tile of each matrix (concatenated mode)
+  int col0[4] = {0, 0, 0, 0};   // first concatenated column of each matrix
+  int ntiles = 0;
+  int ncols = 0;                // concatenated columns (partial row stride)
+  int k = 0;
+  int S = 1;                    // K splits (grid.y)
+  int rows_per_split = 0;
+  int M = 1;                    // activation rows
+  int mb = 1;                   // rows per CTA (grid.z = ceil(M / mb))
+  // input rows
+  const float* X = nullptr;
+  long ldx = 0;
+  const __half* gamma = nullptr;  // RMSNorm prologue (gemv.rs:408-417)
+  // embedding-gather prologue: row m = dequant(emb row emb_idx[m*emb_idx_stride])
+  Q4Mat emb;
+  const uint32_t* emb_idx = nullptr;
+  int emb_idx_stride = 1;
+  float* xnorm_out = nullptr;  // optional copy of the normalised rows
+  long ld_xnorm = 0;
+  // split-K scratch
+  float* part = nullptr;        // [S][M][ncols]
+  unsigned* counters = nullptr; // [ntiles * zblocks], left at zero
+  EpiDesc epi;
+};
+
+// Frame bookkeeping shared by the sampler / argmax epilogue / fusion.
+struct SlotState {
+  int pos;          // next talker position (KV length before the step)
+  int frame;        // frames produced so far
+  int n_trail;      // trailing text rows
+  int done;         // EOS seen
+  int frames_out;   // frames recorded
+  int flags;
+  float temperature;
+  float rep_pen;
+  int top_k;
+  uint32_t eos;
+  unsigned long long rng;
+  uint32_t prev[16];  // repetition-penalty history (generate_new.rs:231,252,267)
+  uint32_t cur[16];   // codes driving the current frame (after forcing)
+};
+
+struct FrameCodes {
+  SlotState* slots = nullptr;
+  uint32_t* codes = nullptr;       // [B][max_frames][16] chosen codes
+  const uint32_t* forced = nullptr;// [B][max_frames][16] or null
+  int max_frames = 0;
+};
+
+// ---- launchers (return cudaError_t of the launch) ----
+size_t gemv_smem_bytes(const GemvDesc& d);
+cudaError_t launch_gemv(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st);
+
+struct AttnDesc {
+  const float* q = nullptr;  // row m: heads*128
+  long ldq = 0;
+  float* out = nullptr;
+  long ldo = 0;
+  KvDesc kv;
+  RowPos rp;
+  int heads = 0, kv_heads = 0;
+  int M = 1;
+  int nsplit = 1;
+  float* part = nullptr;        // [M][kv_heads][nsplit][2 + 2*G + G*128]
+  unsigned* counters = nullptr; // [M][kv_heads]
+};
+cudaError_t launch_attention(const AttnDesc& d, cudaStream_t st);
+
+struct SampleDesc {
+  const float* logits = nullptr;  // [B][ldl]
+  long ldl = 0;
+  int V = 0;
+  int B = 0;
+  FrameCodes fc;
+  unsigned long long* argmax_keys = nullptr;  // [16][B] reset here for the frame
+  int n_keys = 0;
+  // standalone mode (qtts_sample): params/prev/rng given explicitly
+  int standalone = 0;
+  float temperature = 1.0f, rep_pen = 1.0f;
+  int top_k = 0;
+  const uint32_t* prev = nullptr;
+  unsigned long long* rng = nullptr;
+  uint32_t* out = nullptr;
+};
+cudaError_t launch_sample(const SampleDesc& d, cudaStream_t st);
+
+// Frame input fusion (generate_new.rs:255,271-286):
+// x[b] = (emb_codec(code0) + sum_g emb_g(code_{g+1})) + text_add[b]
+struct FuseDesc {
+  float* x = nullptr;            // [B][H]
+  long ldx = 0;
+  float* sem_out = nullptr;      // optional copy of emb_codec(code0) [B][lds]
+  long lds = 0;
+  Q4Mat codec_emb;               // talker codec embedding [V][H]
+  const Q4Mat* group_emb = nullptr;  // device array of p_groups matrices [pV][H]
+  int n_groups = 0;
+  const float* trail = nullptr;  // [B][max_trail][H]
+  int max_trail = 0;
+  const float* tts_pad = nullptr;  // [H]
+  int B = 0, H = 0;
+  FrameCodes fc;
+  int mode = 0;                  // 0: full frame fusion; 1: semantic only (sem_out); 2: acoustic sum only
+  const uint32_t* codes_plain = nullptr;  // mode 1/2 standalone codes
+};
+cudaError_t launch_fuse(const FuseDesc& d, cudaStream_t st);
+
+// Gather dequantised Q4 rows: out[i] = row idx[i] of mat (gemv.rs:378-400).
+cudaError_t launch_embed_rows(const Q4Mat& mat, const uint32_t* idx, int count, float* out, long ldo,
+                              cudaStream_t st);
+// Semantic embedding of the current code0: out[b] = emb(slots[b].cur[0]).
+cudaError_t launch_embed_code0(const Q4Mat& mat, const SlotState* slots, int B, float* out, long ldo,
+                               cudaStream_t st);
+// Elementwise: out[r] = a[r] + b[r] (prefill overlays), rows of n floats.
+cudaError_t launch_add_rows(const float* a, long lda, const float* b, long ldb, float* out, long ldo,
+                            int rows, int n, cudaStream_t st);
+cudaError_t launch_frame_end(SlotState* slots, int B, cudaStream_t st);
+cudaError_t launch_dequant(const Q4Mat& m, float* out, cudaStream_t st);
+cudaError_t launch_f16_gemv(const __half* w, int k, int n, const float* x, int m, float* y,
+                            cudaStream_t st);
+
+}  // namespace qtts

@@ -1,0 +1,230 @@
+// misc.cu -- embedding gathers, frame-input fusion, prefill row assembly,
+// frame bookkeeping, whole-matrix dequant and the F16 GEMV (sm_100a).
+#include "common.cuh"
+#include "kernels.h"
+#include "misc.h"
+
+#include <algorithm>
+
+namespace qtts {
+
+// ---- frame input (generate_new.rs:255, 271-286) ---------------------------
+// x[b][j] = (sem[j] + acs[j]) + text[j], with acs = ((0 + e_0) + e_1) ... + e_14
+// accumulated in group order exactly like get_acoustic_embeddings_sum
+// (code_predictor.rs:280-293).  Element-wise, so bit-identical to the CPU.
+__global__ void fuse_kernel(const FuseDesc d) {
+  const int b = blockIdx.y;
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= d.H) return;
+  const uint32_t* codes;
+  int f = 0, ntr = 0;
+  if (d.codes_plain) {
+    codes = d.codes_plain + (size_t)b * kMaxGroups;
+  } else {
+    const SlotState& sl = d.fc.slots[b];
+    codes = sl.cur;
+    f = sl.frame;
+    ntr = sl.n_trail;
+  }
+  if (d.mode == 2) {  // acoustic sum only (codes[0..n_groups))
+    float acs = 0.0f;
+    for (int g = 0; g < d.n_groups; ++g) {
+      const Q4Mat& E = d.group_emb[g];
+      const uint32_t c = codes[g];
+      acs = acs + q4_value(E.packed + (size_t)c * (E.n / 2), E.scales + (size_t)c * (E.n / 32), j);
+    }
+    d.x[(size_t)b * d.ldx + j] = acs;
+    return;
+  }
+  const uint32_t c0 = codes[0];
+  const float sem = q4_value(d.codec_emb.packed + (size_t)c0 * (d.codec_emb.n / 2),
+                             d.codec_emb.scales + (size_t)c0 * (d.codec_emb.n / 32), j);
+  if (d.sem_out) d.sem_out[(size_t)b * d.lds + j] = sem;
+  if (d.mode == 1) return;
+  float acs = 0.0f;
+  for (int g = 0; g < d.n_groups; ++g) {
+    const Q4Mat& E = d.group_emb[g];
+    const uint32_t c = codes[g + 1];
+    acs = acs + q4_value(E.packed + (size_t)c * (E.n / 2), E.scales + (size_t)c * (E.n / 32), j);
+  }
+  const float* ta = (f < ntr) ? d.trail + ((size_t)b * d.max_trail + f) * d.H : d.tts_pad;
+  d.x[(size_t)b * d.ldx + j] = (sem + acs) + ta[j];
+}
+
+cudaError_t launch_fuse(const FuseDesc& d, cudaStream_t st) {
+  if (d.B <= 0 || d.H <= 0) return cudaErrorInvalidValue;
+  const dim3 grid((d.H + 255) / 256, d.B);
+  fuse_kernel<<<grid, 256, 0, st>>>(d);
+  return cudaGetLastError();
+}
+
+// ---- gathers ----------------------------------------------------------------
+__global__ void embed_rows_kernel(const Q4Mat m, const uint32_t* idx, int count, float* out, long ldo) {
+  const int i = blockIdx.y;
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= count || j >= m.n) return;
+  const uint32_t r = idx[i];
+  out[(size_t)i * ldo + j] = q4_value(m.packed + (size_t)r * (m.n / 2), m.scales + (size_t)r * (m.n / 32), j);
+}
+cudaError_t launch_embed_rows(const Q4Mat& mat, const uint32_t* idx, int count, float* out, long ldo,
+                              cudaStream_t st) {
+  if (count <= 0) return cudaSuccess;
+  const dim3 grid((mat.n + 255) / 256, count);
+  embed_rows_kernel<<<grid, 256, 0, st>>>(mat, idx, count, out, ldo);
+  return cudaGetLastError();
+}
+
+__global__ void embed_code0_kernel(const Q4Mat m, const SlotState* slots, float* out, long ldo) {
+  const int b = blockIdx.y;
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= m.n) return;
+  const uint32_t r = slots[b].cur[0];
+  out[(size_t)b * ldo + j] = q4_value(m.packed + (size_t)r * (m.n / 2), m.scales + (size_t)r * (m.n / 32), j);
+}
+cudaError_t launch_embed_code0(const Q4Mat& mat, const SlotState* slots, int B, float* out, long ldo,
+                               cudaStream_t st) {
+  const dim3 grid((mat.n + 255) / 256, B);
+  embed_code0_kernel<<<grid, 256, 0, st>>>(mat, slots, out, ldo);
+  return cudaGetLastError();
+}
+
+__global__ void add_rows_kernel(const float* a, long lda, const float* b, long ldb, float* out, long ldo, int n) {
+  const int r = blockIdx.y;
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= n) return;
+  out[(size_t)r * ldo + j] = a[(size_t)r * lda + j] + b[(size_t)r * ldb + j];
+}
+cudaError_t launch_add_rows(const float* a, long lda, const float* b, long ldb, float* out, long ldo, int rows,
+                            int n, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  const dim3 grid((n + 255) / 256, rows);
+  add_rows_kernel<<<grid, 256, 0, st>>>(a, lda, b, ldb, out, ldo, n);
+  return cudaGetLastError();
+}
+
+// Prefill rows of generate_new.rs:94-173: each row is codec_emb(tok) +
+// text_proj(row), the raw voice embedding, or a text_proj row alone.
+__global__ void assemble_kernel(const Q4Mat codec, const RowRecipe* rec, const float* tp, long ldtp,
+                                const float* voice, long ldv, float* out, long ldo, int H) {
+  const int r = blockIdx.y;
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= H) return;
+  const RowRecipe q = rec[r];
+  float v;
+  if (q.voice >= 0) {
+    v = voice[(size_t)q.voice * ldv + j];
+  } else if (q.codec >= 0) {
+    const float c = q4_value(codec.packed + (size_t)q.codec * (codec.n / 2),
+                             codec.scales + (size_t)q.codec * (codec.n / 32), j);
+    v = (q.tp >= 0) ? c + tp[(size_t)q.tp * ldtp + j] : c;
+  } else {
+    v = tp[(size_t)q.tp * ldtp + j];
+  }
+  out[(size_t)r * ldo + j] = v;
+}
+cudaError_t launch_assemble(const Q4Mat& codec, const RowRecipe* rec, int rows, const float* tp, long ldtp,
+                            const float* voice, long ldv, float* out, long ldo, int H, cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  const dim3 grid((H + 255) / 256, rows);
+  assemble_kernel<<<grid, 256, 0, st>>>(codec, rec, tp, ldtp, voice, ldv, out, ldo, H);
+  return cudaGetLastError();
+}
+
+__global__ void gather_rows_kernel(const float* src, long lds, const int* idx, float* out, long ldo, int n) {
+  const int r = blockIdx.y;
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= n) return;
+  out[(size_t)r * ldo + j] = src[(size_t)idx[r] * lds + j];
+}
+cudaError_t launch_gather_rows(const float* src, long lds, const int* idx, int rows, float* out, long ldo, int n,
+                               cudaStream_t st) {
+  if (rows <= 0) return cudaSuccess;
+  const dim3 grid((n + 255) / 256, rows);
+  gather_rows_kernel<<<grid, 256, 0, st>>>(src, lds, idx, out, ldo, n);
+  return cudaGetLastError();
+}
+
+// ---- frame bookkeeping --------------------------------------------------------
+__global__ void frame_end_kernel(SlotState* slots, int B) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  SlotState& s = slots[b];
+  if (!s.done) {
+    s.pos += 1;
+    s.frame += 1;
+    s.frames_out = s.frame;
+  }
+}
+cudaError_t launch_frame_end(SlotState* slots, int B, cudaStream_t st) {
+  frame_end_kernel<<<(B + 127) / 128, 128, 0, st>>>(slots, B);
+  return cudaGetLastError();
+}
+
+// Copy logits / talker hidden of the current frame into dump buffers.
+__global__ void dump_kernel(const SlotState* slots, const float* src, long lds, int n, float* dst, int max_frames) {
+  const int b = blockIdx.y;
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= n) return;
+  const int f = slots[b].frame;
+  if (f >= max_frames || slots[b].done) return;
+  dst[((size_t)b * max_frames + f) * n + j] = src[(size_t)b * lds + j];
+}
+cudaError_t launch_dump(const SlotState* slots, int B, const float* src, long lds, int n, float* dst, int max_frames,
+                        cudaStream_t st) {
+  const dim3 grid((n + 255) / 256, B);
+  dump_kernel<<<grid, 256, 0, st>>>(slots, src, lds, n, dst, max_frames);
+  return cudaGetLastError();
+}
+
+// ---- whole-matrix dequant (gemv.rs:378-400 applied to every row) --------------
+__global__ void dequant_kernel(const Q4Mat m, float* out) {
+  const size_t total = (size_t)m.k * m.n / 2;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / (m.n / 2), cb = i % (m.n / 2);
+    const uint8_t b = m.packed[i];
+    const float s = h2f(m.scales[r * (m.n / 32) + (2 * cb) / 32]);
+    out[r * m.n + 2 * cb] = s * (float)((int)(b & 0xF) - 8);
+    out[r * m.n + 2 * cb + 1] = s * (float)((int)(b >> 4) - 8);
+  }
+}
+cudaError_t launch_dequant(const Q4Mat& m, float* out, cudaStream_t st) {
+  dequant_kernel<<<1184, 256, 0, st>>>(m, out);
+  return cudaGetLastError();
+}
+
+// ---- the sampler's exp, element-wise ----------------------------------------------
+__global__ void expf_kernel(const float* x, float* y, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) y[i] = expf_glibc(x[i]);
+}
+cudaError_t launch_expf(const float* x, float* y, int n, cudaStream_t st) {
+  if (n <= 0) return cudaSuccess;
+  expf_kernel<<<std::min((n + 255) / 256, 4096), 256, 0, st>>>(x, y, n);
+  return cudaGetLastError();
+}
+
+// ---- F16 GEMV (gemv.rs:183-196) -------------------------------------------------
+// One thread per (row m, column pair); sequential over k like the reference
+// loop, so each output is the reference's own summation order.
+__global__ void f16_gemv_kernel(const __half* w, int k, int n, const float* x, int m, float* y) {
+  const int j2 = blockIdx.x * blockDim.x + threadIdx.x;
+  const int row = blockIdx.y;
+  if (2 * j2 >= n || row >= m) return;
+  const float* xr = x + (size_t)row * k;
+  float a0 = 0.0f, a1 = 0.0f;
+  for (int kk = 0; kk < k; ++kk) {
+    const __half2 wv = *reinterpret_cast<const __half2*>(w + (size_t)kk * n + 2 * j2);
+    const float xv = xr[kk];
+    a0 = __fadd_rn(a0, __fmul_rn(xv, __low2float(wv)));
+    a1 = __fadd_rn(a1, __fmul_rn(xv, __high2float(wv)));
+  }
+  y[(size_t)row * n + 2 * j2] = a0;
+  y[(size_t)row * n + 2 * j2 + 1] = a1;
+}
+cudaError_t launch_f16_gemv(const __half* w, int k, int n, const float* x, int m, float* y, cudaStream_t st) {
+  if (n % 2) return cudaErrorInvalidValue;
+  const dim3 grid((n / 2 + 127) / 128, m);
+  f16_gemv_kernel<<<grid, 128, 0, st>>>(w, k, n, x, m, y);
+  return cudaGetLastError();
+}
+
+}  // namespace qtts
