@@ -99,7 +99,9 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnDesc d) {
   __syncthreads();
   // thread t < G*32 finalises (g = t/32, dims 4*(t%32)..)
   const int nsp = d.nsplit;
-  const size_t rec = 2 + kHeadDim;  // per (g): m, l, acc[128]
+  // per (split, g) record: m, l, 2 pad, acc[128] -- 132 floats keeps the
+  // float4 accumulator stores 16-byte aligned
+  const size_t rec = kAttnRec;
   float* part = d.part ? d.part + ((size_t)(m * d.kv_heads + h) * nsp) * G * rec : nullptr;
   if (tid < G * 32) {
     const int g = tid / 32, ln = tid % 32;
@@ -119,7 +121,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnDesc d) {
     } else {
       float* r = part + ((size_t)split * G + g) * rec;
       if (ln == 0) { r[0] = M; r[1] = lt; }
-      *reinterpret_cast<float4*>(r + 2 + 4 * ln) = a;
+      *reinterpret_cast<float4*>(r + 4 + 4 * ln) = a;
     }
   }
   if (nsp == 1) return;
@@ -143,7 +145,7 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnDesc d) {
       if (!(ls > 0.0f)) continue;
       const float f = expf(__ldcg(r) - M);
       lt += ls * f;
-      const float4 x = __ldcg(reinterpret_cast<const float4*>(r + 2) + ln);
+      const float4 x = __ldcg(reinterpret_cast<const float4*>(r + 4) + ln);
       a.x += x.x * f; a.y += x.y * f; a.z += x.z * f; a.w += x.w * f;
     }
     float4 o = make_float4(a.x / lt, a.y / lt, a.z / lt, a.w / lt);

@@ -308,7 +308,7 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
   a.q = s.q; a.ldq = qd; a.out = s.attn; a.ldo = qd; a.kv = io.kv; a.rp = io.rp;
   a.heads = io.heads; a.kv_heads = io.kvh; a.M = io.M; a.nsplit = io.nsplit;
   if (a.nsplit > 1) {
-    const size_t need = (size_t)io.M * io.kvh * a.nsplit * (io.heads / io.kvh) * (2 + kHeadDim);
+    const size_t need = (size_t)io.M * io.kvh * a.nsplit * (io.heads / io.kvh) * kAttnRec;
     if (need > s.apart_floats || (size_t)io.M * io.kvh > s.n_acounters)
       return fail(QTTS_ERR_OOM, "attention split scratch too small");
     a.part = s.apart;
@@ -932,6 +932,10 @@ static int gemv_dev(const uint8_t* packed, const uint16_t* scales, int k, int n,
                     void* scratch, size_t scratch_bytes, cudaStream_t st) {
   if (!packed || !scales || !x || !y || k <= 0 || n <= 0 || m <= 0 || n % 32)
     return fail(QTTS_ERR_BADARG, "bad gemv arguments (n must be a multiple of 32)");
+  if (reinterpret_cast<uintptr_t>(packed) % 16 || reinterpret_cast<uintptr_t>(scales) % 2 ||
+      reinterpret_cast<uintptr_t>(x) % 4 || reinterpret_cast<uintptr_t>(y) % 4 ||
+      reinterpret_cast<uintptr_t>(scratch) % 16)
+    return fail(QTTS_ERR_BADARG, "packed and scratch must be 16-byte aligned, x/y 4-byte, scales 2-byte");
   GemvDesc g;
   gemv_plan_standalone(k, n, m, g);
   g.mat[0].packed = packed;

@@ -13,6 +13,7 @@ constexpr int kPageSize = 16;      // KV positions per page
 constexpr int kTileN = 256;        // GEMV columns per CTA tile (8 Q4 groups of 32)
 constexpr int kGemvThreads = 256;  // 8 warps
 constexpr int kMaxGroups = 16;     // codes per frame (1 semantic + 15 acoustic)
+constexpr int kAttnRec = 4 + 128;  // attention split record: m, l, pad, acc[128]
 
 // One Q4 g32 weight in its on-disk [k][n] layout (gemv.rs:26-31).
 struct Q4Mat {
@@ -161,7 +162,7 @@ struct AttnDesc {
   int heads = 0, kv_heads = 0;
   int M = 1;
   int nsplit = 1;
-  float* part = nullptr;        // [M][kv_heads][nsplit][2 + 2*G + G*128]
+  float* part = nullptr;        // [M][kv_heads][nsplit][G][kAttnRec]
   unsigned* counters = nullptr; // [M][kv_heads]
 };
 cudaError_t launch_attention(const AttnDesc& d, cudaStream_t st);
