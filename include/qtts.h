@@ -145,6 +145,24 @@ QTTS_API size_t qtts_q4_gemv_scratch_bytes(int k, int n, int m);
 QTTS_API int qtts_q4_gemv_dev(const uint8_t* packed_dev, const uint16_t* scales_dev, int k, int n,
                      const float* x_dev, int m, float* y_dev, void* scratch_dev,
                      size_t scratch_bytes, void* stream);
+/* No counterpart in the reference.  qtts_q4_gemv_dev for callers that cannot
+ * allocate device memory: a real-time audio thread that may not block inside
+ * a driver allocation, or a host whose GPU memory is already owned by another
+ * framework's caching allocator, where a fresh cudaMalloc can fail or
+ * fragment that pool.  The split-K scratch (tile counters, then partial sums)
+ * comes from a static device array of QTTS_Q4_GEMV_NOALLOC_SCRATCH_BYTES that
+ * every GPU loading the library holds until exit; the caller passes only
+ * inputs and outputs, and the call allocates nothing.  The first call on a
+ * device looks up the array's device address and sets the kernels' shared-
+ * memory attributes, so make that first call before any stream capture.
+ * Every call on a device shares the array, which keeps the last call's
+ * contents: the counters are cleared on each call and the partial sums are
+ * rewritten before they are read, but calls that overlap on the GPU (other
+ * streams or threads) race on it and must be serialised by the caller.
+ * Shapes whose scratch exceeds the array return QTTS_ERR_RANGE. */
+#define QTTS_Q4_GEMV_NOALLOC_SCRATCH_BYTES (4u << 20)
+QTTS_API int qtts_q4_gemv_dev_noalloc(const uint8_t* packed_dev, const uint16_t* scales_dev, int k, int n,
+                                      const float* x_dev, int m, float* y_dev, void* stream);
 /* Same contract with host buffers (copies in, runs, copies out). */
 QTTS_API int qtts_q4_gemv(const uint8_t* packed, const uint16_t* scales, int k, int n, const float* x,
                  int m, float* y);

@@ -241,7 +241,7 @@ static GemvDesc gemv_base(int epi, std::initializer_list<Q4Mat> mats, bool paire
 
 // Split-K choice: about two CTAs per SM, slices of whole 32-row blocks, at
 // most 2048 rows per slice (shared-memory bound of the input slice).
-static void choose_split(int sm_count, GemvDesc& g) {
+void choose_split(int sm_count, GemvDesc& g) {
   g.mb = g.paired ? (g.M >= 2 ? 2 : 1) : (g.M >= 3 ? 4 : (g.M == 2 ? 2 : 1));
   const int zb = ceil_div(g.M, g.mb);
   const int target = 2 * sm_count;
