@@ -11,9 +11,14 @@
 // Grid: (M * kv_heads, nsplit).  A CTA of 4 warps takes one KV head (and its
 // G = heads/kv_heads query heads) over one slice of positions; warps stride
 // over positions, a lane owns 4 of the 128 dims.  Slices are combined by the
-// last CTA of the (row, head) in slice order (deterministic).
+// root CTA of the (row, head) cluster over distributed shared memory, in
+// slice order (deterministic).
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "kernels.h"
+
+namespace cg = cooperative_groups;
 
 namespace qtts {
 
@@ -27,6 +32,8 @@ __device__ __forceinline__ const float* kv_row_c(const KvDesc& kv, int sess, int
 
 template <int G>
 __global__ void __launch_bounds__(128) attn_kernel(const AttnDesc d) {
+  pdl_launch_dependents();
+  pdl_wait();
   constexpr int NW = 4;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int m = blockIdx.x / d.kv_heads, h = blockIdx.x % d.kv_heads;
@@ -99,10 +106,9 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnDesc d) {
   __syncthreads();
   // thread t < G*32 finalises (g = t/32, dims 4*(t%32)..)
   const int nsp = d.nsplit;
-  // per (split, g) record: m, l, 2 pad, acc[128] -- 132 floats keeps the
-  // float4 accumulator stores 16-byte aligned
-  const size_t rec = kAttnRec;
-  float* part = d.part ? d.part + ((size_t)(m * d.kv_heads + h) * nsp) * G * rec : nullptr;
+  // per (g) record of this CTA: m, l, 2 pad, acc[128] -- 132 floats keeps
+  // the float4 accumulator stores 16-byte aligned
+  __shared__ __align__(16) float s_rec[G][kAttnRec];
   if (tid < G * 32) {
     const int g = tid / 32, ln = tid % 32;
     float M = -INFINITY;
@@ -119,53 +125,58 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnDesc d) {
       float4 o = make_float4(a.x / lt, a.y / lt, a.z / lt, a.w / lt);
       *reinterpret_cast<float4*>(d.out + (size_t)m * d.ldo + (h * G + g) * kHeadDim + 4 * ln) = o;
     } else {
-      float* r = part + ((size_t)split * G + g) * rec;
-      if (ln == 0) { r[0] = M; r[1] = lt; }
-      *reinterpret_cast<float4*>(r + 4 + 4 * ln) = a;
+      if (ln == 0) { s_rec[g][0] = M; s_rec[g][1] = lt; }
+      *reinterpret_cast<float4*>(&s_rec[g][4 + 4 * ln]) = a;
     }
   }
   if (nsp == 1) return;
-  __threadfence();
-  __syncthreads();
-  __shared__ unsigned s_ticket;
-  unsigned* ctr = d.counters + (size_t)m * d.kv_heads + h;
-  if (tid == 0) s_ticket = atomicAdd(ctr, 1u);
-  __syncthreads();
-  if (s_ticket != (unsigned)(nsp - 1)) return;
-  __threadfence();
-  if (tid < G * 32) {
+  // the nsplit CTAs of this (row, head) form one cluster: the root combines
+  // the slices over distributed shared memory in slice order
+  cg::cluster_group cl = cg::this_cluster();
+  cl.sync();
+  const bool root = cl.block_rank() == 0;
+  if (root && tid < G * 32) {
     const int g = tid / 32, ln = tid % 32;
     float M = -INFINITY;
-    for (int sp = 0; sp < nsp; ++sp) M = fmaxf(M, __ldcg(part + ((size_t)sp * G + g) * rec));
+    for (int sp = 0; sp < nsp; ++sp) M = fmaxf(M, cl.map_shared_rank(&s_rec[g][0], sp)[0]);
     float lt = 0.0f;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int sp = 0; sp < nsp; ++sp) {
-      const float* r = part + ((size_t)sp * G + g) * rec;
-      const float ls = __ldcg(r + 1);
+      const float* r = cl.map_shared_rank(&s_rec[g][0], sp);
+      const float ls = r[1];
       if (!(ls > 0.0f)) continue;
-      const float f = expf(__ldcg(r) - M);
+      const float f = expf(r[0] - M);
       lt += ls * f;
-      const float4 x = __ldcg(reinterpret_cast<const float4*>(r + 4) + ln);
+      const float4 x = reinterpret_cast<const float4*>(r + 4)[ln];
       a.x += x.x * f; a.y += x.y * f; a.z += x.z * f; a.w += x.w * f;
     }
     float4 o = make_float4(a.x / lt, a.y / lt, a.z / lt, a.w / lt);
     *reinterpret_cast<float4*>(d.out + (size_t)m * d.ldo + (h * G + g) * kHeadDim + 4 * ln) = o;
   }
-  if (tid == 0) *ctr = 0u;
+  cl.sync();  // peers keep their records until the root has read them
 }
 
 cudaError_t launch_attention(const AttnDesc& d, cudaStream_t st) {
   if (d.kv_heads <= 0 || d.heads % d.kv_heads) return cudaErrorInvalidValue;
-  if (d.nsplit > 1 && (!d.part || !d.counters)) return cudaErrorInvalidValue;
+  if (d.nsplit < 1 || d.nsplit > kMaxClusterSplits) return cudaErrorInvalidValue;
   const int G = d.heads / d.kv_heads;
   const dim3 grid(d.M * d.kv_heads, d.nsplit);
+  LaunchOpts o;
+  o.pdl = true;
+  o.cluster_y = (unsigned)d.nsplit;
   switch (G) {
-    case 1: attn_kernel<1><<<grid, 128, 0, st>>>(d); break;
-    case 2: attn_kernel<2><<<grid, 128, 0, st>>>(d); break;
-    case 4: attn_kernel<4><<<grid, 128, 0, st>>>(d); break;
+    case 1: return launch_k(attn_kernel<1>, grid, dim3(128), 0, st, o, d);
+    case 2: return launch_k(attn_kernel<2>, grid, dim3(128), 0, st, o, d);
+    case 4: return launch_k(attn_kernel<4>, grid, dim3(128), 0, st, o, d);
     default: return cudaErrorInvalidValue;
   }
-  return cudaGetLastError();
+}
+
+void attn_init_attributes() {
+  cudaFuncSetAttribute(attn_kernel<1>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaFuncSetAttribute(attn_kernel<2>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaFuncSetAttribute(attn_kernel<4>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaGetLastError();
 }
 
 }  // namespace qtts

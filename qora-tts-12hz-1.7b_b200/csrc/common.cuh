@@ -10,6 +10,12 @@ namespace qtts {
 
 __device__ __forceinline__ float h2f(__half h) { return __half2float(h); }  // exact (half::to_f32)
 
+// Programmatic dependent launch: let the next kernel in the stream launch now;
+// wait until the previous kernel has completed and its writes are visible.
+// Both are no-ops for kernels launched without the PDL attribute.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // 16-byte read-only streaming load (weights are read once per frame).
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
   uint4 r;

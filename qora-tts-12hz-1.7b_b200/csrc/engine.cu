@@ -20,6 +20,16 @@ namespace qtts {
 
 static thread_local std::string g_err;
 void set_error(const std::string& msg) { g_err = msg; }
+
+// Programmatic dependent launch for the frame's kernels; QTTS_PDL=0 turns it
+// off (A/B measurements).
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("QTTS_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 int fail(int code, const std::string& msg) {
   g_err = msg;
   return code;
@@ -102,6 +112,7 @@ DLayer mk_layer(char* base, const LOff& o) {
 }  // namespace
 
 void gemv_init_attributes();
+void attn_init_attributes();
 
 static int model_load(const char* path, int device, Model** out) {
   HModel hm;
@@ -209,6 +220,7 @@ static int model_load(const char* path, int device, Model** out) {
     return fail(QTTS_ERR_CUDA, "cannot upload the embedding table list");
   }
   gemv_init_attributes();
+  attn_init_attributes();
   *out = m;
   return QTTS_OK;
 }
@@ -246,7 +258,7 @@ void choose_split(int sm_count, GemvDesc& g) {
   const int zb = ceil_div(g.M, g.mb);
   const int target = 2 * sm_count;
   int S = (int)std::lround((double)target / (double)(g.ntiles * zb));
-  S = std::max(1, std::min(S, ceil_div(g.k, 32)));
+  S = std::max(1, std::min(std::min(S, kMaxClusterSplits), ceil_div(g.k, 32)));
   int rps = ceil_div(ceil_div(g.k, S), 32) * 32;
   rps = std::min(rps, 2048);
   g.rows_per_split = rps;
@@ -255,16 +267,8 @@ void choose_split(int sm_count, GemvDesc& g) {
 
 static int plan_gemv(Session& s, GemvDesc& g) {
   choose_split(s.m->sm_count, g);
-  while (g.S > 1 && (size_t)g.S * g.M * g.ncols > s.part_floats) {
-    g.rows_per_split = std::min(2048, g.rows_per_split * 2);
-    const int S2 = ceil_div(g.k, g.rows_per_split);
-    if (S2 == g.S) break;
-    g.S = S2;
-  }
-  if (g.S > 1) {
-    if ((size_t)g.S * g.M * g.ncols > s.part_floats) return fail(QTTS_ERR_OOM, "split-K scratch too small");
-    g.part = s.part;
-  }
+  g.cluster = 1;  // split-K partials reduced over distributed shared memory
+  g.pdl = 1;
   const size_t zb = (size_t)ceil_div(g.M, g.mb);
   if ((size_t)g.ntiles * zb > s.n_counters || zb > 4096) return fail(QTTS_ERR_OOM, "tile counter array too small");
   g.counters = s.counters;
@@ -289,6 +293,11 @@ struct LayerIO {
   int rope_rows = 0, skip_oob = 0;
   int heads = 0, kvh = 0, inter = 0;
   int nsplit = 1;
+  // per-256-column sums of squares of the residual rows (row stride kSsqLd):
+  // written by every residual epilogue, read by the next RMSNorm prologue;
+  // ssq_valid = 0 when the input rows came without them (host copies)
+  float* ssq = nullptr;
+  int ssq_valid = 0;
 };
 
 // One transformer layer (talker.rs:279-349 / code_predictor.rs:448-502):
@@ -296,8 +305,20 @@ struct LayerIO {
 // RMSNorm+gate/up+SwiGLU | down+residual.
 static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const LayerIO& io) {
   const int qd = io.heads * kHeadDim;
+  const int nt = ceil_div(io.ldx > 0 ? L.q.k : 0, kTileN);  // tiles of a residual row
+  auto use_ssq = [&](GemvDesc& gd, bool valid) {
+    if (io.ssq && valid) {
+      gd.ssq_in = io.ssq; gd.ssq_ld = kSsqLd; gd.ssq_n = nt;
+    }
+  };
+  auto emit_ssq = [&](GemvDesc& gd) {
+    if (io.ssq) {
+      gd.epi.ssq_out = io.ssq; gd.epi.ssq_ld = kSsqLd;
+    }
+  };
   GemvDesc g = gemv_base(EPI_QKV, {L.q, L.k, L.v}, false, io.M);
   g.X = io.X; g.ldx = io.ldx; g.gamma = L.in_norm;
+  use_ssq(g, io.ssq_valid != 0);
   g.epi.q_out = s.q; g.epi.ldq = qd; g.epi.q_norm = L.q_norm; g.epi.k_norm = L.k_norm;
   g.epi.rope_cos = io.cos; g.epi.rope_sin = io.sin; g.epi.rope_rows = io.rope_rows; g.epi.rope_skip_oob = io.skip_oob;
   g.epi.heads = io.heads; g.epi.kv_heads = io.kvh; g.epi.kv = io.kv; g.epi.rp = io.rp; g.epi.err_flag = s.err_flag;
@@ -318,16 +339,19 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
 
   GemvDesc o = gemv_base(EPI_RESID, {L.o}, false, io.M);
   o.X = s.attn; o.ldx = qd; o.epi.out = io.X; o.epi.ldo = io.ldx;
+  emit_ssq(o);
   RC(plan_gemv(s, o));
   ops.push_back(gemv_op(o));
 
   GemvDesc gu = gemv_base(EPI_SWIGLU, {L.gate, L.up}, true, io.M);
   gu.X = io.X; gu.ldx = io.ldx; gu.gamma = L.post_norm; gu.epi.out = s.h; gu.epi.ldo = io.inter;
+  use_ssq(gu, true);
   RC(plan_gemv(s, gu));
   ops.push_back(gemv_op(gu));
 
   GemvDesc dn = gemv_base(EPI_RESID, {L.down}, false, io.M);
   dn.X = s.h; dn.ldx = io.inter; dn.epi.out = io.X; dn.epi.ldo = io.ldx;
+  emit_ssq(dn);
   RC(plan_gemv(s, dn));
   ops.push_back(gemv_op(dn));
   return QTTS_OK;
@@ -348,27 +372,34 @@ static KvDesc pred_kv(Session& s, int layer) {
 static int talker_nsplit(Session& s, int M) {
   const int byL = ceil_div(s.maxP, 64);
   const int byPar = std::max(1, ceil_div(4L * s.m->sm_count, (long)M * s.m->d.t_kv_heads));
-  return std::max(1, std::min(32, std::min(byL, byPar)));
+  return std::max(1, std::min(kMaxClusterSplits, std::min(byL, byPar)));
 }
 
 // Talker layers over rows X (decode: one row per session; prefill: seq rows).
-static int add_talker(Session& s, std::vector<Op>& ops, float* X, long ldx, int M, const RowPos& rp, int nsplit) {
+// ssq0: sums of squares of the input rows when their producer left them.
+static int add_talker(Session& s, std::vector<Op>& ops, float* X, long ldx, int M, const RowPos& rp, int nsplit,
+                      bool ssq0) {
   const Model& m = *s.m;
   for (int l = 0; l < m.d.t_layers; ++l) {
     LayerIO io;
     io.X = X; io.ldx = ldx; io.M = M; io.rp = rp; io.kv = talker_kv(s, l);
     io.cos = m.t_cos; io.sin = m.t_sin; io.rope_rows = m.d.t_max_pos; io.skip_oob = 0;
     io.heads = m.d.t_heads; io.kvh = m.d.t_kv_heads; io.inter = m.d.t_inter; io.nsplit = nsplit;
+    io.ssq = s.ssq_t;
+    io.ssq_valid = (l > 0 || ssq0) ? 1 : 0;
     RC(add_layer(s, ops, m.tl[l], io));
   }
   return QTTS_OK;
 }
 
 // final norm + codec_head (talker.rs:353-354): logits and the normed hidden.
+// Rows X are the talker residual rows whose sums of squares are in s.ssq_t
+// (row r of X <-> ssq row ssq_row0 + r * ssq_rows_step).
 static int add_codec_head(Session& s, std::vector<Op>& ops, const float* X, long ldx, int M, float* logits,
-                          float* hid, long ldh) {
+                          float* hid, long ldh, long ssq_row0 = 0, long ssq_rows_step = 1) {
   GemvDesc g = gemv_base(EPI_STORE, {s.m->codec_head}, false, M);
   g.X = X; g.ldx = ldx; g.gamma = s.m->t_final;
+  g.ssq_in = s.ssq_t + ssq_row0 * kSsqLd; g.ssq_ld = ssq_rows_step * kSsqLd; g.ssq_n = ceil_div(s.m->d.t_hidden, kTileN);
   g.epi.out = logits; g.epi.ldo = s.m->d.t_vocab;
   g.xnorm_out = hid; g.ld_xnorm = ldh;
   RC(plan_gemv(s, g));
@@ -384,32 +415,37 @@ static int add_predictor(Session& s, std::vector<Op>& ops, int B, bool frame_mod
   const qtts_dims& d = m.d;
   const int pH = d.p_hidden;
   // project_input of both prefill rows (code_predictor.rs:235-236)
+  const int pnt = ceil_div(pH, kTileN);
   GemvDesc pj = gemv_base(EPI_STORE, {m.input_proj}, false, 2 * B);
   pj.X = s.pin; pj.ldx = d.t_hidden; pj.epi.out = s.px; pj.epi.ldo = pH; pj.epi.bias = m.input_proj_b;
+  pj.epi.ssq_out = s.ssq_p; pj.epi.ssq_ld = kSsqLd;
   RC(plan_gemv(s, pj));
   ops.push_back(gemv_op(pj));
-  auto layers = [&](float* X, int M, const RowPos& rp) -> int {
+  auto layers = [&](float* X, int M, const RowPos& rp, float* ssq) -> int {
     for (int l = 0; l < d.p_layers; ++l) {
       LayerIO io;
       io.X = X; io.ldx = pH; io.M = M; io.rp = rp; io.kv = pred_kv(s, l);
       io.cos = m.p_cos; io.sin = m.p_sin; io.rope_rows = d.p_max_pos; io.skip_oob = 1;
       io.heads = d.p_heads; io.kvh = d.p_kv_heads; io.inter = d.p_inter; io.nsplit = 1;
+      io.ssq = ssq; io.ssq_valid = 1;  // every input row comes from a projection epilogue
       RC(add_layer(s, ops, m.pl[l], io));
     }
     return QTTS_OK;
   };
   RowPos rp0;
   rp0.rows_per_sess = 2;  // prefill positions 0, 1 (code_predictor.rs:244, :369)
-  RC(layers(s.px, 2 * B, rp0));
-  auto head = [&](const float* X, long ldx, int g) -> int {  // final norm + lm_heads[g] + argmax
+  RC(layers(s.px, 2 * B, rp0, s.ssq_p));
+  auto head = [&](const float* X, long ldx, int g, const float* ssq, long ssq_ld) -> int {
+    // final norm + lm_heads[g] + argmax
     GemvDesc h = gemv_base(EPI_ARGMAX, {m.lm[g]}, false, B);
     h.X = X; h.ldx = ldx; h.gamma = m.p_final;
+    h.ssq_in = ssq; h.ssq_ld = ssq_ld; h.ssq_n = pnt;
     h.epi.group = g + 1; h.epi.frame_codes = frame_mode ? 1 : 0; h.epi.codes_plain = s.codes_plain;
     RC(plan_gemv(s, h));
     ops.push_back(gemv_op(h, fc));
     return QTTS_OK;
   };
-  RC(head(s.px + pH, 2L * pH, 0));
+  RC(head(s.px + pH, 2L * pH, 0, s.ssq_p + kSsqLd, 2L * kSsqLd));
   for (int g = 1; g < d.p_groups; ++g) {  // code_predictor.rs:253-270
     GemvDesc pe = gemv_base(EPI_STORE, {m.input_proj}, false, B);
     pe.emb = m.p_emb[g - 1];
@@ -421,12 +457,13 @@ static int add_predictor(Session& s, std::vector<Op>& ops, int B, bool frame_mod
       pe.emb_idx_stride = kMaxGroups;
     }
     pe.epi.out = s.px1; pe.epi.ldo = pH; pe.epi.bias = m.input_proj_b;
+    pe.epi.ssq_out = s.ssq_p1; pe.epi.ssq_ld = kSsqLd;
     RC(plan_gemv(s, pe));
     ops.push_back(gemv_op(pe));
     RowPos rp;
     rp.pos_const = g + 1;
-    RC(layers(s.px1, B, rp));
-    RC(head(s.px1, pH, g));
+    RC(layers(s.px1, B, rp, s.ssq_p1));
+    RC(head(s.px1, pH, g, s.ssq_p1, kSsqLd));
   }
   return QTTS_OK;
 }
@@ -501,7 +538,7 @@ static void session_free_all(Session* s) {
   free_generation(*s);
   void* bufs[] = {s->kv_pool, s->page_table, s->pkv_pool, s->slots, s->x, s->pin, s->q, s->attn, s->h,
                   s->px, s->px1, s->logits, s->xpre, s->hid1, s->part, s->counters, s->counters2, s->keys,
-                  s->apart, s->acounters, s->err_flag, s->codes_plain, s->io};
+                  s->apart, s->acounters, s->err_flag, s->codes_plain, s->io, s->ssq_t, s->ssq_p, s->ssq_p1};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (s->st) cudaStreamDestroy(s->st);
@@ -556,6 +593,9 @@ static int session_create(Model* m, int maxB, int maxP, Session** out) {
   A(&s->codes_plain, (size_t)maxB * kMaxGroups);
   s->io_floats = (size_t)s->rows * d.t_hidden + 2 * d.t_hidden + d.t_vocab + 64;
   A(&s->io, s->io_floats);
+  A(&s->ssq_t, (size_t)s->rows * kSsqLd);
+  A(&s->ssq_p, (size_t)2 * maxB * kSsqLd);
+  A(&s->ssq_p1, (size_t)maxB * kSsqLd);
   if (rc == QTTS_OK) {  // pages: slot b owns pages [b*pps, (b+1)*pps)
     std::vector<int> pt((size_t)maxB * s->pages_per_sess);
     for (size_t i = 0; i < pt.size(); ++i) pt[i] = (int)i;
@@ -600,11 +640,12 @@ static int build_frame_ops(Session& s, std::vector<Op>& ops, bool dumps) {
   FuseDesc fd;
   fd.x = s.x; fd.ldx = H; fd.codec_emb = m.codec_emb; fd.group_emb = m.d_group_emb; fd.n_groups = d.p_groups;
   fd.trail = s.trail; fd.max_trail = s.max_trail; fd.tts_pad = s.tts_pad; fd.B = B; fd.H = H; fd.fc = fc;
+  fd.ssq_out = s.ssq_t; fd.ssq_ld = kSsqLd;
   ops.push_back([fd](cudaStream_t st) { return launch_fuse(fd, st); });
   RowPos rp;
   rp.pos_base = &s.slots[0].pos;
   rp.pos_stride = (int)(sizeof(SlotState) / sizeof(int));
-  RC(add_talker(s, ops, s.x, H, B, rp, talker_nsplit(s, B)));
+  RC(add_talker(s, ops, s.x, H, B, rp, talker_nsplit(s, B), true));
   RC(add_codec_head(s, ops, s.x, H, B, s.logits, s.pin, 2L * H));
   ops.push_back([slots, B](cudaStream_t st) { return launch_frame_end(slots, B, st); });
   return QTTS_OK;
@@ -731,9 +772,9 @@ static int generate_begin(Session& s, int n, const qtts_utterance* u, int F, uns
     RowPos rp;
     rp.rows_per_sess = sq;
     rp.sess0 = b0;
-    RC(add_talker(s, ops, X, H, nb * sq, rp, 1));
+    RC(add_talker(s, ops, X, H, nb * sq, rp, 1, false));
     RC(add_codec_head(s, ops, X + (size_t)(sq - 1) * H, (long)sq * H, nb, s.logits + (size_t)b0 * d.t_vocab,
-                      s.pin + (size_t)b0 * 2 * H, 2L * H));
+                      s.pin + (size_t)b0 * 2 * H, 2L * H, sq - 1, sq));
     RC(run_ops(s, ops));
     ops.clear();
     b0 = b1;
@@ -818,8 +859,8 @@ static int prefill_call(Session& s, const float* emb, int n, float* hid, float* 
   std::vector<Op> ops;
   RowPos rp;
   rp.rows_per_sess = n;
-  RC(add_talker(s, ops, s.xpre, H, n, rp, 1));
-  RC(add_codec_head(s, ops, s.xpre + (size_t)(n - 1) * H, H, 1, s.logits, s.hid1, H));
+  RC(add_talker(s, ops, s.xpre, H, n, rp, 1, false));
+  RC(add_codec_head(s, ops, s.xpre + (size_t)(n - 1) * H, H, 1, s.logits, s.hid1, H, n - 1, 1));
   RC(run_ops(s, ops));
   if (hid) CK(cudaMemcpyAsync(hid, s.hid1, sizeof(float) * H, cudaMemcpyDeviceToHost, s.st));
   if (logits) CK(cudaMemcpyAsync(logits, s.logits, sizeof(float) * m.d.t_vocab, cudaMemcpyDeviceToHost, s.st));
@@ -840,7 +881,7 @@ static int talker_step_call(Session& s, const float* emb, int position, float* o
   RowPos rp;
   rp.pos_const = position;
   rp.kv_const = s.kvlen0;
-  RC(add_talker(s, ops, s.x, H, 1, rp, talker_nsplit(s, 1)));
+  RC(add_talker(s, ops, s.x, H, 1, rp, talker_nsplit(s, 1), false));
   RC(add_codec_head(s, ops, s.x, H, 1, s.logits, s.hid1, H));
   RC(run_ops(s, ops));
   CK(cudaMemcpyAsync(out, s.hid1, sizeof(float) * H, cudaMemcpyDeviceToHost, s.st));
@@ -948,6 +989,7 @@ static int gemv_dev(const uint8_t* packed, const uint16_t* scales, int k, int n,
   if (!scratch || scratch_bytes < need) return fail(QTTS_ERR_BADARG, "scratch smaller than qtts_q4_gemv_scratch_bytes()");
   g.counters = reinterpret_cast<unsigned*>(scratch);
   g.part = reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + kCounterBytes);
+  g.cluster = 1;
   gemv_init_attributes();
   const cudaError_t e = launch_gemv(g, FrameCodes{}, st);
   if (e != cudaSuccess) return fail(QTTS_ERR_CUDA, cudaGetErrorString(e));

@@ -71,6 +71,9 @@ struct Session {
   // per-call API
   int kvlen0 = 0;
   float* io = nullptr;  // staging [io_floats]
+  // per-256-column sums of squares of residual rows (talker, predictor
+  // prefill rows, predictor decode rows), row stride kSsqLd
+  float *ssq_t = nullptr, *ssq_p = nullptr, *ssq_p1 = nullptr;
   size_t io_floats = 0;
   // generation
   int B = 0, max_frames = 0, max_trail = 0;

@@ -6,17 +6,30 @@
 // (gemm_q4) and fuses the per-step glue of talker.rs:279-349 and
 // code_predictor.rs:448-505 around them.
 //
-// Work decomposition.  The weight is [k][n] with groups of 32 along n, so an
-// output column needs all k rows.  A CTA owns a 256-column tile (8 groups)
-// and a contiguous slice of rows (split-K).  A warp load covers 4 rows x 128
-// bytes (lane = (row quad, group)); a lane keeps 32 column accumulators per
-// input row in registers.  Rows of the slice are interleaved across the 8
-// warps.  After the slice, lanes reduce over their 4 row offsets with
-// shuffles, warps reduce through shared memory, and the CTA writes its
-// partial.  The last CTA of each tile (atomic ticket) sums the partials in
-// split order -- the result is deterministic -- and runs the epilogue.
+// Work decomposition (both kernels).  The weight is [k][n] with groups of 32
+// along n, so an output column needs all k rows.  A CTA owns a 256-column
+// tile (8 groups) and a contiguous slice of rows (split-K).  A warp load
+// covers 4 rows x 128 bytes (lane = (row offset rr, group gi)); a lane keeps
+// 32 column accumulators per input row.  The S CTAs of a tile form a
+// thread-block cluster and reduce their partials in split order
+// (deterministic).
+//
+// gemv_dec_kernel (one input row, the batch-1 decode path) is shaped for
+// latency: every weight row of a lane is loaded into registers before the
+// programmatic-dependent-launch wait (weights are never written by an earlier
+// kernel; the next kernel is released once this one's FMAs are done), the
+// RMSNorm scale comes from per-tile sums of squares left by the
+// producer of the row, the CTA reduces through shared memory, and the
+// cluster reduction pushes each partial straight into the root CTA's shared
+// memory followed by a single cluster barrier.
+//
+// gemv_q4_kernel (M rows, MB per CTA) serves prefill and batched decode.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "kernels.h"
+
+namespace cg = cooperative_groups;
 
 namespace qtts {
 
@@ -44,207 +57,52 @@ __device__ __forceinline__ float* kv_row(const KvDesc& kv, int sess, int pos, in
   return kv.pool + (blk * kPageSize + (pos % kPageSize)) * kHeadDim;
 }
 
-}  // namespace
+__device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
 
+// RMSNorm scale of a row from the producer's per-tile sums of squares.
+__device__ __forceinline__ float inv_rms_from_ssq(const GemvDesc& d, int m) {
+  const float* p = d.ssq_in + (size_t)m * d.ssq_ld;
+  float ss = 0.0f;
+  for (int t = 0; t < d.ssq_n; ++t) ss += p[t];
+  return 1.0f / sqrtf(ss / (float)d.k + 1e-6f);
+}
+
+// ---------------------------------------------------------------------------
+// Epilogues, run by the root CTA of a tile with v[a][mm] = column tcol+tid of
+// matrix a for input row m0+mm.  All 256 threads take part.
 template <int MB, int NM, int EPI>
-__global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvDesc d, const FrameCodes fc) {
-  extern __shared__ __align__(16) float sm[];
+__device__ __forceinline__ void gemv_epilogue(const GemvDesc& d, const FrameCodes& fc, float (&v)[NM][MB], int mat,
+                                              int tile, int tcol, int m0, int mcnt, int zb, float* sbuf,
+                                              float* ybuf) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int tile = blockIdx.x, split = blockIdx.y, zb = blockIdx.z;
-  const int RPS = d.rows_per_split;
-  float* xs = sm;                               // [MB][RPS]
-  float* red = xs + MB * RPS;                   // [8][NM][MB][256]
-  float* sbuf = red + 8 * NM * MB * kTileN;     // 64 floats
-  float* ybuf = sbuf + 64;                      // [MB][256] (QKV epilogue)
-
-  int mat = 0;
-  if (NM == 1) {
-    while (mat + 1 < d.nmat && tile >= d.tile0[mat + 1]) ++mat;
-  }
-  const int tcol = (NM == 2 ? tile : tile - d.tile0[mat]) * kTileN;
   const int n = d.mat[mat].n;
-  const int r0 = split * RPS;
-  const int r1 = min(d.k, r0 + RPS);
-  const int R = max(0, r1 - r0);
-  const int m0 = zb * MB;
-  const int mcnt = min(MB, d.M - m0);
-
-  // ---- prologue: rows [m0, m0+mcnt) x k-slice [r0, r1) -> shared memory
-  for (int mm = 0; mm < MB; ++mm) {
-    float* xd = xs + mm * RPS;
-    if (mm >= mcnt) {
-      for (int i = tid; i < R; i += kGemvThreads) xd[i] = 0.0f;
-      continue;
-    }
-    const int m = m0 + mm;
-    if (d.emb_idx) {
-      const uint32_t row = d.emb_idx[(size_t)m * d.emb_idx_stride];
-      const uint8_t* prow = d.emb.packed + (size_t)row * (d.emb.n / 2);
-      const __half* srow = d.emb.scales + (size_t)row * (d.emb.n / 32);
-      for (int i = tid; i < R; i += kGemvThreads) xd[i] = q4_value(prow, srow, r0 + i);
-    } else {
-      const float* xr = d.X + (size_t)m * d.ldx;
-      if (d.gamma) {
-        float ss = 0.0f;
-        for (int i = tid; i < d.k; i += kGemvThreads) ss += xr[i] * xr[i];
-        ss = block_sum_256(ss, sbuf);
-        const float inv = 1.0f / sqrtf(ss / (float)d.k + 1e-6f);
-        for (int i = tid; i < R; i += kGemvThreads) xd[i] = xr[r0 + i] * inv * h2f(d.gamma[r0 + i]);
-        if (d.xnorm_out && tile == 0)
-          for (int i = tid; i < R; i += kGemvThreads) d.xnorm_out[(size_t)m * d.ld_xnorm + r0 + i] = xd[i];
-      } else {
-        for (int i = tid; i < R; i += kGemvThreads) xd[i] = xr[r0 + i];
-      }
-    }
-  }
-  __syncthreads();
-
-  // ---- main loop: stream the Q4 slice, accumulate 32 columns per lane
-  const int rr = lane >> 3, gi = lane & 7;
-  const int gcol = tcol + gi * 32;
-  const bool gval = gcol < n;
-  const size_t rowbytes = (size_t)n / 2;
-  const int ngr = n / 32;
-  float2 acc[NM][MB][16];
-#pragma unroll
-  for (int a = 0; a < NM; ++a)
-#pragma unroll
-    for (int b = 0; b < MB; ++b)
-#pragma unroll
-      for (int c = 0; c < 16; ++c) acc[a][b][c] = make_float2(0.0f, 0.0f);
-
-  constexpr int U = (NM * MB >= 4) ? 2 : 4;
-  for (int rb = warp * 4 + rr; rb < R; rb += 32 * U) {
-    uint4 w[U][NM];
-    float s[U][NM];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int rbu = rb + 32 * u;
-      const bool ok = gval && rbu < R;
-#pragma unroll
-      for (int a = 0; a < NM; ++a) {
-        const Q4Mat& Mt = d.mat[NM == 2 ? a : mat];
-        if (ok) {
-          const size_t r = (size_t)(r0 + rbu);
-          w[u][a] = ld_stream16(Mt.packed + r * rowbytes + gcol / 2);
-          s[u][a] = h2f(Mt.scales[r * ngr + gcol / 32]);
-        } else {
-          w[u][a] = make_uint4(0, 0, 0, 0);
-          s[u][a] = 0.0f;
-        }
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int rbu = rb + 32 * u;
-      if (rbu < R) {
-#pragma unroll
-        for (int mm = 0; mm < MB; ++mm) {
-          const float xv = xs[mm * RPS + rbu];
-#pragma unroll
-          for (int a = 0; a < NM; ++a) {
-            const SxPack p = make_sx(s[u][a] * xv);  // s = scale * x (gemv.rs:239)
-            q4_word_fma(w[u][a].x, p, &acc[a][mm][0]);
-            q4_word_fma(w[u][a].y, p, &acc[a][mm][4]);
-            q4_word_fma(w[u][a].z, p, &acc[a][mm][8]);
-            q4_word_fma(w[u][a].w, p, &acc[a][mm][12]);
-          }
-        }
-      }
-    }
-  }
-
-  // ---- reduce the 4 row offsets of a warp, then the 8 warps
-#pragma unroll
-  for (int a = 0; a < NM; ++a)
-#pragma unroll
-    for (int mm = 0; mm < MB; ++mm)
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        float2 v = acc[a][mm][c];
-        v.x += __shfl_xor_sync(0xffffffffu, v.x, 8);
-        v.y += __shfl_xor_sync(0xffffffffu, v.y, 8);
-        v.x += __shfl_xor_sync(0xffffffffu, v.x, 16);
-        v.y += __shfl_xor_sync(0xffffffffu, v.y, 16);
-        acc[a][mm][c] = v;
-      }
-  if (rr == 0) {
-#pragma unroll
-    for (int a = 0; a < NM; ++a)
-#pragma unroll
-      for (int mm = 0; mm < MB; ++mm) {
-        float4* dst = reinterpret_cast<float4*>(red + ((warp * NM + a) * MB + mm) * kTileN + gi * 32);
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          dst[c] = make_float4(acc[a][mm][2 * c].x, acc[a][mm][2 * c].y, acc[a][mm][2 * c + 1].x,
-                               acc[a][mm][2 * c + 1].y);
-      }
-  }
-  __syncthreads();
-  float v[NM][MB];
-#pragma unroll
-  for (int a = 0; a < NM; ++a)
-#pragma unroll
-    for (int mm = 0; mm < MB; ++mm) {
-      float t = 0.0f;
-#pragma unroll
-      for (int w8 = 0; w8 < 8; ++w8) t += red[((w8 * NM + a) * MB + mm) * kTileN + tid];
-      v[a][mm] = t;
-    }
-
-  const int col = tcol + tid;  // column within the matrix
+  const int col = tcol + tid;
   const bool cval = col < n;
-
-  // ---- split-K: deterministic last-CTA reduction
-  if (d.S > 1) {
-#pragma unroll
-    for (int a = 0; a < NM; ++a) {
-      const int cg = d.col0[NM == 2 ? a : mat] + col;
-#pragma unroll
-      for (int mm = 0; mm < MB; ++mm)
-        if (cval && mm < mcnt) d.part[((size_t)split * d.M + m0 + mm) * d.ncols + cg] = v[a][mm];
-    }
-    __threadfence();
-    __syncthreads();
-    __shared__ unsigned s_ticket;
-    unsigned* ctr = d.counters + (size_t)tile * gridDim.z + zb;
-    if (tid == 0) s_ticket = atomicAdd(ctr, 1u);
-    __syncthreads();
-    if (s_ticket != (unsigned)(d.S - 1)) return;
-    __threadfence();
-#pragma unroll
-    for (int a = 0; a < NM; ++a) {
-      const int cg = d.col0[NM == 2 ? a : mat] + col;
-#pragma unroll
-      for (int mm = 0; mm < MB; ++mm) {
-        float t = 0.0f;
-        if (cval && mm < mcnt)
-          for (int sp = 0; sp < d.S; ++sp) t += ld_cg(d.part + ((size_t)sp * d.M + m0 + mm) * d.ncols + cg);
-        v[a][mm] = t;
-      }
-    }
-    if (tid == 0) *ctr = 0u;
-  }
-
-  // ---- epilogues
   const EpiDesc& e = d.epi;
-  if (EPI == EPI_STORE) {
-    const int cg = d.col0[mat] + col;
+  if (EPI == EPI_STORE || EPI == EPI_RESID) {
+    const int cgl = d.col0[mat] + col;
+    const int ltile = (NM == 2 ? tile : tile - d.tile0[mat]);
 #pragma unroll
     for (int mm = 0; mm < MB; ++mm) {
-      if (!cval || mm >= mcnt) continue;
-      float val = v[0][mm];
-      if (e.bias) val = val + e.bias[cg];
-      if (e.act_silu) val = silu_ref(val);
-      e.out[(size_t)(m0 + mm) * e.ldo + cg] = val;
-    }
-  } else if (EPI == EPI_RESID) {
-    const int cg = d.col0[mat] + col;
-#pragma unroll
-    for (int mm = 0; mm < MB; ++mm) {
-      if (!cval || mm >= mcnt) continue;
-      float* o = e.out + (size_t)(m0 + mm) * e.ldo + cg;
-      *o = *o + v[0][mm];
+      float val = 0.0f;
+      if (cval && mm < mcnt) {
+        if (EPI == EPI_STORE) {
+          val = v[0][mm];
+          if (e.bias) val = val + e.bias[cgl];
+          if (e.act_silu) val = silu_ref(val);
+          e.out[(size_t)(m0 + mm) * e.ldo + cgl] = val;
+        } else {
+          float* o = e.out + (size_t)(m0 + mm) * e.ldo + cgl;
+          val = *o + v[0][mm];
+          *o = val;
+        }
+      }
+      if (e.ssq_out) {  // uniform branch: every thread takes part in the block sum
+        const float ss = block_sum_256(val * val, sbuf);
+        if (tid == 0 && mm < mcnt) e.ssq_out[(size_t)(m0 + mm) * e.ssq_ld + ltile] = ss;
+      }
     }
   } else if (EPI == EPI_SWIGLU) {
 #pragma unroll
@@ -353,27 +211,438 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvDesc d,
   }
 }
 
+// Weight words + raw f16 scales of U row-steps of one lane (NM matrices).
+template <int U, int NM>
+struct WBatch {
+  uint4 w[U][NM];
+  unsigned short s[U][NM];
+};
+
+template <int U, int NM>
+__device__ __forceinline__ void load_batch(WBatch<U, NM>& b, const GemvDesc& d, int mat, int r0, int R, int rb,
+                                           int gcol, bool gval, size_t rowbytes, int ngr) {
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int rbu = rb + 32 * u;
+    const bool ok = gval && rbu < R;
+#pragma unroll
+    for (int a = 0; a < NM; ++a) {
+      const Q4Mat& Mt = d.mat[NM == 2 ? a : mat];
+      if (ok) {
+        const size_t r = (size_t)(r0 + rbu);
+        b.w[u][a] = ld_stream16(Mt.packed + r * rowbytes + gcol / 2);
+        b.s[u][a] = __ldg(reinterpret_cast<const unsigned short*>(Mt.scales) + r * ngr + gcol / 32);
+      } else {
+        b.w[u][a] = make_uint4(0, 0, 0, 0);
+        b.s[u][a] = 0;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ float u16_h2f(unsigned short s) { return __half2float(__ushort_as_half(s)); }
+
+}  // namespace
+
+// ===========================================================================
+// M = 1 decode kernel
+template <int NM, int EPI, int NR>
+__global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d, const FrameCodes fc) {
+  extern __shared__ __align__(16) float sm[];
+  const bool clustered = d.cluster && d.S > 1;
+  if (clustered) cluster_arrive_relaxed();  // completes before any DSMEM store below
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x, split = blockIdx.y;
+  float* red = sm;                                  // [8 warps][4 rr][NM][256]
+  float* pbuf = red + 8 * 4 * NM * kTileN;          // [S][NM][256] partials pushed to the root
+  float* sbuf = pbuf + kMaxClusterSplits * NM * kTileN;  // 64 floats
+  float* ybuf = sbuf + 64;                          // [256]
+
+  int mat = 0;
+  if (NM == 1) {
+    while (mat + 1 < d.nmat && tile >= d.tile0[mat + 1]) ++mat;
+  }
+  const int tcol = (NM == 2 ? tile : tile - d.tile0[mat]) * kTileN;
+  const int n = d.mat[mat].n;
+  const int r0 = split * d.rows_per_split;
+  const int R = max(0, min(d.k, r0 + d.rows_per_split) - r0);
+  const int rr = lane >> 3, gi = lane & 7;
+  const int gcol = tcol + gi * 32;
+  const bool gval = gcol < n;
+  const int rb0 = warp * 4 + rr;
+
+  // every weight row of this lane, before waiting on the previous kernel
+  WBatch<NR, NM> wb;
+  load_batch<NR, NM>(wb, d, mat, r0, R, rb0, gcol, gval, (size_t)n / 2, n / 32);
+  pdl_wait();
+
+  // input values of this lane's rows (one dependent round trip)
+  float xv[NR];
+  if (d.emb_idx) {
+    const uint32_t row = d.emb_idx[0];
+    const uint8_t* prow = d.emb.packed + (size_t)row * (d.emb.n / 2);
+    const __half* srow = d.emb.scales + (size_t)row * (d.emb.n / 32);
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+      const int rb = rb0 + 32 * i;
+      xv[i] = rb < R ? q4_value(prow, srow, r0 + rb) : 0.0f;
+    }
+  } else {
+    float inv = 1.0f;
+    if (d.gamma) {
+      if (d.ssq_in) {
+        inv = inv_rms_from_ssq(d, 0);
+      } else {
+        float ss = 0.0f;
+        for (int i = tid; i < d.k; i += kGemvThreads) ss += d.X[i] * d.X[i];
+        ss = block_sum_256(ss, sbuf);
+        inv = 1.0f / sqrtf(ss / (float)d.k + 1e-6f);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+      const int rb = rb0 + 32 * i;
+      float x = 0.0f;
+      if (rb < R) {
+        x = d.X[r0 + rb];
+        if (d.gamma) x = x * inv * h2f(d.gamma[r0 + rb]);  // gemv.rs:414
+      }
+      xv[i] = x;
+    }
+    if (d.xnorm_out && tile == 0 && gi == 0) {
+#pragma unroll
+      for (int i = 0; i < NR; ++i) {
+        const int rb = rb0 + 32 * i;
+        if (rb < R) d.xnorm_out[r0 + rb] = xv[i];
+      }
+    }
+  }
+
+  float2 acc[NM][16];
+#pragma unroll
+  for (int a = 0; a < NM; ++a)
+#pragma unroll
+    for (int c = 0; c < 16; ++c) acc[a][c] = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int i = 0; i < NR; ++i) {
+    if (rb0 + 32 * i < R) {
+#pragma unroll
+      for (int a = 0; a < NM; ++a) {
+        const SxPack p = make_sx(u16_h2f(wb.s[i][a]) * xv[i]);  // s = scale * x (gemv.rs:239)
+        q4_word_fma(wb.w[i][a].x, p, &acc[a][0]);
+        q4_word_fma(wb.w[i][a].y, p, &acc[a][4]);
+        q4_word_fma(wb.w[i][a].z, p, &acc[a][8]);
+        q4_word_fma(wb.w[i][a].w, p, &acc[a][12]);
+      }
+    }
+  }
+
+  // Release the next kernel only now: its CTAs then prefetch their weights
+  // while this one reduces, without crowding out this kernel's own loads.
+  pdl_launch_dependents();
+  // CTA reduction through shared memory: 32 (warp, rr) partials per column
+#pragma unroll
+  for (int a = 0; a < NM; ++a) {
+    float4* dst = reinterpret_cast<float4*>(red + ((warp * 4 + rr) * NM + a) * kTileN + gi * 32);
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      dst[c] = make_float4(acc[a][2 * c].x, acc[a][2 * c].y, acc[a][2 * c + 1].x, acc[a][2 * c + 1].y);
+  }
+  __syncthreads();
+  float v[NM][1];
+#pragma unroll
+  for (int a = 0; a < NM; ++a) {
+    float t = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) t += red[(j * NM + a) * kTileN + tid];
+    v[a][0] = t;
+  }
+
+  if (clustered) {
+    cg::cluster_group cl = cg::this_cluster();
+    const int rank = (int)cl.block_rank();
+    cluster_wait();  // every CTA of the cluster is running: DSMEM is live
+    float* root = cl.map_shared_rank(pbuf, 0);
+#pragma unroll
+    for (int a = 0; a < NM; ++a) root[(rank * NM + a) * kTileN + tid] = v[a][0];
+    cluster_arrive_release();
+    cluster_wait();
+    if (rank != 0) return;
+#pragma unroll
+    for (int a = 0; a < NM; ++a) {
+      float t = 0.0f;
+      for (int sp = 0; sp < d.S; ++sp) t += pbuf[(sp * NM + a) * kTileN + tid];
+      v[a][0] = t;
+    }
+  }
+  gemv_epilogue<1, NM, EPI>(d, fc, v, mat, tile, tcol, 0, 1, 0, sbuf, ybuf);
+}
+
+// ===========================================================================
+// general kernel: M rows, MB per CTA (prefill, batched decode)
+template <int MB, int NM, int EPI>
+__global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvDesc d, const FrameCodes fc) {
+  pdl_launch_dependents();
+  extern __shared__ __align__(16) float sm[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x, split = blockIdx.y, zb = blockIdx.z;
+  const int RPS = d.rows_per_split;
+  float* xs = sm;                               // [MB][RPS]
+  float* red = xs + MB * RPS;                   // [8][NM][MB][256]
+  float* sbuf = red + 8 * NM * MB * kTileN;     // 64 floats
+  float* ybuf = sbuf + 64;                      // [MB][256] (QKV epilogue)
+
+  int mat = 0;
+  if (NM == 1) {
+    while (mat + 1 < d.nmat && tile >= d.tile0[mat + 1]) ++mat;
+  }
+  const int tcol = (NM == 2 ? tile : tile - d.tile0[mat]) * kTileN;
+  const int n = d.mat[mat].n;
+  const int r0 = split * RPS;
+  const int r1 = min(d.k, r0 + RPS);
+  const int R = max(0, r1 - r0);
+  const int m0 = zb * MB;
+  const int mcnt = min(MB, d.M - m0);
+
+  const int rr = lane >> 3, gi = lane & 7;
+  const int gcol = tcol + gi * 32;
+  const bool gval = gcol < n;
+  const size_t rowbytes = (size_t)n / 2;
+  const int ngr = n / 32;
+  constexpr int U = (NM * MB >= 4) ? 2 : 4;
+
+  // first weight batch: issued before waiting on the previous kernel
+  WBatch<U, NM> cur;
+  const int rb0 = warp * 4 + rr;
+  load_batch<U, NM>(cur, d, mat, r0, R, rb0, gcol, gval, rowbytes, ngr);
+  pdl_wait();
+
+  // ---- prologue: rows [m0, m0+mcnt) x k-slice [r0, r1) -> shared memory
+  for (int mm = 0; mm < MB; ++mm) {
+    float* xd = xs + mm * RPS;
+    if (mm >= mcnt) {
+      for (int i = tid; i < R; i += kGemvThreads) xd[i] = 0.0f;
+      continue;
+    }
+    const int m = m0 + mm;
+    if (d.emb_idx) {
+      const uint32_t row = d.emb_idx[(size_t)m * d.emb_idx_stride];
+      const uint8_t* prow = d.emb.packed + (size_t)row * (d.emb.n / 2);
+      const __half* srow = d.emb.scales + (size_t)row * (d.emb.n / 32);
+      for (int i = tid; i < R; i += kGemvThreads) xd[i] = q4_value(prow, srow, r0 + i);
+    } else {
+      const float* xr = d.X + (size_t)m * d.ldx;
+      if (d.gamma) {
+        float inv;
+        if (d.ssq_in) {
+          inv = inv_rms_from_ssq(d, m);
+        } else {
+          float ss = 0.0f;
+          for (int i = tid; i < d.k; i += kGemvThreads) ss += xr[i] * xr[i];
+          ss = block_sum_256(ss, sbuf);
+          inv = 1.0f / sqrtf(ss / (float)d.k + 1e-6f);
+        }
+        for (int i = tid; i < R; i += kGemvThreads) xd[i] = xr[r0 + i] * inv * h2f(d.gamma[r0 + i]);
+        if (d.xnorm_out && tile == 0)
+          for (int i = tid; i < R; i += kGemvThreads) d.xnorm_out[(size_t)m * d.ld_xnorm + r0 + i] = xd[i];
+      } else {
+        for (int i = tid; i < R; i += kGemvThreads) xd[i] = xr[r0 + i];
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- main loop: stream the Q4 slice (double-buffered), 32 columns per lane
+  float2 acc[NM][MB][16];
+#pragma unroll
+  for (int a = 0; a < NM; ++a)
+#pragma unroll
+    for (int b = 0; b < MB; ++b)
+#pragma unroll
+      for (int c = 0; c < 16; ++c) acc[a][b][c] = make_float2(0.0f, 0.0f);
+
+  for (int rb = rb0; rb < R; rb += 32 * U) {
+    WBatch<U, NM> nxt;
+    const bool more = rb + 32 * U < R;
+    if (more) load_batch<U, NM>(nxt, d, mat, r0, R, rb + 32 * U, gcol, gval, rowbytes, ngr);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int rbu = rb + 32 * u;
+      if (rbu < R) {
+#pragma unroll
+        for (int mm = 0; mm < MB; ++mm) {
+          const float xv = xs[mm * RPS + rbu];
+#pragma unroll
+          for (int a = 0; a < NM; ++a) {
+            const SxPack p = make_sx(u16_h2f(cur.s[u][a]) * xv);  // s = scale * x (gemv.rs:239)
+            q4_word_fma(cur.w[u][a].x, p, &acc[a][mm][0]);
+            q4_word_fma(cur.w[u][a].y, p, &acc[a][mm][4]);
+            q4_word_fma(cur.w[u][a].z, p, &acc[a][mm][8]);
+            q4_word_fma(cur.w[u][a].w, p, &acc[a][mm][12]);
+          }
+        }
+      }
+    }
+    if (more) cur = nxt;
+  }
+
+  // ---- reduce the 4 row offsets of a warp, then the 8 warps
+#pragma unroll
+  for (int a = 0; a < NM; ++a)
+#pragma unroll
+    for (int mm = 0; mm < MB; ++mm)
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        float2 v = acc[a][mm][c];
+        v.x += __shfl_xor_sync(0xffffffffu, v.x, 8);
+        v.y += __shfl_xor_sync(0xffffffffu, v.y, 8);
+        v.x += __shfl_xor_sync(0xffffffffu, v.x, 16);
+        v.y += __shfl_xor_sync(0xffffffffu, v.y, 16);
+        acc[a][mm][c] = v;
+      }
+  if (rr == 0) {
+#pragma unroll
+    for (int a = 0; a < NM; ++a)
+#pragma unroll
+      for (int mm = 0; mm < MB; ++mm) {
+        float4* dst = reinterpret_cast<float4*>(red + ((warp * NM + a) * MB + mm) * kTileN + gi * 32);
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          dst[c] = make_float4(acc[a][mm][2 * c].x, acc[a][mm][2 * c].y, acc[a][mm][2 * c + 1].x,
+                               acc[a][mm][2 * c + 1].y);
+      }
+  }
+  __syncthreads();
+  float v[NM][MB];
+#pragma unroll
+  for (int a = 0; a < NM; ++a)
+#pragma unroll
+    for (int mm = 0; mm < MB; ++mm) {
+      float t = 0.0f;
+#pragma unroll
+      for (int w8 = 0; w8 < 8; ++w8) t += red[((w8 * NM + a) * MB + mm) * kTileN + tid];
+      v[a][mm] = t;
+    }
+
+  const int col = tcol + tid;
+  const bool cval = col < n;
+
+  // ---- split-K reduction (deterministic, split order)
+  if (d.S > 1 && d.cluster) {
+    cg::cluster_group cl = cg::this_cluster();
+    __syncthreads();  // every warp has read `red`
+#pragma unroll
+    for (int a = 0; a < NM; ++a)
+#pragma unroll
+      for (int mm = 0; mm < MB; ++mm) red[(a * MB + mm) * kTileN + tid] = v[a][mm];
+    cl.sync();
+    const bool root = cl.block_rank() == 0;
+    if (root) {
+#pragma unroll
+      for (int a = 0; a < NM; ++a)
+#pragma unroll
+        for (int mm = 0; mm < MB; ++mm) {
+          float t = 0.0f;
+          for (int sp = 0; sp < d.S; ++sp) t += cl.map_shared_rank(red, sp)[(a * MB + mm) * kTileN + tid];
+          v[a][mm] = t;
+        }
+    }
+    cl.sync();  // peers keep their shared memory until the root has read it
+    if (!root) return;
+  } else if (d.S > 1) {
+#pragma unroll
+    for (int a = 0; a < NM; ++a) {
+      const int cg0 = d.col0[NM == 2 ? a : mat] + col;
+#pragma unroll
+      for (int mm = 0; mm < MB; ++mm)
+        if (cval && mm < mcnt) d.part[((size_t)split * d.M + m0 + mm) * d.ncols + cg0] = v[a][mm];
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ unsigned s_ticket;
+    unsigned* ctr = d.counters + (size_t)tile * gridDim.z + zb;
+    if (tid == 0) s_ticket = atomicAdd(ctr, 1u);
+    __syncthreads();
+    if (s_ticket != (unsigned)(d.S - 1)) return;
+    __threadfence();
+#pragma unroll
+    for (int a = 0; a < NM; ++a) {
+      const int cg0 = d.col0[NM == 2 ? a : mat] + col;
+#pragma unroll
+      for (int mm = 0; mm < MB; ++mm) {
+        float t = 0.0f;
+        if (cval && mm < mcnt)
+          for (int sp = 0; sp < d.S; ++sp) t += ld_cg(d.part + ((size_t)sp * d.M + m0 + mm) * d.ncols + cg0);
+        v[a][mm] = t;
+      }
+    }
+    if (tid == 0) *ctr = 0u;
+  }
+  gemv_epilogue<MB, NM, EPI>(d, fc, v, mat, tile, tcol, m0, mcnt, zb, sbuf, ybuf);
+}
+
 // ---------------------------------------------------------------------------
+static bool use_dec(const GemvDesc& d) {
+  const int nrmax = d.paired ? kDecRowsNM2 : kDecRowsNM1;
+  return d.M == 1 && (d.cluster || d.S == 1) && d.rows_per_split <= 32 * nrmax;
+}
+
 size_t gemv_smem_bytes(const GemvDesc& d) {
   const int NM = d.paired ? 2 : 1;
+  if (use_dec(d))
+    return sizeof(float) * ((size_t)8 * 4 * NM * kTileN + (size_t)kMaxClusterSplits * NM * kTileN + 64 + kTileN);
   return sizeof(float) * ((size_t)d.mb * d.rows_per_split + 8 * NM * d.mb * kTileN + 64 + d.mb * kTileN);
+}
+
+static LaunchOpts opts(const GemvDesc& d) {
+  LaunchOpts o;
+  o.pdl = d.pdl != 0;
+  o.cluster_y = (d.cluster && d.S > 1) ? (unsigned)d.S : 1u;
+  return o;
 }
 
 template <int MB, int NM, int EPI>
 static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
-  const size_t smem = gemv_smem_bytes(d);
   const dim3 grid(d.ntiles, d.S, (d.M + MB - 1) / MB);
-  gemv_q4_kernel<MB, NM, EPI><<<grid, kGemvThreads, smem, st>>>(d, fc);
-  return cudaGetLastError();
+  return launch_k(gemv_q4_kernel<MB, NM, EPI>, grid, dim3(kGemvThreads), gemv_smem_bytes(d), st, opts(d), d, fc);
+}
+
+template <int NM, int EPI, int NR>
+static cudaError_t launch_dec(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
+  const dim3 grid(d.ntiles, d.S, 1);
+  return launch_k(gemv_dec_kernel<NM, EPI, NR>, grid, dim3(kGemvThreads), gemv_smem_bytes(d), st, opts(d), d, fc);
+}
+
+template <int NM, int EPI>
+static cudaError_t dispatch_dec(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
+  const int nr = (d.rows_per_split + 31) / 32;
+  if (NM == 2) {
+    if (nr <= 2) return launch_dec<2, EPI, 2>(d, fc, st);
+    if (nr <= 4) return launch_dec<2, EPI, 4>(d, fc, st);
+    return launch_dec<2, EPI, kDecRowsNM2>(d, fc, st);
+  }
+  if (nr <= 4) return launch_dec<1, EPI, 4>(d, fc, st);
+  if (nr <= 8) return launch_dec<1, EPI, 8>(d, fc, st);
+  return launch_dec<1, EPI, kDecRowsNM1>(d, fc, st);
 }
 
 template <int MB, int NM, int EPI>
 static void set_attr() {
   cudaFuncSetAttribute(gemv_q4_kernel<MB, NM, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+  cudaFuncSetAttribute(gemv_q4_kernel<MB, NM, EPI>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+}
+template <int NM, int EPI, int NR>
+static void set_attr_dec() {
+  cudaFuncSetAttribute(gemv_dec_kernel<NM, EPI, NR>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+  cudaFuncSetAttribute(gemv_dec_kernel<NM, EPI, NR>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+}
+template <int EPI>
+static void set_attr_dec_nm1() {
+  set_attr_dec<1, EPI, 4>(); set_attr_dec<1, EPI, 8>(); set_attr_dec<1, EPI, kDecRowsNM1>();
 }
 
-// Opt every instantiation into large dynamic shared memory once per device
-// (outside any stream capture).
+// Opt every instantiation into large dynamic shared memory and 16-CTA
+// clusters once per device (outside any stream capture).
 void gemv_init_attributes() {
   static bool done[64] = {false};
   int dev = 0;
@@ -383,6 +652,9 @@ void gemv_init_attributes() {
   set_attr<1, 1, EPI_QKV>(); set_attr<2, 1, EPI_QKV>(); set_attr<4, 1, EPI_QKV>();
   set_attr<1, 1, EPI_ARGMAX>(); set_attr<2, 1, EPI_ARGMAX>(); set_attr<4, 1, EPI_ARGMAX>();
   set_attr<1, 2, EPI_SWIGLU>(); set_attr<2, 2, EPI_SWIGLU>();
+  set_attr_dec_nm1<EPI_STORE>(); set_attr_dec_nm1<EPI_RESID>(); set_attr_dec_nm1<EPI_QKV>();
+  set_attr_dec_nm1<EPI_ARGMAX>();
+  set_attr_dec<2, EPI_SWIGLU, 2>(); set_attr_dec<2, EPI_SWIGLU, 4>(); set_attr_dec<2, EPI_SWIGLU, kDecRowsNM2>();
   cudaGetLastError();
   done[dev] = true;
 }
@@ -391,12 +663,14 @@ template <int EPI>
 static cudaError_t launch_mb(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
   if (d.paired) {
     if (EPI != EPI_SWIGLU) return cudaErrorInvalidValue;
+    if (use_dec(d)) return dispatch_dec<2, EPI_SWIGLU>(d, fc, st);
     if (d.mb == 1) return launch_t<1, 2, EPI_SWIGLU>(d, fc, st);
     if (d.mb == 2) return launch_t<2, 2, EPI_SWIGLU>(d, fc, st);
     return cudaErrorInvalidValue;
   }
   if (EPI == EPI_SWIGLU) return cudaErrorInvalidValue;
   constexpr int E = EPI == EPI_SWIGLU ? EPI_STORE : EPI;
+  if (use_dec(d)) return dispatch_dec<1, E>(d, fc, st);
   if (d.mb == 1) return launch_t<1, 1, E>(d, fc, st);
   if (d.mb == 2) return launch_t<2, 1, E>(d, fc, st);
   if (d.mb == 4) return launch_t<4, 1, E>(d, fc, st);
@@ -405,6 +679,9 @@ static cudaError_t launch_mb(const GemvDesc& d, const FrameCodes& fc, cudaStream
 
 cudaError_t launch_gemv(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
   if (d.ntiles <= 0 || d.S <= 0 || d.M <= 0 || d.rows_per_split <= 0) return cudaErrorInvalidValue;
+  if (d.cluster && d.S > kMaxClusterSplits) return cudaErrorInvalidValue;
+  if (!d.cluster && d.S > 1 && (!d.part || !d.counters)) return cudaErrorInvalidValue;
+  if (d.ssq_in && (d.ssq_n <= 0 || d.ssq_ld < d.ssq_n)) return cudaErrorInvalidValue;
   switch (d.epi_kind) {
     case EPI_STORE: return launch_mb<EPI_STORE>(d, fc, st);
     case EPI_RESID: return launch_mb<EPI_RESID>(d, fc, st);

@@ -85,6 +85,10 @@ struct EpiDesc {
   KvDesc kv;
   RowPos rp;
   int* err_flag = nullptr;
+  // STORE / RESID: per-tile sums of squares of the written row values,
+  // ssq_out[m * ssq_ld + tile], consumed by the next RMSNorm prologue
+  float* ssq_out = nullptr;
+  long ssq_ld = 0;
   // ARGMAX: keys[m] accumulates (order_key(v) << 32 | col); the last tile
   // finalises codes (see FrameCodes).
   unsigned long long* keys = nullptr;
@@ -112,17 +116,32 @@ struct GemvDesc {
   const float* X = nullptr;
   long ldx = 0;
   const __half* gamma = nullptr;  // RMSNorm prologue (gemv.rs:408-417)
+  // sum of squares of each input row as ssq_n tile partials written by the
+  // producer (ssq_in[m * ssq_ld + t]); null = reduce the full row here
+  const float* ssq_in = nullptr;
+  long ssq_ld = 0;
+  int ssq_n = 0;
   // embedding-gather prologue: row m = dequant(emb row emb_idx[m*emb_idx_stride])
   Q4Mat emb;
   const uint32_t* emb_idx = nullptr;
   int emb_idx_stride = 1;
   float* xnorm_out = nullptr;  // optional copy of the normalised rows
   long ld_xnorm = 0;
-  // split-K scratch
+  // split-K reduction: cluster = 1 reduces the S partials of a tile over
+  // distributed shared memory (the S CTAs form one cluster, S <= 16);
+  // cluster = 0 goes through global scratch (part + counters).
+  int cluster = 0;
+  int pdl = 0;
   float* part = nullptr;        // [S][M][ncols]
   unsigned* counters = nullptr; // [ntiles * zblocks], left at zero
   EpiDesc epi;
 };
+constexpr int kMaxClusterSplits = 16;
+// M = 1 decode kernel: weight rows a lane keeps in registers (32 rows per
+// step of the 8 warps x 4 row offsets), per matrix count
+constexpr int kDecRowsNM1 = 12;  // rows per split <= 384
+constexpr int kDecRowsNM2 = 6;   // rows per split <= 192
+constexpr int kSsqLd = 64;       // row stride of the sum-of-squares partials
 
 // Frame bookkeeping shared by the sampler / argmax epilogue / fusion.
 struct SlotState {
@@ -147,6 +166,41 @@ struct FrameCodes {
   const uint32_t* forced = nullptr;// [B][max_frames][16] or null
   int max_frames = 0;
 };
+
+// ---- launch helper: programmatic dependent launch + cluster shape ----
+// PDL lets a kernel start (and prefetch its weights) while its predecessor
+// finishes; the kernel's griddepcontrol.wait orders all dependent reads.
+bool pdl_enabled();
+struct LaunchOpts {
+  bool pdl = false;
+  unsigned cluster_y = 1;  // CTAs of one cluster along grid.y
+};
+template <typename Kern, typename... Args>
+inline cudaError_t launch_k(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, LaunchOpts o,
+                            Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  unsigned n = 0;
+  if (o.cluster_y > 1) {
+    at[n].id = cudaLaunchAttributeClusterDimension;
+    at[n].val.clusterDim.x = 1;
+    at[n].val.clusterDim.y = o.cluster_y;
+    at[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (o.pdl && pdl_enabled()) {
+    at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = at;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
 
 // ---- launchers (return cudaError_t of the launch) ----
 size_t gemv_smem_bytes(const GemvDesc& d);
@@ -199,6 +253,8 @@ struct FuseDesc {
   int max_trail = 0;
   const float* tts_pad = nullptr;  // [H]
   int B = 0, H = 0;
+  float* ssq_out = nullptr;      // per-256-column sums of squares of x [B][ssq_ld]
+  long ssq_ld = 0;
   FrameCodes fc;
   int mode = 0;                  // 0: full frame fusion; 1: semantic only (sem_out); 2: acoustic sum only
   const uint32_t* codes_plain = nullptr;  // mode 1/2 standalone codes

@@ -8,14 +8,20 @@
 
 namespace qtts {
 
+namespace {
+constexpr LaunchOpts kPdl = {true, 1};
+}  // namespace
+
 // ---- frame input (generate_new.rs:255, 271-286) ---------------------------
 // x[b][j] = (sem[j] + acs[j]) + text[j], with acs = ((0 + e_0) + e_1) ... + e_14
 // accumulated in group order exactly like get_acoustic_embeddings_sum
 // (code_predictor.rs:280-293).  Element-wise, so bit-identical to the CPU.
 __global__ void fuse_kernel(const FuseDesc d) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int b = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= d.H) return;
+  if (j >= d.H) return;  // H is a multiple of 256 whenever ssq_out is set (checked at launch)
   const uint32_t* codes;
   int f = 0, ntr = 0;
   if (d.codes_plain) {
@@ -48,18 +54,33 @@ __global__ void fuse_kernel(const FuseDesc d) {
     acs = acs + q4_value(E.packed + (size_t)c * (E.n / 2), E.scales + (size_t)c * (E.n / 32), j);
   }
   const float* ta = (f < ntr) ? d.trail + ((size_t)b * d.max_trail + f) * d.H : d.tts_pad;
-  d.x[(size_t)b * d.ldx + j] = (sem + acs) + ta[j];
+  const float xv = (sem + acs) + ta[j];
+  d.x[(size_t)b * d.ldx + j] = xv;
+  if (d.ssq_out) {  // sum of squares of this 256-column tile for the next RMSNorm
+    __shared__ float sred[8];
+    float q = xv * xv;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+    if ((threadIdx.x & 31) == 0) sred[threadIdx.x >> 5] = q;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float t = 0.0f;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += sred[w];
+      d.ssq_out[(size_t)b * d.ssq_ld + blockIdx.x] = t;
+    }
+  }
 }
 
 cudaError_t launch_fuse(const FuseDesc& d, cudaStream_t st) {
-  if (d.B <= 0 || d.H <= 0) return cudaErrorInvalidValue;
+  if (d.B <= 0 || d.H <= 0 || (d.ssq_out && d.H % 256)) return cudaErrorInvalidValue;
   const dim3 grid((d.H + 255) / 256, d.B);
-  fuse_kernel<<<grid, 256, 0, st>>>(d);
-  return cudaGetLastError();
+  return launch_k(fuse_kernel, dim3(grid), dim3(256), 0, st, kPdl, d);
 }
 
 // ---- gathers ----------------------------------------------------------------
 __global__ void embed_rows_kernel(const Q4Mat m, const uint32_t* idx, int count, float* out, long ldo) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int i = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= count || j >= m.n) return;
@@ -70,11 +91,12 @@ cudaError_t launch_embed_rows(const Q4Mat& mat, const uint32_t* idx, int count, 
                               cudaStream_t st) {
   if (count <= 0) return cudaSuccess;
   const dim3 grid((mat.n + 255) / 256, count);
-  embed_rows_kernel<<<grid, 256, 0, st>>>(mat, idx, count, out, ldo);
-  return cudaGetLastError();
+  return launch_k(embed_rows_kernel, dim3(grid), dim3(256), 0, st, kPdl, mat, idx, count, out, ldo);
 }
 
 __global__ void embed_code0_kernel(const Q4Mat m, const SlotState* slots, float* out, long ldo) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int b = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= m.n) return;
@@ -84,11 +106,12 @@ __global__ void embed_code0_kernel(const Q4Mat m, const SlotState* slots, float*
 cudaError_t launch_embed_code0(const Q4Mat& mat, const SlotState* slots, int B, float* out, long ldo,
                                cudaStream_t st) {
   const dim3 grid((mat.n + 255) / 256, B);
-  embed_code0_kernel<<<grid, 256, 0, st>>>(mat, slots, out, ldo);
-  return cudaGetLastError();
+  return launch_k(embed_code0_kernel, dim3(grid), dim3(256), 0, st, kPdl, mat, slots, out, ldo);
 }
 
 __global__ void add_rows_kernel(const float* a, long lda, const float* b, long ldb, float* out, long ldo, int n) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int r = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= n) return;
@@ -98,14 +121,15 @@ cudaError_t launch_add_rows(const float* a, long lda, const float* b, long ldb, 
                             int n, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
   const dim3 grid((n + 255) / 256, rows);
-  add_rows_kernel<<<grid, 256, 0, st>>>(a, lda, b, ldb, out, ldo, n);
-  return cudaGetLastError();
+  return launch_k(add_rows_kernel, dim3(grid), dim3(256), 0, st, kPdl, a, lda, b, ldb, out, ldo, n);
 }
 
 // Prefill rows of generate_new.rs:94-173: each row is codec_emb(tok) +
 // text_proj(row), the raw voice embedding, or a text_proj row alone.
 __global__ void assemble_kernel(const Q4Mat codec, const RowRecipe* rec, const float* tp, long ldtp,
                                 const float* voice, long ldv, float* out, long ldo, int H) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int r = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= H) return;
@@ -126,11 +150,12 @@ cudaError_t launch_assemble(const Q4Mat& codec, const RowRecipe* rec, int rows, 
                             const float* voice, long ldv, float* out, long ldo, int H, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
   const dim3 grid((H + 255) / 256, rows);
-  assemble_kernel<<<grid, 256, 0, st>>>(codec, rec, tp, ldtp, voice, ldv, out, ldo, H);
-  return cudaGetLastError();
+  return launch_k(assemble_kernel, dim3(grid), dim3(256), 0, st, kPdl, codec, rec, tp, ldtp, voice, ldv, out, ldo, H);
 }
 
 __global__ void gather_rows_kernel(const float* src, long lds, const int* idx, float* out, long ldo, int n) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int r = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= n) return;
@@ -140,12 +165,13 @@ cudaError_t launch_gather_rows(const float* src, long lds, const int* idx, int r
                                cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
   const dim3 grid((n + 255) / 256, rows);
-  gather_rows_kernel<<<grid, 256, 0, st>>>(src, lds, idx, out, ldo, n);
-  return cudaGetLastError();
+  return launch_k(gather_rows_kernel, dim3(grid), dim3(256), 0, st, kPdl, src, lds, idx, out, ldo, n);
 }
 
 // ---- frame bookkeeping --------------------------------------------------------
 __global__ void frame_end_kernel(SlotState* slots, int B) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= B) return;
   SlotState& s = slots[b];
@@ -156,12 +182,13 @@ __global__ void frame_end_kernel(SlotState* slots, int B) {
   }
 }
 cudaError_t launch_frame_end(SlotState* slots, int B, cudaStream_t st) {
-  frame_end_kernel<<<(B + 127) / 128, 128, 0, st>>>(slots, B);
-  return cudaGetLastError();
+  return launch_k(frame_end_kernel, dim3((B + 127) / 128), dim3(128), 0, st, kPdl, slots, B);
 }
 
 // Copy logits / talker hidden of the current frame into dump buffers.
 __global__ void dump_kernel(const SlotState* slots, const float* src, long lds, int n, float* dst, int max_frames) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int b = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= n) return;
@@ -172,12 +199,13 @@ __global__ void dump_kernel(const SlotState* slots, const float* src, long lds, 
 cudaError_t launch_dump(const SlotState* slots, int B, const float* src, long lds, int n, float* dst, int max_frames,
                         cudaStream_t st) {
   const dim3 grid((n + 255) / 256, B);
-  dump_kernel<<<grid, 256, 0, st>>>(slots, src, lds, n, dst, max_frames);
-  return cudaGetLastError();
+  return launch_k(dump_kernel, dim3(grid), dim3(256), 0, st, kPdl, slots, src, lds, n, dst, max_frames);
 }
 
 // ---- whole-matrix dequant (gemv.rs:378-400 applied to every row) --------------
 __global__ void dequant_kernel(const Q4Mat m, float* out) {
+  pdl_launch_dependents();
+  pdl_wait();
   const size_t total = (size_t)m.k * m.n / 2;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const size_t r = i / (m.n / 2), cb = i % (m.n / 2);
@@ -188,12 +216,13 @@ __global__ void dequant_kernel(const Q4Mat m, float* out) {
   }
 }
 cudaError_t launch_dequant(const Q4Mat& m, float* out, cudaStream_t st) {
-  dequant_kernel<<<1184, 256, 0, st>>>(m, out);
-  return cudaGetLastError();
+  return launch_k(dequant_kernel, dim3(1184), dim3(256), 0, st, kPdl, m, out);
 }
 
 // ---- the sampler's exp, element-wise ----------------------------------------------
 __global__ void expf_kernel(const float* x, float* y, int n) {
+  pdl_launch_dependents();
+  pdl_wait();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) y[i] = expf_glibc(x[i]);
 }
 cudaError_t launch_expf(const float* x, float* y, int n, cudaStream_t st) {
@@ -206,6 +235,8 @@ cudaError_t launch_expf(const float* x, float* y, int n, cudaStream_t st) {
 // One thread per (row m, column pair); sequential over k like the reference
 // loop, so each output is the reference's own summation order.
 __global__ void f16_gemv_kernel(const __half* w, int k, int n, const float* x, int m, float* y) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int j2 = blockIdx.x * blockDim.x + threadIdx.x;
   const int row = blockIdx.y;
   if (2 * j2 >= n || row >= m) return;
@@ -223,8 +254,7 @@ __global__ void f16_gemv_kernel(const __half* w, int k, int n, const float* x, i
 cudaError_t launch_f16_gemv(const __half* w, int k, int n, const float* x, int m, float* y, cudaStream_t st) {
   if (n % 2) return cudaErrorInvalidValue;
   const dim3 grid((n / 2 + 127) / 128, m);
-  f16_gemv_kernel<<<grid, 128, 0, st>>>(w, k, n, x, m, y);
-  return cudaGetLastError();
+  return launch_k(f16_gemv_kernel, dim3(grid), dim3(128), 0, st, kPdl, w, k, n, x, m, y);
 }
 
 }  // namespace qtts

@@ -72,6 +72,8 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(const SampleDesc d) {
   __shared__ int ibuf[96];
   __shared__ float s_sum;
   __shared__ unsigned s_prefix, s_need;
+  pdl_launch_dependents();
+  pdl_wait();
   const int tid = threadIdx.x;
   const int b = blockIdx.x;
   const int V = d.V;
@@ -245,8 +247,9 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(const SampleDesc d) {
 
 cudaError_t launch_sample(const SampleDesc& d, cudaStream_t st) {
   if (d.V <= 0 || d.V > kMaxV || d.B <= 0) return cudaErrorInvalidValue;
-  sample_kernel<<<d.B, kThreads, 0, st>>>(d);
-  return cudaGetLastError();
+  LaunchOpts o;
+  o.pdl = true;
+  return launch_k(sample_kernel, dim3(d.B), dim3(kThreads), 0, st, o, d);
 }
 
 }  // namespace qtts
