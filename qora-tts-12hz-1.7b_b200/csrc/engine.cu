@@ -30,6 +30,15 @@ bool pdl_enabled() {
   }();
   return on;
 }
+// Tensor-core path for projections with M >= kTcMinRows; QTTS_TC=0 keeps
+// them on the CUDA-core kernels (A/B measurements).
+bool tc_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("QTTS_TC");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
 int fail(int code, const std::string& msg) {
   g_err = msg;
   return code;
@@ -221,6 +230,7 @@ static int model_load(const char* path, int device, Model** out) {
   }
   gemv_init_attributes();
   attn_init_attributes();
+  tc_init_attributes();
   *out = m;
   return QTTS_OK;
 }
@@ -265,10 +275,50 @@ void choose_split(int sm_count, GemvDesc& g) {
   g.S = ceil_div(g.k, rps);
 }
 
+template <class T>
+static int dalloc(T** p, size_t count, std::vector<void*>* track = nullptr) {
+  if (count == 0) count = 1;
+  if (cudaMalloc(reinterpret_cast<void**>(p), sizeof(T) * count) != cudaSuccess)
+    return fail(QTTS_ERR_OOM, "device allocation failed");
+  if (cudaMemset(*p, 0, sizeof(T) * count) != cudaSuccess) return fail(QTTS_ERR_CUDA, "cudaMemset failed");
+  if (track) track->push_back(*p);
+  return QTTS_OK;
+}
+
+// Grow the tensor-core scratch (operand blocks, split-K partials) to a
+// projection's need.  Planned ops read the pointers when they launch, so a
+// reallocation between planning and running is safe; a live frame graph has
+// them baked in, so growing is refused while one exists.
+static int tc_reserve(Session& s, size_t xsplit_halves, size_t part_floats) {
+  if (xsplit_halves <= s.xsplit_halves && part_floats <= s.part_floats) return QTTS_OK;
+  if (s.graph_exec) return fail(QTTS_ERR_STATE, "tensor-core scratch must grow while a generation is live");
+  CK(cudaStreamSynchronize(s.st));
+  if (xsplit_halves > s.xsplit_halves) {
+    if (s.xsplit) cudaFree(s.xsplit);
+    s.xsplit = nullptr;
+    s.xsplit_halves = 0;
+    RC(dalloc(&s.xsplit, xsplit_halves));
+    s.xsplit_halves = xsplit_halves;
+  }
+  if (part_floats > s.part_floats) {
+    if (s.part) cudaFree(s.part);
+    s.part = nullptr;
+    s.part_floats = 0;
+    RC(dalloc(&s.part, part_floats));
+    s.part_floats = part_floats;
+  }
+  return QTTS_OK;
+}
+
 static int plan_gemv(Session& s, GemvDesc& g) {
   choose_split(s.m->sm_count, g);
   g.cluster = 1;  // split-K partials reduced over distributed shared memory
   g.pdl = 1;
+  if (g.M >= kTcMinRows && tc_enabled()) {
+    tc_plan(s.m->sm_count, g);
+    RC(tc_reserve(s, tc_xsplit_halves(g.M, g.k), (size_t)tc_splits(g) * g.M * g.ncols));
+    g.err_flag = s.err_flag;  // xsplit / part are read from the session at launch (gemv_op)
+  }
   const size_t zb = (size_t)ceil_div(g.M, g.mb);
   if ((size_t)g.ntiles * zb > s.n_counters || zb > 4096) return fail(QTTS_ERR_OOM, "tile counter array too small");
   g.counters = s.counters;
@@ -279,8 +329,16 @@ static int plan_gemv(Session& s, GemvDesc& g) {
   return QTTS_OK;
 }
 
-static Op gemv_op(const GemvDesc& g, const FrameCodes& fc = FrameCodes{}) {
-  return [g, fc](cudaStream_t st) { return launch_gemv(g, fc, st); };
+static Op gemv_op(Session& s, const GemvDesc& g, const FrameCodes& fc = FrameCodes{}) {
+  Session* sp = &s;
+  return [sp, g, fc](cudaStream_t st) {
+    GemvDesc d = g;
+    if (d.tc) {
+      d.xsplit = sp->xsplit;
+      d.part = sp->part;
+    }
+    return launch_gemv(d, fc, st);
+  };
 }
 
 struct LayerIO {
@@ -323,7 +381,7 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
   g.epi.rope_cos = io.cos; g.epi.rope_sin = io.sin; g.epi.rope_rows = io.rope_rows; g.epi.rope_skip_oob = io.skip_oob;
   g.epi.heads = io.heads; g.epi.kv_heads = io.kvh; g.epi.kv = io.kv; g.epi.rp = io.rp; g.epi.err_flag = s.err_flag;
   RC(plan_gemv(s, g));
-  ops.push_back(gemv_op(g));
+  ops.push_back(gemv_op(s, g));
 
   AttnDesc a;
   a.q = s.q; a.ldq = qd; a.out = s.attn; a.ldo = qd; a.kv = io.kv; a.rp = io.rp;
@@ -341,19 +399,19 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
   o.X = s.attn; o.ldx = qd; o.epi.out = io.X; o.epi.ldo = io.ldx;
   emit_ssq(o);
   RC(plan_gemv(s, o));
-  ops.push_back(gemv_op(o));
+  ops.push_back(gemv_op(s, o));
 
   GemvDesc gu = gemv_base(EPI_SWIGLU, {L.gate, L.up}, true, io.M);
   gu.X = io.X; gu.ldx = io.ldx; gu.gamma = L.post_norm; gu.epi.out = s.h; gu.epi.ldo = io.inter;
   use_ssq(gu, true);
   RC(plan_gemv(s, gu));
-  ops.push_back(gemv_op(gu));
+  ops.push_back(gemv_op(s, gu));
 
   GemvDesc dn = gemv_base(EPI_RESID, {L.down}, false, io.M);
   dn.X = s.h; dn.ldx = io.inter; dn.epi.out = io.X; dn.epi.ldo = io.ldx;
   emit_ssq(dn);
   RC(plan_gemv(s, dn));
-  ops.push_back(gemv_op(dn));
+  ops.push_back(gemv_op(s, dn));
   return QTTS_OK;
 }
 
@@ -403,7 +461,7 @@ static int add_codec_head(Session& s, std::vector<Op>& ops, const float* X, long
   g.epi.out = logits; g.epi.ldo = s.m->d.t_vocab;
   g.xnorm_out = hid; g.ld_xnorm = ldh;
   RC(plan_gemv(s, g));
-  ops.push_back(gemv_op(g));
+  ops.push_back(gemv_op(s, g));
   return QTTS_OK;
 }
 
@@ -420,7 +478,7 @@ static int add_predictor(Session& s, std::vector<Op>& ops, int B, bool frame_mod
   pj.X = s.pin; pj.ldx = d.t_hidden; pj.epi.out = s.px; pj.epi.ldo = pH; pj.epi.bias = m.input_proj_b;
   pj.epi.ssq_out = s.ssq_p; pj.epi.ssq_ld = kSsqLd;
   RC(plan_gemv(s, pj));
-  ops.push_back(gemv_op(pj));
+  ops.push_back(gemv_op(s, pj));
   auto layers = [&](float* X, int M, const RowPos& rp, float* ssq) -> int {
     for (int l = 0; l < d.p_layers; ++l) {
       LayerIO io;
@@ -442,7 +500,7 @@ static int add_predictor(Session& s, std::vector<Op>& ops, int B, bool frame_mod
     h.ssq_in = ssq; h.ssq_ld = ssq_ld; h.ssq_n = pnt;
     h.epi.group = g + 1; h.epi.frame_codes = frame_mode ? 1 : 0; h.epi.codes_plain = s.codes_plain;
     RC(plan_gemv(s, h));
-    ops.push_back(gemv_op(h, fc));
+    ops.push_back(gemv_op(s, h, fc));
     return QTTS_OK;
   };
   RC(head(s.px + pH, 2L * pH, 0, s.ssq_p + kSsqLd, 2L * kSsqLd));
@@ -459,7 +517,7 @@ static int add_predictor(Session& s, std::vector<Op>& ops, int B, bool frame_mod
     pe.epi.out = s.px1; pe.epi.ldo = pH; pe.epi.bias = m.input_proj_b;
     pe.epi.ssq_out = s.ssq_p1; pe.epi.ssq_ld = kSsqLd;
     RC(plan_gemv(s, pe));
-    ops.push_back(gemv_op(pe));
+    ops.push_back(gemv_op(s, pe));
     RowPos rp;
     rp.pos_const = g + 1;
     RC(layers(s.px1, B, rp, s.ssq_p1));
@@ -477,12 +535,12 @@ static int add_text_proj(Session& s, std::vector<Op>& ops, const uint32_t* tok_d
   g1.emb = m.text_emb; g1.emb_idx = tok_dev; g1.emb_idx_stride = 1;
   g1.epi.out = h1; g1.epi.ldo = m.fc1.n; g1.epi.bias = m.fc1_b; g1.epi.act_silu = 1;
   RC(plan_gemv(s, g1));
-  ops.push_back(gemv_op(g1));
+  ops.push_back(gemv_op(s, g1));
   GemvDesc g2 = gemv_base(EPI_STORE, {m.fc2}, false, n);
   g2.X = h1; g2.ldx = m.fc1.n;
   g2.epi.out = out; g2.epi.ldo = ldo; g2.epi.bias = m.fc2_b;
   RC(plan_gemv(s, g2));
-  ops.push_back(gemv_op(g2));
+  ops.push_back(gemv_op(s, g2));
   return QTTS_OK;
 }
 
@@ -507,15 +565,6 @@ static int sync_check(Session& s) {
 // ---------------------------------------------------------------------------
 // sessions
 // ---------------------------------------------------------------------------
-template <class T>
-static int dalloc(T** p, size_t count, std::vector<void*>* track = nullptr) {
-  if (count == 0) count = 1;
-  if (cudaMalloc(reinterpret_cast<void**>(p), sizeof(T) * count) != cudaSuccess)
-    return fail(QTTS_ERR_OOM, "device allocation failed");
-  if (cudaMemset(*p, 0, sizeof(T) * count) != cudaSuccess) return fail(QTTS_ERR_CUDA, "cudaMemset failed");
-  if (track) track->push_back(*p);
-  return QTTS_OK;
-}
 
 static void free_generation(Session& s) {
   if (s.graph_exec) cudaGraphExecDestroy(s.graph_exec);
@@ -538,7 +587,7 @@ static void session_free_all(Session* s) {
   free_generation(*s);
   void* bufs[] = {s->kv_pool, s->page_table, s->pkv_pool, s->slots, s->x, s->pin, s->q, s->attn, s->h,
                   s->px, s->px1, s->logits, s->xpre, s->hid1, s->part, s->counters, s->counters2, s->keys,
-                  s->apart, s->acounters, s->err_flag, s->codes_plain, s->io, s->ssq_t, s->ssq_p, s->ssq_p1};
+                  s->apart, s->acounters, s->err_flag, s->codes_plain, s->io, s->ssq_t, s->ssq_p, s->ssq_p1, s->xsplit};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (s->st) cudaStreamDestroy(s->st);
@@ -596,6 +645,12 @@ static int session_create(Model* m, int maxB, int maxP, Session** out) {
   A(&s->ssq_t, (size_t)s->rows * kSsqLd);
   A(&s->ssq_p, (size_t)2 * maxB * kSsqLd);
   A(&s->ssq_p1, (size_t)maxB * kSsqLd);
+  if (s->rows >= kTcMinRows) {  // fp16 hi/lo operand blocks of the tensor-core path
+    const int kmax = std::max({d.t_hidden, d.t_text_hidden, d.t_inter, d.p_hidden, d.p_inter,
+                               d.t_heads * kHeadDim, d.p_heads * kHeadDim});
+    s->xsplit_halves = tc_xsplit_halves(s->rows, kmax);
+    A(&s->xsplit, s->xsplit_halves);
+  }
   if (rc == QTTS_OK) {  // pages: slot b owns pages [b*pps, (b+1)*pps)
     std::vector<int> pt((size_t)maxB * s->pages_per_sess);
     for (size_t i = 0; i < pt.size(); ++i) pt[i] = (int)i;
@@ -784,9 +839,10 @@ static int generate_begin(Session& s, int n, const qtts_utterance* u, int F, uns
   // frame plan -> CUDA graph
   std::vector<Op> fops;
   RC(build_frame_ops(s, fops, dump_logits || dump_hidden));
-  s.frame_kernels = (int)fops.size();
   CK(cudaStreamBeginCapture(s.st, cudaStreamCaptureModeThreadLocal));
+  const long launches0 = g_kernel_launches;
   int rc = run_ops(s, fops);
+  s.frame_kernels = (int)(g_kernel_launches - launches0);
   cudaGraph_t g = nullptr;
   const cudaError_t ce = cudaStreamEndCapture(s.st, &g);
   if (rc != QTTS_OK) {
@@ -960,13 +1016,21 @@ static int gemv_plan_standalone(int k, int n, int m, GemvDesc& g) {
   w.n = n;
   g = gemv_base(EPI_STORE, {w}, false, m);
   choose_split(sms, g);
+  if (m >= kTcMinRows && tc_enabled()) tc_plan(sms, g);
   return QTTS_OK;
+}
+
+// Scratch layout: [counters 16 KB][split-K partials][tensor-core operand blocks]
+static size_t gemv_part_bytes(const GemvDesc& g) {
+  const int S = g.tc ? tc_splits(g) : g.S;
+  const size_t b = (g.tc || S > 1) ? sizeof(float) * (size_t)S * g.M * g.ncols : 0;
+  return (b + 255) & ~(size_t)255;
 }
 
 static size_t gemv_scratch(int k, int n, int m) {
   GemvDesc g;
   gemv_plan_standalone(k, n, m, g);
-  return kCounterBytes + (g.S > 1 ? sizeof(float) * (size_t)g.S * m * n : 0);
+  return kCounterBytes + gemv_part_bytes(g) + (g.tc ? 2 * tc_xsplit_halves(m, k) : 0);
 }
 
 static int gemv_dev(const uint8_t* packed, const uint16_t* scales, int k, int n, const float* x, int m, float* y,
@@ -985,12 +1049,14 @@ static int gemv_dev(const uint8_t* packed, const uint16_t* scales, int k, int n,
   g.epi.out = y; g.epi.ldo = n;
   const size_t zb = (size_t)ceil_div(m, g.mb);
   if (g.ntiles * zb > kCounterBytes / 4) return fail(QTTS_ERR_BADARG, "too many tiles for the counter area");
-  const size_t need = kCounterBytes + (g.S > 1 ? sizeof(float) * (size_t)g.S * m * n : 0);
+  const size_t need = gemv_scratch(k, n, m);
   if (!scratch || scratch_bytes < need) return fail(QTTS_ERR_BADARG, "scratch smaller than qtts_q4_gemv_scratch_bytes()");
   g.counters = reinterpret_cast<unsigned*>(scratch);
   g.part = reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + kCounterBytes);
+  if (g.tc) g.xsplit = reinterpret_cast<__half*>(reinterpret_cast<char*>(scratch) + kCounterBytes + gemv_part_bytes(g));
   g.cluster = 1;
   gemv_init_attributes();
+  tc_init_attributes();
   const cudaError_t e = launch_gemv(g, FrameCodes{}, st);
   if (e != cudaSuccess) return fail(QTTS_ERR_CUDA, cudaGetErrorString(e));
   return QTTS_OK;

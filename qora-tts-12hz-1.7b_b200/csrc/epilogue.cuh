@@ -1,0 +1,184 @@
+// epilogue.cuh -- the projection epilogues shared by the CUDA-core GEMV
+// kernels (gemv.cu) and the tensor-core GEMM (tc_gemm.cu): bias/SiLU store,
+// residual add (+ per-tile sums of squares for the next RMSNorm), SwiGLU,
+// QK-norm + RoPE + KV append, and the argmax of the greedy heads -- the
+// per-step glue of talker.rs:279-349 and code_predictor.rs:448-505.
+#pragma once
+#include "common.cuh"
+#include "kernels.h"
+
+namespace qtts {
+namespace {
+
+// RMSNorm scale of a row from the producer's per-tile sums of squares.
+__device__ __forceinline__ float inv_rms_from_ssq(const GemvDesc& d, int m) {
+  const float* p = d.ssq_in + (size_t)m * d.ssq_ld;
+  float ss = 0.0f;
+  for (int t = 0; t < d.ssq_n; ++t) ss += p[t];
+  return 1.0f / sqrtf(ss / (float)d.k + 1e-6f);
+}
+
+__device__ __forceinline__ float block_sum_256(float v, float* sbuf) {
+  // all 256 threads participate; sbuf >= 8 floats
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) sbuf[warp] = v;
+  __syncthreads();
+  float t = 0.0f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) t += sbuf[w];
+  return t;
+}
+
+__device__ __forceinline__ float* kv_row(const KvDesc& kv, int sess, int pos, int which, int h) {
+  const int page = kv.page_table ? kv.page_table[sess * kv.pages_per_sess + pos / kPageSize] : sess;
+  const size_t blk = (((size_t)page * kv.n_layers + kv.layer) * 2 + which) * kv.kv_heads + h;
+  return kv.pool + (blk * kPageSize + (pos % kPageSize)) * kHeadDim;
+}
+
+// ---------------------------------------------------------------------------
+// Epilogues, run by the root CTA of a tile with v[a][mm] = column tcol+tid of
+// matrix a for input row m0+mm.  All 256 threads take part.
+template <int MB, int NM, int EPI>
+__device__ __forceinline__ void gemv_epilogue(const GemvDesc& d, const FrameCodes& fc, float (&v)[NM][MB], int mat,
+                                              int tile, int tcol, int m0, int mcnt, int zb, float* sbuf,
+                                              float* ybuf) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n = d.mat[mat].n;
+  const int col = tcol + tid;
+  const bool cval = col < n;
+  const EpiDesc& e = d.epi;
+  if (EPI == EPI_STORE || EPI == EPI_RESID) {
+    const int cgl = d.col0[mat] + col;
+    const int ltile = (NM == 2 ? tile : tile - d.tile0[mat]);
+#pragma unroll
+    for (int mm = 0; mm < MB; ++mm) {
+      float val = 0.0f;
+      if (cval && mm < mcnt) {
+        if (EPI == EPI_STORE) {
+          val = v[0][mm];
+          if (e.bias) val = val + e.bias[cgl];
+          if (e.act_silu) val = silu_ref(val);
+          e.out[(size_t)(m0 + mm) * e.ldo + cgl] = val;
+        } else {
+          float* o = e.out + (size_t)(m0 + mm) * e.ldo + cgl;
+          val = *o + v[0][mm];
+          *o = val;
+        }
+      }
+      if (e.ssq_out) {  // uniform branch: every thread takes part in the block sum
+        const float ss = block_sum_256(val * val, sbuf);
+        if (tid == 0 && mm < mcnt) e.ssq_out[(size_t)(m0 + mm) * e.ssq_ld + ltile] = ss;
+      }
+    }
+  } else if (EPI == EPI_SWIGLU) {
+#pragma unroll
+    for (int mm = 0; mm < MB; ++mm) {
+      if (!cval || mm >= mcnt) continue;
+      e.out[(size_t)(m0 + mm) * e.ldo + col] = silu_ref(v[0][mm]) * v[NM - 1][mm];
+    }
+  } else if (EPI == EPI_QKV) {
+    // mat 0 = q, 1 = k, 2 = v; heads of 128 columns never straddle a tile.
+    const int h = col / kHeadDim, dd = col % kHeadDim, hl = tid / kHeadDim;
+#pragma unroll
+    for (int mm = 0; mm < MB; ++mm) {
+      const int m = m0 + mm;
+      const bool live = mm < mcnt;
+      int sess = 0, pos = 0, kvp = 0;
+      if (live) row_pos(e.rp, m, sess, pos, kvp);
+      if (mat == 2) {
+        if (live && cval) {
+          KvDesc kv = e.kv;
+          kv_row(kv, sess, kvp, 1, h)[dd] = v[0][mm];
+        }
+        continue;
+      }
+      // QK-norm (talker.rs:89-99): per head of 128 = 4 warps
+      float x = (live && cval) ? v[0][mm] : 0.0f;
+      float sq = x * x;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      __syncthreads();
+      if (lane == 0) sbuf[warp] = sq;
+      __syncthreads();
+      const float ss = sbuf[hl * 4 + 0] + sbuf[hl * 4 + 1] + sbuf[hl * 4 + 2] + sbuf[hl * 4 + 3];
+      const float inv = 1.0f / sqrtf(ss / (float)kHeadDim + 1e-6f);
+      const __half* g = (mat == 0) ? e.q_norm : e.k_norm;
+      const float y = x * inv * h2f(g[dd]);
+      ybuf[mm * kTileN + tid] = y;
+      __syncthreads();
+      // split-half RoPE (rope.rs:79-92, code_predictor.rs:108-120)
+      const int half = kHeadDim / 2, i = dd % half;
+      const float x1 = ybuf[mm * kTileN + hl * kHeadDim + i];
+      const float x2 = ybuf[mm * kTileN + hl * kHeadDim + half + i];
+      float outv = y;
+      if (live && cval) {
+        if (pos < e.rope_rows && pos >= 0) {
+          const float c = e.rope_cos[(size_t)pos * half + i];
+          const float sn = e.rope_sin[(size_t)pos * half + i];
+          outv = (dd < half) ? (x1 * c - x2 * sn) : (x2 * c + x1 * sn);
+        } else if (!e.rope_skip_oob && e.err_flag) {
+          atomicOr(e.err_flag, 1);
+        }
+        if (mat == 0) {
+          e.q_out[(size_t)m * e.ldq + col] = outv;
+        } else {
+          KvDesc kv = e.kv;
+          kv_row(kv, sess, kvp, 0, h)[dd] = outv;
+        }
+      }
+    }
+  } else if (EPI == EPI_ARGMAX) {
+    __shared__ unsigned long long s_key[8];
+    __shared__ unsigned s_last;
+#pragma unroll
+    for (int mm = 0; mm < MB; ++mm) {
+      unsigned long long key = 0ull;
+      if (cval && mm < mcnt) key = ((unsigned long long)f32_order_key(v[0][mm]) << 32) | (unsigned)col;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+        key = other > key ? other : key;
+      }
+      __syncthreads();
+      if (lane == 0) s_key[warp] = key;
+      __syncthreads();
+      if (tid == 0 && mm < mcnt) {
+        unsigned long long best = s_key[0];
+        for (int w8 = 1; w8 < 8; ++w8) best = s_key[w8] > best ? s_key[w8] : best;
+        atomicMax(e.keys + m0 + mm, best);
+      }
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(e.counters2 + zb, 1u);
+    __syncthreads();
+    if (s_last != (unsigned)(d.ntiles - 1)) return;
+    __threadfence();
+    if (tid < mcnt) {
+      const int m = m0 + tid;
+      const unsigned long long key = atomicExch(e.keys + m, 0ull);
+      const uint32_t code = (uint32_t)(key & 0xffffffffull);
+      if (e.frame_codes) {
+        SlotState& sl = fc.slots[m];
+        const int f = sl.frame;
+        const size_t at = ((size_t)m * fc.max_frames + f) * kMaxGroups + e.group;
+        uint32_t used = code;
+        if (f < fc.max_frames) {
+          fc.codes[at] = code;
+          if (fc.forced) used = fc.forced[at];
+        }
+        sl.cur[e.group] = used;
+        sl.prev[e.group] = used;
+      } else {
+        e.codes_plain[(size_t)m * kMaxGroups + e.group] = code;
+      }
+    }
+    if (tid == 0) e.counters2[zb] = 0u;
+  }
+}
+
+}  // namespace
+}  // namespace qtts

@@ -134,6 +134,13 @@ struct GemvDesc {
   int pdl = 0;
   float* part = nullptr;        // [S][M][ncols]
   unsigned* counters = nullptr; // [ntiles * zblocks], left at zero
+  // tensor-core path (tc_gemm.cu): tc = 1 routes the launch through the
+  // operand split, the tcgen05 GEMM (S K-slices of tc_ks 64-deep stages,
+  // partials in part) and the epilogue kernel
+  int tc = 0;
+  int tc_ks = 0;
+  __half* xsplit = nullptr;     // fp16 hi/lo operand blocks, tc_xsplit_halves(M, k)
+  int* err_flag = nullptr;      // bounded-wait expiry (bit 2)
   EpiDesc epi;
 };
 constexpr int kMaxClusterSplits = 16;
@@ -171,6 +178,8 @@ struct FrameCodes {
 // PDL lets a kernel start (and prefetch its weights) while its predecessor
 // finishes; the kernel's griddepcontrol.wait orders all dependent reads.
 bool pdl_enabled();
+// kernels launched through launch_k by this thread (frame-plan kernel counts)
+inline thread_local long g_kernel_launches = 0;
 struct LaunchOpts {
   bool pdl = false;
   unsigned cluster_y = 1;  // CTAs of one cluster along grid.y
@@ -199,12 +208,26 @@ inline cudaError_t launch_k(Kern kern, dim3 grid, dim3 block, size_t smem, cudaS
   }
   cfg.attrs = at;
   cfg.numAttrs = n;
+  ++g_kernel_launches;
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
 // ---- launchers (return cudaError_t of the launch) ----
 size_t gemv_smem_bytes(const GemvDesc& d);
 cudaError_t launch_gemv(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st);
+
+// tensor-core path (tc_gemm.cu)
+constexpr int kTcRows = 128;     // MMA tile rows (TMEM lanes)
+constexpr int kTcCols = 128;     // CTA tile columns per matrix
+constexpr int kTcK = 64;         // K per pipeline stage
+constexpr int kTcMinRows = 16;   // projections with M >= this take the tensor cores
+bool tc_enabled();               // QTTS_TC=0 keeps every projection on the CUDA cores
+void tc_plan(int sm_count, GemvDesc& g);   // sets tc = 1 and tc_ks
+int tc_splits(const GemvDesc& d);          // K slices of a planned launch
+size_t tc_xsplit_halves(int M, int k);     // operand-split buffer size (fp16 elements)
+size_t tc_smem_bytes(int nm);
+cudaError_t launch_tc(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st);
+void tc_init_attributes();
 
 struct AttnDesc {
   const float* q = nullptr;  // row m: heads*128

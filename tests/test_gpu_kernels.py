@@ -55,8 +55,9 @@ SHAPES = [  # (k=in, n=out): BASELINE config 2 and the real model shapes
 
 
 @pytest.mark.parametrize("k,n", SHAPES)
-@pytest.mark.parametrize("m", [1, 2, 3, 8])
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 16, 64, 130])
 def test_q4_gemv_matches_float64(qtts, k, n, m):
+    # m >= 16 runs on the tcgen05 path (fp16 hi/lo operands, f32 accumulate)
     rng = np.random.default_rng(k * 7 + n + m)
     packed, scales = rand_q4(rng, k, n)
     x = rng.standard_normal((m, k)).astype(np.float32)

@@ -150,6 +150,31 @@ def test_batched_equals_single(qtts, gpu_tiny):
         assert rel_err(lb[i], l1[0]) < 1e-5, i
 
 
+def _forced_batch(cases, F):
+    """Golden codes of each case padded to F frames (last row repeated)."""
+    out = []
+    for c in cases:
+        codes = golden(c)["codes"]
+        pad = np.repeat(codes[-1:], max(0, F - codes.shape[0]), axis=0)
+        out.append(np.concatenate([codes, pad])[:F])
+    return np.stack(out).astype(np.uint32)
+
+
+def test_batched_tensor_core_teacher_forced_tiny(qtts, gpu_tiny):
+    # 20 utterances: every projection of the frame has M >= 16 rows and runs
+    # on the tcgen05 path; each utterance must still match its own oracle run
+    H = gpu_tiny.dims.t_hidden
+    base = ["tiny_greedy", "tiny_sampled", "tiny_speaker", "tiny_notext"]
+    cases = base * 5
+    F = 24
+    s = qtts.Session(gpu_tiny, len(cases), 10 + F)
+    codes, frames, lg, _ = qtts.generate(s, [tiny_case(c, H) for c in cases], F,
+                                         forced=_forced_batch(cases, F), dump_logits=True)
+    s.close()
+    for i, c in enumerate(cases):
+        _check_forced(codes[i], golden(c), lg[i])
+
+
 def test_generate_deterministic(qtts, gpu_tiny):
     u = tiny_case("tiny_sampled", gpu_tiny.dims.t_hidden)
     s = qtts.Session(gpu_tiny, 1, 40)
@@ -194,3 +219,20 @@ def test_1p7b_config3_sampled_teacher_forced(qtts, gpu_1p7b):
     codes, frames, lg, _ = qtts.generate(s, [u], F, forced=g["codes"][None], dump_logits=True)
     _check_forced(codes[0], g, lg[0], max_ties=1)
     s.close()
+
+
+@pytest.mark.slow
+def test_1p7b_config1_batched_tensor_core(qtts, gpu_1p7b):
+    # config 1 replicated 16 times: the frame's projections run with M = 16
+    # on the tcgen05 path and every copy must follow the oracle
+    from qtts_b200 import workload as W
+    g = golden("p1p7b_config1")
+    u, F = W.config1(2048)
+    n = 16
+    s = qtts.Session(gpu_1p7b, n, 10 + F)
+    codes, frames, lg, _ = qtts.generate(s, [u] * n, F, forced=np.repeat(g["codes"][None], n, axis=0),
+                                         dump_logits=True)
+    s.close()
+    for i in range(n):
+        assert frames[i] == F
+        _check_forced(codes[i], g, lg[i], max_ties=1)
