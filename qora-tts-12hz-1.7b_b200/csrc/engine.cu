@@ -10,6 +10,9 @@
 #include <string.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
 #include <cmath>
 #include <string>
 #include <vector>
@@ -261,6 +264,54 @@ static GemvDesc gemv_base(int epi, std::initializer_list<Q4Mat> mats, bool paire
   return g;
 }
 
+// cudaOccupancyMaxActiveClusters per (kernel, cluster size, shared memory,
+// block size), cached: planning asks for the same few shapes over and over.
+int occupancy_clusters(const void* func, const cudaLaunchConfig_t& cfg) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, unsigned, size_t, unsigned, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  unsigned cy = 1;
+  for (unsigned i = 0; i < cfg.numAttrs; ++i)
+    if (cfg.attrs[i].id == cudaLaunchAttributeClusterDimension) cy = cfg.attrs[i].val.clusterDim.y;
+  const auto key = std::make_tuple(func, cy, cfg.dynamicSmemBytes, cfg.blockDim.x, dev);
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, func, &cfg) != cudaSuccess) n = 0;
+  cudaGetLastError();
+  cache[key] = n;
+  return n;
+}
+
+// Clusters of g's launch (as launch_gemv would issue it) that fit at once.
+int gemv_wave_clusters(const GemvDesc& g) {
+  g_occ_query = true;
+  g_occ_clusters = 0;
+  launch_gemv(g, FrameCodes{}, nullptr);
+  g_occ_query = false;
+  return g_occ_clusters;
+}
+
+// With a cluster-reduced K split, every (tile, row block) is one cluster and
+// all of them should be resident in one wave: lower S until they fit.
+static void fit_split_to_wave(GemvDesc& g) {
+  if (g.tc || !g.cluster) return;
+  const long units = (long)g.ntiles * ceil_div(g.M, g.mb);
+  for (int S = g.S; S >= 1; --S) {
+    GemvDesc t = g;
+    const int rps = std::min(ceil_div(ceil_div(g.k, S), 32) * 32, 2048);
+    t.rows_per_split = rps;
+    t.S = ceil_div(g.k, rps);
+    if (t.S > S) continue;
+    if (gemv_wave_clusters(t) >= units) {
+      g = t;
+      return;
+    }
+  }
+}
+
 // Split-K choice: about two CTAs per SM, slices of whole 32-row blocks, at
 // most 2048 rows per slice (shared-memory bound of the input slice).
 void choose_split(int sm_count, GemvDesc& g) {
@@ -285,40 +336,27 @@ static int dalloc(T** p, size_t count, std::vector<void*>* track = nullptr) {
   return QTTS_OK;
 }
 
-// Grow the tensor-core scratch (operand blocks, split-K partials) to a
-// projection's need.  Planned ops read the pointers when they launch, so a
-// reallocation between planning and running is safe; a live frame graph has
-// them baked in, so growing is refused while one exists.
-static int tc_reserve(Session& s, size_t xsplit_halves, size_t part_floats) {
-  if (xsplit_halves <= s.xsplit_halves && part_floats <= s.part_floats) return QTTS_OK;
-  if (s.graph_exec) return fail(QTTS_ERR_STATE, "tensor-core scratch must grow while a generation is live");
-  CK(cudaStreamSynchronize(s.st));
-  if (xsplit_halves > s.xsplit_halves) {
-    if (s.xsplit) cudaFree(s.xsplit);
-    s.xsplit = nullptr;
-    s.xsplit_halves = 0;
-    RC(dalloc(&s.xsplit, xsplit_halves));
-    s.xsplit_halves = xsplit_halves;
-  }
-  if (part_floats > s.part_floats) {
-    if (s.part) cudaFree(s.part);
-    s.part = nullptr;
-    s.part_floats = 0;
-    RC(dalloc(&s.part, part_floats));
-    s.part_floats = part_floats;
-  }
-  return QTTS_OK;
-}
-
 static int plan_gemv(Session& s, GemvDesc& g) {
   choose_split(s.m->sm_count, g);
   g.cluster = 1;  // split-K partials reduced over distributed shared memory
   g.pdl = 1;
+  fit_split_to_wave(g);
   if (g.M >= kTcMinRows && tc_enabled()) {
-    tc_plan(s.m->sm_count, g);
-    RC(tc_reserve(s, tc_xsplit_halves(g.M, g.k), (size_t)tc_splits(g) * g.M * g.ncols));
-    g.err_flag = s.err_flag;  // xsplit / part are read from the session at launch (gemv_op)
+    tc_plan(s.m->sm_count, g);  // one tcgen05 kernel: prologue, GEMM, split-K, epilogue
+    g.err_flag = s.err_flag;
+    g.part = s.part;
+    const size_t zt = (size_t)ceil_div(g.M, kTcRows);
+    if (tc_splits(g) > 1 &&
+        ((size_t)tc_splits(g) * g.M * g.ncols > s.part_floats || 2 * (size_t)g.ntiles * zt > s.n_counters))
+      return fail(QTTS_ERR_OOM, "split-K scratch too small for this projection");
   }
+  static const bool log_plans = [] {
+    const char* v = getenv("QTTS_PLAN_LOG");
+    return v && v[0] == '1';
+  }();
+  if (log_plans)
+    fprintf(stderr, "qtts plan: epi %d k %d ncols %d M %d -> %s S %d rows/split %d\n", g.epi_kind, g.k, g.ncols, g.M,
+            g.tc ? "tcgen05" : "cuda-core", g.tc ? tc_splits(g) : g.S, g.tc ? g.tc_ks * kTcK : g.rows_per_split);
   const size_t zb = (size_t)ceil_div(g.M, g.mb);
   if ((size_t)g.ntiles * zb > s.n_counters || zb > 4096) return fail(QTTS_ERR_OOM, "tile counter array too small");
   g.counters = s.counters;
@@ -329,16 +367,8 @@ static int plan_gemv(Session& s, GemvDesc& g) {
   return QTTS_OK;
 }
 
-static Op gemv_op(Session& s, const GemvDesc& g, const FrameCodes& fc = FrameCodes{}) {
-  Session* sp = &s;
-  return [sp, g, fc](cudaStream_t st) {
-    GemvDesc d = g;
-    if (d.tc) {
-      d.xsplit = sp->xsplit;
-      d.part = sp->part;
-    }
-    return launch_gemv(d, fc, st);
-  };
+static Op gemv_op(const GemvDesc& g, const FrameCodes& fc = FrameCodes{}) {
+  return [g, fc](cudaStream_t st) { return launch_gemv(g, fc, st); };
 }
 
 struct LayerIO {
@@ -363,7 +393,7 @@ struct LayerIO {
 // RMSNorm+gate/up+SwiGLU | down+residual.
 static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const LayerIO& io) {
   const int qd = io.heads * kHeadDim;
-  const int nt = ceil_div(io.ldx > 0 ? L.q.k : 0, kTileN);  // tiles of a residual row
+  const int nt = ceil_div(io.ldx > 0 ? L.q.k : 0, kSsqCols);  // sum-of-squares blocks of a residual row
   auto use_ssq = [&](GemvDesc& gd, bool valid) {
     if (io.ssq && valid) {
       gd.ssq_in = io.ssq; gd.ssq_ld = kSsqLd; gd.ssq_n = nt;
@@ -381,7 +411,7 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
   g.epi.rope_cos = io.cos; g.epi.rope_sin = io.sin; g.epi.rope_rows = io.rope_rows; g.epi.rope_skip_oob = io.skip_oob;
   g.epi.heads = io.heads; g.epi.kv_heads = io.kvh; g.epi.kv = io.kv; g.epi.rp = io.rp; g.epi.err_flag = s.err_flag;
   RC(plan_gemv(s, g));
-  ops.push_back(gemv_op(s, g));
+  ops.push_back(gemv_op(g));
 
   AttnDesc a;
   a.q = s.q; a.ldq = qd; a.out = s.attn; a.ldo = qd; a.kv = io.kv; a.rp = io.rp;
@@ -399,19 +429,19 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
   o.X = s.attn; o.ldx = qd; o.epi.out = io.X; o.epi.ldo = io.ldx;
   emit_ssq(o);
   RC(plan_gemv(s, o));
-  ops.push_back(gemv_op(s, o));
+  ops.push_back(gemv_op(o));
 
   GemvDesc gu = gemv_base(EPI_SWIGLU, {L.gate, L.up}, true, io.M);
   gu.X = io.X; gu.ldx = io.ldx; gu.gamma = L.post_norm; gu.epi.out = s.h; gu.epi.ldo = io.inter;
   use_ssq(gu, true);
   RC(plan_gemv(s, gu));
-  ops.push_back(gemv_op(s, gu));
+  ops.push_back(gemv_op(gu));
 
   GemvDesc dn = gemv_base(EPI_RESID, {L.down}, false, io.M);
   dn.X = s.h; dn.ldx = io.inter; dn.epi.out = io.X; dn.epi.ldo = io.ldx;
   emit_ssq(dn);
   RC(plan_gemv(s, dn));
-  ops.push_back(gemv_op(s, dn));
+  ops.push_back(gemv_op(dn));
   return QTTS_OK;
 }
 
@@ -457,11 +487,11 @@ static int add_codec_head(Session& s, std::vector<Op>& ops, const float* X, long
                           float* hid, long ldh, long ssq_row0 = 0, long ssq_rows_step = 1) {
   GemvDesc g = gemv_base(EPI_STORE, {s.m->codec_head}, false, M);
   g.X = X; g.ldx = ldx; g.gamma = s.m->t_final;
-  g.ssq_in = s.ssq_t + ssq_row0 * kSsqLd; g.ssq_ld = ssq_rows_step * kSsqLd; g.ssq_n = ceil_div(s.m->d.t_hidden, kTileN);
+  g.ssq_in = s.ssq_t + ssq_row0 * kSsqLd; g.ssq_ld = ssq_rows_step * kSsqLd; g.ssq_n = ceil_div(s.m->d.t_hidden, kSsqCols);
   g.epi.out = logits; g.epi.ldo = s.m->d.t_vocab;
   g.xnorm_out = hid; g.ld_xnorm = ldh;
   RC(plan_gemv(s, g));
-  ops.push_back(gemv_op(s, g));
+  ops.push_back(gemv_op(g));
   return QTTS_OK;
 }
 
@@ -473,12 +503,12 @@ static int add_predictor(Session& s, std::vector<Op>& ops, int B, bool frame_mod
   const qtts_dims& d = m.d;
   const int pH = d.p_hidden;
   // project_input of both prefill rows (code_predictor.rs:235-236)
-  const int pnt = ceil_div(pH, kTileN);
+  const int pnt = ceil_div(pH, kSsqCols);
   GemvDesc pj = gemv_base(EPI_STORE, {m.input_proj}, false, 2 * B);
   pj.X = s.pin; pj.ldx = d.t_hidden; pj.epi.out = s.px; pj.epi.ldo = pH; pj.epi.bias = m.input_proj_b;
   pj.epi.ssq_out = s.ssq_p; pj.epi.ssq_ld = kSsqLd;
   RC(plan_gemv(s, pj));
-  ops.push_back(gemv_op(s, pj));
+  ops.push_back(gemv_op(pj));
   auto layers = [&](float* X, int M, const RowPos& rp, float* ssq) -> int {
     for (int l = 0; l < d.p_layers; ++l) {
       LayerIO io;
@@ -500,7 +530,7 @@ static int add_predictor(Session& s, std::vector<Op>& ops, int B, bool frame_mod
     h.ssq_in = ssq; h.ssq_ld = ssq_ld; h.ssq_n = pnt;
     h.epi.group = g + 1; h.epi.frame_codes = frame_mode ? 1 : 0; h.epi.codes_plain = s.codes_plain;
     RC(plan_gemv(s, h));
-    ops.push_back(gemv_op(s, h, fc));
+    ops.push_back(gemv_op(h, fc));
     return QTTS_OK;
   };
   RC(head(s.px + pH, 2L * pH, 0, s.ssq_p + kSsqLd, 2L * kSsqLd));
@@ -517,7 +547,7 @@ static int add_predictor(Session& s, std::vector<Op>& ops, int B, bool frame_mod
     pe.epi.out = s.px1; pe.epi.ldo = pH; pe.epi.bias = m.input_proj_b;
     pe.epi.ssq_out = s.ssq_p1; pe.epi.ssq_ld = kSsqLd;
     RC(plan_gemv(s, pe));
-    ops.push_back(gemv_op(s, pe));
+    ops.push_back(gemv_op(pe));
     RowPos rp;
     rp.pos_const = g + 1;
     RC(layers(s.px1, B, rp, s.ssq_p1));
@@ -535,12 +565,12 @@ static int add_text_proj(Session& s, std::vector<Op>& ops, const uint32_t* tok_d
   g1.emb = m.text_emb; g1.emb_idx = tok_dev; g1.emb_idx_stride = 1;
   g1.epi.out = h1; g1.epi.ldo = m.fc1.n; g1.epi.bias = m.fc1_b; g1.epi.act_silu = 1;
   RC(plan_gemv(s, g1));
-  ops.push_back(gemv_op(s, g1));
+  ops.push_back(gemv_op(g1));
   GemvDesc g2 = gemv_base(EPI_STORE, {m.fc2}, false, n);
   g2.X = h1; g2.ldx = m.fc1.n;
   g2.epi.out = out; g2.epi.ldo = ldo; g2.epi.bias = m.fc2_b;
   RC(plan_gemv(s, g2));
-  ops.push_back(gemv_op(s, g2));
+  ops.push_back(gemv_op(g2));
   return QTTS_OK;
 }
 
@@ -587,7 +617,7 @@ static void session_free_all(Session* s) {
   free_generation(*s);
   void* bufs[] = {s->kv_pool, s->page_table, s->pkv_pool, s->slots, s->x, s->pin, s->q, s->attn, s->h,
                   s->px, s->px1, s->logits, s->xpre, s->hid1, s->part, s->counters, s->counters2, s->keys,
-                  s->apart, s->acounters, s->err_flag, s->codes_plain, s->io, s->ssq_t, s->ssq_p, s->ssq_p1, s->xsplit};
+                  s->apart, s->acounters, s->err_flag, s->codes_plain, s->io, s->ssq_t, s->ssq_p, s->ssq_p1};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (s->st) cudaStreamDestroy(s->st);
@@ -645,12 +675,6 @@ static int session_create(Model* m, int maxB, int maxP, Session** out) {
   A(&s->ssq_t, (size_t)s->rows * kSsqLd);
   A(&s->ssq_p, (size_t)2 * maxB * kSsqLd);
   A(&s->ssq_p1, (size_t)maxB * kSsqLd);
-  if (s->rows >= kTcMinRows) {  // fp16 hi/lo operand blocks of the tensor-core path
-    const int kmax = std::max({d.t_hidden, d.t_text_hidden, d.t_inter, d.p_hidden, d.p_inter,
-                               d.t_heads * kHeadDim, d.p_heads * kHeadDim});
-    s->xsplit_halves = tc_xsplit_halves(s->rows, kmax);
-    A(&s->xsplit, s->xsplit_halves);
-  }
   if (rc == QTTS_OK) {  // pages: slot b owns pages [b*pps, (b+1)*pps)
     std::vector<int> pt((size_t)maxB * s->pages_per_sess);
     for (size_t i = 0; i < pt.size(); ++i) pt[i] = (int)i;
@@ -1011,26 +1035,23 @@ static int gemv_plan_standalone(int k, int n, int m, GemvDesc& g) {
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaGetLastError();
+  gemv_init_attributes();  // the occupancy queries of the planners need them
+  tc_init_attributes();
   Q4Mat w;
   w.k = k;
   w.n = n;
   g = gemv_base(EPI_STORE, {w}, false, m);
   choose_split(sms, g);
-  if (m >= kTcMinRows && tc_enabled()) tc_plan(sms, g);
+  if (m >= kTcMinRows && k % 4 == 0 && tc_enabled()) tc_plan(sms, g);
   return QTTS_OK;
 }
 
-// Scratch layout: [counters 16 KB][split-K partials][tensor-core operand blocks]
-static size_t gemv_part_bytes(const GemvDesc& g) {
-  const int S = g.tc ? tc_splits(g) : g.S;
-  const size_t b = (g.tc || S > 1) ? sizeof(float) * (size_t)S * g.M * g.ncols : 0;
-  return (b + 255) & ~(size_t)255;
-}
-
+// Scratch layout: [tile counters 16 KB][split-K partials of either kernel]
 static size_t gemv_scratch(int k, int n, int m) {
   GemvDesc g;
   gemv_plan_standalone(k, n, m, g);
-  return kCounterBytes + gemv_part_bytes(g) + (g.tc ? 2 * tc_xsplit_halves(m, k) : 0);
+  const size_t S = std::max(g.S > 1 ? g.S : 0, g.tc && tc_splits(g) > 1 ? tc_splits(g) : 0);
+  return kCounterBytes + sizeof(float) * S * m * n;
 }
 
 static int gemv_dev(const uint8_t* packed, const uint16_t* scales, int k, int n, const float* x, int m, float* y,
@@ -1047,16 +1068,21 @@ static int gemv_dev(const uint8_t* packed, const uint16_t* scales, int k, int n,
   g.mat[0].scales = reinterpret_cast<const __half*>(scales);
   g.X = x; g.ldx = k;
   g.epi.out = y; g.epi.ldo = n;
-  const size_t zb = (size_t)ceil_div(m, g.mb);
-  if (g.ntiles * zb > kCounterBytes / 4) return fail(QTTS_ERR_BADARG, "too many tiles for the counter area");
+  const size_t zb = (size_t)ceil_div(m, g.mb), zt = (size_t)ceil_div(m, kTcRows);
+  if (g.ntiles * zb > kCounterBytes / 4 || 2 * g.ntiles * zt > kCounterBytes / 4)
+    return fail(QTTS_ERR_BADARG, "too many tiles for the counter area");
   const size_t need = gemv_scratch(k, n, m);
   if (!scratch || scratch_bytes < need) return fail(QTTS_ERR_BADARG, "scratch smaller than qtts_q4_gemv_scratch_bytes()");
   g.counters = reinterpret_cast<unsigned*>(scratch);
   g.part = reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + kCounterBytes);
-  if (g.tc) g.xsplit = reinterpret_cast<__half*>(reinterpret_cast<char*>(scratch) + kCounterBytes + gemv_part_bytes(g));
+  // the tensor-core kernel's float4 accesses need 16-byte aligned rows
+  if (g.tc && (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 16)) g.tc = 0;
   g.cluster = 1;
   gemv_init_attributes();
   tc_init_attributes();
+  fit_split_to_wave(g);
+  if (!g.tc && g.S > 1 && scratch_bytes < kCounterBytes + sizeof(float) * (size_t)g.S * m * n)
+    return fail(QTTS_ERR_BADARG, "scratch smaller than qtts_q4_gemv_scratch_bytes()");
   const cudaError_t e = launch_gemv(g, FrameCodes{}, st);
   if (e != cudaSuccess) return fail(QTTS_ERR_CUDA, cudaGetErrorString(e));
   return QTTS_OK;

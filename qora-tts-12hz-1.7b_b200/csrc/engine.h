@@ -74,9 +74,6 @@ struct Session {
   // per-256-column sums of squares of residual rows (talker, predictor
   // prefill rows, predictor decode rows), row stride kSsqLd
   float *ssq_t = nullptr, *ssq_p = nullptr, *ssq_p1 = nullptr;
-  // tensor-core path: fp16 hi/lo operand blocks (tc_xsplit_halves)
-  __half* xsplit = nullptr;
-  size_t xsplit_halves = 0;
   size_t io_floats = 0;
   // generation
   int B = 0, max_frames = 0, max_trail = 0;

@@ -32,6 +32,41 @@ __device__ __forceinline__ float block_sum_256(float v, float* sbuf) {
   return t;
 }
 
+// Final code of row m once every tile has folded its maximum into keys[m]
+// (the key is (order key << 32) | column, so the last index wins ties):
+// record it for the frame (teacher forcing substitutes the forced code) or
+// in the plain code array, and reset the key.
+__device__ __forceinline__ void argmax_finalize_row(const EpiDesc& e, const FrameCodes& fc, int m) {
+  const unsigned long long key = atomicExch(e.keys + m, 0ull);
+  const uint32_t code = (uint32_t)(key & 0xffffffffull);
+  if (e.frame_codes) {
+    SlotState& sl = fc.slots[m];
+    const int f = sl.frame;
+    const size_t at = ((size_t)m * fc.max_frames + f) * kMaxGroups + e.group;
+    uint32_t used = code;
+    if (f < fc.max_frames) {
+      fc.codes[at] = code;
+      if (fc.forced) used = fc.forced[at];
+    }
+    sl.cur[e.group] = used;
+    sl.prev[e.group] = used;
+  } else {
+    e.codes_plain[(size_t)m * kMaxGroups + e.group] = code;
+  }
+}
+
+// Sum over the thread's half of a 256-thread block (threads 0-127 / 128-255).
+__device__ __forceinline__ float block_sum_half(float v, float* sbuf) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) sbuf[warp] = v;
+  __syncthreads();
+  const int w0 = warp & 4;
+  return (sbuf[w0] + sbuf[w0 + 1]) + (sbuf[w0 + 2] + sbuf[w0 + 3]);
+}
+
 __device__ __forceinline__ float* kv_row(const KvDesc& kv, int sess, int pos, int which, int h) {
   const int page = kv.page_table ? kv.page_table[sess * kv.pages_per_sess + pos / kPageSize] : sess;
   const size_t blk = (((size_t)page * kv.n_layers + kv.layer) * 2 + which) * kv.kv_heads + h;
@@ -68,9 +103,10 @@ __device__ __forceinline__ void gemv_epilogue(const GemvDesc& d, const FrameCode
           *o = val;
         }
       }
-      if (e.ssq_out) {  // uniform branch: every thread takes part in the block sum
-        const float ss = block_sum_256(val * val, sbuf);
-        if (tid == 0 && mm < mcnt) e.ssq_out[(size_t)(m0 + mm) * e.ssq_ld + ltile] = ss;
+      if (e.ssq_out) {  // uniform branch: every thread takes part in the half-tile sums
+        const float ss = block_sum_half(val * val, sbuf);
+        const int hb = ltile * 2 + (tid >> 7);  // 128-column block of the row
+        if ((tid & 127) == 0 && mm < mcnt && tcol + (tid & 128) < n) e.ssq_out[(size_t)(m0 + mm) * e.ssq_ld + hb] = ss;
       }
     }
   } else if (EPI == EPI_SWIGLU) {
@@ -157,25 +193,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvDesc& d, const FrameCode
     __syncthreads();
     if (s_last != (unsigned)(d.ntiles - 1)) return;
     __threadfence();
-    if (tid < mcnt) {
-      const int m = m0 + tid;
-      const unsigned long long key = atomicExch(e.keys + m, 0ull);
-      const uint32_t code = (uint32_t)(key & 0xffffffffull);
-      if (e.frame_codes) {
-        SlotState& sl = fc.slots[m];
-        const int f = sl.frame;
-        const size_t at = ((size_t)m * fc.max_frames + f) * kMaxGroups + e.group;
-        uint32_t used = code;
-        if (f < fc.max_frames) {
-          fc.codes[at] = code;
-          if (fc.forced) used = fc.forced[at];
-        }
-        sl.cur[e.group] = used;
-        sl.prev[e.group] = used;
-      } else {
-        e.codes_plain[(size_t)m * kMaxGroups + e.group] = code;
-      }
-    }
+    if (tid < mcnt) argmax_finalize_row(e, fc, m0 + tid);
     if (tid == 0) e.counters2[zb] = 0u;
   }
 }

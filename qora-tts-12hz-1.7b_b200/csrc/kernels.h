@@ -86,7 +86,8 @@ struct EpiDesc {
   RowPos rp;
   int* err_flag = nullptr;
   // STORE / RESID: per-tile sums of squares of the written row values,
-  // ssq_out[m * ssq_ld + tile], consumed by the next RMSNorm prologue
+  // ssq_out[m * ssq_ld + t]: sum of squares of the row's kSsqCols-column
+  // block t, consumed by the next RMSNorm prologue
   float* ssq_out = nullptr;
   long ssq_ld = 0;
   // ARGMAX: keys[m] accumulates (order_key(v) << 32 | col); the last tile
@@ -134,13 +135,12 @@ struct GemvDesc {
   int pdl = 0;
   float* part = nullptr;        // [S][M][ncols]
   unsigned* counters = nullptr; // [ntiles * zblocks], left at zero
-  // tensor-core path (tc_gemm.cu): tc = 1 routes the launch through the
-  // operand split, the tcgen05 GEMM (S K-slices of tc_ks 64-deep stages,
-  // partials in part) and the epilogue kernel
+  // tensor-core path (tc_gemm.cu): tc = 1 runs the projection as one
+  // tcgen05 kernel with K slices of tc_ks 64-deep stages reduced inside a
+  // thread-block cluster
   int tc = 0;
   int tc_ks = 0;
-  __half* xsplit = nullptr;     // fp16 hi/lo operand blocks, tc_xsplit_halves(M, k)
-  int* err_flag = nullptr;      // bounded-wait expiry (bit 2)
+  int* err_flag = nullptr;      // bit 4: a bounded wait expired; bit 8: input outside the fp16 range
   EpiDesc epi;
 };
 constexpr int kMaxClusterSplits = 16;
@@ -149,6 +149,7 @@ constexpr int kMaxClusterSplits = 16;
 constexpr int kDecRowsNM1 = 12;  // rows per split <= 384
 constexpr int kDecRowsNM2 = 6;   // rows per split <= 192
 constexpr int kSsqLd = 64;       // row stride of the sum-of-squares partials
+constexpr int kSsqCols = 128;    // columns summed per partial (rows up to 64 * 128 wide)
 
 // Frame bookkeeping shared by the sampler / argmax epilogue / fusion.
 struct SlotState {
@@ -180,6 +181,12 @@ struct FrameCodes {
 bool pdl_enabled();
 // kernels launched through launch_k by this thread (frame-plan kernel counts)
 inline thread_local long g_kernel_launches = 0;
+// Occupancy query mode: with g_occ_query set, launch_k launches nothing and
+// stores in g_occ_clusters how many clusters of the launch fit on the device
+// at once (cudaOccupancyMaxActiveClusters), so planners can size one wave.
+inline thread_local bool g_occ_query = false;
+inline thread_local int g_occ_clusters = 0;
+int occupancy_clusters(const void* func, const cudaLaunchConfig_t& cfg);
 struct LaunchOpts {
   bool pdl = false;
   unsigned cluster_y = 1;  // CTAs of one cluster along grid.y
@@ -208,6 +215,10 @@ inline cudaError_t launch_k(Kern kern, dim3 grid, dim3 block, size_t smem, cudaS
   }
   cfg.attrs = at;
   cfg.numAttrs = n;
+  if (g_occ_query) {
+    g_occ_clusters = occupancy_clusters(reinterpret_cast<const void*>(kern), cfg);
+    return cudaSuccess;
+  }
   ++g_kernel_launches;
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
@@ -222,9 +233,8 @@ constexpr int kTcCols = 128;     // CTA tile columns per matrix
 constexpr int kTcK = 64;         // K per pipeline stage
 constexpr int kTcMinRows = 16;   // projections with M >= this take the tensor cores
 bool tc_enabled();               // QTTS_TC=0 keeps every projection on the CUDA cores
-void tc_plan(int sm_count, GemvDesc& g);   // sets tc = 1 and tc_ks
+void tc_plan(int sm_count, GemvDesc& g);   // sets tc = 1 and tc_ks (K split fitted to one wave)
 int tc_splits(const GemvDesc& d);          // K slices of a planned launch
-size_t tc_xsplit_halves(int M, int k);     // operand-split buffer size (fp16 elements)
 size_t tc_smem_bytes(int nm);
 cudaError_t launch_tc(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st);
 void tc_init_attributes();
@@ -276,7 +286,7 @@ struct FuseDesc {
   int max_trail = 0;
   const float* tts_pad = nullptr;  // [H]
   int B = 0, H = 0;
-  float* ssq_out = nullptr;      // per-256-column sums of squares of x [B][ssq_ld]
+  float* ssq_out = nullptr;      // per-128-column sums of squares of x [B][ssq_ld]
   long ssq_ld = 0;
   FrameCodes fc;
   int mode = 0;                  // 0: full frame fusion; 1: semantic only (sem_out); 2: acoustic sum only

@@ -56,17 +56,17 @@ __global__ void fuse_kernel(const FuseDesc d) {
   const float* ta = (f < ntr) ? d.trail + ((size_t)b * d.max_trail + f) * d.H : d.tts_pad;
   const float xv = (sem + acs) + ta[j];
   d.x[(size_t)b * d.ldx + j] = xv;
-  if (d.ssq_out) {  // sum of squares of this 256-column tile for the next RMSNorm
+  if (d.ssq_out) {  // sums of squares of this tile's two 128-column blocks for the next RMSNorm
     __shared__ float sred[8];
     float q = xv * xv;
 #pragma unroll
     for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
     if ((threadIdx.x & 31) == 0) sred[threadIdx.x >> 5] = q;
     __syncthreads();
-    if (threadIdx.x == 0) {
-      float t = 0.0f;
-      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += sred[w];
-      d.ssq_out[(size_t)b * d.ssq_ld + blockIdx.x] = t;
+    if ((threadIdx.x & 127) == 0) {
+      const int w0 = (threadIdx.x >> 5) & 4;
+      d.ssq_out[(size_t)b * d.ssq_ld + blockIdx.x * 2 + (threadIdx.x >> 7)] =
+          (sred[w0] + sred[w0 + 1]) + (sred[w0 + 2] + sred[w0 + 3]);
     }
   }
 }

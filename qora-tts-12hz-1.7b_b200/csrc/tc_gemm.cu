@@ -1,31 +1,33 @@
 // tc_gemm.cu -- batched Q4 projections on the sm_100a tensor cores (tcgen05).
 //
 // Serves a projection with M >= kTcMinRows input rows (batched decode,
-// prefill): gemm_q4 of gemv.rs:311-375 as a real GEMM, with the same
-// prologues and epilogues as the CUDA-core kernels of gemv.cu.  Three kernels
-// per projection:
+// prefill): gemm_q4 of gemv.rs:311-375 as a real GEMM, with the prologues of
+// the CUDA-core kernels (RMSNorm with the producer's sums of squares,
+// embedding gather) and the same epilogues, in ONE kernel per projection.
 //
-//  1. xsplit_kernel: the RMSNorm / embedding-gather prologue, writing the
-//     input rows as two fp16 operands hi + lo (hi = fp16(x), lo = fp16(x - hi),
-//     x = hi + lo to ~22 bits) already in the UMMA K-major core-matrix order,
-//     one 32 KB block (hi | lo) per (128-row block, 64-deep K stage), so that a
-//     stage of A is one bulk copy.
-//  2. tc_gemm_kernel: a CTA owns one 128-column tile (of both matrices of a
-//     gate/up pair) and one K slice.  Per 64-deep stage a bulk copy brings
-//     the A block (mbarrier complete_tx), the 128 threads dequantise the Q4
-//     tile into fp16 hi + lo in the UMMA MN-major core-matrix order (the Q4
-//     value (q-8)*scale has at most 14 significant bits, so hi + lo holds it
-//     exactly), and one thread issues hi*hi + hi*lo + lo*hi tcgen05.mma
-//     (kind::f16, f32 accumulate in TMEM) and commits them to the stage's
-//     mbarrier.  Two stages are in flight: the MMAs of stage i run while the
-//     threads dequantise stage i+1, and the A block of stage i+2 is fetched
-//     as soon as the MMAs of stage i have drained.  The accumulator is read
-//     back with tcgen05.ld and stored as this slice's partial.  Every
-//     mbarrier wait is bounded in time: on expiry the kernel records an
-//     error, drains (bounded) its own copies and MMAs, frees its TMEM and
-//     returns.
-//  3. tc_epilogue_kernel: sums the K-slice partials in slice order
-//     (deterministic) and runs the epilogue of epilogue.cuh.
+// Work split.  A CTA (256 threads, one per SM) owns one 128-column tile (of
+// both matrices of a gate/up pair), one 128-row block of the input rows and
+// one K slice; the S K-slices of a tile form a thread-block cluster (1, S, 1),
+// with S chosen so that every cluster of the launch is resident in one wave.
+//
+// Main loop, per 64-deep K stage (2-3 stages in flight):
+//   * every thread converts its share of the stage into shared memory:
+//     A = the normalised input rows, B = the dequantised Q4 weights, each as
+//     two fp16 operands hi + lo with lo = fp16((v - hi) * 2^11).  The Q4 value
+//     (q-8)*scale has at most 14 significant bits, so hi + lo holds it
+//     exactly; an f32 input keeps ~22 bits.  Carrying lo scaled by 2^11 keeps
+//     it clear of the fp16 subnormal range.
+//   * one thread issues the tcgen05.mma (kind::f16, f32 accumulators in TMEM):
+//     D_main += A_hi*B_hi, D_cross += A_hi*B_lo + A_lo*B_hi, and commits them
+//     to the stage's mbarrier; the threads meanwhile convert the next stage.
+// Result = D_main + 2^-11 * D_cross (the dropped lo*lo term is ~2^-22).
+//
+// Epilogue: the accumulators go TMEM -> registers -> shared memory; the S
+// CTAs of the cluster then each take a slice of the rows, sum the S partials
+// over distributed shared memory in slice order (deterministic), and run the
+// projection's epilogue with one warp per row: bias/SiLU store, residual add
+// with per-128-column sums of squares, SwiGLU, per-head QK-norm + RoPE + KV
+// append (a head is one 128-column tile), or the greedy argmax.
 //
 // Shared-memory operand layout (no swizzle, 16-byte core-matrix rows):
 //   A (K-major):  row r, k-chunk c (8 elements) at (r/8)*1024 + c*128 + (r%8)*16
@@ -33,6 +35,10 @@
 //   B (MN-major): k row j, column group g (8 columns) at g*1024 + (j/8)*128 + (j%8)*16
 //                 -> LBO 128 B (next 8-deep K group), SBO 1024 B (next 8 columns)
 // A 16-deep MMA step advances both start addresses by 256 B.
+//
+// Every mbarrier wait is bounded in time; on expiry the kernel records an
+// error flag, waits (bounded) for its own MMAs, frees its TMEM and still
+// takes part in the cluster barriers, so no CTA is left waiting.
 #include <cuda_fp16.h>
 
 #include <algorithm>
@@ -45,13 +51,29 @@ namespace qtts {
 
 namespace {
 
-constexpr int TM = kTcRows;     // rows per MMA tile (TMEM lanes)
-constexpr int TN = kTcCols;     // columns per CTA tile (per matrix)
-constexpr int TK = kTcK;        // K per stage
-constexpr int STAGES = 2;
+constexpr int TM = kTcRows;  // rows per MMA tile (TMEM lanes)
+constexpr int TN = kTcCols;  // columns per CTA tile (per matrix)
+constexpr int TK = kTcK;     // K per stage
+constexpr int kThreads = 256;
 constexpr int A_BYTES = TM * TK * 2;  // 16 KB per operand half
 constexpr int B_BYTES = TN * TK * 2;  // 16 KB per operand half
+constexpr int kRedLd = TN + 4;        // staging row stride (floats)
+constexpr int kMaxSplits = 8;  // portable cluster size
+constexpr float kLoScale = 2048.0f;
+constexpr float kLoUnscale = 1.0f / 2048.0f;
 constexpr unsigned long long kWaitNs = 1000000000ull;  // 1 s bound on any wait
+constexpr int kErrTimeout = 4, kErrFp16Range = 8;      // err_flag bits
+
+template <int NM>
+struct TcCfg {
+  static constexpr int STAGES = NM == 1 ? 3 : 2;
+  static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * NM * B_BYTES;
+  static constexpr int PIPE_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int RED_BYTES = NM * TM * kRedLd * 4;
+  static constexpr int AUX = PIPE_BYTES > RED_BYTES ? PIPE_BYTES : RED_BYTES;
+  static constexpr int SMEM = AUX + 1024;  // + barriers, TMEM slot, 1/rms, flags
+  static constexpr uint32_t TMEM_COLS = NM * 2 * TN;  // main + cross per matrix
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -61,11 +83,29 @@ __device__ __forceinline__ unsigned long long globaltimer() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t dsmem_addr(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_dsmem4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
 __device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 // Parity wait bounded by kWaitNs; true when the phase completed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
@@ -88,16 +128,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
     }
   }
 }
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
 // SMEM matrix descriptor: start >> 4, LBO 128 B, SBO 1024 B, version 1, no swizzle.
-__device__ __forceinline__ uint64_t sdesc(const void* p) {
-  const uint64_t start = (smem_u32(p) >> 4) & 0x3FFFu;
-  return start | ((uint64_t)(128u >> 4) << 16) | ((uint64_t)(1024u >> 4) << 32) | (1ull << 46);
+__device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
+  return ((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128u >> 4) << 16) | ((uint64_t)(1024u >> 4) << 32) | (1ull << 46);
 }
 // Instruction descriptor, kind::f16: D f32, A fp16 K-major, B fp16 MN-major, M = 128, N = 128.
 constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | (1u << 16) |
@@ -114,10 +147,51 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
 
-__device__ __forceinline__ void split_h(float x, __half& hi, __half& lo) {
-  hi = __float2half_rn(x);
-  lo = __float2half_rn(x - __half2float(hi));
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+
+// f32 pair -> fp16 hi pair and fp16 (residual * 2^11) pair
+__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(a, b);
+  const float2 hf = __half22float2(h);
+  hi = h2_bits(h);
+  lo = h2_bits(__floats2half2_rn((a - hf.x) * kLoScale, (b - hf.y) * kLoScale));
+}
+
+// Q4 nibbles of byte `byte` of w (low nibble = even column) as half2 (q - 8), exact
+__device__ __forceinline__ __half2 nib_pair(uint32_t w, int byte) {
+  const uint32_t t = w >> (8 * byte);
+  uint32_t bits = (t & 0xFu) | ((t << 12) & 0xF0000u) | 0x64006400u;  // 1024 + q per half
+  return __hsub2(*reinterpret_cast<__half2*>(&bits), __float2half2_rn(1032.0f));
+}
+
+// 8 dequantised weights of one 32-bit word as hi / lo 16-byte core-matrix rows
+__device__ __forceinline__ void dequant_word(uint32_t w, __half2 s2, uint4& hi, uint4& lo) {
+  uint32_t h[4], l[4];
+  const __half2 sc = __float2half2_rn(kLoScale);
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const __half2 q = nib_pair(w, p);
+    const __half2 hh = __hmul2(q, s2);                      // fp16(q * scale)
+    const __half2 rr = __hfma2(q, s2, __hneg2(hh));          // exact residual
+    h[p] = h2_bits(hh);
+    l[p] = h2_bits(__hmul2(rr, sc));
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
 // 128-column tile t of the launch -> matrix, first column within it.
@@ -131,366 +205,486 @@ __device__ __forceinline__ int tc_tile(const GemvDesc& d, int t, int NMv, int& t
   return mat;
 }
 
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Input rows of one stage held in registers: pass p covers rows (tid & 63) + 64 p,
+// 16 consecutive k starting at 16 * (tid >> 6).
+struct ARegs {
+  float x[2][16];
+};
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
-// 1. prologue + operand split.  Grid (nks, ceil(M/TM)), 128 threads; thread r
-// converts row r of the (row block, K stage) block.
-__global__ void __launch_bounds__(128) xsplit_kernel(const GemvDesc d) {
-  pdl_launch_dependents();
-  pdl_wait();
-  const int ks = blockIdx.x, mb = blockIdx.y, r = threadIdx.x;
-  const int m = mb * TM + r;
-  const int nks = (d.k + TK - 1) / TK;
-  const int k0 = ks * TK;
-  __half* hi = d.xsplit + ((size_t)(mb * nks + ks) * 2) * (TM * TK);
-  __half* lo = hi + TM * TK;
-  float xv[TK];
-#pragma unroll
-  for (int j = 0; j < TK; ++j) xv[j] = 0.0f;
-  if (m < d.M) {
-    if (d.emb_idx) {
-      const uint32_t row = d.emb_idx[(size_t)m * d.emb_idx_stride];
-      const uint8_t* prow = d.emb.packed + (size_t)row * (d.emb.n / 2);
-      const __half* srow = d.emb.scales + (size_t)row * (d.emb.n / 32);
-#pragma unroll
-      for (int j = 0; j < TK; ++j)
-        if (k0 + j < d.k) xv[j] = q4_value(prow, srow, k0 + j);
-    } else {
-      const float* xr = d.X + (size_t)m * d.ldx;
-      if (d.gamma) {
-        float inv;
-        if (d.ssq_in) {
-          inv = inv_rms_from_ssq(d, m);
-        } else {
-          float ss = 0.0f;
-          for (int i = 0; i < d.k; ++i) ss += xr[i] * xr[i];
-          inv = 1.0f / sqrtf(ss / (float)d.k + 1e-6f);
-        }
-#pragma unroll
-        for (int j = 0; j < TK; ++j)
-          if (k0 + j < d.k) xv[j] = xr[k0 + j] * inv * h2f(d.gamma[k0 + j]);  // gemv.rs:408-417
-        if (d.xnorm_out) {
-#pragma unroll
-          for (int j = 0; j < TK; ++j)
-            if (k0 + j < d.k) d.xnorm_out[(size_t)m * d.ld_xnorm + k0 + j] = xv[j];
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < TK; ++j)
-          if (k0 + j < d.k) xv[j] = xr[k0 + j];
-      }
-    }
-  }
-  const int grp = r >> 3, rl = r & 7;
-#pragma unroll
-  for (int c = 0; c < TK / 8; ++c) {
-    __align__(16) __half h8[8];
-    __align__(16) __half l8[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) split_h(xv[c * 8 + j], h8[j], l8[j]);
-    const size_t off = (size_t)grp * 512 + (size_t)c * 64 + rl * 8;  // halves
-    *reinterpret_cast<uint4*>(hi + off) = *reinterpret_cast<const uint4*>(h8);
-    *reinterpret_cast<uint4*>(lo + off) = *reinterpret_cast<const uint4*>(l8);
-  }
-}
-
-// ---------------------------------------------------------------------------
-// 2. the tensor-core GEMM.  Grid (2 * ntiles, S, ceil(M/TM)), 128 threads.
-template <int NM>
-__global__ void __launch_bounds__(128, 1) tc_gemm_kernel(const GemvDesc d) {
+// Grid (2 * ntiles, S, ceil(M / 128)), cluster (1, S, 1), 256 threads.
+template <int NM, int EPI>
+__global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, const FrameCodes fc) {
+  using C = TcCfg<NM>;
   extern __shared__ __align__(1024) uint8_t tsm[];
-  // per stage: A hi | A lo | B hi (NM matrices) | B lo (NM matrices); then barriers
-  constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * NM * B_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(tsm + STAGES * STAGE_BYTES);
-  uint64_t* a_full = bars;             // [STAGES] A block landed
-  uint64_t* mma_done = bars + STAGES;  // [STAGES] MMAs of the stage drained
-  uint64_t* fin = bars + 2 * STAGES;   // every MMA drained
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
+  uint64_t* mma_done = reinterpret_cast<uint64_t*>(tsm + C::AUX);  // [STAGES]
+  uint64_t* fin = mma_done + C::STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tsm + C::AUX + 64);
+  unsigned* s_flag = reinterpret_cast<unsigned*>(tsm + C::AUX + 96);
+  float* s_inv = reinterpret_cast<float*>(tsm + C::AUX + 128);  // [128]
+  float* red = reinterpret_cast<float*>(tsm);                   // epilogue staging [NM][128][kRedLd]
 
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int split = blockIdx.y, mb = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int mb = blockIdx.z;
   int tcol;
   const int mat = tc_tile(d, blockIdx.x, NM, tcol);
   const int n = d.mat[mat].n;
+  if (tcol >= n) return;  // empty half tile (n % 256 != 0): the whole cluster leaves together
   const int nks = (d.k + TK - 1) / TK;
-  const int ks0 = split * d.tc_ks;
-  const int nst = max(0, min(nks, ks0 + d.tc_ks) - ks0);
-  if (tcol >= n || nst == 0) return;  // empty half tile (n % 256 != 0) or empty slice
+  const int ks0 = blockIdx.y * d.tc_ks;
+  const int nst = min(nks, ks0 + d.tc_ks) - ks0;  // >= 1 by construction of tc_ks
+  const int m0 = mb * TM;
+  const int Mv = min(TM, d.M - m0);
+  const uint32_t tsm_a = smem_u32(tsm);
+
+  // ---- weights of the first stage: never written by an earlier kernel
+  const int brow = tid & 63, bq = tid >> 6;  // B: k row, 32-column quarter
+  auto load_b = [&](int ks, int a, uint4& w, unsigned short& s) {
+    const Q4Mat& Mt = d.mat[NM == 2 ? a : mat];
+    const int row = ks * TK + brow, col = tcol + bq * 32;
+    if (row < d.k && col < n) {
+      w = __ldg(reinterpret_cast<const uint4*>(Mt.packed + (size_t)row * (n / 2) + col / 2));
+      s = __ldg(reinterpret_cast<const unsigned short*>(Mt.scales) + (size_t)row * (n / 32) + col / 32);
+    } else {
+      w = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);  // q = 8 -> 0
+      s = 0;
+    }
+  };
+  uint4 wn[NM], wn2[NM];  // weights of stages i + 1 and i + 2
+  unsigned short sn[NM], sn2[NM];
+#pragma unroll
+  for (int a = 0; a < NM; ++a) {
+    load_b(ks0, a, wn[a], sn[a]);
+    if (nst > 1) load_b(ks0 + 1, a, wn2[a], sn2[a]);
+  }
 
   if (tid == 0) {
-    for (int s = 0; s < 2 * STAGES + 1; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < C::STAGES + 1; ++s) mbar_init(&mma_done[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    *s_flag = 0u;
   }
-  pdl_wait();  // the operands are ready; TMEM is taken only after this
+  // rows >= Mv of every A buffer stay zero for the whole kernel
+  if (Mv < TM) {
+    const int zrows = TM - Mv;
+    for (int i = tid; i < C::STAGES * 2 * zrows * (TK / 8); i += kThreads) {
+      // rows fastest: 8 consecutive threads fill 8 different 16-byte bank groups
+      const int r = Mv + i % zrows, c = (i / zrows) % (TK / 8), h = i / (zrows * (TK / 8));  // h: stage*2 + half
+      uint8_t* base = tsm + (h >> 1) * C::STAGE_BYTES + (h & 1) * A_BYTES;
+      *reinterpret_cast<uint4*>(base + (r >> 3) * 1024 + c * 128 + (r & 7) * 16) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  pdl_wait();  // activations, norms' sums of squares and KV of earlier kernels are ready
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"((uint32_t)(NM * TN)));
+                 "r"(C::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  // 1 / rms of each row (gemv.rs:408-417)
+  if (d.gamma) {
+    if (d.ssq_in) {
+      for (int r = tid; r < Mv; r += kThreads) s_inv[r] = inv_rms_from_ssq(d, m0 + r);
+    } else {
+      for (int r = warp; r < Mv; r += kThreads / 32) {
+        const float* xr = d.X + (size_t)(m0 + r) * d.ldx;
+        float ss = 0.0f;
+        for (int i = lane; i < d.k; i += 32) ss += xr[i] * xr[i];
+        ss = warp_sum(ss);
+        if (lane == 0) s_inv[r] = 1.0f / sqrtf(ss / (float)d.k + 1e-6f);
+      }
+    }
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
-  // B producer: thread -> k row br of the stage, 64-column half bh; threads
-  // 8j..8j+7 hold 8 consecutive k rows (conflict-free 16-byte smem stores)
-  const int br = (tid & 7) | ((tid >> 4) << 3), bh = (tid >> 3) & 1;
-  const int kg = br >> 3, kr = br & 7;
-  auto load_b = [&](int ks, int a, uint4 (&w)[2], unsigned short (&s)[2]) {
-    const Q4Mat& Mt = d.mat[NM == 2 ? a : mat];
-    const int row = ks * TK + br;
+  // ---- input rows of a stage -> registers (raw) and -> shared memory (split)
+  const int arow = tid & 63, akc = tid >> 6;
+  const int npass = Mv > 64 ? 2 : 1;
+  auto load_a = [&](int ks, ARegs& R) {
+    const int kk0 = ks * TK + akc * 16;
 #pragma unroll
-    for (int g = 0; g < 2; ++g) {
-      const int col = tcol + bh * 64 + g * 32;
-      if (col < n && row < d.k) {
-        w[g] = ld_stream16(Mt.packed + (size_t)row * (n / 2) + col / 2);
-        s[g] = __ldg(reinterpret_cast<const unsigned short*>(Mt.scales) + (size_t)row * (n / 32) + col / 32);
-      } else {
-        w[g] = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);  // q = 8 -> 0
-        s[g] = 0;
-      }
-    }
-  };
-  auto store_b = [&](uint8_t* bhi, uint8_t* blo, const uint4 (&w)[2], const unsigned short (&s)[2]) {
+    for (int p = 0; p < 2; ++p) {
+      const int r = arow + 64 * p;
+      if (p < npass && r < Mv) {
+        const int m = m0 + r;
+        if (d.emb_idx) {
+          const uint32_t er = d.emb_idx[(size_t)m * d.emb_idx_stride];
+          const uint8_t* prow = d.emb.packed + (size_t)er * (d.emb.n / 2);
+          const __half* srow = d.emb.scales + (size_t)er * (d.emb.n / 32);
 #pragma unroll
-    for (int g = 0; g < 2; ++g) {
-      const float sc = __half2float(__ushort_as_half(s[g]));
-      const uint32_t words[4] = {w[g].x, w[g].y, w[g].z, w[g].w};
+          for (int j = 0; j < 16; ++j) R.x[p][j] = (kk0 + j < d.k) ? q4_value(prow, srow, kk0 + j) : 0.0f;
+        } else {
+          const float* xr = d.X + (size_t)m * d.ldx + kk0;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {  // 8 columns per 32-bit word, low nibble first
-        __align__(16) __half h8[8];
-        __align__(16) __half l8[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int qv = (int)((words[q] >> (4 * j)) & 0xFu) - 8;
-          split_h(sc * (float)qv, h8[j], l8[j]);
+          for (int q = 0; q < 4; ++q) {
+            const float4 v = (kk0 + 4 * q < d.k) ? __ldg(reinterpret_cast<const float4*>(xr) + q)
+                                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+            R.x[p][4 * q] = v.x; R.x[p][4 * q + 1] = v.y; R.x[p][4 * q + 2] = v.z; R.x[p][4 * q + 3] = v.w;
+          }
         }
-        const int cg8 = bh * 8 + g * 4 + q;  // 8-column group within the tile
-        const int off = cg8 * 1024 + kg * 128 + kr * 16;
-        *reinterpret_cast<uint4*>(bhi + off) = *reinterpret_cast<const uint4*>(h8);
-        *reinterpret_cast<uint4*>(blo + off) = *reinterpret_cast<const uint4*>(l8);
       }
     }
   };
-  const size_t ablk = (size_t)2 * TM * TK;  // halves per (row block, stage)
-  const __half* abase = d.xsplit + ((size_t)mb * nks + ks0) * ablk;
-
-  // thread 0's bookkeeping of outstanding A copies (for the error drain)
-  unsigned a_uses[STAGES] = {0u, 0u};  // completed a_full waits per buffer
-  bool a_pend[STAGES] = {false, false};
-
-  uint4 wn[NM][2];
-  unsigned short sn[NM][2];
+  float amax = 0.0f;
+  auto store_a = [&](int ks, const ARegs& R, uint8_t* ahi, uint8_t* alo) {
+    const int kk0 = ks * TK + akc * 16;
 #pragma unroll
-  for (int a = 0; a < NM; ++a) load_b(ks0, a, wn[a], sn[a]);
-  if (tid == 0) {
-    for (int i = 0; i < min(STAGES, nst); ++i) {
-      mbar_expect_tx(&a_full[i], 2 * A_BYTES);
-      bulk_g2s(tsm + i * STAGE_BYTES, abase + (size_t)i * ablk, 2 * A_BYTES, &a_full[i]);
-      a_pend[i] = true;
+    for (int p = 0; p < 2; ++p) {
+      const int r = arow + 64 * p;
+      if (p < npass && r < Mv) {
+        float y[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) y[j] = R.x[p][j];
+        if (d.gamma && !d.emb_idx) {
+          const float inv = s_inv[r];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) y[j] = (kk0 + j < d.k) ? y[j] * inv * h2f(d.gamma[kk0 + j]) : 0.0f;
+          if (d.xnorm_out && blockIdx.x == 0) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (kk0 + j < d.k) d.xnorm_out[(size_t)(m0 + r) * d.ld_xnorm + kk0 + j] = y[j];
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {  // two 8-deep k chunks
+          uint32_t h[4], l[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            amax = fmaxf(amax, fmaxf(fabsf(y[c * 8 + 2 * q]), fabsf(y[c * 8 + 2 * q + 1])));
+            split2(y[c * 8 + 2 * q], y[c * 8 + 2 * q + 1], h[q], l[q]);
+          }
+          const int off = (r >> 3) * 1024 + (akc * 2 + c) * 128 + (r & 7) * 16;
+          *reinterpret_cast<uint4*>(ahi + off) = make_uint4(h[0], h[1], h[2], h[3]);
+          *reinterpret_cast<uint4*>(alo + off) = make_uint4(l[0], l[1], l[2], l[3]);
+        }
+      }
     }
-  }
+  };
+  auto store_b = [&](uint8_t* bhi, uint8_t* blo, const uint4& w, unsigned short s) {
+    const __half2 s2 = __half2half2(__ushort_as_half(s));
+    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {  // 8-column group bq * 4 + q
+      uint4 hi, lo;
+      dequant_word(words[q], s2, hi, lo);
+      const int off = (bq * 4 + q) * 1024 + (brow >> 3) * 128 + (brow & 7) * 16;
+      *reinterpret_cast<uint4*>(bhi + off) = hi;
+      *reinterpret_cast<uint4*>(blo + off) = lo;
+    }
+  };
+
+  ARegs an;
+  load_a(ks0, an);
   bool ok = true;
   for (int i = 0; i < nst; ++i) {
-    const int b = i % STAGES;
-    uint8_t* st = tsm + b * STAGE_BYTES;
-    uint4 w[NM][2];
-    unsigned short s[NM][2];
+    const int b = i % C::STAGES;
+    uint8_t* st = tsm + b * C::STAGE_BYTES;
+    const ARegs ac = an;
+    uint4 w[NM];
+    unsigned short s[NM];
 #pragma unroll
     for (int a = 0; a < NM; ++a) {
-      w[a][0] = wn[a][0]; w[a][1] = wn[a][1];
-      s[a][0] = sn[a][0]; s[a][1] = sn[a][1];
+      w[a] = wn[a]; s[a] = sn[a];
+      wn[a] = wn2[a]; sn[a] = sn2[a];
     }
-    if (i + 1 < nst) {
+    // later stages' operands in flight while this one is converted
+    if (i + 1 < nst) load_a(ks0 + i + 1, an);
+    if (i + 2 < nst) {
 #pragma unroll
-      for (int a = 0; a < NM; ++a) load_b(ks0 + i + 1, a, wn[a], sn[a]);
+      for (int a = 0; a < NM; ++a) load_b(ks0 + i + 2, a, wn2[a], sn2[a]);
     }
-    // this buffer's B was read by the MMAs of stage i - STAGES
+    // this buffer was read by the MMAs of stage i - STAGES
     bool w_ok = true;
-    if (i >= STAGES) w_ok = mbar_wait(&mma_done[b], (unsigned)((i / STAGES) - 1) & 1u);
+    if (i >= C::STAGES) w_ok = mbar_wait(&mma_done[b], (unsigned)((i / C::STAGES) - 1) & 1u);
     if (!__syncthreads_and(w_ok)) { ok = false; break; }
+    store_a(ks0 + i, ac, st, st + A_BYTES);
 #pragma unroll
     for (int a = 0; a < NM; ++a)
       store_b(st + 2 * A_BYTES + a * B_BYTES, st + 2 * A_BYTES + (NM + a) * B_BYTES, w[a], s[a]);
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // st.shared -> visible to tcgen05.mma
     __syncthreads();
-    bool t_ok = true;
     if (tid == 0) {
-      t_ok = mbar_wait(&a_full[b], a_uses[b] & 1u);
-      if (t_ok) {
-        ++a_uses[b];
-        a_pend[b] = false;
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint8_t* ahi = st;
-        const uint8_t* alo = st + A_BYTES;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t ahi = tsm_a + b * C::STAGE_BYTES, alo = ahi + A_BYTES;
 #pragma unroll
-        for (int a = 0; a < NM; ++a) {
-          const uint8_t* bhi = st + 2 * A_BYTES + a * B_BYTES;
-          const uint8_t* blo = st + 2 * A_BYTES + (NM + a) * B_BYTES;
-          const uint32_t dt = tmem + (uint32_t)(a * TN);
+      for (int a = 0; a < NM; ++a) {
+        const uint32_t bhi = ahi + 2 * A_BYTES + a * B_BYTES, blo = ahi + 2 * A_BYTES + (NM + a) * B_BYTES;
+        const uint32_t dm = tmem + (uint32_t)(a * 2 * TN), dc = dm + TN;
 #pragma unroll
-          for (int kk = 0; kk < TK / 16; ++kk) {
-            umma(dt, sdesc(ahi + kk * 256), sdesc(bhi + kk * 256), (i > 0 || kk > 0) ? 1u : 0u);
-            umma(dt, sdesc(ahi + kk * 256), sdesc(blo + kk * 256), 1u);
-            umma(dt, sdesc(alo + kk * 256), sdesc(bhi + kk * 256), 1u);
-          }
-        }
-        umma_commit(&mma_done[b]);
-        // the previous stage's MMAs have had a dequantise period to drain:
-        // refill its A buffer with stage i - 1 + STAGES
-        if (i >= 1 && i - 1 + STAGES < nst) {
-          const int pb = (i - 1) % STAGES;
-          t_ok = mbar_wait(&mma_done[pb], (unsigned)((i - 1) / STAGES) & 1u);
-          if (t_ok) {
-            mbar_expect_tx(&a_full[pb], 2 * A_BYTES);
-            bulk_g2s(tsm + pb * STAGE_BYTES, abase + (size_t)(i - 1 + STAGES) * ablk, 2 * A_BYTES, &a_full[pb]);
-            a_pend[pb] = true;
-          }
+        for (int kk = 0; kk < TK / 16; ++kk) {
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          umma(dm, sdesc(ahi + kk * 256), sdesc(bhi + kk * 256), acc);
+          umma(dc, sdesc(ahi + kk * 256), sdesc(blo + kk * 256), acc);
+          umma(dc, sdesc(alo + kk * 256), sdesc(bhi + kk * 256), 1u);
         }
       }
+      umma_commit(&mma_done[b]);
     }
-    if (!__syncthreads_and(t_ok)) { ok = false; break; }
   }
+  pdl_launch_dependents();
   // drain: the commit tracks every earlier tcgen05.mma of thread 0
   if (tid == 0) umma_commit(fin);
   const bool fin_ok = mbar_wait(fin, 0);
-  if (tid == 0) {
-    if (!ok) {  // wait (bounded) for A copies still in flight into this CTA's shared memory
-      for (int b = 0; b < STAGES; ++b)
-        if (a_pend[b]) mbar_wait(&a_full[b], a_uses[b] & 1u);
-    }
-    if ((!ok || !fin_ok) && d.err_flag) atomicOr(d.err_flag, 4);
-  }
+  if (amax > 65504.0f) atomicOr(s_flag, (unsigned)kErrFp16Range);
+  if (!ok || !fin_ok) atomicOr(s_flag, (unsigned)kErrTimeout);
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  // accumulator -> partial [split][m][ncols]: thread = TMEM lane = output row
-  const int m = mb * TM + tid;
-  if (ok && fin_ok) {
+  __syncthreads();
+  const bool good = (*s_flag & kErrTimeout) == 0;
+
+  // ---- accumulators -> shared staging (warp: lane quarter w % 4, column half w / 4)
+  {
+    const int lq = warp & 3, ch = warp >> 2;
+    if (good && lq * 32 < Mv) {
+      const int r = lq * 32 + lane;
 #pragma unroll
-    for (int a = 0; a < NM; ++a) {
-      const int c0 = d.col0[NM == 2 ? a : mat] + tcol;
+      for (int a = 0; a < NM; ++a) {
 #pragma unroll
-      for (int cc = 0; cc < TN / 32; ++cc) {
-        uint32_t r[32];
-        const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(a * TN + cc * 32);
-        asm volatile(
-            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-              "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]),
-              "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]),
-              "=r"(r[30]), "=r"(r[31])
-            : "r"(taddr));
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (m < d.M) {
-          float* dst = d.part + ((size_t)split * d.M + m) * d.ncols + c0 + cc * 32;
+        for (int c = 0; c < 2; ++c) {
+          const int col = ch * 64 + c * 32;
+          float vm[32], vc[32];
+          const uint32_t ta = tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(a * 2 * TN + col);
+          tmem_ld32(ta, vm);
+          tmem_ld32(ta + TN, vc);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+          float4* dst = reinterpret_cast<float4*>(red + ((size_t)a * TM + r) * kRedLd + col);
 #pragma unroll
           for (int q = 0; q < 8; ++q)
-            if (tcol + cc * 32 + q * 4 < n)
-              *reinterpret_cast<float4*>(dst + q * 4) =
-                  make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                              __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+            dst[q] = make_float4(vm[4 * q] + vc[4 * q] * kLoUnscale, vm[4 * q + 1] + vc[4 * q + 1] * kLoUnscale,
+                                 vm[4 * q + 2] + vc[4 * q + 2] * kLoUnscale, vm[4 * q + 3] + vc[4 * q + 3] * kLoUnscale);
         }
       }
     }
   }
-  pdl_launch_dependents();
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
-  if (warp == 0)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"((uint32_t)(NM * TN)));
-}
+  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::TMEM_COLS));
+  if (tid == 0 && *s_flag && d.err_flag) atomicOr(d.err_flag, (int)*s_flag);
 
-// ---------------------------------------------------------------------------
-// 3. partial sum (slice order) + epilogue.  Grid (ntiles, 1, ceil(M/MB)).
-template <int MB, int NM, int EPI>
-__global__ void __launch_bounds__(kGemvThreads) tc_epilogue_kernel(const GemvDesc d, const FrameCodes fc, int S) {
-  pdl_launch_dependents();
-  pdl_wait();
-  __shared__ float sbuf[64];
-  __shared__ float ybuf[MB * kTileN];
-  const int tile = blockIdx.x, zb = blockIdx.z, tid = threadIdx.x;
-  int mat = 0;
-  if (NM == 1) {
-    while (mat + 1 < d.nmat && tile >= d.tile0[mat + 1]) ++mat;
-  }
-  const int tcol = (NM == 2 ? tile : tile - d.tile0[mat]) * kTileN;
-  const int n = d.mat[mat].n;
-  const int m0 = zb * MB, mcnt = min(MB, d.M - m0);
-  const int col = tcol + tid;
-  float v[NM][MB];
+  cluster_sync_all();  // every K slice's staging is complete
+
+  // ---- this CTA's slice of rows: sum the S partials over the cluster, then
+  // the epilogue with one warp per row
+  const int S = (int)gridDim.y;
+  const uint32_t rank = cluster_rank();
+  const int R = (Mv + S - 1) / S;
+  const int rb = (int)rank * R, re = min(Mv, rb + R);
+  const EpiDesc& e = d.epi;
+  const int cc = lane * 4;    // this lane's 4 columns within the tile
+  const int col = tcol + cc;  // column within the matrix
+  const bool cval = col < n;  // n % 32 == 0: all 4 valid or none
+  for (int r = rb + warp; good && r < re; r += kThreads / 32) {
+    float4 acc[NM];
 #pragma unroll
-  for (int a = 0; a < NM; ++a)
+    for (int a = 0; a < NM; ++a) {
+      const uint32_t la = smem_u32(red + ((size_t)a * TM + r) * kRedLd + cc);
+      float4 part[kMaxSplits];
 #pragma unroll
-    for (int mm = 0; mm < MB; ++mm) {
-      float t = 0.0f;
-      if (col < n && mm < mcnt) {
-        const size_t c = (size_t)d.col0[NM == 2 ? a : mat] + col;
-        for (int sp = 0; sp < S; ++sp) t += __ldcg(d.part + ((size_t)sp * d.M + m0 + mm) * d.ncols + c);
-      }
-      v[a][mm] = t;
+      for (int p = 0; p < kMaxSplits; ++p)  // all loads in flight before the ordered sum
+        if (p < S) part[p] = ld_dsmem4(dsmem_addr(la, (uint32_t)p));
+      float4 t4 = part[0];
+#pragma unroll
+      for (int p = 1; p < kMaxSplits; ++p)
+        if (p < S) {
+          t4.x += part[p].x; t4.y += part[p].y; t4.z += part[p].z; t4.w += part[p].w;
+        }
+      acc[a] = t4;
     }
-  gemv_epilogue<MB, NM, EPI>(d, fc, v, mat, tile, tcol, m0, mcnt, zb, sbuf, ybuf);
+    const int m = m0 + r;
+    if (EPI == EPI_STORE || EPI == EPI_RESID) {
+      float vv[4] = {acc[0].x, acc[0].y, acc[0].z, acc[0].w};
+      const int cgl = d.col0[mat] + col;
+      if (cval) {
+        float* o = e.out + (size_t)m * e.ldo + cgl;
+        if (EPI == EPI_STORE) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (e.bias) vv[j] = vv[j] + e.bias[cgl + j];
+            if (e.act_silu) vv[j] = silu_ref(vv[j]);
+          }
+        } else {
+          const float4 ov = *reinterpret_cast<const float4*>(o);
+          vv[0] = ov.x + vv[0]; vv[1] = ov.y + vv[1]; vv[2] = ov.z + vv[2]; vv[3] = ov.w + vv[3];
+        }
+        *reinterpret_cast<float4*>(o) = make_float4(vv[0], vv[1], vv[2], vv[3]);
+      }
+      if (e.ssq_out) {
+        const float ss = warp_sum(cval ? (vv[0] * vv[0] + vv[1] * vv[1]) + (vv[2] * vv[2] + vv[3] * vv[3]) : 0.0f);
+        if (lane == 0) e.ssq_out[(size_t)m * e.ssq_ld + tcol / kSsqCols] = ss;
+      }
+    } else if (EPI == EPI_SWIGLU) {
+      if (cval) {
+        const float g[4] = {acc[0].x, acc[0].y, acc[0].z, acc[0].w};
+        const float u[4] = {acc[NM - 1].x, acc[NM - 1].y, acc[NM - 1].z, acc[NM - 1].w};
+        *reinterpret_cast<float4*>(e.out + (size_t)m * e.ldo + col) =
+            make_float4(silu_ref(g[0]) * u[0], silu_ref(g[1]) * u[1], silu_ref(g[2]) * u[2], silu_ref(g[3]) * u[3]);
+      }
+    } else if (EPI == EPI_QKV) {
+      // mat 0 = q, 1 = k, 2 = v; the tile is head tcol / 128
+      const int h = tcol / kHeadDim;
+      int sess, pos, kvp;
+      row_pos(e.rp, m, sess, pos, kvp);
+      if (mat == 2) {
+        KvDesc kv = e.kv;
+        *reinterpret_cast<float4*>(kv_row(kv, sess, kvp, 1, h) + cc) = acc[0];
+      } else {
+        const float vv[4] = {acc[0].x, acc[0].y, acc[0].z, acc[0].w};
+        const float ss = warp_sum((vv[0] * vv[0] + vv[1] * vv[1]) + (vv[2] * vv[2] + vv[3] * vv[3]));
+        const float inv = 1.0f / sqrtf(ss / (float)kHeadDim + 1e-6f);  // talker.rs:89-99
+        const __half* gn = (mat == 0) ? e.q_norm : e.k_norm;
+        float y[4], pr[4], o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) y[j] = vv[j] * inv * h2f(gn[cc + j]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) pr[j] = __shfl_xor_sync(0xffffffffu, y[j], 16);  // column +- 64
+        const int half = kHeadDim / 2;
+        const bool in_range = pos < e.rope_rows && pos >= 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {  // split-half RoPE (rope.rs:79-92)
+          const int dd = cc + j, i = dd % half;
+          const float x1 = dd < half ? y[j] : pr[j];
+          const float x2 = dd < half ? pr[j] : y[j];
+          o[j] = y[j];
+          if (in_range) {
+            const float c = e.rope_cos[(size_t)pos * half + i];
+            const float sn = e.rope_sin[(size_t)pos * half + i];
+            o[j] = (dd < half) ? (x1 * c - x2 * sn) : (x2 * c + x1 * sn);
+          }
+        }
+        if (!in_range && !e.rope_skip_oob && e.err_flag && lane == 0) atomicOr(e.err_flag, 1);
+        float* dst;
+        if (mat == 0) {
+          dst = e.q_out + (size_t)m * e.ldq + col;
+        } else {
+          KvDesc kv = e.kv;
+          dst = kv_row(kv, sess, kvp, 0, h) + cc;
+        }
+        *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+      }
+    } else if (EPI == EPI_ARGMAX) {
+      const float vv[4] = {acc[0].x, acc[0].y, acc[0].z, acc[0].w};
+      unsigned long long key = 0ull;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const unsigned long long kj = cval ? (((unsigned long long)f32_order_key(vv[j]) << 32) | (unsigned)(col + j)) : 0ull;
+        key = kj > key ? kj : key;
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+        key = other > key ? other : key;
+      }
+      if (lane == 0) atomicMax(e.keys + m, key);
+    }
+  }
+  cluster_sync_all();  // peers keep their staging until every slice is read
+  if (EPI == EPI_ARGMAX) {
+    __shared__ unsigned s_last;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+      const unsigned total = (unsigned)(((n + TN - 1) / TN) * S);  // CTAs of this row block
+      s_last = atomicAdd(e.counters2 + mb, 1u) == total - 1 ? 1u : 0u;
+    }
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      for (int r = tid; r < Mv; r += kThreads) argmax_finalize_row(e, fc, m0 + r);
+      if (tid == 0) e.counters2[mb] = 0u;
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
-size_t tc_smem_bytes(int nm) { return (size_t)STAGES * (2 * A_BYTES + 2 * nm * B_BYTES) + 128; }
-
-size_t tc_xsplit_halves(int M, int k) {
-  return (size_t)((M + TM - 1) / TM) * TM * (size_t)((k + TK - 1) / TK) * TK * 2;
-}
+size_t tc_smem_bytes(int nm) { return nm == 2 ? (size_t)TcCfg<2>::SMEM : (size_t)TcCfg<1>::SMEM; }
 
 int tc_splits(const GemvDesc& d) { return ((d.k + TK - 1) / TK + d.tc_ks - 1) / d.tc_ks; }
 
+// K slices: the largest S (at most a portable cluster of 8, at most the
+// 64-deep stages there are) whose clusters (one per tile and row block) are
+// all resident in one wave; S = 1 always is.
 void tc_plan(int sm_count, GemvDesc& g) {
   const long nks = (g.k + TK - 1) / TK;
-  const long ctas = 2L * g.ntiles * ((g.M + TM - 1) / TM);  // 128-column tiles x row blocks
-  const long S = std::max(1L, std::min(nks, (sm_count + ctas - 1) / ctas));
-  g.tc_ks = (int)((nks + S - 1) / S);
+  long tiles = 0;
+  if (g.paired) {
+    tiles = (g.mat[0].n + TN - 1) / TN;
+  } else {
+    for (int i = 0; i < g.nmat; ++i) tiles += (g.mat[i].n + TN - 1) / TN;
+  }
+  const long units = tiles * ((g.M + TM - 1) / TM);
   g.tc = 1;
+  g.tc_ks = (int)nks;
+  for (long S = std::min<long>(kMaxSplits, std::min<long>(nks, std::max<long>(1, sm_count / units))); S > 1; --S) {
+    GemvDesc t = g;
+    t.tc_ks = (int)((nks + S - 1) / S);
+    if (tc_splits(t) != S) continue;
+    g_occ_query = true;
+    g_occ_clusters = 0;
+    launch_tc(t, FrameCodes{}, nullptr);
+    g_occ_query = false;
+    // the empty half tiles of an odd 128-column count are clusters too
+    const long clusters = 2L * g.ntiles * ((g.M + TM - 1) / TM);
+    if (g_occ_clusters >= clusters) {
+      g.tc_ks = t.tc_ks;
+      return;
+    }
+  }
 }
 
-template <int MB, int NM, int EPI>
-static cudaError_t launch_epi(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
+static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Operand and output layouts the kernel's vector accesses need.
+bool tc_layout_ok(const GemvDesc& d) {
+  if (!d.emb_idx && (!al16(d.X) || d.ldx % 4 || d.k % 4)) return false;
+  const EpiDesc& e = d.epi;
+  if (d.epi_kind != EPI_ARGMAX && d.epi_kind != EPI_QKV && (!al16(e.out) || e.ldo % 4)) return false;
+  if (d.epi_kind == EPI_QKV && (!al16(e.q_out) || e.ldq % 4 || !al16(e.kv.pool))) return false;
+  return true;
+}
+
+template <int NM, int EPI>
+static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
+  const int S = tc_splits(d);
   LaunchOpts o;
   o.pdl = d.pdl != 0;
-  const dim3 grid(d.ntiles, 1, (d.M + MB - 1) / MB);
-  return launch_k(tc_epilogue_kernel<MB, NM, EPI>, grid, dim3(kGemvThreads), 0, st, o, d, fc, tc_splits(d));
+  o.cluster_y = (unsigned)S;
+  const dim3 grid(2 * d.ntiles, S, (d.M + TM - 1) / TM);
+  return launch_k(tc_proj_kernel<NM, EPI>, grid, dim3(kThreads), (size_t)TcCfg<NM>::SMEM, st, o, d, fc);
 }
 
 cudaError_t launch_tc(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
-  if (!d.xsplit || !d.part || d.tc_ks <= 0 || d.M <= 0 || d.k <= 0) return cudaErrorInvalidValue;
-  if (reinterpret_cast<uintptr_t>(d.xsplit) % 16) return cudaErrorMisalignedAddress;
-  const int nks = (d.k + TK - 1) / TK;
-  const int S = tc_splits(d);
-  const int zt = (d.M + TM - 1) / TM;
-  LaunchOpts o;
-  o.pdl = d.pdl != 0;
-  cudaError_t e = launch_k(xsplit_kernel, dim3(nks, zt), dim3(128), 0, st, o, d);
-  if (e != cudaSuccess) return e;
-  const dim3 grid(2 * d.ntiles, S, zt);
-  e = d.paired ? launch_k(tc_gemm_kernel<2>, grid, dim3(128), tc_smem_bytes(2), st, o, d)
-               : launch_k(tc_gemm_kernel<1>, grid, dim3(128), tc_smem_bytes(1), st, o, d);
-  if (e != cudaSuccess) return e;
-  if (d.paired) return launch_epi<2, 2, EPI_SWIGLU>(d, fc, st);
+  if (d.tc_ks <= 0 || d.M <= 0 || d.k <= 0 || tc_splits(d) > kMaxSplits) return cudaErrorInvalidValue;
+  if (!tc_layout_ok(d)) return cudaErrorMisalignedAddress;
+  if (d.epi_kind == EPI_ARGMAX && (d.M + TM - 1) / TM > 4096) return cudaErrorInvalidValue;
+  if (d.paired) return d.epi_kind == EPI_SWIGLU ? launch_t<2, EPI_SWIGLU>(d, fc, st) : cudaErrorInvalidValue;
   switch (d.epi_kind) {
-    case EPI_STORE: return launch_epi<4, 1, EPI_STORE>(d, fc, st);
-    case EPI_RESID: return launch_epi<4, 1, EPI_RESID>(d, fc, st);
-    case EPI_QKV: return launch_epi<4, 1, EPI_QKV>(d, fc, st);
-    case EPI_ARGMAX: return launch_epi<4, 1, EPI_ARGMAX>(d, fc, st);
+    case EPI_STORE: return launch_t<1, EPI_STORE>(d, fc, st);
+    case EPI_RESID: return launch_t<1, EPI_RESID>(d, fc, st);
+    case EPI_QKV: return launch_t<1, EPI_QKV>(d, fc, st);
+    case EPI_ARGMAX: return launch_t<1, EPI_ARGMAX>(d, fc, st);
     default: return cudaErrorInvalidValue;
   }
 }
 
-// Opt the GEMM into its dynamic shared memory once per device (outside any
-// stream capture).
+// Opt the kernels into their dynamic shared memory once per device (outside
+// any stream capture).
 void tc_init_attributes() {
   static bool done[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || done[dev]) return;
-  cudaFuncSetAttribute(tc_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc_smem_bytes(1));
-  cudaFuncSetAttribute(tc_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tc_smem_bytes(2));
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<2, EPI_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<2>::SMEM);
   cudaGetLastError();
   done[dev] = true;
 }
