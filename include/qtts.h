@@ -142,8 +142,8 @@ QTTS_API int qtts_frame_kernel_count(qtts_session* s);
  * [k][n] layout (packed k*n/2 bytes, low nibble = even column; scales
  * k*n/32 f16).  scratch_dev: split-K tile counters and partials,
  * qtts_q4_gemv_scratch_bytes() bytes, zero-filled before its first use (every
- * call leaves the counters at zero again).  m >= 16 with 16-byte aligned x/y
- * and k % 4 == 0 runs on the tensor cores (tcgen05). */
+ * call leaves the counters at zero again).  m >= 16 with 16-byte aligned x/y,
+ * k % 4 == 0 and n % 64 == 0 runs on the tensor cores (tcgen05). */
 QTTS_API size_t qtts_q4_gemv_scratch_bytes(int k, int n, int m);
 QTTS_API int qtts_q4_gemv_dev(const uint8_t* packed_dev, const uint16_t* scales_dev, int k, int n,
                      const float* x_dev, int m, float* y_dev, void* scratch_dev,

@@ -1042,7 +1042,7 @@ static int gemv_plan_standalone(int k, int n, int m, GemvDesc& g) {
   w.n = n;
   g = gemv_base(EPI_STORE, {w}, false, m);
   choose_split(sms, g);
-  if (m >= kTcMinRows && k % 4 == 0 && tc_enabled()) tc_plan(sms, g);
+  if (m >= kTcMinRows && k % 4 == 0 && n % 64 == 0 && tc_enabled()) tc_plan(sms, g);
   return QTTS_OK;
 }
 

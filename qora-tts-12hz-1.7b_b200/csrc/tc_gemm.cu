@@ -5,21 +5,26 @@
 // the CUDA-core kernels (RMSNorm with the producer's sums of squares,
 // embedding gather) and the same epilogues, in ONE kernel per projection.
 //
-// Work split.  A CTA (256 threads, one per SM) owns one 128-column tile (of
+// Work split.  A CTA (16 warps, one CTA per SM) owns one 128-column tile (of
 // both matrices of a gate/up pair), one 128-row block of the input rows and
 // one K slice; the S K-slices of a tile form a thread-block cluster (1, S, 1),
 // with S chosen so that every cluster of the launch is resident in one wave.
 //
 // Main loop, per 64-deep K stage (2-3 stages in flight):
-//   * every thread converts its share of the stage into shared memory:
-//     A = the normalised input rows, B = the dequantised Q4 weights, each as
+//   * the raw Q4 tile of the stage (packed bytes + f16 scales) has been
+//     streaming into a shared-memory ring by cp.async 3-5 stages ahead;
+//   * warps 0-6 dequantise it and warps 7-14 normalise the input rows (held
+//     in registers one stage ahead), into
+//     shared memory: A = the normalised input rows, B = the Q4 weights, each as
 //     two fp16 operands hi + lo with lo = fp16((v - hi) * 2^11).  The Q4 value
 //     (q-8)*scale has at most 14 significant bits, so hi + lo holds it
 //     exactly; an f32 input keeps ~22 bits.  Carrying lo scaled by 2^11 keeps
 //     it clear of the fp16 subnormal range.
-//   * one thread issues the tcgen05.mma (kind::f16, f32 accumulators in TMEM):
-//     D_main += A_hi*B_hi, D_cross += A_hi*B_lo + A_lo*B_hi, and commits them
-//     to the stage's mbarrier; the threads meanwhile convert the next stage.
+//   * the converters arrive on the stage's "full" mbarrier; warp 15 waits on
+//     it and issues the tcgen05.mma (kind::f16, f32 accumulators in TMEM):
+//     D_main += A_hi*B_hi, D_cross += A_hi*B_lo + A_lo*B_hi, committing them
+//     to the stage's "done" mbarrier, while the converters (synchronised
+//     among themselves by a named barrier) already convert the next stage.
 // Result = D_main + 2^-11 * D_cross (the dropped lo*lo term is ~2^-22).
 //
 // Epilogue: the accumulators go TMEM -> registers -> shared memory; the S
@@ -42,6 +47,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "epilogue.cuh"
@@ -54,7 +60,10 @@ namespace {
 constexpr int TM = kTcRows;  // rows per MMA tile (TMEM lanes)
 constexpr int TN = kTcCols;  // columns per CTA tile (per matrix)
 constexpr int TK = kTcK;     // K per stage
-constexpr int kThreads = 256;
+constexpr int kBConv = 224;           // warps 0-6 dequantise the weights
+constexpr int kConv = 480;            // + warps 7-14 split the input rows
+constexpr int kMmaWarp = kConv / 32;  // warp 15 issues the tensor-core MMAs
+constexpr int kThreads = kConv + 32;
 constexpr int A_BYTES = TM * TK * 2;  // 16 KB per operand half
 constexpr int B_BYTES = TN * TK * 2;  // 16 KB per operand half
 constexpr int kRedLd = TN + 4;        // staging row stride (floats)
@@ -64,16 +73,34 @@ constexpr float kLoUnscale = 1.0f / 2048.0f;
 constexpr unsigned long long kWaitNs = 1000000000ull;  // 1 s bound on any wait
 constexpr int kErrTimeout = 4, kErrFp16Range = 8;      // err_flag bits
 
+constexpr int kRawRow = 80;                       // raw packed row stride: 64 B + pad (conflict-free 16 B reads)
+constexpr int kRawMat = TK * kRawRow + TK * 8;     // one matrix's raw stage: packed rows + 4 f16 scales per row
+
 template <int NM>
 struct TcCfg {
-  static constexpr int STAGES = NM == 1 ? 3 : 2;
+  static constexpr int STAGES = NM == 1 ? 3 : 2;             // operand stages (fp16 hi/lo, UMMA layout)
+  static constexpr int RS = NM == 1 ? 5 : 3;                 // raw weight stages in flight (cp.async ring)
   static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * NM * B_BYTES;
   static constexpr int PIPE_BYTES = STAGES * STAGE_BYTES;
-  static constexpr int RED_BYTES = NM * TM * kRedLd * 4;
-  static constexpr int AUX = PIPE_BYTES > RED_BYTES ? PIPE_BYTES : RED_BYTES;
+  static constexpr int RAW_STAGE = NM * kRawMat;
+  static constexpr int RAW_BYTES = RS * RAW_STAGE;
+  static constexpr int RED_BYTES = NM * TM * kRedLd * 4;     // epilogue staging, over the operand stages
+  static_assert(RED_BYTES <= PIPE_BYTES, "staging must fit the operand stages");
+  static constexpr int AUX = PIPE_BYTES + RAW_BYTES;
   static constexpr int SMEM = AUX + 1024;  // + barriers, TMEM slot, 1/rms, flags
   static constexpr uint32_t TMEM_COLS = NM * 2 * TN;  // main + cross per matrix
 };
+
+// global -> shared asynchronous copies (cp.async); src_size < size zero-fills
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_size) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_size) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src, uint32_t src_size) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(dst), "l"(src), "r"(src_size) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -103,6 +130,22 @@ __device__ __forceinline__ float4 ld_dsmem4(uint32_t addr) {
                : "r"(addr)
                : "memory");
   return v;
+}
+// Barrier 1 over the converter threads, AND-reducing a status.
+__device__ __forceinline__ bool conv_sync_and(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "n"(kConv)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 __device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
@@ -211,8 +254,8 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-// Input rows of one stage held in registers: pass p covers rows (tid & 63) + 64 p,
-// 16 consecutive k starting at 16 * (tid >> 6).
+// Input rows of one stage held in registers by an input-row thread: pass p
+// covers row (at & 63) + 64 p, 16 consecutive k starting at 16 * ((at >> 6) & 3).
 struct ARegs {
   float x[2][16];
 };
@@ -220,13 +263,14 @@ struct ARegs {
 }  // namespace
 
 // ---------------------------------------------------------------------------
-// Grid (2 * ntiles, S, ceil(M / 128)), cluster (1, S, 1), 256 threads.
+// Grid (2 * ntiles, S, ceil(M / 128)), cluster (1, S, 1), 512 threads.
 template <int NM, int EPI>
 __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, const FrameCodes fc) {
   using C = TcCfg<NM>;
   extern __shared__ __align__(1024) uint8_t tsm[];
-  uint64_t* mma_done = reinterpret_cast<uint64_t*>(tsm + C::AUX);  // [STAGES]
-  uint64_t* fin = mma_done + C::STAGES;
+  uint64_t* mma_done = reinterpret_cast<uint64_t*>(tsm + C::AUX);  // [STAGES] MMAs of the stage drained
+  uint64_t* full = mma_done + C::STAGES;                             // [STAGES] operands of the stage written
+  uint64_t* fin = full + C::STAGES;                                  // every MMA drained
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tsm + C::AUX + 64);
   unsigned* s_flag = reinterpret_cast<unsigned*>(tsm + C::AUX + 96);
   float* s_inv = reinterpret_cast<float*>(tsm + C::AUX + 128);  // [128]
@@ -245,29 +289,42 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   const int Mv = min(TM, d.M - m0);
   const uint32_t tsm_a = smem_u32(tsm);
 
-  // ---- weights of the first stage: never written by an earlier kernel
-  const int brow = tid & 63, bq = tid >> 6;  // B: k row, 32-column quarter
-  auto load_b = [&](int ks, int a, uint4& w, unsigned short& s) {
-    const Q4Mat& Mt = d.mat[NM == 2 ? a : mat];
-    const int row = ks * TK + brow, col = tcol + bq * 32;
-    if (row < d.k && col < n) {
-      w = __ldg(reinterpret_cast<const uint4*>(Mt.packed + (size_t)row * (n / 2) + col / 2));
-      s = __ldg(reinterpret_cast<const unsigned short*>(Mt.scales) + (size_t)row * (n / 32) + col / 32);
-    } else {
-      w = make_uint4(0x88888888u, 0x88888888u, 0x88888888u, 0x88888888u);  // q = 8 -> 0
-      s = 0;
+  // ---- raw weight tiles stream into the ring RS - 1 stages ahead; the
+  // weights are never written by an earlier kernel, so this starts before
+  // the programmatic-dependent-launch wait
+  const uint32_t raw_a = tsm_a + C::PIPE_BYTES;
+  auto issue_b = [&](int ks, int slot) {
+    for (int c = tid; c < NM * 384; c += kConv) {
+      const int a = c / 384, cc = c % 384;
+      const Q4Mat& Mt = d.mat[NM == 2 ? a : mat];
+      const uint32_t base = raw_a + slot * C::RAW_STAGE + a * kRawMat;
+      const int row = (cc < 256 ? cc >> 2 : (cc - 256) >> 1), grow = ks * TK + row;
+      if (cc < 256) {  // 16 bytes = 32 columns of packed nibbles
+        const int ch = cc & 3;
+        const bool v = grow < d.k && tcol + ch * 32 < n;
+        const uint8_t* src = v ? Mt.packed + (size_t)grow * (n / 2) + tcol / 2 + ch * 16 : Mt.packed;
+        cp_async16(base + row * kRawRow + ch * 16, src, v ? 16u : 0u);
+      } else {         // 4 bytes = 2 f16 scales = 64 columns
+        const int h = (cc - 256) & 1;
+        const bool v = grow < d.k && tcol + h * 64 < n;
+        const __half* src = v ? Mt.scales + (size_t)grow * (n / 32) + tcol / 32 + h * 2 : Mt.scales;
+        cp_async4(base + TK * kRawRow + row * 8 + h * 4, src, v ? 4u : 0u);
+      }
     }
   };
-  uint4 wn[NM], wn2[NM];  // weights of stages i + 1 and i + 2
-  unsigned short sn[NM], sn2[NM];
-#pragma unroll
-  for (int a = 0; a < NM; ++a) {
-    load_b(ks0, a, wn[a], sn[a]);
-    if (nst > 1) load_b(ks0 + 1, a, wn2[a], sn2[a]);
+  if (tid < kConv) {
+    for (int j = 0; j < C::RS - 1; ++j) {
+      if (j < nst) issue_b(ks0 + j, j);
+      cp_async_commit();
+    }
   }
 
   if (tid == 0) {
-    for (int s = 0; s < C::STAGES + 1; ++s) mbar_init(&mma_done[s], 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&mma_done[s], 1);
+      mbar_init(&full[s], kConv);
+    }
+    mbar_init(fin, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     *s_flag = 0u;
   }
@@ -306,8 +363,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
   const uint32_t tmem = *tmem_slot;
 
-  // ---- input rows of a stage -> registers (raw) and -> shared memory (split)
-  const int arow = tid & 63, akc = tid >> 6;
+  // ---- input rows of a stage (warps 7-14): registers one stage ahead ->
+  // shared memory (split).  Thread: row (at & 63) + 64 p, 16-deep k slice at / 64.
+  const bool a_thr = tid >= kBConv && tid < kConv;
+  const int at = tid - kBConv, arow = at & 63, akc = (at >> 6) & 3;
   const int npass = Mv > 64 ? 2 : 1;
   auto load_a = [&](int ks, ARegs& R) {
     const int kk0 = ks * TK + akc * 16;
@@ -369,7 +428,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       }
     }
   };
-  auto store_b = [&](uint8_t* bhi, uint8_t* blo, const uint4& w, unsigned short s) {
+  // B (warps 0-6): task = (k row brow, 32-column quarter bq of the tile), from the raw ring
+  auto store_b = [&](uint8_t* bhi, uint8_t* blo, int slot, int a, int brow, int bq) {
+    const uint8_t* base = tsm + C::PIPE_BYTES + slot * C::RAW_STAGE + a * kRawMat;
+    const uint4 w = *reinterpret_cast<const uint4*>(base + brow * kRawRow + bq * 16);
+    const unsigned short s = *reinterpret_cast<const unsigned short*>(base + TK * kRawRow + brow * 8 + bq * 2);
     const __half2 s2 = __half2half2(__ushort_as_half(s));
     const uint32_t words[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -382,57 +445,67 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
     }
   };
 
-  ARegs an;
-  load_a(ks0, an);
   bool ok = true;
-  for (int i = 0; i < nst; ++i) {
-    const int b = i % C::STAGES;
-    uint8_t* st = tsm + b * C::STAGE_BYTES;
-    const ARegs ac = an;
-    uint4 w[NM];
-    unsigned short s[NM];
-#pragma unroll
-    for (int a = 0; a < NM; ++a) {
-      w[a] = wn[a]; s[a] = sn[a];
-      wn[a] = wn2[a]; sn[a] = sn2[a];
-    }
-    // later stages' operands in flight while this one is converted
-    if (i + 1 < nst) load_a(ks0 + i + 1, an);
-    if (i + 2 < nst) {
-#pragma unroll
-      for (int a = 0; a < NM; ++a) load_b(ks0 + i + 2, a, wn2[a], sn2[a]);
-    }
-    // this buffer was read by the MMAs of stage i - STAGES
-    bool w_ok = true;
-    if (i >= C::STAGES) w_ok = mbar_wait(&mma_done[b], (unsigned)((i / C::STAGES) - 1) & 1u);
-    if (!__syncthreads_and(w_ok)) { ok = false; break; }
-    store_a(ks0 + i, ac, st, st + A_BYTES);
-#pragma unroll
-    for (int a = 0; a < NM; ++a)
-      store_b(st + 2 * A_BYTES + a * B_BYTES, st + 2 * A_BYTES + (NM + a) * B_BYTES, w[a], s[a]);
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // st.shared -> visible to tcgen05.mma
-    __syncthreads();
-    if (tid == 0) {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const uint32_t ahi = tsm_a + b * C::STAGE_BYTES, alo = ahi + A_BYTES;
-#pragma unroll
-      for (int a = 0; a < NM; ++a) {
-        const uint32_t bhi = ahi + 2 * A_BYTES + a * B_BYTES, blo = ahi + 2 * A_BYTES + (NM + a) * B_BYTES;
-        const uint32_t dm = tmem + (uint32_t)(a * 2 * TN), dc = dm + TN;
-#pragma unroll
-        for (int kk = 0; kk < TK / 16; ++kk) {
-          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          umma(dm, sdesc(ahi + kk * 256), sdesc(bhi + kk * 256), acc);
-          umma(dc, sdesc(ahi + kk * 256), sdesc(blo + kk * 256), acc);
-          umma(dc, sdesc(alo + kk * 256), sdesc(bhi + kk * 256), 1u);
+  if (tid < kConv) {
+    // ---- converters
+    ARegs an;
+    if (a_thr) load_a(ks0, an);
+    for (int i = 0; i < nst; ++i) {
+      const int b = i % C::STAGES;
+      uint8_t* st = tsm + b * C::STAGE_BYTES;
+      const ARegs ac = an;
+      if (a_thr && i + 1 < nst) load_a(ks0 + i + 1, an);  // input rows one stage ahead
+      cp_async_wait<C::RS - 2>();  // this thread's raw copies of stage i have landed
+      // this operand buffer was read by the MMAs of stage i - STAGES
+      bool w_ok = true;
+      if (i >= C::STAGES) w_ok = mbar_wait(&mma_done[b], (unsigned)((i / C::STAGES) - 1) & 1u);
+      // publishes every converter's raw copies of stage i; every conversion of
+      // stage i - 1 is done, so its raw slot takes stage i + RS - 1
+      if (!conv_sync_and(w_ok)) { ok = false; break; }
+      if (i + C::RS - 1 < nst) issue_b(ks0 + i + C::RS - 1, (i + C::RS - 1) % C::RS);
+      cp_async_commit();
+      if (a_thr) {
+        store_a(ks0 + i, ac, st, st + A_BYTES);
+      } else if (tid < kBConv) {
+        for (int tk = tid; tk < NM * 256; tk += kBConv) {
+          const int a = tk >> 8, brow = tk & 63, bq = (tk >> 6) & 3;
+          store_b(st + 2 * A_BYTES + a * B_BYTES, st + 2 * A_BYTES + (NM + a) * B_BYTES, i % C::RS, a, brow, bq);
         }
       }
-      umma_commit(&mma_done[b]);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // st.shared -> visible to tcgen05.mma
+      mbar_arrive(&full[b]);
     }
+  } else if (warp == kMmaWarp) {
+    // ---- MMA issue
+    for (int i = 0; i < nst; ++i) {
+      const int b = i % C::STAGES;
+      const bool f_ok = mbar_wait(&full[b], (unsigned)(i / C::STAGES) & 1u);
+      if (!__all_sync(0xffffffffu, f_ok)) { ok = false; break; }
+      if (lane == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t ahi = tsm_a + b * C::STAGE_BYTES, alo = ahi + A_BYTES;
+#pragma unroll
+        for (int a = 0; a < NM; ++a) {
+          const uint32_t bhi = ahi + 2 * A_BYTES + a * B_BYTES, blo = ahi + 2 * A_BYTES + (NM + a) * B_BYTES;
+          const uint32_t dm = tmem + (uint32_t)(a * 2 * TN), dc = dm + TN;
+#pragma unroll
+          for (int kk = 0; kk < TK / 16; ++kk) {
+            const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+            umma(dm, sdesc(ahi + kk * 256), sdesc(bhi + kk * 256), acc);
+            umma(dc, sdesc(ahi + kk * 256), sdesc(blo + kk * 256), acc);
+            umma(dc, sdesc(alo + kk * 256), sdesc(bhi + kk * 256), 1u);
+          }
+        }
+        umma_commit(&mma_done[b]);
+      }
+      __syncwarp();
+    }
+    // the commit tracks every earlier tcgen05.mma of this thread
+    if (lane == 0) umma_commit(fin);
   }
+  cp_async_wait<0>();  // no copy may land after the ring is reused for staging
   pdl_launch_dependents();
-  // drain: the commit tracks every earlier tcgen05.mma of thread 0
-  if (tid == 0) umma_commit(fin);
+  __syncthreads();
   const bool fin_ok = mbar_wait(fin, 0);
   if (amax > 65504.0f) atomicOr(s_flag, (unsigned)kErrFp16Range);
   if (!ok || !fin_ok) atomicOr(s_flag, (unsigned)kErrTimeout);
@@ -440,16 +513,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   __syncthreads();
   const bool good = (*s_flag & kErrTimeout) == 0;
 
-  // ---- accumulators -> shared staging (warp: lane quarter w % 4, column half w / 4)
+  // ---- accumulators -> shared staging (warp: lane quarter w % 4, 32-column block w / 4)
   {
-    const int lq = warp & 3, ch = warp >> 2;
+    const int lq = warp & 3, cb = warp >> 2;
     if (good && lq * 32 < Mv) {
       const int r = lq * 32 + lane;
 #pragma unroll
       for (int a = 0; a < NM; ++a) {
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int col = ch * 64 + c * 32;
+        {
+          const int col = cb * 32;
           float vm[32], vc[32];
           const uint32_t ta = tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(a * 2 * TN + col);
           tmem_ld32(ta, vm);
@@ -622,7 +694,11 @@ void tc_plan(int sm_count, GemvDesc& g) {
   const long units = tiles * ((g.M + TM - 1) / TM);
   g.tc = 1;
   g.tc_ks = (int)nks;
-  for (long S = std::min<long>(kMaxSplits, std::min<long>(nks, std::max<long>(1, sm_count / units))); S > 1; --S) {
+  static const long max_s = [] {  // QTTS_TC_SPLITS caps S (measurements)
+    const char* v = getenv("QTTS_TC_SPLITS");
+    return v ? std::max(1L, std::min<long>(kMaxSplits, atol(v))) : (long)kMaxSplits;
+  }();
+  for (long S = std::min<long>(max_s, std::min<long>(nks, std::max<long>(1, sm_count / units))); S > 1; --S) {
     GemvDesc t = g;
     t.tc_ks = (int)((nks + S - 1) / S);
     if (tc_splits(t) != S) continue;
@@ -641,8 +717,11 @@ void tc_plan(int sm_count, GemvDesc& g) {
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Operand and output layouts the kernel's vector accesses need.
+// Operand and output layouts the kernel's vector and asynchronous accesses
+// need (4-byte scale copies: rows of n / 32 scales start 4-byte aligned).
 bool tc_layout_ok(const GemvDesc& d) {
+  for (int i = 0; i < (d.paired ? 2 : d.nmat); ++i)
+    if (d.mat[i].n % 64 || !al16(d.mat[i].packed) || (reinterpret_cast<uintptr_t>(d.mat[i].scales) & 3u)) return false;
   if (!d.emb_idx && (!al16(d.X) || d.ldx % 4 || d.k % 4)) return false;
   const EpiDesc& e = d.epi;
   if (d.epi_kind != EPI_ARGMAX && d.epi_kind != EPI_QKV && (!al16(e.out) || e.ldo % 4)) return false;
