@@ -58,13 +58,19 @@ def frame_weight_bytes():
     return talker + head + pred_layers + proj + heads
 
 
-def load_peaks():
+def load_peaks_raw():
     try:
         with open(PEAKS_PATH) as f:
-            p = json.load(f)
-        return float(p["hbm_gbs"]), "measured"
+            return json.load(f)
     except Exception:
-        return 6650.0, "fallback"
+        return {}
+
+
+def load_peaks():
+    p = load_peaks_raw()
+    if "hbm_gbs" in p:
+        return float(p["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
 
 
 class ClockSampler:
@@ -184,11 +190,14 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def gemv_roofline(Q, torch, peak, peak_kind, stream):
-    """Time the dominant kernel (Q4 GEMV, talker gate/up shape k=2048,
-    n=6144, batch 1) on rotating weight copies larger than L2."""
-    k, n, m = 2048, 6144, 1
-    alg = q4_bytes(k, n) + 4 * k * m + 4 * n * m
+# DRAM bytes (read + write) of one k=2048 n=6144 m=1 launch of the batch-1
+# GEMV, from the ncu capture summarised in profiles/gemv_dec_2048x6144_ncu.md
+GEMV_TRAFFIC_BYTES = 7128320
+
+
+def time_q4_launches(Q, torch, k, n, m):
+    """Average device time of back-to-back qtts_q4_gemv_dev launches (one
+    CUDA graph of 200) rotating over weight copies larger than L2."""
     copies = max(4, (512 << 20) // q4_bytes(k, n) + 1)
     packed = [torch.randint(0, 256, (k * n // 2,), dtype=torch.uint8, device="cuda") for _ in range(copies)]
     scales = [(torch.rand(k * n // 32, device="cuda") * 0.02).half() for _ in range(copies)]
@@ -220,11 +229,72 @@ def gemv_roofline(Q, torch, peak, peak_kind, stream):
             g.replay()
         e1.record(s)
     e1.synchronize()
-    dt = e0.elapsed_time(e1) / 1e3 / (3 * reps)
+    return e0.elapsed_time(e1) / 1e3 / (3 * reps)
+
+
+def gemv_roofline(Q, torch, peak, peak_kind):
+    """The dominant kernel of the batch-1 frame: the Q4 GEMV (split-K,
+    cluster-reduced gemv_dec_kernel) at the talker gate shape k=2048, n=6144."""
+    k, n, m = 2048, 6144, 1
+    alg = q4_bytes(k, n) + 4 * k * m + 4 * n * m
+    dt = time_q4_launches(Q, torch, k, n, m)
     ach = alg / dt / 1e9
     return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
-            "traffic": None, "kernel": "gemv_q4_kernel<1,1,EPI_STORE> k=2048 n=6144 m=1",
+            "traffic": GEMV_TRAFFIC_BYTES, "kernel": "gemv_dec_kernel (Q4 GEMV) k=2048 n=6144 m=1",
             "us_per_launch": dt * 1e6, "algorithmic_bytes": alg, "peak_kind": f"hbm_gbs ({peak_kind})"}
+
+
+def tc_roofline(Q, torch, peaks):
+    """The dominant kernel of the batched frame: the tcgen05 projection at the
+    talker gate shape k=2048, n=6144 with 64 rows.  Useful FLOPs 2*m*k*n; the
+    tensor pipe executes 3 fp16 MMAs per product (hi/lo split) on 128-row
+    tiles, reported as executed_tflops."""
+    k, n, m = 2048, 6144, 64
+    dt = time_q4_launches(Q, torch, k, n, m)
+    fl = 2.0 * m * k * n
+    peak = peaks.get("bf16_tflops_sustained") or 1400.0
+    ach = fl / dt / 1e12
+    return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+            "traffic": None, "kernel": "tc_proj_kernel (tcgen05 Q4 projection) k=2048 n=6144 m=64",
+            "us_per_launch": dt * 1e6, "algorithmic_flops": fl,
+            "executed_tflops": 3 * (128 / m) * ach, "weight_gbs": q4_bytes(k, n) / dt / 1e9,
+            "peak_kind": "bf16_tflops_sustained (measured)" if "bf16_tflops_sustained" in peaks else "fallback"}
+
+
+# BASELINE config 2: the projection shapes of the model (out x in) at
+# batch 1, 8, 64 and 256.
+CONFIG2_SHAPES = [("q_proj", 2048, 4096), ("k_proj", 2048, 1024), ("v_proj", 2048, 1024), ("o_proj", 2048, 2048),
+                  ("gate/up_proj", 2048, 6144), ("down_proj", 6144, 2048), ("input_proj", 2048, 1024),
+                  ("group_head", 1024, 2048)]
+CONFIG2_BATCHES = [1, 8, 64, 256]
+
+
+def run_config2(args, Q, torch, peak, peak_kind):
+    """Isolated Q4 GEMV / GEMM microbench: device time per
+    launch over rotating weight copies larger than L2; m >= 16 runs on the
+    tcgen05 kernel, smaller m on the CUDA-core GEMV."""
+    rows = []
+    for name, k, n in CONFIG2_SHAPES:
+        for m in CONFIG2_BATCHES:
+            if args.only and args.only != f"{k}x{n}x{m}":
+                continue
+            dt = time_q4_launches(Q, torch, k, n, m)
+            alg = q4_bytes(k, n) + 4 * m * (k + n)
+            rows.append({"shape": name, "k": k, "n": n, "m": m, "us_per_launch": dt * 1e6,
+                         "gbs": alg / dt / 1e9, "useful_tflops": 2.0 * m * k * n / dt / 1e12,
+                         "kernel": "tc_proj_kernel" if m >= 16 else "gemv (CUDA cores)"})
+    head = [r for r in rows if r["k"] == 2048 and r["n"] == 6144 and r["m"] == 1] or rows[:1]
+    gbs = head[0]["gbs"] if head else None
+    line = {"metric": "Q4 GEMV HBM GB/s", "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": 3 * 200,
+            "warmup": 8, "ms_per_step": head[0]["us_per_launch"] / 1e3 if head else None,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config2: isolated Q4 GEMV/GEMM, x ~ N(0,1) f32, weights rotated over > 512 MB",
+                       "headline": "gate/up_proj k=2048 n=6144 m=1"},
+            "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
+                         "frac": gbs / peak if gbs else None, "traffic": GEMV_TRAFFIC_BYTES,
+                         "peak_kind": f"hbm_gbs ({peak_kind})"},
+            "microbench": rows}
+    print(json.dumps(line), flush=True)
 
 
 def main():
@@ -233,7 +303,8 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="config1", choices=["config1", "config4"])
+    ap.add_argument("--workload", default="config1", choices=["config1", "config2", "config4"])
+    ap.add_argument("--only", default="", help="config2: one case, KxNxM")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -253,6 +324,14 @@ def main():
     from qtts_b200.replicas import max_over_ranks
 
     torch.cuda.set_device(local)
+    if args.workload == "config2":
+        peak, peak_kind = load_peaks()
+        if rank == 0:
+            run_config2(args, Q, torch, peak, peak_kind)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
     if rank == 0:
         W.model_path("1p7b")
     barrier(world)
@@ -311,7 +390,10 @@ def main():
     h2d = sum(int(np.asarray(x["text"]).nbytes) + (2048 * 4 if x.get("voice") is not None else 0) for x in utts)
     d2h = B * args.steps * 16 * 4 + B * 4
 
-    roof = gemv_roofline(Q, torch, peak, peak_kind, sess.stream)
+    if args.workload == "config1":
+        roof = gemv_roofline(Q, torch, peak, peak_kind)
+    else:
+        roof = tc_roofline(Q, torch, load_peaks_raw())
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
