@@ -234,6 +234,7 @@ static int model_load(const char* path, int device, Model** out) {
   gemv_init_attributes();
   attn_init_attributes();
   tc_init_attributes();
+  pred_persist_init_attributes();
   *out = m;
   return QTTS_OK;
 }
@@ -556,6 +557,64 @@ static int add_predictor(Session& s, std::vector<Op>& ops, int B, bool frame_mod
   return QTTS_OK;
 }
 
+// The predictor of one utterance as one persistent cooperative kernel
+// (pred_persist.cu) instead of ~400 launches, opt-in with QTTS_PERSIST=1.  Its
+// phases cost about what a programmatic-dependent-launch graph node costs (a
+// grid barrier ~1.2 us plus the global round trips of the phase), so the
+// launch-per-projection plan stays the default.  `used` is false when the
+// shape is not covered.
+static bool persist_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("QTTS_PERSIST");
+    return v && v[0] == '1';
+  }();
+  return on;
+}
+
+static int add_predictor_persistent(Session& s, std::vector<Op>& ops, bool frame_mode, const FrameCodes& fc,
+                                    bool& used) {
+  used = false;
+  const Model& m = *s.m;
+  const qtts_dims& d = m.d;
+  if (!persist_enabled() || !s.pp_sync || d.p_layers > kPPMaxLayers) return QTTS_OK;
+  PredPersistDesc p;
+  p.pH = d.p_hidden; p.heads = d.p_heads; p.kvh = d.p_kv_heads; p.inter = d.p_inter; p.layers = d.p_layers;
+  p.groups = d.p_groups; p.t_hidden = d.t_hidden; p.rope_rows = d.p_max_pos;
+  for (int l = 0; l < d.p_layers; ++l) {
+    const DLayer& L = m.pl[l];
+    p.L[l].q = L.q; p.L[l].k = L.k; p.L[l].v = L.v; p.L[l].o = L.o;
+    p.L[l].gate = L.gate; p.L[l].up = L.up; p.L[l].down = L.down;
+    p.L[l].q_norm = L.q_norm; p.L[l].k_norm = L.k_norm; p.L[l].in_norm = L.in_norm; p.L[l].post_norm = L.post_norm;
+  }
+  p.proj = m.input_proj; p.proj_b = m.input_proj_b;
+  for (int g = 0; g < d.p_groups && g < kMaxGroups; ++g) {
+    if (g < (int)m.p_emb.size()) p.emb[g] = m.p_emb[g];
+    if (g < (int)m.lm.size()) p.lm[g] = m.lm[g];
+  }
+  p.final_norm = m.p_final; p.cos = m.p_cos; p.sin = m.p_sin;
+  p.kv = s.pkv_pool; p.pin = s.pin; p.part = s.part; p.X = s.pp_X; p.attn = s.attn;
+  p.bar = reinterpret_cast<unsigned*>(s.pp_sync); p.keys = s.pp_sync + 1; p.err_flag = s.err_flag;
+  p.fc = fc; p.frame_mode = frame_mode ? 1 : 0; p.codes_plain = s.codes_plain;
+  if (const char* v = getenv("QTTS_PP_SPLITS")) {  // "proj,qkv,o,gu,down" K slices (measurements)
+    int a[5];
+    if (sscanf(v, "%d,%d,%d,%d,%d", &a[0], &a[1], &a[2], &a[3], &a[4]) == 5) {
+      p.s_proj = a[0]; p.s_qkv = a[1]; p.s_o = a[2]; p.s_gu = a[3]; p.s_down = a[4];
+    }
+  }
+  if (!pred_persist_supported(p) || pred_persist_part_floats(p) > s.part_floats) return QTTS_OK;
+  g_occ_query = true;
+  g_occ_clusters = 0;
+  launch_pred_persist(p, 1, nullptr);
+  g_occ_query = false;
+  const int grid = std::min(128, g_occ_clusters * m.sm_count);
+  if (grid < d.p_heads) return QTTS_OK;  // the attention phase needs one CTA per query head
+  unsigned long long* sync = s.pp_sync;
+  ops.push_back([sync](cudaStream_t st) { return cudaMemsetAsync(sync, 0, 4 * sizeof(unsigned long long), st); });
+  ops.push_back([p, grid](cudaStream_t st) { return launch_pred_persist(p, grid, st); });
+  used = true;
+  return QTTS_OK;
+}
+
 // embed_text_token for rows of token ids (talker.rs:105-116):
 // fc1(emb) + b1 -> silu -> fc2 + b2.
 static int add_text_proj(Session& s, std::vector<Op>& ops, const uint32_t* tok_dev, int n, float* h1, float* out,
@@ -617,7 +676,7 @@ static void session_free_all(Session* s) {
   free_generation(*s);
   void* bufs[] = {s->kv_pool, s->page_table, s->pkv_pool, s->slots, s->x, s->pin, s->q, s->attn, s->h,
                   s->px, s->px1, s->logits, s->xpre, s->hid1, s->part, s->counters, s->counters2, s->keys,
-                  s->apart, s->acounters, s->err_flag, s->codes_plain, s->io, s->ssq_t, s->ssq_p, s->ssq_p1};
+                  s->apart, s->acounters, s->err_flag, s->codes_plain, s->io, s->ssq_t, s->ssq_p, s->ssq_p1, s->pp_X, s->pp_sync};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (s->st) cudaStreamDestroy(s->st);
@@ -675,6 +734,8 @@ static int session_create(Model* m, int maxB, int maxP, Session** out) {
   A(&s->ssq_t, (size_t)s->rows * kSsqLd);
   A(&s->ssq_p, (size_t)2 * maxB * kSsqLd);
   A(&s->ssq_p1, (size_t)maxB * kSsqLd);
+  A(&s->pp_X, (size_t)4 * d.p_hidden);  // persistent predictor: residual rows, barrier counter + argmax keys
+  A(&s->pp_sync, (size_t)4);
   if (rc == QTTS_OK) {  // pages: slot b owns pages [b*pps, (b+1)*pps)
     std::vector<int> pt((size_t)maxB * s->pages_per_sess);
     for (size_t i = 0; i < pt.size(); ++i) pt[i] = (int)i;
@@ -715,7 +776,9 @@ static int build_frame_ops(Session& s, std::vector<Op>& ops, bool dumps) {
   const Q4Mat ce = m.codec_emb;
   float* sem = s.pin + H;
   ops.push_back([=](cudaStream_t st) { return launch_embed_code0(ce, slots, B, sem, 2L * H, st); });
-  RC(add_predictor(s, ops, B, true, fc));
+  bool persistent = false;
+  if (B == 1) RC(add_predictor_persistent(s, ops, true, fc, persistent));
+  if (!persistent) RC(add_predictor(s, ops, B, true, fc));
   FuseDesc fd;
   fd.x = s.x; fd.ldx = H; fd.codec_emb = m.codec_emb; fd.group_emb = m.d_group_emb; fd.n_groups = d.p_groups;
   fd.trail = s.trail; fd.max_trail = s.max_trail; fd.tts_pad = s.tts_pad; fd.B = B; fd.H = H; fd.fc = fc;
@@ -979,7 +1042,9 @@ static int predict_call(Session& s, const float* hidden, const float* sem, uint3
   CK(cudaMemcpyAsync(s.pin, hidden, sizeof(float) * H, cudaMemcpyHostToDevice, s.st));
   CK(cudaMemcpyAsync(s.pin + H, sem, sizeof(float) * H, cudaMemcpyHostToDevice, s.st));
   std::vector<Op> ops;
-  RC(add_predictor(s, ops, 1, false, FrameCodes{}));
+  bool persistent = false;
+  RC(add_predictor_persistent(s, ops, false, FrameCodes{}, persistent));
+  if (!persistent) RC(add_predictor(s, ops, 1, false, FrameCodes{}));
   RC(run_ops(s, ops));
   uint32_t c[kMaxGroups];
   CK(cudaMemcpyAsync(c, s.codes_plain, sizeof(c), cudaMemcpyDeviceToHost, s.st));

@@ -239,6 +239,44 @@ size_t tc_smem_bytes(int nm);
 cudaError_t launch_tc(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st);
 void tc_init_attributes();
 
+// persistent code predictor of one utterance (pred_persist.cu)
+constexpr int kPPThreads = 256;
+constexpr int kPPMaxLayers = 8;
+constexpr int kPPMaxSlice = 1024;   // K rows of a unit (and the head's hidden size)
+constexpr int kPPMaxHidden = 2048;  // predictor hidden size
+constexpr int kPPMaxPos = 32;       // predictor positions (prefill 2 + 14 decode)
+constexpr int kPPSmem = (8192 * 2 + 2 * kPPMaxSlice + 2 * kPPMaxHidden + 32 + 4 + 3 * 2 * kHeadDim + 2 * kPPMaxPos) * 4;
+struct PPLayer {
+  Q4Mat q, k, v, o, gate, up, down;
+  const __half *q_norm = nullptr, *k_norm = nullptr, *in_norm = nullptr, *post_norm = nullptr;
+};
+struct PredPersistDesc {
+  int pH = 0, heads = 0, kvh = 0, inter = 0, layers = 0, groups = 0, t_hidden = 0, rope_rows = 0;
+  PPLayer L[kPPMaxLayers];
+  Q4Mat proj;
+  const float* proj_b = nullptr;
+  Q4Mat emb[kMaxGroups], lm[kMaxGroups];
+  const __half* final_norm = nullptr;
+  const float *cos = nullptr, *sin = nullptr;
+  float* kv = nullptr;         // predictor KV page of the utterance: [layer][K|V][kv_head][16][128]
+  const float* pin = nullptr;  // [talker hidden | semantic embedding], t_hidden each
+  float* part = nullptr;       // split-K partials (pred_persist_part_floats)
+  float* X = nullptr;          // residual rows: [2][pH] layer input, [2][pH] after attention
+  float* attn = nullptr;       // [2][heads * 128]
+  unsigned long long* keys = nullptr;  // [2] argmax keys, zero at launch
+  unsigned* bar = nullptr;     // grid-barrier counter, zero at launch
+  int* err_flag = nullptr;     // bit 16: a grid barrier gave up
+  FrameCodes fc;
+  int frame_mode = 0;
+  uint32_t* codes_plain = nullptr;
+  int s_proj = 8, s_qkv = 4, s_o = 8, s_gu = 2, s_down = 8;  // K slices per projection
+};
+size_t pred_persist_part_floats(const PredPersistDesc& d);
+bool pred_persist_supported(const PredPersistDesc& d);
+cudaError_t launch_pred_persist(const PredPersistDesc& d, int grid, cudaStream_t st);
+void pred_persist_init_attributes();
+
+
 struct AttnDesc {
   const float* q = nullptr;  // row m: heads*128
   long ldq = 0;
