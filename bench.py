@@ -303,7 +303,7 @@ def main():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="config1", choices=["config1", "config2", "config4"])
+    ap.add_argument("--workload", default="config1", choices=["config1", "config2", "config3", "config4"])
     ap.add_argument("--only", default="", help="config2: one case, KxNxM")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -343,6 +343,10 @@ def main():
         u, _ = W.config1(2048)
         utts = [dict(u, seed=int(u["seed"]) + rank)]
         wl = "config1: 1.7B Q4 talker+predictor, batch 1 per GPU, greedy, 32-token prompt + voice embedding"
+    elif args.workload == "config3":
+        u, _ = W.config3(2048)
+        utts = [dict(u, seed=int(u["seed"]) + rank)]
+        wl = "config3: 1.7B Q4, batch 1 per GPU, T=0.8 top-k 50, 96-token prompt, long KV (use --steps 2000)"
     else:
         utts, _ = W.config4(64, 2048)
         wl = "config4: 1.7B Q4, 64 utterances per GPU, T=0.8 top-k 50, prompts 16-256 tokens"
@@ -390,7 +394,7 @@ def main():
     h2d = sum(int(np.asarray(x["text"]).nbytes) + (2048 * 4 if x.get("voice") is not None else 0) for x in utts)
     d2h = B * args.steps * 16 * 4 + B * 4
 
-    if args.workload == "config1":
+    if args.workload in ("config1", "config3"):
         roof = gemv_roofline(Q, torch, peak, peak_kind)
     else:
         roof = tc_roofline(Q, torch, load_peaks_raw())
