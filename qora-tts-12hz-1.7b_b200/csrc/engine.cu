@@ -11,6 +11,7 @@
 
 #include <algorithm>
 #include <map>
+#include <memory>
 #include <mutex>
 #include <tuple>
 #include <cmath>
@@ -368,8 +369,35 @@ static int plan_gemv(Session& s, GemvDesc& g) {
   return QTTS_OK;
 }
 
+// The projection planned last in the current op list: the next one planned
+// fills in its L2-prefetch targets (GemvDesc::pf_*), so every projection
+// pulls its successor's weights into L2 while it runs.  QTTS_L2_PREFETCH=0
+// turns this off (measurements).
+static thread_local std::shared_ptr<GemvDesc> g_prev_gemv;
+static bool l2_prefetch_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("QTTS_L2_PREFETCH");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+static void chain_reset() { g_prev_gemv.reset(); }
+
 static Op gemv_op(const GemvDesc& g, const FrameCodes& fc = FrameCodes{}) {
-  return [g, fc](cudaStream_t st) { return launch_gemv(g, fc, st); };
+  auto sp = std::make_shared<GemvDesc>(g);
+  if (g_prev_gemv && l2_prefetch_enabled()) {
+    GemvDesc& p = *g_prev_gemv;
+    const int nm = g.paired ? 2 : g.nmat;
+    for (int i = 0; i < nm && i < 3; ++i) {
+      const Q4Mat& w = g.mat[i];
+      p.pf_ptr[2 * i] = w.packed;
+      p.pf_bytes[2 * i] = (uint32_t)((size_t)w.k * w.n / 2);
+      p.pf_ptr[2 * i + 1] = reinterpret_cast<const uint8_t*>(w.scales);
+      p.pf_bytes[2 * i + 1] = (uint32_t)(((size_t)w.k * w.n / 32 * 2) & ~(size_t)15);
+    }
+  }
+  g_prev_gemv = sp;
+  return [sp, fc](cudaStream_t st) { return launch_gemv(*sp, fc, st); };
 }
 
 struct LayerIO {
@@ -387,6 +415,9 @@ struct LayerIO {
   // ssq_valid = 0 when the input rows came without them (host copies)
   float* ssq = nullptr;
   int ssq_valid = 0;
+  // M = 1 with a short cache (the predictor): attention folded into the
+  // o_proj kernel's input prologue when its K split is one head per slice
+  int fuse_attn = 0;
 };
 
 // One transformer layer (talker.rs:279-349 / code_predictor.rs:448-502):
@@ -414,22 +445,27 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
   RC(plan_gemv(s, g));
   ops.push_back(gemv_op(g));
 
-  AttnDesc a;
-  a.q = s.q; a.ldq = qd; a.out = s.attn; a.ldo = qd; a.kv = io.kv; a.rp = io.rp;
-  a.heads = io.heads; a.kv_heads = io.kvh; a.M = io.M; a.nsplit = io.nsplit;
-  if (a.nsplit > 1) {
-    const size_t need = (size_t)io.M * io.kvh * a.nsplit * (io.heads / io.kvh) * kAttnRec;
-    if (need > s.apart_floats || (size_t)io.M * io.kvh > s.n_acounters)
-      return fail(QTTS_ERR_OOM, "attention split scratch too small");
-    a.part = s.apart;
-    a.counters = s.acounters;
-  }
-  ops.push_back([a](cudaStream_t st) { return launch_attention(a, st); });
-
   GemvDesc o = gemv_base(EPI_RESID, {L.o}, false, io.M);
   o.X = s.attn; o.ldx = qd; o.epi.out = io.X; o.epi.ldo = io.ldx;
   emit_ssq(o);
   RC(plan_gemv(s, o));
+  const bool fused = io.fuse_attn && io.M == 1 && !o.tc && o.rows_per_split == kHeadDim && o.S * kHeadDim == qd &&
+                     gemv_uses_decode_kernel(o);
+  if (fused) {
+    o.attn_in = 1; o.attn_q = s.q; o.attn_kv = io.kv; o.attn_rp = io.rp; o.attn_group = io.heads / io.kvh;
+  } else {
+    AttnDesc a;
+    a.q = s.q; a.ldq = qd; a.out = s.attn; a.ldo = qd; a.kv = io.kv; a.rp = io.rp;
+    a.heads = io.heads; a.kv_heads = io.kvh; a.M = io.M; a.nsplit = io.nsplit;
+    if (a.nsplit > 1) {
+      const size_t need = (size_t)io.M * io.kvh * a.nsplit * (io.heads / io.kvh) * kAttnRec;
+      if (need > s.apart_floats || (size_t)io.M * io.kvh > s.n_acounters)
+        return fail(QTTS_ERR_OOM, "attention split scratch too small");
+      a.part = s.apart;
+      a.counters = s.acounters;
+    }
+    ops.push_back([a](cudaStream_t st) { return launch_attention(a, st); });
+  }
   ops.push_back(gemv_op(o));
 
   GemvDesc gu = gemv_base(EPI_SWIGLU, {L.gate, L.up}, true, io.M);
@@ -517,6 +553,7 @@ static int add_predictor(Session& s, std::vector<Op>& ops, int B, bool frame_mod
       io.cos = m.p_cos; io.sin = m.p_sin; io.rope_rows = d.p_max_pos; io.skip_oob = 1;
       io.heads = d.p_heads; io.kvh = d.p_kv_heads; io.inter = d.p_inter; io.nsplit = 1;
       io.ssq = ssq; io.ssq_valid = 1;  // every input row comes from a projection epilogue
+      io.fuse_attn = (M == 1 && d.p_groups + 1 <= kAttnInMaxPos) ? 1 : 0;
       RC(add_layer(s, ops, m.pl[l], io));
     }
     return QTTS_OK;
@@ -634,6 +671,7 @@ static int add_text_proj(Session& s, std::vector<Op>& ops, const uint32_t* tok_d
 }
 
 static int run_ops(Session& s, const std::vector<Op>& ops) {
+  chain_reset();  // the next op list starts its own prefetch chain
   for (const Op& op : ops) {
     const cudaError_t e = op(s.st);
     if (e != cudaSuccess) return fail(QTTS_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
@@ -755,6 +793,7 @@ static int session_create(Model* m, int maxB, int maxP, Session** out) {
 // generation (generate_new.rs:191-300)
 // ---------------------------------------------------------------------------
 static int build_frame_ops(Session& s, std::vector<Op>& ops, bool dumps) {
+  chain_reset();
   const Model& m = *s.m;
   const qtts_dims& d = m.d;
   const int B = s.B, H = d.t_hidden, V = d.t_vocab;
@@ -1143,6 +1182,10 @@ static int gemv_dev(const uint8_t* packed, const uint16_t* scales, int k, int n,
   // the tensor-core kernel's float4 accesses need 16-byte aligned rows
   if (g.tc && (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 16)) g.tc = 0;
   g.cluster = 1;
+  // programmatic dependent launch, as in the frame: the kernel loads its
+  // weights while the previous kernel on the stream finishes and waits for it
+  // before reading x or writing y
+  g.pdl = 1;
   gemv_init_attributes();
   tc_init_attributes();
   fit_split_to_wave(g);

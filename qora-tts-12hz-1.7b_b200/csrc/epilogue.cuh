@@ -10,6 +10,27 @@
 namespace qtts {
 namespace {
 
+// L2 prefetch of the next projection's weights: every CTA of the launch takes
+// an equal 16-byte-aligned share of each region and thread 0 issues one bulk
+// prefetch per region (no registers, no shared memory, no completion to wait
+// for).  DRAM then streams the next layer's weights while this one computes.
+__device__ __forceinline__ void prefetch_next_weights(const GemvDesc& d) {
+  if (threadIdx.x != 0) return;
+  const unsigned nctas = gridDim.x * gridDim.y * gridDim.z;
+  const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+#pragma unroll
+  for (int i = 0; i < 6; ++i) {
+    const uint32_t bytes = d.pf_bytes[i];
+    if (!d.pf_ptr[i] || bytes == 0) continue;
+    const uint32_t share = ((bytes + nctas - 1) / nctas + 15u) & ~15u;
+    const uint32_t b0 = cta * share;
+    if (b0 >= bytes) continue;
+    const uint32_t n = min(share, bytes - b0) & ~15u;
+    if (n == 0) continue;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(d.pf_ptr[i] + b0), "r"(n) : "memory");
+  }
+}
+
 // RMSNorm scale of a row from the producer's per-tile sums of squares.
 __device__ __forceinline__ float inv_rms_from_ssq(const GemvDesc& d, int m) {
   const float* p = d.ssq_in + (size_t)m * d.ssq_ld;
@@ -79,7 +100,7 @@ __device__ __forceinline__ float* kv_row(const KvDesc& kv, int sess, int pos, in
 template <int MB, int NM, int EPI>
 __device__ __forceinline__ void gemv_epilogue(const GemvDesc& d, const FrameCodes& fc, float (&v)[NM][MB], int mat,
                                               int tile, int tcol, int m0, int mcnt, int zb, float* sbuf,
-                                              float* ybuf) {
+                                              float* ybuf, const float* res_pre = nullptr) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n = d.mat[mat].n;
   const int col = tcol + tid;
@@ -99,7 +120,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvDesc& d, const FrameCode
           e.out[(size_t)(m0 + mm) * e.ldo + cgl] = val;
         } else {
           float* o = e.out + (size_t)(m0 + mm) * e.ldo + cgl;
-          val = *o + v[0][mm];
+          val = (res_pre ? res_pre[mm] : *o) + v[0][mm];  // residual loaded ahead by the caller when given
           *o = val;
         }
       }

@@ -83,6 +83,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
   extern __shared__ __align__(16) float sm[];
   const bool clustered = d.cluster && d.S > 1;
   if (clustered) cluster_arrive_relaxed();  // completes before any DSMEM store below
+  prefetch_next_weights(d);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
   float* red = sm;                                  // [8 warps][4 rr][NM][256]
@@ -108,6 +109,13 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
   load_batch<NR, NM>(wb, d, mat, r0, R, rb0, gcol, gval, (size_t)n / 2, n / 32);
   pdl_wait();
 
+  // the residual this CTA's epilogue will add (root CTA, EPI_RESID): loaded
+  // now, alongside the inputs, instead of after the reduction
+  float res_pre[1] = {0.0f};
+  if (EPI == EPI_RESID && (!clustered || split == 0)) {
+    const int col = tcol + tid;
+    if (col < n) res_pre[0] = d.epi.out[d.col0[mat] + col];
+  }
   // input values of this lane's rows (one dependent round trip)
   float xv[NR];
   if (d.emb_idx) {
@@ -118,6 +126,48 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
     for (int i = 0; i < NR; ++i) {
       const int rb = rb0 + 32 * i;
       xv[i] = rb < R ? q4_value(prow, srow, r0 + rb) : 0.0f;
+    }
+  } else if (d.attn_in) {
+    // this K slice is query head h = r0 / 128: its attention output over
+    // cache positions [0, kvp] (code_predictor.rs:467-491) is the input slice
+    float* obuf = ybuf;        // [128] attention output
+    float* sc = ybuf + 128;    // [kAttnInMaxPos] scores, then weights
+    const int h = r0 / kHeadDim, hk = h / d.attn_group;
+    int sess, pos, kvp;
+    row_pos(d.attn_rp, 0, sess, pos, kvp);
+    const int L = kvp + 1;
+    const float4 q = *reinterpret_cast<const float4*>(d.attn_q + h * kHeadDim + 4 * lane);
+    const float scale = 1.0f / sqrtf((float)kHeadDim);
+    for (int j = warp; j < L; j += kGemvThreads / 32) {
+      const float4 kk = *reinterpret_cast<const float4*>(kv_row(d.attn_kv, sess, j, 0, hk) + 4 * lane);
+      float dot = q.x * kk.x + q.y * kk.y + q.z * kk.z + q.w * kk.w;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      if (lane == 0) sc[j] = dot * scale;
+    }
+    __syncthreads();
+    if (warp == 0) {  // max-subtracted softmax over the L <= 32 scores
+      const float s = lane < L ? sc[lane] : -INFINITY;
+      float mx = s;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float e = lane < L ? expf(s - mx) : 0.0f;
+      float sum = e;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (lane < L) sc[lane] = e * (1.0f / sum);
+    }
+    __syncthreads();
+    if (tid < kHeadDim) {
+      float o = 0.0f;
+      for (int j = 0; j < L; ++j) o += sc[j] * kv_row(d.attn_kv, sess, j, 1, hk)[tid];
+      obuf[tid] = o;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+      const int rb = rb0 + 32 * i;
+      xv[i] = rb < R ? obuf[rb] : 0.0f;
     }
   } else {
     float inv = 1.0f;
@@ -207,7 +257,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
       v[a][0] = t;
     }
   }
-  gemv_epilogue<1, NM, EPI>(d, fc, v, mat, tile, tcol, 0, 1, 0, sbuf, ybuf);
+  gemv_epilogue<1, NM, EPI>(d, fc, v, mat, tile, tcol, 0, 1, 0, sbuf, ybuf, EPI == EPI_RESID ? res_pre : nullptr);
 }
 
 // ===========================================================================
@@ -215,6 +265,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
 template <int MB, int NM, int EPI>
 __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvDesc d, const FrameCodes fc) {
   pdl_launch_dependents();
+  prefetch_next_weights(d);
   extern __shared__ __align__(16) float sm[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x, split = blockIdx.y, zb = blockIdx.z;
@@ -509,7 +560,11 @@ static cudaError_t launch_mb(const GemvDesc& d, const FrameCodes& fc, cudaStream
   return cudaErrorInvalidValue;
 }
 
+bool gemv_uses_decode_kernel(const GemvDesc& d) { return !d.tc && use_dec(d); }
+
 cudaError_t launch_gemv(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
+  if (d.attn_in && (d.tc || !use_dec(d) || d.rows_per_split != kHeadDim || d.epi_kind != EPI_RESID))
+    return cudaErrorInvalidValue;  // the attention prologue lives in the decode kernel only
   if (d.tc) return launch_tc(d, fc, st);
   if (d.ntiles <= 0 || d.S <= 0 || d.M <= 0 || d.rows_per_split <= 0) return cudaErrorInvalidValue;
   if (d.cluster && d.S > kMaxClusterSplits) return cudaErrorInvalidValue;

@@ -138,12 +138,24 @@ struct GemvDesc {
   // tensor-core path (tc_gemm.cu): tc = 1 runs the projection as one
   // tcgen05 kernel with K slices of tc_ks 64-deep stages reduced inside a
   // thread-block cluster
+  // attention prologue (M = 1, short KV): the input rows [r0, r0 + 128) of a
+  // K slice are the attention output of query head r0 / 128 over the cache
+  int attn_in = 0;
+  const float* attn_q = nullptr;  // rotated queries [heads * 128]
+  KvDesc attn_kv;
+  RowPos attn_rp;
+  int attn_group = 1;             // query heads per KV head
   int tc = 0;
   int tc_ks = 0;
+  // weights of the next projection in the frame (packed and scales of up to
+  // three matrices), pulled into L2 by this launch's CTAs as they start
+  const uint8_t* pf_ptr[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+  uint32_t pf_bytes[6] = {0, 0, 0, 0, 0, 0};
   int* err_flag = nullptr;      // bit 4: a bounded wait expired; bit 8: input outside the fp16 range
   EpiDesc epi;
 };
 constexpr int kMaxClusterSplits = 16;
+constexpr int kAttnInMaxPos = 32;  // cache positions the attention prologue handles
 // M = 1 decode kernel: weight rows a lane keeps in registers (32 rows per
 // step of the 8 warps x 4 row offsets), per matrix count
 constexpr int kDecRowsNM1 = 12;  // rows per split <= 384
@@ -226,6 +238,7 @@ inline cudaError_t launch_k(Kern kern, dim3 grid, dim3 block, size_t smem, cudaS
 // ---- launchers (return cudaError_t of the launch) ----
 size_t gemv_smem_bytes(const GemvDesc& d);
 cudaError_t launch_gemv(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st);
+bool gemv_uses_decode_kernel(const GemvDesc& d);  // M = 1 plan served by gemv_dec_kernel
 
 // tensor-core path (tc_gemm.cu)
 constexpr int kTcRows = 128;     // MMA tile rows (TMEM lanes)

@@ -282,6 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   const int mat = tc_tile(d, blockIdx.x, NM, tcol);
   const int n = d.mat[mat].n;
   if (tcol >= n) return;  // empty half tile (n % 256 != 0): the whole cluster leaves together
+  prefetch_next_weights(d);
   const int nks = (d.k + TK - 1) / TK;
   const int ks0 = blockIdx.y * d.tc_ks;
   const int nst = min(nks, ks0 + d.tc_ks) - ks0;  // >= 1 by construction of tc_ks
