@@ -74,6 +74,19 @@ __device__ __forceinline__ void load_batch(WBatch<U, NM>& b, const GemvDesc& d, 
 
 __device__ __forceinline__ float u16_h2f(unsigned short s) { return __half2float(__ushort_as_half(s)); }
 
+// One 256-column row of a reduction buffer, written by the 8 lanes gi = 0..7
+// of a 4-row warp slice (32 columns each).  Lane gi writes its 16-byte chunk c
+// at chunk (c + gi) % 8 of its group, so the 8 lanes of a store phase hit 8
+// different bank groups instead of one; red_col gives the physical index of
+// logical column col.
+__device__ __forceinline__ void red_store(float* row, int gi, const float2 (&acc)[16]) {
+  float4* dst = reinterpret_cast<float4*>(row + gi * 32);
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    dst[(c + gi) & 7] = make_float4(acc[2 * c].x, acc[2 * c].y, acc[2 * c + 1].x, acc[2 * c + 1].y);
+}
+__device__ __forceinline__ int red_col(int col) { return (col & ~31) | ((col + 4 * (col >> 5)) & 31); }
+
 }  // namespace
 
 // ===========================================================================
@@ -104,9 +117,17 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
   const bool gval = gcol < n;
   const int rb0 = warp * 4 + rr;
 
-  // every weight row of this lane, before waiting on the previous kernel
+  // every weight row of this lane and, for an RMSNorm prologue, the norm
+  // weights of its rows, before waiting on the previous kernel
   WBatch<NR, NM> wb;
   load_batch<NR, NM>(wb, d, mat, r0, R, rb0, gcol, gval, (size_t)n / 2, n / 32);
+  const bool norm_in = d.gamma && !d.emb_idx && !d.attn_in;
+  float gv[NR];
+#pragma unroll
+  for (int i = 0; i < NR; ++i) {
+    const int rb = rb0 + 32 * i;
+    gv[i] = (norm_in && rb < R) ? h2f(d.gamma[r0 + rb]) : 0.0f;
+  }
   pdl_wait();
 
   // the residual this CTA's epilogue will add (root CTA, EPI_RESID): loaded
@@ -116,7 +137,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
     const int col = tcol + tid;
     if (col < n) res_pre[0] = d.epi.out[d.col0[mat] + col];
   }
-  // input values of this lane's rows (one dependent round trip)
+  // Input values of this lane's rows.  Every load of a prologue is issued
+  // before the first of them is used (one dependent round trip), and the
+  // wait on the cluster barrier (every CTA of the cluster running, so DSMEM
+  // is live) overlaps them.
   float xv[NR];
   if (d.emb_idx) {
     const uint32_t row = d.emb_idx[0];
@@ -127,6 +151,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
       const int rb = rb0 + 32 * i;
       xv[i] = rb < R ? q4_value(prow, srow, r0 + rb) : 0.0f;
     }
+    if (clustered) cluster_wait();
   } else if (d.attn_in) {
     // this K slice is query head h = r0 / 128: its attention output over
     // cache positions [0, kvp] (code_predictor.rs:467-491) is the input slice
@@ -136,14 +161,27 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
     int sess, pos, kvp;
     row_pos(d.attn_rp, 0, sess, pos, kvp);
     const int L = kvp + 1;
+    constexpr int kPw = kAttnInMaxPos / (kGemvThreads / 32);  // positions per warp
     const float4 q = *reinterpret_cast<const float4*>(d.attn_q + h * kHeadDim + 4 * lane);
+    float4 kk[kPw];
+#pragma unroll
+    for (int t = 0; t < kPw; ++t) {
+      const int j = warp + t * (kGemvThreads / 32);
+      kk[t] = j < L ? *reinterpret_cast<const float4*>(kv_row(d.attn_kv, sess, j, 0, hk) + 4 * lane)
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float vc[kAttnInMaxPos];  // V column tid of every position (threads < 128)
+#pragma unroll
+    for (int j = 0; j < kAttnInMaxPos; ++j) vc[j] = (j < L && tid < kHeadDim) ? kv_row(d.attn_kv, sess, j, 1, hk)[tid] : 0.0f;
+    if (clustered) cluster_wait();
     const float scale = 1.0f / sqrtf((float)kHeadDim);
-    for (int j = warp; j < L; j += kGemvThreads / 32) {
-      const float4 kk = *reinterpret_cast<const float4*>(kv_row(d.attn_kv, sess, j, 0, hk) + 4 * lane);
-      float dot = q.x * kk.x + q.y * kk.y + q.z * kk.z + q.w * kk.w;
+#pragma unroll
+    for (int t = 0; t < kPw; ++t) {
+      const int j = warp + t * (kGemvThreads / 32);
+      float dot = q.x * kk[t].x + q.y * kk[t].y + q.z * kk[t].z + q.w * kk[t].w;
 #pragma unroll
       for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-      if (lane == 0) sc[j] = dot * scale;
+      if (lane == 0 && j < L) sc[j] = dot * scale;
     }
     __syncthreads();
     if (warp == 0) {  // max-subtracted softmax over the L <= 32 scores
@@ -160,7 +198,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
     __syncthreads();
     if (tid < kHeadDim) {
       float o = 0.0f;
-      for (int j = 0; j < L; ++j) o += sc[j] * kv_row(d.attn_kv, sess, j, 1, hk)[tid];
+#pragma unroll
+      for (int j = 0; j < kAttnInMaxPos; ++j)
+        if (j < L) o += sc[j] * vc[j];
       obuf[tid] = o;
     }
     __syncthreads();
@@ -170,9 +210,25 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
       xv[i] = rb < R ? obuf[rb] : 0.0f;
     }
   } else {
-    float inv = 1.0f;
+#pragma unroll
+    for (int i = 0; i < NR; ++i) {
+      const int rb = rb0 + 32 * i;
+      xv[i] = rb < R ? d.X[r0 + rb] : 0.0f;
+    }
+    // the producer's per-tile sums of squares (at most 16 tiles here)
+    const bool ssq16 = d.gamma && d.ssq_in && d.ssq_n <= 16;
+    float sv[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) sv[j] = (ssq16 && j < d.ssq_n) ? d.ssq_in[j] : 0.0f;
+    if (clustered) cluster_wait();
     if (d.gamma) {
-      if (d.ssq_in) {
+      float inv;
+      if (ssq16) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) ss += sv[j];  // tile order; the zero padding adds nothing
+        inv = 1.0f / sqrtf(ss / (float)d.k + 1e-6f);
+      } else if (d.ssq_in) {
         inv = inv_rms_from_ssq(d, 0);
       } else {
         float ss = 0.0f;
@@ -180,16 +236,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
         ss = block_sum_256(ss, sbuf);
         inv = 1.0f / sqrtf(ss / (float)d.k + 1e-6f);
       }
-    }
 #pragma unroll
-    for (int i = 0; i < NR; ++i) {
-      const int rb = rb0 + 32 * i;
-      float x = 0.0f;
-      if (rb < R) {
-        x = d.X[r0 + rb];
-        if (d.gamma) x = x * inv * h2f(d.gamma[r0 + rb]);  // gemv.rs:414
-      }
-      xv[i] = x;
+      for (int i = 0; i < NR; ++i) xv[i] = xv[i] * inv * gv[i];  // gemv.rs:414
     }
     if (d.xnorm_out && tile == 0 && gi == 0) {
 #pragma unroll
@@ -223,27 +271,23 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
   // while this one reduces, without crowding out this kernel's own loads.
   pdl_launch_dependents();
   // CTA reduction through shared memory: 32 (warp, rr) partials per column
+  // (group-rotated rows: red_store / red_col)
 #pragma unroll
-  for (int a = 0; a < NM; ++a) {
-    float4* dst = reinterpret_cast<float4*>(red + ((warp * 4 + rr) * NM + a) * kTileN + gi * 32);
-#pragma unroll
-    for (int c = 0; c < 8; ++c)
-      dst[c] = make_float4(acc[a][2 * c].x, acc[a][2 * c].y, acc[a][2 * c + 1].x, acc[a][2 * c + 1].y);
-  }
+  for (int a = 0; a < NM; ++a) red_store(red + ((warp * 4 + rr) * NM + a) * kTileN, gi, acc[a]);
   __syncthreads();
   float v[NM][1];
+  const int pc = red_col(tid);
 #pragma unroll
   for (int a = 0; a < NM; ++a) {
     float t = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 32; ++j) t += red[(j * NM + a) * kTileN + tid];
+    for (int j = 0; j < 32; ++j) t += red[(j * NM + a) * kTileN + pc];
     v[a][0] = t;
   }
 
   if (clustered) {
     cg::cluster_group cl = cg::this_cluster();
     const int rank = (int)cl.block_rank();
-    cluster_wait();  // every CTA of the cluster is running: DSMEM is live
     float* root = cl.map_shared_rank(pbuf, 0);
 #pragma unroll
     for (int a = 0; a < NM; ++a) root[(rank * NM + a) * kTileN + tid] = v[a][0];
@@ -387,23 +431,18 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvDesc d,
 #pragma unroll
     for (int a = 0; a < NM; ++a)
 #pragma unroll
-      for (int mm = 0; mm < MB; ++mm) {
-        float4* dst = reinterpret_cast<float4*>(red + ((warp * NM + a) * MB + mm) * kTileN + gi * 32);
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          dst[c] = make_float4(acc[a][mm][2 * c].x, acc[a][mm][2 * c].y, acc[a][mm][2 * c + 1].x,
-                               acc[a][mm][2 * c + 1].y);
-      }
+      for (int mm = 0; mm < MB; ++mm) red_store(red + ((warp * NM + a) * MB + mm) * kTileN, gi, acc[a][mm]);
   }
   __syncthreads();
   float v[NM][MB];
+  const int pc = red_col(tid);
 #pragma unroll
   for (int a = 0; a < NM; ++a)
 #pragma unroll
     for (int mm = 0; mm < MB; ++mm) {
       float t = 0.0f;
 #pragma unroll
-      for (int w8 = 0; w8 < 8; ++w8) t += red[((w8 * NM + a) * MB + mm) * kTileN + tid];
+      for (int w8 = 0; w8 < 8; ++w8) t += red[((w8 * NM + a) * MB + mm) * kTileN + pc];
       v[a][mm] = t;
     }
 
