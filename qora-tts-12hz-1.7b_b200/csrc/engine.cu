@@ -320,8 +320,13 @@ void choose_split(int sm_count, GemvDesc& g) {
   g.mb = g.paired ? (g.M >= 2 ? 2 : 1) : (g.M >= 3 ? 4 : (g.M == 2 ? 2 : 1));
   const int zb = ceil_div(g.M, g.mb);
   const int target = 2 * sm_count;
+  static const int max_splits = [] {  // QTTS_GEMV_MAX_SPLITS caps S (measurements)
+    const char* v = getenv("QTTS_GEMV_MAX_SPLITS");
+    const int s = v ? atoi(v) : 0;
+    return s > 0 ? std::min(s, kMaxClusterSplits) : kMaxClusterSplits;
+  }();
   int S = (int)std::lround((double)target / (double)(g.ntiles * zb));
-  S = std::max(1, std::min(std::min(S, kMaxClusterSplits), ceil_div(g.k, 32)));
+  S = std::max(1, std::min(std::min(S, max_splits), ceil_div(g.k, 32)));
   int rps = ceil_div(ceil_div(g.k, S), 32) * 32;
   rps = std::min(rps, 2048);
   g.rows_per_split = rps;
@@ -343,9 +348,9 @@ static int plan_gemv(Session& s, GemvDesc& g) {
   g.cluster = 1;  // split-K partials reduced over distributed shared memory
   g.pdl = 1;
   fit_split_to_wave(g);
+  g.err_flag = s.err_flag;
   if (g.M >= kTcMinRows && tc_enabled()) {
     tc_plan(s.m->sm_count, g);  // one tcgen05 kernel: prologue, GEMM, split-K, epilogue
-    g.err_flag = s.err_flag;
     g.part = s.part;
     const size_t zt = (size_t)ceil_div(g.M, kTcRows);
     if (tc_splits(g) > 1 &&
@@ -684,7 +689,9 @@ static int sync_check(Session& s) {
   CK(cudaMemcpy(&flag, s.err_flag, sizeof(int), cudaMemcpyDeviceToHost));
   if (flag) {
     CK(cudaMemset(s.err_flag, 0, sizeof(int)));
-    return fail(QTTS_ERR_RANGE, "position beyond the talker RoPE table (rope.rs:73 would panic)");
+    if (flag & kErrRopeRange) return fail(QTTS_ERR_RANGE, "position beyond the talker RoPE table (rope.rs:73 would panic)");
+    if (flag & kErrFp16Input) return fail(QTTS_ERR_RANGE, "tensor-core input outside the fp16 range");
+    return fail(QTTS_ERR_TIMEOUT, "a bounded device wait expired (cluster peer, pipeline or grid barrier)");
   }
   return QTTS_OK;
 }

@@ -104,12 +104,62 @@ __device__ __forceinline__ float* kv_row(const KvDesc& kv, int sess, int pos, in
 }
 
 // ---------------------------------------------------------------------------
+// QKV epilogue inputs of one thread (column tcol + tid of matrix mat, input
+// row 0) gathered during the decode kernel's prologue, so the epilogue makes
+// no dependent global round trip: the QK-norm weight (before the wait: a
+// weight), the rope position (issued with the inputs), then the RoPE factors
+// and the destination (issued once the position has arrived, consumed only
+// after the reduction).
+struct QkvPre {
+  bool on = false;
+  float g = 0.0f;                   // q_norm / k_norm weight of the column
+  int pos_raw = 0;                  // pos_base entry (or pos_const)
+  int sess = 0, pos = 0, kvp = 0;
+  int page = 0;                     // KV page of (sess, kvp)
+  bool rope_ok = false;             // pos inside the RoPE table
+  float c = 0.0f, sn = 0.0f;        // cos / sin of (pos, column % 64)
+};
+__device__ __forceinline__ void qkv_pre_weights(QkvPre& q, const GemvDesc& d, int mat, int col) {
+  if (mat == 2 || col >= d.mat[mat].n) return;
+  q.g = h2f((mat == 0 ? d.epi.q_norm : d.epi.k_norm)[col % kHeadDim]);
+}
+__device__ __forceinline__ void qkv_pre_pos(QkvPre& q, const GemvDesc& d) {
+  const RowPos& rp = d.epi.rp;
+  q.sess = rp.sess0;
+  q.pos_raw = rp.pos_base ? rp.pos_base[q.sess * rp.pos_stride] : rp.pos_const;
+}
+// Loads whose results are consumed only in the epilogue (no stall here).
+__device__ __forceinline__ void qkv_pre_rest(QkvPre& q, const GemvDesc& d, int mat, int col) {
+  const EpiDesc& e = d.epi;
+  q.pos = q.pos_raw;  // row 0 of the session (row_pos with m = 0)
+  q.kvp = e.rp.kv_const >= 0 ? e.rp.kv_const : q.pos;
+  if (col >= d.mat[mat].n) return;
+  if (mat != 0) q.page = e.kv.page_table ? e.kv.page_table[q.sess * e.kv.pages_per_sess + q.kvp / kPageSize] : q.sess;
+  if (mat == 2) return;
+  const int half = kHeadDim / 2, i = (col % kHeadDim) % half;
+  q.rope_ok = q.pos < e.rope_rows && q.pos >= 0;
+  if (q.rope_ok) {
+    q.c = e.rope_cos[(size_t)q.pos * half + i];
+    q.sn = e.rope_sin[(size_t)q.pos * half + i];
+  }
+}
+// Destination of the column: q_out, or its K / V cache element (kv_row).
+__device__ __forceinline__ float* qkv_dst(const QkvPre& q, const EpiDesc& e, int mat, int col) {
+  if (mat == 0) return e.q_out + col;
+  const KvDesc& kv = e.kv;
+  const int h = col / kHeadDim;
+  const size_t blk = (((size_t)q.page * kv.n_layers + kv.layer) * 2 + (mat == 2 ? 1 : 0)) * kv.kv_heads + h;
+  return kv.pool + (blk * kPageSize + (q.kvp % kPageSize)) * kHeadDim + col % kHeadDim;
+}
+
+// ---------------------------------------------------------------------------
 // Epilogues, run by the root CTA of a tile with v[a][mm] = column tcol+tid of
 // matrix a for input row m0+mm.  All 256 threads take part.
 template <int MB, int NM, int EPI>
 __device__ __forceinline__ void gemv_epilogue(const GemvDesc& d, const FrameCodes& fc, float (&v)[NM][MB], int mat,
                                               int tile, int tcol, int m0, int mcnt, int zb, float* sbuf,
-                                              float* ybuf, const float* res_pre = nullptr) {
+                                              float* ybuf, const float* res_pre = nullptr,
+                                              const QkvPre* qp = nullptr) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n = d.mat[mat].n;
   const int col = tcol + tid;
@@ -148,6 +198,37 @@ __device__ __forceinline__ void gemv_epilogue(const GemvDesc& d, const FrameCode
   } else if (EPI == EPI_QKV) {
     // mat 0 = q, 1 = k, 2 = v; heads of 128 columns never straddle a tile.
     const int h = col / kHeadDim, dd = col % kHeadDim, hl = tid / kHeadDim;
+    if (MB == 1 && qp && qp->on) {  // one row, everything it needs preloaded
+      if (mat == 2) {
+        if (cval) *qkv_dst(*qp, e, mat, col) = v[0][0];
+        return;
+      }
+      const float x = cval ? v[0][0] : 0.0f;
+      float sq = x * x;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      __syncthreads();
+      if (lane == 0) sbuf[warp] = sq;
+      __syncthreads();
+      const float ss = sbuf[hl * 4 + 0] + sbuf[hl * 4 + 1] + sbuf[hl * 4 + 2] + sbuf[hl * 4 + 3];
+      const float inv = 1.0f / sqrtf(ss / (float)kHeadDim + 1e-6f);
+      const float y = x * inv * qp->g;
+      ybuf[tid] = y;
+      __syncthreads();
+      const int half = kHeadDim / 2, i = dd % half;
+      const float x1 = ybuf[hl * kHeadDim + i];
+      const float x2 = ybuf[hl * kHeadDim + half + i];
+      if (cval) {
+        float outv = y;
+        if (qp->rope_ok) {
+          outv = (dd < half) ? (x1 * qp->c - x2 * qp->sn) : (x2 * qp->c + x1 * qp->sn);
+        } else if (!e.rope_skip_oob && e.err_flag) {
+          atomicOr(e.err_flag, kErrRopeRange);
+        }
+        *qkv_dst(*qp, e, mat, col) = outv;
+      }
+      return;
+    }
 #pragma unroll
     for (int mm = 0; mm < MB; ++mm) {
       const int m = m0 + mm;
@@ -186,7 +267,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvDesc& d, const FrameCode
           const float sn = e.rope_sin[(size_t)pos * half + i];
           outv = (dd < half) ? (x1 * c - x2 * sn) : (x2 * c + x1 * sn);
         } else if (!e.rope_skip_oob && e.err_flag) {
-          atomicOr(e.err_flag, 1);
+          atomicOr(e.err_flag, kErrRopeRange);
         }
         if (mat == 0) {
           e.q_out[(size_t)m * e.ldq + col] = outv;

@@ -39,8 +39,53 @@ namespace {
 __device__ __forceinline__ float ld_cg(const float* p) { return __ldcg(p); }
 
 __device__ __forceinline__ void cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
-__device__ __forceinline__ void cluster_arrive_release() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
+__device__ __forceinline__ uint32_t dsmem_map(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+// mbarrier with one arrival (the root's expect-tx), made visible to the
+// cluster before the CTA's barrier.cluster.arrive.relaxed.
+__device__ __forceinline__ void mbar_init_cluster(uint64_t* bar) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n\tfence.mbarrier_init.release.cluster;" ::"r"(smem_addr(bar))
+               : "memory");
+}
+__device__ __forceinline__ void mbar_expect_arrive(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+// Remote 4-byte store into a peer CTA's shared memory that completes 4
+// transaction bytes on the peer's mbarrier.
+__device__ __forceinline__ void st_async_f32(uint32_t raddr, float v, uint32_t rbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(raddr), "f"(v),
+               "r"(rbar)
+               : "memory");
+}
+// Phase-0 wait with cluster-scope acquire (the peers' st.async data), bounded
+// by one second of %globaltimer; false when it ran out.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar) {
+  const uint32_t a = smem_addr(bar);
+  unsigned long long t0 = 0;
+  for (unsigned it = 0;; ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], 0;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(a)
+        : "memory");
+    if (done) return true;
+    if ((it & 255u) == 0) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (it == 0) t0 = t;
+      else if (t - t0 > 1000000000ull) return false;
+    }
+  }
+}
 
 
 // Weight words + raw f16 scales of U row-steps of one lane (NM matrices).
@@ -95,14 +140,18 @@ template <int NM, int EPI, int NR>
 __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d, const FrameCodes fc) {
   extern __shared__ __align__(16) float sm[];
   const bool clustered = d.cluster && d.S > 1;
-  if (clustered) cluster_arrive_relaxed();  // completes before any DSMEM store below
-  prefetch_next_weights(d);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x, split = blockIdx.y;
   float* red = sm;                                  // [8 warps][4 rr][NM][256]
   float* pbuf = red + 8 * 4 * NM * kTileN;          // [S][NM][256] partials pushed to the root
   float* sbuf = pbuf + kMaxClusterSplits * NM * kTileN;  // 64 floats
   float* ybuf = sbuf + 64;                          // [256]
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(ybuf + kTileN);  // root: partials landed
+  if (clustered) {
+    if (split == 0 && tid == 0) mbar_init_cluster(mbar);
+    cluster_arrive_relaxed();  // the wait below precedes any DSMEM store
+  }
+  prefetch_next_weights(d);
 
   int mat = 0;
   if (NM == 1) {
@@ -128,7 +177,13 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
     const int rb = rb0 + 32 * i;
     gv[i] = (norm_in && rb < R) ? h2f(d.gamma[r0 + rb]) : 0.0f;
   }
+  QkvPre qp;  // QKV root CTA: what its epilogue reads, gathered in the prologue
+  if (EPI == EPI_QKV && (!clustered || split == 0)) {
+    qp.on = true;
+    qkv_pre_weights(qp, d, mat, tcol + tid);
+  }
   pdl_wait();
+  if (EPI == EPI_QKV && qp.on) qkv_pre_pos(qp, d);
 
   // the residual this CTA's epilogue will add (root CTA, EPI_RESID): loaded
   // now, alongside the inputs, instead of after the reduction
@@ -152,6 +207,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
       xv[i] = rb < R ? q4_value(prow, srow, r0 + rb) : 0.0f;
     }
     if (clustered) cluster_wait();
+    if (EPI == EPI_QKV && qp.on) qkv_pre_rest(qp, d, mat, tcol + tid);
   } else if (d.attn_in) {
     // this K slice is query head h = r0 / 128: its attention output over
     // cache positions [0, kvp] (code_predictor.rs:467-491) is the input slice
@@ -174,6 +230,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
 #pragma unroll
     for (int j = 0; j < kAttnInMaxPos; ++j) vc[j] = (j < L && tid < kHeadDim) ? kv_row(d.attn_kv, sess, j, 1, hk)[tid] : 0.0f;
     if (clustered) cluster_wait();
+    if (EPI == EPI_QKV && qp.on) qkv_pre_rest(qp, d, mat, tcol + tid);
     const float scale = 1.0f / sqrtf((float)kHeadDim);
 #pragma unroll
     for (int t = 0; t < kPw; ++t) {
@@ -221,6 +278,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
 #pragma unroll
     for (int j = 0; j < 16; ++j) sv[j] = (ssq16 && j < d.ssq_n) ? d.ssq_in[j] : 0.0f;
     if (clustered) cluster_wait();
+    if (EPI == EPI_QKV && qp.on) qkv_pre_rest(qp, d, mat, tcol + tid);
     if (d.gamma) {
       float inv;
       if (ssq16) {
@@ -286,22 +344,30 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
   }
 
   if (clustered) {
-    cg::cluster_group cl = cg::this_cluster();
-    const int rank = (int)cl.block_rank();
-    float* root = cl.map_shared_rank(pbuf, 0);
+    // Split-K: every other CTA of the cluster pushes its partial into the
+    // root's shared memory with st.async, which completes bytes on the root's
+    // mbarrier, and leaves; only the root waits (no second cluster barrier).
+    const int rank = split;  // the cluster spans grid.y
+    if (rank != 0) {
+      const uint32_t rp = dsmem_map(smem_addr(pbuf), 0), rm = dsmem_map(smem_addr(mbar), 0);
 #pragma unroll
-    for (int a = 0; a < NM; ++a) root[(rank * NM + a) * kTileN + tid] = v[a][0];
-    cluster_arrive_release();
-    cluster_wait();
-    if (rank != 0) return;
+      for (int a = 0; a < NM; ++a) st_async_f32(rp + 4u * (uint32_t)((rank * NM + a) * kTileN + tid), v[a][0], rm);
+      return;
+    }
+    if (tid == 0) mbar_expect_arrive(mbar, (uint32_t)((d.S - 1) * NM * kTileN * sizeof(float)));
+    if (!mbar_wait_cluster(mbar)) {  // a peer never delivered: flag it, write nothing
+      if (tid == 0 && d.err_flag) atomicOr(d.err_flag, kErrWaitExpired);
+      return;
+    }
 #pragma unroll
     for (int a = 0; a < NM; ++a) {
-      float t = 0.0f;
-      for (int sp = 0; sp < d.S; ++sp) t += pbuf[(sp * NM + a) * kTileN + tid];
+      float t = v[a][0];  // split 0 first, then the others in split order
+      for (int sp = 1; sp < d.S; ++sp) t += pbuf[(sp * NM + a) * kTileN + tid];
       v[a][0] = t;
     }
   }
-  gemv_epilogue<1, NM, EPI>(d, fc, v, mat, tile, tcol, 0, 1, 0, sbuf, ybuf, EPI == EPI_RESID ? res_pre : nullptr);
+  gemv_epilogue<1, NM, EPI>(d, fc, v, mat, tile, tcol, 0, 1, 0, sbuf, ybuf, EPI == EPI_RESID ? res_pre : nullptr,
+                            EPI == EPI_QKV ? &qp : nullptr);
 }
 
 // ===========================================================================
@@ -512,7 +578,7 @@ static bool use_dec(const GemvDesc& d) {
 size_t gemv_smem_bytes(const GemvDesc& d) {
   const int NM = d.paired ? 2 : 1;
   if (use_dec(d))
-    return sizeof(float) * ((size_t)8 * 4 * NM * kTileN + (size_t)kMaxClusterSplits * NM * kTileN + 64 + kTileN);
+    return sizeof(float) * ((size_t)8 * 4 * NM * kTileN + (size_t)kMaxClusterSplits * NM * kTileN + 64 + kTileN + 4);
   return sizeof(float) * ((size_t)d.mb * d.rows_per_split + 8 * NM * d.mb * kTileN + 64 + d.mb * kTileN);
 }
 

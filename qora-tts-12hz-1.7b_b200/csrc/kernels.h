@@ -154,6 +154,11 @@ struct GemvDesc {
   int* err_flag = nullptr;      // bit 4: a bounded wait expired; bit 8: input outside the fp16 range
   EpiDesc epi;
 };
+// err_flag bits shared by the kernels (the session's flag word)
+constexpr int kErrRopeRange = 1;     // a position beyond the talker RoPE table
+constexpr int kErrWaitExpired = 4;   // a bounded device wait ran out
+constexpr int kErrFp16Input = 8;     // a tensor-core input outside the fp16 range
+constexpr int kErrGridBarrier = 16;  // a persistent kernel's grid barrier gave up
 constexpr int kMaxClusterSplits = 16;
 constexpr int kAttnInMaxPos = 32;  // cache positions the attention prologue handles
 // M = 1 decode kernel: weight rows a lane keeps in registers (32 rows per

@@ -60,7 +60,7 @@ __device__ __forceinline__ void grid_sync(const PredPersistDesc& d, unsigned pha
     unsigned it = 0;
     while (ld_acquire(d.bar) < target) {
       if (++it > kSpinLimit) {
-        atomicOr(d.err_flag, 16);
+        atomicOr(d.err_flag, kErrGridBarrier);
         break;
       }
       __nanosleep(32);

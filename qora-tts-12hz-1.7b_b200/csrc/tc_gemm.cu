@@ -71,7 +71,7 @@ constexpr int kMaxSplits = 8;  // portable cluster size
 constexpr float kLoScale = 2048.0f;
 constexpr float kLoUnscale = 1.0f / 2048.0f;
 constexpr unsigned long long kWaitNs = 1000000000ull;  // 1 s bound on any wait
-constexpr int kErrTimeout = 4, kErrFp16Range = 8;      // err_flag bits
+constexpr int kErrTimeout = kErrWaitExpired, kErrFp16Range = kErrFp16Input;      // err_flag bits
 
 constexpr int kRawRow = 80;                       // raw packed row stride: 64 B + pad (conflict-free 16 B reads)
 constexpr int kRawMat = TK * kRawRow + TK * 8;     // one matrix's raw stage: packed rows + 4 f16 scales per row
@@ -632,7 +632,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
             o[j] = (dd < half) ? (x1 * c - x2 * sn) : (x2 * c + x1 * sn);
           }
         }
-        if (!in_range && !e.rope_skip_oob && e.err_flag && lane == 0) atomicOr(e.err_flag, 1);
+        if (!in_range && !e.rope_skip_oob && e.err_flag && lane == 0) atomicOr(e.err_flag, kErrRopeRange);
         float* dst;
         if (mat == 0) {
           dst = e.q_out + (size_t)m * e.ldq + col;
