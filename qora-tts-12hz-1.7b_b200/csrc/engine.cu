@@ -299,7 +299,11 @@ int gemv_wave_clusters(const GemvDesc& g) {
 // With a cluster-reduced K split, every (tile, row block) is one cluster and
 // all of them should be resident in one wave: lower S until they fit.
 static void fit_split_to_wave(GemvDesc& g) {
-  if (g.tc || !g.cluster) return;
+  static const bool on = [] {  // QTTS_WAVE_FIT=0: keep choose_split's S (measurements)
+    const char* v = getenv("QTTS_WAVE_FIT");
+    return !(v && v[0] == '0');
+  }();
+  if (g.tc || !g.cluster || !on) return;
   const long units = (long)g.ntiles * ceil_div(g.M, g.mb);
   for (int S = g.S; S >= 1; --S) {
     GemvDesc t = g;
@@ -372,6 +376,16 @@ static int plan_gemv(Session& s, GemvDesc& g) {
     g.epi.keys = s.keys;
   }
   return QTTS_OK;
+}
+
+// QTTS_GLU_SPLIT=0 keeps the paired gate/up launch for one decode row too
+// (measurements).
+static bool glu_split_enabled() {
+  static const bool on = [] {
+    const char* v = getenv("QTTS_GLU_SPLIT");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 // The projection planned last in the current op list: the next one planned
@@ -473,16 +487,36 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
   }
   ops.push_back(gemv_op(o));
 
-  GemvDesc gu = gemv_base(EPI_SWIGLU, {L.gate, L.up}, true, io.M);
-  gu.X = io.X; gu.ldx = io.ldx; gu.gamma = L.post_norm; gu.epi.out = s.h; gu.epi.ldo = io.inter;
-  use_ssq(gu, true);
-  RC(plan_gemv(s, gu));
-  ops.push_back(gemv_op(gu));
-
   GemvDesc dn = gemv_base(EPI_RESID, {L.down}, false, io.M);
   dn.X = s.h; dn.ldx = io.inter; dn.epi.out = io.X; dn.epi.ldo = io.ldx;
   emit_ssq(dn);
   RC(plan_gemv(s, dn));
+
+  // One decode row: gate and up as two matrices of one launch (twice the
+  // tiles, so more K slices fit the decode kernel's registers), SiLU on the
+  // gate columns in its epilogue, the product silu(gate) * up taken by the
+  // down projection's prologue (x_glu).  Otherwise the paired SwiGLU launch.
+  GemvDesc gs = gemv_base(EPI_STORE, {L.gate, L.up}, false, io.M);
+  gs.X = io.X; gs.ldx = io.ldx; gs.gamma = L.post_norm; gs.epi.out = s.h; gs.epi.ldo = 2L * io.inter;
+  gs.epi.act_silu = 1;  // matrix 0 = gate
+  use_ssq(gs, true);
+  bool split_glu = false;
+  if (io.M == 1 && glu_split_enabled() && (size_t)2 * io.inter <= s.h_floats) {
+    RC(plan_gemv(s, gs));
+    GemvDesc dg = dn;
+    dg.x_glu = io.inter;
+    split_glu = gemv_uses_decode_kernel(gs) && gemv_uses_decode_kernel(dg);
+    if (split_glu) dn = dg;
+  }
+  if (split_glu) {
+    ops.push_back(gemv_op(gs));
+  } else {
+    GemvDesc gu = gemv_base(EPI_SWIGLU, {L.gate, L.up}, true, io.M);
+    gu.X = io.X; gu.ldx = io.ldx; gu.gamma = L.post_norm; gu.epi.out = s.h; gu.epi.ldo = io.inter;
+    use_ssq(gu, true);
+    RC(plan_gemv(s, gu));
+    ops.push_back(gemv_op(gu));
+  }
   ops.push_back(gemv_op(dn));
   return QTTS_OK;
 }
@@ -500,7 +534,12 @@ static KvDesc pred_kv(Session& s, int layer) {
   return k;
 }
 static int talker_nsplit(Session& s, int M) {
-  const int byL = ceil_div(s.maxP, 64);
+  static const int per_split = [] {  // QTTS_ATTN_CHUNK: cache positions per split (measurements)
+    const char* v = getenv("QTTS_ATTN_CHUNK");
+    const int c = v ? atoi(v) : 0;
+    return c > 0 ? c : 32;
+  }();
+  const int byL = ceil_div(s.maxP, per_split);
   const int byPar = std::max(1, ceil_div(4L * s.m->sm_count, (long)M * s.m->d.t_kv_heads));
   return std::max(1, std::min(kMaxClusterSplits, std::min(byL, byPar)));
 }
@@ -757,6 +796,7 @@ static int session_create(Model* m, int maxB, int maxP, Session** out) {
   A(&s->q, (size_t)s->rows * qmax);
   A(&s->attn, (size_t)s->rows * qmax);
   A(&s->h, (size_t)s->rows * imax);
+  s->h_floats = (size_t)s->rows * imax;
   A(&s->px, (size_t)2 * maxB * d.p_hidden);
   A(&s->px1, (size_t)maxB * d.p_hidden);
   A(&s->logits, (size_t)maxB * d.t_vocab);

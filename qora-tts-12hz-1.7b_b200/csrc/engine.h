@@ -54,6 +54,7 @@ struct Session {
   // activations
   int rows = 0;  // row capacity of q/attn/h/xpre (10 * maxB)
   float *x = nullptr, *pin = nullptr, *q = nullptr, *attn = nullptr, *h = nullptr;
+  size_t h_floats = 0;  // capacity of h
   float *px = nullptr, *px1 = nullptr, *logits = nullptr, *xpre = nullptr, *hid1 = nullptr;
   // scratch
   float* part = nullptr;

@@ -175,7 +175,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvDesc& d, const FrameCode
         if (EPI == EPI_STORE) {
           val = v[0][mm];
           if (e.bias) val = val + e.bias[cgl];
-          if (e.act_silu) val = silu_ref(val);
+          if ((e.act_silu >> mat) & 1) val = silu_ref(val);
           e.out[(size_t)(m0 + mm) * e.ldo + cgl] = val;
         } else {
           float* o = e.out + (size_t)(m0 + mm) * e.ldo + cgl;

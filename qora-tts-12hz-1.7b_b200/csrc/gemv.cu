@@ -267,10 +267,12 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
       xv[i] = rb < R ? obuf[rb] : 0.0f;
     }
   } else {
+    float xg[NR];  // GLU: the up half of the row
 #pragma unroll
     for (int i = 0; i < NR; ++i) {
       const int rb = rb0 + 32 * i;
       xv[i] = rb < R ? d.X[r0 + rb] : 0.0f;
+      xg[i] = (d.x_glu && rb < R) ? d.X[d.x_glu + r0 + rb] : 0.0f;
     }
     // the producer's per-tile sums of squares (at most 16 tiles here)
     const bool ssq16 = d.gamma && d.ssq_in && d.ssq_n <= 16;
@@ -296,6 +298,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
       }
 #pragma unroll
       for (int i = 0; i < NR; ++i) xv[i] = xv[i] * inv * gv[i];  // gemv.rs:414
+    }
+    if (d.x_glu) {
+#pragma unroll
+      for (int i = 0; i < NR; ++i) xv[i] = xv[i] * xg[i];  // silu(gate) * up (gemv.rs:449-451)
     }
     if (d.xnorm_out && tile == 0 && gi == 0) {
 #pragma unroll
@@ -670,6 +676,8 @@ bool gemv_uses_decode_kernel(const GemvDesc& d) { return !d.tc && use_dec(d); }
 cudaError_t launch_gemv(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
   if (d.attn_in && (d.tc || !use_dec(d) || d.rows_per_split != kHeadDim || d.epi_kind != EPI_RESID))
     return cudaErrorInvalidValue;  // the attention prologue lives in the decode kernel only
+  if (d.x_glu && (d.tc || !use_dec(d) || d.gamma || d.emb_idx || d.attn_in || d.paired))
+    return cudaErrorInvalidValue;  // the GLU prologue lives in the decode kernel's plain input path
   if (d.tc) return launch_tc(d, fc, st);
   if (d.ntiles <= 0 || d.S <= 0 || d.M <= 0 || d.rows_per_split <= 0) return cudaErrorInvalidValue;
   if (d.cluster && d.S > kMaxClusterSplits) return cudaErrorInvalidValue;

@@ -71,7 +71,7 @@ struct EpiDesc {
   float* out = nullptr;
   long ldo = 0;
   const float* bias = nullptr;
-  int act_silu = 0;
+  int act_silu = 0;  // bit a: SiLU on the columns of matrix a (after the bias)
   // QKV
   float* q_out = nullptr;
   long ldq = 0;
@@ -152,6 +152,9 @@ struct GemvDesc {
   const uint8_t* pf_ptr[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   uint32_t pf_bytes[6] = {0, 0, 0, 0, 0, 0};
   int* err_flag = nullptr;      // bit 4: a bounded wait expired; bit 8: input outside the fp16 range
+  // GLU input (decode kernel only): x[r] = X[r] * X[x_glu + r], the SwiGLU
+  // product of a row holding silu(gate) in [0, x_glu) and up in [x_glu, 2 x_glu)
+  int x_glu = 0;
   EpiDesc epi;
 };
 // err_flag bits shared by the kernels (the session's flag word)

@@ -581,7 +581,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             if (e.bias) vv[j] = vv[j] + e.bias[cgl + j];
-            if (e.act_silu) vv[j] = silu_ref(vv[j]);
+            if ((e.act_silu >> mat) & 1) vv[j] = silu_ref(vv[j]);
           }
         } else {
           const float4 ov = *reinterpret_cast<const float4*>(o);
