@@ -347,11 +347,40 @@ static int dalloc(T** p, size_t count, std::vector<void*>* track = nullptr) {
   return QTTS_OK;
 }
 
+// One decode row whose register-resident K slices would not fit one wave:
+// stage each CTA's slice in shared memory instead, one CTA per SM (about
+// sm_count / tiles K slices), when the slice and its cluster fit.  Opt-in
+// (QTTS_STAGED=1): with one 8-warp CTA per SM the dequant-FMA runs at a low
+// issue rate, and on the talker's gate/up it measured slower than the
+// general kernel it replaces (321 vs 338 frames/s at batch 1).
+static void try_staged(int sm_count, GemvDesc& g) {
+  static const bool on = [] {
+    const char* v = getenv("QTTS_STAGED");
+    return v && v[0] == '1';
+  }();
+  if (!on || g.M != 1 || gemv_uses_decode_kernel(g) || !gemv_staged_eligible(g)) return;
+  GemvDesc t = g;
+  t.staged = 1;
+  t.cluster = 1;
+  for (int S = std::min(kMaxClusterSplits, std::max(1, sm_count / g.ntiles)); S >= 1; --S) {
+    const int rps = ceil_div(ceil_div(g.k, S), 32) * 32;
+    if (rps > 32 * kDecRowsStg) return;  // fewer slices are only longer
+    t.rows_per_split = rps;
+    t.S = ceil_div(g.k, rps);
+    if (gemv_smem_bytes(t) > (size_t)kDecStgMaxSmem) return;
+    if (gemv_wave_clusters(t) >= g.ntiles) {
+      g = t;
+      return;
+    }
+  }
+}
+
 static int plan_gemv(Session& s, GemvDesc& g) {
   choose_split(s.m->sm_count, g);
   g.cluster = 1;  // split-K partials reduced over distributed shared memory
   g.pdl = 1;
   fit_split_to_wave(g);
+  try_staged(s.m->sm_count, g);
   g.err_flag = s.err_flag;
   if (g.M >= kTcMinRows && tc_enabled()) {
     tc_plan(s.m->sm_count, g);  // one tcgen05 kernel: prologue, GEMM, split-K, epilogue
@@ -367,7 +396,8 @@ static int plan_gemv(Session& s, GemvDesc& g) {
   }();
   if (log_plans)
     fprintf(stderr, "qtts plan: epi %d k %d ncols %d M %d -> %s S %d rows/split %d\n", g.epi_kind, g.k, g.ncols, g.M,
-            g.tc ? "tcgen05" : "cuda-core", g.tc ? tc_splits(g) : g.S, g.tc ? g.tc_ks * kTcK : g.rows_per_split);
+            g.tc ? "tcgen05" : (g.staged ? "cuda-core staged" : "cuda-core"), g.tc ? tc_splits(g) : g.S,
+            g.tc ? g.tc_ks * kTcK : g.rows_per_split);
   const size_t zb = (size_t)ceil_div(g.M, g.mb);
   if ((size_t)g.ntiles * zb > s.n_counters || zb > 4096) return fail(QTTS_ERR_OOM, "tile counter array too small");
   g.counters = s.counters;

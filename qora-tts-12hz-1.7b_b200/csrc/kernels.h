@@ -155,6 +155,9 @@ struct GemvDesc {
   // GLU input (decode kernel only): x[r] = X[r] * X[x_glu + r], the SwiGLU
   // product of a row holding silu(gate) in [0, x_glu) and up in [x_glu, 2 x_glu)
   int x_glu = 0;
+  // decode kernel with the CTA's weight slice staged in shared memory
+  // (gemv_staged_eligible) instead of registers: more rows per K slice
+  int staged = 0;
   EpiDesc epi;
 };
 // err_flag bits shared by the kernels (the session's flag word)
@@ -168,6 +171,8 @@ constexpr int kAttnInMaxPos = 32;  // cache positions the attention prologue han
 // step of the 8 warps x 4 row offsets), per matrix count
 constexpr int kDecRowsNM1 = 12;  // rows per split <= 384
 constexpr int kDecRowsNM2 = 6;   // rows per split <= 192
+constexpr int kDecRowsStg = 24;  // staged (weights in shared memory): rows per split <= 768
+constexpr int kDecStgMaxSmem = 227 * 1024;  // dynamic shared memory of a staged decode CTA
 constexpr int kSsqLd = 64;       // row stride of the sum-of-squares partials
 constexpr int kSsqCols = 128;    // columns summed per partial (rows up to 64 * 128 wide)
 
@@ -247,6 +252,7 @@ inline cudaError_t launch_k(Kern kern, dim3 grid, dim3 block, size_t smem, cudaS
 size_t gemv_smem_bytes(const GemvDesc& d);
 cudaError_t launch_gemv(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st);
 bool gemv_uses_decode_kernel(const GemvDesc& d);  // M = 1 plan served by gemv_dec_kernel
+bool gemv_staged_eligible(const GemvDesc& d);     // M = 1 plan may stage its weights in shared memory
 
 // tensor-core path (tc_gemm.cu)
 constexpr int kTcRows = 128;     // MMA tile rows (TMEM lanes)
