@@ -214,7 +214,15 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
   WBatch<STG ? 1 : NR, NM> wb;
   if constexpr (STG) stg_issue<NM>(d, mat, tcol, r0, R, smem_addr(sm));
   else load_batch<NR, NM>(wb, d, mat, r0, R, rb0, gcol, gval, (size_t)n / 2, n / 32);
-  const bool norm_in = d.gamma && !d.emb_idx && !d.attn_in;
+  // Prologue forms compiled per epilogue (the host rejects other pairings):
+  // the embedding gather feeds STORE launches (input_proj, text fc1), the
+  // attention and GLU inputs feed RESID launches (O, down), RMSNorm feeds the
+  // rest.  Keeping the unused forms out keeps each instance's code small: a
+  // batch-1 frame cycles through a few instances, and instruction fetch is a
+  // top stall of these short kernels.
+  constexpr bool kEmb = EPI == EPI_STORE, kAttn = EPI == EPI_RESID, kGlu = EPI == EPI_RESID,
+                 kNorm = EPI != EPI_RESID;
+  const bool norm_in = kNorm && d.gamma && !d.emb_idx && !d.attn_in;
   float gv[NR];
 #pragma unroll
   for (int i = 0; i < NR; ++i) {
@@ -241,7 +249,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
   // wait on the cluster barrier (every CTA of the cluster running, so DSMEM
   // is live) overlaps them.
   float xv[NR];
-  if (d.emb_idx) {
+  if (kEmb && d.emb_idx) {
     const uint32_t row = d.emb_idx[0];
     const uint8_t* prow = d.emb.packed + (size_t)row * (d.emb.n / 2);
     const __half* srow = d.emb.scales + (size_t)row * (d.emb.n / 32);
@@ -252,7 +260,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
     }
     if (clustered) cluster_wait();
     if (EPI == EPI_QKV && qp.on) qkv_pre_rest(qp, d, mat, tcol + tid);
-  } else if (d.attn_in) {
+  } else if (kAttn && d.attn_in) {
     // this K slice is query head h = r0 / 128: its attention output over
     // cache positions [0, kvp] (code_predictor.rs:467-491) is the input slice
     float* obuf = ybuf;        // [128] attention output
@@ -316,16 +324,16 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
     for (int i = 0; i < NR; ++i) {
       const int rb = rb0 + 32 * i;
       xv[i] = rb < R ? d.X[r0 + rb] : 0.0f;
-      xg[i] = (d.x_glu && rb < R) ? d.X[d.x_glu + r0 + rb] : 0.0f;
+      xg[i] = (kGlu && d.x_glu && rb < R) ? d.X[d.x_glu + r0 + rb] : 0.0f;
     }
     // the producer's per-tile sums of squares (at most 16 tiles here)
-    const bool ssq16 = d.gamma && d.ssq_in && d.ssq_n <= 16;
+    const bool ssq16 = kNorm && d.gamma && d.ssq_in && d.ssq_n <= 16;
     float sv[16];
 #pragma unroll
     for (int j = 0; j < 16; ++j) sv[j] = (ssq16 && j < d.ssq_n) ? d.ssq_in[j] : 0.0f;
     if (clustered) cluster_wait();
     if (EPI == EPI_QKV && qp.on) qkv_pre_rest(qp, d, mat, tcol + tid);
-    if (d.gamma) {
+    if (kNorm && d.gamma) {
       float inv;
       if (ssq16) {
         float ss = 0.0f;
@@ -343,7 +351,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
 #pragma unroll
       for (int i = 0; i < NR; ++i) xv[i] = xv[i] * inv * gv[i];  // gemv.rs:414
     }
-    if (d.x_glu) {
+    if (kGlu && d.x_glu) {
 #pragma unroll
       for (int i = 0; i < NR; ++i) xv[i] = xv[i] * xg[i];  // silu(gate) * up (gemv.rs:449-451)
     }
@@ -710,7 +718,9 @@ static cudaError_t dispatch_dec(const GemvDesc& d, const FrameCodes& fc, cudaStr
     if (nr <= 4) return launch_dec<2, EPI, 4>(d, fc, st);
     return launch_dec<2, EPI, kDecRowsNM2>(d, fc, st);
   }
-  if (nr <= 4) return launch_dec<1, EPI, 4>(d, fc, st);
+  // residual projections (O and down) share one instance: fewer distinct
+  // kernels in a layer's instruction stream
+  if (nr <= 4 && EPI != EPI_RESID) return launch_dec<1, EPI, 4>(d, fc, st);
   if (nr <= 8) return launch_dec<1, EPI, 8>(d, fc, st);
   return launch_dec<1, EPI, kDecRowsNM1>(d, fc, st);
 }
@@ -774,8 +784,11 @@ bool gemv_uses_decode_kernel(const GemvDesc& d) { return !d.tc && use_dec(d); }
 cudaError_t launch_gemv(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
   if (d.attn_in && (d.tc || !use_dec(d) || d.rows_per_split != kHeadDim || d.epi_kind != EPI_RESID))
     return cudaErrorInvalidValue;  // the attention prologue lives in the decode kernel only
-  if (d.x_glu && (d.tc || !use_dec(d) || d.gamma || d.emb_idx || d.attn_in || d.paired))
+  if (d.x_glu && (d.tc || !use_dec(d) || d.gamma || d.emb_idx || d.attn_in || d.paired || d.epi_kind != EPI_RESID))
     return cudaErrorInvalidValue;  // the GLU prologue lives in the decode kernel's plain input path
+  if (!d.tc && use_dec(d) &&
+      ((d.emb_idx && d.epi_kind != EPI_STORE) || (d.gamma && d.epi_kind == EPI_RESID)))
+    return cudaErrorInvalidValue;  // prologue forms the decode kernel compiles per epilogue
   if (d.tc) return launch_tc(d, fc, st);
   if (d.ntiles <= 0 || d.S <= 0 || d.M <= 0 || d.rows_per_split <= 0) return cudaErrorInvalidValue;
   if (d.cluster && d.S > kMaxClusterSplits) return cudaErrorInvalidValue;
