@@ -321,7 +321,8 @@ static void fit_split_to_wave(GemvDesc& g) {
 // Split-K choice: about two CTAs per SM, slices of whole 32-row blocks, at
 // most 2048 rows per slice (shared-memory bound of the input slice).
 void choose_split(int sm_count, GemvDesc& g) {
-  g.mb = g.paired ? (g.M >= 2 ? 2 : 1) : (g.M >= 3 ? 4 : (g.M == 2 ? 2 : 1));
+  // up to kDecMaxM rows: one row per CTA (the decode kernel's grid.z)
+  g.mb = g.M <= kDecMaxM ? 1 : (g.paired ? 2 : 4);
   const int zb = ceil_div(g.M, g.mb);
   const int target = 2 * sm_count;
   static const int max_splits = [] {  // QTTS_GEMV_MAX_SPLITS caps S (measurements)
@@ -498,10 +499,11 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
   o.X = s.attn; o.ldx = qd; o.epi.out = io.X; o.epi.ldo = io.ldx;
   emit_ssq(o);
   RC(plan_gemv(s, o));
-  const bool fused = io.fuse_attn && io.M == 1 && !o.tc && o.rows_per_split == kHeadDim && o.S * kHeadDim == qd &&
+  const bool fused = io.fuse_attn && io.M <= kDecMaxM && !o.tc && o.rows_per_split == kHeadDim && o.S * kHeadDim == qd &&
                      gemv_uses_decode_kernel(o);
   if (fused) {
-    o.attn_in = 1; o.attn_q = s.q; o.attn_kv = io.kv; o.attn_rp = io.rp; o.attn_group = io.heads / io.kvh;
+    o.attn_in = 1; o.attn_q = s.q; o.attn_ldq = qd; o.attn_kv = io.kv; o.attn_rp = io.rp;
+    o.attn_group = io.heads / io.kvh;
   } else {
     AttnDesc a;
     a.q = s.q; a.ldq = qd; a.out = s.attn; a.ldo = qd; a.kv = io.kv; a.rp = io.rp;
@@ -531,10 +533,11 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
   gs.epi.act_silu = 1;  // matrix 0 = gate
   use_ssq(gs, true);
   bool split_glu = false;
-  if (io.M == 1 && glu_split_enabled() && (size_t)2 * io.inter <= s.h_floats) {
+  if (io.M <= kDecMaxM && glu_split_enabled() && (size_t)2 * io.inter * io.M <= s.h_floats) {
     RC(plan_gemv(s, gs));
     GemvDesc dg = dn;
     dg.x_glu = io.inter;
+    dg.ldx = 2L * io.inter;
     split_glu = gemv_uses_decode_kernel(gs) && gemv_uses_decode_kernel(dg);
     if (split_glu) dn = dg;
   }
@@ -627,7 +630,7 @@ static int add_predictor(Session& s, std::vector<Op>& ops, int B, bool frame_mod
       io.cos = m.p_cos; io.sin = m.p_sin; io.rope_rows = d.p_max_pos; io.skip_oob = 1;
       io.heads = d.p_heads; io.kvh = d.p_kv_heads; io.inter = d.p_inter; io.nsplit = 1;
       io.ssq = ssq; io.ssq_valid = 1;  // every input row comes from a projection epilogue
-      io.fuse_attn = (M == 1 && d.p_groups + 1 <= kAttnInMaxPos) ? 1 : 0;
+      io.fuse_attn = (M <= kDecMaxM && d.p_groups + 1 <= kAttnInMaxPos) ? 1 : 0;
       RC(add_layer(s, ops, m.pl[l], io));
     }
     return QTTS_OK;

@@ -105,7 +105,7 @@ __device__ __forceinline__ float* kv_row(const KvDesc& kv, int sess, int pos, in
 
 // ---------------------------------------------------------------------------
 // QKV epilogue inputs of one thread (column tcol + tid of matrix mat, input
-// row 0) gathered during the decode kernel's prologue, so the epilogue makes
+// row m) gathered during the decode kernel's prologue, so the epilogue makes
 // no dependent global round trip: the QK-norm weight (before the wait: a
 // weight), the rope position (issued with the inputs), then the RoPE factors
 // and the destination (issued once the position has arrived, consumed only
@@ -113,6 +113,7 @@ __device__ __forceinline__ float* kv_row(const KvDesc& kv, int sess, int pos, in
 struct QkvPre {
   bool on = false;
   float g = 0.0f;                   // q_norm / k_norm weight of the column
+  int m = 0, r = 0;                 // input row; its index within the session's rows
   int pos_raw = 0;                  // pos_base entry (or pos_const)
   int sess = 0, pos = 0, kvp = 0;
   int page = 0;                     // KV page of (sess, kvp)
@@ -123,16 +124,19 @@ __device__ __forceinline__ void qkv_pre_weights(QkvPre& q, const GemvDesc& d, in
   if (mat == 2 || col >= d.mat[mat].n) return;
   q.g = h2f((mat == 0 ? d.epi.q_norm : d.epi.k_norm)[col % kHeadDim]);
 }
-__device__ __forceinline__ void qkv_pre_pos(QkvPre& q, const GemvDesc& d) {
-  const RowPos& rp = d.epi.rp;
-  q.sess = rp.sess0;
+__device__ __forceinline__ void qkv_pre_pos(QkvPre& q, const GemvDesc& d, int m) {
+  const RowPos& rp = d.epi.rp;  // row_pos, split in two loads' halves
+  const int sl = m / rp.rows_per_sess;
+  q.m = m;
+  q.r = m - sl * rp.rows_per_sess;
+  q.sess = rp.sess0 + sl;
   q.pos_raw = rp.pos_base ? rp.pos_base[q.sess * rp.pos_stride] : rp.pos_const;
 }
 // Loads whose results are consumed only in the epilogue (no stall here).
 __device__ __forceinline__ void qkv_pre_rest(QkvPre& q, const GemvDesc& d, int mat, int col) {
   const EpiDesc& e = d.epi;
-  q.pos = q.pos_raw;  // row 0 of the session (row_pos with m = 0)
-  q.kvp = e.rp.kv_const >= 0 ? e.rp.kv_const : q.pos;
+  q.pos = q.pos_raw + q.r;
+  q.kvp = e.rp.kv_const >= 0 ? e.rp.kv_const + q.r : q.pos;
   if (col >= d.mat[mat].n) return;
   if (mat != 0) q.page = e.kv.page_table ? e.kv.page_table[q.sess * e.kv.pages_per_sess + q.kvp / kPageSize] : q.sess;
   if (mat == 2) return;
@@ -145,7 +149,7 @@ __device__ __forceinline__ void qkv_pre_rest(QkvPre& q, const GemvDesc& d, int m
 }
 // Destination of the column: q_out, or its K / V cache element (kv_row).
 __device__ __forceinline__ float* qkv_dst(const QkvPre& q, const EpiDesc& e, int mat, int col) {
-  if (mat == 0) return e.q_out + col;
+  if (mat == 0) return e.q_out + (size_t)q.m * e.ldq + col;
   const KvDesc& kv = e.kv;
   const int h = col / kHeadDim;
   const size_t blk = (((size_t)q.page * kv.n_layers + kv.layer) * 2 + (mat == 2 ? 1 : 0)) * kv.kv_heads + h;

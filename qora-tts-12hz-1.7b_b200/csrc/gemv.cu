@@ -175,7 +175,7 @@ __host__ __device__ inline int dec_front_floats(int NM, bool stg, int rows) {
 }
 
 // ===========================================================================
-// M = 1 decode kernel
+// Decode kernel: M <= kDecMaxM input rows, one per blockIdx.z
 // STG: the weight slice is staged in shared memory (rows per split up to
 // 32 * NR, no weight registers) instead of held in registers.
 template <int NM, int EPI, int NR, bool STG>
@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
   extern __shared__ __align__(16) float sm[];
   const bool clustered = d.cluster && d.S > 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int tile = blockIdx.x, split = blockIdx.y;
+  const int tile = blockIdx.x, split = blockIdx.y, m = blockIdx.z;  // input row m
   float* red = sm;                                  // [8 warps][4 rr][NM][256] (STG: over the weights)
   float* pbuf = sm + dec_front_floats(NM, STG, d.rows_per_split);  // [S][NM][256] partials pushed to the root
   float* sbuf = pbuf + kMaxClusterSplits * NM * kTileN;  // 64 floats
@@ -235,14 +235,14 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
     qkv_pre_weights(qp, d, mat, tcol + tid);
   }
   pdl_wait();
-  if (EPI == EPI_QKV && qp.on) qkv_pre_pos(qp, d);
+  if (EPI == EPI_QKV && qp.on) qkv_pre_pos(qp, d, m);
 
   // the residual this CTA's epilogue will add (root CTA, EPI_RESID): loaded
   // now, alongside the inputs, instead of after the reduction
   float res_pre[1] = {0.0f};
   if (EPI == EPI_RESID && (!clustered || split == 0)) {
     const int col = tcol + tid;
-    if (col < n) res_pre[0] = d.epi.out[d.col0[mat] + col];
+    if (col < n) res_pre[0] = d.epi.out[(size_t)m * d.epi.ldo + d.col0[mat] + col];
   }
   // Input values of this lane's rows.  Every load of a prologue is issued
   // before the first of them is used (one dependent round trip), and the
@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
   // is live) overlaps them.
   float xv[NR];
   if (kEmb && d.emb_idx) {
-    const uint32_t row = d.emb_idx[0];
+    const uint32_t row = d.emb_idx[(size_t)m * d.emb_idx_stride];
     const uint8_t* prow = d.emb.packed + (size_t)row * (d.emb.n / 2);
     const __half* srow = d.emb.scales + (size_t)row * (d.emb.n / 32);
 #pragma unroll
@@ -267,10 +267,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
     float* sc = ybuf + 128;    // [kAttnInMaxPos] scores, then weights
     const int h = r0 / kHeadDim, hk = h / d.attn_group;
     int sess, pos, kvp;
-    row_pos(d.attn_rp, 0, sess, pos, kvp);
+    row_pos(d.attn_rp, m, sess, pos, kvp);
     const int L = kvp + 1;
     constexpr int kPw = kAttnInMaxPos / (kGemvThreads / 32);  // positions per warp
-    const float4 q = *reinterpret_cast<const float4*>(d.attn_q + h * kHeadDim + 4 * lane);
+    const float4 q = *reinterpret_cast<const float4*>(d.attn_q + (size_t)m * d.attn_ldq + h * kHeadDim + 4 * lane);
     float4 kk[kPw];
 #pragma unroll
     for (int t = 0; t < kPw; ++t) {
@@ -319,18 +319,19 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
       xv[i] = rb < R ? obuf[rb] : 0.0f;
     }
   } else {
+    const float* xr = d.X + (size_t)m * d.ldx;
     float xg[NR];  // GLU: the up half of the row
 #pragma unroll
     for (int i = 0; i < NR; ++i) {
       const int rb = rb0 + 32 * i;
-      xv[i] = rb < R ? d.X[r0 + rb] : 0.0f;
-      xg[i] = (kGlu && d.x_glu && rb < R) ? d.X[d.x_glu + r0 + rb] : 0.0f;
+      xv[i] = rb < R ? xr[r0 + rb] : 0.0f;
+      xg[i] = (kGlu && d.x_glu && rb < R) ? xr[d.x_glu + r0 + rb] : 0.0f;
     }
     // the producer's per-tile sums of squares (at most 16 tiles here)
     const bool ssq16 = kNorm && d.gamma && d.ssq_in && d.ssq_n <= 16;
     float sv[16];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) sv[j] = (ssq16 && j < d.ssq_n) ? d.ssq_in[j] : 0.0f;
+    for (int j = 0; j < 16; ++j) sv[j] = (ssq16 && j < d.ssq_n) ? d.ssq_in[(size_t)m * d.ssq_ld + j] : 0.0f;
     if (clustered) cluster_wait();
     if (EPI == EPI_QKV && qp.on) qkv_pre_rest(qp, d, mat, tcol + tid);
     if (kNorm && d.gamma) {
@@ -341,10 +342,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
         for (int j = 0; j < 16; ++j) ss += sv[j];  // tile order; the zero padding adds nothing
         inv = 1.0f / sqrtf(ss / (float)d.k + 1e-6f);
       } else if (d.ssq_in) {
-        inv = inv_rms_from_ssq(d, 0);
+        inv = inv_rms_from_ssq(d, m);
       } else {
         float ss = 0.0f;
-        for (int i = tid; i < d.k; i += kGemvThreads) ss += d.X[i] * d.X[i];
+        for (int i = tid; i < d.k; i += kGemvThreads) ss += xr[i] * xr[i];
         ss = block_sum_256(ss, sbuf);
         inv = 1.0f / sqrtf(ss / (float)d.k + 1e-6f);
       }
@@ -359,7 +360,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
 #pragma unroll
       for (int i = 0; i < NR; ++i) {
         const int rb = rb0 + 32 * i;
-        if (rb < R) d.xnorm_out[r0 + rb] = xv[i];
+        if (rb < R) d.xnorm_out[(size_t)m * d.ld_xnorm + r0 + rb] = xv[i];
       }
     }
   }
@@ -454,7 +455,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
       v[a][0] = t;
     }
   }
-  gemv_epilogue<1, NM, EPI>(d, fc, v, mat, tile, tcol, 0, 1, 0, sbuf, ybuf, EPI == EPI_RESID ? res_pre : nullptr,
+  gemv_epilogue<1, NM, EPI>(d, fc, v, mat, tile, tcol, m, 1, m, sbuf, ybuf, EPI == EPI_RESID ? res_pre : nullptr,
                             EPI == EPI_QKV ? &qp : nullptr);
 }
 
@@ -660,7 +661,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvDesc d,
 // ---------------------------------------------------------------------------
 static bool use_dec(const GemvDesc& d) {
   const int nrmax = d.staged ? kDecRowsStg : (d.paired ? kDecRowsNM2 : kDecRowsNM1);
-  return d.M == 1 && (d.cluster || d.S == 1) && d.rows_per_split <= 32 * nrmax;
+  return d.M <= kDecMaxM && d.mb == 1 && (d.cluster || d.S == 1) && d.rows_per_split <= 32 * nrmax;
 }
 
 // A staged decode launch reads whole 16-byte chunks: every matrix's columns a
@@ -700,7 +701,7 @@ static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_
 
 template <int NM, int EPI, int NR, bool STG = false>
 static cudaError_t launch_dec(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
-  const dim3 grid(d.ntiles, d.S, 1);
+  const dim3 grid(d.ntiles, d.S, d.M);
   return launch_k(gemv_dec_kernel<NM, EPI, NR, STG>, grid, dim3(kGemvThreads), gemv_smem_bytes(d), st, opts(d), d,
                   fc);
 }

@@ -141,7 +141,8 @@ struct GemvDesc {
   // attention prologue (M = 1, short KV): the input rows [r0, r0 + 128) of a
   // K slice are the attention output of query head r0 / 128 over the cache
   int attn_in = 0;
-  const float* attn_q = nullptr;  // rotated queries [heads * 128]
+  const float* attn_q = nullptr;  // rotated queries [M][heads * 128], row stride attn_ldq
+  long attn_ldq = 0;
   KvDesc attn_kv;
   RowPos attn_rp;
   int attn_group = 1;             // query heads per KV head
@@ -170,6 +171,7 @@ constexpr int kAttnInMaxPos = 32;  // cache positions the attention prologue han
 // M = 1 decode kernel: weight rows a lane keeps in registers (32 rows per
 // step of the 8 warps x 4 row offsets), per matrix count
 constexpr int kDecRowsNM1 = 12;  // rows per split <= 384
+constexpr int kDecMaxM = 2;      // decode kernel: input rows per launch (one per grid.z)
 constexpr int kDecRowsNM2 = 6;   // rows per split <= 192
 constexpr int kDecRowsStg = 24;  // staged (weights in shared memory): rows per split <= 768
 constexpr int kDecStgMaxSmem = 227 * 1024;  // dynamic shared memory of a staged decode CTA
