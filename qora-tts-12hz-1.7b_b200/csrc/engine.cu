@@ -376,11 +376,39 @@ static void try_staged(int sm_count, GemvDesc& g) {
   }
 }
 
+// Decode rows whose register-resident K slices fit the decode kernel only
+// with more clusters than one wave holds (the talker's gate/up pair): keep
+// about two CTAs per SM and reduce the slices through global memory (the
+// last CTA of a tile to arrive sums them) instead of a cluster, which frees
+// the CTAs from cluster placement.  QTTS_GLOBAL_SPLIT=0 turns it off.
+static void try_global_split(Session& s, GemvDesc& g) {
+  static const bool on = [] {
+    const char* v = getenv("QTTS_GLOBAL_SPLIT");
+    return !(v && v[0] == '0');
+  }();
+  if (!on || g.M > kDecMaxM || g.tc || gemv_uses_decode_kernel(g)) return;
+  GemvDesc t = g;
+  choose_split(s.m->sm_count, t);
+  t.cluster = 0;
+  const int nrmax = t.paired ? kDecRowsNM2 : kDecRowsNM1;
+  while (t.rows_per_split > 32 * nrmax && t.S < kMaxClusterSplits) {
+    const int S = t.S + 1;
+    t.rows_per_split = ceil_div(ceil_div(t.k, S), 32) * 32;
+    t.S = ceil_div(t.k, t.rows_per_split);
+  }
+  t.part = s.part;
+  if (!gemv_uses_decode_kernel(t) || (size_t)t.S * t.M * t.ncols > s.part_floats ||
+      (size_t)t.ntiles * t.M > s.n_counters)
+    return;
+  g = t;
+}
+
 static int plan_gemv(Session& s, GemvDesc& g) {
   choose_split(s.m->sm_count, g);
   g.cluster = 1;  // split-K partials reduced over distributed shared memory
   g.pdl = 1;
   fit_split_to_wave(g);
+  try_global_split(s, g);
   try_staged(s.m->sm_count, g);
   g.err_flag = s.err_flag;
   if (g.M >= kTcMinRows && tc_enabled()) {
@@ -397,7 +425,8 @@ static int plan_gemv(Session& s, GemvDesc& g) {
   }();
   if (log_plans)
     fprintf(stderr, "qtts plan: epi %d k %d ncols %d M %d -> %s S %d rows/split %d\n", g.epi_kind, g.k, g.ncols, g.M,
-            g.tc ? "tcgen05" : (g.staged ? "cuda-core staged" : "cuda-core"), g.tc ? tc_splits(g) : g.S,
+            g.tc ? "tcgen05" : (g.staged ? "cuda-core staged" : (g.cluster ? "cuda-core" : "cuda-core global-split")),
+            g.tc ? tc_splits(g) : g.S,
             g.tc ? g.tc_ks * kTcK : g.rows_per_split);
   const size_t zb = (size_t)ceil_div(g.M, g.mb);
   if ((size_t)g.ntiles * zb > s.n_counters || zb > 4096) return fail(QTTS_ERR_OOM, "tile counter array too small");

@@ -229,8 +229,11 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
     const int rb = rb0 + 32 * i;
     gv[i] = (norm_in && rb < R) ? h2f(d.gamma[r0 + rb]) : 0.0f;
   }
+  // The CTA that runs the epilogue: the cluster's root, or (global split-K,
+  // the last CTA of a tile to arrive) any of them, so all gather its inputs.
+  const bool may_epi = !clustered || split == 0;
   QkvPre qp;  // QKV root CTA: what its epilogue reads, gathered in the prologue
-  if (EPI == EPI_QKV && (!clustered || split == 0)) {
+  if (EPI == EPI_QKV && may_epi) {
     qp.on = true;
     qkv_pre_weights(qp, d, mat, tcol + tid);
   }
@@ -240,7 +243,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
   // the residual this CTA's epilogue will add (root CTA, EPI_RESID): loaded
   // now, alongside the inputs, instead of after the reduction
   float res_pre[1] = {0.0f};
-  if (EPI == EPI_RESID && (!clustered || split == 0)) {
+  if (EPI == EPI_RESID && may_epi) {
     const int col = tcol + tid;
     if (col < n) res_pre[0] = d.epi.out[(size_t)m * d.epi.ldo + d.col0[mat] + col];
   }
@@ -455,6 +458,37 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
       v[a][0] = t;
     }
   }
+  else if (d.S > 1) {
+    // Global split-K (no cluster): each slice writes its partials, the last
+    // CTA of the tile to arrive sums all slices in split order
+    // (deterministic) and runs the epilogue.
+    const bool cv = tcol + tid < n;
+#pragma unroll
+    for (int a = 0; a < NM; ++a)
+      if (cv) d.part[((size_t)split * d.M + m) * d.ncols + d.col0[NM == 2 ? a : mat] + tcol + tid] = v[a][0];
+    __threadfence();
+    __syncthreads();
+    unsigned* ctr = d.counters + (size_t)tile * gridDim.z + m;
+    if (tid == 0) *reinterpret_cast<volatile unsigned*>(sbuf) = atomicAdd(ctr, 1u);
+    __syncthreads();
+    if (*reinterpret_cast<volatile unsigned*>(sbuf) != (unsigned)(d.S - 1)) return;
+    __syncthreads();  // every thread has read the ticket before sbuf is reused
+    __threadfence();
+#pragma unroll
+    for (int a = 0; a < NM; ++a) {
+      float pv[kMaxClusterSplits];
+      const size_t c = (size_t)d.col0[NM == 2 ? a : mat] + tcol + tid;
+#pragma unroll
+      for (int sp = 0; sp < kMaxClusterSplits; ++sp)
+        pv[sp] = (sp < d.S && cv) ? __ldcg(d.part + ((size_t)sp * d.M + m) * d.ncols + c) : 0.0f;
+      float t = 0.0f;
+#pragma unroll
+      for (int sp = 0; sp < kMaxClusterSplits; ++sp)
+        if (sp < d.S) t += pv[sp];
+      v[a][0] = t;
+    }
+    if (tid == 0) *ctr = 0u;  // ready for the next launch
+  }
   gemv_epilogue<1, NM, EPI>(d, fc, v, mat, tile, tcol, m, 1, m, sbuf, ybuf, EPI == EPI_RESID ? res_pre : nullptr,
                             EPI == EPI_QKV ? &qp : nullptr);
 }
@@ -661,7 +695,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvDesc d,
 // ---------------------------------------------------------------------------
 static bool use_dec(const GemvDesc& d) {
   const int nrmax = d.staged ? kDecRowsStg : (d.paired ? kDecRowsNM2 : kDecRowsNM1);
-  return d.M <= kDecMaxM && d.mb == 1 && (d.cluster || d.S == 1) && d.rows_per_split <= 32 * nrmax;
+  return d.M <= kDecMaxM && d.mb == 1 && d.S <= kMaxClusterSplits && d.rows_per_split <= 32 * nrmax;
 }
 
 // A staged decode launch reads whole 16-byte chunks: every matrix's columns a

@@ -1,7 +1,8 @@
 """The opt-in staged decode GEMV (QTTS_STAGED=1: the CTA's weight slice in
 shared memory, gemv.cu gemv_dec_kernel<..., STG = true>) on the 1.7B config-1
-fixture.  The talker's gate/up pair is the projection it takes over; the
-planner log must show it, and the teacher-forced codes and logits must match
+fixture.  With the global split-K plan off (QTTS_GLOBAL_SPLIT=0) the
+talker's gate/up pair is the projection it takes over; the planner log must
+show it, and the teacher-forced codes and logits must match
 the oracle as on the default path.  The environment switch is read once per
 process, so the run is a child process."""
 import os
@@ -34,7 +35,7 @@ print("staged decode parity ok")
 
 
 def test_staged_decode_gemv_1p7b_config1():
-    env = dict(os.environ, QTTS_STAGED="1", QTTS_PLAN_LOG="1")
+    env = dict(os.environ, QTTS_STAGED="1", QTTS_GLOBAL_SPLIT="0", QTTS_PLAN_LOG="1")
     r = subprocess.run([sys.executable, "-c", CHILD.format(tests=HERE)], env=env, capture_output=True, text=True,
                        timeout=900, cwd=os.path.dirname(HERE))
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
