@@ -382,16 +382,22 @@ static void try_staged(int sm_count, GemvDesc& g) {
 // last CTA of a tile to arrive sums them) instead of a cluster, which frees
 // the CTAs from cluster placement.  QTTS_GLOBAL_SPLIT=0 turns it off.
 static void try_global_split(Session& s, GemvDesc& g) {
-  static const bool on = [] {
+  static const int mode = [] {  // 0 off, 1 in place of the general kernel, 2 also when it adds CTAs
     const char* v = getenv("QTTS_GLOBAL_SPLIT");
-    return !(v && v[0] == '0');
+    return v ? atoi(v) : 1;
   }();
-  if (!on || g.M > kDecMaxM || g.tc || gemv_uses_decode_kernel(g)) return;
+  if (mode == 0 || g.M > kDecMaxM || g.tc) return;
+  if (mode == 1 && gemv_uses_decode_kernel(g)) return;
   GemvDesc t = g;
   choose_split(s.m->sm_count, t);
   t.cluster = 0;
+  if (mode == 2) {  // about two CTAs per SM, beyond the cluster limit
+    const int S = std::max(1, std::min(kMaxGlobalSplits, (int)std::lround(2.0 * s.m->sm_count / (t.ntiles * t.M))));
+    t.rows_per_split = ceil_div(ceil_div(t.k, S), 32) * 32;
+    t.S = ceil_div(t.k, t.rows_per_split);
+  }
   const int nrmax = t.paired ? kDecRowsNM2 : kDecRowsNM1;
-  while (t.rows_per_split > 32 * nrmax && t.S < kMaxClusterSplits) {
+  while (t.rows_per_split > 32 * nrmax && t.S < kMaxGlobalSplits) {
     const int S = t.S + 1;
     t.rows_per_split = ceil_div(ceil_div(t.k, S), 32) * 32;
     t.S = ceil_div(t.k, t.rows_per_split);
@@ -400,6 +406,7 @@ static void try_global_split(Session& s, GemvDesc& g) {
   if (!gemv_uses_decode_kernel(t) || (size_t)t.S * t.M * t.ncols > s.part_floats ||
       (size_t)t.ntiles * t.M > s.n_counters)
     return;
+  if (gemv_uses_decode_kernel(g) && (long)t.ntiles * t.S <= (long)g.ntiles * g.S) return;
   g = t;
 }
 

@@ -476,15 +476,17 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
     __threadfence();
 #pragma unroll
     for (int a = 0; a < NM; ++a) {
-      float pv[kMaxClusterSplits];
       const size_t c = (size_t)d.col0[NM == 2 ? a : mat] + tcol + tid;
-#pragma unroll
-      for (int sp = 0; sp < kMaxClusterSplits; ++sp)
-        pv[sp] = (sp < d.S && cv) ? __ldcg(d.part + ((size_t)sp * d.M + m) * d.ncols + c) : 0.0f;
       float t = 0.0f;
+      for (int sp0 = 0; sp0 < d.S; sp0 += 16) {  // 16 slices' loads in flight, added in split order
+        float pv[16];
 #pragma unroll
-      for (int sp = 0; sp < kMaxClusterSplits; ++sp)
-        if (sp < d.S) t += pv[sp];
+        for (int j = 0; j < 16; ++j)
+          pv[j] = (sp0 + j < d.S && cv) ? __ldcg(d.part + ((size_t)(sp0 + j) * d.M + m) * d.ncols + c) : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (sp0 + j < d.S) t += pv[j];
+      }
       v[a][0] = t;
     }
     if (tid == 0) *ctr = 0u;  // ready for the next launch
@@ -695,7 +697,8 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvDesc d,
 // ---------------------------------------------------------------------------
 static bool use_dec(const GemvDesc& d) {
   const int nrmax = d.staged ? kDecRowsStg : (d.paired ? kDecRowsNM2 : kDecRowsNM1);
-  return d.M <= kDecMaxM && d.mb == 1 && d.S <= kMaxClusterSplits && d.rows_per_split <= 32 * nrmax;
+  return d.M <= kDecMaxM && d.mb == 1 && d.S <= (d.cluster ? kMaxClusterSplits : kMaxGlobalSplits) &&
+         d.rows_per_split <= 32 * nrmax;
 }
 
 // A staged decode launch reads whole 16-byte chunks: every matrix's columns a

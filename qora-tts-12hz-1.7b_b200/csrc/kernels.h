@@ -167,6 +167,7 @@ constexpr int kErrWaitExpired = 4;   // a bounded device wait ran out
 constexpr int kErrFp16Input = 8;     // a tensor-core input outside the fp16 range
 constexpr int kErrGridBarrier = 16;  // a persistent kernel's grid barrier gave up
 constexpr int kMaxClusterSplits = 16;
+constexpr int kMaxGlobalSplits = 64;  // decode kernel, split-K reduced through global memory
 constexpr int kAttnInMaxPos = 32;  // cache positions the attention prologue handles
 // M = 1 decode kernel: weight rows a lane keeps in registers (32 rows per
 // step of the 8 warps x 4 row offsets), per matrix count
