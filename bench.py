@@ -306,6 +306,8 @@ def main():
     ap.add_argument("--workload", default="config1", choices=["config1", "config2", "config3", "config4"])
     ap.add_argument("--only", default="", help="config2: one case, KxNxM")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--full-prompt", action="store_true",
+                    help="prefill the whole text (ragged KV lengths across utterances; config4)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank, world, local = dist_setup(args)
@@ -352,8 +354,9 @@ def main():
         wl = "config4: 1.7B Q4, 64 utterances per GPU, T=0.8 top-k 50, prompts 16-256 tokens"
     B = len(utts)
     F = args.warmup + args.steps + 1
-    sess = Q.Session(model, B, 10 + F + 1)
-    gen = Q.Generation(sess, utts, F)
+    max_text = max(len(u["text"]) for u in utts)
+    sess = Q.Session(model, B, 10 + (max_text if args.full_prompt else 0) + F + 1)
+    gen = Q.Generation(sess, utts, F, full_prompt=args.full_prompt)
     stream = torch.cuda.ExternalStream(sess.stream)
     gen.frames(args.warmup)
     torch.cuda.synchronize()
@@ -389,7 +392,7 @@ def main():
     torch.cuda.synchronize()
     barrier(world)
     t0 = time.perf_counter()
-    codes_e2e, fr_e2e, _, _ = Q.generate(sess, utts, args.steps)
+    codes_e2e, fr_e2e, _, _ = Q.generate(sess, utts, args.steps, full_prompt=args.full_prompt)
     t_e2e = max_over_ranks(time.perf_counter() - t0)
     h2d = sum(int(np.asarray(x["text"]).nbytes) + (2048 * 4 if x.get("voice") is not None else 0) for x in utts)
     d2h = B * args.steps * 16 * 4 + B * 4
@@ -410,6 +413,8 @@ def main():
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": wl, "global_batch": world * B, "frames_timed": args.steps,
                    "kv_len_start": 10 + args.warmup, "l2": "inputs larger than L2 (860 MB weights per frame)",
+                   "prompt": ("full prefill: KV lengths 9 + prompt tokens (ragged)" if args.full_prompt
+                              else "generate_new: 10-row prefill, text trailing into the frames"),
                    "parallelism": f"{world} independent replicas (utterance sharding, no collective)"},
         "ms_per_frame_batch1": ms_per_step if B == 1 else None,
         "frame_roofline": {"bytes_per_frame": frame_bytes, "achieved_gbs": frame_gbs, "peak_gbs": peak,

@@ -70,6 +70,12 @@ typedef struct {
 
 /* qtts_generate flags */
 #define QTTS_IGNORE_EOS 1u /* run all max_frames (benchmarks with random weights) */
+/* Benchmark mode of this library (not a reference mode): after the
+ * generate_new.rs:94-173 prefill rows, text tokens 1..n_text-1 are prefilled
+ * as embed_text(tok) + embed_codec(CODEC_PAD) rows, so utterances with
+ * different prompt lengths decode over KV caches of different lengths; the
+ * frames' trailing text is then TTS_EOS followed by TTS_PAD. */
+#define QTTS_FULL_PROMPT 2u
 
 QTTS_API const char* qtts_last_error(void);
 QTTS_API int qtts_version(void);

@@ -282,7 +282,7 @@ class Model:
         return seq, hid, lg
 
     def generate(self, text, params: Params, seed: int, speaker_id=0, language_id=2050, voice=None,
-                 ignore_eos=True, forced=None, dump_logits=False, dump_hidden=False):
+                 ignore_eos=True, forced=None, dump_logits=False, dump_hidden=False, full_prompt=False):
         text = np.ascontiguousarray(text, np.uint32)
         F = params.max_codes
         codes = np.zeros((F, 16), np.uint32)
@@ -292,7 +292,8 @@ class Model:
         v = None if voice is None else np.ascontiguousarray(voice, np.float32)
         n = lib().oq_generate(self.h, _p(text, C.c_uint32), text.size, speaker_id, language_id,
                               fptr(v) if v is not None else None, C.byref(params), seed,
-                              1 if ignore_eos else 0, _p(fc, C.c_uint32) if fc is not None else None,
+                              (1 if ignore_eos else 0) | (2 if full_prompt else 0),
+                              _p(fc, C.c_uint32) if fc is not None else None,
                               _p(codes, C.c_uint32), fptr(lg) if lg is not None else None,
                               fptr(hd) if hd is not None else None)
         if n < 0:

@@ -1098,12 +1098,17 @@ uint32_t oq_sample_token(const float* logits, size_t n, const oq_params* p, cons
   return out;
 }
 
-/* generate_new.rs:84-188 prefill_custom_voice */
-int oq_prefill_custom_voice(const oq_model* m, const uint32_t* text, int n_text, uint32_t speaker_id,
-                            uint32_t language_id, const float* voice, oq_kv* kv, float* last_hidden,
-                            float* logits) {
+/* generate_new.rs:84-188 prefill_custom_voice.  full_prompt (a benchmark
+ * mode of this build, not of the reference): the remaining text tokens
+ * 1..n_text-1 follow as prefill rows embed_text(tok) + embed_codec(CODEC_PAD),
+ * so prompts of different lengths leave caches of different lengths; the
+ * frame loop's trailing text then holds TTS_EOS only. */
+static int prefill_rows(const oq_model* m, const uint32_t* text, int n_text, uint32_t speaker_id,
+                        uint32_t language_id, const float* voice, int full_prompt, oq_kv* kv,
+                        float* last_hidden, float* logits) {
   const int H = m->d.t_hidden;
-  float* x = (float*)calloc((size_t)10 * H, sizeof(float));
+  const int extra = (full_prompt && n_text > 1) ? n_text - 1 : 0;
+  float* x = (float*)calloc((size_t)(10 + extra) * H, sizeof(float));
   float* a = (float*)malloc(sizeof(float) * H);
   float* b = (float*)malloc(sizeof(float) * H);
   int seq = 0;
@@ -1153,18 +1158,34 @@ int oq_prefill_custom_voice(const oq_model* m, const uint32_t* text, int n_text,
     }
     free(pad); free(bos);
   }
+  if (extra) {
+    oq_embed_codec_token(m, CODEC_PAD, a);
+    for (int i = 1; i < n_text; i++) {
+      oq_embed_text_token(m, text[i], b);
+      float* o = x + (size_t)(seq++) * H;
+      for (int j = 0; j < H; j++) o[j] = b[j] + a[j];
+    }
+  }
   int rc = oq_prefill_talker_raw(m, x, seq, kv, last_hidden);
   if (rc == 0) oq_apply_codec_head(m, last_hidden, logits);
   free(x); free(a); free(b);
   return rc ? rc : seq;
 }
 
+int oq_prefill_custom_voice(const oq_model* m, const uint32_t* text, int n_text, uint32_t speaker_id,
+                            uint32_t language_id, const float* voice, oq_kv* kv, float* last_hidden,
+                            float* logits) {
+  return prefill_rows(m, text, n_text, speaker_id, language_id, voice, 0, kv, last_hidden, logits);
+}
+
 /* generate_new.rs:191-300 generate_speech (frame loop; audio decode out of
- * scope) with teacher forcing and dumps for parity work. */
+ * scope) with teacher forcing and dumps for parity work.  flags: bit 0
+ * ignore EOS (benchmarks), bit 1 full_prompt (see prefill_rows). */
 int oq_generate(const oq_model* m, const uint32_t* text, int n_text, uint32_t speaker_id,
                 uint32_t language_id, const float* voice, const oq_params* p, uint64_t seed,
-                int ignore_eos, const uint32_t* forced, uint32_t* codes_out, float* logits_dump,
+                int flags, const uint32_t* forced, uint32_t* codes_out, float* logits_dump,
                 float* hidden_dump) {
+  const int ignore_eos = flags & 1, full_prompt = (flags >> 1) & 1;
   const int H = m->d.t_hidden, V = m->d.t_vocab, G = m->n_lm;
   oq_kv* tkv = oq_talker_kv_new(m);
   oq_kv* pkv = oq_predictor_kv_new(m);
@@ -1173,13 +1194,13 @@ int oq_generate(const oq_model* m, const uint32_t* text, int n_text, uint32_t sp
   float* logits = (float*)malloc(sizeof(float) * V);
   float* sem = (float*)malloc(sizeof(float) * H);
   float* acs = (float*)malloc(sizeof(float) * H);
-  int rc = oq_prefill_custom_voice(m, text, n_text, speaker_id, language_id, voice, tkv, hidden, logits);
+  int rc = prefill_rows(m, text, n_text, speaker_id, language_id, voice, full_prompt, tkv, hidden, logits);
   int frames = 0;
   if (rc < 0) goto done;
-  int position = n_text == 0 ? 9 : 10;                            /* :216 */
-  int n_trail = (n_text > 1 ? n_text - 1 : 0) + 1;                /* :314-326 */
+  int position = rc;                                              /* :216 (9 or 10 rows) */
+  int n_trail = (!full_prompt && n_text > 1 ? n_text - 1 : 0) + 1; /* :314-326 */
   float* trail = (float*)malloc(sizeof(float) * (size_t)n_trail * H);
-  for (int i = 1; i < n_text; i++) oq_embed_text_token(m, text[i], trail + (size_t)(i - 1) * H);
+  for (int i = 1; i < n_trail; i++) oq_embed_text_token(m, text[i], trail + (size_t)(i - 1) * H);
   oq_embed_text_token(m, TTS_EOS, trail + (size_t)(n_trail - 1) * H);
   float* tts_pad = (float*)malloc(sizeof(float) * H);
   oq_embed_text_token(m, TTS_PAD, tts_pad);

@@ -126,10 +126,14 @@ int oq_prefill_custom_voice(const oq_model* m, const uint32_t* text, int n_text,
  *            next step; the oracle's own choices still land in codes_out)
  *   logits_dump nullable [max_codes*V]: logits sampled at each frame
  *   hidden_dump nullable [max_codes*H]: talker hidden fed to the predictor
- * Returns the number of frames produced (EOS stops unless ignore_eos). */
+ *   flags    bit 0: ignore EOS (benchmarks with random weights); bit 1:
+ *            full prompt (a benchmark mode of this build: text tokens
+ *            1..n-1 prefilled as embed_text + embed_codec(CODEC_PAD) rows,
+ *            trailing text = TTS_EOS, then TTS_PAD)
+ * Returns the number of frames produced (EOS stops unless ignored). */
 int oq_generate(const oq_model* m, const uint32_t* text, int n_text,
                 uint32_t speaker_id, uint32_t language_id, const float* voice_emb,
-                const oq_params* p, uint64_t seed, int ignore_eos,
+                const oq_params* p, uint64_t seed, int flags,
                 const uint32_t* forced, uint32_t* codes_out, float* logits_dump,
                 float* hidden_dump);
 

@@ -948,12 +948,45 @@ static int build_frame_ops(Session& s, std::vector<Op>& ops, bool dumps) {
   return QTTS_OK;
 }
 
+// Grow the row-sized session buffers (prefill rows: activations, queries,
+// attention output, FFN hidden, sums of squares, attention counters, staging)
+// to `rows`.  Only between generations: no captured graph refers to them.
+static int ensure_rows(Session& s, int rows) {
+  if (rows <= s.rows) return QTTS_OK;
+  const qtts_dims& d = s.m->d;
+  const int qmax = std::max(d.t_heads, d.p_heads) * kHeadDim;
+  const int imax = std::max(d.t_inter, d.p_inter);
+  float** bufs[] = {&s.q, &s.attn, &s.h, &s.xpre, &s.io, &s.ssq_t};
+  for (float** b : bufs) {
+    cudaFree(*b);
+    *b = nullptr;
+  }
+  cudaFree(s.acounters);
+  s.acounters = nullptr;
+  s.rows = rows;
+  RC(dalloc(&s.q, (size_t)rows * qmax));
+  RC(dalloc(&s.attn, (size_t)rows * qmax));
+  RC(dalloc(&s.h, (size_t)rows * imax));
+  s.h_floats = (size_t)rows * imax;
+  RC(dalloc(&s.xpre, (size_t)rows * d.t_hidden));
+  s.io_floats = (size_t)rows * d.t_hidden + 2 * d.t_hidden + d.t_vocab + 64;
+  RC(dalloc(&s.io, s.io_floats));
+  RC(dalloc(&s.ssq_t, (size_t)rows * kSsqLd));
+  s.n_acounters = (size_t)rows * std::max(d.t_kv_heads, d.p_kv_heads);
+  RC(dalloc(&s.acounters, s.n_acounters));
+  return QTTS_OK;
+}
+
 static int generate_begin(Session& s, int n, const qtts_utterance* u, int F, unsigned flags, const uint32_t* forced,
                           bool dump_logits, bool dump_hidden) {
   const Model& m = *s.m;
   const qtts_dims& d = m.d;
   if (n <= 0 || n > s.maxB || !u || F <= 0) return fail(QTTS_ERR_BADARG, "bad generate arguments");
-  if (10 + F > s.maxP) return fail(QTTS_ERR_RANGE, "prefill + max_frames exceeds the session's max_positions");
+  const bool full_prompt = (flags & QTTS_FULL_PROMPT) != 0;
+  int max_prefill = 10;
+  for (int b = 0; b < n; ++b)
+    if (full_prompt && u[b].n_text > 1) max_prefill = std::max(max_prefill, 9 + u[b].n_text);
+  if (max_prefill + F > s.maxP) return fail(QTTS_ERR_RANGE, "prefill + max_frames exceeds the session's max_positions");
   CK(cudaSetDevice(m.device));
   CK(cudaStreamSynchronize(s.st));
   free_generation(s);
@@ -975,8 +1008,13 @@ static int generate_begin(Session& s, int n, const qtts_utterance* u, int F, uns
       if ((int)q.text[i] >= d.t_text_vocab) return fail(QTTS_ERR_BADARG, "text token outside the text vocabulary");
       tok.push_back(q.text[i]);
     }
-    max_trail = std::max(max_trail, std::max(q.n_text - 1, 0) + 1);
+    max_trail = std::max(max_trail, (full_prompt ? 0 : std::max(q.n_text - 1, 0)) + 1);
     if (q.voice) ++n_voice;
+  }
+  if (full_prompt) {  // all prefill rows live in xpre at once
+    int rows = 0;
+    for (int b = 0; b < n; ++b) rows += u[b].n_text > 0 ? 9 + u[b].n_text : 9;
+    RC(ensure_rows(s, rows));
   }
   s.B = n;
   s.max_frames = F;
@@ -989,7 +1027,7 @@ static int generate_begin(Session& s, int n, const qtts_utterance* u, int F, uns
   RC(dalloc(&s.tp, (size_t)Nt * H, &T));
   RC(dalloc(&s.tp_h1, (size_t)Nt * m.fc1.n, &T));
   RC(dalloc(&s.tp_tok, (size_t)Nt, &T));
-  RC(dalloc(&s.recipes, (size_t)n * 10, &T));
+  RC(dalloc(&s.recipes, (size_t)n * max_prefill, &T));
   RC(dalloc(&s.trail, (size_t)n * max_trail * H, &T));
   RC(dalloc(&s.trail_idx, (size_t)n * max_trail, &T));
   RC(dalloc(&s.voices, (size_t)std::max(n_voice, 1) * H, &T));
@@ -998,7 +1036,7 @@ static int generate_begin(Session& s, int n, const qtts_utterance* u, int F, uns
   if (forced) CK(cudaMemcpy(s.forced, forced, sizeof(uint32_t) * n * F * kMaxGroups, cudaMemcpyHostToDevice));
   CK(cudaMemcpy(s.tp_tok, tok.data(), sizeof(uint32_t) * Nt, cudaMemcpyHostToDevice));
   // prefill recipes (generate_new.rs:94-173) and trailing text rows (:314-326)
-  std::vector<RowRecipe> rec((size_t)n * 10, RowRecipe{-1, -1, -1, 0});
+  std::vector<RowRecipe> rec((size_t)n * max_prefill, RowRecipe{-1, -1, -1, 0});
   std::vector<int> seq(n), row0(n), trail_idx((size_t)n * max_trail, 5);
   std::vector<SlotState> slots(n);
   int vi = 0, nrows = 0;
@@ -1019,10 +1057,12 @@ static int generate_begin(Session& s, int n, const qtts_utterance* u, int F, uns
     }
     r[t++] = {(int)CODEC_PAD, 4, -1, 0};  // PAD + TTS_BOS
     if (q.n_text > 0) r[t++] = {(int)CODEC_BOS, text_row[b], -1, 0};
+    if (full_prompt)  // the rest of the text as prefill rows (QTTS_FULL_PROMPT)
+      for (int i = 1; i < q.n_text; ++i) r[t++] = {(int)CODEC_PAD, text_row[b] + i, -1, 0};
     seq[b] = t;
     nrows += t;
-    const int ntr = std::max(q.n_text - 1, 0) + 1;
-    for (int i = 1; i < q.n_text; ++i) trail_idx[(size_t)b * max_trail + i - 1] = text_row[b] + i;
+    const int ntr = (full_prompt ? 0 : std::max(q.n_text - 1, 0)) + 1;
+    for (int i = 1; i < ntr; ++i) trail_idx[(size_t)b * max_trail + i - 1] = text_row[b] + i;
     trail_idx[(size_t)b * max_trail + ntr - 1] = 5;  // TTS_EOS
     SlotState& sl = slots[b];
     memset(&sl, 0, sizeof(sl));

@@ -23,6 +23,7 @@ OK = 0
 ERR_BADARG, ERR_OOM, ERR_CUDA, ERR_TIMEOUT, ERR_FORMAT, ERR_IO, ERR_STATE, ERR_NODEV, ERR_RANGE = (
     -1, -2, -3, -4, -5, -6, -7, -8, -9)
 IGNORE_EOS = 1
+FULL_PROMPT = 2  # benchmark mode: the whole text prefilled (qtts.h QTTS_FULL_PROMPT)
 
 
 class QttsError(RuntimeError):
@@ -293,13 +294,19 @@ class _Utts:
         self.n = len(utterances)
 
 
+def _flags(ignore_eos: bool, full_prompt: bool) -> int:
+    return (IGNORE_EOS if ignore_eos else 0) | (FULL_PROMPT if full_prompt else 0)
+
+
 def generate(sess: Session, utterances, max_frames: int, ignore_eos: bool = True, forced=None,
-             dump_logits: bool = False, dump_hidden: bool = False):
+             dump_logits: bool = False, dump_hidden: bool = False, full_prompt: bool = False):
     """The generate_new.rs:191-300 frame loop for a batch of utterances.
 
     Each utterance is a dict(text=token ids, voice=None|[H], speaker_id,
-    language_id, seed, params=SampleParams).  Returns (codes [n][F][16],
-    frames [n], logits [n][F][V] | None, hidden [n][F][H] | None)."""
+    language_id, seed, params=SampleParams).  full_prompt: the benchmark mode
+    that prefills the whole text (ragged KV lengths; qtts.h QTTS_FULL_PROMPT).
+    Returns (codes [n][F][16], frames [n], logits [n][F][V] | None,
+    hidden [n][F][H] | None)."""
     u = _Utts(utterances)
     n = u.n
     codes = np.zeros((n, max_frames, 16), np.uint32)
@@ -307,7 +314,7 @@ def generate(sess: Session, utterances, max_frames: int, ignore_eos: bool = True
     lg = np.zeros((n, max_frames, sess.V), np.float32) if dump_logits else None
     hd = np.zeros((n, max_frames, sess.H), np.float32) if dump_hidden else None
     fc = None if forced is None else np.ascontiguousarray(forced, np.uint32).reshape(n, max_frames, 16)
-    _check(lib.qtts_generate(sess.h, n, u.arr, max_frames, IGNORE_EOS if ignore_eos else 0,
+    _check(lib.qtts_generate(sess.h, n, u.arr, max_frames, _flags(ignore_eos, full_prompt),
                              _u32p(fc) if fc is not None else None, _u32p(codes),
                              frames.ctypes.data_as(C.POINTER(C.c_int)),
                              _fp(lg) if lg is not None else None, _fp(hd) if hd is not None else None))
@@ -318,13 +325,14 @@ class Generation:
     """generate() split for timing: begin (prefill + graph capture), frames
     (asynchronous graph replays on the session stream), end (sync + copy)."""
 
-    def __init__(self, sess: Session, utterances, max_frames: int, ignore_eos: bool = True, forced=None):
+    def __init__(self, sess: Session, utterances, max_frames: int, ignore_eos: bool = True, forced=None,
+                 full_prompt: bool = False):
         self.sess = sess
         self.u = _Utts(utterances)
         self.max_frames = max_frames
         self.forced = None if forced is None else np.ascontiguousarray(forced, np.uint32)
         _check(lib.qtts_generate_begin(sess.h, self.u.n, self.u.arr, max_frames,
-                                       IGNORE_EOS if ignore_eos else 0,
+                                       _flags(ignore_eos, full_prompt),
                                        _u32p(self.forced) if self.forced is not None else None))
 
     def frames(self, n: int):

@@ -236,3 +236,42 @@ def test_1p7b_config1_batched_tensor_core(qtts, gpu_1p7b):
     for i in range(n):
         assert frames[i] == F
         _check_forced(codes[i], g, lg[i], max_ties=1)
+
+
+def _oracle_run(oracle_mod, om, utt, frames, full_prompt):
+    """The oracle's own run of one utterance, shaped like a golden fixture."""
+    p = oracle_mod.make_params(frames, float(utt["params"].temperature), int(utt["params"].top_k),
+                               float(utt["params"].repetition_penalty))
+    n, codes, lg, _ = om.generate(utt["text"], p, utt["seed"], speaker_id=utt.get("speaker_id", 0),
+                                  language_id=utt.get("language_id", 2050), voice=utt.get("voice"),
+                                  ignore_eos=True, dump_logits=True, full_prompt=full_prompt)
+    idx = np.argsort(-lg, axis=-1, kind="stable")[..., :5].astype(np.int32)
+    return dict(codes=codes, frames=np.int32(n), top_idx=idx, top_val=np.take_along_axis(lg, idx, axis=-1),
+                absmax=np.abs(lg).max(axis=1).astype(np.float32), logits=lg,
+                logit_frames=np.arange(frames, dtype=np.int32))
+
+
+def test_full_prompt_ragged_batch_tiny(qtts, gpu_tiny, tiny_oracle, oracle_mod):
+    # QTTS_FULL_PROMPT: the whole text is prefilled, so prompts of 1, 6 and 19
+    # tokens leave caches of 9, 15 and 28 positions; the batch decodes over
+    # the ragged (paged) caches and every utterance must follow its own
+    # oracle run, teacher-forced with the oracle's codes
+    from qtts_b200 import make_params
+    from qtts_b200 import workload as W
+    H = gpu_tiny.dims.t_hidden
+    utts = [dict(text=W.tokens(31, 6), voice=None, speaker_id=3001, language_id=2055, seed=5,
+                 params=make_params(0.9, 20, 1.05)),
+            dict(text=W.tokens(32, 19), voice=W.voice_embedding(33, H), seed=6, params=make_params(1.0, 1, 1.05)),
+            dict(text=W.tokens(34, 1), voice=None, speaker_id=3002, seed=7, params=make_params(0.8, 50, 1.05))]
+    F = 10
+    ref = [_oracle_run(oracle_mod, tiny_oracle, u, F, True) for u in utts]
+    s = qtts.Session(gpu_tiny, len(utts), 40 + F)
+    forced = np.stack([r["codes"] for r in ref]).astype(np.uint32)
+    codes, frames, lg, _ = qtts.generate(s, utts, F, forced=forced, dump_logits=True, full_prompt=True)
+    s.close()
+    for i, r in enumerate(ref):
+        assert frames[i] == F
+        _check_forced(codes[i], r, lg[i])
+    # the mode changes the trajectory: the default mode's first logits differ
+    plain = _oracle_run(oracle_mod, tiny_oracle, utts[1], 1, False)
+    assert rel_err(plain["logits"][0], ref[1]["logits"][0]) > 1e-3

@@ -230,3 +230,16 @@ def test_golden_meta_present():
     meta = np.load(os.path.join(GOLDEN, "meta.npz"))
     assert int(meta["threads"]) == 8
     assert len(str(meta["tiny_sha256"])) == 64
+
+
+def test_oracle_full_prompt_mode(oracle_mod, tiny_path):
+    # the benchmark mode that prefills the whole text: runs, and its first
+    # logits differ from the generate_new mode's (the text lands in the cache)
+    m = oracle_mod.Model(tiny_path)
+    text = np.arange(7, dtype=np.uint32) * 1013 + 55
+    p = oracle_mod.make_params(3, 1.0, 1, 1.05)
+    n0, c0, l0, _ = m.generate(text, p, 1, dump_logits=True)
+    n1, c1, l1, _ = m.generate(text, p, 1, dump_logits=True, full_prompt=True)
+    m.close()
+    assert n0 == n1 == 3
+    assert np.abs(l0[0] - l1[0]).max() > 0
