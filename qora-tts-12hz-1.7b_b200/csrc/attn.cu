@@ -33,11 +33,33 @@ __device__ __forceinline__ const float* kv_row_c(const KvDesc& kv, int sess, int
 template <int G>
 __global__ void __launch_bounds__(128) attn_kernel(const AttnDesc d) {
   pdl_launch_dependents();
-  pdl_wait();
   constexpr int NW = 4;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int m = blockIdx.x / d.kv_heads, h = blockIdx.x % d.kv_heads;
   const int split = blockIdx.y;
+  if (tid == 0 && d.l2_prefetch) {
+    // Before the wait: pull this CTA's K / V rows into L2 (one bulk prefetch
+    // per page and K / V).  A hint only: the position is read through L2 and
+    // may be a step old, and rows the q/k/v step is writing are refetched by
+    // the loads after the wait; every address stays inside the pool.
+    const RowPos& rp = d.rp;
+    const int sl = m / rp.rows_per_sess, r = m - sl * rp.rows_per_sess;
+    const int ss = rp.sess0 + sl;
+    const int ps = (rp.pos_base ? __ldcg(rp.pos_base + ss * rp.pos_stride) : rp.pos_const) + r;
+    const int kv = rp.kv_const >= 0 ? rp.kv_const + r : ps;
+    if (kv >= 0 && kv < d.kv.pages_per_sess * kPageSize) {
+      const int Lp = kv + 1, ch = (Lp + d.nsplit - 1) / d.nsplit;
+      const int q0 = split * ch, q1 = min(Lp, q0 + ch);
+      for (int pg = q0 / kPageSize; pg * kPageSize < q1; ++pg) {
+        const int a = max(q0, pg * kPageSize), b = min(q1, (pg + 1) * kPageSize);
+        for (int which = 0; which < 2; ++which)
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(kv_row_c(d.kv, ss, a, which, h)),
+                       "r"((uint32_t)((b - a) * kHeadDim * sizeof(float)))
+                       : "memory");
+      }
+    }
+  }
+  pdl_wait();
   int sess, pos, kvp;
   row_pos(d.rp, m, sess, pos, kvp);
   const int L = kvp + 1;  // cache entries [0, kvp] (talker.rs:301-302)

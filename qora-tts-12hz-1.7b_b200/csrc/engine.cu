@@ -544,6 +544,11 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
     AttnDesc a;
     a.q = s.q; a.ldq = qd; a.out = s.attn; a.ldo = qd; a.kv = io.kv; a.rp = io.rp;
     a.heads = io.heads; a.kv_heads = io.kvh; a.M = io.M; a.nsplit = io.nsplit;
+    static const bool kv_pf = [] {  // QTTS_ATTN_PREFETCH=0: no K / V L2 prefetch (measurements)
+      const char* v = getenv("QTTS_ATTN_PREFETCH");
+      return !(v && v[0] == '0');
+    }();
+    a.l2_prefetch = kv_pf ? 1 : 0;
     if (a.nsplit > 1) {
       const size_t need = (size_t)io.M * io.kvh * a.nsplit * (io.heads / io.kvh) * kAttnRec;
       if (need > s.apart_floats || (size_t)io.M * io.kvh > s.n_acounters)

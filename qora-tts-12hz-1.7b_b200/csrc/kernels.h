@@ -319,6 +319,7 @@ struct AttnDesc {
   int nsplit = 1;
   float* part = nullptr;        // [M][kv_heads][nsplit][G][kAttnRec]
   unsigned* counters = nullptr; // [M][kv_heads]
+  int l2_prefetch = 1;          // pull the CTA's K / V rows into L2 before the dependent-launch wait
 };
 cudaError_t launch_attention(const AttnDesc& d, cudaStream_t st);
 
