@@ -429,22 +429,26 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       }
     }
   };
-  // B (warps 0-6): task = (k row brow, 32-column quarter bq of the tile), from the raw ring
-  auto store_b = [&](uint8_t* bhi, uint8_t* blo, int slot, int a, int brow, int bq) {
+
+
+  // one 32-bit word of the raw stage (row brow, 8-column group g8 of the tile)
+  // as 8 hi + 8 lo fp16 values in the operand layout; consecutive words are
+  // consecutive rows of one group, so a warp's stores fill 512 contiguous bytes
+  auto store_word = [&](uint8_t* stb, int slot, int w) {
+    const int a = w / 1024, g8 = (w >> 6) & 15, brow = w & 63;
     const uint8_t* base = tsm + C::PIPE_BYTES + slot * C::RAW_STAGE + a * kRawMat;
-    const uint4 w = *reinterpret_cast<const uint4*>(base + brow * kRawRow + bq * 16);
-    const unsigned short s = *reinterpret_cast<const unsigned short*>(base + TK * kRawRow + brow * 8 + bq * 2);
-    const __half2 s2 = __half2half2(__ushort_as_half(s));
-    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {  // 8-column group bq * 4 + q
-      uint4 hi, lo;
-      dequant_word(words[q], s2, hi, lo);
-      const int off = (bq * 4 + q) * 1024 + (brow >> 3) * 128 + (brow & 7) * 16;
-      *reinterpret_cast<uint4*>(bhi + off) = hi;
-      *reinterpret_cast<uint4*>(blo + off) = lo;
-    }
+    const uint32_t word = *reinterpret_cast<const uint32_t*>(base + brow * kRawRow + (g8 >> 2) * 16 + (g8 & 3) * 4);
+    const unsigned short sc = *reinterpret_cast<const unsigned short*>(base + TK * kRawRow + brow * 8 + (g8 >> 2) * 2);
+    uint4 hi, lo;
+    dequant_word(word, __half2half2(__ushort_as_half(sc)), hi, lo);
+    const int off = g8 * 1024 + (brow >> 3) * 128 + (brow & 7) * 16;
+    *reinterpret_cast<uint4*>(stb + a * B_BYTES + off) = hi;
+    *reinterpret_cast<uint4*>(stb + (NM + a) * B_BYTES + off) = lo;
   };
+  // Weight words per stage: the B warps take kWordsB each (strided by their
+  // count), the input-row warps the rest after their rows, which balances the
+  // two (an input-row thread's rows take about as long as 3-4 words).
+  constexpr int kWords = NM * 1024, kWordsB = NM == 1 ? 4 : 6;
 
   bool ok = true;
   if (tid < kConv) {
@@ -467,11 +471,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       cp_async_commit();
       if (a_thr) {
         store_a(ks0 + i, ac, st, st + A_BYTES);
+        for (int w = kBConv * kWordsB + (tid - kBConv); w < kWords; w += kConv - kBConv)
+          store_word(st + 2 * A_BYTES, i % C::RS, w);
       } else if (tid < kBConv) {
-        for (int tk = tid; tk < NM * 256; tk += kBConv) {
-          const int a = tk >> 8, brow = tk & 63, bq = (tk >> 6) & 3;
-          store_b(st + 2 * A_BYTES + a * B_BYTES, st + 2 * A_BYTES + (NM + a) * B_BYTES, i % C::RS, a, brow, bq);
-        }
+#pragma unroll
+        for (int k = 0; k < kWordsB; ++k) store_word(st + 2 * A_BYTES, i % C::RS, tid + k * kBConv);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // st.shared -> visible to tcgen05.mma
       mbar_arrive(&full[b]);
