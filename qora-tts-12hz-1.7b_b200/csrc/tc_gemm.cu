@@ -15,14 +15,16 @@
 //     streaming into a shared-memory ring by cp.async 3-5 stages ahead;
 //   * warps 0-6 dequantise it and warps 7-14 normalise the input rows (held
 //     in registers one stage ahead), into
-//     shared memory: A = the normalised input rows, B = the Q4 weights, each as
+//     shared memory: X = the normalised input rows, W = the Q4 weights, each as
 //     two fp16 operands hi + lo with lo = fp16((v - hi) * 2^11).  The Q4 value
 //     (q-8)*scale has at most 14 significant bits, so hi + lo holds it
 //     exactly; an f32 input keeps ~22 bits.  Carrying lo scaled by 2^11 keeps
 //     it clear of the fp16 subnormal range.
 //   * the converters arrive on the stage's "full" mbarrier; warp 15 waits on
-//     it and issues the tcgen05.mma (kind::f16, f32 accumulators in TMEM):
-//     D_main += A_hi*B_hi, D_cross += A_hi*B_lo + A_lo*B_hi, committing them
+//     it and issues the tcgen05.mma (kind::f16, f32 accumulators in TMEM)
+//     with the weights as operand A (M = the tile's 128 columns) and the
+//     input rows as operand B (N = the CTA's rows rounded up to 16):
+//     D_main += W_hi*X_hi, D_cross += W_lo*X_hi + W_hi*X_lo, committing them
 //     to the stage's "done" mbarrier, while the converters (synchronised
 //     among themselves by a named barrier) already convert the next stage.
 // Result = D_main + 2^-11 * D_cross (the dropped lo*lo term is ~2^-22).
@@ -35,9 +37,9 @@
 // append (a head is one 128-column tile), or the greedy argmax.
 //
 // Shared-memory operand layout (no swizzle, 16-byte core-matrix rows):
-//   A (K-major):  row r, k-chunk c (8 elements) at (r/8)*1024 + c*128 + (r%8)*16
+//   X (K-major):  row r, k-chunk c (8 elements) at (r/8)*1024 + c*128 + (r%8)*16
 //                 -> LBO 128 B (next 8-deep K chunk), SBO 1024 B (next 8 rows)
-//   B (MN-major): k row j, column group g (8 columns) at g*1024 + (j/8)*128 + (j%8)*16
+//   W (MN-major): k row j, column group g (8 columns) at g*1024 + (j/8)*128 + (j%8)*16
 //                 -> LBO 128 B (next 8-deep K group), SBO 1024 B (next 8 columns)
 // A 16-deep MMA step advances both start addresses by 256 B.
 //
@@ -175,16 +177,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
 __device__ __forceinline__ uint64_t sdesc(uint32_t saddr) {
   return ((saddr >> 4) & 0x3FFFu) | ((uint64_t)(128u >> 4) << 16) | ((uint64_t)(1024u >> 4) << 32) | (1ull << 46);
 }
-// Instruction descriptor, kind::f16: D f32, A fp16 K-major, B fp16 MN-major, M = 128, N = 128.
-constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | (1u << 16) |
-                            ((uint32_t)(TN >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
+// Instruction descriptor, kind::f16: D f32, A = the weights (fp16, MN-major:
+// the 128 columns of the tile are the MMA's M), B = the input rows (fp16,
+// K-major: N = the CTA's rows rounded up to 16), so a block of 64 rows costs
+// half the tensor-pipe cycles of a 128-row tile.
+__device__ __forceinline__ uint32_t idesc_rows(int nrows) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | (1u << 15) | (0u << 16) | ((uint32_t)(nrows >> 3) << 17) |
+         ((uint32_t)(TN >> 4) << 24);
+}
 
-__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate));
+      "l"(a), "l"(b), "r"(idesc), "r"(accumulate));
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
@@ -329,9 +336,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     *s_flag = 0u;
   }
-  // rows >= Mv of every A buffer stay zero for the whole kernel
-  if (Mv < TM) {
-    const int zrows = TM - Mv;
+  // rows [Mv, Nr) of every input-row buffer stay zero for the whole kernel
+  // (the MMAs read Nr rows; rows past Nr are never read)
+  const int Nr = (Mv + 15) & ~15;
+  const uint32_t idesc = idesc_rows(Nr);
+  if (Mv < Nr) {
+    const int zrows = Nr - Mv;
     for (int i = tid; i < C::STAGES * 2 * zrows * (TK / 8); i += kThreads) {
       // rows fastest: 8 consecutive threads fill 8 different 16-byte bank groups
       const int r = Mv + i % zrows, c = (i / zrows) % (TK / 8), h = i / (zrows * (TK / 8));  // h: stage*2 + half
@@ -488,17 +498,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       if (!__all_sync(0xffffffffu, f_ok)) { ok = false; break; }
       if (lane == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t ahi = tsm_a + b * C::STAGE_BYTES, alo = ahi + A_BYTES;
+        const uint32_t xhi = tsm_a + b * C::STAGE_BYTES, xlo = xhi + A_BYTES;  // input rows (MMA operand B)
 #pragma unroll
         for (int a = 0; a < NM; ++a) {
-          const uint32_t bhi = ahi + 2 * A_BYTES + a * B_BYTES, blo = ahi + 2 * A_BYTES + (NM + a) * B_BYTES;
+          // weights (MMA operand A)
+          const uint32_t whi = xhi + 2 * A_BYTES + a * B_BYTES, wlo = xhi + 2 * A_BYTES + (NM + a) * B_BYTES;
           const uint32_t dm = tmem + (uint32_t)(a * 2 * TN), dc = dm + TN;
 #pragma unroll
           for (int kk = 0; kk < TK / 16; ++kk) {
             const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-            umma(dm, sdesc(ahi + kk * 256), sdesc(bhi + kk * 256), acc);
-            umma(dc, sdesc(ahi + kk * 256), sdesc(blo + kk * 256), acc);
-            umma(dc, sdesc(alo + kk * 256), sdesc(bhi + kk * 256), 1u);
+            umma(dm, sdesc(whi + kk * 256), sdesc(xhi + kk * 256), idesc, acc);
+            umma(dc, sdesc(wlo + kk * 256), sdesc(xhi + kk * 256), idesc, acc);
+            umma(dc, sdesc(whi + kk * 256), sdesc(xlo + kk * 256), idesc, 1u);
           }
         }
         umma_commit(&mma_done[b]);
@@ -518,26 +529,23 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   __syncthreads();
   const bool good = (*s_flag & kErrTimeout) == 0;
 
-  // ---- accumulators -> shared staging (warp: lane quarter w % 4, 32-column block w / 4)
+  // ---- accumulators -> shared staging.  TMEM lane = column of the tile,
+  // TMEM column = input row.  Warp: lane quarter w % 4 (columns), 32-row block
+  // w / 4; a store instruction writes 32 consecutive columns of one row.
   {
-    const int lq = warp & 3, cb = warp >> 2;
-    if (good && lq * 32 < Mv) {
-      const int r = lq * 32 + lane;
+    const int lq = warp & 3, rb = warp >> 2;
+    if (good && rb * 32 < Mv) {
+      const int c = lq * 32 + lane;
 #pragma unroll
       for (int a = 0; a < NM; ++a) {
-        {
-          const int col = cb * 32;
-          float vm[32], vc[32];
-          const uint32_t ta = tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(a * 2 * TN + col);
-          tmem_ld32(ta, vm);
-          tmem_ld32(ta + TN, vc);
-          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-          float4* dst = reinterpret_cast<float4*>(red + ((size_t)a * TM + r) * kRedLd + col);
+        float vm[32], vc[32];
+        const uint32_t ta = tmem + ((uint32_t)(lq * 32) << 16) + (uint32_t)(a * 2 * TN + rb * 32);
+        tmem_ld32(ta, vm);
+        tmem_ld32(ta + TN, vc);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        float* dst = red + ((size_t)a * TM + rb * 32) * kRedLd + c;
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            dst[q] = make_float4(vm[4 * q] + vc[4 * q] * kLoUnscale, vm[4 * q + 1] + vc[4 * q + 1] * kLoUnscale,
-                                 vm[4 * q + 2] + vc[4 * q + 2] * kLoUnscale, vm[4 * q + 3] + vc[4 * q + 3] * kLoUnscale);
-        }
+        for (int j = 0; j < 32; ++j) dst[(size_t)j * kRedLd] = vm[j] + vc[j] * kLoUnscale;
       }
     }
   }
