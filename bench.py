@@ -247,8 +247,8 @@ def gemv_roofline(Q, torch, peak, peak_kind):
 def tc_roofline(Q, torch, peaks):
     """The dominant kernel of the batched frame: the tcgen05 projection at the
     talker gate shape k=2048, n=6144 with 64 rows.  Useful FLOPs 2*m*k*n; the
-    tensor pipe executes 3 fp16 MMAs per product (hi/lo split) on 128-row
-    tiles, reported as executed_tflops."""
+    tensor pipe executes 3 fp16 MMAs per product (hi/lo split) with the rows
+    padded to a multiple of 16, reported as executed_tflops."""
     k, n, m = 2048, 6144, 64
     dt = time_q4_launches(Q, torch, k, n, m)
     fl = 2.0 * m * k * n
@@ -257,7 +257,7 @@ def tc_roofline(Q, torch, peaks):
     return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
             "traffic": None, "kernel": "tc_proj_kernel (tcgen05 Q4 projection) k=2048 n=6144 m=64",
             "us_per_launch": dt * 1e6, "algorithmic_flops": fl,
-            "executed_tflops": 3 * (128 / m) * ach, "weight_gbs": q4_bytes(k, n) / dt / 1e9,
+            "executed_tflops": 3 * (((m + 15) // 16 * 16) / m) * ach, "weight_gbs": q4_bytes(k, n) / dt / 1e9,
             "peak_kind": "bf16_tflops_sustained (measured)" if "bf16_tflops_sustained" in peaks else "fallback"}
 
 
@@ -267,6 +267,36 @@ CONFIG2_SHAPES = [("q_proj", 2048, 4096), ("k_proj", 2048, 1024), ("v_proj", 204
                   ("gate/up_proj", 2048, 6144), ("down_proj", 6144, 2048), ("input_proj", 2048, 1024),
                   ("group_head", 1024, 2048)]
 CONFIG2_BATCHES = [1, 8, 64, 256]
+
+
+def time_quantize(Q, torch, k, n, copies=4, reps=40):
+    """Device time of one quantize_f32_to_q4 launch (gemv.rs:92-130): one
+    CUDA graph of back-to-back launches rotating over f32 sources larger
+    than L2 together (no host launch cost in the timed region)."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    src = [torch.randn(k * n, device="cuda", generator=g) * 0.02 for _ in range(copies)]
+    packed = torch.empty(k * n // 2, dtype=torch.uint8, device="cuda")
+    scales = torch.empty(k * n // 32, dtype=torch.int16, device="cuda")
+    s = torch.cuda.Stream()
+    sp = s.cuda_stream
+    with torch.cuda.stream(s):
+        for i in range(3):
+            Q.q4_quantize_dev(src[i % copies].data_ptr(), k, n, packed.data_ptr(), scales.data_ptr(), sp)
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=s, capture_error_mode="thread_local"):
+        for i in range(reps):
+            Q.q4_quantize_dev(src[i % copies].data_ptr(), k, n, packed.data_ptr(), scales.data_ptr(), sp)
+    gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        e0.record(s)
+        for _ in range(3):
+            gr.replay()
+        e1.record(s)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / 1e3 / (3 * reps)
 
 
 def run_config2(args, Q, torch, peak, peak_kind):
@@ -283,6 +313,12 @@ def run_config2(args, Q, torch, peak, peak_kind):
             rows.append({"shape": name, "k": k, "n": n, "m": m, "us_per_launch": dt * 1e6,
                          "gbs": alg / dt / 1e9, "useful_tflops": 2.0 * m * k * n / dt / 1e12,
                          "kernel": "tc_proj_kernel" if m >= 16 else "gemv (CUDA cores)"})
+    if not args.only or args.only == "quantize":
+        # the converter's quantize_f32_to_q4 on the GPU: reads 4 B, writes 0.5625 B per value
+        k, n = 2048, 6144
+        dt = time_quantize(Q, torch, k, n)
+        rows.append({"shape": "quantize_f32_to_q4", "k": k, "n": n, "m": None, "us_per_launch": dt * 1e6,
+                     "gbs": (4.0 + 0.5625) * k * n / dt / 1e9, "kernel": "q4_quantize_kernel"})
     head = [r for r in rows if r["k"] == 2048 and r["n"] == 6144 and r["m"] == 1] or rows[:1]
     gbs = head[0]["gbs"] if head else None
     line = {"metric": "Q4 GEMV HBM GB/s", "value": gbs, "unit": "GB/s", "n_gpus": 1, "steps": 3 * 200,

@@ -184,6 +184,15 @@ QTTS_API int qtts_f16_gemv_dev(const uint16_t* w_dev, int k, int n, const float*
 /* gemv.rs:378-400 dequant of the whole matrix: out[k][n] = f32(scale)*(q-8). */
 QTTS_API int qtts_q4_dequant_dev(const uint8_t* packed_dev, const uint16_t* scales_dev, int k, int n,
                         float* out_dev, void* stream);
+/* gemv.rs:92-130 quantize_f32_to_q4 on device pointers: data[k][n] f32 ->
+ * packed[k*n/2] (low nibble = even column) + scales[k*n/32] f16, the on-disk
+ * layout, bit-identical to the reference (scale = f16(absmax/7), q =
+ * clamp(round(v/scale), -8, 7) + 8, NaN -> 0).  n % 32 == 0; data 16-byte
+ * aligned, packed and scales 2-byte aligned. */
+QTTS_API int qtts_q4_quantize_dev(const float* data_dev, int k, int n, uint8_t* packed_dev, uint16_t* scales_dev,
+                                  void* stream);
+/* Same with host buffers (copies in, runs, copies out). */
+QTTS_API int qtts_q4_quantize(const float* data, int k, int n, uint8_t* packed, uint16_t* scales);
 
 #ifdef __cplusplus
 }

@@ -224,7 +224,9 @@ void oq_quantize_q4(const float* data, size_t k, size_t n, uint8_t* packed, uint
         float r0 = roundf(v0 * inv), r1 = roundf(v1 * inv); /* Rust round: half away from 0 */
         r0 = r0 < -8.0f ? -8.0f : (r0 > 7.0f ? 7.0f : r0);
         r1 = r1 < -8.0f ? -8.0f : (r1 > 7.0f ? 7.0f : r1);
-        uint8_t q0 = (uint8_t)(r0 + 8.0f), q1 = (uint8_t)(r1 + 8.0f);
+        /* f32::clamp keeps NaN and Rust's `as u8` maps NaN to 0 (saturating
+         * cast); a C cast of NaN is undefined, so spell it out */
+        uint8_t q0 = r0 != r0 ? 0 : (uint8_t)(r0 + 8.0f), q1 = r1 != r1 ? 0 : (uint8_t)(r1 + 8.0f);
         packed[gi * 16 + j / 2] = (uint8_t)(q0 | (q1 << 4));
       }
     }

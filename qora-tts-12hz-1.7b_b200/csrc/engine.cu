@@ -1557,5 +1557,30 @@ int qtts_q4_dequant_dev(const uint8_t* packed, const uint16_t* scales, int k, in
   const cudaError_t e = launch_dequant(q, out, (cudaStream_t)stream);
   return e == cudaSuccess ? QTTS_OK : fail(QTTS_ERR_CUDA, cudaGetErrorString(e));
 }
+int qtts_q4_quantize_dev(const float* data, int k, int n, uint8_t* packed, uint16_t* scales, void* stream) {
+  if (!data || !packed || !scales || k <= 0 || n <= 0 || n % 32) return fail(QTTS_ERR_BADARG, "bad quantize arguments");
+  if ((reinterpret_cast<uintptr_t>(data) & 15u) || (reinterpret_cast<uintptr_t>(packed) & 1u) ||
+      (reinterpret_cast<uintptr_t>(scales) & 1u))
+    return fail(QTTS_ERR_BADARG, "quantize: data must be 16-byte aligned, packed and scales 2-byte aligned");
+  const cudaError_t e = launch_q4_quantize(data, (size_t)k, (size_t)n, packed, scales, (cudaStream_t)stream);
+  return e == cudaSuccess ? QTTS_OK : fail(QTTS_ERR_CUDA, cudaGetErrorString(e));
+}
+int qtts_q4_quantize(const float* data, int k, int n, uint8_t* packed, uint16_t* scales) {
+  if (!data || !packed || !scales || k <= 0 || n <= 0 || n % 32) return fail(QTTS_ERR_BADARG, "bad quantize arguments");
+  const size_t db = sizeof(float) * (size_t)k * n, pb = (size_t)k * n / 2, sb = (size_t)k * n / 32 * 2;
+  const size_t a = (db + 255) & ~(size_t)255, b = (pb + 255) & ~(size_t)255;
+  char* buf = nullptr;
+  if (cudaMalloc(&buf, a + b + sb) != cudaSuccess) return fail(QTTS_ERR_OOM, "device allocation failed");
+  int rc = QTTS_OK;
+  if (cudaMemcpy(buf, data, db, cudaMemcpyHostToDevice) != cudaSuccess) rc = fail(QTTS_ERR_CUDA, "copy to device failed");
+  if (rc == QTTS_OK)
+    rc = qtts_q4_quantize_dev(reinterpret_cast<float*>(buf), k, n, reinterpret_cast<uint8_t*>(buf + a),
+                              reinterpret_cast<uint16_t*>(buf + a + b), nullptr);
+  if (rc == QTTS_OK && (cudaMemcpy(packed, buf + a, pb, cudaMemcpyDeviceToHost) != cudaSuccess ||
+                        cudaMemcpy(scales, buf + a + b, sb, cudaMemcpyDeviceToHost) != cudaSuccess))
+    rc = fail(QTTS_ERR_CUDA, "copy from device failed");
+  cudaFree(buf);
+  return rc;
+}
 
 }  // extern "C"

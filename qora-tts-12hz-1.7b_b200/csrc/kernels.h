@@ -374,6 +374,9 @@ cudaError_t launch_add_rows(const float* a, long lda, const float* b, long ldb, 
                             int rows, int n, cudaStream_t st);
 cudaError_t launch_frame_end(SlotState* slots, int B, cudaStream_t st);
 cudaError_t launch_dequant(const Q4Mat& m, float* out, cudaStream_t st);
+// f32 [k][n] -> Q4 g32 (gemv.rs:92-130), bit-identical to the reference.
+cudaError_t launch_q4_quantize(const float* data, size_t k, size_t n, uint8_t* packed, uint16_t* scales,
+                               cudaStream_t st);
 cudaError_t launch_f16_gemv(const __half* w, int k, int n, const float* x, int m, float* y,
                             cudaStream_t st);
 

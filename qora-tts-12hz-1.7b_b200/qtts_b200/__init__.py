@@ -99,6 +99,8 @@ def _load():
         "qtts_f16_gemv_dev": (C.c_int, [P, C.c_int, C.c_int, P, C.c_int, P, P]),
         "qtts_q4_dequant_dev": (C.c_int, [P, P, C.c_int, C.c_int, P, P]),
         "qtts_expf_dev": (C.c_int, [P, P, C.c_int, P]),
+        "qtts_q4_quantize_dev": (C.c_int, [P, C.c_int, C.c_int, P, P, P]),
+        "qtts_q4_quantize": (C.c_int, [fp, C.c_int, C.c_int, C.POINTER(C.c_uint8), C.POINTER(C.c_uint16)]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -372,6 +374,22 @@ def f16_gemv_dev(w_ptr, k, n, x_ptr, m, y_ptr, stream=0):
 
 def q4_dequant_dev(packed_ptr, scales_ptr, k, n, out_ptr, stream=0):
     _check(lib.qtts_q4_dequant_dev(packed_ptr, scales_ptr, k, n, out_ptr, stream or None))
+
+
+def quantize_f32_to_q4(data: np.ndarray, k: int, n: int) -> tuple[np.ndarray, np.ndarray]:
+    """gemv.rs:92-130 on the GPU: f32 [k][n] -> (packed u8 [k*n/2], scales f16 bits u16 [k*n/32])."""
+    d = np.ascontiguousarray(data, np.float32).reshape(-1)
+    if d.size != k * n:
+        raise QttsError(ERR_BADARG, f"data has {d.size} values, expected {k}*{n}")
+    packed = np.empty(k * n // 2, np.uint8)
+    scales = np.empty(k * n // 32, np.uint16)
+    _check(lib.qtts_q4_quantize(_fp(d), k, n, packed.ctypes.data_as(C.POINTER(C.c_uint8)),
+                                scales.ctypes.data_as(C.POINTER(C.c_uint16))))
+    return packed, scales
+
+
+def q4_quantize_dev(data_ptr, k, n, packed_ptr, scales_ptr, stream=0):
+    _check(lib.qtts_q4_quantize_dev(data_ptr, k, n, packed_ptr, scales_ptr, stream or None))
 
 
 def expf_dev(x_ptr, y_ptr, n, stream=0):

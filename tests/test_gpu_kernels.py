@@ -7,7 +7,7 @@ import ctypes
 import numpy as np
 import pytest
 
-from conftest import golden, has_gpu
+from conftest import golden, has_gpu, quantize_edge_data
 
 pytestmark = pytest.mark.gpu
 if has_gpu():
@@ -47,6 +47,53 @@ def test_dequant_bit_exact(qtts):
         qtts.q4_dequant_dev(dp.data_ptr(), ds.data_ptr(), k, n, out.data_ptr())
         torch.cuda.synchronize()
         assert np.array_equal(out.cpu().numpy().reshape(k, n), dequant_np(packed, scales, k, n))
+
+
+@pytest.mark.parametrize("k,n", [(8, 96), (3, 96), (1, 32), (64, 2048), (2048, 6144)])
+def test_quantize_bit_exact(qtts, oracle_mod, k, n):
+    # gemv.rs:92-130 on the GPU against the oracle: packed nibbles and f16
+    # scales bit-identical, special cases included (NaN, inf, ties, subnormals)
+    rng = np.random.default_rng(k * n)
+    if k * n >= 8 * 96:
+        data = quantize_edge_data(rng, k, n)
+    else:
+        data = (rng.standard_normal((k, n)) * 0.02).astype(np.float32)
+        data.reshape(-1)[20] = np.nan
+        data.reshape(-1)[:16] = np.array([0.5, -2.5, 7.0, 3.5] * 4, np.float32) * (1.0 if k > 1 else 1e-3)
+    ref_p, ref_s = oracle_mod.quantize_q4(data, k, n)
+    dd = torch.from_numpy(data).cuda()
+    dp = torch.full((k * n // 2,), 0xAB, dtype=torch.uint8, device="cuda")
+    ds = torch.full((k * n // 32,), 0x5A5A, dtype=torch.int16, device="cuda")
+    qtts.q4_quantize_dev(dd.data_ptr(), k, n, dp.data_ptr(), ds.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(ds.cpu().numpy().view(np.uint16), ref_s)
+    assert np.array_equal(dp.cpu().numpy(), ref_p)
+    hp, hs = qtts.quantize_f32_to_q4(data, k, n)  # host-buffer entry point
+    assert np.array_equal(hp, ref_p) and np.array_equal(hs, ref_s)
+
+
+def test_quantize_round_trip_and_errors(qtts):
+    # dequantised weights quantise back to themselves when every group's
+    # absmax is 7 * scale (q = 1 or 15 present) and the scale is a power of two
+    rng = np.random.default_rng(7)
+    k, n = 128, 256
+    q = rng.integers(1, 16, (k, n)).astype(np.int32)  # q = 0 (value -8s) would raise the absmax
+    q[:, ::32] = 15  # absmax = 7 * scale in every group
+    s = np.exp2(rng.integers(-12, -4, (k, n // 32))).astype(np.float32)
+    w = (np.repeat(s, 32, axis=1) * (q - 8)).astype(np.float32)
+    packed, scales = qtts.quantize_f32_to_q4(w, k, n)
+    assert np.array_equal(scales.view(np.float16).astype(np.float32).reshape(k, n // 32), s)
+    back = np.empty((k, n), np.int32)
+    back[:, 0::2] = packed.reshape(k, n // 2) & 0xF
+    back[:, 1::2] = packed.reshape(k, n // 2) >> 4
+    assert np.array_equal(back, q)
+    with pytest.raises(qtts.QttsError):
+        qtts.quantize_f32_to_q4(np.zeros((2, 48), np.float32), 2, 48)  # n % 32 != 0
+    dd = torch.zeros(2 * 64 + 4, dtype=torch.float32, device="cuda")
+    dp = torch.zeros(64, dtype=torch.uint8, device="cuda")
+    ds = torch.zeros(4, dtype=torch.int16, device="cuda")
+    with pytest.raises(qtts.QttsError):  # misaligned source: rejected on the host
+        qtts.q4_quantize_dev(dd.data_ptr() + 4, 2, 64, dp.data_ptr(), ds.data_ptr())
 
 
 SHAPES = [  # (k=in, n=out): BASELINE config 2 and the real model shapes

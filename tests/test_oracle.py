@@ -11,7 +11,7 @@ import os
 import numpy as np
 import pytest
 
-from conftest import GOLDEN, golden
+from conftest import GOLDEN, golden, quantize_edge_data, quantize_np
 
 LIBM = ctypes.CDLL("libm.so.6")
 LIBM.expf.restype = ctypes.c_float
@@ -58,6 +58,23 @@ def test_quantize_layout_and_nibble_order(oracle_mod):
     assert packed[32] == (8 | (15 << 4))
     deq = np.stack([oracle_mod.embed_q4(packed, scales, n, r) for r in range(k)])
     assert np.max(np.abs(deq - data)) <= 0.5 * 0.5 / 7 * 7 + 1e-6
+
+
+@pytest.mark.parametrize("k,n", [(8, 96), (64, 2048)])
+def test_quantize_matches_numpy_restatement(oracle_mod, k, n):
+    # pins the oracle's quantize_f32_to_q4 on the special cases (NaN, inf,
+    # ties, subnormals, f16 overflow) against an independent restatement
+    data = quantize_edge_data(np.random.default_rng(k), k, n)
+    packed, scales = oracle_mod.quantize_q4(data, k, n)
+    ref_p, ref_s = quantize_np(data)
+    assert np.array_equal(scales, ref_s)
+    assert np.array_equal(packed, ref_p)
+    g = packed[:16 * 4].reshape(4, 16)
+    # group 1 (absmax 7, scale 1): 0.5 -> 1+8, -0.5 -> -1+8, 2.5 -> 3+8 (half away from zero)
+    assert (g[1, 0] & 0xF, g[1, 0] >> 4) == (9, 7)
+    assert (g[1, 2] & 0xF, g[1, 2] >> 4) == (11, 5)
+    assert np.all(g[0] == 0x88) and scales[0] == 0          # all-zero group
+    assert np.all(g[3] == 0) and scales[3] == 0              # all-NaN group: NaN as u8 = 0
 
 
 def dequant_np(packed, scales, k, n):
