@@ -349,31 +349,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       *reinterpret_cast<uint4*>(base + (r >> 3) * 1024 + c * 128 + (r & 7) * 16) = make_uint4(0, 0, 0, 0);
     }
   }
-  pdl_wait();  // activations, norms' sums of squares and KV of earlier kernels are ready
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(C::TMEM_COLS));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-  }
-  // 1 / rms of each row (gemv.rs:408-417)
-  if (d.gamma) {
-    if (d.ssq_in) {
-      for (int r = tid; r < Mv; r += kThreads) s_inv[r] = inv_rms_from_ssq(d, m0 + r);
-    } else {
-      for (int r = warp; r < Mv; r += kThreads / 32) {
-        const float* xr = d.X + (size_t)(m0 + r) * d.ldx;
-        float ss = 0.0f;
-        for (int i = lane; i < d.k; i += 32) ss += xr[i] * xr[i];
-        ss = warp_sum(ss);
-        if (lane == 0) s_inv[r] = 1.0f / sqrtf(ss / (float)d.k + 1e-6f);
-      }
-    }
-  }
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-  __syncthreads();
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-  const uint32_t tmem = *tmem_slot;
-
   // ---- input rows of a stage (warps 7-14): registers one stage ahead ->
   // shared memory (split).  Thread: row (at & 63) + 64 p, 16-deep k slice at / 64.
   const bool a_thr = tid >= kBConv && tid < kConv;
@@ -404,6 +379,35 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       }
     }
   };
+  pdl_wait();  // activations, norms' sums of squares and KV of earlier kernels are ready
+  // the first stage's input rows are issued now, so their round trip overlaps
+  // the TMEM allocation and the 1/rms loads below
+  ARegs an;
+  if (a_thr) load_a(ks0, an);
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(C::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  // 1 / rms of each row (gemv.rs:408-417)
+  if (d.gamma) {
+    if (d.ssq_in) {
+      for (int r = tid; r < Mv; r += kThreads) s_inv[r] = inv_rms_from_ssq(d, m0 + r);
+    } else {
+      for (int r = warp; r < Mv; r += kThreads / 32) {
+        const float* xr = d.X + (size_t)(m0 + r) * d.ldx;
+        float ss = 0.0f;
+        for (int i = lane; i < d.k; i += 32) ss += xr[i] * xr[i];
+        ss = warp_sum(ss);
+        if (lane == 0) s_inv[r] = 1.0f / sqrtf(ss / (float)d.k + 1e-6f);
+      }
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
   float amax = 0.0f;
   auto store_a = [&](int ks, const ARegs& R, uint8_t* ahi, uint8_t* alo) {
     const int kk0 = ks * TK + akc * 16;
@@ -462,9 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
 
   bool ok = true;
   if (tid < kConv) {
-    // ---- converters
-    ARegs an;
-    if (a_thr) load_a(ks0, an);
+    // ---- converters (the input-row threads hold stage 0's rows in `an`)
     for (int i = 0; i < nst; ++i) {
       const int b = i % C::STAGES;
       uint8_t* st = tsm + b * C::STAGE_BYTES;
@@ -566,11 +568,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   const int cc = lane * 4;    // this lane's 4 columns within the tile
   const int col = tcol + cc;  // column within the matrix
   const bool cval = col < n;  // n % 32 == 0: all 4 valid or none
+  // Pass 1: the sums go into this CTA's own staging rows [rb, re), which no
+  // peer reads (each reads only the rows of its own slice).
   for (int r = rb + warp; good && r < re; r += kThreads / 32) {
-    float4 acc[NM];
 #pragma unroll
     for (int a = 0; a < NM; ++a) {
-      const uint32_t la = smem_u32(red + ((size_t)a * TM + r) * kRedLd + cc);
+      float* row = red + ((size_t)a * TM + r) * kRedLd + cc;
+      const uint32_t la = smem_u32(row);
       float4 part[kMaxSplits];
 #pragma unroll
       for (int p = 0; p < kMaxSplits; ++p)  // all loads in flight before the ordered sum
@@ -581,8 +585,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
         if (p < S) {
           t4.x += part[p].x; t4.y += part[p].y; t4.z += part[p].z; t4.w += part[p].w;
         }
-      acc[a] = t4;
+      *reinterpret_cast<float4*>(row) = t4;
     }
+  }
+  // This CTA's reads of its peers' staging are done: arrive now and wait at
+  // the very end, so the barrier's latency overlaps the epilogue.
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  // Pass 2: the epilogue, one warp per row (the warp that summed the row).
+  for (int r = rb + warp; good && r < re; r += kThreads / 32) {
+    float4 acc[NM];
+#pragma unroll
+    for (int a = 0; a < NM; ++a) acc[a] = *reinterpret_cast<const float4*>(red + ((size_t)a * TM + r) * kRedLd + cc);
     const int m = m0 + r;
     if (EPI == EPI_STORE || EPI == EPI_RESID) {
       float vv[4] = {acc[0].x, acc[0].y, acc[0].z, acc[0].w};
@@ -670,7 +683,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       if (lane == 0) atomicMax(e.keys + m, key);
     }
   }
-  cluster_sync_all();  // peers keep their staging until every slice is read
+  // peers keep their staging until every CTA has read its slice
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
   if (EPI == EPI_ARGMAX) {
     __shared__ unsigned s_last;
     __threadfence();
