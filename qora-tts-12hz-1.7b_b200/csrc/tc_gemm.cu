@@ -221,20 +221,19 @@ __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t&
   lo = h2_bits(__floats2half2_rn((a - hf.x) * kLoScale, (b - hf.y) * kLoScale));
 }
 
-// Q4 nibbles of byte `byte` of w (low nibble = even column) as half2 (q - 8), exact
-__device__ __forceinline__ __half2 nib_pair(uint32_t w, int byte) {
-  const uint32_t t = w >> (8 * byte);
-  uint32_t bits = (t & 0xFu) | ((t << 12) & 0xF0000u) | 0x64006400u;  // 1024 + q per half
-  return __hsub2(*reinterpret_cast<__half2*>(&bits), __float2half2_rn(1032.0f));
-}
-
-// 8 dequantised weights of one 32-bit word as hi / lo 16-byte core-matrix rows
+// 8 dequantised weights of one 32-bit word (nibble i = column i of the word,
+// gemv.rs:124) as hi / lo 16-byte core-matrix rows.  One shift + LOP3 turns
+// nibbles p and p + 4 into the half2 (1024 + q_p, 1024 + q_{p+4}), so a row
+// holds the columns in the order 0,4,1,5,2,6,3,7; the MMA's M rows may come in
+// any order, and the epilogue maps the accumulator lanes back (tc_col).
 __device__ __forceinline__ void dequant_word(uint32_t w, __half2 s2, uint4& hi, uint4& lo) {
   uint32_t h[4], l[4];
   const __half2 sc = __float2half2_rn(kLoScale);
+  const __half2 k1032 = __float2half2_rn(1032.0f);
 #pragma unroll
   for (int p = 0; p < 4; ++p) {
-    const __half2 q = nib_pair(w, p);
+    uint32_t bits = ((w >> (4 * p)) & 0x000F000Fu) | 0x64006400u;  // 1024 + q per half
+    const __half2 q = __hsub2(*reinterpret_cast<__half2*>(&bits), k1032);  // q - 8, exact
     const __half2 hh = __hmul2(q, s2);                      // fp16(q * scale)
     const __half2 rr = __hfma2(q, s2, __hneg2(hh));          // exact residual
     h[p] = h2_bits(hh);
@@ -243,6 +242,9 @@ __device__ __forceinline__ void dequant_word(uint32_t w, __half2 s2, uint4& hi, 
   hi = make_uint4(h[0], h[1], h[2], h[3]);
   lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
+// Column of the tile held by accumulator lane c (the MMA's M row c): rows
+// store each 8-column group in the order 0,4,1,5,2,6,3,7.
+__device__ __forceinline__ int tc_col(int c) { return (c & ~7) | ((c & 7) >> 1) | ((c & 1) << 2); }
 
 // 128-column tile t of the launch -> matrix, first column within it.
 __device__ __forceinline__ int tc_tile(const GemvDesc& d, int t, int NMv, int& tcol) {
@@ -420,8 +422,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
         for (int j = 0; j < 16; ++j) y[j] = R.x[p][j];
         if (d.gamma && !d.emb_idx) {
           const float inv = s_inv[r];
+          if (kk0 + 16 <= d.k && (reinterpret_cast<uintptr_t>(d.gamma) & 15u) == 0) {  // two 16-byte loads
+            const uint4 g4[2] = {__ldg(reinterpret_cast<const uint4*>(d.gamma + kk0)),
+                                 __ldg(reinterpret_cast<const uint4*>(d.gamma + kk0) + 1)};
+            const __half2* g2 = reinterpret_cast<const __half2*>(g4);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) y[j] = (kk0 + j < d.k) ? y[j] * inv * h2f(d.gamma[kk0 + j]) : 0.0f;
+            for (int j = 0; j < 8; ++j) {
+              const float2 g = __half22float2(g2[j]);
+              y[2 * j] = y[2 * j] * inv * g.x;
+              y[2 * j + 1] = y[2 * j + 1] * inv * g.y;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) y[j] = (kk0 + j < d.k) ? y[j] * inv * h2f(d.gamma[kk0 + j]) : 0.0f;
+          }
           if (d.xnorm_out && blockIdx.x == 0) {
 #pragma unroll
             for (int j = 0; j < 16; ++j)
@@ -537,7 +551,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   {
     const int lq = warp & 3, rb = warp >> 2;
     if (good && rb * 32 < Mv) {
-      const int c = lq * 32 + lane;
+      const int c = tc_col(lq * 32 + lane);
 #pragma unroll
       for (int a = 0; a < NM; ++a) {
         float vm[32], vc[32];
