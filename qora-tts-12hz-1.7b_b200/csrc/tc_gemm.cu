@@ -459,24 +459,46 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   };
 
 
-  // one 32-bit word of the raw stage (row brow, 8-column group g8 of the tile)
-  // as 8 hi + 8 lo fp16 values in the operand layout; consecutive words are
-  // consecutive rows of one group, so a warp's stores fill 512 contiguous bytes
-  auto store_word = [&](uint8_t* stb, int slot, int w) {
-    const int a = w / 1024, g8 = (w >> 6) & 15, brow = w & 63;
+  // Raw stage chunk q = (matrix q >> 8, 16-byte chunk ch = (q >> 6) & 3 of the
+  // row, row q & 63): 32 columns, 4 words, one f16 scale.  Consecutive q are
+  // consecutive rows, so a warp's 16-byte loads are conflict-free (80-byte
+  // row stride) and each of its operand stores fills 512 contiguous bytes.
+  // Word k of chunk ch is the 8-column group g8 = 4 ch + k, stored at
+  // g8 * 1024 + (row / 8) * 128 + (row % 8) * 16 (hi; lo NM operands later).
+  auto chunk_at = [&](int slot, int q, const uint8_t*& raw, uint8_t*& dst, uint8_t* stb) {
+    const int a = q >> 8, ch = (q >> 6) & 3, brow = q & 63;
     const uint8_t* base = tsm + C::PIPE_BYTES + slot * C::RAW_STAGE + a * kRawMat;
-    const uint32_t word = *reinterpret_cast<const uint32_t*>(base + brow * kRawRow + (g8 >> 2) * 16 + (g8 & 3) * 4);
-    const unsigned short sc = *reinterpret_cast<const unsigned short*>(base + TK * kRawRow + brow * 8 + (g8 >> 2) * 2);
-    uint4 hi, lo;
-    dequant_word(word, __half2half2(__ushort_as_half(sc)), hi, lo);
-    const int off = g8 * 1024 + (brow >> 3) * 128 + (brow & 7) * 16;
-    *reinterpret_cast<uint4*>(stb + a * B_BYTES + off) = hi;
-    *reinterpret_cast<uint4*>(stb + (NM + a) * B_BYTES + off) = lo;
+    raw = base + brow * kRawRow + ch * 16;
+    dst = stb + a * B_BYTES + ch * 4096 + (brow >> 3) * 128 + (brow & 7) * 16;
+    return __half2half2(__ushort_as_half(*reinterpret_cast<const unsigned short*>(base + TK * kRawRow + brow * 8 + ch * 2)));
   };
-  // Weight words per stage: the B warps take kWordsB each (strided by their
-  // count), the input-row warps the rest after their rows, which balances the
-  // two (an input-row thread's rows take about as long as 3-4 words).
-  constexpr int kWords = NM * 1024, kWordsB = NM == 1 ? 4 : 6;
+  auto store_chunk = [&](uint8_t* stb, int slot, int q) {
+    const uint8_t* raw;
+    uint8_t* dst;
+    const __half2 s2 = chunk_at(slot, q, raw, dst, stb);
+    const uint4 w4 = *reinterpret_cast<const uint4*>(raw);
+    const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint4 hi, lo;
+      dequant_word(wv[k], s2, hi, lo);
+      *reinterpret_cast<uint4*>(dst + k * 1024) = hi;
+      *reinterpret_cast<uint4*>(dst + NM * B_BYTES + k * 1024) = lo;
+    }
+  };
+  auto store_word = [&](uint8_t* stb, int slot, int q, int k) {  // word k of chunk q
+    const uint8_t* raw;
+    uint8_t* dst;
+    const __half2 s2 = chunk_at(slot, q, raw, dst, stb);
+    uint4 hi, lo;
+    dequant_word(*reinterpret_cast<const uint32_t*>(raw + 4 * k), s2, hi, lo);
+    *reinterpret_cast<uint4*>(dst + k * 1024) = hi;
+    *reinterpret_cast<uint4*>(dst + NM * B_BYTES + k * 1024) = lo;
+  };
+  // Chunks per stage: NM * 256.  The weight warps take NM chunks each; the
+  // 32 NM chunks left go to the input-row threads one word each (after their
+  // rows, which take about as long as 3-4 words).
+  constexpr int kChunksRem = NM * 256 - kBConv * NM;
 
   bool ok = true;
   if (tid < kConv) {
@@ -497,11 +519,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       cp_async_commit();
       if (a_thr) {
         store_a(ks0 + i, ac, st, st + A_BYTES);
-        for (int w = kBConv * kWordsB + (tid - kBConv); w < kWords; w += kConv - kBConv)
-          store_word(st + 2 * A_BYTES, i % C::RS, w);
+        if (at < 4 * kChunksRem) store_word(st + 2 * A_BYTES, i % C::RS, kBConv * NM + at % kChunksRem, at / kChunksRem);
       } else if (tid < kBConv) {
 #pragma unroll
-        for (int k = 0; k < kWordsB; ++k) store_word(st + 2 * A_BYTES, i % C::RS, tid + k * kBConv);
+        for (int j = 0; j < NM; ++j) store_chunk(st + 2 * A_BYTES, i % C::RS, tid + j * kBConv);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // st.shared -> visible to tcgen05.mma
       mbar_arrive(&full[b]);
