@@ -190,9 +190,11 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-# DRAM bytes (read + write) of one k=2048 n=6144 m=1 launch of the batch-1
-# GEMV, from the ncu capture summarised in profiles/gemv_dec_2048x6144_ncu.md
-GEMV_TRAFFIC_BYTES = 7128320
+# DRAM bytes (read + write) of one k=2048 n=6144 launch, from the ncu
+# captures summarised in profiles/gemv_dec_2048x6144_ncu.md (batch-1 GEMV,
+# m=1) and profiles/tc_proj_2048x6144_m64_ncu.md (tcgen05 projection, m=64)
+GEMV_TRAFFIC_BYTES = 7142912
+TC_TRAFFIC_BYTES = 7687168
 
 
 def time_q4_launches(Q, torch, k, n, m):
@@ -255,7 +257,7 @@ def tc_roofline(Q, torch, peaks):
     peak = peaks.get("bf16_tflops_sustained") or 1400.0
     ach = fl / dt / 1e12
     return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
-            "traffic": None, "kernel": "tc_proj_kernel (tcgen05 Q4 projection) k=2048 n=6144 m=64",
+            "traffic": TC_TRAFFIC_BYTES, "kernel": "tc_proj_kernel (tcgen05 Q4 projection) k=2048 n=6144 m=64",
             "us_per_launch": dt * 1e6, "algorithmic_flops": fl,
             "executed_tflops": 3 * (((m + 15) // 16 * 16) / m) * ach, "weight_gbs": q4_bytes(k, n) / dt / 1e9,
             "peak_kind": "bf16_tflops_sustained (measured)" if "bf16_tflops_sustained" in peaks else "fallback"}
