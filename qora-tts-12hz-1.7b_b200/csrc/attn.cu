@@ -80,7 +80,14 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnDesc d) {
     acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
 
+  // Each warp takes U positions per step (pb, pb + NW, ...).  The U partial
+  // dot products of a lane are reduced together: two transposing butterfly
+  // rounds leave lane group j = lane / 8 with position j's sum over 16 and
+  // then 8 lanes, three more rounds finish it (6 shuffles for 4 dots instead
+  // of 20), and lane 8 j broadcasts it.  The online softmax then updates once
+  // per step: one rescale for the block's max, one exp per position.
   constexpr int U = 4;
+  const bool hi16 = (lane & 16) != 0, hi8 = (lane & 8) != 0;
   for (int pb = p0 + warp; pb < p1; pb += NW * U) {
     float4 k4[U], v4[U];
 #pragma unroll
@@ -89,28 +96,47 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnDesc d) {
       if (p < p1) {
         k4[u] = *reinterpret_cast<const float4*>(kv_row_c(d.kv, sess, p, 0, h) + 4 * lane);
         v4[u] = *reinterpret_cast<const float4*>(kv_row_c(d.kv, sess, p, 1, h) + 4 * lane);
+      } else {
+        k4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        v4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
       }
     }
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int p = pb + NW * u;
-      if (p >= p1) break;
+    for (int g = 0; g < G; ++g) {
+      float dp[U];
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        float dot = q[g].x * k4[u].x + q[g].y * k4[u].y + q[g].z * k4[u].z + q[g].w * k4[u].w;
+      for (int u = 0; u < U; ++u) dp[u] = q[g].x * k4[u].x + q[g].y * k4[u].y + q[g].z * k4[u].z + q[g].w * k4[u].w;
+      // round 1 (xor 16): lanes < 16 keep positions 0, 1; lanes >= 16 keep 2, 3
+      float a0 = hi16 ? dp[2] : dp[0], a1 = hi16 ? dp[3] : dp[1];
+      const float b0 = hi16 ? dp[0] : dp[2], b1 = hi16 ? dp[1] : dp[3];
+      a0 += __shfl_xor_sync(0xffffffffu, b0, 16);
+      a1 += __shfl_xor_sync(0xffffffffu, b1, 16);
+      // round 2 (xor 8): lane group j = lane / 8 keeps position j
+      float c = hi8 ? a1 : a0;
+      c += __shfl_xor_sync(0xffffffffu, hi8 ? a0 : a1, 8);
+      c += __shfl_xor_sync(0xffffffffu, c, 4);
+      c += __shfl_xor_sync(0xffffffffu, c, 2);
+      c += __shfl_xor_sync(0xffffffffu, c, 1);
+      float sc[U];
+      float mn = mx[g];
 #pragma unroll
-        for (int o = 16; o; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-        const float s = dot * scale;
-        const float mn = fmaxf(mx[g], s);
-        const float corr = expf(mx[g] - mn);
-        const float pe = expf(s - mn);
-        l[g] = l[g] * corr + pe;
-        acc[g].x = acc[g].x * corr + pe * v4[u].x;
-        acc[g].y = acc[g].y * corr + pe * v4[u].y;
-        acc[g].z = acc[g].z * corr + pe * v4[u].z;
-        acc[g].w = acc[g].w * corr + pe * v4[u].w;
-        mx[g] = mn;
+      for (int u = 0; u < U; ++u) {
+        sc[u] = __shfl_sync(0xffffffffu, c, 8 * u) * scale;
+        if (pb + NW * u >= p1) sc[u] = -INFINITY;
+        mn = fmaxf(mn, sc[u]);
       }
+      const float corr = expf(mx[g] - mn);
+      float lsum = l[g] * corr;
+      float4 a4 = make_float4(acc[g].x * corr, acc[g].y * corr, acc[g].z * corr, acc[g].w * corr);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const float pe = expf(sc[u] - mn);  // 0 for the positions past p1
+        lsum += pe;
+        a4.x += pe * v4[u].x; a4.y += pe * v4[u].y; a4.z += pe * v4[u].z; a4.w += pe * v4[u].w;
+      }
+      l[g] = lsum;
+      acc[g] = a4;
+      mx[g] = mn;
     }
   }
 
