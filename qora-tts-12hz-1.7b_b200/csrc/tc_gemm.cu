@@ -213,12 +213,15 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
-// f32 pair -> fp16 hi pair and fp16 (residual * 2^11) pair
+// f32 pair -> fp16 hi pair and fp16 (residual * 2^11) pair; the residual
+// a - hi is exact in f32 and the scaling by 2^11 too (sm_100 f32x2 ops)
 __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
   const __half2 h = __floats2half2_rn(a, b);
   const float2 hf = __half22float2(h);
   hi = h2_bits(h);
-  lo = h2_bits(__floats2half2_rn((a - hf.x) * kLoScale, (b - hf.y) * kLoScale));
+  const float2 r = __fmul2_rn(__ffma2_rn(hf, make_float2(-1.0f, -1.0f), make_float2(a, b)),
+                              make_float2(kLoScale, kLoScale));
+  lo = h2_bits(__floats2half2_rn(r.x, r.y));
 }
 
 // 8 dequantised weights of one 32-bit word (nibble i = column i of the word,
@@ -427,10 +430,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
                                  __ldg(reinterpret_cast<const uint4*>(d.gamma + kk0) + 1)};
             const __half2* g2 = reinterpret_cast<const __half2*>(g4);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float2 g = __half22float2(g2[j]);
-              y[2 * j] = y[2 * j] * inv * g.x;
-              y[2 * j + 1] = y[2 * j + 1] * inv * g.y;
+            for (int j = 0; j < 8; ++j) {  // (x * inv) * gamma, pairwise in f32x2 (gemv.rs:414)
+              const float2 t = __fmul2_rn(__fmul2_rn(make_float2(y[2 * j], y[2 * j + 1]), make_float2(inv, inv)),
+                                          __half22float2(g2[j]));
+              y[2 * j] = t.x;
+              y[2 * j + 1] = t.y;
             }
           } else {
 #pragma unroll
