@@ -268,15 +268,16 @@ __device__ __forceinline__ float warp_sum(float v) {
 
 // Input rows of one stage held in registers by an input-row thread: pass p
 // covers row (at & 63) + 64 p, 16 consecutive k starting at 16 * ((at >> 6) & 3).
+template <int NP>
 struct ARegs {
-  float x[2][16];
+  float x[NP][16];
 };
 
 }  // namespace
 
 // ---------------------------------------------------------------------------
 // Grid (2 * ntiles, S, ceil(M / 128)), cluster (1, S, 1), 512 threads.
-template <int NM, int EPI>
+template <int NM, int EPI, int NP>
 __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, const FrameCodes fc) {
   using C = TcCfg<NM>;
   extern __shared__ __align__(1024) uint8_t tsm[];
@@ -358,11 +359,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   // shared memory (split).  Thread: row (at & 63) + 64 p, 16-deep k slice at / 64.
   const bool a_thr = tid >= kBConv && tid < kConv;
   const int at = tid - kBConv, arow = at & 63, akc = (at >> 6) & 3;
-  const int npass = Mv > 64 ? 2 : 1;
-  auto load_a = [&](int ks, ARegs& R) {
+  const int npass = NP == 1 ? 1 : (Mv > 64 ? 2 : 1);  // NP: passes compiled (1: blocks of <= 64 rows)
+  auto load_a = [&](int ks, ARegs<NP>& R) {
     const int kk0 = ks * TK + akc * 16;
 #pragma unroll
-    for (int p = 0; p < 2; ++p) {
+    for (int p = 0; p < NP; ++p) {
       const int r = arow + 64 * p;
       if (p < npass && r < Mv) {
         const int m = m0 + r;
@@ -387,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   pdl_wait();  // activations, norms' sums of squares and KV of earlier kernels are ready
   // the first stage's input rows are issued now, so their round trip overlaps
   // the TMEM allocation and the 1/rms loads below
-  ARegs an;
+  ARegs<NP> an;
   if (a_thr) load_a(ks0, an);
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -414,10 +415,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   const uint32_t tmem = *tmem_slot;
 
   float amax = 0.0f;
-  auto store_a = [&](int ks, const ARegs& R, uint8_t* ahi, uint8_t* alo) {
+  auto store_a = [&](int ks, const ARegs<NP>& R, uint8_t* ahi, uint8_t* alo) {
     const int kk0 = ks * TK + akc * 16;
 #pragma unroll
-    for (int p = 0; p < 2; ++p) {
+    for (int p = 0; p < NP; ++p) {
       const int r = arow + 64 * p;
       if (p < npass && r < Mv) {
         float y[16];
@@ -510,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
     for (int i = 0; i < nst; ++i) {
       const int b = i % C::STAGES;
       uint8_t* st = tsm + b * C::STAGE_BYTES;
-      const ARegs ac = an;
+      const ARegs<NP> ac = an;
       if (a_thr && i + 1 < nst) load_a(ks0 + i + 1, an);  // input rows one stage ahead
       cp_async_wait<C::RS - 2>();  // this thread's raw copies of stage i have landed
       // this operand buffer was read by the MMAs of stage i - STAGES
@@ -795,14 +796,21 @@ bool tc_layout_ok(const GemvDesc& d) {
   return true;
 }
 
-template <int NM, int EPI>
-static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
+template <int NM, int EPI, int NP>
+static cudaError_t launch_np(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
   const int S = tc_splits(d);
   LaunchOpts o;
   o.pdl = d.pdl != 0;
   o.cluster_y = (unsigned)S;
   const dim3 grid(2 * d.ntiles, S, (d.M + TM - 1) / TM);
-  return launch_k(tc_proj_kernel<NM, EPI>, grid, dim3(kThreads), (size_t)TcCfg<NM>::SMEM, st, o, d, fc);
+  return launch_k(tc_proj_kernel<NM, EPI, NP>, grid, dim3(kThreads), (size_t)TcCfg<NM>::SMEM, st, o, d, fc);
+}
+
+template <int NM, int EPI>
+static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
+  // row blocks of at most 64 rows run the instance compiled for one input-row pass
+  if (d.M <= TM / 2) return launch_np<NM, EPI, 1>(d, fc, st);
+  return launch_np<NM, EPI, 2>(d, fc, st);
 }
 
 cudaError_t launch_tc(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
@@ -825,11 +833,16 @@ void tc_init_attributes() {
   static bool done[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || done[dev]) return;
-  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_STORE>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
-  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
-  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
-  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_ARGMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
-  cudaFuncSetAttribute(tc_proj_kernel<2, EPI_SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<2>::SMEM);
+cudaFuncSetAttribute(tc_proj_kernel<1, EPI_STORE, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_RESID, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_QKV, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_ARGMAX, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<2, EPI_SWIGLU, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<2>::SMEM);
+cudaFuncSetAttribute(tc_proj_kernel<1, EPI_STORE, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_RESID, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_QKV, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_ARGMAX, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<2, EPI_SWIGLU, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<2>::SMEM);
   cudaGetLastError();
   done[dev] = true;
 }
