@@ -357,6 +357,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   }
   // ---- input rows of a stage (warps 7-14): registers one stage ahead ->
   // shared memory (split).  Thread: row (at & 63) + 64 p, 16-deep k slice at / 64.
+  // the embedding gather and the normed-row copy serve STORE launches only
+  // (input_proj, text fc1, codec head); other kinds compile without them
+  constexpr bool kEmb = EPI == EPI_STORE;
   const bool a_thr = tid >= kBConv && tid < kConv;
   const int at = tid - kBConv, arow = at & 63, akc = (at >> 6) & 3;
   const int npass = NP == 1 ? 1 : (Mv > 64 ? 2 : 1);  // NP: passes compiled (1: blocks of <= 64 rows)
@@ -367,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       const int r = arow + 64 * p;
       if (p < npass && r < Mv) {
         const int m = m0 + r;
-        if (d.emb_idx) {
+        if (kEmb && d.emb_idx) {
           const uint32_t er = d.emb_idx[(size_t)m * d.emb_idx_stride];
           const uint8_t* prow = d.emb.packed + (size_t)er * (d.emb.n / 2);
           const __half* srow = d.emb.scales + (size_t)er * (d.emb.n / 32);
@@ -424,7 +427,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
         float y[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) y[j] = R.x[p][j];
-        if (d.gamma && !d.emb_idx) {
+        if (d.gamma && !(kEmb && d.emb_idx)) {
           const float inv = s_inv[r];
           if (kk0 + 16 <= d.k && (reinterpret_cast<uintptr_t>(d.gamma) & 15u) == 0) {  // two 16-byte loads
             const uint4 g4[2] = {__ldg(reinterpret_cast<const uint4*>(d.gamma + kk0)),
@@ -441,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
 #pragma unroll
             for (int j = 0; j < 16; ++j) y[j] = (kk0 + j < d.k) ? y[j] * inv * h2f(d.gamma[kk0 + j]) : 0.0f;
           }
-          if (d.xnorm_out && blockIdx.x == 0) {
+          if (kEmb && d.xnorm_out && blockIdx.x == 0) {
 #pragma unroll
             for (int j = 0; j < 16; ++j)
               if (kk0 + j < d.k) d.xnorm_out[(size_t)(m0 + r) * d.ld_xnorm + kk0 + j] = y[j];
@@ -816,6 +819,7 @@ static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_
 cudaError_t launch_tc(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
   if (d.tc_ks <= 0 || d.M <= 0 || d.k <= 0 || tc_splits(d) > kMaxSplits) return cudaErrorInvalidValue;
   if (!tc_layout_ok(d)) return cudaErrorMisalignedAddress;
+  if (d.epi_kind != EPI_STORE && (d.emb_idx || d.xnorm_out)) return cudaErrorInvalidValue;
   if (d.epi_kind == EPI_ARGMAX && (d.M + TM - 1) / TM > 4096) return cudaErrorInvalidValue;
   if (d.paired) return d.epi_kind == EPI_SWIGLU ? launch_t<2, EPI_SWIGLU>(d, fc, st) : cudaErrorInvalidValue;
   switch (d.epi_kind) {
