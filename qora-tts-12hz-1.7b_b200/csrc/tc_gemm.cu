@@ -307,22 +307,51 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   // weights are never written by an earlier kernel, so this starts before
   // the programmatic-dependent-launch wait
   const uint32_t raw_a = tsm_a + C::PIPE_BYTES;
+  // A thread's raw chunks are fixed for the whole kernel (chunk c = tid + j *
+  // kConv of NM * 384: 256 packed 16-byte chunks, then 128 4-byte scale pairs
+  // per matrix); per stage only the source row moves, by TK rows.
+  struct RawChunk {
+    const uint8_t* src0;  // row `row` of the tile's columns
+    size_t stride;        // bytes per TK rows
+    uint32_t dst;         // offset in a raw stage
+    int row;              // row within the stage
+    bool on, pk;          // chunk exists; packed (16 bytes) or scales (4 bytes)
+  };
+  RawChunk rc[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int c = tid + j * kConv;
+    rc[j].on = tid < kConv && c < NM * 384;
+    const int a = rc[j].on ? c / 384 : 0, cc = c % 384;
+    const Q4Mat& Mt = d.mat[NM == 2 ? a : mat];
+    rc[j].pk = cc < 256;
+    if (rc[j].pk) {  // 16 bytes = 32 columns of packed nibbles
+      const int ch = cc & 3;
+      rc[j].row = cc >> 2;
+      rc[j].on = rc[j].on && tcol + ch * 32 < n;
+      rc[j].src0 = Mt.packed + (size_t)rc[j].row * (n / 2) + tcol / 2 + ch * 16;
+      rc[j].stride = (size_t)TK * (n / 2);
+      rc[j].dst = (uint32_t)(a * kRawMat + rc[j].row * kRawRow + ch * 16);
+    } else {         // 4 bytes = 2 f16 scales = 64 columns
+      const int h = (cc - 256) & 1;
+      rc[j].row = (cc - 256) >> 1;
+      rc[j].on = rc[j].on && tcol + h * 64 < n;
+      rc[j].src0 = reinterpret_cast<const uint8_t*>(Mt.scales + (size_t)rc[j].row * (n / 32) + tcol / 32 + h * 2);
+      rc[j].stride = (size_t)TK * (n / 32) * 2;
+      rc[j].dst = (uint32_t)(a * kRawMat + TK * kRawRow + rc[j].row * 8 + h * 4);
+    }
+  }
+  // Chunks past K or past n are zero-filled (source size 0) from a valid address.
   auto issue_b = [&](int ks, int slot) {
-    for (int c = tid; c < NM * 384; c += kConv) {
-      const int a = c / 384, cc = c % 384;
-      const Q4Mat& Mt = d.mat[NM == 2 ? a : mat];
-      const uint32_t base = raw_a + slot * C::RAW_STAGE + a * kRawMat;
-      const int row = (cc < 256 ? cc >> 2 : (cc - 256) >> 1), grow = ks * TK + row;
-      if (cc < 256) {  // 16 bytes = 32 columns of packed nibbles
-        const int ch = cc & 3;
-        const bool v = grow < d.k && tcol + ch * 32 < n;
-        const uint8_t* src = v ? Mt.packed + (size_t)grow * (n / 2) + tcol / 2 + ch * 16 : Mt.packed;
-        cp_async16(base + row * kRawRow + ch * 16, src, v ? 16u : 0u);
-      } else {         // 4 bytes = 2 f16 scales = 64 columns
-        const int h = (cc - 256) & 1;
-        const bool v = grow < d.k && tcol + h * 64 < n;
-        const __half* src = v ? Mt.scales + (size_t)grow * (n / 32) + tcol / 32 + h * 2 : Mt.scales;
-        cp_async4(base + TK * kRawRow + row * 8 + h * 4, src, v ? 4u : 0u);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      if (j * kConv >= NM * 384) break;
+      const bool v = rc[j].on && ks * TK + rc[j].row < d.k;
+      const uint8_t* src = v ? rc[j].src0 + (size_t)ks * rc[j].stride : d.mat[0].packed;
+      const uint32_t dst = raw_a + slot * C::RAW_STAGE + rc[j].dst;
+      if (tid + j * kConv < NM * 384) {
+        if (rc[j].pk) cp_async16(dst, src, v ? 16u : 0u);
+        else cp_async4(dst, src, v ? 4u : 0u);
       }
     }
   };
