@@ -127,6 +127,49 @@ DLayer mk_layer(char* base, const LOff& o) {
 void gemv_init_attributes();
 void attn_init_attributes();
 
+// The code predictor's projections (layers, input_proj, group heads) run 15
+// times per frame.  For batched decode their weights are expanded once into
+// the tensor-core operand layout (4 bytes per weight, ~450 MB for 1.7B), so
+// those launches copy operand tiles instead of dequantising them at every
+// group step.  Optional: without the memory (or with QTTS_EXPAND=0) the
+// launches dequantise as the others do.
+static void expand_predictor(Model* m) {
+  static const bool on = [] {
+    const char* v = getenv("QTTS_EXPAND");
+    return !(v && v[0] == '0');
+  }();
+  if (!on || !tc_enabled()) return;
+  std::vector<Q4Mat*> mats;
+  for (auto& L : m->pl)
+    for (Q4Mat* w : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down}) mats.push_back(w);
+  if (m->has_proj) mats.push_back(&m->input_proj);
+  for (auto& w : m->lm) mats.push_back(&w);
+  mats.erase(std::remove_if(mats.begin(), mats.end(), [](const Q4Mat* w) { return w->n % 64 != 0; }), mats.end());
+  size_t total = 0;
+  for (Q4Mat* w : mats) total += (tc_expand_bytes(w->k, w->n) + 255) & ~(size_t)255;
+  if (total == 0 || cudaMalloc(&m->wx_arena, total) != cudaSuccess) {
+    cudaGetLastError();
+    m->wx_arena = nullptr;
+    return;
+  }
+  size_t off = 0;
+  bool ok = true;
+  for (Q4Mat* w : mats) {
+    ok = ok && tc_expand(*w, m->wx_arena + off, nullptr) == cudaSuccess;
+    w->wx = m->wx_arena + off;
+    off += (tc_expand_bytes(w->k, w->n) + 255) & ~(size_t)255;
+  }
+  ok = ok && cudaDeviceSynchronize() == cudaSuccess;
+  if (!ok) {  // fall back to in-kernel dequantisation
+    for (Q4Mat* w : mats) w->wx = nullptr;
+    cudaFree(m->wx_arena);
+    m->wx_arena = nullptr;
+    cudaGetLastError();
+    return;
+  }
+  m->wx_bytes = total;
+}
+
 static int model_load(const char* path, int device, Model** out) {
   HModel hm;
   std::string err;
@@ -236,6 +279,7 @@ static int model_load(const char* path, int device, Model** out) {
   attn_init_attributes();
   tc_init_attributes();
   pred_persist_init_attributes();
+  expand_predictor(m);
   *out = m;
   return QTTS_OK;
 }
@@ -1409,6 +1453,7 @@ int qtts_model_free(qtts_model* h) {
   cudaSetDevice(h->m->device);
   cudaFree(h->m->arena);
   cudaFree(h->m->d_group_emb);
+  if (h->m->wx_arena) cudaFree(h->m->wx_arena);
   delete h->m;
   delete h;
   return QTTS_OK;
@@ -1419,7 +1464,7 @@ int qtts_model_dims(const qtts_model* h, qtts_dims* out) {
   *out = h->m->d;
   return QTTS_OK;
 }
-size_t qtts_model_device_bytes(const qtts_model* h) { return h ? h->m->bytes : 0; }
+size_t qtts_model_device_bytes(const qtts_model* h) { return h ? h->m->bytes + h->m->wx_bytes : 0; }
 
 int qtts_session_create(qtts_model* h, int max_batch, int max_positions, qtts_session** out) {
   if (!h || !out) return fail(QTTS_ERR_BADARG, "null argument");

@@ -36,6 +36,8 @@ struct Model {
   const __half *t_final = nullptr, *p_final = nullptr;
   std::vector<Q4Mat> p_emb, lm;
   Q4Mat* d_group_emb = nullptr;  // device copy of p_emb for the fusion kernel
+  uint8_t* wx_arena = nullptr;   // predictor layer weights expanded for the tensor cores (optional)
+  size_t wx_bytes = 0;
   bool has_proj = false;
 };
 

@@ -20,6 +20,9 @@ struct Q4Mat {
   const uint8_t* packed = nullptr;  // k*n/2 bytes, low nibble = even column
   const __half* scales = nullptr;   // k*n/32 f16, groups of 32 along n
   int k = 0, n = 0;
+  // optional: the weights expanded once into the tensor-core operand layout
+  // (fp16 hi / lo blocks per 128-column tile and 64-row stage, tc_expand)
+  const uint8_t* wx = nullptr;
 };
 
 // Paged KV addressing.  A page holds kPageSize positions of every layer:
@@ -267,6 +270,10 @@ void tc_plan(int sm_count, GemvDesc& g);   // sets tc = 1 and tc_ks (K split fit
 int tc_splits(const GemvDesc& d);          // K slices of a planned launch
 size_t tc_smem_bytes(int nm);
 cudaError_t launch_tc(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st);
+// Expanded tensor-core operands of a Q4 weight: bytes needed, and the
+// expansion (one launch; the blocks are what the projection's converters write).
+size_t tc_expand_bytes(int k, int n);
+cudaError_t tc_expand(const Q4Mat& w, uint8_t* out, cudaStream_t st);
 void tc_init_attributes();
 
 // persistent code predictor of one utterance (pred_persist.cu)

@@ -152,6 +152,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
 __device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// Bulk copy global -> this CTA's shared memory (no multicast), completing its
+// bytes on the CTA's mbarrier; addresses and size multiples of 16 bytes.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
 // Parity wait bounded by kWaitNs; true when the phase completed.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
   const uint32_t a = smem_u32(bar);
@@ -277,7 +287,7 @@ struct ARegs {
 
 // ---------------------------------------------------------------------------
 // Grid (2 * ntiles, S, ceil(M / 128)), cluster (1, S, 1), 512 threads.
-template <int NM, int EPI, int NP>
+template <int NM, int EPI, int NP, bool WX>
 __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, const FrameCodes fc) {
   using C = TcCfg<NM>;
   extern __shared__ __align__(1024) uint8_t tsm[];
@@ -287,6 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tsm + C::AUX + 64);
   unsigned* s_flag = reinterpret_cast<unsigned*>(tsm + C::AUX + 96);
   float* s_inv = reinterpret_cast<float*>(tsm + C::AUX + 128);  // [128]
+  uint64_t* wfull = reinterpret_cast<uint64_t*>(tsm + C::AUX + 640);  // [STAGES] (WX) weight tiles of the stage landed
   float* red = reinterpret_cast<float*>(tsm);                   // epilogue staging [NM][128][kRedLd]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -355,12 +366,28 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       }
     }
   };
-  if (tid < kConv) {
+  if (!WX && tid < kConv) {
     for (int j = 0; j < C::RS - 1; ++j) {
       if (j < nst) issue_b(ks0 + j, j);
       cp_async_commit();
     }
   }
+  // WX: the stage's expanded weight tiles (16 KB hi + 16 KB lo per matrix,
+  // block (tile, stage) of the matrix's expansion) by bulk copies into the
+  // operand buffer, completing on wfull[buffer]; one thread issues them
+  const int nks_all = (d.k + TK - 1) / TK;
+  auto issue_w = [&](int i) {
+    const int b = i % C::STAGES;
+    const uint32_t st_a = tsm_a + (uint32_t)(b * C::STAGE_BYTES);
+    mbar_expect_tx(&wfull[b], (uint32_t)(NM * 2 * B_BYTES));
+#pragma unroll
+    for (int a = 0; a < NM; ++a) {
+      const Q4Mat& Mt = d.mat[NM == 2 ? a : mat];
+      const uint8_t* src = Mt.wx + ((size_t)(tcol / TN) * nks_all + (ks0 + i)) * (2 * B_BYTES);
+      bulk_g2s(st_a + 2 * A_BYTES + a * B_BYTES, src, B_BYTES, &wfull[b]);
+      bulk_g2s(st_a + 2 * A_BYTES + (NM + a) * B_BYTES, src + B_BYTES, B_BYTES, &wfull[b]);
+    }
+  };
 
   if (tid == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -368,8 +395,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       mbar_init(&full[s], kConv);
     }
     mbar_init(fin, 1);
+    if (WX)
+      for (int s = 0; s < C::STAGES; ++s) mbar_init(&wfull[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     *s_flag = 0u;
+    // the weights never depend on an earlier kernel: the first stages' tiles
+    // are requested before the dependent-launch wait
+    if (WX)
+      for (int j = 0; j < C::STAGES && j < nst; ++j) issue_w(j);
   }
   // rows [Mv, Nr) of every input-row buffer stay zero for the whole kernel
   // (the MMAs read Nr rows; rows past Nr are never read)
@@ -549,15 +582,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       // this operand buffer was read by the MMAs of stage i - STAGES
       bool w_ok = true;
       if (i >= C::STAGES) w_ok = mbar_wait(&mma_done[b], (unsigned)((i / C::STAGES) - 1) & 1u);
+      if (WX && tid == 0 && i >= C::STAGES && w_ok) issue_w(i);  // the buffer's MMAs are done
       // publishes every converter's raw copies of stage i; every conversion of
       // stage i - 1 is done, so its raw slot takes stage i + RS - 1
       if (!conv_sync_and(w_ok)) { ok = false; break; }
-      if (i + C::RS - 1 < nst) issue_b(ks0 + i + C::RS - 1, (i + C::RS - 1) % C::RS);
+      if (!WX && i + C::RS - 1 < nst) issue_b(ks0 + i + C::RS - 1, (i + C::RS - 1) % C::RS);
       cp_async_commit();
       if (a_thr) {
         store_a(ks0 + i, ac, st, st + A_BYTES);
-        if (at < 4 * kChunksRem) store_word(st + 2 * A_BYTES, i % C::RS, kBConv * NM + at % kChunksRem, at / kChunksRem);
-      } else if (tid < kBConv) {
+        if (!WX && at < 4 * kChunksRem) store_word(st + 2 * A_BYTES, i % C::RS, kBConv * NM + at % kChunksRem, at / kChunksRem);
+      } else if (!WX && tid < kBConv) {
 #pragma unroll
         for (int j = 0; j < NM; ++j) store_chunk(st + 2 * A_BYTES, i % C::RS, tid + j * kBConv);
       }
@@ -568,7 +602,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
     // ---- MMA issue
     for (int i = 0; i < nst; ++i) {
       const int b = i % C::STAGES;
-      const bool f_ok = mbar_wait(&full[b], (unsigned)(i / C::STAGES) & 1u);
+      bool f_ok = mbar_wait(&full[b], (unsigned)(i / C::STAGES) & 1u);
+      if (WX && f_ok) f_ok = mbar_wait(&wfull[b], (unsigned)(i / C::STAGES) & 1u);
       if (!__all_sync(0xffffffffu, f_ok)) { ok = false; break; }
       if (lane == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -828,20 +863,26 @@ bool tc_layout_ok(const GemvDesc& d) {
   return true;
 }
 
-template <int NM, int EPI, int NP>
+template <int NM, int EPI, int NP, bool WX = false>
 static cudaError_t launch_np(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
   const int S = tc_splits(d);
   LaunchOpts o;
   o.pdl = d.pdl != 0;
   o.cluster_y = (unsigned)S;
   const dim3 grid(2 * d.ntiles, S, (d.M + TM - 1) / TM);
-  return launch_k(tc_proj_kernel<NM, EPI, NP>, grid, dim3(kThreads), (size_t)TcCfg<NM>::SMEM, st, o, d, fc);
+  return launch_k(tc_proj_kernel<NM, EPI, NP, WX>, grid, dim3(kThreads), (size_t)TcCfg<NM>::SMEM, st, o, d, fc);
 }
 
 template <int NM, int EPI>
 static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
-  // row blocks of at most 64 rows run the instance compiled for one input-row pass
-  if (d.M <= TM / 2) return launch_np<NM, EPI, 1>(d, fc, st);
+  // row blocks of at most 64 rows run the instance compiled for one input-row
+  // pass; with every matrix expanded (tc_expand), the one fed by bulk copies
+  if (d.M <= TM / 2) {
+    bool wx = true;
+    for (int i = 0; i < (NM == 2 ? 2 : d.nmat); ++i) wx = wx && d.mat[i].wx != nullptr;
+    if (wx) return launch_np<NM, EPI, 1, true>(d, fc, st);
+    return launch_np<NM, EPI, 1>(d, fc, st);
+  }
   return launch_np<NM, EPI, 2>(d, fc, st);
 }
 
@@ -860,22 +901,73 @@ cudaError_t launch_tc(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) 
   }
 }
 
+// ---------------------------------------------------------------------------
+// Weight expansion for the WX instances: block (tile t of 128 columns, stage
+// ks of 64 rows) at ((t * nks) + ks) * 32 KB holds the 16 KB hi then 16 KB lo
+// fp16 operand tiles exactly as store_chunk writes them (rows past k and
+// columns past n zero); a thread per 16-byte packed chunk.
+__global__ void tc_expand_kernel(const Q4Mat w, uint8_t* out) {
+  const int nt = (w.n + TN - 1) / TN, nks = (w.k + TK - 1) / TK;
+  const size_t nchunks = (size_t)nt * nks * 256;
+  for (size_t c = (size_t)blockIdx.x * blockDim.x + threadIdx.x; c < nchunks; c += (size_t)gridDim.x * blockDim.x) {
+    const int q = (int)(c & 255);
+    const size_t blk = c >> 8;
+    const int ks = (int)(blk % nks), t = (int)(blk / nks);
+    const int ch = (q >> 6) & 3, brow = q & 63;
+    const int row = ks * TK + brow, col = t * TN + ch * 32;
+    uint4 w4 = make_uint4(0, 0, 0, 0);
+    unsigned short sc = 0;
+    if (row < w.k && col < w.n) {
+      w4 = *reinterpret_cast<const uint4*>(w.packed + (size_t)row * (w.n / 2) + col / 2);
+      sc = reinterpret_cast<const unsigned short*>(w.scales)[(size_t)row * (w.n / 32) + col / 32];
+    }
+    const __half2 s2 = __half2half2(__ushort_as_half(sc));
+    uint8_t* dst = out + blk * (2 * B_BYTES) + ch * 4096 + (brow >> 3) * 128 + (brow & 7) * 16;
+    const uint32_t wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      uint4 hi, lo;
+      dequant_word(wv[k], s2, hi, lo);
+      *reinterpret_cast<uint4*>(dst + k * 1024) = hi;
+      *reinterpret_cast<uint4*>(dst + B_BYTES + k * 1024) = lo;
+    }
+  }
+}
+
+size_t tc_expand_bytes(int k, int n) {
+  return (size_t)((n + TN - 1) / TN) * ((k + TK - 1) / TK) * (2 * B_BYTES);
+}
+
+cudaError_t tc_expand(const Q4Mat& w, uint8_t* out, cudaStream_t st) {
+  if (!w.packed || !w.scales || !out || w.k <= 0 || w.n <= 0 || w.n % 64 || !al16(w.packed) || !al16(out))
+    return cudaErrorInvalidValue;
+  const size_t nchunks = tc_expand_bytes(w.k, w.n) / (2 * B_BYTES) * 256;
+  const unsigned grid = (unsigned)std::min<size_t>((nchunks + 255) / 256, 148 * 8);
+  tc_expand_kernel<<<grid, 256, 0, st>>>(w, out);
+  return cudaGetLastError();
+}
+
 // Opt the kernels into their dynamic shared memory once per device (outside
 // any stream capture).
 void tc_init_attributes() {
   static bool done[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || done[dev]) return;
-cudaFuncSetAttribute(tc_proj_kernel<1, EPI_STORE, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
-  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_RESID, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
-  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_QKV, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
-  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_ARGMAX, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
-  cudaFuncSetAttribute(tc_proj_kernel<2, EPI_SWIGLU, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<2>::SMEM);
-cudaFuncSetAttribute(tc_proj_kernel<1, EPI_STORE, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
-  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_RESID, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
-  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_QKV, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
-  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_ARGMAX, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
-  cudaFuncSetAttribute(tc_proj_kernel<2, EPI_SWIGLU, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<2>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_STORE, 1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_STORE, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_RESID, 1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_RESID, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_QKV, 1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_QKV, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_ARGMAX, 1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_ARGMAX, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<2, EPI_SWIGLU, 1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<2>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<2, EPI_SWIGLU, 1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<2>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_STORE, 2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_RESID, 2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_QKV, 2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_ARGMAX, 2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<2, EPI_SWIGLU, 2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<2>::SMEM);
   cudaGetLastError();
   done[dev] = true;
 }
