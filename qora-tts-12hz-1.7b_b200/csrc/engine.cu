@@ -127,19 +127,23 @@ DLayer mk_layer(char* base, const LOff& o) {
 void gemv_init_attributes();
 void attn_init_attributes();
 
-// The code predictor's projections (layers, input_proj, group heads) run 15
-// times per frame.  For batched decode their weights are expanded once into
-// the tensor-core operand layout (4 bytes per weight, ~450 MB for 1.7B), so
-// those launches copy operand tiles instead of dequantising them at every
-// group step.  Optional: without the memory (or with QTTS_EXPAND=0) the
-// launches dequantise as the others do.
+// For batched decode the layer projections (talker and code predictor) and
+// the predictor's input_proj and group heads are expanded once into the
+// tensor-core operand layout (4 bytes per weight: ~6 GB for 1.7B, of the
+// GPU's 180 GB), so those launches copy operand tiles instead of
+// dequantising them; the predictor's are otherwise dequantised 15 times per
+// frame.  Optional: without the memory, or with QTTS_EXPAND=1 (predictor
+// only) / 0 (none), the other launches dequantise in the kernel.
 static void expand_predictor(Model* m) {
-  static const bool on = [] {
+  static const int mode = [] {
     const char* v = getenv("QTTS_EXPAND");
-    return !(v && v[0] == '0');
+    return v ? atoi(v) : 2;
   }();
-  if (!on || !tc_enabled()) return;
+  if (mode == 0 || !tc_enabled()) return;
   std::vector<Q4Mat*> mats;
+  if (mode >= 2)  // the talker's layer projections as well (QTTS_EXPAND=1: predictor only)
+    for (auto& L : m->tl)
+      for (Q4Mat* w : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down}) mats.push_back(w);
   for (auto& L : m->pl)
     for (Q4Mat* w : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down}) mats.push_back(w);
   if (m->has_proj) mats.push_back(&m->input_proj);
