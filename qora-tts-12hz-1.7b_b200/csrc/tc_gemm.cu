@@ -877,12 +877,14 @@ template <int NM, int EPI>
 static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
   // row blocks of at most 64 rows run the instance compiled for one input-row
   // pass; with every matrix expanded (tc_expand), the one fed by bulk copies
+  // (up to one 128-row block: more blocks would copy each tile again)
+  bool wx = true;
+  for (int i = 0; i < (NM == 2 ? 2 : d.nmat); ++i) wx = wx && d.mat[i].wx != nullptr;
   if (d.M <= TM / 2) {
-    bool wx = true;
-    for (int i = 0; i < (NM == 2 ? 2 : d.nmat); ++i) wx = wx && d.mat[i].wx != nullptr;
     if (wx) return launch_np<NM, EPI, 1, true>(d, fc, st);
     return launch_np<NM, EPI, 1>(d, fc, st);
   }
+  if (wx && d.M <= TM) return launch_np<NM, EPI, 2, true>(d, fc, st);
   return launch_np<NM, EPI, 2>(d, fc, st);
 }
 
@@ -968,6 +970,11 @@ void tc_init_attributes() {
   cudaFuncSetAttribute(tc_proj_kernel<1, EPI_QKV, 2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
   cudaFuncSetAttribute(tc_proj_kernel<1, EPI_ARGMAX, 2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
   cudaFuncSetAttribute(tc_proj_kernel<2, EPI_SWIGLU, 2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<2>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_STORE, 2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_RESID, 2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_QKV, 2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<1, EPI_ARGMAX, 2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<1>::SMEM);
+  cudaFuncSetAttribute(tc_proj_kernel<2, EPI_SWIGLU, 2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcCfg<2>::SMEM);
   cudaGetLastError();
   done[dev] = true;
 }

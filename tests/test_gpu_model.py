@@ -160,12 +160,15 @@ def _forced_batch(cases, F):
     return np.stack(out).astype(np.uint32)
 
 
-def test_batched_tensor_core_teacher_forced_tiny(qtts, gpu_tiny):
-    # 20 utterances: every projection of the frame has M >= 16 rows and runs
-    # on the tcgen05 path; each utterance must still match its own oracle run
+@pytest.mark.parametrize("reps", [5, 10])
+def test_batched_tensor_core_teacher_forced_tiny(qtts, gpu_tiny, reps):
+    # 20 / 40 utterances: every projection of the frame has M >= 16 rows and
+    # runs on the tcgen05 path (with 40, the predictor's two-row first step
+    # has 80 rows: the two-pass instance, fed by the expanded weights); each
+    # utterance must still match its own oracle run
     H = gpu_tiny.dims.t_hidden
     base = ["tiny_greedy", "tiny_sampled", "tiny_speaker", "tiny_notext"]
-    cases = base * 5
+    cases = base * reps
     F = 24
     s = qtts.Session(gpu_tiny, len(cases), 10 + F)
     codes, frames, lg, _ = qtts.generate(s, [tiny_case(c, H) for c in cases], F,
