@@ -29,6 +29,13 @@
 //     among themselves by a named barrier) already convert the next stage.
 // Result = D_main + 2^-11 * D_cross (the dropped lo*lo term is ~2^-22).
 //
+// Expanded weights (WX instances): when every matrix of the launch carries
+// the tiles tc_expand wrote at load, one thread bulk-copies each stage's
+// 32 KB hi/lo tiles per matrix straight into the operand buffer (the first
+// stages before the dependent-launch wait, the others once the buffer's
+// MMAs are done) and the MMA warp also waits on that copy's mbarrier; the
+// converters then only split the input rows.
+//
 // Epilogue: the accumulators go TMEM -> registers -> shared memory; the S
 // CTAs of the cluster then each take a slice of the rows, sum the S partials
 // over distributed shared memory in slice order (deterministic), and run the
