@@ -411,6 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
     if (WX)
       for (int j = 0; j < C::STAGES && j < nst; ++j) issue_w(j);
   }
+  int w_issued = (WX && tid == 0) ? min(C::STAGES, nst) : 0;  // stages whose weight copies were issued
   // rows [Mv, Nr) of every input-row buffer stay zero for the whole kernel
   // (the MMAs read Nr rows; rows past Nr are never read)
   const int Nr = (Mv + 15) & ~15;
@@ -589,7 +590,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       // this operand buffer was read by the MMAs of stage i - STAGES
       bool w_ok = true;
       if (i >= C::STAGES) w_ok = mbar_wait(&mma_done[b], (unsigned)((i / C::STAGES) - 1) & 1u);
-      if (WX && tid == 0 && i >= C::STAGES && w_ok) issue_w(i);  // the buffer's MMAs are done
+      if (WX && tid == 0 && i >= C::STAGES && w_ok) {  // the buffer's MMAs are done
+        issue_w(i);
+        w_issued = i + 1;
+      }
       // publishes every converter's raw copies of stage i; every conversion of
       // stage i - 1 is done, so its raw slot takes stage i + RS - 1
       if (!conv_sync_and(w_ok)) { ok = false; break; }
@@ -636,6 +640,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
     if (lane == 0) umma_commit(fin);
   }
   cp_async_wait<0>();  // no copy may land after the ring is reused for staging
+  if (WX && tid == 0) {  // nor a weight copy (bounded; all have landed unless a wait timed out)
+    for (int j = max(0, w_issued - C::STAGES); j < w_issued; ++j)
+      if (!mbar_wait(&wfull[j % C::STAGES], (unsigned)(j / C::STAGES) & 1u)) atomicOr(s_flag, (unsigned)kErrTimeout);
+  }
   pdl_launch_dependents();
   __syncthreads();
   const bool fin_ok = mbar_wait(fin, 0);
