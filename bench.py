@@ -257,7 +257,10 @@ def tc_roofline(Q, torch, peaks):
     peak = peaks.get("bf16_tflops_sustained") or 1400.0
     ach = fl / dt / 1e12
     return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
-            "traffic": TC_TRAFFIC_BYTES, "kernel": "tc_proj_kernel (tcgen05 Q4 projection) k=2048 n=6144 m=64",
+            "traffic": TC_TRAFFIC_BYTES,
+            "kernel": "tc_proj_kernel (tcgen05 Q4 projection, weights dequantised in the kernel, as "
+                      "qtts_q4_gemv_dev runs it; the frame's layer projections copy expanded operand tiles) "
+                      "k=2048 n=6144 m=64",
             "us_per_launch": dt * 1e6, "algorithmic_flops": fl,
             "executed_tflops": 3 * (((m + 15) // 16 * 16) / m) * ach, "weight_gbs": q4_bytes(k, n) / dt / 1e9,
             "peak_kind": "bf16_tflops_sustained (measured)" if "bf16_tflops_sustained" in peaks else "fallback"}
