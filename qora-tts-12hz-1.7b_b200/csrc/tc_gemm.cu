@@ -85,14 +85,17 @@ constexpr int kErrTimeout = kErrWaitExpired, kErrFp16Range = kErrFp16Input;     
 constexpr int kRawRow = 80;                       // raw packed row stride: 64 B + pad (conflict-free 16 B reads)
 constexpr int kRawMat = TK * kRawRow + TK * 8;     // one matrix's raw stage: packed rows + 4 f16 scales per row
 
-template <int NM>
+// CMP (compact): expanded weights and one input-row pass -- X halves of 64
+// rows and no raw ring, which leaves room for a fourth single-matrix stage.
+template <int NM, bool CMP = false>
 struct TcCfg {
-  static constexpr int STAGES = NM == 1 ? 3 : 2;             // operand stages (fp16 hi/lo, UMMA layout)
-  static constexpr int RS = NM == 1 ? 5 : 3;                 // raw weight stages in flight (cp.async ring)
-  static constexpr int STAGE_BYTES = 2 * A_BYTES + 2 * NM * B_BYTES;
+  static constexpr int XB = CMP ? A_BYTES / 2 : A_BYTES;    // bytes per input-row operand half
+  static constexpr int STAGES = NM == 1 ? (CMP ? 4 : 3) : 2;  // operand stages (fp16 hi/lo, UMMA layout)
+  static constexpr int RS = CMP ? 2 : (NM == 1 ? 5 : 3);     // raw weight stages in flight (cp.async ring)
+  static constexpr int STAGE_BYTES = 2 * XB + 2 * NM * B_BYTES;
   static constexpr int PIPE_BYTES = STAGES * STAGE_BYTES;
   static constexpr int RAW_STAGE = NM * kRawMat;
-  static constexpr int RAW_BYTES = RS * RAW_STAGE;
+  static constexpr int RAW_BYTES = CMP ? 0 : RS * RAW_STAGE;  // the compact form has no raw ring
   static constexpr int RED_BYTES = NM * TM * kRedLd * 4;     // epilogue staging, over the operand stages
   static_assert(RED_BYTES <= PIPE_BYTES, "staging must fit the operand stages");
   static constexpr int AUX = PIPE_BYTES + RAW_BYTES;
@@ -296,15 +299,16 @@ struct ARegs {
 // Grid (2 * ntiles, S, ceil(M / 128)), cluster (1, S, 1), 512 threads.
 template <int NM, int EPI, int NP, bool WX>
 __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, const FrameCodes fc) {
-  using C = TcCfg<NM>;
+  using C = TcCfg<NM, WX && NP == 1>;
   extern __shared__ __align__(1024) uint8_t tsm[];
+  static_assert(C::STAGES <= 4, "barrier area holds 4 stages");
   uint64_t* mma_done = reinterpret_cast<uint64_t*>(tsm + C::AUX);  // [STAGES] MMAs of the stage drained
-  uint64_t* full = mma_done + C::STAGES;                             // [STAGES] operands of the stage written
-  uint64_t* fin = full + C::STAGES;                                  // every MMA drained
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tsm + C::AUX + 64);
-  unsigned* s_flag = reinterpret_cast<unsigned*>(tsm + C::AUX + 96);
+  uint64_t* full = mma_done + 4;                                     // [STAGES] operands of the stage written
+  uint64_t* wfull = full + 4;                                        // [STAGES] (WX) weight tiles of the stage landed
+  uint64_t* fin = wfull + 4;                                         // every MMA drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tsm + C::AUX + 104);
+  unsigned* s_flag = reinterpret_cast<unsigned*>(tsm + C::AUX + 112);
   float* s_inv = reinterpret_cast<float*>(tsm + C::AUX + 128);  // [128]
-  uint64_t* wfull = reinterpret_cast<uint64_t*>(tsm + C::AUX + 640);  // [STAGES] (WX) weight tiles of the stage landed
   float* red = reinterpret_cast<float*>(tsm);                   // epilogue staging [NM][128][kRedLd]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -391,8 +395,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
     for (int a = 0; a < NM; ++a) {
       const Q4Mat& Mt = d.mat[NM == 2 ? a : mat];
       const uint8_t* src = Mt.wx + ((size_t)(tcol / TN) * nks_all + (ks0 + i)) * (2 * B_BYTES);
-      bulk_g2s(st_a + 2 * A_BYTES + a * B_BYTES, src, B_BYTES, &wfull[b]);
-      bulk_g2s(st_a + 2 * A_BYTES + (NM + a) * B_BYTES, src + B_BYTES, B_BYTES, &wfull[b]);
+      bulk_g2s(st_a + 2 * C::XB + a * B_BYTES, src, B_BYTES, &wfull[b]);
+      bulk_g2s(st_a + 2 * C::XB + (NM + a) * B_BYTES, src + B_BYTES, B_BYTES, &wfull[b]);
     }
   };
 
@@ -421,7 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
     for (int i = tid; i < C::STAGES * 2 * zrows * (TK / 8); i += kThreads) {
       // rows fastest: 8 consecutive threads fill 8 different 16-byte bank groups
       const int r = Mv + i % zrows, c = (i / zrows) % (TK / 8), h = i / (zrows * (TK / 8));  // h: stage*2 + half
-      uint8_t* base = tsm + (h >> 1) * C::STAGE_BYTES + (h & 1) * A_BYTES;
+      uint8_t* base = tsm + (h >> 1) * C::STAGE_BYTES + (h & 1) * C::XB;
       *reinterpret_cast<uint4*>(base + (r >> 3) * 1024 + c * 128 + (r & 7) * 16) = make_uint4(0, 0, 0, 0);
     }
   }
@@ -600,11 +604,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       if (!WX && i + C::RS - 1 < nst) issue_b(ks0 + i + C::RS - 1, (i + C::RS - 1) % C::RS);
       cp_async_commit();
       if (a_thr) {
-        store_a(ks0 + i, ac, st, st + A_BYTES);
-        if (!WX && at < 4 * kChunksRem) store_word(st + 2 * A_BYTES, i % C::RS, kBConv * NM + at % kChunksRem, at / kChunksRem);
+        store_a(ks0 + i, ac, st, st + C::XB);
+        if (!WX && at < 4 * kChunksRem) store_word(st + 2 * C::XB, i % C::RS, kBConv * NM + at % kChunksRem, at / kChunksRem);
       } else if (!WX && tid < kBConv) {
 #pragma unroll
-        for (int j = 0; j < NM; ++j) store_chunk(st + 2 * A_BYTES, i % C::RS, tid + j * kBConv);
+        for (int j = 0; j < NM; ++j) store_chunk(st + 2 * C::XB, i % C::RS, tid + j * kBConv);
       }
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // st.shared -> visible to tcgen05.mma
       mbar_arrive(&full[b]);
@@ -618,11 +622,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       if (!__all_sync(0xffffffffu, f_ok)) { ok = false; break; }
       if (lane == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t xhi = tsm_a + b * C::STAGE_BYTES, xlo = xhi + A_BYTES;  // input rows (MMA operand B)
+        const uint32_t xhi = tsm_a + b * C::STAGE_BYTES, xlo = xhi + C::XB;  // input rows (MMA operand B)
 #pragma unroll
         for (int a = 0; a < NM; ++a) {
           // weights (MMA operand A)
-          const uint32_t whi = xhi + 2 * A_BYTES + a * B_BYTES, wlo = xhi + 2 * A_BYTES + (NM + a) * B_BYTES;
+          const uint32_t whi = xhi + 2 * C::XB + a * B_BYTES, wlo = xhi + 2 * C::XB + (NM + a) * B_BYTES;
           const uint32_t dm = tmem + (uint32_t)(a * 2 * TN), dc = dm + TN;
 #pragma unroll
           for (int kk = 0; kk < TK / 16; ++kk) {
@@ -885,7 +889,8 @@ static cudaError_t launch_np(const GemvDesc& d, const FrameCodes& fc, cudaStream
   o.pdl = d.pdl != 0;
   o.cluster_y = (unsigned)S;
   const dim3 grid(2 * d.ntiles, S, (d.M + TM - 1) / TM);
-  return launch_k(tc_proj_kernel<NM, EPI, NP, WX>, grid, dim3(kThreads), (size_t)TcCfg<NM>::SMEM, st, o, d, fc);
+  return launch_k(tc_proj_kernel<NM, EPI, NP, WX>, grid, dim3(kThreads), (size_t)TcCfg<NM, WX && NP == 1>::SMEM, st,
+                  o, d, fc);
 }
 
 template <int NM, int EPI>
