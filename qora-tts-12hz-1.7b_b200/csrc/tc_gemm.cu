@@ -10,11 +10,12 @@
 // one K slice; the S K-slices of a tile form a thread-block cluster (1, S, 1),
 // with S chosen so that every cluster of the launch is resident in one wave.
 //
-// Main loop, per 64-deep K stage (2-3 stages in flight):
+// Main loop, per 64-deep K stage (2-4 operand stages in flight):
 //   * the raw Q4 tile of the stage (packed bytes + f16 scales) has been
 //     streaming into a shared-memory ring by cp.async 3-5 stages ahead;
-//   * warps 0-6 dequantise it and warps 7-14 normalise the input rows (held
-//     in registers one stage ahead), into
+//   * warps 0-6 dequantise it (a thread per 16-byte chunk of 32 columns) and
+//     warps 7-14 normalise the input rows (held in registers one stage
+//     ahead) and take the leftover chunks word by word, into
 //     shared memory: X = the normalised input rows, W = the Q4 weights, each as
 //     two fp16 operands hi + lo with lo = fp16((v - hi) * 2^11).  The Q4 value
 //     (q-8)*scale has at most 14 significant bits, so hi + lo holds it
@@ -47,12 +48,14 @@
 //   X (K-major):  row r, k-chunk c (8 elements) at (r/8)*1024 + c*128 + (r%8)*16
 //                 -> LBO 128 B (next 8-deep K chunk), SBO 1024 B (next 8 rows)
 //   W (MN-major): k row j, column group g (8 columns) at g*1024 + (j/8)*128 + (j%8)*16
-//                 -> LBO 128 B (next 8-deep K group), SBO 1024 B (next 8 columns)
+//                 -> LBO 128 B (next 8-deep K group), SBO 1024 B (next 8 columns);
+//                 a 16-byte row holds the group's columns in the order
+//                 0,4,1,5,2,6,3,7 (tc_col maps accumulator lanes back)
 // A 16-deep MMA step advances both start addresses by 256 B.
 //
 // Every mbarrier wait is bounded in time; on expiry the kernel records an
-// error flag, waits (bounded) for its own MMAs, frees its TMEM and still
-// takes part in the cluster barriers, so no CTA is left waiting.
+// error flag, waits (bounded) for its own copies and MMAs, frees its TMEM
+// and still takes part in the cluster barriers, so no CTA is left waiting.
 #include <cuda_fp16.h>
 
 #include <algorithm>
