@@ -134,7 +134,7 @@ void attn_init_attributes();
 // dequantising them; the predictor's are otherwise dequantised 15 times per
 // frame.  Optional: without the memory, or with QTTS_EXPAND=1 (predictor
 // only) / 0 (none), the other launches dequantise in the kernel.
-static void expand_predictor(Model* m) {
+static void expand_weights(Model* m) {
   static const int mode = [] {
     const char* v = getenv("QTTS_EXPAND");
     return v ? atoi(v) : 2;
@@ -283,7 +283,7 @@ static int model_load(const char* path, int device, Model** out) {
   attn_init_attributes();
   tc_init_attributes();
   pred_persist_init_attributes();
-  expand_predictor(m);
+  expand_weights(m);
   *out = m;
   return QTTS_OK;
 }
