@@ -121,3 +121,15 @@ def test_bad_arguments_fail_cleanly_without_gpu(qtts):
     x = np.zeros(4, np.float32)
     assert qtts.lib.qtts_generate_frames(None, 1) == qtts.ERR_BADARG
     del x
+
+
+def test_quantize_arguments_rejected_on_the_host(qtts):
+    # gemv.rs:92-130 needs n % 32 == 0; these are refused before any CUDA call
+    with pytest.raises(qtts.QttsError) as e:
+        qtts.quantize_f32_to_q4(np.zeros((2, 48), np.float32), 2, 48)
+    assert e.value.code == qtts.ERR_BADARG
+    with pytest.raises(qtts.QttsError) as e:
+        qtts.quantize_f32_to_q4(np.zeros((2, 64), np.float32), 3, 64)  # size mismatch
+    assert e.value.code == qtts.ERR_BADARG
+    assert qtts.lib.qtts_q4_quantize(None, 2, 64, None, None) == qtts.ERR_BADARG
+    assert qtts.lib.qtts_q4_quantize_dev(None, 2, 64, None, None, None) == qtts.ERR_BADARG
