@@ -106,12 +106,12 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnDesc d) {
       float dp[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) dp[u] = q[g].x * k4[u].x + q[g].y * k4[u].y + q[g].z * k4[u].z + q[g].w * k4[u].w;
-      // round 1 (xor 16): lanes < 16 keep positions 0, 1; lanes >= 16 keep 2, 3
+      // step 1 (xor 16): lanes < 16 keep positions 0, 1; lanes >= 16 keep 2, 3
       float a0 = hi16 ? dp[2] : dp[0], a1 = hi16 ? dp[3] : dp[1];
       const float b0 = hi16 ? dp[0] : dp[2], b1 = hi16 ? dp[1] : dp[3];
       a0 += __shfl_xor_sync(0xffffffffu, b0, 16);
       a1 += __shfl_xor_sync(0xffffffffu, b1, 16);
-      // round 2 (xor 8): lane group j = lane / 8 keeps position j
+      // step 2 (xor 8): lane group j = lane / 8 keeps position j
       float c = hi8 ? a1 : a0;
       c += __shfl_xor_sync(0xffffffffu, hi8 ? a0 : a1, 8);
       c += __shfl_xor_sync(0xffffffffu, c, 4);

@@ -73,9 +73,11 @@ __device__ __forceinline__ float q4_value(const uint8_t* packed_row, const __hal
 // SiLU exactly as gemv.rs:449-451 writes it (x / (1 + exp(-x))).
 __device__ __forceinline__ float silu_ref(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x))); }
 
-// Orderable 32-bit key of an f32 (total order of non-NaN values).
+// Orderable 32-bit key of an f32 (total order of non-NaN values).  -0.0 is
+// first turned into +0.0 (x + 0 rounds -0 to +0), so the two zeros share a
+// key as they compare equal under partial_cmp (code_predictor.rs:328-334).
 __device__ __forceinline__ uint32_t f32_order_key(float f) {
-  uint32_t u = __float_as_uint(f);
+  uint32_t u = __float_as_uint(__fadd_rn(f, 0.0f));
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
@@ -88,6 +90,10 @@ __device__ __forceinline__ uint32_t f32_order_key(float f) {
 // evaluation order with explicit round-to-nearest double ops; it was checked
 // bit-for-bit against the host expf on every float in [-110, 90].
 // Table entries: bits of the correctly rounded 2^(i/32) minus (i << 47).
+// Method, table layout and polynomial coefficients: the expf of ARM's
+// optimized-routines project (licence: MIT OR Apache-2.0 WITH
+// LLVM-exception), the code glibc imported for its expf; the values here
+// were recomputed (exp2l) and the steps restated from that published method.
 __device__ __constant__ uint64_t kExp2Tab[32] = {
     0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
     0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,

@@ -25,24 +25,6 @@ namespace qtts {
 static thread_local std::string g_err;
 void set_error(const std::string& msg) { g_err = msg; }
 
-// Programmatic dependent launch for the frame's kernels; QTTS_PDL=0 turns it
-// off (A/B measurements).
-bool pdl_enabled() {
-  static const bool on = [] {
-    const char* v = getenv("QTTS_PDL");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
-// Tensor-core path for projections with M >= kTcMinRows; QTTS_TC=0 keeps
-// them on the CUDA-core kernels (A/B measurements).
-bool tc_enabled() {
-  static const bool on = [] {
-    const char* v = getenv("QTTS_TC");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
 int fail(int code, const std::string& msg) {
   g_err = msg;
   return code;
@@ -132,18 +114,11 @@ void attn_init_attributes();
 // tensor-core operand layout (4 bytes per weight: ~6 GB for 1.7B, of the
 // GPU's 180 GB), so those launches copy operand tiles instead of
 // dequantising them; the predictor's are otherwise dequantised 15 times per
-// frame.  Optional: without the memory, or with QTTS_EXPAND=1 (predictor
-// only) / 0 (none), the other launches dequantise in the kernel.
+// frame.  Optional: without the memory the launches dequantise in the kernel.
 static void expand_weights(Model* m) {
-  static const int mode = [] {
-    const char* v = getenv("QTTS_EXPAND");
-    return v ? atoi(v) : 2;
-  }();
-  if (mode == 0 || !tc_enabled()) return;
   std::vector<Q4Mat*> mats;
-  if (mode >= 2)  // the talker's layer projections as well (QTTS_EXPAND=1: predictor only)
-    for (auto& L : m->tl)
-      for (Q4Mat* w : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down}) mats.push_back(w);
+  for (auto& L : m->tl)
+    for (Q4Mat* w : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down}) mats.push_back(w);
   for (auto& L : m->pl)
     for (Q4Mat* w : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down}) mats.push_back(w);
   if (m->has_proj) mats.push_back(&m->input_proj);
@@ -282,7 +257,6 @@ static int model_load(const char* path, int device, Model** out) {
   gemv_init_attributes();
   attn_init_attributes();
   tc_init_attributes();
-  pred_persist_init_attributes();
   expand_weights(m);
   *out = m;
   return QTTS_OK;
@@ -347,11 +321,7 @@ int gemv_wave_clusters(const GemvDesc& g) {
 // With a cluster-reduced K split, every (tile, row block) is one cluster and
 // all of them should be resident in one wave: lower S until they fit.
 static void fit_split_to_wave(GemvDesc& g) {
-  static const bool on = [] {  // QTTS_WAVE_FIT=0: keep choose_split's S (measurements)
-    const char* v = getenv("QTTS_WAVE_FIT");
-    return !(v && v[0] == '0');
-  }();
-  if (g.tc || !g.cluster || !on) return;
+  if (g.tc || !g.cluster) return;
   const long units = (long)g.ntiles * ceil_div(g.M, g.mb);
   for (int S = g.S; S >= 1; --S) {
     GemvDesc t = g;
@@ -373,13 +343,8 @@ void choose_split(int sm_count, GemvDesc& g) {
   g.mb = g.M <= kDecMaxM ? 1 : (g.paired ? 2 : 4);
   const int zb = ceil_div(g.M, g.mb);
   const int target = 2 * sm_count;
-  static const int max_splits = [] {  // QTTS_GEMV_MAX_SPLITS caps S (measurements)
-    const char* v = getenv("QTTS_GEMV_MAX_SPLITS");
-    const int s = v ? atoi(v) : 0;
-    return s > 0 ? std::min(s, kMaxClusterSplits) : kMaxClusterSplits;
-  }();
   int S = (int)std::lround((double)target / (double)(g.ntiles * zb));
-  S = std::max(1, std::min(std::min(S, max_splits), ceil_div(g.k, 32)));
+  S = std::max(1, std::min(std::min(S, kMaxClusterSplits), ceil_div(g.k, 32)));
   int rps = ceil_div(ceil_div(g.k, S), 32) * 32;
   rps = std::min(rps, 2048);
   g.rows_per_split = rps;
@@ -396,54 +361,16 @@ static int dalloc(T** p, size_t count, std::vector<void*>* track = nullptr) {
   return QTTS_OK;
 }
 
-// One decode row whose register-resident K slices would not fit one wave:
-// stage each CTA's slice in shared memory instead, one CTA per SM (about
-// sm_count / tiles K slices), when the slice and its cluster fit.  Opt-in
-// (QTTS_STAGED=1): with one 8-warp CTA per SM the dequant-FMA runs at a low
-// issue rate, and on the talker's gate/up it measured slower than the
-// general kernel it replaces (321 vs 338 frames/s at batch 1).
-static void try_staged(int sm_count, GemvDesc& g) {
-  static const bool on = [] {
-    const char* v = getenv("QTTS_STAGED");
-    return v && v[0] == '1';
-  }();
-  if (!on || g.M != 1 || gemv_uses_decode_kernel(g) || !gemv_staged_eligible(g)) return;
-  GemvDesc t = g;
-  t.staged = 1;
-  t.cluster = 1;
-  for (int S = std::min(kMaxClusterSplits, std::max(1, sm_count / g.ntiles)); S >= 1; --S) {
-    const int rps = ceil_div(ceil_div(g.k, S), 32) * 32;
-    if (rps > 32 * kDecRowsStg) return;  // fewer slices are only longer
-    t.rows_per_split = rps;
-    t.S = ceil_div(g.k, rps);
-    if (gemv_smem_bytes(t) > (size_t)kDecStgMaxSmem) return;
-    if (gemv_wave_clusters(t) >= g.ntiles) {
-      g = t;
-      return;
-    }
-  }
-}
-
 // Decode rows whose register-resident K slices fit the decode kernel only
 // with more clusters than one wave holds (the talker's gate/up pair): keep
 // about two CTAs per SM and reduce the slices through global memory (the
 // last CTA of a tile to arrive sums them) instead of a cluster, which frees
-// the CTAs from cluster placement.  QTTS_GLOBAL_SPLIT=0 turns it off.
+// the CTAs from cluster placement.
 static void try_global_split(Session& s, GemvDesc& g) {
-  static const int mode = [] {  // 0 off, 1 in place of the general kernel, 2 also when it adds CTAs
-    const char* v = getenv("QTTS_GLOBAL_SPLIT");
-    return v ? atoi(v) : 1;
-  }();
-  if (mode == 0 || g.M > kDecMaxM || g.tc) return;
-  if (mode == 1 && gemv_uses_decode_kernel(g)) return;
+  if (g.M > kDecMaxM || g.tc || gemv_uses_decode_kernel(g)) return;
   GemvDesc t = g;
   choose_split(s.m->sm_count, t);
   t.cluster = 0;
-  if (mode == 2) {  // about two CTAs per SM, beyond the cluster limit
-    const int S = std::max(1, std::min(kMaxGlobalSplits, (int)std::lround(2.0 * s.m->sm_count / (t.ntiles * t.M))));
-    t.rows_per_split = ceil_div(ceil_div(t.k, S), 32) * 32;
-    t.S = ceil_div(t.k, t.rows_per_split);
-  }
   const int nrmax = t.paired ? kDecRowsNM2 : kDecRowsNM1;
   while (t.rows_per_split > 32 * nrmax && t.S < kMaxGlobalSplits) {
     const int S = t.S + 1;
@@ -464,9 +391,8 @@ static int plan_gemv(Session& s, GemvDesc& g) {
   g.pdl = 1;
   fit_split_to_wave(g);
   try_global_split(s, g);
-  try_staged(s.m->sm_count, g);
   g.err_flag = s.err_flag;
-  if (g.M >= kTcMinRows && tc_enabled()) {
+  if (g.M >= kTcMinRows) {
     tc_plan(s.m->sm_count, g);  // one tcgen05 kernel: prologue, GEMM, split-K, epilogue
     g.part = s.part;
     const size_t zt = (size_t)ceil_div(g.M, kTcRows);
@@ -474,15 +400,6 @@ static int plan_gemv(Session& s, GemvDesc& g) {
         ((size_t)tc_splits(g) * g.M * g.ncols > s.part_floats || 2 * (size_t)g.ntiles * zt > s.n_counters))
       return fail(QTTS_ERR_OOM, "split-K scratch too small for this projection");
   }
-  static const bool log_plans = [] {
-    const char* v = getenv("QTTS_PLAN_LOG");
-    return v && v[0] == '1';
-  }();
-  if (log_plans)
-    fprintf(stderr, "qtts plan: epi %d k %d ncols %d M %d -> %s S %d rows/split %d\n", g.epi_kind, g.k, g.ncols, g.M,
-            g.tc ? "tcgen05" : (g.staged ? "cuda-core staged" : (g.cluster ? "cuda-core" : "cuda-core global-split")),
-            g.tc ? tc_splits(g) : g.S,
-            g.tc ? g.tc_ks * kTcK : g.rows_per_split);
   const size_t zb = (size_t)ceil_div(g.M, g.mb);
   if ((size_t)g.ntiles * zb > s.n_counters || zb > 4096) return fail(QTTS_ERR_OOM, "tile counter array too small");
   g.counters = s.counters;
@@ -493,33 +410,15 @@ static int plan_gemv(Session& s, GemvDesc& g) {
   return QTTS_OK;
 }
 
-// QTTS_GLU_SPLIT=0 keeps the paired gate/up launch for one decode row too
-// (measurements).
-static bool glu_split_enabled() {
-  static const bool on = [] {
-    const char* v = getenv("QTTS_GLU_SPLIT");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
-
 // The projection planned last in the current op list: the next one planned
 // fills in its L2-prefetch targets (GemvDesc::pf_*), so every projection
-// pulls its successor's weights into L2 while it runs.  QTTS_L2_PREFETCH=0
-// turns this off (measurements).
+// pulls its successor's weights into L2 while it runs.
 static thread_local std::shared_ptr<GemvDesc> g_prev_gemv;
-static bool l2_prefetch_enabled() {
-  static const bool on = [] {
-    const char* v = getenv("QTTS_L2_PREFETCH");
-    return !(v && v[0] == '0');
-  }();
-  return on;
-}
 static void chain_reset() { g_prev_gemv.reset(); }
 
 static Op gemv_op(const GemvDesc& g, const FrameCodes& fc = FrameCodes{}) {
   auto sp = std::make_shared<GemvDesc>(g);
-  if (g_prev_gemv && l2_prefetch_enabled()) {
+  if (g_prev_gemv) {
     GemvDesc& p = *g_prev_gemv;
     const int nm = g.paired ? 2 : g.nmat;
     for (int i = 0; i < nm && i < 3; ++i) {
@@ -592,11 +491,6 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
     AttnDesc a;
     a.q = s.q; a.ldq = qd; a.out = s.attn; a.ldo = qd; a.kv = io.kv; a.rp = io.rp;
     a.heads = io.heads; a.kv_heads = io.kvh; a.M = io.M; a.nsplit = io.nsplit;
-    static const bool kv_pf = [] {  // QTTS_ATTN_PREFETCH=0: no K / V L2 prefetch (measurements)
-      const char* v = getenv("QTTS_ATTN_PREFETCH");
-      return !(v && v[0] == '0');
-    }();
-    a.l2_prefetch = kv_pf ? 1 : 0;
     if (a.nsplit > 1) {
       const size_t need = (size_t)io.M * io.kvh * a.nsplit * (io.heads / io.kvh) * kAttnRec;
       if (need > s.apart_floats || (size_t)io.M * io.kvh > s.n_acounters)
@@ -622,7 +516,7 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
   gs.epi.act_silu = 1;  // matrix 0 = gate
   use_ssq(gs, true);
   bool split_glu = false;
-  if (io.M <= kDecMaxM && glu_split_enabled() && (size_t)2 * io.inter * io.M <= s.h_floats) {
+  if (io.M <= kDecMaxM && (size_t)2 * io.inter * io.M <= s.h_floats) {
     RC(plan_gemv(s, gs));
     GemvDesc dg = dn;
     dg.x_glu = io.inter;
@@ -655,13 +549,10 @@ static KvDesc pred_kv(Session& s, int layer) {
   k.n_layers = s.m->d.p_layers; k.kv_heads = s.m->d.p_kv_heads; k.layer = layer;
   return k;
 }
+// Attention splits of the talker cache: 32 positions per split, about four
+// CTAs per SM at most.
 static int talker_nsplit(Session& s, int M) {
-  static const int per_split = [] {  // QTTS_ATTN_CHUNK: cache positions per split (measurements)
-    const char* v = getenv("QTTS_ATTN_CHUNK");
-    const int c = v ? atoi(v) : 0;
-    return c > 0 ? c : 32;
-  }();
-  const int byL = ceil_div(s.maxP, per_split);
+  const int byL = ceil_div(s.maxP, 32);
   const int byPar = std::max(1, ceil_div(4L * s.m->sm_count, (long)M * s.m->d.t_kv_heads));
   return std::max(1, std::min(kMaxClusterSplits, std::min(byL, byPar)));
 }
@@ -760,64 +651,6 @@ static int add_predictor(Session& s, std::vector<Op>& ops, int B, bool frame_mod
   return QTTS_OK;
 }
 
-// The predictor of one utterance as one persistent cooperative kernel
-// (pred_persist.cu) instead of ~400 launches, opt-in with QTTS_PERSIST=1.  Its
-// phases cost about what a programmatic-dependent-launch graph node costs (a
-// grid barrier ~1.2 us plus the global round trips of the phase), so the
-// launch-per-projection plan stays the default.  `used` is false when the
-// shape is not covered.
-static bool persist_enabled() {
-  static const bool on = [] {
-    const char* v = getenv("QTTS_PERSIST");
-    return v && v[0] == '1';
-  }();
-  return on;
-}
-
-static int add_predictor_persistent(Session& s, std::vector<Op>& ops, bool frame_mode, const FrameCodes& fc,
-                                    bool& used) {
-  used = false;
-  const Model& m = *s.m;
-  const qtts_dims& d = m.d;
-  if (!persist_enabled() || !s.pp_sync || d.p_layers > kPPMaxLayers) return QTTS_OK;
-  PredPersistDesc p;
-  p.pH = d.p_hidden; p.heads = d.p_heads; p.kvh = d.p_kv_heads; p.inter = d.p_inter; p.layers = d.p_layers;
-  p.groups = d.p_groups; p.t_hidden = d.t_hidden; p.rope_rows = d.p_max_pos;
-  for (int l = 0; l < d.p_layers; ++l) {
-    const DLayer& L = m.pl[l];
-    p.L[l].q = L.q; p.L[l].k = L.k; p.L[l].v = L.v; p.L[l].o = L.o;
-    p.L[l].gate = L.gate; p.L[l].up = L.up; p.L[l].down = L.down;
-    p.L[l].q_norm = L.q_norm; p.L[l].k_norm = L.k_norm; p.L[l].in_norm = L.in_norm; p.L[l].post_norm = L.post_norm;
-  }
-  p.proj = m.input_proj; p.proj_b = m.input_proj_b;
-  for (int g = 0; g < d.p_groups && g < kMaxGroups; ++g) {
-    if (g < (int)m.p_emb.size()) p.emb[g] = m.p_emb[g];
-    if (g < (int)m.lm.size()) p.lm[g] = m.lm[g];
-  }
-  p.final_norm = m.p_final; p.cos = m.p_cos; p.sin = m.p_sin;
-  p.kv = s.pkv_pool; p.pin = s.pin; p.part = s.part; p.X = s.pp_X; p.attn = s.attn;
-  p.bar = reinterpret_cast<unsigned*>(s.pp_sync); p.keys = s.pp_sync + 1; p.err_flag = s.err_flag;
-  p.fc = fc; p.frame_mode = frame_mode ? 1 : 0; p.codes_plain = s.codes_plain;
-  if (const char* v = getenv("QTTS_PP_SPLITS")) {  // "proj,qkv,o,gu,down" K slices (measurements)
-    int a[5];
-    if (sscanf(v, "%d,%d,%d,%d,%d", &a[0], &a[1], &a[2], &a[3], &a[4]) == 5) {
-      p.s_proj = a[0]; p.s_qkv = a[1]; p.s_o = a[2]; p.s_gu = a[3]; p.s_down = a[4];
-    }
-  }
-  if (!pred_persist_supported(p) || pred_persist_part_floats(p) > s.part_floats) return QTTS_OK;
-  g_occ_query = true;
-  g_occ_clusters = 0;
-  launch_pred_persist(p, 1, nullptr);
-  g_occ_query = false;
-  const int grid = std::min(128, g_occ_clusters * m.sm_count);
-  if (grid < d.p_heads) return QTTS_OK;  // the attention phase needs one CTA per query head
-  unsigned long long* sync = s.pp_sync;
-  ops.push_back([sync](cudaStream_t st) { return cudaMemsetAsync(sync, 0, 4 * sizeof(unsigned long long), st); });
-  ops.push_back([p, grid](cudaStream_t st) { return launch_pred_persist(p, grid, st); });
-  used = true;
-  return QTTS_OK;
-}
-
 // embed_text_token for rows of token ids (talker.rs:105-116):
 // fc1(emb) + b1 -> silu -> fc2 + b2.
 static int add_text_proj(Session& s, std::vector<Op>& ops, const uint32_t* tok_dev, int n, float* h1, float* out,
@@ -882,7 +715,7 @@ static void session_free_all(Session* s) {
   free_generation(*s);
   void* bufs[] = {s->kv_pool, s->page_table, s->pkv_pool, s->slots, s->x, s->pin, s->q, s->attn, s->h,
                   s->px, s->px1, s->logits, s->xpre, s->hid1, s->part, s->counters, s->counters2, s->keys,
-                  s->apart, s->acounters, s->err_flag, s->codes_plain, s->io, s->ssq_t, s->ssq_p, s->ssq_p1, s->pp_X, s->pp_sync};
+                  s->apart, s->acounters, s->err_flag, s->codes_plain, s->io, s->ssq_t, s->ssq_p, s->ssq_p1};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (s->st) cudaStreamDestroy(s->st);
@@ -941,8 +774,6 @@ static int session_create(Model* m, int maxB, int maxP, Session** out) {
   A(&s->ssq_t, (size_t)s->rows * kSsqLd);
   A(&s->ssq_p, (size_t)2 * maxB * kSsqLd);
   A(&s->ssq_p1, (size_t)maxB * kSsqLd);
-  A(&s->pp_X, (size_t)4 * d.p_hidden);  // persistent predictor: residual rows, barrier counter + argmax keys
-  A(&s->pp_sync, (size_t)4);
   if (rc == QTTS_OK) {  // pages: slot b owns pages [b*pps, (b+1)*pps)
     std::vector<int> pt((size_t)maxB * s->pages_per_sess);
     for (size_t i = 0; i < pt.size(); ++i) pt[i] = (int)i;
@@ -984,9 +815,7 @@ static int build_frame_ops(Session& s, std::vector<Op>& ops, bool dumps) {
   const Q4Mat ce = m.codec_emb;
   float* sem = s.pin + H;
   ops.push_back([=](cudaStream_t st) { return launch_embed_code0(ce, slots, B, sem, 2L * H, st); });
-  bool persistent = false;
-  if (B == 1) RC(add_predictor_persistent(s, ops, true, fc, persistent));
-  if (!persistent) RC(add_predictor(s, ops, B, true, fc));
+  RC(add_predictor(s, ops, B, true, fc));
   FuseDesc fd;
   fd.x = s.x; fd.ldx = H; fd.codec_emb = m.codec_emb; fd.group_emb = m.d_group_emb; fd.n_groups = d.p_groups;
   fd.trail = s.trail; fd.max_trail = s.max_trail; fd.tts_pad = s.tts_pad; fd.B = B; fd.H = H; fd.fc = fc;
@@ -1290,9 +1119,7 @@ static int predict_call(Session& s, const float* hidden, const float* sem, uint3
   CK(cudaMemcpyAsync(s.pin, hidden, sizeof(float) * H, cudaMemcpyHostToDevice, s.st));
   CK(cudaMemcpyAsync(s.pin + H, sem, sizeof(float) * H, cudaMemcpyHostToDevice, s.st));
   std::vector<Op> ops;
-  bool persistent = false;
-  RC(add_predictor_persistent(s, ops, false, FrameCodes{}, persistent));
-  if (!persistent) RC(add_predictor(s, ops, 1, false, FrameCodes{}));
+  RC(add_predictor(s, ops, 1, false, FrameCodes{}));
   RC(run_ops(s, ops));
   uint32_t c[kMaxGroups];
   CK(cudaMemcpyAsync(c, s.codes_plain, sizeof(c), cudaMemcpyDeviceToHost, s.st));
@@ -1355,7 +1182,7 @@ static int gemv_plan_standalone(int k, int n, int m, GemvDesc& g) {
   w.n = n;
   g = gemv_base(EPI_STORE, {w}, false, m);
   choose_split(sms, g);
-  if (m >= kTcMinRows && k % 4 == 0 && n % 64 == 0 && tc_enabled()) tc_plan(sms, g);
+  if (m >= kTcMinRows && k % 4 == 0 && n % 64 == 0) tc_plan(sms, g);
   return QTTS_OK;
 }
 

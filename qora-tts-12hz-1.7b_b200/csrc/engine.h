@@ -77,9 +77,6 @@ struct Session {
   // per-256-column sums of squares of residual rows (talker, predictor
   // prefill rows, predictor decode rows), row stride kSsqLd
   float *ssq_t = nullptr, *ssq_p = nullptr, *ssq_p1 = nullptr;
-  // persistent predictor: residual rows [4][p_hidden]; [0] barrier counter, [1..2] argmax keys
-  float* pp_X = nullptr;
-  unsigned long long* pp_sync = nullptr;
   size_t io_floats = 0;
   // generation
   int B = 0, max_frames = 0, max_trail = 0;

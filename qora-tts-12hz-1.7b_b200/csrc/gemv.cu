@@ -14,7 +14,7 @@
 // thread-block cluster and reduce their partials in split order
 // (deterministic).
 //
-// gemv_dec_kernel (one input row, the batch-1 decode path) is shaped for
+// q4mv_dec_kernel (one input row, the batch-1 decode path) is shaped for
 // latency: every weight row of a lane is loaded into registers before the
 // programmatic-dependent-launch wait (weights are never written by an earlier
 // kernel; the next kernel is released once this one's FMAs are done), the
@@ -23,7 +23,7 @@
 // cluster reduction pushes each partial straight into the root CTA's shared
 // memory followed by a single cluster barrier.
 //
-// gemv_q4_kernel (M rows, MB per CTA) serves prefill and batched decode.
+// q4mv_rows_kernel (M rows, MB per CTA) serves prefill and small batches.
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -132,60 +132,22 @@ __device__ __forceinline__ void red_store(float* row, int gi, const float2 (&acc
 }
 __device__ __forceinline__ int red_col(int col) { return (col & ~31) | ((col + 4 * (col >> 5)) & 31); }
 
-// Staged decode variant: the CTA's whole weight slice sits in shared memory,
-// kStgRowBytes per (row, matrix): 128 bytes of packed nibbles (256 columns)
-// then the 8 f16 scales of the row's 8 groups.
-constexpr int kStgRowBytes = 144;
-__device__ __forceinline__ void stg_cp16(uint32_t dst, const void* src, uint32_t src_size) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_size) : "memory");
-}
-// Every 16-byte chunk of rows [r0, r0 + R) x the tile's 256 columns of the NM
-// matrices, issued by all threads before the dependent-launch wait
-// (zero-filled past n; the host checks n % 256 == 0 and 16-byte alignment).
-template <int NM>
-__device__ __forceinline__ void stg_issue(const GemvDesc& d, int mat, int tcol, int r0, int R, uint32_t wst) {
-  const int per_row = NM * 9;
-  for (int c = threadIdx.x; c < R * per_row; c += kGemvThreads) {
-    const int row = c / per_row, rem = c - row * per_row, a = rem / 9, ch = rem - a * 9;
-    const Q4Mat& Mt = d.mat[NM == 2 ? a : mat];
-    const int n = Mt.n;
-    const uint32_t dst = wst + (uint32_t)((row * NM + a) * kStgRowBytes + ch * 16);
-    const size_t grow = (size_t)(r0 + row);
-    if (ch < 8) {
-      const bool v = tcol + ch * 32 < n;
-      stg_cp16(dst, v ? Mt.packed + grow * (n / 2) + tcol / 2 + ch * 16 : Mt.packed, v ? 16u : 0u);
-    } else {
-      const int groups = min(8, max(0, (n - tcol) / 32));
-      stg_cp16(dst, groups ? reinterpret_cast<const uint8_t*>(Mt.scales + grow * (n / 32) + tcol / 32)
-                           : reinterpret_cast<const uint8_t*>(Mt.scales),
-               (uint32_t)(2 * groups));
-    }
-  }
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-
 }  // namespace
 
 // Floats of shared memory before the split-K partial buffer: the CTA
-// reduction buffer, or (staged) the weight slice it overlays when larger.
-__host__ __device__ inline int dec_front_floats(int NM, bool stg, int rows) {
-  const int red = 8 * 4 * NM * kTileN;
-  const int wst = rows * NM * kStgRowBytes / 4;
-  return stg && wst > red ? wst : red;
-}
+// reduction buffer [8 warps][4 row offsets][NM][256].
+__host__ __device__ inline int dec_front_floats(int NM) { return 8 * 4 * NM * kTileN; }
 
 // ===========================================================================
 // Decode kernel: M <= kDecMaxM input rows, one per blockIdx.z
-// STG: the weight slice is staged in shared memory (rows per split up to
-// 32 * NR, no weight registers) instead of held in registers.
-template <int NM, int EPI, int NR, bool STG>
-__global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d, const FrameCodes fc) {
+template <int NM, int EPI, int NR>
+__global__ void __launch_bounds__(kGemvThreads) q4mv_dec_kernel(const GemvDesc d, const FrameCodes fc) {
   extern __shared__ __align__(16) float sm[];
   const bool clustered = d.cluster && d.S > 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int tile = blockIdx.x, split = blockIdx.y, m = blockIdx.z;  // input row m
-  float* red = sm;                                  // [8 warps][4 rr][NM][256] (STG: over the weights)
-  float* pbuf = sm + dec_front_floats(NM, STG, d.rows_per_split);  // [S][NM][256] partials pushed to the root
+  float* red = sm;                                  // [8 warps][4 rr][NM][256]
+  float* pbuf = sm + dec_front_floats(NM);          // [S][NM][256] partials pushed to the root
   float* sbuf = pbuf + kMaxClusterSplits * NM * kTileN;  // 64 floats
   float* ybuf = sbuf + 64;                          // [256]
   uint64_t* mbar = reinterpret_cast<uint64_t*>(ybuf + kTileN);  // root: partials landed
@@ -208,12 +170,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
   const bool gval = gcol < n;
   const int rb0 = warp * 4 + rr;
 
-  // every weight row of this lane (STG: of the CTA, into shared memory) and,
-  // for an RMSNorm prologue, the norm weights of its rows, before waiting on
-  // the previous kernel
-  WBatch<STG ? 1 : NR, NM> wb;
-  if constexpr (STG) stg_issue<NM>(d, mat, tcol, r0, R, smem_addr(sm));
-  else load_batch<NR, NM>(wb, d, mat, r0, R, rb0, gcol, gval, (size_t)n / 2, n / 32);
+  // every weight row of this lane and, for an RMSNorm prologue, the norm
+  // weights of its rows, before waiting on the previous kernel
+  WBatch<NR, NM> wb;
+  load_batch<NR, NM>(wb, d, mat, r0, R, rb0, gcol, gval, (size_t)n / 2, n / 32);
   // Prologue forms compiled per epilogue (the host rejects other pairings):
   // the embedding gather feeds STORE launches (input_proj, text fc1), the
   // attention and GLU inputs feed RESID launches (O, down), RMSNorm feeds the
@@ -373,41 +333,17 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
   for (int a = 0; a < NM; ++a)
 #pragma unroll
     for (int c = 0; c < 16; ++c) acc[a][c] = make_float2(0.0f, 0.0f);
-  if constexpr (STG) {
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    __syncthreads();  // every thread's chunks of the slice have landed
-    const uint8_t* wsb = reinterpret_cast<const uint8_t*>(sm);
+  const WBatch<NR, NM>& wr = wb;
 #pragma unroll
-    for (int i = 0; i < NR; ++i) {
-      const int rb = rb0 + 32 * i;
-      if (rb < R) {
+  for (int i = 0; i < NR; ++i) {
+    if (rb0 + 32 * i < R) {
 #pragma unroll
-        for (int a = 0; a < NM; ++a) {
-          const uint8_t* rowp = wsb + (rb * NM + a) * kStgRowBytes;
-          const uint4 w = *reinterpret_cast<const uint4*>(rowp + gi * 16);
-          const unsigned short sc = *reinterpret_cast<const unsigned short*>(rowp + 128 + gi * 2);
-          const SxPack p = make_sx(u16_h2f(sc) * xv[i]);  // s = scale * x (gemv.rs:239)
-          q4_word_fma(w.x, p, &acc[a][0]);
-          q4_word_fma(w.y, p, &acc[a][4]);
-          q4_word_fma(w.z, p, &acc[a][8]);
-          q4_word_fma(w.w, p, &acc[a][12]);
-        }
-      }
-    }
-    __syncthreads();  // the reduction buffer overlays the slice
-  } else {
-    const WBatch<NR, NM>& wr = wb;
-#pragma unroll
-    for (int i = 0; i < NR; ++i) {
-      if (rb0 + 32 * i < R) {
-#pragma unroll
-        for (int a = 0; a < NM; ++a) {
-          const SxPack p = make_sx(u16_h2f(wr.s[i][a]) * xv[i]);  // s = scale * x (gemv.rs:239)
-          q4_word_fma(wr.w[i][a].x, p, &acc[a][0]);
-          q4_word_fma(wr.w[i][a].y, p, &acc[a][4]);
-          q4_word_fma(wr.w[i][a].z, p, &acc[a][8]);
-          q4_word_fma(wr.w[i][a].w, p, &acc[a][12]);
-        }
+      for (int a = 0; a < NM; ++a) {
+        const SxPack p = make_sx(u16_h2f(wr.s[i][a]) * xv[i]);  // s = scale * x (gemv.rs:239)
+        q4_word_fma(wr.w[i][a].x, p, &acc[a][0]);
+        q4_word_fma(wr.w[i][a].y, p, &acc[a][4]);
+        q4_word_fma(wr.w[i][a].z, p, &acc[a][8]);
+        q4_word_fma(wr.w[i][a].w, p, &acc[a][12]);
       }
     }
   }
@@ -498,7 +434,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_dec_kernel(const GemvDesc d
 // ===========================================================================
 // general kernel: M rows, MB per CTA (prefill, batched decode)
 template <int MB, int NM, int EPI>
-__global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvDesc d, const FrameCodes fc) {
+__global__ void __launch_bounds__(kGemvThreads) q4mv_rows_kernel(const GemvDesc d, const FrameCodes fc) {
   pdl_launch_dependents();
   prefetch_next_weights(d);
   extern __shared__ __align__(16) float sm[];
@@ -696,29 +632,15 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4_kernel(const GemvDesc d,
 
 // ---------------------------------------------------------------------------
 static bool use_dec(const GemvDesc& d) {
-  const int nrmax = d.staged ? kDecRowsStg : (d.paired ? kDecRowsNM2 : kDecRowsNM1);
+  const int nrmax = d.paired ? kDecRowsNM2 : kDecRowsNM1;
   return d.M <= kDecMaxM && d.mb == 1 && d.S <= (d.cluster ? kMaxClusterSplits : kMaxGlobalSplits) &&
          d.rows_per_split <= 32 * nrmax;
-}
-
-// A staged decode launch reads whole 16-byte chunks: every matrix's columns a
-// multiple of 256 and its packed and scale arrays 16-byte aligned.
-bool gemv_staged_eligible(const GemvDesc& d) {
-  if (d.M != 1 || d.emb_idx || d.attn_in || d.tc) return false;
-  if (!(d.epi_kind == EPI_STORE || d.epi_kind == EPI_RESID || (d.epi_kind == EPI_SWIGLU && d.paired))) return false;
-  const int nm = d.paired ? 2 : d.nmat;
-  for (int i = 0; i < nm; ++i) {
-    const Q4Mat& m = d.mat[i];
-    if (m.n % 256 != 0 || (reinterpret_cast<uintptr_t>(m.packed) & 15) || (reinterpret_cast<uintptr_t>(m.scales) & 15))
-      return false;
-  }
-  return true;
 }
 
 size_t gemv_smem_bytes(const GemvDesc& d) {
   const int NM = d.paired ? 2 : 1;
   if (use_dec(d))
-    return sizeof(float) * ((size_t)dec_front_floats(NM, d.staged != 0, d.rows_per_split) +
+    return sizeof(float) * ((size_t)dec_front_floats(NM) +
                             (size_t)kMaxClusterSplits * NM * kTileN + 64 + kTileN + 4);
   return sizeof(float) * ((size_t)d.mb * d.rows_per_split + 8 * NM * d.mb * kTileN + 64 + d.mb * kTileN);
 }
@@ -733,24 +655,19 @@ static LaunchOpts opts(const GemvDesc& d) {
 template <int MB, int NM, int EPI>
 static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
   const dim3 grid(d.ntiles, d.S, (d.M + MB - 1) / MB);
-  return launch_k(gemv_q4_kernel<MB, NM, EPI>, grid, dim3(kGemvThreads), gemv_smem_bytes(d), st, opts(d), d, fc);
+  return launch_k(q4mv_rows_kernel<MB, NM, EPI>, grid, dim3(kGemvThreads), gemv_smem_bytes(d), st, opts(d), d, fc);
 }
 
-template <int NM, int EPI, int NR, bool STG = false>
+template <int NM, int EPI, int NR>
 static cudaError_t launch_dec(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
   const dim3 grid(d.ntiles, d.S, d.M);
-  return launch_k(gemv_dec_kernel<NM, EPI, NR, STG>, grid, dim3(kGemvThreads), gemv_smem_bytes(d), st, opts(d), d,
+  return launch_k(q4mv_dec_kernel<NM, EPI, NR>, grid, dim3(kGemvThreads), gemv_smem_bytes(d), st, opts(d), d,
                   fc);
 }
 
 template <int NM, int EPI>
 static cudaError_t dispatch_dec(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
   const int nr = (d.rows_per_split + 31) / 32;
-  if (d.staged) {
-    if constexpr ((NM == 1 && (EPI == EPI_STORE || EPI == EPI_RESID)) || (NM == 2 && EPI == EPI_SWIGLU))
-      return launch_dec<NM, EPI, kDecRowsStg, true>(d, fc, st);
-    return cudaErrorInvalidValue;
-  }
   if (NM == 2) {
     if (nr <= 2) return launch_dec<2, EPI, 2>(d, fc, st);
     if (nr <= 4) return launch_dec<2, EPI, 4>(d, fc, st);
@@ -765,14 +682,13 @@ static cudaError_t dispatch_dec(const GemvDesc& d, const FrameCodes& fc, cudaStr
 
 template <int MB, int NM, int EPI>
 static void set_attr() {
-  cudaFuncSetAttribute(gemv_q4_kernel<MB, NM, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
-  cudaFuncSetAttribute(gemv_q4_kernel<MB, NM, EPI>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaFuncSetAttribute(q4mv_rows_kernel<MB, NM, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+  cudaFuncSetAttribute(q4mv_rows_kernel<MB, NM, EPI>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
 }
-template <int NM, int EPI, int NR, bool STG = false>
+template <int NM, int EPI, int NR>
 static void set_attr_dec() {
-  cudaFuncSetAttribute(gemv_dec_kernel<NM, EPI, NR, STG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       STG ? kDecStgMaxSmem : 160 * 1024);
-  cudaFuncSetAttribute(gemv_dec_kernel<NM, EPI, NR, STG>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaFuncSetAttribute(q4mv_dec_kernel<NM, EPI, NR>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+  cudaFuncSetAttribute(q4mv_dec_kernel<NM, EPI, NR>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
 }
 template <int EPI>
 static void set_attr_dec_nm1() {
@@ -793,8 +709,6 @@ void gemv_init_attributes() {
   set_attr_dec_nm1<EPI_STORE>(); set_attr_dec_nm1<EPI_RESID>(); set_attr_dec_nm1<EPI_QKV>();
   set_attr_dec_nm1<EPI_ARGMAX>();
   set_attr_dec<2, EPI_SWIGLU, 2>(); set_attr_dec<2, EPI_SWIGLU, 4>(); set_attr_dec<2, EPI_SWIGLU, kDecRowsNM2>();
-  set_attr_dec<1, EPI_STORE, kDecRowsStg, true>(); set_attr_dec<1, EPI_RESID, kDecRowsStg, true>();
-  set_attr_dec<2, EPI_SWIGLU, kDecRowsStg, true>();
   cudaGetLastError();
   done[dev] = true;
 }

@@ -159,16 +159,12 @@ struct GemvDesc {
   // GLU input (decode kernel only): x[r] = X[r] * X[x_glu + r], the SwiGLU
   // product of a row holding silu(gate) in [0, x_glu) and up in [x_glu, 2 x_glu)
   int x_glu = 0;
-  // decode kernel with the CTA's weight slice staged in shared memory
-  // (gemv_staged_eligible) instead of registers: more rows per K slice
-  int staged = 0;
   EpiDesc epi;
 };
 // err_flag bits shared by the kernels (the session's flag word)
 constexpr int kErrRopeRange = 1;     // a position beyond the talker RoPE table
 constexpr int kErrWaitExpired = 4;   // a bounded device wait ran out
 constexpr int kErrFp16Input = 8;     // a tensor-core input outside the fp16 range
-constexpr int kErrGridBarrier = 16;  // a persistent kernel's grid barrier gave up
 constexpr int kMaxClusterSplits = 16;
 constexpr int kMaxGlobalSplits = 64;  // decode kernel, split-K reduced through global memory
 constexpr int kAttnInMaxPos = 32;  // cache positions the attention prologue handles
@@ -177,8 +173,6 @@ constexpr int kAttnInMaxPos = 32;  // cache positions the attention prologue han
 constexpr int kDecRowsNM1 = 12;  // rows per split <= 384
 constexpr int kDecMaxM = 2;      // decode kernel: input rows per launch (one per grid.z)
 constexpr int kDecRowsNM2 = 6;   // rows per split <= 192
-constexpr int kDecRowsStg = 24;  // staged (weights in shared memory): rows per split <= 768
-constexpr int kDecStgMaxSmem = 227 * 1024;  // dynamic shared memory of a staged decode CTA
 constexpr int kSsqLd = 64;       // row stride of the sum-of-squares partials
 constexpr int kSsqCols = 128;    // columns summed per partial (rows up to 64 * 128 wide)
 
@@ -209,7 +203,6 @@ struct FrameCodes {
 // ---- launch helper: programmatic dependent launch + cluster shape ----
 // PDL lets a kernel start (and prefetch its weights) while its predecessor
 // finishes; the kernel's griddepcontrol.wait orders all dependent reads.
-bool pdl_enabled();
 // kernels launched through launch_k by this thread (frame-plan kernel counts)
 inline thread_local long g_kernel_launches = 0;
 // Occupancy query mode: with g_occ_query set, launch_k launches nothing and
@@ -239,7 +232,7 @@ inline cudaError_t launch_k(Kern kern, dim3 grid, dim3 block, size_t smem, cudaS
     at[n].val.clusterDim.z = 1;
     ++n;
   }
-  if (o.pdl && pdl_enabled()) {
+  if (o.pdl) {
     at[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[n].val.programmaticStreamSerializationAllowed = 1;
     ++n;
@@ -258,14 +251,12 @@ inline cudaError_t launch_k(Kern kern, dim3 grid, dim3 block, size_t smem, cudaS
 size_t gemv_smem_bytes(const GemvDesc& d);
 cudaError_t launch_gemv(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st);
 bool gemv_uses_decode_kernel(const GemvDesc& d);  // M = 1 plan served by gemv_dec_kernel
-bool gemv_staged_eligible(const GemvDesc& d);     // M = 1 plan may stage its weights in shared memory
 
 // tensor-core path (tc_gemm.cu)
 constexpr int kTcRows = 128;     // MMA tile rows (TMEM lanes)
 constexpr int kTcCols = 128;     // CTA tile columns per matrix
 constexpr int kTcK = 64;         // K per pipeline stage
 constexpr int kTcMinRows = 16;   // projections with M >= this take the tensor cores
-bool tc_enabled();               // QTTS_TC=0 keeps every projection on the CUDA cores
 void tc_plan(int sm_count, GemvDesc& g);   // sets tc = 1 and tc_ks (K split fitted to one wave)
 int tc_splits(const GemvDesc& d);          // K slices of a planned launch
 size_t tc_smem_bytes(int nm);
@@ -276,42 +267,6 @@ size_t tc_expand_bytes(int k, int n);
 cudaError_t tc_expand(const Q4Mat& w, uint8_t* out, cudaStream_t st);
 void tc_init_attributes();
 
-// persistent code predictor of one utterance (pred_persist.cu)
-constexpr int kPPThreads = 256;
-constexpr int kPPMaxLayers = 8;
-constexpr int kPPMaxSlice = 1024;   // K rows of a unit (and the head's hidden size)
-constexpr int kPPMaxHidden = 2048;  // predictor hidden size
-constexpr int kPPMaxPos = 32;       // predictor positions (prefill 2 + 14 decode)
-constexpr int kPPSmem = (8192 * 2 + 2 * kPPMaxSlice + 2 * kPPMaxHidden + 32 + 4 + 3 * 2 * kHeadDim + 2 * kPPMaxPos) * 4;
-struct PPLayer {
-  Q4Mat q, k, v, o, gate, up, down;
-  const __half *q_norm = nullptr, *k_norm = nullptr, *in_norm = nullptr, *post_norm = nullptr;
-};
-struct PredPersistDesc {
-  int pH = 0, heads = 0, kvh = 0, inter = 0, layers = 0, groups = 0, t_hidden = 0, rope_rows = 0;
-  PPLayer L[kPPMaxLayers];
-  Q4Mat proj;
-  const float* proj_b = nullptr;
-  Q4Mat emb[kMaxGroups], lm[kMaxGroups];
-  const __half* final_norm = nullptr;
-  const float *cos = nullptr, *sin = nullptr;
-  float* kv = nullptr;         // predictor KV page of the utterance: [layer][K|V][kv_head][16][128]
-  const float* pin = nullptr;  // [talker hidden | semantic embedding], t_hidden each
-  float* part = nullptr;       // split-K partials (pred_persist_part_floats)
-  float* X = nullptr;          // residual rows: [2][pH] layer input, [2][pH] after attention
-  float* attn = nullptr;       // [2][heads * 128]
-  unsigned long long* keys = nullptr;  // [2] argmax keys, zero at launch
-  unsigned* bar = nullptr;     // grid-barrier counter, zero at launch
-  int* err_flag = nullptr;     // bit 16: a grid barrier gave up
-  FrameCodes fc;
-  int frame_mode = 0;
-  uint32_t* codes_plain = nullptr;
-  int s_proj = 8, s_qkv = 4, s_o = 8, s_gu = 2, s_down = 8;  // K slices per projection
-};
-size_t pred_persist_part_floats(const PredPersistDesc& d);
-bool pred_persist_supported(const PredPersistDesc& d);
-cudaError_t launch_pred_persist(const PredPersistDesc& d, int grid, cudaStream_t st);
-void pred_persist_init_attributes();
 
 
 struct AttnDesc {

@@ -850,11 +850,7 @@ void tc_plan(int sm_count, GemvDesc& g) {
   const long units = tiles * ((g.M + TM - 1) / TM);
   g.tc = 1;
   g.tc_ks = (int)nks;
-  static const long max_s = [] {  // QTTS_TC_SPLITS caps S (measurements)
-    const char* v = getenv("QTTS_TC_SPLITS");
-    return v ? std::max(1L, std::min<long>(kMaxSplits, atol(v))) : (long)kMaxSplits;
-  }();
-  for (long S = std::min<long>(max_s, std::min<long>(nks, std::max<long>(1, sm_count / units))); S > 1; --S) {
+  for (long S = std::min<long>(kMaxSplits, std::min<long>(nks, std::max<long>(1, sm_count / units))); S > 1; --S) {
     GemvDesc t = g;
     t.tc_ks = (int)((nks + S - 1) / S);
     if (tc_splits(t) != S) continue;

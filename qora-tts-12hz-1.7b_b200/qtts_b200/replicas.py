@@ -1,4 +1,4 @@
-"""Independent-utterance sharding across the GPUs of one box (BASELINE
+"""Independent-utterance sharding across the GPUs of one box (benchmark
 config 5: 512 utterances, 64 per GPU, no collective on the data path).
 
 Each rank owns a contiguous block of utterance ids and a full model replica

@@ -1,4 +1,4 @@
-"""Seeded synthetic inputs for the BASELINE configs (no datasets, no
+"""Seeded synthetic inputs for the benchmark configs (no datasets, no
 checkpoints: weights are the seeded synthetic .qora-tts, inputs are seeded
 token ids and speaker embeddings with the configs' shapes).
 

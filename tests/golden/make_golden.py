@@ -7,7 +7,10 @@ the seeded synthetic weights.  They pin the GPU path to the oracle and the
 oracle to itself across machines (parity with the Rust crate stays
 unpinned).  Weights are identified by the sha256 of the synthetic file.
 
-    python tests/golden/make_golden.py [--skip-1p7b]
+    python tests/golden/make_golden.py [--skip-1p7b] [--only NAME[,NAME...]]
+
+--only regenerates just the named fixtures (tiny_long_kv, p1p7b_config3_2000,
+p1p7b_config4_64); the long 1.7B cases take tens of minutes on 8 cores.
 
 The oracle uses 8 K-split chunks for the large talker GEMVs (the reference's
 threading policy, gemv.rs:268-309, on an 8-thread host).
@@ -102,10 +105,54 @@ def sampler_kats():
                 state_out=np.array([c[6] for c in cases], np.uint64))
 
 
+def tiny_long_kv(m):
+    """Tiny model, config-3 sampling (T=0.8, top-k 50, seed 42), 2000 frames:
+    the talker attention runs over ~2010 cached positions (talker.rs:305-331)."""
+    u3, frames = W.config3(m.dims.t_hidden)
+    return run_case(m, u3, frames, keep_frames=[0, 1, 999, 1500, frames - 1])
+
+
+def p1p7b_config3_2000(m):
+    """1.7B, benchmark config 3 in full: 96-token prompt, T=0.8 / top-k 50 /
+    seed 42, 2000 frames (KV to ~2010 positions)."""
+    u3, frames = W.config3(2048)
+    return run_case(m, u3, frames, keep_frames=[0, 999, frames - 1])
+
+
+def p1p7b_config4_64(m, frames=3):
+    """1.7B, benchmark config 4's 64 utterances (ragged 16-256-token prompts,
+    own voice and seed each, T=0.8 / top-k 50), `frames` frames each, one
+    oracle run per utterance; stacked along a leading utterance axis."""
+    utts, _ = W.config4(64, 2048)
+    runs = [run_case(m, u, frames, keep_frames=[0, frames - 1]) for u in utts]
+    out = {k: np.stack([r[k] for r in runs]) for k in runs[0] if k != "seconds"}
+    out["seconds"] = np.float64(sum(float(r["seconds"]) for r in runs))
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--skip-1p7b", action="store_true")
+    ap.add_argument("--only", default="", help="comma-separated fixture names")
     args = ap.parse_args()
+    if args.only:
+        O.set_threads(THREADS)
+        only = set(args.only.split(","))
+        if "tiny_long_kv" in only:
+            m = O.Model(oracle_model("tiny"))
+            r = tiny_long_kv(m)
+            np.savez_compressed(os.path.join(OUT, "tiny_long_kv.npz"), **r)
+            print("tiny_long_kv frames", int(r["frames"]), "s", float(r["seconds"]), flush=True)
+            m.close()
+        big = [n for n in ("p1p7b_config3_2000", "p1p7b_config4_64") if n in only]
+        if big:
+            m = O.Model(oracle_model("1p7b"))
+            for name in big:
+                r = globals()[name](m)
+                np.savez_compressed(os.path.join(OUT, f"{name}.npz"), **r)
+                print(name, "s", float(r["seconds"]), flush=True)
+            m.close()
+        return
     meta_path = os.path.join(OUT, "meta.npz")
     old_meta = dict(np.load(meta_path)) if os.path.exists(meta_path) else {}
     O.set_threads(THREADS)

@@ -96,7 +96,7 @@ def test_quantize_round_trip_and_errors(qtts):
         qtts.q4_quantize_dev(dd.data_ptr() + 4, 2, 64, dp.data_ptr(), ds.data_ptr())
 
 
-SHAPES = [  # (k=in, n=out): BASELINE config 2 and the real model shapes
+SHAPES = [  # (k=in, n=out): benchmark config 2 and the real model shapes
     (2048, 4096), (2048, 2048), (2048, 1024), (2048, 6144), (6144, 2048), (2048, 3072),
     (1024, 2048), (1024, 1024), (1024, 3072), (3072, 1024), (64, 96), (100, 160), (33, 32)]
 
