@@ -1,19 +1,26 @@
 """Benchmark of the QORA-TTS 1.7B per-frame codec decode loop on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload config1|config4]
+                    [--workload config5|config1|config2|config3|config4] [--full-prompt]
 
 One step = one frame of the hot path (code-0 sample, 15-group predictor
 expansion, frame-input fusion, 28-layer talker step, codec head) for every
-utterance of the batch.  Default workload: BASELINE config 1 (1.7B, batch 1,
-greedy, 32-token prompt + speaker embedding) on each GPU; with N GPUs each
-rank decodes its own utterance (independent utterances, no collective on the
-data path: "scaling": "weak").  value = frames of all ranks / max-over-ranks
-device time of the K timed frames.  Weights (860 MB Q4 per frame) exceed the
-126 MB L2, so every frame streams them from HBM.
+utterance the GPU holds.
 
---impl reference times the CPU oracle (a line-faithful restatement of the
-Rust reference; the crate itself cannot be built here) on the host cores.
+Default workload, config 5: 512 utterances (prompts of 16-256 tokens, own
+voice and seed each, T=0.8 / top-k 50, 500 frames) split into contiguous
+blocks over the N GPUs (strong scaling), each GPU decoding its block as
+waves of 64 utterances: one CUDA graph per wave and frame, the waves of a
+GPU serialised on the device so that every GPU always works on one batch of
+64 rows.  value = frames of all ranks / max-over-ranks device time of the K
+timed steps.  The timed steps sit at the middle of the 500-frame utterances
+(the cache holds ~260 positions), after W warm-up steps and untimed frames.
+The batch-1 headline (config 1: one greedy utterance, 32-token prompt) is
+timed on every rank as the line's `batch1` sub-record.
+
+--impl reference times the CPU oracle (a line-faithful C restatement of the
+Rust reference, which cannot be built here) on the host cores, one frame per
+step at the same cache length.
 """
 from __future__ import annotations
 
@@ -35,10 +42,18 @@ for _p in (REPO, PKG):
 
 METRIC = "codec frames/sec"
 PEAKS_PATH = os.path.join(REPO, "MEASURED_PEAKS.json")
-# per-frame unique Q4 bytes of the 1.7B model (talker 793.0 MB + codec head
-# 3.54 MB + predictor layers 44.26 MB + input_proj 1.18 MB + 15 lm heads
-# 17.69 MB; norms included) -- computed exactly from the dims below
-KV_BYTES_PER_POS = 28 * 8 * 128 * 2 * 4  # talker K+V read per position, f32
+MODEL_DIR = os.environ.get("QTTS_MODEL_DIR", "/tmp/qtts_models")
+MODEL_1P7B = os.path.join(MODEL_DIR, "qtts_1p7b_seed0.qora-tts")
+KV_BYTES_PER_POS = 28 * 8 * 128 * 2 * 4  # talker K+V read per cached position, f32
+WAVE = 64  # utterances a GPU decodes at once (config 5: 64 per GPU)
+# frames per utterance of each workload (the timed window sits at the middle)
+UTT_FRAMES = {"config1": 100, "config3": 2000, "config4": 500, "config5": 500}
+# DRAM bytes (read + write) of one config-5 frame step's tc_proj_kernel
+# launches (all of them, 64 rows), from an ncu capture of
+#   python bench.py --workload config4 --steps 2 --warmup 3 --no-cpu-baseline
+# with --metrics dram__bytes_read.sum,dram__bytes_write.sum -k regex:tc_proj
+# at the commit this constant was last updated with; None when not captured.
+TC_FRAME_TRAFFIC_BYTES = None
 
 
 def q4_bytes(k, n):
@@ -46,6 +61,9 @@ def q4_bytes(k, n):
 
 
 def frame_weight_bytes():
+    """Unique Q4 bytes a frame reads (talker 793.0 MB + codec head 3.54 MB +
+    predictor layers 44.26 MB + input_proj 1.18 MB + 15 lm heads 17.69 MB,
+    norms included), computed from the 1.7B dims."""
     H, I, q, kv, V = 2048, 6144, 2048, 1024, 3072
     talker = 28 * (q4_bytes(H, q) + 2 * q4_bytes(H, kv) + q4_bytes(q, H) + 2 * q4_bytes(H, I) + q4_bytes(I, H)
                    + (128 * 2 + H * 2) * 2)
@@ -145,57 +163,90 @@ def barrier(world):
         dist.barrier()
 
 
-def cpu_baseline_measure(kv_len, frames, budget_s=25.0):
-    """Time the oracle's frame step on the host cores (bounded sample)."""
+def reduce_over_ranks(value: float, op: str) -> float:
+    """Max or sum of a per-rank float over the process group (identity at N=1)."""
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()) or dist.get_world_size() == 1:
+        return float(value)
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([float(value)], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def timed_window(workload, steps, warmup):
+    """First timed frame: the K timed frames are centred on the middle of the
+    workload's utterances (at least `warmup` frames in)."""
+    L = UTT_FRAMES.get(workload, steps)
+    return max(warmup, L // 2 - steps // 2) if steps < L else warmup
+
+
+# ---------------------------------------------------------------------------
+# CPU baselines (the oracle: test infrastructure, timed here as the baseline)
+
+def _oracle_model_path():
+    """The seeded synthetic 1.7B model, written by the oracle's own writer
+    when absent (byte-identical to the library's writer)."""
     from oracle import oracle as O
-    from qtts_b200 import workload as W
+    os.makedirs(MODEL_DIR, exist_ok=True)
+    if not os.path.exists(MODEL_1P7B):
+        tmp = MODEL_1P7B + f".tmp{os.getpid()}"
+        O.synth_write(tmp, O.dims_1p7b(), 0)
+        os.replace(tmp, MODEL_1P7B)
+    return MODEL_1P7B
+
+
+def cpu_baseline_measure(kv_len, frames, budget_s=15.0):
+    """The oracle's frame step (talker + predictor + sampler of one utterance)
+    at cache length kv_len on all host cores, for a bounded sample."""
+    from oracle import oracle as O
     threads = os.cpu_count() or 1
     O.set_threads(threads)
-    m = O.Model(W.model_path("1p7b"))
+    m = O.Model(_oracle_model_path())
     t0 = time.time()
     per = m.time_frames(kv_len, 1)  # warm-up frame
     n = max(1, min(frames, int(budget_s / max(per, 1e-3))))
     per = m.time_frames(kv_len, n)
     m.close()
     return {"value": 1.0 / per, "unit": "frames/s", "cores": threads, "kind": "port",
-            "sample": f"{n} frames of config-1 decode at KV length {kv_len} (talker+predictor+sampler), "
-                      f"oracle restatement of the Rust CPU engine, gemv.rs:268 thread policy",
+            "sample": f"{n} frames of one utterance at cache length {kv_len} (talker+predictor+sampler); "
+                      f"oracle restatement of the Rust CPU engine with its gemv.rs:268 thread policy; the "
+                      f"reference has no batching, so batched configs run as sequential utterances",
             "seconds_per_frame": per, "wall_s": time.time() - t0}
 
 
 def run_reference(args, rank, world):
+    """--impl reference: the oracle's frame step on the host cores, one frame
+    per step, at the cache length of the GPU arm's timed window."""
     if rank != 0:
         return
-    kv_len = 10 + args.warmup + args.steps // 2
     from oracle import oracle as O
-    from qtts_b200 import workload as W
+    start = timed_window(args.workload, args.steps, args.warmup)
+    kv_len = 10 + start + args.steps // 2
     threads = os.cpu_count() or 1
     O.set_threads(threads)
-    m = O.Model(W.model_path("1p7b"))
+    m = O.Model(_oracle_model_path())
     m.time_frames(kv_len, max(1, min(args.warmup, 2)))
-    per_steps = []
-    for _ in range(args.steps):
-        per_steps.append(m.time_frames(kv_len, 1))
+    per_steps = [m.time_frames(kv_len, 1) for _ in range(args.steps)]
     m.close()
     per = sum(per_steps) / len(per_steps)
     v = 1.0 / per
     line = {"metric": METRIC, "value": v, "unit": "frames/s", "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "config1: 1.7B Q4 batch-1 greedy decode step (CPU oracle, one frame per step)",
-                       "kv_len": kv_len},
+            "scaling": "strong" if args.workload == "config5" else "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": f"{args.workload}: 1.7B Q4 decode, one utterance's frame per step on the CPU "
+                                   f"(the reference is single-utterance; batched configs are sequential utterances)",
+                       "kv_len": kv_len, "frames_window": [start, start + args.steps]},
             "cpu_baseline": {"value": v, "unit": "frames/s", "cores": threads, "kind": "port",
-                             "sample": f"{args.steps} single frames at KV length {kv_len}"},
+                             "sample": f"{args.steps} single frames at cache length {kv_len}"},
             "e2e": {"value": v, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-# DRAM bytes (read + write) of one k=2048 n=6144 launch, from the ncu
-# captures summarised in profiles/gemv_dec_2048x6144_ncu.md (batch-1 GEMV,
-# m=1) and profiles/tc_proj_2048x6144_m64_ncu.md (tcgen05 projection, m=64)
-GEMV_TRAFFIC_BYTES = 7142912
-TC_TRAFFIC_BYTES = 7687168
-
+# ---------------------------------------------------------------------------
+# config 2: isolated Q4 GEMV / GEMM microbench
 
 def time_q4_launches(Q, torch, k, n, m):
     """Average device time of back-to-back qtts_q4_gemv_dev launches (one
@@ -214,8 +265,6 @@ def time_q4_launches(Q, torch, k, n, m):
             Q.q4_gemv_dev(packed[i % copies].data_ptr(), scales[i % copies].data_ptr(), k, n, x.data_ptr(), m,
                           y.data_ptr(), scr.data_ptr(), sb, sp)
     torch.cuda.synchronize()
-    # back-to-back launches captured in one CUDA graph (no host launch cost
-    # in the timed region), rotating over weight copies larger than L2
     reps = 200
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g, stream=s, capture_error_mode="thread_local"):
@@ -234,40 +283,7 @@ def time_q4_launches(Q, torch, k, n, m):
     return e0.elapsed_time(e1) / 1e3 / (3 * reps)
 
 
-def gemv_roofline(Q, torch, peak, peak_kind):
-    """The dominant kernel of the batch-1 frame: the Q4 GEMV (split-K,
-    cluster-reduced gemv_dec_kernel) at the talker gate shape k=2048, n=6144."""
-    k, n, m = 2048, 6144, 1
-    alg = q4_bytes(k, n) + 4 * k * m + 4 * n * m
-    dt = time_q4_launches(Q, torch, k, n, m)
-    ach = alg / dt / 1e9
-    return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
-            "traffic": GEMV_TRAFFIC_BYTES, "kernel": "gemv_dec_kernel (Q4 GEMV) k=2048 n=6144 m=1",
-            "us_per_launch": dt * 1e6, "algorithmic_bytes": alg, "peak_kind": f"hbm_gbs ({peak_kind})"}
-
-
-def tc_roofline(Q, torch, peaks):
-    """The dominant kernel of the batched frame: the tcgen05 projection at the
-    talker gate shape k=2048, n=6144 with 64 rows.  Useful FLOPs 2*m*k*n; the
-    tensor pipe executes 3 fp16 MMAs per product (hi/lo split) with the rows
-    padded to a multiple of 16, reported as executed_tflops."""
-    k, n, m = 2048, 6144, 64
-    dt = time_q4_launches(Q, torch, k, n, m)
-    fl = 2.0 * m * k * n
-    peak = peaks.get("bf16_tflops_sustained") or 1400.0
-    ach = fl / dt / 1e12
-    return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
-            "traffic": TC_TRAFFIC_BYTES,
-            "kernel": "tc_proj_kernel (tcgen05 Q4 projection, weights dequantised in the kernel, as "
-                      "qtts_q4_gemv_dev runs it; the frame's layer projections copy expanded operand tiles) "
-                      "k=2048 n=6144 m=64",
-            "us_per_launch": dt * 1e6, "algorithmic_flops": fl,
-            "executed_tflops": 3 * (((m + 15) // 16 * 16) / m) * ach, "weight_gbs": q4_bytes(k, n) / dt / 1e9,
-            "peak_kind": "bf16_tflops_sustained (measured)" if "bf16_tflops_sustained" in peaks else "fallback"}
-
-
-# BASELINE config 2: the projection shapes of the model (out x in) at
-# batch 1, 8, 64 and 256.
+# the projection shapes of the model (out x in) at batch 1, 8, 64 and 256
 CONFIG2_SHAPES = [("q_proj", 2048, 4096), ("k_proj", 2048, 1024), ("v_proj", 2048, 1024), ("o_proj", 2048, 2048),
                   ("gate/up_proj", 2048, 6144), ("down_proj", 6144, 2048), ("input_proj", 2048, 1024),
                   ("group_head", 1024, 2048)]
@@ -277,7 +293,7 @@ CONFIG2_BATCHES = [1, 8, 64, 256]
 def time_quantize(Q, torch, k, n, copies=4, reps=40):
     """Device time of one quantize_f32_to_q4 launch (gemv.rs:92-130): one
     CUDA graph of back-to-back launches rotating over f32 sources larger
-    than L2 together (no host launch cost in the timed region)."""
+    than L2 together."""
     g = torch.Generator(device="cuda").manual_seed(0)
     src = [torch.randn(k * n, device="cuda", generator=g) * 0.02 for _ in range(copies)]
     packed = torch.empty(k * n // 2, dtype=torch.uint8, device="cuda")
@@ -305,9 +321,9 @@ def time_quantize(Q, torch, k, n, copies=4, reps=40):
 
 
 def run_config2(args, Q, torch, peak, peak_kind):
-    """Isolated Q4 GEMV / GEMM microbench: device time per
-    launch over rotating weight copies larger than L2; m >= 16 runs on the
-    tcgen05 kernel, smaller m on the CUDA-core GEMV."""
+    """Isolated Q4 GEMV / GEMM microbench: device time per launch over
+    rotating weight copies larger than L2; m >= 16 runs on the tcgen05
+    kernel, smaller m on the CUDA-core kernels."""
     rows = []
     for name, k, n in CONFIG2_SHAPES:
         for m in CONFIG2_BATCHES:
@@ -317,10 +333,10 @@ def run_config2(args, Q, torch, peak, peak_kind):
             alg = q4_bytes(k, n) + 4 * m * (k + n)
             rows.append({"shape": name, "k": k, "n": n, "m": m, "us_per_launch": dt * 1e6,
                          "gbs": alg / dt / 1e9, "useful_tflops": 2.0 * m * k * n / dt / 1e12,
-                         "kernel": "tc_proj_kernel" if m >= 16 else "gemv (CUDA cores)"})
+                         "kernel": "tc_proj_kernel" if m >= 16 else ("q4mv_dec_kernel" if m <= 2 else
+                                                                     "q4mv_rows_kernel")})
     if not args.only or args.only == "quantize":
-        # the converter's quantize_f32_to_q4 on the GPU: reads 4 B, writes 0.5625 B per value
-        k, n = 2048, 6144
+        k, n = 2048, 6144  # quantize_f32_to_q4 on the GPU: reads 4 B, writes 0.5625 B per value
         dt = time_quantize(Q, torch, k, n)
         rows.append({"shape": "quantize_f32_to_q4", "k": k, "n": n, "m": None, "us_per_launch": dt * 1e6,
                      "gbs": (4.0 + 0.5625) * k * n / dt / 1e9, "kernel": "q4_quantize_kernel"})
@@ -332,23 +348,197 @@ def run_config2(args, Q, torch, peak, peak_kind):
             "config": {"workload": "config2: isolated Q4 GEMV/GEMM, x ~ N(0,1) f32, weights rotated over > 512 MB",
                        "headline": "gate/up_proj k=2048 n=6144 m=1"},
             "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak, "unit": "GB/s",
-                         "frac": gbs / peak if gbs else None, "traffic": GEMV_TRAFFIC_BYTES,
+                         "frac": gbs / peak if gbs else None, "traffic": None,
                          "peak_kind": f"hbm_gbs ({peak_kind})"},
             "microbench": rows}
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------
+# frame workloads
+
+def workload_utts(args, rank, world, W):
+    if args.workload == "config1":
+        u, _ = W.config1(2048)
+        return [dict(u, seed=int(u["seed"]) + rank)], \
+            "config1: 1.7B Q4 talker+predictor, one greedy utterance per GPU, 32-token prompt + voice embedding"
+    if args.workload == "config3":
+        u, _ = W.config3(2048)
+        return [dict(u, seed=int(u["seed"]) + rank)], \
+            "config3: 1.7B Q4, one utterance per GPU, T=0.8 top-k 50, 96-token prompt, 2000 frames"
+    if args.workload == "config4":
+        utts, _ = W.config4(WAVE, 2048)
+        return utts, "config4: 1.7B Q4, 64 utterances per GPU, T=0.8 top-k 50, prompts 16-256 tokens"
+    utts, _ = W.config5_shard(rank, world)
+    return utts, (f"config5: 1.7B Q4, 512 utterances (prompts 16-256 tokens, T=0.8 top-k 50) split over "
+                  f"{world} GPU(s), waves of {WAVE} per GPU")
+
+
+class Waves:
+    """The rank's utterances as waves of up to 64, one session + generation
+    each; a step launches one frame graph per wave, the waves chained through
+    events so that the GPU runs one wave at a time."""
+
+    def __init__(self, Q, torch, model, utts, frames, full_prompt):
+        self.torch = torch
+        self.waves = [utts[i:i + WAVE] for i in range(0, len(utts), WAVE)]
+        max_text = max(len(u["text"]) for u in utts)
+        self.maxp = 10 + (max_text if full_prompt else 0) + frames + 1
+        self.sessions = [Q.Session(model, len(w), self.maxp) for w in self.waves]
+        self.gens = [Q.Generation(s, w, frames, full_prompt=full_prompt) for s, w in zip(self.sessions, self.waves)]
+        self.streams = [torch.cuda.ExternalStream(s.stream) for s in self.sessions]
+        self.last = torch.cuda.Event()
+        self.last_stream = self.streams[0]
+        self.last.record(self.last_stream)
+
+    def first_stream(self):
+        self.streams[0].wait_event(self.last)
+        return self.streams[0]
+
+    def steps(self, n):
+        for _ in range(n):
+            for g, st in zip(self.gens, self.streams):
+                st.wait_event(self.last)
+                g.frames(1)
+                self.last.record(st)
+                self.last_stream = st
+
+    def close(self):
+        for s in self.sessions:
+            s.close()
+
+
+def run_frames(args, rank, world, local, Q, W, torch, model, peak, peak_kind):
+    import numpy as np
+    utts, wl = workload_utts(args, rank, world, W)
+    start = timed_window(args.workload, args.steps, args.warmup)
+    F = start + args.steps + 1
+    wv = Waves(Q, torch, model, utts, F, args.full_prompt)
+    wv.steps(start)  # warm-up steps and the frames before the timed window (untimed)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.2)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0.record(wv.first_stream())
+    wv.steps(args.steps)
+    e1.record(wv.last_stream)
+    e1.synchronize()
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    t = reduce_over_ranks(e0.elapsed_time(e1) / 1e3, "max")
+    n_utt = len(utts)
+    total_utt = reduce_over_ranks(n_utt, "sum")
+    for g in wv.gens:
+        codes, frames = g.end()
+        assert int(frames.min()) >= start + args.steps, frames
+    nk = wv.sessions[0].frame_kernel_count()
+    kv_mid = 10 + start + args.steps // 2
+    res = {"t": t, "value": total_utt * args.steps / t, "ms_per_step": t / args.steps * 1e3, "n_utt": n_utt,
+           "total_utt": total_utt, "waves": len(wv.waves), "kernels_per_frame": nk, "start": start,
+           "kv_mid": kv_mid, "clocks": clk, "wl": wl}
+
+    # e2e: the public qtts_generate call per wave with host buffers (prefill,
+    # the frame graph replays of frames 0..F-1, codes copied back); the frame
+    # graph captured above is reused (same shape)
+    torch.cuda.synchronize()
+    barrier(world)
+    t0 = time.perf_counter()
+    for s, w in zip(wv.sessions, wv.waves):
+        Q.generate(s, w, F, full_prompt=args.full_prompt)
+    t_e2e = reduce_over_ranks(time.perf_counter() - t0, "max")
+    res["e2e"] = {"value": total_utt * F / t_e2e, "unit": "frames/s",
+                  "h2d_bytes_per_step": sum(int(np.asarray(x["text"]).nbytes) + (2048 * 4 if x.get("voice") is not None
+                                                                                 else 0) for x in utts) / F,
+                  "d2h_bytes_per_step": (n_utt * F * 16 * 4 + n_utt * 4) / F,
+                  "includes": f"per wave: qtts_generate = prefill + {F} frame-graph replays (frames 0..{F - 1}) + "
+                              f"codes to the host; the frame graph is reused across calls",
+                  "graph_captures_per_wave": wv.sessions[0].graph_captures()}
+
+    # the dominant kernel family of a frame step (tc_proj_kernel at 64 rows,
+    # CUDA-core q4mv_dec_kernel at batch 1): one frame's launches of it
+    # replayed alone, CUDA events on the session stream
+    fam = Q.FAMILY_TC_PROJ if n_utt >= 16 else Q.FAMILY_Q4MV_DEC
+    ft = wv.sessions[0].family_time(fam, reps=20)
+    res["family"] = ft
+    res["fam"] = fam
+    wv.close()
+    return res
+
+
+def roofline_tc(ft, peaks, ms_frame, B):
+    """tc_proj_kernel, all its launches in one frame step of B utterances:
+    useful FLOPs (2*M*k*n per matrix) over their device time."""
+    peak = peaks.get("bf16_tflops_sustained") or 1400.0
+    sec = ft["ms"] / 1e3
+    ach = ft["flops"] / sec / 1e12 if sec > 0 else None
+    return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s",
+            "frac": ach / peak if ach else None,
+            "traffic": TC_FRAME_TRAFFIC_BYTES / ft["launches"] if TC_FRAME_TRAFFIC_BYTES else None,
+            "kernel": f"tc_proj_kernel: every tcgen05 projection of one frame step ({B} rows), "
+                      f"{ft['launches']} launches replayed alone in frame order",
+            "us_per_launch": ft["ms"] * 1e3 / max(ft["launches"], 1), "ms_per_frame_step": ft["ms"],
+            "share_of_step": ft["ms"] / ms_frame if ms_frame else None,
+            "algorithmic_flops_per_launch": ft["flops"] / max(ft["launches"], 1),
+            "q4_weight_gbs": ft["weight_bytes"] / sec / 1e9 if sec > 0 else None,
+            "peak_kind": "bf16_tflops_sustained (measured)" if "bf16_tflops_sustained" in peaks else "fallback",
+            "note": "tensor pipe executes 3 fp16 MMAs per product (hi/lo split for f32 accuracy); weights are read "
+                    "as expanded fp16 hi/lo operand tiles (4 B per weight) for the layer projections"}
+
+
+def roofline_dec(ft, peak, peak_kind, ms_frame):
+    """q4mv_dec_kernel, all its launches in one batch-1 frame: algorithmic
+    Q4 weight bytes (k*n*0.5625 per matrix, every launch counted, so the
+    predictor's L2-resident weights count once per read) over device time."""
+    sec = ft["ms"] / 1e3
+    ach = ft["weight_bytes"] / sec / 1e9 if sec > 0 else None
+    return {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak if ach else None,
+            "traffic": None,
+            "kernel": f"q4mv_dec_kernel: every one-row Q4 GEMV of one batch-1 frame, {ft['launches']} launches "
+                      f"replayed alone in frame order",
+            "us_per_launch": ft["ms"] * 1e3 / max(ft["launches"], 1), "ms_per_frame": ft["ms"],
+            "share_of_frame": ft["ms"] / ms_frame if ms_frame else None,
+            "algorithmic_bytes_per_launch": ft["weight_bytes"] / max(ft["launches"], 1),
+            "peak_kind": f"hbm_gbs ({peak_kind})"}
+
+
+def frame_roofline(B, ms_step, kv_mid, peak, peak_kind):
+    """(unique Q4 weight bytes + KV read) per frame step / step time."""
+    by = frame_weight_bytes() + B * kv_mid * KV_BYTES_PER_POS
+    gbs = by / (ms_step / 1e3) / 1e9
+    return {"bytes_per_step": by, "achieved_gbs": gbs, "peak_gbs": peak, "frac": gbs / peak, "peak_kind": peak_kind}
+
+
+def run_batch1(args, rank, world, local, Q, W, torch, model, peak, peak_kind):
+    """Config 1 on this GPU: one greedy utterance, frames timed in the middle
+    of its 100-frame run; the headline b=1 ms/frame."""
+    sub = argparse.Namespace(**vars(args))
+    sub.workload = "config1"
+    sub.steps = min(args.steps if args.workload == "config1" else 50, 90)
+    sub.full_prompt = False
+    r = run_frames(sub, rank, world, local, Q, W, torch, model, peak, peak_kind)
+    return {"ms_per_frame": r["ms_per_step"], "frames_per_s_per_gpu": 1e3 / r["ms_per_step"],
+            "frames_timed": sub.steps, "kv_len_mid": r["kv_mid"], "kernels_per_frame": r["kernels_per_frame"],
+            "frame_roofline": frame_roofline(1, r["ms_per_step"], r["kv_mid"], peak, peak_kind),
+            "roofline": roofline_dec(r["family"], peak, peak_kind, r["ms_per_step"]),
+            "e2e_frames_per_s": r["e2e"]["value"] / world, "clocks": r["clocks"]}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="config1", choices=["config1", "config2", "config3", "config4"])
+    ap.add_argument("--workload", default="config5", choices=["config1", "config2", "config3", "config4", "config5"])
     ap.add_argument("--only", default="", help="config2: one case, KxNxM")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batch1", action="store_true", help="skip the config-1 sub-record")
     ap.add_argument("--full-prompt", action="store_true",
-                    help="prefill the whole text (ragged KV lengths across utterances; config4)")
+                    help="prefill the whole text (ragged KV lengths across utterances; config4/5)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     rank, world, local = dist_setup(args)
@@ -359,16 +549,15 @@ def main():
             dist.destroy_process_group()
         return
 
-    import numpy as np
     import torch
 
     import qtts_b200 as Q
     from qtts_b200 import workload as W
-    from qtts_b200.replicas import max_over_ranks
 
     torch.cuda.set_device(local)
+    peak, peak_kind = load_peaks()
+    peaks = load_peaks_raw()
     if args.workload == "config2":
-        peak, peak_kind = load_peaks()
         if rank == 0:
             run_config2(args, Q, torch, peak, peak_kind)
         if world > 1:
@@ -378,98 +567,48 @@ def main():
     if rank == 0:
         W.model_path("1p7b")
     barrier(world)
-    path = W.model_path("1p7b")
-    model = Q.Model(path, local)
-    peak, peak_kind = load_peaks()
+    model = Q.Model(W.model_path("1p7b"), local)
 
-    if args.workload == "config1":
-        u, _ = W.config1(2048)
-        utts = [dict(u, seed=int(u["seed"]) + rank)]
-        wl = "config1: 1.7B Q4 talker+predictor, batch 1 per GPU, greedy, 32-token prompt + voice embedding"
-    elif args.workload == "config3":
-        u, _ = W.config3(2048)
-        utts = [dict(u, seed=int(u["seed"]) + rank)]
-        wl = "config3: 1.7B Q4, batch 1 per GPU, T=0.8 top-k 50, 96-token prompt, long KV (use --steps 2000)"
-    else:
-        utts, _ = W.config4(64, 2048)
-        wl = "config4: 1.7B Q4, 64 utterances per GPU, T=0.8 top-k 50, prompts 16-256 tokens"
-    B = len(utts)
-    F = args.warmup + args.steps + 1
-    max_text = max(len(u["text"]) for u in utts)
-    sess = Q.Session(model, B, 10 + (max_text if args.full_prompt else 0) + F + 1)
-    gen = Q.Generation(sess, utts, F, full_prompt=args.full_prompt)
-    stream = torch.cuda.ExternalStream(sess.stream)
-    gen.frames(args.warmup)
-    torch.cuda.synchronize()
-    clocks = ClockSampler(local)
-    clocks.start()
-    time.sleep(0.2)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize()
-    e0.record(stream)
-    gen.frames(args.steps)
-    e1.record(stream)
-    e1.synchronize()
-    torch.cuda.synchronize()
-    barrier(world)
-    clk = clocks.stop()
-    t_local = e0.elapsed_time(e1) / 1e3
-    t = max_over_ranks(t_local)
-    codes, frames = gen.end()
-    assert int(frames.min()) >= args.warmup + args.steps, frames
-    value = world * B * args.steps / t
-    ms_per_step = t / args.steps * 1e3
-    nk = sess.frame_kernel_count()
-
-    # frame-level roofline: unique Q4 bytes + KV read per frame
-    kv_mid = 10 + args.warmup + args.steps // 2
-    frame_bytes = frame_weight_bytes() + B * kv_mid * KV_BYTES_PER_POS
-    frame_gbs = frame_bytes / (t / args.steps) / 1e9
-
-    # e2e: the public C-ABI call with host buffers (prefill, graph replays,
-    # codes copied back), K frames
-    sess.reset()
-    torch.cuda.synchronize()
-    barrier(world)
-    t0 = time.perf_counter()
-    codes_e2e, fr_e2e, _, _ = Q.generate(sess, utts, args.steps, full_prompt=args.full_prompt)
-    t_e2e = max_over_ranks(time.perf_counter() - t0)
-    h2d = sum(int(np.asarray(x["text"]).nbytes) + (2048 * 4 if x.get("voice") is not None else 0) for x in utts)
-    d2h = B * args.steps * 16 * 4 + B * 4
-
-    if args.workload in ("config1", "config3"):
-        roof = gemv_roofline(Q, torch, peak, peak_kind)
-    else:
-        roof = tc_roofline(Q, torch, load_peaks_raw())
+    r = run_frames(args, rank, world, local, Q, W, torch, model, peak, peak_kind)
+    batched = r["n_utt"] >= 16
+    b1 = None
+    if not args.no_batch1 and args.workload != "config1":
+        b1 = run_batch1(args, rank, world, local, Q, W, torch, model, peak, peak_kind)
+        b1["ms_per_frame"] = reduce_over_ranks(b1["ms_per_frame"], "max")
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
-            cpu = cpu_baseline_measure(kv_mid, 20)
+            cpu = cpu_baseline_measure(r["kv_mid"], 20)
         except Exception as ex:  # reported, never fatal for the GPU line
             cpu = {"value": None, "error": str(ex)}
+    B = r["n_utt"] / r["waves"]
+    roof = roofline_tc(r["family"], peaks, r["ms_per_step"] / r["waves"], int(B)) if batched else \
+        roofline_dec(r["family"], peak, peak_kind, r["ms_per_step"])
     line = {
-        "metric": METRIC, "value": value, "unit": "frames/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+        "metric": METRIC, "value": r["value"], "unit": "frames/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+        "scaling": "strong" if args.workload == "config5" else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": wl, "global_batch": world * B, "frames_timed": args.steps,
-                   "kv_len_start": 10 + args.warmup, "l2": "inputs larger than L2 (860 MB weights per frame)",
+        "config": {"workload": r["wl"], "global_batch": int(r["total_utt"]), "utterances_per_gpu": r["n_utt"],
+                   "waves_per_gpu": r["waves"], "frames_timed": args.steps,
+                   "frames_window": [r["start"], r["start"] + args.steps], "kv_len_mid": r["kv_mid"],
+                   "l2": "inputs larger than L2 (0.86 GB of Q4 weights per frame step; 6 GB of expanded "
+                         "tensor-core operand tiles at batch >= 16)",
                    "prompt": ("full prefill: KV lengths 9 + prompt tokens (ragged)" if args.full_prompt
-                              else "generate_new: 10-row prefill, text trailing into the frames"),
-                   "parallelism": f"{world} independent replicas (utterance sharding, no collective)"},
-        "ms_per_frame_batch1": ms_per_step if B == 1 else None,
-        "frame_roofline": {"bytes_per_frame": frame_bytes, "achieved_gbs": frame_gbs, "peak_gbs": peak,
-                           "frac": frame_gbs / peak, "peak_kind": peak_kind},
+                              else "generate_new: 10-row prefill, the text trailing into the frames"),
+                   "parallelism": f"{world} independent replicas, utterances sharded, no collective"},
+        "ms_per_frame_batch1": (r["ms_per_step"] if not batched else (b1 or {}).get("ms_per_frame")),
+        "frame_roofline": frame_roofline(B, r["ms_per_step"] / r["waves"], r["kv_mid"], peak, peak_kind),
         "roofline": roof,
+        "batch1": b1,
         "cpu_baseline": cpu,
-        "e2e": {"value": world * B * args.steps / t_e2e, "unit": "frames/s", "h2d_bytes_per_step": h2d / args.steps,
-                "d2h_bytes_per_step": d2h / args.steps, "includes": "prefill + graph capture + K frames + D2H"},
-        "gpu_launches": nk * args.steps, "kernels_per_frame": nk,
-        "clocks": clk,
+        "e2e": r["e2e"],
+        "gpu_launches": r["kernels_per_frame"] * r["waves"] * args.steps,
+        "kernels_per_frame": r["kernels_per_frame"],
+        "clocks": r["clocks"],
     }
     if rank == 0:
         print(json.dumps(line), flush=True)
-    sess.close()
     model.close()
     if world > 1:
         import torch.distributed as dist

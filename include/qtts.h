@@ -142,6 +142,27 @@ QTTS_API int qtts_generate_end(qtts_session* s, uint32_t* codes_out, int* frames
                       float* hidden_dump);
 /* Number of kernels one frame launches (CUDA-graph nodes). */
 QTTS_API int qtts_frame_kernel_count(qtts_session* s);
+/* Frame graphs this session has captured.  qtts_generate / _begin reuse the
+ * last one while the batch size, max_frames, trailing-text rows, forcing and
+ * dump options are unchanged (the per-generation buffers are grow-only). */
+QTTS_API int qtts_frame_graph_captures(qtts_session* s);
+
+/* ---- profiling (no counterpart in the reference) -------------------------- */
+/* Kernel families of the frame plan. */
+#define QTTS_FAMILY_Q4MV_DEC 1  /* q4mv_dec_kernel: one-row CUDA-core Q4 GEMV */
+#define QTTS_FAMILY_Q4MV_ROWS 2 /* q4mv_rows_kernel: 2-15-row CUDA-core Q4 GEMV */
+#define QTTS_FAMILY_TC_PROJ 3   /* tc_proj_kernel: tcgen05 Q4 projection */
+#define QTTS_FAMILY_ATTN 4      /* attn_kernel: GQA over the paged cache */
+/* Device time of one frame's launches of one family, captured without the
+ * frame's other launches (same order, parameters and dependent-launch links)
+ * and replayed `reps` times between CUDA events on the session stream.  Needs
+ * a generation begun on the session; the replays rewrite the current frame's
+ * cache entries, activations and codes, so that generation ends (the next
+ * qtts_generate / _begin starts afresh).  Outputs: ms per replay, launches
+ * per replay, their useful FLOPs (2*M*k*n per projection matrix) and their
+ * Q4 weight bytes (k*n*0.5625 per matrix). */
+QTTS_API int qtts_frame_family_time(qtts_session* s, int family, int reps, float* ms_per_replay, int* launches,
+                                    double* flops, double* weight_bytes);
 
 /* ---- kernels on device pointers (gemv.rs:149 gemv / :157 gemm) ------------ */
 /* y[m][n] = sum_k x[m][k] * W[k][n] for a Q4 g32 weight in the on-disk
@@ -164,6 +185,11 @@ QTTS_API int qtts_q4_gemv_dev(const uint8_t* packed_dev, const uint16_t* scales_
  * inputs and outputs, and the call allocates nothing.  The first call on a
  * device looks up the array's device address and sets the kernels' shared-
  * memory attributes, so make that first call before any stream capture.
+ * Under CUDA's lazy module loading that first call may also load this
+ * library's device code, which reserves the array inside the driver: make
+ * it once per device as a warm-up, off the real-time thread.  The address
+ * and attributes are kept for the life of the process, so the entry point
+ * must not be used across a cudaDeviceReset of that device.
  * Every call on a device shares the array, which keeps the last call's
  * contents: the counters are cleared on each call and the partial sums are
  * rewritten before they are read, but calls that overlap on the GPU (other

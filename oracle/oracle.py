@@ -61,6 +61,7 @@ def lib():
             "oq_h2f": (C.c_float, [C.c_uint16]),
             "oq_f2h": (C.c_uint16, [C.c_float]),
             "oq_synth_write": (C.c_int, [C.c_char_p, C.POINTER(Dims), C.c_uint64]),
+            "oq_set_tie_period": (None, [C.c_int]),
             "oq_dims_1p7b": (None, [C.POINTER(Dims)]),
             "oq_dims_tiny": (None, [C.POINTER(Dims)]),
             "oq_load": (P, [C.c_char_p, C.c_char_p, C.c_int]),
@@ -130,6 +131,17 @@ def synth_write(path: str, dims: Dims, seed: int = 0) -> None:
     rc = lib().oq_synth_write(path.encode(), C.byref(dims), seed)
     if rc != 0:
         raise IOError(f"oracle synth_write failed for {path}")
+
+
+def synth_write_tied_heads(path: str, dims: Dims, seed: int = 0, period: int = 7) -> None:
+    """Test fixture: the synthetic model with every predictor head's column j
+    equal to column j % period (bit-equal logits in each residue class, so
+    the greedy argmax meets exact ties)."""
+    lib().oq_set_tie_period(period)
+    try:
+        synth_write(path, dims, seed)
+    finally:
+        lib().oq_set_tie_period(0)
 
 
 def set_threads(n: int) -> None:

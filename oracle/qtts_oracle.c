@@ -394,6 +394,31 @@ static void w_f16w(wctx* c, uint64_t k, uint64_t n) {
   for (uint64_t i = 0; i < k * n; i++) { uint16_t h = oq_f2h((float)(gauss(&s) * 0.02)); w_bytes(c, &h, 2); }
 }
 static void w_weight(wctx* c, int fmt, uint64_t k, uint64_t n) { if (fmt == 1) w_q4(c, k, n); else w_f16w(c, k, n); }
+/* Test fixture, not a reference format: a Q4 weight whose column j equals
+ * column j % period in every row (one scale per row for all its groups, the
+ * nibbles of the first `period` columns repeated), so a projection through
+ * it gives bit-equal outputs on every column of a residue class.  Used for
+ * the predictor heads to exercise argmax ties (code_predictor.rs:328-334). */
+static int g_tie_period = 0;
+void oq_set_tie_period(int period) { g_tie_period = period > 0 ? period : 0; }
+static void w_q4_tied(wctx* c, uint64_t k, uint64_t n, int period) {
+  uint64_t s = stream_seed(c->seed, ++c->id);
+  w_u64(c, k); w_u64(c, n);
+  w_u64(c, k * n / 2);
+  uint8_t* row = (uint8_t*)malloc(n / 2);
+  uint8_t nib[64];
+  for (uint64_t r = 0; r < k; r++) {
+    for (int j = 0; j < period; j++) nib[j] = (uint8_t)(sm64(&s) & 15u);
+    for (uint64_t j = 0; j < n; j += 2) row[j / 2] = (uint8_t)(nib[j % period] | (nib[(j + 1) % period] << 4));
+    w_bytes(c, row, n / 2);
+  }
+  free(row);
+  w_u64(c, k * n / 32);
+  for (uint64_t r = 0; r < k; r++) {
+    const uint16_t h = oq_f2h((float)fabs(gauss(&s) * 0.02));
+    for (uint64_t g = 0; g < n / 32; g++) w_bytes(c, &h, 2);
+  }
+}
 static void w_norm(wctx* c, uint64_t n) { /* write_f16_vec_io of ones */
   ++c->id;
   w_u64(c, n);
@@ -485,7 +510,10 @@ int oq_synth_write(const char* path, const oq_dims* d, uint64_t seed) {
     w_norm(&c, d->p_hidden); w_norm(&c, d->p_hidden);
   }
   w_u32(&c, d->p_groups);
-  for (int g = 0; g < d->p_groups; g++) w_weight(&c, fmt, d->p_hidden, d->p_vocab);
+  for (int g = 0; g < d->p_groups; g++) {
+    if (fmt == 1 && g_tie_period > 0 && g_tie_period <= 64) w_q4_tied(&c, d->p_hidden, d->p_vocab, g_tie_period);
+    else w_weight(&c, fmt, d->p_hidden, d->p_vocab);
+  }
   w_norm(&c, d->p_hidden);
   {
     size_t n = (size_t)d->p_max_pos * (d->p_head_dim / 2);

@@ -55,6 +55,9 @@ uint16_t oq_f2h(float f);
 
 /* -- synthetic weights in the .qora-tts layout (save.rs:23-137) -- */
 int oq_synth_write(const char* path, const oq_dims* d, uint64_t seed);
+/* Test fixture: predictor heads written with column j == column j % period
+ * (0 = the ordinary synthetic heads); applies to later oq_synth_write calls. */
+void oq_set_tie_period(int period);
 void oq_dims_1p7b(oq_dims* d);
 void oq_dims_tiny(oq_dims* d);
 /* seeded synthetic inputs shared by tests and bench */

@@ -212,6 +212,7 @@ cudaError_t launch_attention(const AttnDesc& d, cudaStream_t st) {
   LaunchOpts o;
   o.pdl = true;
   o.cluster_y = (unsigned)d.nsplit;
+  if (g_occ_query) g_occ_family = FAM_ATTN;
   switch (G) {
     case 1: return launch_k(attn_kernel<1>, grid, dim3(128), 0, st, o, d);
     case 2: return launch_k(attn_kernel<2>, grid, dim3(128), 0, st, o, d);

@@ -694,18 +694,40 @@ static int sync_check(Session& s) {
 // sessions
 // ---------------------------------------------------------------------------
 
-static void free_generation(Session& s) {
+// Ends the generation in progress.  Its buffers and captured frame graph stay
+// for the next generation of the same shape.
+static void free_generation(Session& s) { s.generating = false; }
+
+static void destroy_graph(Session& s) {
   if (s.graph_exec) cudaGraphExecDestroy(s.graph_exec);
   if (s.graph) cudaGraphDestroy(s.graph);
   s.graph_exec = nullptr;
   s.graph = nullptr;
-  for (void* p : s.gen_allocs) cudaFree(p);
-  s.gen_allocs.clear();
-  s.codes = nullptr; s.forced = nullptr; s.trail = nullptr; s.tts_pad = nullptr; s.tp = nullptr; s.tp_h1 = nullptr;
-  s.tp_tok = nullptr; s.recipes = nullptr; s.trail_idx = nullptr; s.voices = nullptr;
-  s.dump_logits = nullptr; s.dump_hidden = nullptr;
-  s.generating = false;
+  s.graph_key = Session::GraphKey{};
   s.frame_kernels = 0;
+}
+
+// Grow-only per-generation buffer `slot` of at least `bytes`.
+static int gen_buf(Session& s, int slot, size_t bytes, void** out) {
+  Session::GenBuf& b = s.gen[slot];
+  bytes = std::max<size_t>(bytes, 16);
+  if (bytes > b.bytes) {
+    if (b.p) cudaFree(b.p);
+    b.p = nullptr;
+    b.bytes = 0;
+    ++s.buf_epoch;
+    if (cudaMalloc(&b.p, bytes) != cudaSuccess) return fail(QTTS_ERR_OOM, "device allocation failed");
+    b.bytes = bytes;
+  }
+  *out = b.p;
+  return QTTS_OK;
+}
+template <class T>
+static int gen_alloc(Session& s, int slot, T** p, size_t count) {
+  void* v = nullptr;
+  RC(gen_buf(s, slot, sizeof(T) * count, &v));
+  *p = static_cast<T*>(v);
+  return QTTS_OK;
 }
 
 static void session_free_all(Session* s) {
@@ -713,6 +735,9 @@ static void session_free_all(Session* s) {
   cudaSetDevice(s->m->device);
   if (s->st) cudaStreamSynchronize(s->st);
   free_generation(*s);
+  destroy_graph(*s);
+  for (auto& b : s->gen)
+    if (b.p) cudaFree(b.p);
   void* bufs[] = {s->kv_pool, s->page_table, s->pkv_pool, s->slots, s->x, s->pin, s->q, s->attn, s->h,
                   s->px, s->px1, s->logits, s->xpre, s->hid1, s->part, s->counters, s->counters2, s->keys,
                   s->apart, s->acounters, s->err_flag, s->codes_plain, s->io, s->ssq_t, s->ssq_p, s->ssq_p1};
@@ -846,6 +871,7 @@ static int ensure_rows(Session& s, int rows) {
   cudaFree(s.acounters);
   s.acounters = nullptr;
   s.rows = rows;
+  ++s.buf_epoch;  // a cached frame graph refers to the old buffers
   RC(dalloc(&s.q, (size_t)rows * qmax));
   RC(dalloc(&s.attn, (size_t)rows * qmax));
   RC(dalloc(&s.h, (size_t)rows * imax));
@@ -903,18 +929,24 @@ static int generate_begin(Session& s, int n, const qtts_utterance* u, int F, uns
   s.max_trail = max_trail;
   s.flags = flags;
   const int Nt = (int)tok.size();
-  std::vector<void*>& T = s.gen_allocs;
-  RC(dalloc(&s.codes, (size_t)n * F * kMaxGroups, &T));
-  if (forced) RC(dalloc(&s.forced, (size_t)n * F * kMaxGroups, &T));
-  RC(dalloc(&s.tp, (size_t)Nt * H, &T));
-  RC(dalloc(&s.tp_h1, (size_t)Nt * m.fc1.n, &T));
-  RC(dalloc(&s.tp_tok, (size_t)Nt, &T));
-  RC(dalloc(&s.recipes, (size_t)n * max_prefill, &T));
-  RC(dalloc(&s.trail, (size_t)n * max_trail * H, &T));
-  RC(dalloc(&s.trail_idx, (size_t)n * max_trail, &T));
-  RC(dalloc(&s.voices, (size_t)std::max(n_voice, 1) * H, &T));
-  if (dump_logits) RC(dalloc(&s.dump_logits, (size_t)n * F * d.t_vocab, &T));
-  if (dump_hidden) RC(dalloc(&s.dump_hidden, (size_t)n * F * H, &T));
+  RC(gen_alloc(s, 0, &s.codes, (size_t)n * F * kMaxGroups));
+  s.forced = nullptr;
+  if (forced) RC(gen_alloc(s, 1, &s.forced, (size_t)n * F * kMaxGroups));
+  RC(gen_alloc(s, 2, &s.tp, (size_t)Nt * H));
+  RC(gen_alloc(s, 3, &s.tp_h1, (size_t)Nt * m.fc1.n));
+  RC(gen_alloc(s, 4, &s.tp_tok, (size_t)Nt));
+  RC(gen_alloc(s, 5, &s.recipes, (size_t)n * max_prefill));
+  RC(gen_alloc(s, 6, &s.trail, (size_t)n * max_trail * H));
+  RC(gen_alloc(s, 7, &s.trail_idx, (size_t)n * max_trail));
+  RC(gen_alloc(s, 8, &s.voices, (size_t)std::max(n_voice, 1) * H));
+  s.dump_logits = nullptr;
+  s.dump_hidden = nullptr;
+  if (dump_logits) RC(gen_alloc(s, 9, &s.dump_logits, (size_t)n * F * d.t_vocab));
+  if (dump_hidden) RC(gen_alloc(s, 10, &s.dump_hidden, (size_t)n * F * H));
+  // frames an utterance never reaches (EOS) read back as zero
+  CK(cudaMemsetAsync(s.codes, 0, sizeof(uint32_t) * n * F * kMaxGroups, s.st));
+  if (s.dump_logits) CK(cudaMemsetAsync(s.dump_logits, 0, sizeof(float) * n * F * d.t_vocab, s.st));
+  if (s.dump_hidden) CK(cudaMemsetAsync(s.dump_hidden, 0, sizeof(float) * n * F * H, s.st));
   if (forced) CK(cudaMemcpy(s.forced, forced, sizeof(uint32_t) * n * F * kMaxGroups, cudaMemcpyHostToDevice));
   CK(cudaMemcpy(s.tp_tok, tok.data(), sizeof(uint32_t) * Nt, cudaMemcpyHostToDevice));
   // prefill recipes (generate_new.rs:94-173) and trailing text rows (:314-326)
@@ -1000,7 +1032,15 @@ static int generate_begin(Session& s, int n, const qtts_utterance* u, int F, uns
   }
   RC(sync_check(s));
 
-  // frame plan -> CUDA graph
+  // frame plan -> CUDA graph, reused while nothing it bakes in has changed
+  Session::GraphKey key;
+  key.B = n; key.F = F; key.max_trail = max_trail; key.forced = forced ? 1 : 0;
+  key.dump_logits = dump_logits ? 1 : 0; key.dump_hidden = dump_hidden ? 1 : 0; key.epoch = s.buf_epoch;
+  if (s.graph_exec && s.graph_key == key) {
+    s.generating = true;
+    return QTTS_OK;
+  }
+  destroy_graph(s);
   std::vector<Op> fops;
   RC(build_frame_ops(s, fops, dump_logits || dump_hidden));
   CK(cudaStreamBeginCapture(s.st, cudaStreamCaptureModeThreadLocal));
@@ -1016,6 +1056,8 @@ static int generate_begin(Session& s, int n, const qtts_utterance* u, int F, uns
   if (ce != cudaSuccess) return fail(QTTS_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
   s.graph = g;
   CK(cudaGraphInstantiate(&s.graph_exec, g, 0));
+  s.graph_key = key;
+  ++s.graph_captures;
   s.generating = true;
   return QTTS_OK;
 }
@@ -1039,6 +1081,73 @@ static int generate_end(Session& s, uint32_t* codes, int* frames_out, float* dl,
   }
   if (dl && s.dump_logits) CK(cudaMemcpy(dl, s.dump_logits, sizeof(float) * n * F * d.t_vocab, cudaMemcpyDeviceToHost));
   if (dh && s.dump_hidden) CK(cudaMemcpy(dh, s.dump_hidden, sizeof(float) * n * F * d.t_hidden, cudaMemcpyDeviceToHost));
+  return QTTS_OK;
+}
+
+// Profiling: one frame's launches of kernel family `fam`, built exactly as
+// the frame plan builds them (order, parameters, dependent-launch links,
+// L2-prefetch targets), captured without the frame's other launches and
+// replayed `reps` times between events on the session stream.  The replays
+// rewrite the current frame's cache entries, activations and codes, so the
+// generation in progress ends here.
+static int family_time(Session& s, int fam, int reps, float* ms, int* launches, double* flops, double* wbytes) {
+  if (!s.graph_exec) return fail(QTTS_ERR_STATE, "no frame plan: begin a generation first");
+  if (reps <= 0 || reps > 100000) return fail(QTTS_ERR_BADARG, "bad repetition count");
+  CK(cudaStreamSynchronize(s.st));
+  std::vector<Op> fops, sel;
+  RC(build_frame_ops(s, fops, false));
+  double fl = 0.0, wb = 0.0;
+  for (const Op& op : fops) {  // sort by family without launching
+    g_occ_query = true;
+    g_occ_family = FAM_OTHER;
+    g_occ_flops = g_occ_wbytes = 0.0;
+    const cudaError_t qe = op(nullptr);
+    g_occ_query = false;
+    if (qe != cudaSuccess) return fail(QTTS_ERR_CUDA, std::string("launch plan: ") + cudaGetErrorString(qe));
+    if (g_occ_family == fam) {
+      sel.push_back(op);
+      fl += g_occ_flops;
+      wb += g_occ_wbytes;
+    }
+  }
+  s.generating = false;
+  *ms = 0.0f;
+  *launches = 0;
+  *flops = fl;
+  *wbytes = wb;
+  if (sel.empty()) return QTTS_OK;
+  CK(cudaStreamBeginCapture(s.st, cudaStreamCaptureModeThreadLocal));
+  const long l0 = g_kernel_launches;
+  const int rc = run_ops(s, sel);
+  const int nl = (int)(g_kernel_launches - l0);
+  cudaGraph_t g = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(s.st, &g);
+  if (rc != QTTS_OK) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (ce != cudaSuccess) return fail(QTTS_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
+  cudaGraphExec_t ge = nullptr;
+  const cudaError_t ie = cudaGraphInstantiate(&ge, g, 0);
+  cudaGraphDestroy(g);
+  if (ie != cudaSuccess) return fail(QTTS_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ie));
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  cudaError_t err = cudaEventCreate(&e0);
+  if (err == cudaSuccess) err = cudaEventCreate(&e1);
+  for (int i = 0; err == cudaSuccess && i < 3; ++i) err = cudaGraphLaunch(ge, s.st);  // warm-up
+  if (err == cudaSuccess) err = cudaEventRecord(e0, s.st);
+  for (int i = 0; err == cudaSuccess && i < reps; ++i) err = cudaGraphLaunch(ge, s.st);
+  if (err == cudaSuccess) err = cudaEventRecord(e1, s.st);
+  if (err == cudaSuccess) err = cudaEventSynchronize(e1);
+  float t = 0.0f;
+  if (err == cudaSuccess) err = cudaEventElapsedTime(&t, e0, e1);
+  if (e0) cudaEventDestroy(e0);
+  if (e1) cudaEventDestroy(e1);
+  cudaGraphExecDestroy(ge);
+  if (err != cudaSuccess) return fail(QTTS_ERR_CUDA, std::string("family replay: ") + cudaGetErrorString(err));
+  RC(sync_check(s));
+  *ms = t / (float)reps;
+  *launches = nl;
   return QTTS_OK;
 }
 
@@ -1381,6 +1490,14 @@ int qtts_generate(qtts_session* h, int n_utt, const qtts_utterance* utts, int ma
   return generate_end(s, codes_out, frames_out, logits_dump, hidden_dump);
 }
 int qtts_frame_kernel_count(qtts_session* h) { return h ? h->s->frame_kernels : 0; }
+int qtts_frame_graph_captures(qtts_session* h) { return h ? h->s->graph_captures : 0; }
+int qtts_frame_family_time(qtts_session* h, int family, int reps, float* ms, int* launches, double* flops,
+                           double* weight_bytes) {
+  SESS(h);
+  if (!ms || !launches || !flops || !weight_bytes) return fail(QTTS_ERR_BADARG, "null output");
+  if (family < FAM_Q4MV_DEC || family > FAM_ATTN) return fail(QTTS_ERR_BADARG, "unknown kernel family");
+  return family_time(s, family, reps, ms, launches, flops, weight_bytes);
+}
 
 size_t qtts_q4_gemv_scratch_bytes(int k, int n, int m) {
   if (k <= 0 || n <= 0 || m <= 0) return 0;

@@ -97,7 +97,28 @@ struct Session {
   cudaGraphExec_t graph_exec = nullptr;
   int frame_kernels = 0;
   bool generating = false;
-  std::vector<void*> gen_allocs;
+  // Per-generation device buffers (codes, forcing, text rows, dumps, ...),
+  // grow-only: a buffer moves only when a generation needs more than it
+  // holds, which bumps buf_epoch.  The frame graph bakes in pointers, so it
+  // is reused across generations while graph_key (batch, frames, trailing
+  // rows, forcing and dumps, buffer epoch) is unchanged.
+  struct GenBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+  };
+  static constexpr int kGenBufs = 11;
+  GenBuf gen[kGenBufs];
+  unsigned long buf_epoch = 0;
+  struct GraphKey {
+    int B = -1, F = -1, max_trail = -1, forced = 0, dump_logits = 0, dump_hidden = 0;
+    unsigned long epoch = 0;
+    bool operator==(const GraphKey& o) const {
+      return B == o.B && F == o.F && max_trail == o.max_trail && forced == o.forced &&
+             dump_logits == o.dump_logits && dump_hidden == o.dump_hidden && epoch == o.epoch;
+    }
+  };
+  GraphKey graph_key;
+  int graph_captures = 0;  // frame graphs captured by this session (cache misses)
 };
 
 }  // namespace qtts

@@ -734,6 +734,15 @@ static cudaError_t launch_mb(const GemvDesc& d, const FrameCodes& fc, cudaStream
 bool gemv_uses_decode_kernel(const GemvDesc& d) { return !d.tc && use_dec(d); }
 
 cudaError_t launch_gemv(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
+  if (g_occ_query) {  // family and algorithmic work of this launch (profiling)
+    g_occ_family = d.tc ? FAM_TC_PROJ : (use_dec(d) ? FAM_Q4MV_DEC : FAM_Q4MV_ROWS);
+    g_occ_flops = g_occ_wbytes = 0.0;
+    for (int i = 0; i < (d.paired ? 2 : d.nmat); ++i) {
+      const double kn = (double)d.mat[i].k * d.mat[i].n;
+      g_occ_flops += 2.0 * d.M * kn;
+      g_occ_wbytes += kn * 0.5625;
+    }
+  }
   if (d.attn_in && (d.tc || !use_dec(d) || d.rows_per_split != kHeadDim || d.epi_kind != EPI_RESID))
     return cudaErrorInvalidValue;  // the attention prologue lives in the decode kernel only
   if (d.x_glu && (d.tc || !use_dec(d) || d.gamma || d.emb_idx || d.attn_in || d.paired || d.epi_kind != EPI_RESID))

@@ -210,6 +210,13 @@ inline thread_local long g_kernel_launches = 0;
 // at once (cudaOccupancyMaxActiveClusters), so planners can size one wave.
 inline thread_local bool g_occ_query = false;
 inline thread_local int g_occ_clusters = 0;
+// Kernel family of the last launch issued in occupancy-query mode, and the
+// algorithmic work of a projection launch (useful FLOPs 2*M*k*n, Q4 weight
+// bytes k*n*0.5625): lets the profiling entry point sort a frame's launches
+// by family without launching them.
+enum KernelFamily : int { FAM_OTHER = 0, FAM_Q4MV_DEC = 1, FAM_Q4MV_ROWS = 2, FAM_TC_PROJ = 3, FAM_ATTN = 4 };
+inline thread_local int g_occ_family = FAM_OTHER;
+inline thread_local double g_occ_flops = 0.0, g_occ_wbytes = 0.0;
 int occupancy_clusters(const void* func, const cudaLaunchConfig_t& cfg);
 struct LaunchOpts {
   bool pdl = false;

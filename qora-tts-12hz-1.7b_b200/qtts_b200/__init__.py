@@ -24,6 +24,8 @@ ERR_BADARG, ERR_OOM, ERR_CUDA, ERR_TIMEOUT, ERR_FORMAT, ERR_IO, ERR_STATE, ERR_N
     -1, -2, -3, -4, -5, -6, -7, -8, -9)
 IGNORE_EOS = 1
 FULL_PROMPT = 2  # benchmark mode: the whole text prefilled (qtts.h QTTS_FULL_PROMPT)
+# kernel families of the frame plan (qtts.h QTTS_FAMILY_*)
+FAMILY_Q4MV_DEC, FAMILY_Q4MV_ROWS, FAMILY_TC_PROJ, FAMILY_ATTN = 1, 2, 3, 4
 
 
 class QttsError(RuntimeError):
@@ -92,6 +94,9 @@ def _load():
         "qtts_generate_frames": (C.c_int, [P, C.c_int]),
         "qtts_generate_end": (C.c_int, [P, u32p, C.POINTER(C.c_int), fp, fp]),
         "qtts_frame_kernel_count": (C.c_int, [P]),
+        "qtts_frame_graph_captures": (C.c_int, [P]),
+        "qtts_frame_family_time": (C.c_int, [P, C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_int),
+                                             C.POINTER(C.c_double), C.POINTER(C.c_double)]),
         "qtts_q4_gemv_scratch_bytes": (C.c_size_t, [C.c_int, C.c_int, C.c_int]),
         "qtts_q4_gemv_dev": (C.c_int, [P, P, C.c_int, C.c_int, P, C.c_int, P, P, C.c_size_t, P]),
         "qtts_q4_gemv": (C.c_int, [C.POINTER(C.c_uint8), C.POINTER(C.c_uint16), C.c_int, C.c_int, fp,
@@ -205,6 +210,20 @@ class Session:
 
     def frame_kernel_count(self) -> int:
         return lib.qtts_frame_kernel_count(self.h)
+
+    def graph_captures(self) -> int:
+        """Frame graphs captured so far (a generation of an unchanged shape
+        reuses the last one)."""
+        return lib.qtts_frame_graph_captures(self.h)
+
+    def family_time(self, family: int, reps: int = 50) -> dict:
+        """Profiling: device time of one frame's launches of one kernel
+        family replayed alone (qtts.h qtts_frame_family_time).  Ends the
+        generation in progress."""
+        ms, n = C.c_float(), C.c_int()
+        fl, wb = C.c_double(), C.c_double()
+        _check(lib.qtts_frame_family_time(self.h, family, reps, C.byref(ms), C.byref(n), C.byref(fl), C.byref(wb)))
+        return {"ms": ms.value, "launches": n.value, "flops": fl.value, "weight_bytes": wb.value}
 
 
 # ---- reference-facing functions (talker.rs / code_predictor.rs / generate_new.rs)

@@ -278,3 +278,118 @@ def test_full_prompt_ragged_batch_tiny(qtts, gpu_tiny, tiny_oracle, oracle_mod):
     # the mode changes the trajectory: the default mode's first logits differ
     plain = _oracle_run(oracle_mod, tiny_oracle, utts[1], 1, False)
     assert rel_err(plain["logits"][0], ref[1]["logits"][0]) > 1e-3
+
+
+def test_frame_graph_reused_across_generations(qtts, gpu_tiny):
+    # qtts_generate keeps the frame graph (and the per-generation buffers it
+    # points at) between calls of the same shape; calls of other shapes, with
+    # and without forcing and dumps, in any order, must still give what a
+    # fresh session gives
+    H = gpu_tiny.dims.t_hidden
+    gs, gg = golden("tiny_sampled"), golden("tiny_greedy")
+    us, ug = tiny_case("tiny_sampled", H), tiny_case("tiny_greedy", H)
+    F = 12
+    s = qtts.Session(gpu_tiny, 3, 10 + F + 8)
+    for _ in range(2):
+        c, f, lg, _ = qtts.generate(s, [us], F, dump_logits=True)
+        assert np.array_equal(c[0], gs["codes"][:F])
+        c, f, _, _ = qtts.generate(s, [ug], F, forced=gg["codes"][None, :F])
+        assert np.array_equal(c[0], gg["codes"][:F])
+        c, f, _, _ = qtts.generate(s, [ug, us], F)
+        assert np.array_equal(c[1], gs["codes"][:F])
+        c, f, _, _ = qtts.generate(s, [us], F + 8)
+        assert np.array_equal(c[0][:F], gs["codes"][:F])
+    s.close()
+
+
+def _golden_or_skip(name):
+    import os
+    from conftest import GOLDEN
+    if not os.path.exists(os.path.join(GOLDEN, name + ".npz")):
+        pytest.skip(f"fixture {name} not generated (tests/golden/make_golden.py --only {name})")
+    return golden(name)
+
+
+def test_long_kv_tiny_2000_frames(qtts, gpu_tiny):
+    # config-3 sampling (T=0.8, top-k 50, seed 42) for 2000 frames: the
+    # talker attention runs over up to ~2010 cached positions
+    # (talker.rs:305-331, softmax_raw gemv.rs:434-445), split across CTAs
+    g = golden("tiny_long_kv")
+    F = g["codes"].shape[0]
+    assert F == 2000
+    s = qtts.Session(gpu_tiny, 1, 10 + F + 1)
+    codes, frames, lg, _ = qtts.generate(s, [tiny_case("tiny_sampled", gpu_tiny.dims.t_hidden)], F,
+                                         forced=g["codes"][None], dump_logits=True)
+    s.close()
+    assert frames[0] == F
+    _check_forced(codes[0], g, lg[0])
+
+
+@pytest.mark.parametrize("copies", [1, 20])
+def test_argmax_exact_ties_last_index_wins(qtts, oracle_mod, tmp_path, copies):
+    # predictor heads whose column j equals column j % 7: every group's
+    # logits tie exactly across ~292 columns, and the reference's
+    # max_by(partial_cmp) returns the LAST maximal index
+    # (code_predictor.rs:328-334).  One utterance runs the one-row decode
+    # kernel's argmax epilogue, twenty the tensor-core kernel's; both must pick
+    # the oracle's index (2041..2047) in every group of every frame.
+    path = str(tmp_path / "tied.qora-tts")
+    oracle_mod.synth_write_tied_heads(path, oracle_mod.dims_tiny(), 0, 7)
+    om = oracle_mod.Model(path)
+    gm = qtts.Model(path, 0)
+    H = gm.dims.t_hidden
+    base = [tiny_case("tiny_greedy", H), tiny_case("tiny_sampled", H)]
+    F = 6
+    refs = [_oracle_run(oracle_mod, om, u, F, False) for u in base]
+    for r in refs:
+        assert np.all(r["codes"][:, 1:] >= 2041), r["codes"]
+    utts = (base * copies)[:max(copies, 1)] if copies > 1 else base[:1]
+    ref_of = [refs[i % 2] for i in range(len(utts))]
+    s = qtts.Session(gm, len(utts), 10 + F + 1)
+    forced = np.stack([r["codes"] for r in ref_of]).astype(np.uint32)
+    codes, frames, lg, _ = qtts.generate(s, utts, F, forced=forced, dump_logits=True)
+    s.close()
+    gm.close()
+    om.close()
+    for i, r in enumerate(ref_of):
+        assert np.array_equal(codes[i][:, 1:], r["codes"][:, 1:]), (i, codes[i][:, 1:], r["codes"][:, 1:])
+        _check_forced(codes[i], r, lg[i])
+
+
+@pytest.mark.slow
+def test_1p7b_config3_2000_frames_teacher_forced(qtts, gpu_1p7b):
+    # benchmark config 3 in full: 96-token prompt, T=0.8 / top-k 50 / seed 42,
+    # 2000 frames, the cache growing to ~2010 positions
+    from qtts_b200 import workload as W
+    g = _golden_or_skip("p1p7b_config3_2000")
+    u, F = W.config3(2048)
+    assert g["codes"].shape[0] == F
+    s = qtts.Session(gpu_1p7b, 1, 10 + F + 1)
+    codes, frames, lg, _ = qtts.generate(s, [u], F, forced=g["codes"][None], dump_logits=True)
+    s.close()
+    assert frames[0] == F
+    ties = _check_forced(codes[0], g, lg[0], max_ties=2)
+    print("near-ties tolerated:", ties)
+
+
+@pytest.mark.slow
+def test_1p7b_config4_64_utterances_teacher_forced(qtts, gpu_1p7b):
+    # benchmark config 4's 64 distinct utterances (prompts of 16-256 tokens
+    # trailing into the frames, own voice and seed each, T=0.8 / top-k 50) in
+    # one batch: every projection runs the tensor-core kernel at 64 rows (the
+    # compact-stage instance fed by the expanded weights; the predictor's
+    # two-row first step at 128 rows), and each utterance must follow its own
+    # oracle run
+    from qtts_b200 import workload as W
+    g = _golden_or_skip("p1p7b_config4_64")
+    utts, _ = W.config4(64, 2048)
+    F = g["codes"].shape[1]
+    s = qtts.Session(gpu_1p7b, 64, 10 + F + 1)
+    codes, frames, lg, _ = qtts.generate(s, utts, F, forced=g["codes"], dump_logits=True)
+    s.close()
+    ties = 0
+    for i in range(64):
+        assert frames[i] == F
+        gi = {k: (g[k][i] if np.ndim(g[k]) > 0 else g[k]) for k in g}
+        ties += _check_forced(codes[i], gi, lg[i], max_ties=1)
+    print("near-ties tolerated:", ties)
