@@ -77,6 +77,9 @@ struct Session {
   // per-256-column sums of squares of residual rows (talker, predictor
   // prefill rows, predictor decode rows), row stride kSsqLd
   float *ssq_t = nullptr, *ssq_p = nullptr, *ssq_p1 = nullptr;
+  // one-row layer phases: two residual rows, then the attention phases'
+  // and the MLP phases' partial rows ([kPhaseMaxParts][kPhaseMaxH] each)
+  float* ph = nullptr;
   size_t io_floats = 0;
   // generation
   int B = 0, max_frames = 0, max_trail = 0;

@@ -290,6 +290,16 @@ __global__ void __launch_bounds__(kGemvThreads) q4mv_dec_kernel(const GemvDesc d
       xv[i] = rb < R ? xr[r0 + rb] : 0.0f;
       xg[i] = (kGlu && d.x_glu && rb < R) ? xr[d.x_glu + r0 + rb] : 0.0f;
     }
+    if (kNorm && d.nparts) {  // residual partials of the layer phases, added in order
+      for (int p = 0; p < d.nparts; ++p) {
+        const float* pr = d.parts + (size_t)p * d.parts_ld;
+#pragma unroll
+        for (int i = 0; i < NR; ++i) {
+          const int rb = rb0 + 32 * i;
+          if (rb < R) xv[i] += pr[r0 + rb];
+        }
+      }
+    }
     // the producer's per-tile sums of squares (at most 16 tiles here)
     const bool ssq16 = kNorm && d.gamma && d.ssq_in && d.ssq_n <= 16;
     float sv[16];
@@ -308,7 +318,11 @@ __global__ void __launch_bounds__(kGemvThreads) q4mv_dec_kernel(const GemvDesc d
         inv = inv_rms_from_ssq(d, m);
       } else {
         float ss = 0.0f;
-        for (int i = tid; i < d.k; i += kGemvThreads) ss += xr[i] * xr[i];
+        for (int i = tid; i < d.k; i += kGemvThreads) {
+          float v = xr[i];
+          for (int p = 0; p < d.nparts; ++p) v += d.parts[(size_t)p * d.parts_ld + i];
+          ss += v * v;
+        }
         ss = block_sum_256(ss, sbuf);
         inv = 1.0f / sqrtf(ss / (float)d.k + 1e-6f);
       }
@@ -750,6 +764,8 @@ cudaError_t launch_gemv(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st
   if (!d.tc && use_dec(d) &&
       ((d.emb_idx && d.epi_kind != EPI_STORE) || (d.gamma && d.epi_kind == EPI_RESID)))
     return cudaErrorInvalidValue;  // prologue forms the decode kernel compiles per epilogue
+  if (d.nparts && (d.tc || !use_dec(d) || !d.gamma || d.ssq_in || d.emb_idx || d.attn_in || d.x_glu))
+    return cudaErrorInvalidValue;  // residual partials: the decode kernel's full-row RMSNorm prologue only
   if (d.tc) return launch_tc(d, fc, st);
   if (d.ntiles <= 0 || d.S <= 0 || d.M <= 0 || d.rows_per_split <= 0) return cudaErrorInvalidValue;
   if (d.cluster && d.S > kMaxClusterSplits) return cudaErrorInvalidValue;
