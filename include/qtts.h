@@ -104,6 +104,15 @@ QTTS_API int qtts_session_create(qtts_model* m, int max_batch, int max_positions
 QTTS_API int qtts_session_free(qtts_session* s);
 QTTS_API int qtts_session_reset(qtts_session* s);
 QTTS_API void* qtts_session_stream(qtts_session* s); /* cudaStream_t the session launches on */
+/* No counterpart in the reference (it has no failure detection: it panics).
+ * Bound, in nanoseconds, on the device wait in which the one-row GEMV's
+ * cluster root collects its peers' split-K partials (default 1 s; takes
+ * effect for the next generation or per-call step).  A wait that runs out
+ * makes the call return QTTS_ERR_TIMEOUT, and keeps waiting for at most 1 s
+ * more so that no peer's transfer is left in flight into the waiting CTA;
+ * the outputs of such a call are undefined.  A short budget exercises the
+ * timeout path without a GPU fault. */
+QTTS_API int qtts_session_set_wait_budget(qtts_session* s, uint64_t ns);
 
 /* ---- per-call reference API (slot 0 of the session, batch 1) ------------- */
 QTTS_API int qtts_embed_text(qtts_session* s, uint32_t token, float* out);  /* talker.rs:105 */

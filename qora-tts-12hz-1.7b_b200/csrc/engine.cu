@@ -257,7 +257,6 @@ static int model_load(const char* path, int device, Model** out) {
   gemv_init_attributes();
   attn_init_attributes();
   tc_init_attributes();
-  phase_init_attributes();
   expand_weights(m);
   *out = m;
   return QTTS_OK;
@@ -393,6 +392,7 @@ static int plan_gemv(Session& s, GemvDesc& g) {
   fit_split_to_wave(g);
   try_global_split(s, g);
   g.err_flag = s.err_flag;
+  g.wait_ns = s.wait_ns;
   if (g.M >= kTcMinRows) {
     tc_plan(s.m->sm_count, g);  // one tcgen05 kernel: prologue, GEMM, split-K, epilogue
     g.part = s.part;
@@ -558,99 +558,11 @@ static int talker_nsplit(Session& s, int M) {
   return std::max(1, std::min(kMaxClusterSplits, std::min(byL, byPar)));
 }
 
-// Where a layer stack's output row lives: X (+ the partial rows `parts`
-// added on read when the stack ran as one-row phases).
-struct StackOut {
-  const float* parts = nullptr;  // [nparts][ld]
-  int nparts = 0;
-  const float* X = nullptr;
-  long ld = 0;
-};
-
-// The weights of q (x3) as L2-prefetch regions (packed, scales) of a GemvDesc.
-static void set_prefetch(const uint8_t** ptr, uint32_t* bytes, int nreg, std::initializer_list<Q4Mat> mats) {
-  int i = 0;
-  for (const Q4Mat& w : mats) {
-    if (i + 2 > nreg || !w.packed) break;
-    ptr[i] = w.packed;
-    bytes[i] = (uint32_t)((size_t)w.k * w.n / 2);
-    ptr[i + 1] = reinterpret_cast<const uint8_t*>(w.scales);
-    bytes[i + 1] = (uint32_t)(((size_t)w.k * w.n / 32 * 2) & ~(size_t)15);
-    i += 2;
-  }
-}
-
-// A stack of layers at one input row as attention / MLP phases (phase.cu):
-// two launches per layer instead of five.  `x0` is the stack's input row;
-// `next` the weights of the launch that follows the stack (L2 prefetch).
-// Returns false when a shape is not covered (the caller keeps the
-// per-projection plan).
-static bool phases_supported(const qtts_dims& d, bool talker) {
-  int C, U, CB;
-  const int H = talker ? d.t_hidden : d.p_hidden;
-  return attn_phase_supported(H, talker ? d.t_heads : d.p_heads, talker ? d.t_kv_heads : d.p_kv_heads, &C) &&
-         mlp_phase_supported(H, talker ? d.t_inter : d.p_inter, &U, &CB);
-}
-static StackOut add_stack_phases(Session& s, std::vector<Op>& ops, const std::vector<DLayer>& layers, const LayerIO& io,
-                                 const float* x0, const Q4Mat& next) {
-  const int H = layers[0].q.k;
-  int CA = 0, U = 0, CB = 0;
-  attn_phase_supported(H, io.heads, io.kvh, &CA);
-  mlp_phase_supported(H, io.inter, &U, &CB);
-  float* r[2] = {s.ph, s.ph + kPhaseMaxH};
-  float* pa = s.ph + 2 * kPhaseMaxH;
-  float* pb = pa + (size_t)kPhaseMaxParts * kPhaseMaxH;
-  const int ncl = io.inter / (32 * U) / CB;
-  // the launch before the stack pulls the first layer's q/k/v into L2
-  if (g_prev_gemv) set_prefetch(g_prev_gemv->pf_ptr, g_prev_gemv->pf_bytes, 6, {layers[0].q, layers[0].k, layers[0].v});
-  g_prev_gemv.reset();
-  PhaseResid in;
-  in.base = x0;
-  const int n = (int)layers.size();
-  for (int l = 0; l < n; ++l) {
-    const DLayer& L = layers[l];
-    auto a = std::make_shared<AttnPhaseDesc>();
-    a->H = H; a->kvh = io.kvh; a->C = CA; a->in = in; a->in.out = r[0]; a->gamma = L.in_norm;
-    a->q = L.q; a->k = L.k; a->v = L.v; a->o = L.o; a->q_norm = L.q_norm; a->k_norm = L.k_norm;
-    a->rope_cos = io.cos; a->rope_sin = io.sin; a->rope_rows = io.rope_rows; a->rope_skip_oob = io.skip_oob;
-    a->kv = io.kv; a->kv.layer = l; a->rp = io.rp; a->parts_out = pa; a->err_flag = s.err_flag;
-    set_prefetch(a->pf_ptr, a->pf_bytes, 8, {L.gate, L.up, L.down});
-    auto b = std::make_shared<MlpPhaseDesc>();
-    b->H = H; b->I = io.inter; b->U = U; b->C = CB;
-    b->in.base = r[0]; b->in.parts = pa; b->in.nparts = io.kvh; b->in.out = r[1];
-    b->gamma = L.post_norm; b->gate = L.gate; b->up = L.up; b->down = L.down; b->parts_out = pb;
-    if (l + 1 < n) set_prefetch(b->pf_ptr, b->pf_bytes, 8, {layers[l + 1].q, layers[l + 1].k, layers[l + 1].v, layers[l + 1].o});
-    else set_prefetch(b->pf_ptr, b->pf_bytes, 8, {next});
-    ops.push_back([a](cudaStream_t st) { return launch_attn_phase(*a, st); });
-    ops.push_back([b](cudaStream_t st) { return launch_mlp_phase(*b, st); });
-    in.base = r[1];
-    in.parts = pb;
-    in.nparts = ncl;
-    in.out = nullptr;
-  }
-  StackOut o;
-  o.X = r[1];
-  o.parts = pb;
-  o.nparts = ncl;
-  o.ld = H;
-  return o;
-}
-
 // Talker layers over rows X (decode: one row per session; prefill: seq rows).
 // ssq0: sums of squares of the input rows when their producer left them.
-// One decode row runs the layer phases; `out` then says where the row is.
 static int add_talker(Session& s, std::vector<Op>& ops, float* X, long ldx, int M, const RowPos& rp, int nsplit,
-                      bool ssq0, StackOut* out = nullptr) {
+                      bool ssq0) {
   const Model& m = *s.m;
-  if (out) *out = StackOut{nullptr, 0, X, 0};
-  if (M == 1 && out && phases_supported(m.d, true)) {
-    LayerIO io;
-    io.X = X; io.ldx = ldx; io.M = 1; io.rp = rp; io.kv = talker_kv(s, 0);
-    io.cos = m.t_cos; io.sin = m.t_sin; io.rope_rows = m.d.t_max_pos; io.skip_oob = 0;
-    io.heads = m.d.t_heads; io.kvh = m.d.t_kv_heads; io.inter = m.d.t_inter;
-    *out = add_stack_phases(s, ops, m.tl, io, X, m.codec_head);
-    return QTTS_OK;
-  }
   for (int l = 0; l < m.d.t_layers; ++l) {
     LayerIO io;
     io.X = X; io.ldx = ldx; io.M = M; io.rp = rp; io.kv = talker_kv(s, l);
@@ -667,15 +579,10 @@ static int add_talker(Session& s, std::vector<Op>& ops, float* X, long ldx, int 
 // Rows X are the talker residual rows whose sums of squares are in s.ssq_t
 // (row r of X <-> ssq row ssq_row0 + r * ssq_rows_step).
 static int add_codec_head(Session& s, std::vector<Op>& ops, const float* X, long ldx, int M, float* logits,
-                          float* hid, long ldh, long ssq_row0 = 0, long ssq_rows_step = 1,
-                          const StackOut* so = nullptr) {
+                          float* hid, long ldh, long ssq_row0 = 0, long ssq_rows_step = 1) {
   GemvDesc g = gemv_base(EPI_STORE, {s.m->codec_head}, false, M);
   g.X = X; g.ldx = ldx; g.gamma = s.m->t_final;
   g.ssq_in = s.ssq_t + ssq_row0 * kSsqLd; g.ssq_ld = ssq_rows_step * kSsqLd; g.ssq_n = ceil_div(s.m->d.t_hidden, kSsqCols);
-  if (so && so->nparts) {  // the row as the layer phases left it: X + partial rows
-    g.X = so->X; g.ssq_in = nullptr; g.ssq_n = 0;
-    g.parts = so->parts; g.nparts = so->nparts; g.parts_ld = so->ld;
-  }
   g.epi.out = logits; g.epi.ldo = s.m->d.t_vocab;
   g.xnorm_out = hid; g.ld_xnorm = ldh;
   RC(plan_gemv(s, g));
@@ -712,16 +619,11 @@ static int add_predictor(Session& s, std::vector<Op>& ops, int B, bool frame_mod
   RowPos rp0;
   rp0.rows_per_sess = 2;  // prefill positions 0, 1 (code_predictor.rs:244, :369)
   RC(layers(s.px, 2 * B, rp0, s.ssq_p));
-  auto head = [&](const float* X, long ldx, int g, const float* ssq, long ssq_ld,
-                  const StackOut* so = nullptr) -> int {
+  auto head = [&](const float* X, long ldx, int g, const float* ssq, long ssq_ld) -> int {
     // final norm + lm_heads[g] + argmax
     GemvDesc h = gemv_base(EPI_ARGMAX, {m.lm[g]}, false, B);
     h.X = X; h.ldx = ldx; h.gamma = m.p_final;
     h.ssq_in = ssq; h.ssq_ld = ssq_ld; h.ssq_n = pnt;
-    if (so && so->nparts) {  // the row as the layer phases left it
-      h.X = so->X; h.ssq_in = nullptr; h.ssq_n = 0;
-      h.parts = so->parts; h.nparts = so->nparts; h.parts_ld = so->ld;
-    }
     h.epi.group = g + 1; h.epi.frame_codes = frame_mode ? 1 : 0; h.epi.codes_plain = s.codes_plain;
     RC(plan_gemv(s, h));
     ops.push_back(gemv_op(h, fc));
@@ -744,15 +646,6 @@ static int add_predictor(Session& s, std::vector<Op>& ops, int B, bool frame_mod
     ops.push_back(gemv_op(pe));
     RowPos rp;
     rp.pos_const = g + 1;
-    if (B == 1 && phases_supported(d, false)) {  // one row: the layer phases
-      LayerIO io;
-      io.X = s.px1; io.ldx = pH; io.M = 1; io.rp = rp; io.kv = pred_kv(s, 0);
-      io.cos = m.p_cos; io.sin = m.p_sin; io.rope_rows = d.p_max_pos; io.skip_oob = 1;
-      io.heads = d.p_heads; io.kvh = d.p_kv_heads; io.inter = d.p_inter;
-      const StackOut so = add_stack_phases(s, ops, m.pl, io, s.px1, m.lm[g]);
-      RC(head(s.px1, pH, g, nullptr, 0, &so));
-      continue;
-    }
     RC(layers(s.px1, B, rp, s.ssq_p1));
     RC(head(s.px1, pH, g, s.ssq_p1, kSsqLd));
   }
@@ -848,7 +741,7 @@ static void session_free_all(Session* s) {
     if (b.p) cudaFree(b.p);
   void* bufs[] = {s->kv_pool, s->page_table, s->pkv_pool, s->slots, s->x, s->pin, s->q, s->attn, s->h,
                   s->px, s->px1, s->logits, s->xpre, s->hid1, s->part, s->counters, s->counters2, s->keys,
-                  s->apart, s->acounters, s->err_flag, s->codes_plain, s->io, s->ssq_t, s->ssq_p, s->ssq_p1, s->ph};
+                  s->apart, s->acounters, s->err_flag, s->codes_plain, s->io, s->ssq_t, s->ssq_p, s->ssq_p1};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (s->st) cudaStreamDestroy(s->st);
@@ -907,7 +800,6 @@ static int session_create(Model* m, int maxB, int maxP, Session** out) {
   A(&s->ssq_t, (size_t)s->rows * kSsqLd);
   A(&s->ssq_p, (size_t)2 * maxB * kSsqLd);
   A(&s->ssq_p1, (size_t)maxB * kSsqLd);
-  A(&s->ph, (size_t)(2 + 2 * kPhaseMaxParts) * kPhaseMaxH);
   if (rc == QTTS_OK) {  // pages: slot b owns pages [b*pps, (b+1)*pps)
     std::vector<int> pt((size_t)maxB * s->pages_per_sess);
     for (size_t i = 0; i < pt.size(); ++i) pt[i] = (int)i;
@@ -958,9 +850,8 @@ static int build_frame_ops(Session& s, std::vector<Op>& ops, bool dumps) {
   RowPos rp;
   rp.pos_base = &s.slots[0].pos;
   rp.pos_stride = (int)(sizeof(SlotState) / sizeof(int));
-  StackOut so;
-  RC(add_talker(s, ops, s.x, H, B, rp, talker_nsplit(s, B), true, &so));
-  RC(add_codec_head(s, ops, s.x, H, B, s.logits, s.pin, 2L * H, 0, 1, &so));
+  RC(add_talker(s, ops, s.x, H, B, rp, talker_nsplit(s, B), true));
+  RC(add_codec_head(s, ops, s.x, H, B, s.logits, s.pin, 2L * H));
   ops.push_back([slots, B](cudaStream_t st) { return launch_frame_end(slots, B, st); });
   return QTTS_OK;
 }
@@ -1146,6 +1037,7 @@ static int generate_begin(Session& s, int n, const qtts_utterance* u, int F, uns
   Session::GraphKey key;
   key.B = n; key.F = F; key.max_trail = max_trail; key.forced = forced ? 1 : 0;
   key.dump_logits = dump_logits ? 1 : 0; key.dump_hidden = dump_hidden ? 1 : 0; key.epoch = s.buf_epoch;
+  key.wait_ns = s.wait_ns;
   if (s.graph_exec && s.graph_key == key) {
     s.generating = true;
     return QTTS_OK;
@@ -1320,9 +1212,8 @@ static int talker_step_call(Session& s, const float* emb, int position, float* o
   RowPos rp;
   rp.pos_const = position;
   rp.kv_const = s.kvlen0;
-  StackOut so;
-  RC(add_talker(s, ops, s.x, H, 1, rp, talker_nsplit(s, 1), false, &so));
-  RC(add_codec_head(s, ops, s.x, H, 1, s.logits, s.hid1, H, 0, 1, &so));
+  RC(add_talker(s, ops, s.x, H, 1, rp, talker_nsplit(s, 1), false));
+  RC(add_codec_head(s, ops, s.x, H, 1, s.logits, s.hid1, H));
   RC(run_ops(s, ops));
   CK(cudaMemcpyAsync(out, s.hid1, sizeof(float) * H, cudaMemcpyDeviceToHost, s.st));
   CK(cudaMemcpyAsync(out + H, s.logits, sizeof(float) * V, cudaMemcpyDeviceToHost, s.st));
@@ -1541,6 +1432,11 @@ int qtts_session_reset(qtts_session* h) {
   return QTTS_OK;
 }
 void* qtts_session_stream(qtts_session* h) { return h ? (void*)h->s->st : nullptr; }
+int qtts_session_set_wait_budget(qtts_session* h, uint64_t ns) {
+  if (!h || ns == 0) return fail(QTTS_ERR_BADARG, "null session or zero budget");
+  h->s->wait_ns = ns;
+  return QTTS_OK;
+}
 
 #define SESS(h)                                                      \
   if (!h) return fail(QTTS_ERR_BADARG, "null session");              \

@@ -77,9 +77,6 @@ struct Session {
   // per-256-column sums of squares of residual rows (talker, predictor
   // prefill rows, predictor decode rows), row stride kSsqLd
   float *ssq_t = nullptr, *ssq_p = nullptr, *ssq_p1 = nullptr;
-  // one-row layer phases: two residual rows, then the attention phases'
-  // and the MLP phases' partial rows ([kPhaseMaxParts][kPhaseMaxH] each)
-  float* ph = nullptr;
   size_t io_floats = 0;
   // generation
   int B = 0, max_frames = 0, max_trail = 0;
@@ -115,13 +112,18 @@ struct Session {
   struct GraphKey {
     int B = -1, F = -1, max_trail = -1, forced = 0, dump_logits = 0, dump_hidden = 0;
     unsigned long epoch = 0;
+    unsigned long long wait_ns = 0;
     bool operator==(const GraphKey& o) const {
       return B == o.B && F == o.F && max_trail == o.max_trail && forced == o.forced &&
-             dump_logits == o.dump_logits && dump_hidden == o.dump_hidden && epoch == o.epoch;
+             dump_logits == o.dump_logits && dump_hidden == o.dump_hidden && epoch == o.epoch &&
+             wait_ns == o.wait_ns;
     }
   };
   GraphKey graph_key;
   int graph_captures = 0;  // frame graphs captured by this session (cache misses)
+  // budget of the one-row GEMV's split-K cluster wait (tests of the timeout
+  // path set it short); part of the frame graph's key
+  unsigned long long wait_ns = 1000000000ull;
 };
 
 }  // namespace qtts

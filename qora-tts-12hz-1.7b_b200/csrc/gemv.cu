@@ -64,25 +64,40 @@ __device__ __forceinline__ void st_async_f32(uint32_t raddr, float v, uint32_t r
                : "memory");
 }
 // Phase-0 wait with cluster-scope acquire (the peers' st.async data), bounded
-// by one second of %globaltimer; false when it ran out.
-__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar) {
+// by limit_ns of %globaltimer (1 s unless the launch's budget is shorter);
+// false when it ran out.  A budget below 1 s polls with the non-blocking
+// test_wait and reads the clock on every try (try_wait may suspend the
+// thread until the data arrives, which a short budget would never see).
+constexpr unsigned long long kWaitNs = 1000000000ull;
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, unsigned long long limit_ns) {
   const uint32_t a = smem_addr(bar);
+  const bool short_budget = limit_ns < kWaitNs;
   unsigned long long t0 = 0;
   for (unsigned it = 0;; ++it) {
     uint32_t done;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], 0;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done)
-        : "r"(a)
-        : "memory");
+    if (short_budget) {
+      asm volatile(
+          "{\n\t.reg .pred p;\n\t"
+          "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], 0;\n\t"
+          "selp.u32 %0, 1, 0, p;\n\t}"
+          : "=r"(done)
+          : "r"(a)
+          : "memory");
+    } else {
+      asm volatile(
+          "{\n\t.reg .pred p;\n\t"
+          "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], 0;\n\t"
+          "selp.u32 %0, 1, 0, p;\n\t}"
+          : "=r"(done)
+          : "r"(a)
+          : "memory");
+    }
     if (done) return true;
-    if ((it & 255u) == 0) {
+    if ((it & 255u) == 0 || short_budget) {
       unsigned long long t;
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
       if (it == 0) t0 = t;
-      else if (t - t0 > 1000000000ull) return false;
+      else if (t - t0 > limit_ns) return false;
     }
   }
 }
@@ -290,16 +305,6 @@ __global__ void __launch_bounds__(kGemvThreads) q4mv_dec_kernel(const GemvDesc d
       xv[i] = rb < R ? xr[r0 + rb] : 0.0f;
       xg[i] = (kGlu && d.x_glu && rb < R) ? xr[d.x_glu + r0 + rb] : 0.0f;
     }
-    if (kNorm && d.nparts) {  // residual partials of the layer phases, added in order
-      for (int p = 0; p < d.nparts; ++p) {
-        const float* pr = d.parts + (size_t)p * d.parts_ld;
-#pragma unroll
-        for (int i = 0; i < NR; ++i) {
-          const int rb = rb0 + 32 * i;
-          if (rb < R) xv[i] += pr[r0 + rb];
-        }
-      }
-    }
     // the producer's per-tile sums of squares (at most 16 tiles here)
     const bool ssq16 = kNorm && d.gamma && d.ssq_in && d.ssq_n <= 16;
     float sv[16];
@@ -318,11 +323,7 @@ __global__ void __launch_bounds__(kGemvThreads) q4mv_dec_kernel(const GemvDesc d
         inv = inv_rms_from_ssq(d, m);
       } else {
         float ss = 0.0f;
-        for (int i = tid; i < d.k; i += kGemvThreads) {
-          float v = xr[i];
-          for (int p = 0; p < d.nparts; ++p) v += d.parts[(size_t)p * d.parts_ld + i];
-          ss += v * v;
-        }
+        for (int i = tid; i < d.k; i += kGemvThreads) ss += xr[i] * xr[i];
         ss = block_sum_256(ss, sbuf);
         inv = 1.0f / sqrtf(ss / (float)d.k + 1e-6f);
       }
@@ -392,9 +393,12 @@ __global__ void __launch_bounds__(kGemvThreads) q4mv_dec_kernel(const GemvDesc d
       return;
     }
     if (tid == 0) mbar_expect_arrive(mbar, (uint32_t)((d.S - 1) * NM * kTileN * sizeof(float)));
-    if (!mbar_wait_cluster(mbar)) {  // a peer never delivered: flag it, write nothing
+    // Within the launch's budget; past it the error is recorded and the
+    // wait goes on (bounded by 1 s), so that no peer's push is still in
+    // flight into this CTA when it moves on.
+    if (!mbar_wait_cluster(mbar, d.wait_ns)) {
       if (tid == 0 && d.err_flag) atomicOr(d.err_flag, kErrWaitExpired);
-      return;
+      if (!mbar_wait_cluster(mbar, kWaitNs)) return;  // a peer never delivered: write nothing
     }
 #pragma unroll
     for (int a = 0; a < NM; ++a) {
@@ -764,8 +768,6 @@ cudaError_t launch_gemv(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st
   if (!d.tc && use_dec(d) &&
       ((d.emb_idx && d.epi_kind != EPI_STORE) || (d.gamma && d.epi_kind == EPI_RESID)))
     return cudaErrorInvalidValue;  // prologue forms the decode kernel compiles per epilogue
-  if (d.nparts && (d.tc || !use_dec(d) || !d.gamma || d.ssq_in || d.emb_idx || d.attn_in || d.x_glu))
-    return cudaErrorInvalidValue;  // residual partials: the decode kernel's full-row RMSNorm prologue only
   if (d.tc) return launch_tc(d, fc, st);
   if (d.ntiles <= 0 || d.S <= 0 || d.M <= 0 || d.rows_per_split <= 0) return cudaErrorInvalidValue;
   if (d.cluster && d.S > kMaxClusterSplits) return cudaErrorInvalidValue;

@@ -156,14 +156,12 @@ struct GemvDesc {
   const uint8_t* pf_ptr[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
   uint32_t pf_bytes[6] = {0, 0, 0, 0, 0, 0};
   int* err_flag = nullptr;      // bit 4: a bounded wait expired; bit 8: input outside the fp16 range
+  // budget of the decode kernel's split-K wait (the root's wait for its
+  // cluster peers' partials), 1 s unless a test of the timeout path sets it
+  unsigned long long wait_ns = 1000000000ull;
   // GLU input (decode kernel only): x[r] = X[r] * X[x_glu + r], the SwiGLU
   // product of a row holding silu(gate) in [0, x_glu) and up in [x_glu, 2 x_glu)
   int x_glu = 0;
-  // residual partials (decode kernel, RMSNorm prologue): the input row is
-  // X + sum_p parts[p] (p in order), the sum of squares taken over that sum
-  const float* parts = nullptr;  // [nparts][parts_ld]
-  int nparts = 0;
-  long parts_ld = 0;
   EpiDesc epi;
 };
 // err_flag bits shared by the kernels (the session's flag word)
@@ -219,8 +217,7 @@ inline thread_local int g_occ_clusters = 0;
 // algorithmic work of a projection launch (useful FLOPs 2*M*k*n, Q4 weight
 // bytes k*n*0.5625): lets the profiling entry point sort a frame's launches
 // by family without launching them.
-enum KernelFamily : int { FAM_OTHER = 0, FAM_Q4MV_DEC = 1, FAM_Q4MV_ROWS = 2, FAM_TC_PROJ = 3, FAM_ATTN = 4,
-                          FAM_PHASE = 5 };
+enum KernelFamily : int { FAM_OTHER = 0, FAM_Q4MV_DEC = 1, FAM_Q4MV_ROWS = 2, FAM_TC_PROJ = 3, FAM_ATTN = 4 };
 inline thread_local int g_occ_family = FAM_OTHER;
 inline thread_local double g_occ_flops = 0.0, g_occ_wbytes = 0.0;
 int occupancy_clusters(const void* func, const cudaLaunchConfig_t& cfg);
@@ -281,64 +278,6 @@ cudaError_t tc_expand(const Q4Mat& w, uint8_t* out, cudaStream_t st);
 void tc_init_attributes();
 
 
-
-// ---- one-row decode layer as two cluster-local phases (phase.cu) ----------
-// A layer (talker.rs:279-349, code_predictor.rs:448-502) runs as phase A
-// (attention block) and phase B (MLP block).  Neither materialises the
-// residual row: each phase reads r = base + sum_p parts[p] (in order p =
-// 0, 1, ...), writes r for the next phase (CTA 0) and leaves its own
-// output as partial rows that the next phase adds on read.
-constexpr int kPhaseThreads = 256;
-constexpr int kPhaseMaxParts = 16;
-constexpr int kPhaseMaxH = 2048;
-struct PhaseResid {
-  const float* base = nullptr;   // [H]
-  const float* parts = nullptr;  // [nparts][H]
-  int nparts = 0;
-  float* out = nullptr;          // r, written by the first CTA (optional)
-};
-// Phase A: a cluster of C CTAs per KV head j.  Rank r multiplies rows
-// [r H/C, (r+1) H/C) of q (the 2 query heads of j), k and v; the cluster
-// sums the slices over distributed shared memory; every CTA applies QK-norm
-// and RoPE; rank 0 appends k, v to the cache; the ranks split the positions
-// of the attention and combine them; rank r then multiplies the 256
-// attention outputs by columns [r H/C, (r+1) H/C) of o's rows [256 j, 256 j
-// + 256): parts_out[j] is KV head j's share of the o projection.
-struct AttnPhaseDesc {
-  int H = 0, kvh = 0, C = 16;
-  PhaseResid in;
-  const __half* gamma = nullptr;  // input RMSNorm
-  Q4Mat q, k, v, o;
-  const __half *q_norm = nullptr, *k_norm = nullptr;
-  const float *rope_cos = nullptr, *rope_sin = nullptr;
-  int rope_rows = 0, rope_skip_oob = 0;
-  KvDesc kv;
-  RowPos rp;
-  float* parts_out = nullptr;  // [kvh][H]
-  int* err_flag = nullptr;
-  const uint8_t* pf_ptr[8] = {};  // next phase's weights, pulled into L2
-  uint32_t pf_bytes[8] = {};
-};
-// Phase B: CTA u owns 32 U columns of the intermediate dim: gate and up
-// over all H rows, silu(gate) * up, then those 32 U rows of down over all H
-// columns; the C CTAs of a cluster sum their partial rows over distributed
-// shared memory: parts_out[cluster] is the cluster's share of down.
-struct MlpPhaseDesc {
-  int H = 0, I = 0, U = 1, C = 16;
-  PhaseResid in;
-  const __half* gamma = nullptr;  // post-attention RMSNorm
-  Q4Mat gate, up, down;
-  float* parts_out = nullptr;  // [I / (32 U) / C][H]
-  const uint8_t* pf_ptr[8] = {};
-  uint32_t pf_bytes[8] = {};
-};
-bool attn_phase_supported(int H, int heads, int kvh, int* C);
-bool mlp_phase_supported(int H, int I, int* U, int* C);
-size_t attn_phase_smem(const AttnPhaseDesc& d);
-size_t mlp_phase_smem(const MlpPhaseDesc& d);
-cudaError_t launch_attn_phase(const AttnPhaseDesc& d, cudaStream_t st);
-cudaError_t launch_mlp_phase(const MlpPhaseDesc& d, cudaStream_t st);
-void phase_init_attributes();
 
 struct AttnDesc {
   const float* q = nullptr;  // row m: heads*128

@@ -81,6 +81,7 @@ def _load():
         "qtts_session_free": (C.c_int, [P]),
         "qtts_session_reset": (C.c_int, [P]),
         "qtts_session_stream": (P, [P]),
+        "qtts_session_set_wait_budget": (C.c_int, [P, C.c_uint64]),
         "qtts_embed_text": (C.c_int, [P, C.c_uint32, fp]),
         "qtts_embed_codec": (C.c_int, [P, C.c_uint32, fp]),
         "qtts_prefill": (C.c_int, [P, fp, C.c_int, fp, fp]),
@@ -196,6 +197,11 @@ class Session:
 
     def reset(self):
         _check(lib.qtts_session_reset(self.h))
+
+    def set_wait_budget(self, ns: int):
+        """Bound (ns) on the first device wait of each exchange in the one-row
+        layer launches (qtts.h qtts_session_set_wait_budget)."""
+        _check(lib.qtts_session_set_wait_budget(self.h, int(ns)))
 
     def close(self):
         if getattr(self, "h", None):

@@ -393,3 +393,25 @@ def test_1p7b_config4_64_utterances_teacher_forced(qtts, gpu_1p7b):
         gi = {k: (g[k][i] if np.ndim(g[k]) > 0 else g[k]) for k in g}
         ties += _check_forced(codes[i], gi, lg[i], max_ties=1)
     print("near-ties tolerated:", ties)
+
+
+def test_wait_budget_timeout_reported_then_fresh_session_works(qtts, gpu_tiny):
+    # A 1 ns budget makes the one-row GEMV's split-K cluster wait run out:
+    # the root CTA records it, keeps waiting (bounded) for its peers'
+    # partials, and returns; qtts_generate reports QTTS_ERR_TIMEOUT.  No GPU
+    # wait is left hanging: a fresh session on the same model then generates
+    # the golden codes.
+    H = gpu_tiny.dims.t_hidden
+    g = golden("tiny_greedy")
+    u = tiny_case("tiny_greedy", H)
+    F = 4
+    s = qtts.Session(gpu_tiny, 1, 10 + F + 1)
+    s.set_wait_budget(1)
+    with pytest.raises(qtts.QttsError) as ex:
+        qtts.generate(s, [u], F)
+    assert ex.value.code == qtts.ERR_TIMEOUT
+    s.close()
+    s2 = qtts.Session(gpu_tiny, 1, 10 + F + 1)
+    codes, frames, _, _ = qtts.generate(s2, [u], F)
+    assert np.array_equal(codes[0], g["codes"][:F])
+    s2.close()
