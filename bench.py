@@ -323,7 +323,7 @@ def time_quantize(Q, torch, k, n, copies=4, reps=40):
 def run_config2(args, Q, torch, peak, peak_kind):
     """Isolated Q4 GEMV / GEMM microbench: device time per launch over
     rotating weight copies larger than L2; m >= 16 runs on the tcgen05
-    kernel, smaller m on the CUDA-core kernels."""
+    kernel, m <= 2 on the one-row decode kernel, 3..15 on the batch kernel."""
     rows = []
     for name, k, n in CONFIG2_SHAPES:
         for m in CONFIG2_BATCHES:
@@ -334,7 +334,7 @@ def run_config2(args, Q, torch, peak, peak_kind):
             rows.append({"shape": name, "k": k, "n": n, "m": m, "us_per_launch": dt * 1e6,
                          "gbs": alg / dt / 1e9, "useful_tflops": 2.0 * m * k * n / dt / 1e12,
                          "kernel": "tc_proj_kernel" if m >= 16 else ("q4mv_dec_kernel" if m <= 2 else
-                                                                     "q4mv_rows_kernel")})
+                                                                     "q4mv_batch_kernel")})
     if not args.only or args.only == "quantize":
         k, n = 2048, 6144  # quantize_f32_to_q4 on the GPU: reads 4 B, writes 0.5625 B per value
         dt = time_quantize(Q, torch, k, n)

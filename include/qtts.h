@@ -159,9 +159,10 @@ QTTS_API int qtts_frame_graph_captures(qtts_session* s);
 /* ---- profiling (no counterpart in the reference) -------------------------- */
 /* Kernel families of the frame plan. */
 #define QTTS_FAMILY_Q4MV_DEC 1  /* q4mv_dec_kernel: one-row CUDA-core Q4 GEMV */
-#define QTTS_FAMILY_Q4MV_ROWS 2 /* q4mv_rows_kernel: 2-15-row CUDA-core Q4 GEMV */
+#define QTTS_FAMILY_Q4MV_ROWS 2 /* q4mv_rows_kernel: multi-row CUDA-core Q4 GEMV (shapes the others do not take) */
 #define QTTS_FAMILY_TC_PROJ 3   /* tc_proj_kernel: tcgen05 Q4 projection */
 #define QTTS_FAMILY_ATTN 4      /* attn_kernel: GQA over the paged cache */
+#define QTTS_FAMILY_Q4MV_BATCH 5 /* q4mv_batch_kernel: 3-15-row CUDA-core Q4 GEMV */
 /* Device time of one frame's launches of one family, captured without the
  * frame's other launches (same order, parameters and dependent-launch links)
  * and replayed `reps` times between CUDA events on the session stream.  Needs

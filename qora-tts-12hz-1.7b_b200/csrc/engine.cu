@@ -336,6 +336,31 @@ static void fit_split_to_wave(GemvDesc& g) {
   }
 }
 
+// Batches of 3..15 rows (q4mv_batch_kernel): 8 input rows per CTA (4 for a
+// gate/up pair), K slices of whole 8-row steps of at most kBatchMaxRpsNM1/NM2 rows,
+// the slices of a tile in one cluster.  Starting from about two CTAs per SM,
+// the largest split whose clusters all fit in one wave.
+static void batch_plan(int sm_count, GemvDesc& g) {
+  if (g.tc || g.M <= kDecMaxM || g.M >= kTcMinRows || g.attn_in || g.x_glu) return;
+  GemvDesc t = g;
+  t.batch = 1;
+  t.cluster = 1;
+  t.mb = g.paired ? kBatchRowsNM2 : kBatchRowsNM1;
+  const long units = (long)t.ntiles * ceil_div(t.M, t.mb);
+  int S0 = (int)std::lround(2.0 * sm_count / (double)units);
+  S0 = std::max(1, std::min(S0, kMaxClusterSplits));
+  for (int S = S0; S >= 1; --S) {
+    t.rows_per_split = ceil_div(ceil_div(g.k, S), 8) * 8;
+    if (t.rows_per_split > (g.paired ? kBatchMaxRpsNM2 : kBatchMaxRpsNM1)) return;  // a smaller split only grows it
+    t.S = ceil_div(g.k, t.rows_per_split);
+    if (t.S > S) continue;
+    if (S == 1 || gemv_wave_clusters(t) >= units) {
+      g = t;
+      return;
+    }
+  }
+}
+
 // Split-K choice: about two CTAs per SM, slices of whole 32-row blocks, at
 // most 2048 rows per slice (shared-memory bound of the input slice).
 void choose_split(int sm_count, GemvDesc& g) {
@@ -391,6 +416,7 @@ static int plan_gemv(Session& s, GemvDesc& g) {
   g.pdl = 1;
   fit_split_to_wave(g);
   try_global_split(s, g);
+  batch_plan(s.m->sm_count, g);
   g.err_flag = s.err_flag;
   g.wait_ns = s.wait_ns;
   if (g.M >= kTcMinRows) {
@@ -1336,7 +1362,13 @@ static int gemv_dev(const uint8_t* packed, const uint16_t* scales, int k, int n,
   gemv_init_attributes();
   tc_init_attributes();
   fit_split_to_wave(g);
-  if (!g.tc && g.S > 1 && scratch_bytes < kCounterBytes + sizeof(float) * (size_t)g.S * m * n)
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    sms = 148;
+  cudaGetLastError();
+  batch_plan(sms, g);
+  // partial sums go through the scratch only for a K split reduced in global memory
+  if (!g.tc && !g.cluster && g.S > 1 && scratch_bytes < kCounterBytes + sizeof(float) * (size_t)g.S * m * n)
     return fail(QTTS_ERR_BADARG, "scratch smaller than qtts_q4_gemv_scratch_bytes()");
   const cudaError_t e = launch_gemv(g, FrameCodes{}, st);
   if (e != cudaSuccess) return fail(QTTS_ERR_CUDA, cudaGetErrorString(e));

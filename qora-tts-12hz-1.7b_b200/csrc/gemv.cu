@@ -648,6 +648,296 @@ __global__ void __launch_bounds__(kGemvThreads) q4mv_rows_kernel(const GemvDesc 
   gemv_epilogue<MB, NM, EPI>(d, fc, v, mat, tile, tcol, m0, mcnt, zb, sbuf, ybuf);
 }
 
+// ===========================================================================
+// Batch kernel: 3..15 input rows (small decode batches), MB per CTA.
+//
+// The CTA's weight slice (RPS rows x 256 columns of each matrix) and its
+// group scales are staged in shared memory before the dependency wait, so
+// the whole slice is in flight at once.  Thread (warp w, lane l) owns the 8
+// columns of weight word l (group l / 4) and the slice rows w, w + 8, ...:
+// each word is dequantised once and applied to all MB input rows.  The 8
+// warps' partials are reduced through shared memory; row mm of the tile then
+// belongs to cluster rank mm % S, which receives the other ranks' partials
+// of that row by st.async, adds them in split order (deterministic) and runs
+// the epilogue for it.
+__host__ __device__ inline size_t batch_main_bytes(int NM, int MB, int rps) {
+  const size_t front = (size_t)rps * (NM * (128 + 16) + MB * 8);  // words, scales, (x, x) pairs
+  const size_t red = (size_t)8 * NM * MB * kTileN * sizeof(float);  // warp partials (reuse the front)
+  return front > red ? front : red;
+}
+__host__ __device__ inline size_t batch_recv_bytes(int NM, int MB, int S) {
+  return (size_t)S * ((MB + S - 1) / S) * NM * kTileN * sizeof(float);
+}
+
+namespace {
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+}  // namespace
+
+template <int MB, int NM, int EPI>
+#ifndef QTTS_BATCH_MINB
+#define QTTS_BATCH_MINB 1
+#endif
+__global__ void __launch_bounds__(kGemvThreads, QTTS_BATCH_MINB) q4mv_batch_kernel(const GemvDesc d, const FrameCodes fc) {
+  extern __shared__ __align__(16) unsigned char smb[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tile = blockIdx.x, split = blockIdx.y, zb = blockIdx.z;
+  const int S = d.S, RPS = d.rows_per_split;
+  const bool clustered = S > 1;  // the S slices of a tile form one cluster
+  const int RO = (MB + S - 1) / S;  // rows of the tile a rank may own
+  uint32_t* wsm = reinterpret_cast<uint32_t*>(smb);                                    // [NM][RPS][32]
+  unsigned short* ssm = reinterpret_cast<unsigned short*>(smb + (size_t)NM * RPS * 128);  // [NM][RPS][8]
+  float2* xsm = reinterpret_cast<float2*>(smb + (size_t)NM * RPS * 144);                // [RPS][MB]
+  float* red = reinterpret_cast<float*>(smb);                                          // [8][NM][MB][256]
+  float* recv = reinterpret_cast<float*>(smb + batch_main_bytes(NM, MB, RPS));          // [S][RO][NM][256]
+  float* sbuf = recv + (size_t)S * RO * NM * kTileN;                                   // 64 floats
+  float* ybuf = sbuf + 64;                                                             // [256]
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(ybuf + kTileN);                         // this rank's rows landed
+  const int m0 = zb * MB, mcnt = min(MB, d.M - m0);
+  const int nown = split < mcnt ? (mcnt - split + S - 1) / S : 0;  // rows split, split + S, ...
+  if (clustered) {
+    if (tid == 0) mbar_init_cluster(mbar);
+    cluster_arrive_relaxed();  // the wait below precedes any DSMEM store
+  }
+  prefetch_next_weights(d);
+
+  int mat = 0;
+  if (NM == 1) {
+    while (mat + 1 < d.nmat && tile >= d.tile0[mat + 1]) ++mat;
+  }
+  const int tcol = (NM == 2 ? tile : tile - d.tile0[mat]) * kTileN;
+  const int n = d.mat[mat].n;
+  const int r0 = split * RPS;
+  const int R = max(0, min(d.k, r0 + RPS) - r0);
+  const size_t rowbytes = (size_t)n / 2;
+  const int ngr = n / 32;
+
+  // Weight slice -> shared memory by cp.async, zero-filled past the slice or
+  // the matrix (weights are never written by an earlier kernel: issued before
+  // the dependency wait, they land while the prologue runs)
+#pragma unroll
+  for (int a = 0; a < NM; ++a) {
+    const Q4Mat& Mt = d.mat[NM == 2 ? a : mat];
+    for (int e = tid; e < RPS * 8; e += kGemvThreads) {
+      const int r = e >> 3, c = e & 7;
+      const bool ok = r < R && tcol + 32 * c < n;
+      const uint8_t* src = ok ? Mt.packed + (size_t)(r0 + r) * rowbytes + tcol / 2 + 16 * c : Mt.packed;
+      cp_async16(smem_addr(wsm + ((size_t)a * RPS * 8 + e) * 4), src, ok ? 16u : 0u);
+    }
+  }
+  // group scales: 16 bytes (8 groups) per slice row by cp.async when the
+  // scale rows are 16-byte aligned (n a multiple of 256), else plain loads
+  const bool sc16 = (n & 255) == 0;
+#pragma unroll
+  for (int a = 0; a < NM; ++a) {
+    const unsigned short* sc = reinterpret_cast<const unsigned short*>(d.mat[NM == 2 ? a : mat].scales);
+    if (sc16 && (reinterpret_cast<uintptr_t>(sc) & 15) == 0) {
+      for (int r = tid; r < RPS; r += kGemvThreads) {
+        const bool ok = r < R;
+        cp_async16(smem_addr(ssm + ((size_t)a * RPS + r) * 8), ok ? sc + (size_t)(r0 + r) * ngr + tcol / 32 : sc,
+                   ok ? 16u : 0u);
+      }
+    } else {
+      for (int e0 = tid; e0 < RPS * 8; e0 += 8 * kGemvThreads) {
+        unsigned short t[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int e = e0 + u * kGemvThreads, r = e >> 3, gg = e & 7;
+          t[u] = (r < R && tcol + 32 * gg < n) ? __ldg(sc + (size_t)(r0 + r) * ngr + tcol / 32 + gg)
+                                              : (unsigned short)0;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (e0 + u * kGemvThreads < RPS * 8) ssm[(size_t)a * RPS * 8 + e0 + u * kGemvThreads] = t[u];
+      }
+    }
+  }
+  cp_async_commit();
+  pdl_wait();
+
+  // ---- prologue: rows [m0, m0 + mcnt) x K slice [r0, r0 + R) -> (x, x)
+  // pairs; thread i takes slice row i of every input row, all loads first
+  float inv[MB];
+#pragma unroll
+  for (int mm = 0; mm < MB; ++mm) inv[mm] = 1.0f;
+  if (!d.emb_idx && d.gamma) {  // RMSNorm scale of each row
+    if (d.ssq_in) {
+#pragma unroll
+      for (int mm = 0; mm < MB; ++mm)
+        if (mm < mcnt) inv[mm] = inv_rms_from_ssq(d, m0 + mm);
+    } else {
+      for (int mm = 0; mm < mcnt; ++mm) {  // uniform: every thread takes part in the row sum
+        const float* xr = d.X + (size_t)(m0 + mm) * d.ldx;
+        float ss = 0.0f;
+        for (int i = tid; i < d.k; i += kGemvThreads) ss += xr[i] * xr[i];
+        ss = block_sum_256(ss, sbuf);
+        const float t = 1.0f / sqrtf(ss / (float)d.k + 1e-6f);
+#pragma unroll
+        for (int q = 0; q < MB; ++q)
+          if (q == mm) inv[q] = t;
+      }
+    }
+  }
+  for (int i = tid; i < RPS; i += kGemvThreads) {
+    float x[MB];
+    const bool in = i < R;
+    if (d.emb_idx) {
+#pragma unroll
+      for (int mm = 0; mm < MB; ++mm) {
+        x[mm] = 0.0f;
+        if (in && mm < mcnt) {
+          const uint32_t row = d.emb_idx[(size_t)(m0 + mm) * d.emb_idx_stride];
+          x[mm] = q4_value(d.emb.packed + (size_t)row * (d.emb.n / 2), d.emb.scales + (size_t)row * (d.emb.n / 32),
+                           r0 + i);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int mm = 0; mm < MB; ++mm) x[mm] = (in && mm < mcnt) ? d.X[(size_t)(m0 + mm) * d.ldx + r0 + i] : 0.0f;
+      if (d.gamma) {
+        const float gm = in ? h2f(d.gamma[r0 + i]) : 0.0f;
+#pragma unroll
+        for (int mm = 0; mm < MB; ++mm) {
+          x[mm] = x[mm] * inv[mm] * gm;  // gemv.rs:414
+          if (d.xnorm_out && tile == 0 && in && mm < mcnt) d.xnorm_out[(size_t)(m0 + mm) * d.ld_xnorm + r0 + i] = x[mm];
+        }
+      }
+    }
+    float4* xd = reinterpret_cast<float4*>(xsm + (size_t)i * MB);
+#pragma unroll
+    for (int q = 0; q < MB / 2; ++q) xd[q] = make_float4(x[2 * q], x[2 * q], x[2 * q + 1], x[2 * q + 1]);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+
+  // ---- main loop: one staged row per step, 8 columns x MB rows per thread
+  float2 acc[NM][MB][4];
+#pragma unroll
+  for (int a = 0; a < NM; ++a)
+#pragma unroll
+    for (int b = 0; b < MB; ++b)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[a][b][j] = make_float2(0.0f, 0.0f);
+  const int g = lane >> 2;
+  const int nsteps = (R + 7) >> 3;  // rows past the slice in the last step are zero
+#pragma unroll 4
+  for (int i = 0; i < nsteps; ++i) {
+    const int r = warp + 8 * i;
+    float2 xx[MB];
+    const float4* xp = reinterpret_cast<const float4*>(xsm + (size_t)r * MB);
+#pragma unroll
+    for (int q = 0; q < MB / 2; ++q) {
+      const float4 t = xp[q];
+      xx[2 * q] = make_float2(t.x, t.y);
+      xx[2 * q + 1] = make_float2(t.z, t.w);
+    }
+#pragma unroll
+    for (int a = 0; a < NM; ++a) {
+      const uint32_t w = wsm[((size_t)a * RPS + r) * 32 + lane];
+      const float s = u16_h2f(ssm[((size_t)a * RPS + r) * 8 + g]);
+      // Weight values s * (q - 8), exact in f32 (an f16 scale times a 4-bit
+      // integer): nibble j of byte b is column 2b + j (low nibble first,
+      // gemv.rs:124); 0x43000000 | q << 16 is the float 128 + q, and one
+      // fused multiply-add (128 + q) * s - 136 * s, its product exact and
+      // 136 * s exact, rounds nothing.
+      const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+      const float2 ss = make_float2(s, s), cc = make_float2(-136.0f * s, -136.0f * s);
+      float2 wv[4];
+#pragma unroll
+      for (int b = 0; b < 4; ++b)
+        wv[b] = __ffma2_rn(make_float2(__uint_as_float(__byte_perm(lo, 0x43000000u, 0x7054u | (b << 8))),
+                                       __uint_as_float(__byte_perm(hi, 0x43000000u, 0x7054u | (b << 8)))),
+                           ss, cc);
+#pragma unroll
+      for (int mm = 0; mm < MB; ++mm)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) acc[a][mm][b] = __ffma2_rn(wv[b], xx[mm], acc[a][mm][b]);
+    }
+  }
+
+  // Release the next kernel only now (as the decode kernel does).
+  pdl_launch_dependents();
+  // ---- CTA reduction over the 8 warps.  Lane l's 8 columns are two 16-byte
+  // chunks, stored in swapped order when bit 2 of l is set, so that the 8
+  // lanes of a store phase hit 8 different bank groups.
+  __syncthreads();  // every warp is done with the staged slice (red reuses it)
+  {
+    const int sw = (lane >> 2) & 1;
+#pragma unroll
+    for (int a = 0; a < NM; ++a)
+#pragma unroll
+      for (int mm = 0; mm < MB; ++mm) {
+        float4* dst = reinterpret_cast<float4*>(red + ((size_t)(warp * NM + a) * MB + mm) * kTileN + 8 * lane);
+        dst[sw] = make_float4(acc[a][mm][0].x, acc[a][mm][0].y, acc[a][mm][1].x, acc[a][mm][1].y);
+        dst[sw ^ 1] = make_float4(acc[a][mm][2].x, acc[a][mm][2].y, acc[a][mm][3].x, acc[a][mm][3].y);
+      }
+  }
+  __syncthreads();
+  const int pc = tid ^ (((tid >> 5) & 1) << 2);  // physical index of column tid
+  float v[NM][MB];
+#pragma unroll
+  for (int a = 0; a < NM; ++a)
+#pragma unroll
+    for (int mm = 0; mm < MB; ++mm) {
+      float pv[8];
+#pragma unroll
+      for (int w8 = 0; w8 < 8; ++w8) pv[w8] = red[((size_t)(w8 * NM + a) * MB + mm) * kTileN + pc];
+      float t = 0.0f;
+#pragma unroll
+      for (int w8 = 0; w8 < 8; ++w8) t += pv[w8];  // warp order
+      v[a][mm] = t;
+    }
+
+  // ---- split-K: row mm's partial goes to rank mm % S (slot [split][mm / S])
+  if (clustered) cluster_wait();  // every rank's mbarrier is initialised, its CTA running
+  {
+    int o = 0, ro = 0;  // rank and slot of row mm (mm % S, mm / S)
+#pragma unroll
+    for (int mm = 0; mm < MB; ++mm) {
+      if (mm < mcnt) {
+#pragma unroll
+        for (int a = 0; a < NM; ++a) {
+          const int idx = ((split * RO + ro) * NM + a) * kTileN + tid;
+          if (o == split) {
+            recv[idx] = v[a][mm];  // read back below by this same thread
+          } else {
+            st_async_f32(dsmem_map(smem_addr(recv + idx), (uint32_t)o), v[a][mm],
+                         dsmem_map(smem_addr(mbar), (uint32_t)o));
+          }
+        }
+      }
+      if (++o == S) {
+        o = 0;
+        ++ro;
+      }
+    }
+  }
+  if (nown == 0) return;
+  if (clustered) {
+    if (tid == 0) mbar_expect_arrive(mbar, (uint32_t)((S - 1) * nown * NM * kTileN * sizeof(float)));
+    // within the launch's budget; past it the error is recorded and the wait
+    // goes on (bounded by 1 s) so that no peer's push is still in flight
+    if (!mbar_wait_cluster(mbar, d.wait_ns)) {
+      if (tid == 0 && d.err_flag) atomicOr(d.err_flag, kErrWaitExpired);
+      if (!mbar_wait_cluster(mbar, kWaitNs)) return;  // a peer never delivered: write nothing
+    }
+  }
+  for (int ro = 0; ro < nown; ++ro) {
+    const int m = m0 + split + ro * S;
+    float v1[NM][1];
+#pragma unroll
+    for (int a = 0; a < NM; ++a) {
+      float t = 0.0f;
+      for (int sp = 0; sp < S; ++sp) t += recv[((sp * RO + ro) * NM + a) * kTileN + tid];  // split order
+      v1[a][0] = t;
+    }
+    gemv_epilogue<1, NM, EPI>(d, fc, v1, mat, tile, tcol, m, 1, m, sbuf, ybuf);
+  }
+}
+
 // ---------------------------------------------------------------------------
 static bool use_dec(const GemvDesc& d) {
   const int nrmax = d.paired ? kDecRowsNM2 : kDecRowsNM1;
@@ -655,8 +945,18 @@ static bool use_dec(const GemvDesc& d) {
          d.rows_per_split <= 32 * nrmax;
 }
 
+static bool use_batch(const GemvDesc& d) {
+  return d.batch && (d.paired ? d.mb == kBatchRowsNM2 : (d.mb == kBatchRowsNM1 || d.mb == kBatchRowsNM1 / 2)) &&
+         d.S >= 1 && d.S <= kMaxClusterSplits &&
+         d.rows_per_split % 8 == 0 && d.rows_per_split <= (d.paired ? kBatchMaxRpsNM2 : kBatchMaxRpsNM1) && (long)d.S * d.rows_per_split >= d.k &&
+         (d.S == 1 || d.cluster);
+}
+
 size_t gemv_smem_bytes(const GemvDesc& d) {
   const int NM = d.paired ? 2 : 1;
+  if (d.batch)
+    return batch_main_bytes(NM, d.mb, d.rows_per_split) + batch_recv_bytes(NM, d.mb, d.S) +
+           sizeof(float) * (64 + kTileN) + 16;
   if (use_dec(d))
     return sizeof(float) * ((size_t)dec_front_floats(NM) +
                             (size_t)kMaxClusterSplits * NM * kTileN + 64 + kTileN + 4);
@@ -674,6 +974,13 @@ template <int MB, int NM, int EPI>
 static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
   const dim3 grid(d.ntiles, d.S, (d.M + MB - 1) / MB);
   return launch_k(q4mv_rows_kernel<MB, NM, EPI>, grid, dim3(kGemvThreads), gemv_smem_bytes(d), st, opts(d), d, fc);
+}
+
+template <int MB, int NM, int EPI>
+static cudaError_t launch_b(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
+  const dim3 grid(d.ntiles, d.S, (d.M + MB - 1) / MB);
+  return launch_k(q4mv_batch_kernel<MB, NM, EPI>, grid, dim3(kGemvThreads), gemv_smem_bytes(d), st, opts(d), d,
+                  fc);
 }
 
 template <int NM, int EPI, int NR>
@@ -708,6 +1015,11 @@ static void set_attr_dec() {
   cudaFuncSetAttribute(q4mv_dec_kernel<NM, EPI, NR>, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
   cudaFuncSetAttribute(q4mv_dec_kernel<NM, EPI, NR>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
 }
+template <int MB, int NM, int EPI>
+static void set_attr_b() {
+  cudaFuncSetAttribute(q4mv_batch_kernel<MB, NM, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+  cudaFuncSetAttribute(q4mv_batch_kernel<MB, NM, EPI>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+}
 template <int EPI>
 static void set_attr_dec_nm1() {
   set_attr_dec<1, EPI, 4>(); set_attr_dec<1, EPI, 8>(); set_attr_dec<1, EPI, kDecRowsNM1>();
@@ -727,12 +1039,25 @@ void gemv_init_attributes() {
   set_attr_dec_nm1<EPI_STORE>(); set_attr_dec_nm1<EPI_RESID>(); set_attr_dec_nm1<EPI_QKV>();
   set_attr_dec_nm1<EPI_ARGMAX>();
   set_attr_dec<2, EPI_SWIGLU, 2>(); set_attr_dec<2, EPI_SWIGLU, 4>(); set_attr_dec<2, EPI_SWIGLU, kDecRowsNM2>();
+  set_attr_b<kBatchRowsNM1, 1, EPI_STORE>(); set_attr_b<kBatchRowsNM1, 1, EPI_RESID>();
+  set_attr_b<kBatchRowsNM1, 1, EPI_QKV>(); set_attr_b<kBatchRowsNM1, 1, EPI_ARGMAX>();
+  set_attr_b<kBatchRowsNM1 / 2, 1, EPI_STORE>(); set_attr_b<kBatchRowsNM1 / 2, 1, EPI_RESID>();
+  set_attr_b<kBatchRowsNM1 / 2, 1, EPI_QKV>(); set_attr_b<kBatchRowsNM1 / 2, 1, EPI_ARGMAX>();
+  set_attr_b<kBatchRowsNM2, 2, EPI_SWIGLU>();
   cudaGetLastError();
   done[dev] = true;
 }
 
 template <int EPI>
 static cudaError_t launch_mb(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
+  if (d.batch) {
+    if (!use_batch(d)) return cudaErrorInvalidValue;
+    if (d.paired) return EPI == EPI_SWIGLU ? launch_b<kBatchRowsNM2, 2, EPI_SWIGLU>(d, fc, st) : cudaErrorInvalidValue;
+    if (EPI == EPI_SWIGLU) return cudaErrorInvalidValue;
+    constexpr int E = EPI == EPI_SWIGLU ? EPI_STORE : EPI;
+    if (d.mb == kBatchRowsNM1 / 2) return launch_b<kBatchRowsNM1 / 2, 1, E>(d, fc, st);
+    return launch_b<kBatchRowsNM1, 1, E>(d, fc, st);
+  }
   if (d.paired) {
     if (EPI != EPI_SWIGLU) return cudaErrorInvalidValue;
     if (use_dec(d)) return dispatch_dec<2, EPI_SWIGLU>(d, fc, st);
@@ -749,11 +1074,11 @@ static cudaError_t launch_mb(const GemvDesc& d, const FrameCodes& fc, cudaStream
   return cudaErrorInvalidValue;
 }
 
-bool gemv_uses_decode_kernel(const GemvDesc& d) { return !d.tc && use_dec(d); }
+bool gemv_uses_decode_kernel(const GemvDesc& d) { return !d.tc && !d.batch && use_dec(d); }
 
 cudaError_t launch_gemv(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
   if (g_occ_query) {  // family and algorithmic work of this launch (profiling)
-    g_occ_family = d.tc ? FAM_TC_PROJ : (use_dec(d) ? FAM_Q4MV_DEC : FAM_Q4MV_ROWS);
+    g_occ_family = d.tc ? FAM_TC_PROJ : d.batch ? FAM_Q4MV_BATCH : (use_dec(d) ? FAM_Q4MV_DEC : FAM_Q4MV_ROWS);
     g_occ_flops = g_occ_wbytes = 0.0;
     for (int i = 0; i < (d.paired ? 2 : d.nmat); ++i) {
       const double kn = (double)d.mat[i].k * d.mat[i].n;
@@ -761,11 +1086,12 @@ cudaError_t launch_gemv(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st
       g_occ_wbytes += kn * 0.5625;
     }
   }
+  if (d.batch && (d.tc || d.attn_in || d.x_glu)) return cudaErrorInvalidValue;
   if (d.attn_in && (d.tc || !use_dec(d) || d.rows_per_split != kHeadDim || d.epi_kind != EPI_RESID))
     return cudaErrorInvalidValue;  // the attention prologue lives in the decode kernel only
   if (d.x_glu && (d.tc || !use_dec(d) || d.gamma || d.emb_idx || d.attn_in || d.paired || d.epi_kind != EPI_RESID))
     return cudaErrorInvalidValue;  // the GLU prologue lives in the decode kernel's plain input path
-  if (!d.tc && use_dec(d) &&
+  if (!d.tc && !d.batch && use_dec(d) &&
       ((d.emb_idx && d.epi_kind != EPI_STORE) || (d.gamma && d.epi_kind == EPI_RESID)))
     return cudaErrorInvalidValue;  // prologue forms the decode kernel compiles per epilogue
   if (d.tc) return launch_tc(d, fc, st);

@@ -162,6 +162,9 @@ struct GemvDesc {
   // GLU input (decode kernel only): x[r] = X[r] * X[x_glu + r], the SwiGLU
   // product of a row holding silu(gate) in [0, x_glu) and up in [x_glu, 2 x_glu)
   int x_glu = 0;
+  // batch kernel (3..15 rows on the CUDA cores): mb rows per CTA, the K
+  // slices of a tile reduced row by row inside their cluster
+  int batch = 0;
   EpiDesc epi;
 };
 // err_flag bits shared by the kernels (the session's flag word)
@@ -176,6 +179,12 @@ constexpr int kAttnInMaxPos = 32;  // cache positions the attention prologue han
 constexpr int kDecRowsNM1 = 12;  // rows per split <= 384
 constexpr int kDecMaxM = 2;      // decode kernel: input rows per launch (one per grid.z)
 constexpr int kDecRowsNM2 = 6;   // rows per split <= 192
+// batch kernel: input rows per CTA (one matrix / a gate-up pair) and the
+// largest K slice it stages in shared memory (one matrix / a pair)
+constexpr int kBatchRowsNM1 = 8;
+constexpr int kBatchRowsNM2 = 4;
+constexpr int kBatchMaxRpsNM1 = 768;
+constexpr int kBatchMaxRpsNM2 = 512;
 constexpr int kSsqLd = 64;       // row stride of the sum-of-squares partials
 constexpr int kSsqCols = 128;    // columns summed per partial (rows up to 64 * 128 wide)
 
@@ -217,7 +226,9 @@ inline thread_local int g_occ_clusters = 0;
 // algorithmic work of a projection launch (useful FLOPs 2*M*k*n, Q4 weight
 // bytes k*n*0.5625): lets the profiling entry point sort a frame's launches
 // by family without launching them.
-enum KernelFamily : int { FAM_OTHER = 0, FAM_Q4MV_DEC = 1, FAM_Q4MV_ROWS = 2, FAM_TC_PROJ = 3, FAM_ATTN = 4 };
+enum KernelFamily : int {
+  FAM_OTHER = 0, FAM_Q4MV_DEC = 1, FAM_Q4MV_ROWS = 2, FAM_TC_PROJ = 3, FAM_ATTN = 4, FAM_Q4MV_BATCH = 5
+};
 inline thread_local int g_occ_family = FAM_OTHER;
 inline thread_local double g_occ_flops = 0.0, g_occ_wbytes = 0.0;
 int occupancy_clusters(const void* func, const cudaLaunchConfig_t& cfg);

@@ -25,7 +25,7 @@ ERR_BADARG, ERR_OOM, ERR_CUDA, ERR_TIMEOUT, ERR_FORMAT, ERR_IO, ERR_STATE, ERR_N
 IGNORE_EOS = 1
 FULL_PROMPT = 2  # benchmark mode: the whole text prefilled (qtts.h QTTS_FULL_PROMPT)
 # kernel families of the frame plan (qtts.h QTTS_FAMILY_*)
-FAMILY_Q4MV_DEC, FAMILY_Q4MV_ROWS, FAMILY_TC_PROJ, FAMILY_ATTN = 1, 2, 3, 4
+FAMILY_Q4MV_DEC, FAMILY_Q4MV_ROWS, FAMILY_TC_PROJ, FAMILY_ATTN, FAMILY_Q4MV_BATCH = 1, 2, 3, 4, 5
 
 
 class QttsError(RuntimeError):

@@ -102,9 +102,11 @@ SHAPES = [  # (k=in, n=out): benchmark config 2 and the real model shapes
 
 
 @pytest.mark.parametrize("k,n", SHAPES)
-@pytest.mark.parametrize("m", [1, 2, 3, 8, 16, 64, 130])
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8, 9, 15, 16, 64, 130])
 def test_q4_gemv_matches_float64(qtts, k, n, m):
-    # m >= 16 runs on the tcgen05 path (fp16 hi/lo operands, f32 accumulate)
+    # m = 3..15 runs the batch kernel (8 rows per CTA: 9 and 15 leave a
+    # partial second row block); m >= 16 the tcgen05 path (fp16 hi/lo
+    # operands, f32 accumulate)
     rng = np.random.default_rng(k * 7 + n + m)
     packed, scales = rand_q4(rng, k, n)
     x = rng.standard_normal((m, k)).astype(np.float32)
@@ -125,9 +127,10 @@ def test_q4_gemv_matches_oracle(qtts, oracle_mod, k, n):
     assert np.max(np.abs(y - yo)) <= RTOL * np.max(np.abs(yo))
 
 
-def test_q4_gemv_dev_deterministic(qtts):
+@pytest.mark.parametrize("m", [1, 8, 15])
+def test_q4_gemv_dev_deterministic(qtts, m):
     rng = np.random.default_rng(5)
-    k, n, m = 2048, 6144, 1
+    k, n = 2048, 6144
     packed, scales = rand_q4(rng, k, n)
     dp = torch.from_numpy(packed).cuda()
     ds = torch.from_numpy(scales.view(np.int16)).cuda()
@@ -141,6 +144,17 @@ def test_q4_gemv_dev_deterministic(qtts):
         outs.append(y)
     torch.cuda.synchronize()
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+    if m > 1:  # row i of a batch equals the same row computed alone, to f32 rounding
+        y1 = torch.empty(1, n, device="cuda")
+        sb1 = qtts.q4_gemv_scratch_bytes(k, n, 1)
+        scr1 = torch.zeros(sb1, dtype=torch.uint8, device="cuda")
+        qtts.q4_gemv_dev(dp.data_ptr(), ds.data_ptr(), k, n, x[m - 1:].data_ptr(), 1, y1.data_ptr(),
+                         scr1.data_ptr(), sb1)
+        torch.cuda.synchronize()
+        d = (outs[0][m - 1] - y1[0]).abs().max().item()
+        assert d <= RTOL * y1.abs().max().item(), d
+    if m != 1:
+        return
     with pytest.raises(qtts.QttsError):
         qtts.q4_gemv_dev(dp.data_ptr(), ds.data_ptr(), k, n, x.data_ptr(), m, outs[0].data_ptr(),
                          scr.data_ptr(), 16)

@@ -178,6 +178,23 @@ def test_batched_tensor_core_teacher_forced_tiny(qtts, gpu_tiny, reps):
         _check_forced(codes[i], golden(c), lg[i])
 
 
+@pytest.mark.parametrize("n", [3, 12])
+def test_batched_small_teacher_forced_tiny(qtts, gpu_tiny, n):
+    # 3 and 12 utterances: the frame's projections have 3..15 rows and run
+    # on the batch kernel (12 rows: a full and a partial 8-row block; the
+    # predictor's two-row first step of 3 utterances has 6 rows); every
+    # utterance must match its own oracle run
+    H = gpu_tiny.dims.t_hidden
+    cases = (["tiny_greedy", "tiny_sampled", "tiny_speaker", "tiny_notext"] * 3)[:n]
+    F = 24
+    s = qtts.Session(gpu_tiny, len(cases), 10 + F)
+    codes, frames, lg, _ = qtts.generate(s, [tiny_case(c, H) for c in cases], F,
+                                         forced=_forced_batch(cases, F), dump_logits=True)
+    s.close()
+    for i, c in enumerate(cases):
+        _check_forced(codes[i], golden(c), lg[i])
+
+
 def test_generate_deterministic(qtts, gpu_tiny):
     u = tiny_case("tiny_sampled", gpu_tiny.dims.t_hidden)
     s = qtts.Session(gpu_tiny, 1, 40)
@@ -232,6 +249,24 @@ def test_1p7b_config1_batched_tensor_core(qtts, gpu_1p7b):
     g = golden("p1p7b_config1")
     u, F = W.config1(2048)
     n = 16
+    s = qtts.Session(gpu_1p7b, n, 10 + F)
+    codes, frames, lg, _ = qtts.generate(s, [u] * n, F, forced=np.repeat(g["codes"][None], n, axis=0),
+                                         dump_logits=True)
+    s.close()
+    for i in range(n):
+        assert frames[i] == F
+        _check_forced(codes[i], g, lg[i], max_ties=1)
+
+
+@pytest.mark.slow
+def test_1p7b_config1_small_batch(qtts, gpu_1p7b):
+    # config 1 replicated 5 times: the frame's projections run with M = 5 on
+    # the batch kernel at the model's real shapes (the talker's gate/up pair,
+    # the QKV, residual and argmax epilogues); every copy must follow the oracle
+    from qtts_b200 import workload as W
+    g = golden("p1p7b_config1")
+    u, F = W.config1(2048)
+    n = 5
     s = qtts.Session(gpu_1p7b, n, 10 + F)
     codes, frames, lg, _ = qtts.generate(s, [u] * n, F, forced=np.repeat(g["codes"][None], n, axis=0),
                                          dump_logits=True)
