@@ -10,10 +10,11 @@ utterance the GPU holds.
 Default workload, config 5: 512 utterances (prompts of 16-256 tokens, own
 voice and seed each, T=0.8 / top-k 50, 500 frames) split into contiguous
 blocks over the N GPUs (strong scaling), each GPU decoding its block as
-waves of 64 utterances: one CUDA graph per wave and frame, the waves of a
-GPU serialised on the device so that every GPU always works on one batch of
-64 rows.  value = frames of all ranks / max-over-ranks device time of the K
-timed steps.  The timed steps sit at the middle of the 500-frame utterances
+waves of up to 128 utterances (one session and one CUDA graph per wave and
+frame), up to 4 waves side by side on their own streams (--wave, --lanes).
+A projection of one wave is latency-bound and leaves SMs idle that another
+wave's kernels fill.  value = frames of all ranks / max-over-ranks device
+time of the K timed steps.  The timed steps sit at the middle of the 500-frame utterances
 (the cache holds ~260 positions), after W warm-up steps and untimed frames.
 The batch-1 headline (config 1: one greedy utterance, 32-token prompt) is
 timed on every rank as the line's `batch1` sub-record.
@@ -45,7 +46,10 @@ PEAKS_PATH = os.path.join(REPO, "MEASURED_PEAKS.json")
 MODEL_DIR = os.environ.get("QTTS_MODEL_DIR", "/tmp/qtts_models")
 MODEL_1P7B = os.path.join(MODEL_DIR, "qtts_1p7b_seed0.qora-tts")
 KV_BYTES_PER_POS = 28 * 8 * 128 * 2 * 4  # talker K+V read per cached position, f32
-WAVE = 64  # utterances a GPU decodes at once (config 5: 64 per GPU)
+WAVE = 64  # utterances of one session (config 4: 64 concurrent utterances per GPU)
+# config 5 (512 utterances over the GPUs): a GPU's share runs as sessions of
+# up to 128 utterances, up to 4 of them side by side on their own streams
+WAVE5, LANES5 = 128, 4
 # frames per utterance of each workload (the timed window sits at the middle)
 UTT_FRAMES = {"config1": 100, "config3": 2000, "config4": 500, "config5": 500}
 # DRAM bytes (read + write) of one config-5 frame step's tc_proj_kernel
@@ -371,37 +375,51 @@ def workload_utts(args, rank, world, W):
         return utts, "config4: 1.7B Q4, 64 utterances per GPU, T=0.8 top-k 50, prompts 16-256 tokens"
     utts, _ = W.config5_shard(rank, world)
     return utts, (f"config5: 1.7B Q4, 512 utterances (prompts 16-256 tokens, T=0.8 top-k 50) split over "
-                  f"{world} GPU(s), waves of {WAVE} per GPU")
+                  f"{world} GPU(s), waves of up to {args.wave} per GPU, {args.lanes} side by side")
 
 
 class Waves:
-    """The rank's utterances as waves of up to 64, one session + generation
-    each; a step launches one frame graph per wave, the waves chained through
-    events so that the GPU runs one wave at a time."""
+    """The rank's utterances as waves of up to `wave`, one session +
+    generation each; a step launches one frame graph per wave.  The waves are spread
+    over `lanes` chains of events: the waves of one lane run one after the
+    other, the lanes side by side on their sessions' streams (a projection of
+    one wave leaves SMs idle that a kernel of another lane can use)."""
 
-    def __init__(self, Q, torch, model, utts, frames, full_prompt):
+    def __init__(self, Q, torch, model, utts, frames, full_prompt, lanes=1, wave=WAVE):
         self.torch = torch
-        self.waves = [utts[i:i + WAVE] for i in range(0, len(utts), WAVE)]
+        self.waves = [utts[i:i + wave] for i in range(0, len(utts), wave)]
+        self.lanes = max(1, min(lanes, len(self.waves)))
         max_text = max(len(u["text"]) for u in utts)
         self.maxp = 10 + (max_text if full_prompt else 0) + frames + 1
         self.sessions = [Q.Session(model, len(w), self.maxp) for w in self.waves]
         self.gens = [Q.Generation(s, w, frames, full_prompt=full_prompt) for s, w in zip(self.sessions, self.waves)]
         self.streams = [torch.cuda.ExternalStream(s.stream) for s in self.sessions]
-        self.last = torch.cuda.Event()
-        self.last_stream = self.streams[0]
-        self.last.record(self.last_stream)
+        self.root = torch.cuda.current_stream()
+        self.ev = [torch.cuda.Event() for _ in range(self.lanes)]
+        for e in self.ev:
+            e.record(self.root)
 
-    def first_stream(self):
-        self.streams[0].wait_event(self.last)
-        return self.streams[0]
+    def start(self, e0):
+        """Record e0 on the root stream; every lane starts after it."""
+        e0.record(self.root)
+        for l in range(self.lanes):
+            self.ev[l] = e0
 
     def steps(self, n):
         for _ in range(n):
-            for g, st in zip(self.gens, self.streams):
-                st.wait_event(self.last)
+            for i, (g, st) in enumerate(zip(self.gens, self.streams)):
+                l = i % self.lanes
+                st.wait_event(self.ev[l])
                 g.frames(1)
-                self.last.record(st)
-                self.last_stream = st
+                e = self.torch.cuda.Event()
+                e.record(st)
+                self.ev[l] = e
+
+    def join(self, e1):
+        """Record e1 on the root stream once every lane is done."""
+        for e in self.ev:
+            self.root.wait_event(e)
+        e1.record(self.root)
 
     def close(self):
         for s in self.sessions:
@@ -413,7 +431,7 @@ def run_frames(args, rank, world, local, Q, W, torch, model, peak, peak_kind):
     utts, wl = workload_utts(args, rank, world, W)
     start = timed_window(args.workload, args.steps, args.warmup)
     F = start + args.steps + 1
-    wv = Waves(Q, torch, model, utts, F, args.full_prompt)
+    wv = Waves(Q, torch, model, utts, F, args.full_prompt, lanes=args.lanes, wave=args.wave)
     wv.steps(start)  # warm-up steps and the frames before the timed window (untimed)
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
@@ -422,9 +440,9 @@ def run_frames(args, rank, world, local, Q, W, torch, model, peak, peak_kind):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
-    e0.record(wv.first_stream())
+    wv.start(e0)
     wv.steps(args.steps)
-    e1.record(wv.last_stream)
+    wv.join(e1)
     e1.synchronize()
     torch.cuda.synchronize()
     barrier(world)
@@ -439,23 +457,34 @@ def run_frames(args, rank, world, local, Q, W, torch, model, peak, peak_kind):
     kv_mid = 10 + start + args.steps // 2
     res = {"t": t, "value": total_utt * args.steps / t, "ms_per_step": t / args.steps * 1e3, "n_utt": n_utt,
            "total_utt": total_utt, "waves": len(wv.waves), "kernels_per_frame": nk, "start": start,
-           "kv_mid": kv_mid, "clocks": clk, "wl": wl}
+           "kv_mid": kv_mid, "clocks": clk, "wl": wl, "lanes": wv.lanes}
 
     # e2e: the public qtts_generate call per wave with host buffers (prefill,
     # the frame graph replays of frames 0..F-1, codes copied back); the frame
     # graph captured above is reused (same shape)
     torch.cuda.synchronize()
     barrier(world)
+    def lane_e2e(l):  # the waves of one lane, one public call each (ctypes drops the GIL inside)
+        for i in range(l, len(wv.waves), wv.lanes):
+            Q.generate(wv.sessions[i], wv.waves[i], F, full_prompt=args.full_prompt)
     t0 = time.perf_counter()
-    for s, w in zip(wv.sessions, wv.waves):
-        Q.generate(s, w, F, full_prompt=args.full_prompt)
+    if wv.lanes == 1:
+        lane_e2e(0)
+    else:
+        import threading
+        th = [threading.Thread(target=lane_e2e, args=(l,)) for l in range(wv.lanes)]
+        for x in th:
+            x.start()
+        for x in th:
+            x.join()
     t_e2e = reduce_over_ranks(time.perf_counter() - t0, "max")
     res["e2e"] = {"value": total_utt * F / t_e2e, "unit": "frames/s",
                   "h2d_bytes_per_step": sum(int(np.asarray(x["text"]).nbytes) + (2048 * 4 if x.get("voice") is not None
                                                                                  else 0) for x in utts) / F,
                   "d2h_bytes_per_step": (n_utt * F * 16 * 4 + n_utt * 4) / F,
                   "includes": f"per wave: qtts_generate = prefill + {F} frame-graph replays (frames 0..{F - 1}) + "
-                              f"codes to the host; the frame graph is reused across calls",
+                              f"codes to the host; the frame graph is reused across calls; "
+                              f"{wv.lanes} host thread(s), one per lane of waves",
                   "graph_captures_per_wave": wv.sessions[0].graph_captures()}
 
     # the dominant kernel family of a frame step (tc_proj_kernel at 64 rows,
@@ -469,9 +498,11 @@ def run_frames(args, rank, world, local, Q, W, torch, model, peak, peak_kind):
     return res
 
 
-def roofline_tc(ft, peaks, ms_frame, B):
-    """tc_proj_kernel, all its launches in one frame step of B utterances:
-    useful FLOPs (2*M*k*n per matrix) over their device time."""
+def roofline_tc(ft, peaks, ms_step, waves, B):
+    """tc_proj_kernel, all its launches in one frame step of one wave of B
+    utterances: useful FLOPs (2*M*k*n per matrix) over their device time,
+    replayed alone; `overlapped` credits the same FLOPs of every wave to the
+    timed step, whose waves run side by side."""
     peak = peaks.get("bf16_tflops_sustained") or 1400.0
     sec = ft["ms"] / 1e3
     ach = ft["flops"] / sec / 1e12 if sec > 0 else None
@@ -481,7 +512,11 @@ def roofline_tc(ft, peaks, ms_frame, B):
             "kernel": f"tc_proj_kernel: every tcgen05 projection of one frame step ({B} rows), "
                       f"{ft['launches']} launches replayed alone in frame order",
             "us_per_launch": ft["ms"] * 1e3 / max(ft["launches"], 1), "ms_per_frame_step": ft["ms"],
-            "share_of_step": ft["ms"] / ms_frame if ms_frame else None,
+            "overlapped": {"achieved": ft["flops"] * waves / (ms_step / 1e3) / 1e12,
+                           "frac": ft["flops"] * waves / (ms_step / 1e3) / 1e12 / peak,
+                           "lanes_overlap": ft["ms"] * waves / ms_step,
+                           "note": "the family's FLOPs of every wave over the timed step time; lanes_overlap = "
+                                   "waves x the family time alone / step time"},
             "algorithmic_flops_per_launch": ft["flops"] / max(ft["launches"], 1),
             "q4_weight_gbs": ft["weight_bytes"] / sec / 1e9 if sec > 0 else None,
             "peak_kind": "bf16_tflops_sustained (measured)" if "bf16_tflops_sustained" in peaks else "fallback",
@@ -535,11 +570,19 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="config5", choices=["config1", "config2", "config3", "config4", "config5"])
     ap.add_argument("--only", default="", help="config2: one case, KxNxM")
+    ap.add_argument("--lanes", type=int, default=None,
+                    help=f"frame workloads: waves run side by side (event chains); config5 {LANES5}, else 1")
+    ap.add_argument("--wave", type=int, default=None,
+                    help=f"frame workloads: utterances per wave (one session each); config5 {WAVE5}, else {WAVE}")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batch1", action="store_true", help="skip the config-1 sub-record")
     ap.add_argument("--full-prompt", action="store_true",
                     help="prefill the whole text (ragged KV lengths across utterances; config4/5)")
     args = ap.parse_args()
+    if args.wave is None:
+        args.wave = WAVE5 if args.workload == "config5" else WAVE
+    if args.lanes is None:
+        args.lanes = LANES5 if args.workload == "config5" else 1
     args.warmup = max(3, args.warmup)
     rank, world, local = dist_setup(args)
     if args.impl == "reference":
@@ -582,7 +625,7 @@ def main():
         except Exception as ex:  # reported, never fatal for the GPU line
             cpu = {"value": None, "error": str(ex)}
     B = r["n_utt"] / r["waves"]
-    roof = roofline_tc(r["family"], peaks, r["ms_per_step"] / r["waves"], int(B)) if batched else \
+    roof = roofline_tc(r["family"], peaks, r["ms_per_step"], r["waves"], int(B)) if batched else \
         roofline_dec(r["family"], peak, peak_kind, r["ms_per_step"])
     line = {
         "metric": METRIC, "value": r["value"], "unit": "frames/s", "n_gpus": world, "steps": args.steps,
@@ -590,7 +633,7 @@ def main():
         "scaling": "strong" if args.workload == "config5" else "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": r["wl"], "global_batch": int(r["total_utt"]), "utterances_per_gpu": r["n_utt"],
-                   "waves_per_gpu": r["waves"], "frames_timed": args.steps,
+                   "waves_per_gpu": r["waves"], "wave_lanes": r["lanes"], "frames_timed": args.steps,
                    "frames_window": [r["start"], r["start"] + args.steps], "kv_len_mid": r["kv_mid"],
                    "l2": "inputs larger than L2 (0.86 GB of Q4 weights per frame step; 6 GB of expanded "
                          "tensor-core operand tiles at batch >= 16)",

@@ -427,8 +427,10 @@ static int plan_gemv(Session& s, GemvDesc& g) {
         ((size_t)tc_splits(g) * g.M * g.ncols > s.part_floats || 2 * (size_t)g.ntiles * zt > s.n_counters))
       return fail(QTTS_ERR_OOM, "split-K scratch too small for this projection");
   }
+  // the CUDA-core kernels' tile counters (the tensor-core kernel's are checked above)
   const size_t zb = (size_t)ceil_div(g.M, g.mb);
-  if ((size_t)g.ntiles * zb > s.n_counters || zb > 4096) return fail(QTTS_ERR_OOM, "tile counter array too small");
+  if (!g.tc && ((size_t)g.ntiles * zb > s.n_counters || zb > 4096))
+    return fail(QTTS_ERR_OOM, "tile counter array too small");
   g.counters = s.counters;
   if (g.epi_kind == EPI_ARGMAX) {
     g.epi.counters2 = s.counters2;

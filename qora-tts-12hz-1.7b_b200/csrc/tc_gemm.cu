@@ -294,6 +294,7 @@ __device__ __forceinline__ float warp_sum(float v) {
 template <int NP>
 struct ARegs {
   float x[NP][16];
+  uint4 g[2];  // the RMSNorm weights of the 16-deep k slice (same for every row)
 };
 
 }  // namespace
@@ -440,8 +441,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   const bool a_thr = tid >= kBConv && tid < kConv;
   const int at = tid - kBConv, arow = at & 63, akc = (at >> 6) & 3;
   const int npass = NP == 1 ? 1 : (Mv > 64 ? 2 : 1);  // NP: passes compiled (1: blocks of <= 64 rows)
+  const bool g16 = d.gamma && (reinterpret_cast<uintptr_t>(d.gamma) & 15u) == 0;
   auto load_a = [&](int ks, ARegs<NP>& R) {
     const int kk0 = ks * TK + akc * 16;
+    if (g16 && kk0 + 16 <= d.k && !(kEmb && d.emb_idx)) {  // with the rows, one stage ahead
+      R.g[0] = __ldg(reinterpret_cast<const uint4*>(d.gamma + kk0));
+      R.g[1] = __ldg(reinterpret_cast<const uint4*>(d.gamma + kk0) + 1);
+    }
 #pragma unroll
     for (int p = 0; p < NP; ++p) {
       const int r = arow + 64 * p;
@@ -506,10 +512,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
         for (int j = 0; j < 16; ++j) y[j] = R.x[p][j];
         if (d.gamma && !(kEmb && d.emb_idx)) {
           const float inv = s_inv[r];
-          if (kk0 + 16 <= d.k && (reinterpret_cast<uintptr_t>(d.gamma) & 15u) == 0) {  // two 16-byte loads
-            const uint4 g4[2] = {__ldg(reinterpret_cast<const uint4*>(d.gamma + kk0)),
-                                 __ldg(reinterpret_cast<const uint4*>(d.gamma + kk0) + 1)};
-            const __half2* g2 = reinterpret_cast<const __half2*>(g4);
+          if (kk0 + 16 <= d.k && g16) {  // the two 16-byte loads issued with the rows
+            const __half2* g2 = reinterpret_cast<const __half2*>(R.g);
 #pragma unroll
             for (int j = 0; j < 8; ++j) {  // (x * inv) * gamma, pairwise in f32x2 (gemv.rs:414)
               const float2 t = __fmul2_rn(__fmul2_rn(make_float2(y[2 * j], y[2 * j + 1]), make_float2(inv, inv)),

@@ -160,12 +160,14 @@ def _forced_batch(cases, F):
     return np.stack(out).astype(np.uint32)
 
 
-@pytest.mark.parametrize("reps", [5, 10])
+@pytest.mark.parametrize("reps", [5, 10, 32])
 def test_batched_tensor_core_teacher_forced_tiny(qtts, gpu_tiny, reps):
-    # 20 / 40 utterances: every projection of the frame has M >= 16 rows and
-    # runs on the tcgen05 path (with 40, the predictor's two-row first step
-    # has 80 rows: the two-pass instance, fed by the expanded weights); each
-    # utterance must still match its own oracle run
+    # 20 / 40 / 128 utterances: every projection of the frame has M >= 16
+    # rows and runs on the tcgen05 path (with 40, the predictor's two-row
+    # first step has 80 rows: the two-pass instance, fed by the expanded
+    # weights; with 128, the talker has one full 128-row block and the
+    # predictor's first step two); each utterance must still match its own
+    # oracle run
     H = gpu_tiny.dims.t_hidden
     base = ["tiny_greedy", "tiny_sampled", "tiny_speaker", "tiny_notext"]
     cases = base * reps
@@ -193,6 +195,33 @@ def test_batched_small_teacher_forced_tiny(qtts, gpu_tiny, n):
     s.close()
     for i, c in enumerate(cases):
         _check_forced(codes[i], golden(c), lg[i])
+
+
+def test_concurrent_sessions_match_sequential(qtts, gpu_tiny):
+    # two sessions whose frame graphs replay side by side on their own
+    # streams (the way the benchmark overlaps waves) must produce exactly
+    # the codes of the same sessions run one after the other
+    H = gpu_tiny.dims.t_hidden
+    base = ["tiny_greedy", "tiny_sampled", "tiny_speaker", "tiny_notext"]
+    waves = [[tiny_case(c, H) for c in base * 5], [tiny_case(c, H) for c in (base * 5)[::-1]]]
+    F = 16
+    ref = []
+    for w in waves:  # sequential
+        s = qtts.Session(gpu_tiny, len(w), 10 + F)
+        g = qtts.Generation(s, w, F)
+        g.frames(F)
+        ref.append(g.end()[0])
+        s.close()
+    sess = [qtts.Session(gpu_tiny, len(w), 10 + F) for w in waves]
+    gens = [qtts.Generation(s, w, F) for s, w in zip(sess, waves)]
+    for _ in range(F):  # interleaved launches, no synchronisation between the sessions
+        for g in gens:
+            g.frames(1)
+    got = [g.end()[0] for g in gens]
+    for s in sess:
+        s.close()
+    for a, b in zip(got, ref):
+        assert np.array_equal(a, b)
 
 
 def test_generate_deterministic(qtts, gpu_tiny):
