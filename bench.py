@@ -10,8 +10,8 @@ utterance the GPU holds.
 Default workload, config 5: 512 utterances (prompts of 16-256 tokens, own
 voice and seed each, T=0.8 / top-k 50, 500 frames) split into contiguous
 blocks over the N GPUs (strong scaling), each GPU decoding its block as
-waves of up to 128 utterances (one session and one CUDA graph per wave and
-frame), up to 4 waves side by side on their own streams (--wave, --lanes).
+waves of up to 256 utterances (one session and one CUDA graph per wave and
+frame), up to 2 waves side by side on their own streams (--wave, --lanes).
 A projection of one wave is latency-bound and leaves SMs idle that another
 wave's kernels fill.  value = frames of all ranks / max-over-ranks device
 time of the K timed steps.  The timed steps sit at the middle of the 500-frame utterances
@@ -48,8 +48,8 @@ MODEL_1P7B = os.path.join(MODEL_DIR, "qtts_1p7b_seed0.qora-tts")
 KV_BYTES_PER_POS = 28 * 8 * 128 * 2 * 4  # talker K+V read per cached position, f32
 WAVE = 64  # utterances of one session (config 4: 64 concurrent utterances per GPU)
 # config 5 (512 utterances over the GPUs): a GPU's share runs as sessions of
-# up to 128 utterances, up to 4 of them side by side on their own streams
-WAVE5, LANES5 = 128, 4
+# up to 256 utterances, up to 2 of them side by side on their own streams
+WAVE5, LANES5 = 256, 2
 # frames per utterance of each workload (the timed window sits at the middle)
 UTT_FRAMES = {"config1": 100, "config3": 2000, "config4": 500, "config5": 500}
 # DRAM bytes (read + write) of one config-5 frame step's tc_proj_kernel

@@ -700,9 +700,11 @@ static int add_text_proj(Session& s, std::vector<Op>& ops, const uint32_t* tok_d
 
 static int run_ops(Session& s, const std::vector<Op>& ops) {
   chain_reset();  // the next op list starts its own prefetch chain
-  for (const Op& op : ops) {
-    const cudaError_t e = op(s.st);
-    if (e != cudaSuccess) return fail(QTTS_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
+  for (size_t i = 0; i < ops.size(); ++i) {
+    const cudaError_t e = ops[i](s.st);
+    if (e != cudaSuccess)
+      return fail(QTTS_ERR_CUDA, "kernel launch (op " + std::to_string(i) + " of " + std::to_string(ops.size()) +
+                                     "): " + cudaGetErrorString(e));
   }
   return QTTS_OK;
 }

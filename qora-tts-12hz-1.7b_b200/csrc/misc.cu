@@ -8,6 +8,8 @@
 
 namespace qtts {
 
+constexpr int kMaxGridY = 65535;  // grid.y limit: row kernels loop over the rest
+
 namespace {
 constexpr LaunchOpts kPdl = {true, 1};
 }  // namespace
@@ -81,16 +83,17 @@ cudaError_t launch_fuse(const FuseDesc& d, cudaStream_t st) {
 __global__ void embed_rows_kernel(const Q4Mat m, const uint32_t* idx, int count, float* out, long ldo) {
   pdl_launch_dependents();
   pdl_wait();
-  const int i = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= count || j >= m.n) return;
-  const uint32_t r = idx[i];
-  out[(size_t)i * ldo + j] = q4_value(m.packed + (size_t)r * (m.n / 2), m.scales + (size_t)r * (m.n / 32), j);
+  if (j >= m.n) return;
+  for (int i = blockIdx.y; i < count; i += gridDim.y) {  // rows past grid.y's 65535 limit loop
+    const uint32_t r = idx[i];
+    out[(size_t)i * ldo + j] = q4_value(m.packed + (size_t)r * (m.n / 2), m.scales + (size_t)r * (m.n / 32), j);
+  }
 }
 cudaError_t launch_embed_rows(const Q4Mat& mat, const uint32_t* idx, int count, float* out, long ldo,
                               cudaStream_t st) {
   if (count <= 0) return cudaSuccess;
-  const dim3 grid((mat.n + 255) / 256, count);
+  const dim3 grid((mat.n + 255) / 256, std::min(count, kMaxGridY));
   return launch_k(embed_rows_kernel, dim3(grid), dim3(256), 0, st, kPdl, mat, idx, count, out, ldo);
 }
 
@@ -109,63 +112,64 @@ cudaError_t launch_embed_code0(const Q4Mat& mat, const SlotState* slots, int B, 
   return launch_k(embed_code0_kernel, dim3(grid), dim3(256), 0, st, kPdl, mat, slots, out, ldo);
 }
 
-__global__ void add_rows_kernel(const float* a, long lda, const float* b, long ldb, float* out, long ldo, int n) {
+__global__ void add_rows_kernel(const float* a, long lda, const float* b, long ldb, float* out, long ldo, int rows,
+                                int n) {
   pdl_launch_dependents();
   pdl_wait();
-  const int r = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= n) return;
-  out[(size_t)r * ldo + j] = a[(size_t)r * lda + j] + b[(size_t)r * ldb + j];
+  for (int r = blockIdx.y; r < rows; r += gridDim.y) out[(size_t)r * ldo + j] = a[(size_t)r * lda + j] + b[(size_t)r * ldb + j];
 }
 cudaError_t launch_add_rows(const float* a, long lda, const float* b, long ldb, float* out, long ldo, int rows,
                             int n, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
-  const dim3 grid((n + 255) / 256, rows);
-  return launch_k(add_rows_kernel, dim3(grid), dim3(256), 0, st, kPdl, a, lda, b, ldb, out, ldo, n);
+  const dim3 grid((n + 255) / 256, std::min(rows, kMaxGridY));
+  return launch_k(add_rows_kernel, dim3(grid), dim3(256), 0, st, kPdl, a, lda, b, ldb, out, ldo, rows, n);
 }
 
 // Prefill rows of generate_new.rs:94-173: each row is codec_emb(tok) +
 // text_proj(row), the raw voice embedding, or a text_proj row alone.
 __global__ void assemble_kernel(const Q4Mat codec, const RowRecipe* rec, const float* tp, long ldtp,
-                                const float* voice, long ldv, float* out, long ldo, int H) {
+                                const float* voice, long ldv, float* out, long ldo, int H, int rows) {
   pdl_launch_dependents();
   pdl_wait();
-  const int r = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= H) return;
-  const RowRecipe q = rec[r];
-  float v;
-  if (q.voice >= 0) {
-    v = voice[(size_t)q.voice * ldv + j];
-  } else if (q.codec >= 0) {
-    const float c = q4_value(codec.packed + (size_t)q.codec * (codec.n / 2),
-                             codec.scales + (size_t)q.codec * (codec.n / 32), j);
-    v = (q.tp >= 0) ? c + tp[(size_t)q.tp * ldtp + j] : c;
-  } else {
-    v = tp[(size_t)q.tp * ldtp + j];
+  for (int r = blockIdx.y; r < rows; r += gridDim.y) {
+    const RowRecipe q = rec[r];
+    float v;
+    if (q.voice >= 0) {
+      v = voice[(size_t)q.voice * ldv + j];
+    } else if (q.codec >= 0) {
+      const float c = q4_value(codec.packed + (size_t)q.codec * (codec.n / 2),
+                               codec.scales + (size_t)q.codec * (codec.n / 32), j);
+      v = (q.tp >= 0) ? c + tp[(size_t)q.tp * ldtp + j] : c;
+    } else {
+      v = tp[(size_t)q.tp * ldtp + j];
+    }
+    out[(size_t)r * ldo + j] = v;
   }
-  out[(size_t)r * ldo + j] = v;
 }
 cudaError_t launch_assemble(const Q4Mat& codec, const RowRecipe* rec, int rows, const float* tp, long ldtp,
                             const float* voice, long ldv, float* out, long ldo, int H, cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
-  const dim3 grid((H + 255) / 256, rows);
-  return launch_k(assemble_kernel, dim3(grid), dim3(256), 0, st, kPdl, codec, rec, tp, ldtp, voice, ldv, out, ldo, H);
+  const dim3 grid((H + 255) / 256, std::min(rows, kMaxGridY));
+  return launch_k(assemble_kernel, dim3(grid), dim3(256), 0, st, kPdl, codec, rec, tp, ldtp, voice, ldv, out, ldo, H,
+                  rows);
 }
 
-__global__ void gather_rows_kernel(const float* src, long lds, const int* idx, float* out, long ldo, int n) {
+__global__ void gather_rows_kernel(const float* src, long lds, const int* idx, float* out, long ldo, int rows, int n) {
   pdl_launch_dependents();
   pdl_wait();
-  const int r = blockIdx.y;
   const int j = blockIdx.x * blockDim.x + threadIdx.x;
   if (j >= n) return;
-  out[(size_t)r * ldo + j] = src[(size_t)idx[r] * lds + j];
+  for (int r = blockIdx.y; r < rows; r += gridDim.y) out[(size_t)r * ldo + j] = src[(size_t)idx[r] * lds + j];
 }
 cudaError_t launch_gather_rows(const float* src, long lds, const int* idx, int rows, float* out, long ldo, int n,
                                cudaStream_t st) {
   if (rows <= 0) return cudaSuccess;
-  const dim3 grid((n + 255) / 256, rows);
-  return launch_k(gather_rows_kernel, dim3(grid), dim3(256), 0, st, kPdl, src, lds, idx, out, ldo, n);
+  const dim3 grid((n + 255) / 256, std::min(rows, kMaxGridY));
+  return launch_k(gather_rows_kernel, dim3(grid), dim3(256), 0, st, kPdl, src, lds, idx, out, ldo, rows, n);
 }
 
 // ---- frame bookkeeping --------------------------------------------------------
@@ -238,22 +242,24 @@ __global__ void f16_gemv_kernel(const __half* w, int k, int n, const float* x, i
   pdl_launch_dependents();
   pdl_wait();
   const int j2 = blockIdx.x * blockDim.x + threadIdx.x;
-  const int row = blockIdx.y;
-  if (2 * j2 >= n || row >= m) return;
-  const float* xr = x + (size_t)row * k;
-  float a0 = 0.0f, a1 = 0.0f;
-  for (int kk = 0; kk < k; ++kk) {
-    const __half2 wv = *reinterpret_cast<const __half2*>(w + (size_t)kk * n + 2 * j2);
-    const float xv = xr[kk];
-    a0 = __fadd_rn(a0, __fmul_rn(xv, __low2float(wv)));
-    a1 = __fadd_rn(a1, __fmul_rn(xv, __high2float(wv)));
+  if (2 * j2 >= n) return;
+  for (int row = blockIdx.y; row < m; row += gridDim.y) {
+    const float* xr = x + (size_t)row * k;
+    float a0 = 0.0f, a1 = 0.0f;
+    for (int kk = 0; kk < k; ++kk) {
+      const __half2 wv = *reinterpret_cast<const __half2*>(w + (size_t)kk * n + 2 * j2);
+      const float xv = xr[kk];
+      a0 = __fadd_rn(a0, __fmul_rn(xv, __low2float(wv)));
+      a1 = __fadd_rn(a1, __fmul_rn(xv, __high2float(wv)));
+    }
+    y[(size_t)row * n + 2 * j2] = a0;
+    y[(size_t)row * n + 2 * j2 + 1] = a1;
   }
-  y[(size_t)row * n + 2 * j2] = a0;
-  y[(size_t)row * n + 2 * j2 + 1] = a1;
 }
 cudaError_t launch_f16_gemv(const __half* w, int k, int n, const float* x, int m, float* y, cudaStream_t st) {
   if (n % 2) return cudaErrorInvalidValue;
-  const dim3 grid((n / 2 + 127) / 128, m);
+  if (m <= 0) return cudaSuccess;
+  const dim3 grid((n / 2 + 127) / 128, std::min(m, kMaxGridY));
   return launch_k(f16_gemv_kernel, dim3(grid), dim3(128), 0, st, kPdl, w, k, n, x, m, y);
 }
 

@@ -224,6 +224,26 @@ def test_concurrent_sessions_match_sequential(qtts, gpu_tiny):
         assert np.array_equal(a, b)
 
 
+def test_prefill_rows_past_grid_limit_tiny(qtts, gpu_tiny):
+    # 270 utterances of 255 text tokens: about 68000 trailing-text rows, more
+    # than a launch's 65535 grid rows, so the row kernels loop; the first and
+    # the last utterance must decode exactly as they do alone
+    from qtts_b200 import make_params
+    from qtts_b200 import workload as W
+    H = gpu_tiny.dims.t_hidden
+    utts = [dict(text=W.tokens(100 + i, 255), voice=W.voice_embedding(200 + i, H), seed=7 + i,
+                 params=make_params(0.8, 50, 1.05)) for i in range(270)]
+    F = 4
+    s = qtts.Session(gpu_tiny, len(utts), 10 + F)
+    cb, fb, _, _ = qtts.generate(s, utts, F)
+    s.close()
+    for i in (0, len(utts) - 1):
+        s1 = qtts.Session(gpu_tiny, 1, 10 + F)
+        c1, f1, _, _ = qtts.generate(s1, [utts[i]], F)
+        s1.close()
+        assert np.array_equal(cb[i], c1[0]), i
+
+
 def test_generate_deterministic(qtts, gpu_tiny):
     u = tiny_case("tiny_sampled", gpu_tiny.dims.t_hidden)
     s = qtts.Session(gpu_tiny, 1, 40)
