@@ -430,7 +430,7 @@ def run_frames(args, rank, world, local, Q, W, torch, model, peak, peak_kind):
     import numpy as np
     utts, wl = workload_utts(args, rank, world, W)
     start = timed_window(args.workload, args.steps, args.warmup)
-    F = start + args.steps + 1
+    F = start + args.steps + 1 + (1 if args.profile_step else 0)
     wv = Waves(Q, torch, model, utts, F, args.full_prompt, lanes=args.lanes, wave=args.wave)
     wv.steps(start)  # warm-up steps and the frames before the timed window (untimed)
     torch.cuda.synchronize()
@@ -450,6 +450,16 @@ def run_frames(args, rank, world, local, Q, W, torch, model, peak, peak_kind):
     t = reduce_over_ranks(e0.elapsed_time(e1) / 1e3, "max")
     n_utt = len(utts)
     total_utt = reduce_over_ranks(n_utt, "sum")
+    if args.profile_step:
+        # one more step of every wave inside cudaProfilerStart/Stop (no-ops
+        # without a profiler): `ncu --profile-from-start off` sees exactly it
+        torch.cuda.synchronize()
+        torch.cuda.profiler.start()
+        wv.start(torch.cuda.Event())
+        wv.steps(1)
+        wv.join(torch.cuda.Event())
+        torch.cuda.synchronize()
+        torch.cuda.profiler.stop()
     for g in wv.gens:
         codes, frames = g.end()
         assert int(frames.min()) >= start + args.steps, frames
@@ -576,6 +586,9 @@ def main():
                     help=f"frame workloads: utterances per wave (one session each); config5 {WAVE5}, else {WAVE}")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batch1", action="store_true", help="skip the config-1 sub-record")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="after the timed steps, one more step inside cudaProfilerStart/Stop (for ncu "
+                         "--profile-from-start off)")
     ap.add_argument("--full-prompt", action="store_true",
                     help="prefill the whole text (ragged KV lengths across utterances; config4/5)")
     args = ap.parse_args()

@@ -520,6 +520,11 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
     AttnDesc a;
     a.q = s.q; a.ldq = qd; a.out = s.attn; a.ldo = qd; a.kv = io.kv; a.rp = io.rp;
     a.heads = io.heads; a.kv_heads = io.kvh; a.M = io.M; a.nsplit = io.nsplit;
+    // The early L2 prefetch of the K / V rows helps while everything it pulls
+    // stays resident until read (small batches, long caches).  With many rows
+    // the launch's cache (up to M * kv_heads * maxP positions, K and V of
+    // 512 bytes each) exceeds L2 and prefetched lines evict each other first.
+    a.l2_prefetch = (double)io.M * io.kvh * s.maxP * 2.0 * kHeadDim * sizeof(float) <= kAttnPrefetchMaxBytes;
     if (a.nsplit > 1) {
       const size_t need = (size_t)io.M * io.kvh * a.nsplit * (io.heads / io.kvh) * kAttnRec;
       if (need > s.apart_floats || (size_t)io.M * io.kvh > s.n_acounters)

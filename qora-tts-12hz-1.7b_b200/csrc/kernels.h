@@ -304,6 +304,9 @@ struct AttnDesc {
   unsigned* counters = nullptr; // [M][kv_heads]
   int l2_prefetch = 1;          // pull the CTA's K / V rows into L2 before the dependent-launch wait
 };
+// largest cache (K + V bytes over all rows of a launch) whose rows the
+// attention kernel prefetches into L2 (126 MB) before its dependency wait
+constexpr double kAttnPrefetchMaxBytes = 48.0 * (1 << 20);
 cudaError_t launch_attention(const AttnDesc& d, cudaStream_t st);
 
 struct SampleDesc {
