@@ -422,6 +422,8 @@ static int plan_gemv(Session& s, GemvDesc& g) {
   if (g.M >= kTcMinRows) {
     tc_plan(s.m->sm_count, g);  // one tcgen05 kernel: prologue, GEMM, split-K, epilogue
     g.part = s.part;
+    g.xs_buf = s.xs_buf;
+    g.xs_bytes = s.xs_bytes;
     const size_t zt = (size_t)ceil_div(g.M, kTcRows);
     if (tc_splits(g) > 1 &&
         ((size_t)tc_splits(g) * g.M * g.ncols > s.part_floats || 2 * (size_t)g.ntiles * zt > s.n_counters))
@@ -776,7 +778,8 @@ static void session_free_all(Session* s) {
     if (b.p) cudaFree(b.p);
   void* bufs[] = {s->kv_pool, s->page_table, s->pkv_pool, s->slots, s->x, s->pin, s->q, s->attn, s->h,
                   s->px, s->px1, s->logits, s->xpre, s->hid1, s->part, s->counters, s->counters2, s->keys,
-                  s->apart, s->acounters, s->err_flag, s->codes_plain, s->io, s->ssq_t, s->ssq_p, s->ssq_p1};
+                  s->apart, s->acounters, s->err_flag, s->codes_plain, s->io, s->ssq_t, s->ssq_p, s->ssq_p1,
+                  s->xs_buf};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (s->st) cudaStreamDestroy(s->st);
@@ -826,6 +829,16 @@ static int session_create(Model* m, int maxB, int maxP, Session** out) {
   A(&s->keys, (size_t)std::max(maxB * 10, 4096));
   s->apart_floats = (size_t)8 << 20;
   A(&s->apart, s->apart_floats);
+  // split input-row tiles for the frame's tensor-core launches with row blocks
+  // of more than 64 rows (up to 2 rows per utterance, at most 1024 rows; larger
+  // launches split their rows in the kernel): 128-row blocks x 64-deep stages
+  // x 32 KB (fp16 hi + lo), over the widest input of any projection
+  if (2 * maxB > 64) {
+    const int xrows = std::min(2 * maxB, 1024);
+    const int kmax = std::max(std::max(imax, qmax), std::max(d.t_hidden, d.p_hidden));
+    s->xs_bytes = (size_t)ceil_div(xrows, 128) * ceil_div(kmax, 64) * 32768;
+    A(&s->xs_buf, s->xs_bytes);
+  }
   s->n_acounters = (size_t)s->rows * std::max(d.t_kv_heads, d.p_kv_heads);
   A(&s->acounters, s->n_acounters);
   A(&s->err_flag, (size_t)1);

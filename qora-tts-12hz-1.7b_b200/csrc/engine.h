@@ -65,6 +65,8 @@ struct Session {
   size_t n_counters = 0;
   unsigned* counters2 = nullptr;
   unsigned long long* keys = nullptr;
+  uint8_t* xs_buf = nullptr;  // input rows split into tensor-core operand tiles (row blocks > 64 rows)
+  size_t xs_bytes = 0;
   float* apart = nullptr;
   size_t apart_floats = 0;
   unsigned* acounters = nullptr;

@@ -151,6 +151,12 @@ struct GemvDesc {
   int attn_group = 1;             // query heads per KV head
   int tc = 0;
   int tc_ks = 0;
+  // tensor-core launches of more than 64 rows per block: session scratch
+  // for the input rows split once into operand tiles (tc_xsplit_kernel),
+  // and, set for the projection kernel at launch, the split tiles
+  uint8_t* xs_buf = nullptr;
+  size_t xs_bytes = 0;
+  const uint8_t* x_split = nullptr;
   // weights of the next projection in the frame (packed and scales of up to
   // three matrices), pulled into L2 by this launch's CTAs as they start
   const uint8_t* pf_ptr[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};

@@ -328,6 +328,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   const int m0 = mb * TM;
   const int Mv = min(TM, d.M - m0);
   const uint32_t tsm_a = smem_u32(tsm);
+  // Row blocks of more than 64 rows on the on-disk weights may get their
+  // input rows split once for all column tiles (tc_xsplit_kernel): the
+  // stage's two X operand halves then arrive by one bulk copy, and every
+  // converter warp dequantises weights.
+  const bool xs = !WX && NP == 2 && d.x_split != nullptr;
 
   // ---- raw weight tiles stream into the ring RS - 1 stages ahead; the
   // weights are never written by an earlier kernel, so this starts before
@@ -403,6 +408,14 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       bulk_g2s(st_a + 2 * C::XB + (NM + a) * B_BYTES, src + B_BYTES, B_BYTES, &wfull[b]);
     }
   };
+  // pre-split input rows: block (row block mb, stage) of the split tiles,
+  // hi then lo, straight into the stage's X halves, completing on wfull
+  auto issue_xs = [&](int i) {
+    const int b = i % C::STAGES;
+    mbar_expect_tx(&wfull[b], (uint32_t)(2 * C::XB));
+    bulk_g2s(tsm_a + (uint32_t)(b * C::STAGE_BYTES), d.x_split + ((size_t)mb * nks_all + (ks0 + i)) * (2 * C::XB),
+             (uint32_t)(2 * C::XB), &wfull[b]);
+  };
 
   if (tid == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -410,7 +423,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       mbar_init(&full[s], kConv);
     }
     mbar_init(fin, 1);
-    if (WX)
+    if (WX || xs)
       for (int s = 0; s < C::STAGES; ++s) mbar_init(&wfull[s], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     *s_flag = 0u;
@@ -424,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   // (the MMAs read Nr rows; rows past Nr are never read)
   const int Nr = (Mv + 15) & ~15;
   const uint32_t idesc = idesc_rows(Nr);
-  if (Mv < Nr) {
+  if (!xs && Mv < Nr) {  // (the split tiles carry their zero rows)
     const int zrows = Nr - Mv;
     for (int i = tid; i < C::STAGES * 2 * zrows * (TK / 8); i += kThreads) {
       // rows fastest: 8 consecutive threads fill 8 different 16-byte bank groups
@@ -475,14 +488,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   // the first stage's input rows are issued now, so their round trip overlaps
   // the TMEM allocation and the 1/rms loads below
   ARegs<NP> an;
-  if (a_thr) load_a(ks0, an);
+  if (a_thr && !xs) load_a(ks0, an);
+  if (xs && tid == 0) {  // the split tiles come from the kernel just before: after the wait
+    for (int j = 0; j < C::STAGES && j < nst; ++j) issue_xs(j);
+    w_issued = min(C::STAGES, nst);
+  }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                  "r"(C::TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
-  // 1 / rms of each row (gemv.rs:408-417)
-  if (d.gamma) {
+  // 1 / rms of each row (gemv.rs:408-417; applied by the split kernel instead)
+  if (d.gamma && !xs) {
     if (d.ssq_in) {
       for (int r = tid; r < Mv; r += kThreads) s_inv[r] = inv_rms_from_ssq(d, m0 + r);
     } else {
@@ -596,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       const int b = i % C::STAGES;
       uint8_t* st = tsm + b * C::STAGE_BYTES;
       const ARegs<NP> ac = an;
-      if (a_thr && i + 1 < nst) load_a(ks0 + i + 1, an);  // input rows one stage ahead
+      if (a_thr && !xs && i + 1 < nst) load_a(ks0 + i + 1, an);  // input rows one stage ahead
       cp_async_wait<C::RS - 2>();  // this thread's raw copies of stage i have landed
       // this operand buffer was read by the MMAs of stage i - STAGES
       bool w_ok = true;
@@ -605,12 +622,18 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
         issue_w(i);
         w_issued = i + 1;
       }
+      if (xs && tid == 0 && i >= C::STAGES && w_ok) {
+        issue_xs(i);
+        w_issued = i + 1;
+      }
       // publishes every converter's raw copies of stage i; every conversion of
       // stage i - 1 is done, so its raw slot takes stage i + RS - 1
       if (!conv_sync_and(w_ok)) { ok = false; break; }
       if (!WX && i + C::RS - 1 < nst) issue_b(ks0 + i + C::RS - 1, (i + C::RS - 1) % C::RS);
       cp_async_commit();
-      if (a_thr) {
+      if (xs) {  // weights only, every converter thread
+        for (int q = tid; q < NM * 256; q += kConv) store_chunk(st + 2 * C::XB, i % C::RS, q);
+      } else if (a_thr) {
         store_a(ks0 + i, ac, st, st + C::XB);
         if (!WX && at < 4 * kChunksRem) store_word(st + 2 * C::XB, i % C::RS, kBConv * NM + at % kChunksRem, at / kChunksRem);
       } else if (!WX && tid < kBConv) {
@@ -625,7 +648,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
     for (int i = 0; i < nst; ++i) {
       const int b = i % C::STAGES;
       bool f_ok = mbar_wait(&full[b], (unsigned)(i / C::STAGES) & 1u);
-      if (WX && f_ok) f_ok = mbar_wait(&wfull[b], (unsigned)(i / C::STAGES) & 1u);
+      if ((WX || xs) && f_ok) f_ok = mbar_wait(&wfull[b], (unsigned)(i / C::STAGES) & 1u);
       if (!__all_sync(0xffffffffu, f_ok)) { ok = false; break; }
       if (lane == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -651,7 +674,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
     if (lane == 0) umma_commit(fin);
   }
   cp_async_wait<0>();  // no copy may land after the ring is reused for staging
-  if (WX && tid == 0) {  // nor a weight copy (bounded; all have landed unless a wait timed out)
+  if ((WX || xs) && tid == 0) {  // nor a weight (or split-row) copy (bounded; all have landed unless a wait timed out)
     for (int j = max(0, w_issued - C::STAGES); j < w_issued; ++j)
       if (!mbar_wait(&wfull[j % C::STAGES], (unsigned)(j / C::STAGES) & 1u)) atomicOr(s_flag, (unsigned)kErrTimeout);
   }
@@ -896,6 +919,91 @@ static cudaError_t launch_np(const GemvDesc& d, const FrameCodes& fc, cudaStream
                   o, d, fc);
 }
 
+// ---------------------------------------------------------------------------
+// Input rows split once for a projection whose column tiles would each split
+// them again (row blocks of more than 64 rows): block (row block rb of 128
+// rows, stage ks of 64) at (rb * nks + ks) * 2 * A_BYTES holds the fp16 hi
+// then the fp16 (lo * 2^11) operand half, K-major core matrices, exactly as
+// the projection kernel's input-row threads write them: the same RMSNorm
+// (1/rms from the producer's sums of squares or over the row, then x * inv *
+// gamma pairwise), the same split; rows past M and k past K are zero.
+// 512 threads: row r = tid % 128, 16-deep slice tid / 128 of the stage.
+__global__ void __launch_bounds__(512) tc_xsplit_kernel(const GemvDesc d, uint8_t* out) {
+  __shared__ float s_inv[TM];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int ks = blockIdx.x, rb = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = tid & (TM - 1), akc = tid >> 7;
+  const int m = rb * TM + r, kk0 = ks * TK + akc * 16;
+  const int nks = (d.k + TK - 1) / TK;
+  if (d.gamma) {
+    if (d.ssq_in) {
+      if (tid < TM && rb * TM + tid < d.M) s_inv[tid] = inv_rms_from_ssq(d, rb * TM + tid);
+    } else {
+      for (int rr = warp; rr < TM; rr += 16) {
+        if (rb * TM + rr >= d.M) break;
+        const float* xr = d.X + (size_t)(rb * TM + rr) * d.ldx;
+        float ss = 0.0f;
+        for (int i = lane; i < d.k; i += 32) ss += xr[i] * xr[i];
+        ss = warp_sum(ss);
+        if (lane == 0) s_inv[rr] = 1.0f / sqrtf(ss / (float)d.k + 1e-6f);
+      }
+    }
+    __syncthreads();
+  }
+  float y[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) y[j] = 0.0f;
+  if (m < d.M) {
+    const float* xr = d.X + (size_t)m * d.ldx + kk0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 v = (kk0 + 4 * q < d.k) ? __ldg(reinterpret_cast<const float4*>(xr) + q)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      y[4 * q] = v.x; y[4 * q + 1] = v.y; y[4 * q + 2] = v.z; y[4 * q + 3] = v.w;
+    }
+    if (d.gamma) {
+      const float inv = s_inv[r];
+      if (kk0 + 16 <= d.k && (reinterpret_cast<uintptr_t>(d.gamma) & 15u) == 0) {
+        const uint4 g4[2] = {__ldg(reinterpret_cast<const uint4*>(d.gamma + kk0)),
+                             __ldg(reinterpret_cast<const uint4*>(d.gamma + kk0) + 1)};
+        const __half2* g2 = reinterpret_cast<const __half2*>(g4);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {  // (x * inv) * gamma, pairwise in f32x2 (gemv.rs:414)
+          const float2 t = __fmul2_rn(__fmul2_rn(make_float2(y[2 * j], y[2 * j + 1]), make_float2(inv, inv)),
+                                      __half22float2(g2[j]));
+          y[2 * j] = t.x;
+          y[2 * j + 1] = t.y;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) y[j] = (kk0 + j < d.k) ? y[j] * inv * h2f(d.gamma[kk0 + j]) : 0.0f;
+      }
+    }
+  }
+  float amax = 0.0f;
+  uint8_t* hi = out + ((size_t)rb * nks + ks) * (2 * A_BYTES);
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {  // two 8-deep k chunks
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      amax = fmaxf(amax, fmaxf(fabsf(y[c * 8 + 2 * q]), fabsf(y[c * 8 + 2 * q + 1])));
+      split2(y[c * 8 + 2 * q], y[c * 8 + 2 * q + 1], h[q], l[q]);
+    }
+    const int off = (r >> 3) * 1024 + (akc * 2 + c) * 128 + (r & 7) * 16;
+    *reinterpret_cast<uint4*>(hi + off) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(hi + A_BYTES + off) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+  if (amax > 65504.0f && d.err_flag) atomicOr(d.err_flag, kErrFp16Range);
+}
+
+// Bytes of split tiles a launch of M rows over K needs.
+static size_t tc_xsplit_bytes(int M, int k) {
+  return (size_t)((M + TM - 1) / TM) * ((k + TK - 1) / TK) * (2 * A_BYTES);
+}
+
 template <int NM, int EPI>
 static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
   // row blocks of at most 64 rows run the instance compiled for one input-row
@@ -908,6 +1016,21 @@ static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_
     return launch_np<NM, EPI, 1>(d, fc, st);
   }
   if (wx && d.M <= TM) return launch_np<NM, EPI, 2, true>(d, fc, st);
+  // input rows split once for every column tile when the session's scratch
+  // holds them (not for the embedding gather or the normed-row copy)
+  if (d.xs_buf && !d.emb_idx && !d.xnorm_out && d.X && tc_xsplit_bytes(d.M, d.k) <= d.xs_bytes &&
+      (reinterpret_cast<uintptr_t>(d.xs_buf) & 15u) == 0) {
+    GemvDesc e = d;
+    e.x_split = d.xs_buf;
+    if (!g_occ_query) {
+      const dim3 grid((d.k + TK - 1) / TK, (d.M + TM - 1) / TM);
+      LaunchOpts o;
+      o.pdl = d.pdl != 0;
+      const cudaError_t err = launch_k(tc_xsplit_kernel, grid, dim3(512), 0, st, o, d, d.xs_buf);
+      if (err != cudaSuccess) return err;
+    }
+    return launch_np<NM, EPI, 2>(e, fc, st);
+  }
   return launch_np<NM, EPI, 2>(d, fc, st);
 }
 
