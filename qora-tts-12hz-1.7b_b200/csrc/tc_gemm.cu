@@ -931,12 +931,31 @@ static cudaError_t launch_np(const GemvDesc& d, const FrameCodes& fc, cudaStream
 __global__ void __launch_bounds__(512) tc_xsplit_kernel(const GemvDesc d, uint8_t* out) {
   __shared__ float s_inv[TM];
   pdl_launch_dependents();
-  pdl_wait();
   const int ks = blockIdx.x, rb = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r = tid & (TM - 1), akc = tid >> 7;
   const int m = rb * TM + r, kk0 = ks * TK + akc * 16;
   const int nks = (d.k + TK - 1) / TK;
+  const bool g16 = d.gamma && kk0 + 16 <= d.k && (reinterpret_cast<uintptr_t>(d.gamma) & 15u) == 0;
+  uint4 g4[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+  if (g16) {  // norm weights never depend on an earlier kernel: before the wait
+    g4[0] = __ldg(reinterpret_cast<const uint4*>(d.gamma + kk0));
+    g4[1] = __ldg(reinterpret_cast<const uint4*>(d.gamma + kk0) + 1);
+  }
+  pdl_wait();
+  // every load is issued before the first is used: the row slice, then the
+  // producer's sums of squares of the block's rows
+  float y[16];
+  const bool live = m < d.M;
+  {
+    const float* xr = d.X + (size_t)(live ? m : 0) * d.ldx + kk0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 v = (live && kk0 + 4 * q < d.k) ? __ldg(reinterpret_cast<const float4*>(xr) + q)
+                                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+      y[4 * q] = v.x; y[4 * q + 1] = v.y; y[4 * q + 2] = v.z; y[4 * q + 3] = v.w;
+    }
+  }
   if (d.gamma) {
     if (d.ssq_in) {
       if (tid < TM && rb * TM + tid < d.M) s_inv[tid] = inv_rms_from_ssq(d, rb * TM + tid);
@@ -951,23 +970,9 @@ __global__ void __launch_bounds__(512) tc_xsplit_kernel(const GemvDesc d, uint8_
       }
     }
     __syncthreads();
-  }
-  float y[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) y[j] = 0.0f;
-  if (m < d.M) {
-    const float* xr = d.X + (size_t)m * d.ldx + kk0;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float4 v = (kk0 + 4 * q < d.k) ? __ldg(reinterpret_cast<const float4*>(xr) + q)
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
-      y[4 * q] = v.x; y[4 * q + 1] = v.y; y[4 * q + 2] = v.z; y[4 * q + 3] = v.w;
-    }
-    if (d.gamma) {
+    if (live) {
       const float inv = s_inv[r];
-      if (kk0 + 16 <= d.k && (reinterpret_cast<uintptr_t>(d.gamma) & 15u) == 0) {
-        const uint4 g4[2] = {__ldg(reinterpret_cast<const uint4*>(d.gamma + kk0)),
-                             __ldg(reinterpret_cast<const uint4*>(d.gamma + kk0) + 1)};
+      if (g16) {
         const __half2* g2 = reinterpret_cast<const __half2*>(g4);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {  // (x * inv) * gamma, pairwise in f32x2 (gemv.rs:414)
