@@ -631,8 +631,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       if (!conv_sync_and(w_ok)) { ok = false; break; }
       if (!WX && i + C::RS - 1 < nst) issue_b(ks0 + i + C::RS - 1, (i + C::RS - 1) % C::RS);
       cp_async_commit();
-      if (xs) {  // weights only, every converter thread
-        for (int q = tid; q < NM * 256; q += kConv) store_chunk(st + 2 * C::XB, i % C::RS, q);
+      if (xs) {  // weights only, every converter thread: a chunk each, and the
+        // chunks past the threads (a gate/up pair: 32) one word each over as many threads
+        if (tid < NM * 256) store_chunk(st + 2 * C::XB, i % C::RS, tid);
+        constexpr int kXsRem = NM * 256 - kConv;
+        if (kXsRem > 0 && tid < 4 * kXsRem)
+          store_word(st + 2 * C::XB, i % C::RS, kConv + tid % (kXsRem > 0 ? kXsRem : 1), tid / (kXsRem > 0 ? kXsRem : 1));
       } else if (a_thr) {
         store_a(ks0 + i, ac, st, st + C::XB);
         if (!WX && at < 4 * kChunksRem) store_word(st + 2 * C::XB, i % C::RS, kBConv * NM + at % kChunksRem, at / kChunksRem);
