@@ -172,6 +172,10 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnDesc d) {
     if (nsp == 1) {
       float4 o = make_float4(a.x / lt, a.y / lt, a.z / lt, a.w / lt);
       *reinterpret_cast<float4*>(d.out + (size_t)m * d.ldo + (h * G + g) * kHeadDim + 4 * ln) = o;
+      if (d.xs_out) {  // the o projection's input rows, split for its tensor-core kernel
+        xs_store4(d.xs_out, d.heads * kHeadDim, m, (h * G + g) * kHeadDim + 4 * ln, o);
+        if (fp16_overflow4(o) && d.err_flag) atomicOr(d.err_flag, kErrFp16Input);
+      }
     } else {
       if (ln == 0) { s_rec[g][0] = M; s_rec[g][1] = lt; }
       *reinterpret_cast<float4*>(&s_rec[g][4 + 4 * ln]) = a;

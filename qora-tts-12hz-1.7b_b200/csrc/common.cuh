@@ -63,6 +63,41 @@ __device__ __forceinline__ void q4_word_fma(uint32_t w, const SxPack& s, float2*
   acc[3] = __ffma2_rn(d3, s.d, acc[3]);
 }
 
+// ---- input rows split for the tensor-core projection ----------------------
+// An f32 pair becomes the fp16 pair hi = fp16(x) and the fp16 pair
+// lo = fp16((x - hi) * 2^11): x - hi is exact in f32 and so is the scaling,
+// and the 2^11 keeps lo clear of the fp16 subnormals (sm_100 f32x2 ops).
+constexpr float kSplitLoScale = 2048.0f;
+__device__ __forceinline__ uint32_t half2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __half2 h = __floats2half2_rn(a, b);
+  const float2 hf = __half22float2(h);
+  hi = half2_bits(h);
+  const float2 r = __fmul2_rn(__ffma2_rn(hf, make_float2(-1.0f, -1.0f), make_float2(a, b)),
+                              make_float2(kSplitLoScale, kSplitLoScale));
+  lo = half2_bits(__floats2half2_rn(r.x, r.y));
+}
+// Split tiles of a projection's input rows (K wide): block (row m / 128,
+// column c / 64) of 32 KB holds the hi half then the lo half, each K-major
+// core matrices of 8 rows x 16 bytes, row r and column j of the block at
+// (r / 8) * 1024 + (j / 8) * 128 + (r % 8) * 16 + (j % 8) * 2.
+constexpr int kXsRows = 128, kXsK = 64, kXsHalf = kXsRows * kXsK * 2;
+// Row m, columns c..c+3 (c % 4 == 0) of value v; the producer of a row
+// writes all of its K columns.
+__device__ __forceinline__ void xs_store4(uint8_t* buf, int K, int m, int c, float4 v) {
+  const int nks = (K + kXsK - 1) / kXsK, r = m & (kXsRows - 1), j = c & (kXsK - 1);
+  uint8_t* p = buf + ((size_t)(m / kXsRows) * nks + c / kXsK) * (2 * kXsHalf) + (r >> 3) * 1024 + (j >> 3) * 128 +
+               (r & 7) * 16 + (j & 7) * 2;
+  uint32_t h0, l0, h1, l1;
+  split_pair(v.x, v.y, h0, l0);
+  split_pair(v.z, v.w, h1, l1);
+  *reinterpret_cast<uint2*>(p) = make_uint2(h0, h1);
+  *reinterpret_cast<uint2*>(p + kXsHalf) = make_uint2(l0, l1);
+}
+__device__ __forceinline__ bool fp16_overflow4(float4 v) {
+  return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))) > 65504.0f;
+}
+
 // Dequantised value of column j of a Q4 row (gemv.rs:393-396): f32(scale)*(q-8).
 __device__ __forceinline__ float q4_value(const uint8_t* packed_row, const __half* scales_row, int j) {
   const uint8_t b = packed_row[j >> 1];

@@ -534,6 +534,12 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
       a.part = s.apart;
       a.counters = s.acounters;
     }
+    // o on split input rows (tensor cores, > 64 rows): the attention writes them
+    if (a.nsplit == 1 && s.xs_buf2 && tc_takes_split(o)) {
+      a.xs_out = s.xs_buf2;
+      a.err_flag = s.err_flag;
+      o.x_split_pre = s.xs_buf2;
+    }
     ops.push_back([a](cudaStream_t st) { return launch_attention(a, st); });
   }
   ops.push_back(gemv_op(o));
@@ -567,6 +573,13 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
     gu.X = io.X; gu.ldx = io.ldx; gu.gamma = L.post_norm; gu.epi.out = s.h; gu.epi.ldo = io.inter;
     use_ssq(gu, true);
     RC(plan_gemv(s, gu));
+    // down on split input rows: the gate/up epilogue writes them (its own
+    // input rows come split from the other buffer)
+    if (gu.tc && s.xs_buf2 && tc_takes_split(dn)) {
+      gu.xs_out = s.xs_buf2;
+      gu.xs_out_k = io.inter;
+      dn.x_split_pre = s.xs_buf2;
+    }
     ops.push_back(gemv_op(gu));
   }
   ops.push_back(gemv_op(dn));
@@ -779,7 +792,7 @@ static void session_free_all(Session* s) {
   void* bufs[] = {s->kv_pool, s->page_table, s->pkv_pool, s->slots, s->x, s->pin, s->q, s->attn, s->h,
                   s->px, s->px1, s->logits, s->xpre, s->hid1, s->part, s->counters, s->counters2, s->keys,
                   s->apart, s->acounters, s->err_flag, s->codes_plain, s->io, s->ssq_t, s->ssq_p, s->ssq_p1,
-                  s->xs_buf};
+                  s->xs_buf, s->xs_buf2};
   for (void* p : bufs)
     if (p) cudaFree(p);
   if (s->st) cudaStreamDestroy(s->st);
@@ -833,11 +846,14 @@ static int session_create(Model* m, int maxB, int maxP, Session** out) {
   // of more than 64 rows (up to 2 rows per utterance, at most 1024 rows; larger
   // launches split their rows in the kernel): 128-row blocks x 64-deep stages
   // x 32 KB (fp16 hi + lo), over the widest input of any projection
+  // (two buffers: the split kernel fills one, while the producers of the o
+  // and down inputs, attention and the gate/up epilogue, write the other)
   if (2 * maxB > 64) {
     const int xrows = std::min(2 * maxB, 1024);
     const int kmax = std::max(std::max(imax, qmax), std::max(d.t_hidden, d.p_hidden));
     s->xs_bytes = (size_t)ceil_div(xrows, 128) * ceil_div(kmax, 64) * 32768;
     A(&s->xs_buf, s->xs_bytes);
+    A(&s->xs_buf2, s->xs_bytes);
   }
   s->n_acounters = (size_t)s->rows * std::max(d.t_kv_heads, d.p_kv_heads);
   A(&s->acounters, s->n_acounters);

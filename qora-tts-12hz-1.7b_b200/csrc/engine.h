@@ -66,6 +66,7 @@ struct Session {
   unsigned* counters2 = nullptr;
   unsigned long long* keys = nullptr;
   uint8_t* xs_buf = nullptr;  // input rows split into tensor-core operand tiles (row blocks > 64 rows)
+  uint8_t* xs_buf2 = nullptr; // the same, written by the producers of the o and down inputs
   size_t xs_bytes = 0;
   float* apart = nullptr;
   size_t apart_floats = 0;

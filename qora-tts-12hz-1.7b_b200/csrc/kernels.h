@@ -157,6 +157,12 @@ struct GemvDesc {
   uint8_t* xs_buf = nullptr;
   size_t xs_bytes = 0;
   const uint8_t* x_split = nullptr;
+  // split tiles of this launch's input written by its producer (no split
+  // kernel), and split tiles of this launch's output for its consumer
+  // (SwiGLU epilogue of the tensor-core kernel), xs_out_k columns wide
+  const uint8_t* x_split_pre = nullptr;
+  uint8_t* xs_out = nullptr;
+  int xs_out_k = 0;
   // weights of the next projection in the frame (packed and scales of up to
   // three matrices), pulled into L2 by this launch's CTAs as they start
   const uint8_t* pf_ptr[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
@@ -309,11 +315,16 @@ struct AttnDesc {
   float* part = nullptr;        // [M][kv_heads][nsplit][G][kAttnRec]
   unsigned* counters = nullptr; // [M][kv_heads]
   int l2_prefetch = 1;          // pull the CTA's K / V rows into L2 before the dependent-launch wait
+  // the output rows also as split tiles for the o projection (heads * 128
+  // wide; one position slice only), and the flag word for values past fp16
+  uint8_t* xs_out = nullptr;
+  int* err_flag = nullptr;
 };
 // largest cache (K + V bytes over all rows of a launch) whose rows the
 // attention kernel prefetches into L2 (126 MB) before its dependency wait
 constexpr double kAttnPrefetchMaxBytes = 48.0 * (1 << 20);
 cudaError_t launch_attention(const AttnDesc& d, cudaStream_t st);
+bool tc_takes_split(const GemvDesc& d);
 
 struct SampleDesc {
   const float* logits = nullptr;  // [B][ldl]

@@ -236,16 +236,10 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
 
-// f32 pair -> fp16 hi pair and fp16 (residual * 2^11) pair; the residual
-// a - hi is exact in f32 and the scaling by 2^11 too (sm_100 f32x2 ops)
-__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
-  const __half2 h = __floats2half2_rn(a, b);
-  const float2 hf = __half22float2(h);
-  hi = h2_bits(h);
-  const float2 r = __fmul2_rn(__ffma2_rn(hf, make_float2(-1.0f, -1.0f), make_float2(a, b)),
-                              make_float2(kLoScale, kLoScale));
-  lo = h2_bits(__floats2half2_rn(r.x, r.y));
-}
+// f32 pair -> fp16 hi pair and fp16 (residual * 2^11) pair (common.cuh)
+__device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) { split_pair(a, b, hi, lo); }
+static_assert(kXsRows == TM && kXsK == TK && kXsHalf == A_BYTES && kSplitLoScale == kLoScale,
+              "split tiles are the input-row operand halves");
 
 // 8 dequantised weights of one 32-bit word (nibble i = column i of the word,
 // gemv.rs:124) as hi / lo 16-byte core-matrix rows.  One shift + LOP3 turns
@@ -782,8 +776,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       if (cval) {
         const float g[4] = {acc[0].x, acc[0].y, acc[0].z, acc[0].w};
         const float u[4] = {acc[NM - 1].x, acc[NM - 1].y, acc[NM - 1].z, acc[NM - 1].w};
-        *reinterpret_cast<float4*>(e.out + (size_t)m * e.ldo + col) =
+        const float4 hv =
             make_float4(silu_ref(g[0]) * u[0], silu_ref(g[1]) * u[1], silu_ref(g[2]) * u[2], silu_ref(g[3]) * u[3]);
+        *reinterpret_cast<float4*>(e.out + (size_t)m * e.ldo + col) = hv;
+        if (d.xs_out) {  // the down projection's input rows, split for its tensor-core kernel
+          xs_store4(d.xs_out, d.xs_out_k, m, col, hv);
+          if (fp16_overflow4(hv) && d.err_flag) atomicOr(d.err_flag, kErrFp16Range);
+        }
       }
     } else if (EPI == EPI_QKV) {
       // mat 0 = q, 1 = k, 2 = v; the tile is head tcol / 128
@@ -1013,6 +1012,17 @@ static size_t tc_xsplit_bytes(int M, int k) {
   return (size_t)((M + TM - 1) / TM) * ((k + TK - 1) / TK) * (2 * A_BYTES);
 }
 
+// Whether a planned launch runs the tensor-core instance that reads split
+// input rows (the branch of launch_t below): its producer may then write
+// them directly.
+bool tc_takes_split(const GemvDesc& d) {
+  if (!d.tc || !d.xs_buf || d.emb_idx || d.xnorm_out || !d.X || d.M <= TM / 2) return false;
+  bool wx = true;
+  for (int i = 0; i < (d.paired ? 2 : d.nmat); ++i) wx = wx && d.mat[i].wx != nullptr;
+  if (wx && d.M <= TM) return false;
+  return tc_xsplit_bytes(d.M, d.k) <= d.xs_bytes;
+}
+
 template <int NM, int EPI>
 static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
   // row blocks of at most 64 rows run the instance compiled for one input-row
@@ -1025,6 +1035,11 @@ static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_
     return launch_np<NM, EPI, 1>(d, fc, st);
   }
   if (wx && d.M <= TM) return launch_np<NM, EPI, 2, true>(d, fc, st);
+  if (d.x_split_pre) {  // the producer of the input rows wrote them split
+    GemvDesc e = d;
+    e.x_split = d.x_split_pre;
+    return launch_np<NM, EPI, 2>(e, fc, st);
+  }
   // input rows split once for every column tile when the session's scratch
   // holds them (not for the embedding gather or the normed-row copy)
   if (d.xs_buf && !d.emb_idx && !d.xnorm_out && d.X && tc_xsplit_bytes(d.M, d.k) <= d.xs_bytes &&
