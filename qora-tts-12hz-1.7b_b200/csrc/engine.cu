@@ -842,12 +842,12 @@ static int session_create(Model* m, int maxB, int maxP, Session** out) {
   A(&s->keys, (size_t)std::max(maxB * 10, 4096));
   s->apart_floats = (size_t)8 << 20;
   A(&s->apart, s->apart_floats);
-  // split input-row tiles for the frame's tensor-core launches with row blocks
-  // of more than 64 rows (up to 2 rows per utterance, at most 1024 rows; larger
-  // launches split their rows in the kernel): 128-row blocks x 64-deep stages
-  // x 32 KB (fp16 hi + lo), over the widest input of any projection
-  // (two buffers: the split kernel fills one, while the producers of the o
-  // and down inputs, attention and the gate/up epilogue, write the other)
+  // split input-row tiles for the frame's tensor-core launches (up to 2 rows
+  // per utterance, at most 1024 rows; larger launches split their rows in
+  // the kernel): 128-row blocks x 64-deep stages x 32 KB (fp16 hi + lo),
+  // over the widest input of any projection (two buffers: the split kernel
+  // fills one, while the producers of the o and down inputs, attention and
+  // the gate/up epilogue, write the other)
   if (2 * maxB > 64) {
     const int xrows = std::min(2 * maxB, 1024);
     const int kmax = std::max(std::max(imax, qmax), std::max(d.t_hidden, d.p_hidden));

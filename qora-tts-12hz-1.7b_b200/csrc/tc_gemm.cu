@@ -1016,34 +1016,27 @@ static size_t tc_xsplit_bytes(int M, int k) {
 // input rows (the branch of launch_t below): its producer may then write
 // them directly.
 bool tc_takes_split(const GemvDesc& d) {
-  if (!d.tc || !d.xs_buf || d.emb_idx || d.xnorm_out || !d.X || d.M <= TM / 2) return false;
-  bool wx = true;
-  for (int i = 0; i < (d.paired ? 2 : d.nmat); ++i) wx = wx && d.mat[i].wx != nullptr;
-  if (wx && d.M <= TM) return false;
+  if (!d.tc || !d.xs_buf || d.emb_idx || d.xnorm_out || !d.X || d.M <= TM / 2 ||
+      (reinterpret_cast<uintptr_t>(d.xs_buf) & 15u))
+    return false;
   return tc_xsplit_bytes(d.M, d.k) <= d.xs_bytes;
 }
 
 template <int NM, int EPI>
 static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
-  // row blocks of at most 64 rows run the instance compiled for one input-row
-  // pass; with every matrix expanded (tc_expand), the one fed by bulk copies
-  // (up to one 128-row block: more blocks would copy each tile again)
-  bool wx = true;
-  for (int i = 0; i < (NM == 2 ? 2 : d.nmat); ++i) wx = wx && d.mat[i].wx != nullptr;
-  if (d.M <= TM / 2) {
-    if (wx) return launch_np<NM, EPI, 1, true>(d, fc, st);
-    return launch_np<NM, EPI, 1>(d, fc, st);
-  }
-  if (wx && d.M <= TM) return launch_np<NM, EPI, 2, true>(d, fc, st);
+  // Row blocks of more than 64 rows take their input rows split once per
+  // projection (or by their producer) whenever the session's scratch holds
+  // them: the instance with 128-row operand halves then dequantises weights
+  // with every converter warp (at 128 rows this beat the expanded tiles by
+  // 12-16%; at 64 rows the expanded tiles win).  Row blocks of at most 64 rows
+  // run the instance compiled for one input-row pass; with every matrix
+  // expanded (tc_expand), the one fed by bulk copies.
   if (d.x_split_pre) {  // the producer of the input rows wrote them split
     GemvDesc e = d;
     e.x_split = d.x_split_pre;
     return launch_np<NM, EPI, 2>(e, fc, st);
   }
-  // input rows split once for every column tile when the session's scratch
-  // holds them (not for the embedding gather or the normed-row copy)
-  if (d.xs_buf && !d.emb_idx && !d.xnorm_out && d.X && tc_xsplit_bytes(d.M, d.k) <= d.xs_bytes &&
-      (reinterpret_cast<uintptr_t>(d.xs_buf) & 15u) == 0) {
+  if (tc_takes_split(d)) {
     GemvDesc e = d;
     e.x_split = d.xs_buf;
     if (!g_occ_query) {
@@ -1055,6 +1048,13 @@ static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_
     }
     return launch_np<NM, EPI, 2>(e, fc, st);
   }
+  bool wx = true;
+  for (int i = 0; i < (NM == 2 ? 2 : d.nmat); ++i) wx = wx && d.mat[i].wx != nullptr;
+  if (d.M <= TM / 2) {
+    if (wx) return launch_np<NM, EPI, 1, true>(d, fc, st);
+    return launch_np<NM, EPI, 1>(d, fc, st);
+  }
+  if (wx && d.M <= TM) return launch_np<NM, EPI, 2, true>(d, fc, st);
   return launch_np<NM, EPI, 2>(d, fc, st);
 }
 
