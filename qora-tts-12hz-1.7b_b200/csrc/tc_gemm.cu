@@ -746,7 +746,74 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   // the very end, so the barrier's latency overlaps the epilogue.
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   // Pass 2: the epilogue, one warp per row (the warp that summed the row).
-  for (int r = rb + warp; good && r < re; r += kThreads / 32) {
+  if (EPI == EPI_QKV && good) {
+    // q / k / v: mat 0 = q, 1 = k, 2 = v; the tile is head tcol / 128.  The
+    // rows' positions and KV pages are loaded up front (lane j: the warp's
+    // j-th row), and the RoPE factors of the next row while this one is
+    // processed, so the chain of dependent loads is paid about once per warp.
+    const int h = tcol / kHeadDim, half = kHeadDim / 2;
+    const int nrw = re > rb + warp ? (re - rb - warp + 15) / 16 : 0;  // this warp's rows (<= 8)
+    int p_sess = 0, p_pos = 0, p_kvp = 0, p_page = 0;
+    if (lane < nrw) {
+      row_pos(e.rp, m0 + rb + warp + 16 * lane, p_sess, p_pos, p_kvp);
+      p_page = (mat == 2 || mat == 1) ? (e.kv.page_table ? e.kv.page_table[p_sess * e.kv.pages_per_sess + p_kvp / kPageSize]
+                                                         : p_sess)
+                                      : 0;
+    }
+    float gv[4] = {0.f, 0.f, 0.f, 0.f};
+    if (mat != 2) {
+      const __half* gn = (mat == 0) ? e.q_norm : e.k_norm;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) gv[j] = h2f(gn[cc + j]);
+    }
+    auto rope_ld = [&](int pos, float4& c4, float4& s4) {
+      if (mat != 2 && pos < e.rope_rows && pos >= 0) {
+        c4 = __ldg(reinterpret_cast<const float4*>(e.rope_cos + (size_t)pos * half + (cc % half)));
+        s4 = __ldg(reinterpret_cast<const float4*>(e.rope_sin + (size_t)pos * half + (cc % half)));
+      }
+    };
+    float4 cn = make_float4(0.f, 0.f, 0.f, 0.f), sn4 = cn;
+    if (nrw > 0) rope_ld(__shfl_sync(0xffffffffu, p_pos, 0), cn, sn4);
+    for (int jr = 0; jr < nrw; ++jr) {
+      const int r = rb + warp + 16 * jr, m = m0 + r;
+      const int pos = __shfl_sync(0xffffffffu, p_pos, jr), kvp = __shfl_sync(0xffffffffu, p_kvp, jr);
+      const int page = __shfl_sync(0xffffffffu, p_page, jr);
+      const float4 c4 = cn, s4 = sn4;
+      if (jr + 1 < nrw) rope_ld(__shfl_sync(0xffffffffu, p_pos, jr + 1), cn, sn4);
+      const float4 acc0 = *reinterpret_cast<const float4*>(red + (size_t)r * kRedLd + cc);
+      // the row's 16 KB block of the paged cache (kv_row with the page known)
+      auto kvp_row = [&](int which) {
+        const size_t blk = (((size_t)page * e.kv.n_layers + e.kv.layer) * 2 + which) * e.kv.kv_heads + h;
+        return e.kv.pool + (blk * kPageSize + (kvp % kPageSize)) * kHeadDim;
+      };
+      if (mat == 2) {
+        *reinterpret_cast<float4*>(kvp_row(1) + cc) = acc0;
+        continue;
+      }
+      const float vv[4] = {acc0.x, acc0.y, acc0.z, acc0.w};
+      const float ss = warp_sum((vv[0] * vv[0] + vv[1] * vv[1]) + (vv[2] * vv[2] + vv[3] * vv[3]));
+      const float inv = 1.0f / sqrtf(ss / (float)kHeadDim + 1e-6f);  // talker.rs:89-99
+      float y[4], pr[4], o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) y[j] = vv[j] * inv * gv[j];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) pr[j] = __shfl_xor_sync(0xffffffffu, y[j], 16);  // column +- 64
+      const bool in_range = pos < e.rope_rows && pos >= 0;
+      const float cf[4] = {c4.x, c4.y, c4.z, c4.w}, sf[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {  // split-half RoPE (rope.rs:79-92)
+        const int dd = cc + j;
+        const float x1 = dd < half ? y[j] : pr[j];
+        const float x2 = dd < half ? pr[j] : y[j];
+        o[j] = y[j];
+        if (in_range) o[j] = (dd < half) ? (x1 * cf[j] - x2 * sf[j]) : (x2 * cf[j] + x1 * sf[j]);
+      }
+      if (!in_range && !e.rope_skip_oob && e.err_flag && lane == 0) atomicOr(e.err_flag, kErrRopeRange);
+      float* dst = (mat == 0) ? e.q_out + (size_t)m * e.ldq + col : kvp_row(0) + cc;
+      *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  for (int r = rb + warp; EPI != EPI_QKV && good && r < re; r += kThreads / 32) {
     float4 acc[NM];
 #pragma unroll
     for (int a = 0; a < NM; ++a) acc[a] = *reinterpret_cast<const float4*>(red + ((size_t)a * TM + r) * kRedLd + cc);
@@ -783,48 +850,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
           xs_store4(d.xs_out, d.xs_out_k, m, col, hv);
           if (fp16_overflow4(hv) && d.err_flag) atomicOr(d.err_flag, kErrFp16Range);
         }
-      }
-    } else if (EPI == EPI_QKV) {
-      // mat 0 = q, 1 = k, 2 = v; the tile is head tcol / 128
-      const int h = tcol / kHeadDim;
-      int sess, pos, kvp;
-      row_pos(e.rp, m, sess, pos, kvp);
-      if (mat == 2) {
-        KvDesc kv = e.kv;
-        *reinterpret_cast<float4*>(kv_row(kv, sess, kvp, 1, h) + cc) = acc[0];
-      } else {
-        const float vv[4] = {acc[0].x, acc[0].y, acc[0].z, acc[0].w};
-        const float ss = warp_sum((vv[0] * vv[0] + vv[1] * vv[1]) + (vv[2] * vv[2] + vv[3] * vv[3]));
-        const float inv = 1.0f / sqrtf(ss / (float)kHeadDim + 1e-6f);  // talker.rs:89-99
-        const __half* gn = (mat == 0) ? e.q_norm : e.k_norm;
-        float y[4], pr[4], o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) y[j] = vv[j] * inv * h2f(gn[cc + j]);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) pr[j] = __shfl_xor_sync(0xffffffffu, y[j], 16);  // column +- 64
-        const int half = kHeadDim / 2;
-        const bool in_range = pos < e.rope_rows && pos >= 0;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {  // split-half RoPE (rope.rs:79-92)
-          const int dd = cc + j, i = dd % half;
-          const float x1 = dd < half ? y[j] : pr[j];
-          const float x2 = dd < half ? pr[j] : y[j];
-          o[j] = y[j];
-          if (in_range) {
-            const float c = e.rope_cos[(size_t)pos * half + i];
-            const float sn = e.rope_sin[(size_t)pos * half + i];
-            o[j] = (dd < half) ? (x1 * c - x2 * sn) : (x2 * c + x1 * sn);
-          }
-        }
-        if (!in_range && !e.rope_skip_oob && e.err_flag && lane == 0) atomicOr(e.err_flag, kErrRopeRange);
-        float* dst;
-        if (mat == 0) {
-          dst = e.q_out + (size_t)m * e.ldq + col;
-        } else {
-          KvDesc kv = e.kv;
-          dst = kv_row(kv, sess, kvp, 0, h) + cc;
-        }
-        *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
       }
     } else if (EPI == EPI_ARGMAX) {
       const float vv[4] = {acc[0].x, acc[0].y, acc[0].z, acc[0].w};
