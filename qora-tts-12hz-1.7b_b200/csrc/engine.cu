@@ -1362,11 +1362,17 @@ static int gemv_plan_standalone(int k, int n, int m, GemvDesc& g) {
 }
 
 // Scratch layout: [tile counters 16 KB][split-K partials of either kernel]
+// [split input rows of a tensor-core launch of more than 64 rows, 16-byte
+// aligned]
+static size_t gemv_part_bytes(const GemvDesc& g, int m, int n) {
+  const size_t S = std::max(g.S > 1 ? g.S : 0, g.tc && tc_splits(g) > 1 ? tc_splits(g) : 0);
+  return (sizeof(float) * S * m * n + 15) & ~(size_t)15;
+}
 static size_t gemv_scratch(int k, int n, int m) {
   GemvDesc g;
   gemv_plan_standalone(k, n, m, g);
-  const size_t S = std::max(g.S > 1 ? g.S : 0, g.tc && tc_splits(g) > 1 ? tc_splits(g) : 0);
-  return kCounterBytes + sizeof(float) * S * m * n;
+  const size_t xs = g.tc && m > 64 ? tc_xsplit_scratch_bytes(m, k) : 0;
+  return kCounterBytes + gemv_part_bytes(g, m, n) + xs;
 }
 
 static int gemv_dev(const uint8_t* packed, const uint16_t* scales, int k, int n, const float* x, int m, float* y,
@@ -1390,6 +1396,10 @@ static int gemv_dev(const uint8_t* packed, const uint16_t* scales, int k, int n,
   if (!scratch || scratch_bytes < need) return fail(QTTS_ERR_BADARG, "scratch smaller than qtts_q4_gemv_scratch_bytes()");
   g.counters = reinterpret_cast<unsigned*>(scratch);
   g.part = reinterpret_cast<float*>(reinterpret_cast<char*>(scratch) + kCounterBytes);
+  if (g.tc && m > 64) {  // the input rows split once for every column tile, as in the frame
+    g.xs_buf = reinterpret_cast<uint8_t*>(scratch) + kCounterBytes + gemv_part_bytes(g, m, n);
+    g.xs_bytes = tc_xsplit_scratch_bytes(m, k);
+  }
   // the tensor-core kernel's float4 accesses need 16-byte aligned rows
   if (g.tc && (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(y) % 16)) g.tc = 0;
   g.cluster = 1;

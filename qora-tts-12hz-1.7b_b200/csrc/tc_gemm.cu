@@ -1041,6 +1041,7 @@ __global__ void __launch_bounds__(512) tc_xsplit_kernel(const GemvDesc d, uint8_
 static size_t tc_xsplit_bytes(int M, int k) {
   return (size_t)((M + TM - 1) / TM) * ((k + TK - 1) / TK) * (2 * A_BYTES);
 }
+size_t tc_xsplit_scratch_bytes(int M, int k) { return tc_xsplit_bytes(M, k); }
 
 // Whether a planned launch runs the tensor-core instance that reads split
 // input rows (the branch of launch_t below): its producer may then write
