@@ -41,23 +41,16 @@ for _p in (REPO, PKG):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
-METRIC = "codec frames/sec"
-PEAKS_PATH = os.path.join(REPO, "MEASURED_PEAKS.json")
-MODEL_DIR = os.environ.get("QTTS_MODEL_DIR", "/tmp/qtts_models")
-MODEL_1P7B = os.path.join(MODEL_DIR, "qtts_1p7b_seed0.qora-tts")
-KV_BYTES_PER_POS = 28 * 8 * 128 * 2 * 4  # talker K+V read per cached position, f32
-WAVE = 64  # utterances of one session (config 4: 64 concurrent utterances per GPU)
-# config 5 (512 utterances over the GPUs): a GPU's share runs as sessions of
-# up to 256 utterances, up to 2 of them side by side on their own streams
-WAVE5, LANES5 = 256, 2
-# frames per utterance of each workload (the timed window sits at the middle)
-UTT_FRAMES = {"config1": 100, "config3": 2000, "config4": 500, "config5": 500}
-# DRAM bytes (read + write) of one config-5 frame step's tc_proj_kernel
-# launches (all of them, 64 rows), from an ncu capture of
-#   python bench.py --workload config4 --steps 2 --warmup 3 --no-cpu-baseline
-# with --metrics dram__bytes_read.sum,dram__bytes_write.sum -k regex:tc_proj
-# at the commit this constant was last updated with; None when not captured.
-TC_FRAME_TRAFFIC_BYTES = None
+# DRAM bytes per algorithmic byte of tc_proj_kernel at 256 rows: ncu's
+# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the gate
+# shape 2048 x 6144 x 256 (9.26 MB) over its Q4 weight and input-row bytes
+# (9.18 MB), from
+#   python bench.py --workload config2 --only 2048x6144x256
+# under `ncu --set full -k regex:tc_proj -s 10 -c 1`.  The frame's launches
+# are too large to capture with more than one pass; their traffic is this
+# ratio times their algorithmic weight bytes (their split input rows were just
+# written by the kernel before them and come from L2).
+TC_TRAFFIC_RATIO = 9.26 / 9.18
 
 
 def q4_bytes(k, n):
@@ -518,7 +511,9 @@ def roofline_tc(ft, peaks, ms_step, waves, B):
     ach = ft["flops"] / sec / 1e12 if sec > 0 else None
     return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s",
             "frac": ach / peak if ach else None,
-            "traffic": TC_FRAME_TRAFFIC_BYTES / ft["launches"] if TC_FRAME_TRAFFIC_BYTES else None,
+            "traffic": TC_TRAFFIC_RATIO * ft["weight_bytes"] / max(ft["launches"], 1),
+            "traffic_note": "per launch: the measured DRAM/algorithmic ratio of one 256-row launch (ncu, small "
+                            "case) x the family's mean Q4 weight bytes per launch",
             "kernel": f"tc_proj_kernel: every tcgen05 projection of one frame step ({B} rows), "
                       f"{ft['launches']} launches replayed alone in frame order",
             "us_per_launch": ft["ms"] * 1e3 / max(ft["launches"], 1), "ms_per_frame_step": ft["ms"],
@@ -530,8 +525,10 @@ def roofline_tc(ft, peaks, ms_step, waves, B):
             "algorithmic_flops_per_launch": ft["flops"] / max(ft["launches"], 1),
             "q4_weight_gbs": ft["weight_bytes"] / sec / 1e9 if sec > 0 else None,
             "peak_kind": "bf16_tflops_sustained (measured)" if "bf16_tflops_sustained" in peaks else "fallback",
-            "note": "tensor pipe executes 3 fp16 MMAs per product (hi/lo split for f32 accuracy); weights are read "
-                    "as expanded fp16 hi/lo operand tiles (4 B per weight) for the layer projections"}
+            "note": "tensor pipe executes 3 fp16 MMAs per product (hi/lo split for f32 accuracy); above 64 rows "
+                    "the Q4 weights are dequantised in the kernel and the input rows arrive split (the family's "
+                    "time includes the split kernels of the normed inputs); at <= 64 rows the expanded fp16 "
+                    "hi/lo operand tiles (4 B per weight) are copied instead"}
 
 
 def roofline_dec(ft, peak, peak_kind, ms_frame):
