@@ -41,6 +41,17 @@ for _p in (REPO, PKG):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
+METRIC = "codec frames/sec"
+PEAKS_PATH = os.path.join(REPO, "MEASURED_PEAKS.json")
+MODEL_DIR = os.environ.get("QTTS_MODEL_DIR", "/tmp/qtts_models")
+MODEL_1P7B = os.path.join(MODEL_DIR, "qtts_1p7b_seed0.qora-tts")
+KV_BYTES_PER_POS = 28 * 8 * 128 * 2 * 4  # talker K+V read per cached position, f32
+WAVE = 64  # utterances of one session (config 4: 64 concurrent utterances per GPU)
+# config 5 (512 utterances over the GPUs): a GPU's share runs as sessions of
+# up to 256 utterances, up to 2 of them side by side on their own streams
+WAVE5, LANES5 = 256, 2
+# frames per utterance of each workload (the timed window sits at the middle)
+UTT_FRAMES = {"config1": 100, "config3": 2000, "config4": 500, "config5": 500}
 # DRAM bytes per algorithmic byte of tc_proj_kernel at 256 rows: ncu's
 # dram__bytes_read.sum + dram__bytes_write.sum of one launch of the gate
 # shape 2048 x 6144 x 256 (9.26 MB) over its Q4 weight and input-row bytes
