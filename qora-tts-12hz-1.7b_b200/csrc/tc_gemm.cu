@@ -322,11 +322,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   const int m0 = mb * TM;
   const int Mv = min(TM, d.M - m0);
   const uint32_t tsm_a = smem_u32(tsm);
-  // Row blocks of more than 64 rows on the on-disk weights may get their
-  // input rows split once for all column tiles (tc_xsplit_kernel): the
-  // stage's two X operand halves then arrive by one bulk copy, and every
-  // converter warp dequantises weights.
-  const bool xs = !WX && NP == 2 && d.x_split != nullptr;
+  // Row blocks of more than 64 rows may get their input rows split once for
+  // all column tiles (tc_xsplit_kernel, or the rows' producer): the stage's
+  // two X operand halves then arrive by one bulk copy, and every converter
+  // warp dequantises weights -- or, with expanded weights, the stage is bulk
+  // copies only (weights and rows on the same mbarrier) and nothing converts.
+  const bool xs = NP == 2 && d.x_split != nullptr;
 
   // ---- raw weight tiles stream into the ring RS - 1 stages ahead; the
   // weights are never written by an earlier kernel, so this starts before
@@ -393,7 +394,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   auto issue_w = [&](int i) {
     const int b = i % C::STAGES;
     const uint32_t st_a = tsm_a + (uint32_t)(b * C::STAGE_BYTES);
-    mbar_expect_tx(&wfull[b], (uint32_t)(NM * 2 * B_BYTES));
+    // with split rows the stage's row copy (issued later, after the
+    // dependent-launch wait for the first stages) completes on the same phase
+    mbar_expect_tx(&wfull[b], (uint32_t)(NM * 2 * B_BYTES + (xs ? 2 * C::XB : 0)));
 #pragma unroll
     for (int a = 0; a < NM; ++a) {
       const Q4Mat& Mt = d.mat[NM == 2 ? a : mat];
@@ -406,7 +409,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
   // hi then lo, straight into the stage's X halves, completing on wfull
   auto issue_xs = [&](int i) {
     const int b = i % C::STAGES;
-    mbar_expect_tx(&wfull[b], (uint32_t)(2 * C::XB));
+    if (!WX) mbar_expect_tx(&wfull[b], (uint32_t)(2 * C::XB));  // (WX: counted by issue_w)
     bulk_g2s(tsm_a + (uint32_t)(b * C::STAGE_BYTES), d.x_split + ((size_t)mb * nks_all + (ks0 + i)) * (2 * C::XB),
              (uint32_t)(2 * C::XB), &wfull[b]);
   };
@@ -627,10 +630,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       cp_async_commit();
       if (xs) {  // weights only, every converter thread: a chunk each, and the
         // chunks past the threads (a gate/up pair: 32) one word each over as many threads
-        if (tid < NM * 256) store_chunk(st + 2 * C::XB, i % C::RS, tid);
-        constexpr int kXsRem = NM * 256 - kConv;
-        if (kXsRem > 0 && tid < 4 * kXsRem)
-          store_word(st + 2 * C::XB, i % C::RS, kConv + tid % (kXsRem > 0 ? kXsRem : 1), tid / (kXsRem > 0 ? kXsRem : 1));
+        if (!WX) {
+          if (tid < NM * 256) store_chunk(st + 2 * C::XB, i % C::RS, tid);
+          constexpr int kXsRem = NM * 256 - kConv;
+          if (kXsRem > 0 && tid < 4 * kXsRem)
+            store_word(st + 2 * C::XB, i % C::RS, kConv + tid % (kXsRem > 0 ? kXsRem : 1),
+                       tid / (kXsRem > 0 ? kXsRem : 1));
+        }
       } else if (a_thr) {
         store_a(ks0 + i, ac, st, st + C::XB);
         if (!WX && at < 4 * kChunksRem) store_word(st + 2 * C::XB, i % C::RS, kBConv * NM + at % kChunksRem, at / kChunksRem);
@@ -1062,10 +1068,12 @@ static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_
   // 12-16%; at 64 rows the expanded tiles win).  Row blocks of at most 64 rows
   // run the instance compiled for one input-row pass; with every matrix
   // expanded (tc_expand), the one fed by bulk copies.
+  bool wx = true;
+  for (int i = 0; i < (NM == 2 ? 2 : d.nmat); ++i) wx = wx && d.mat[i].wx != nullptr;
   if (d.x_split_pre) {  // the producer of the input rows wrote them split
     GemvDesc e = d;
     e.x_split = d.x_split_pre;
-    return launch_np<NM, EPI, 2>(e, fc, st);
+    return wx ? launch_np<NM, EPI, 2, true>(e, fc, st) : launch_np<NM, EPI, 2>(e, fc, st);
   }
   if (tc_takes_split(d)) {
     GemvDesc e = d;
@@ -1077,10 +1085,8 @@ static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_
       const cudaError_t err = launch_k(tc_xsplit_kernel, grid, dim3(512), 0, st, o, d, d.xs_buf);
       if (err != cudaSuccess) return err;
     }
-    return launch_np<NM, EPI, 2>(e, fc, st);
+    return wx ? launch_np<NM, EPI, 2, true>(e, fc, st) : launch_np<NM, EPI, 2>(e, fc, st);
   }
-  bool wx = true;
-  for (int i = 0; i < (NM == 2 ? 2 : d.nmat); ++i) wx = wx && d.mat[i].wx != nullptr;
   if (d.M <= TM / 2) {
     if (wx) return launch_np<NM, EPI, 1, true>(d, fc, st);
     return launch_np<NM, EPI, 1>(d, fc, st);
