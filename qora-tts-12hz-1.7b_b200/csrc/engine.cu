@@ -449,7 +449,11 @@ static void chain_reset() { g_prev_gemv.reset(); }
 
 static Op gemv_op(const GemvDesc& g, const FrameCodes& fc = FrameCodes{}) {
   auto sp = std::make_shared<GemvDesc>(g);
-  if (g_prev_gemv) {
+  // A launch that streams expanded tiles (4 bytes a weight) reads no Q4
+  // bytes, and prefetching its tiles measured slower than none (config 5:
+  // 24.0k with those of at most 32 MB, 24.9k with none; config 4 9.04k vs
+  // 9.15k): its predecessor prefetches nothing.
+  if (g_prev_gemv && !tc_reads_expanded(g)) {
     GemvDesc& p = *g_prev_gemv;
     const int nm = g.paired ? 2 : g.nmat;
     for (int i = 0; i < nm && i < 3; ++i) {

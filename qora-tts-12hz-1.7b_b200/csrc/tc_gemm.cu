@@ -1059,6 +1059,16 @@ bool tc_takes_split(const GemvDesc& d) {
   return tc_xsplit_bytes(d.M, d.k) <= d.xs_bytes;
 }
 
+// Whether a tensor-core launch of `d` streams the expanded weight tiles (the
+// choice launch_t makes below): every matrix expanded, and a row block of at
+// most 64 rows, split input rows, or at most 128 rows.
+bool tc_reads_expanded(const GemvDesc& d) {
+  if (!d.tc) return false;
+  for (int i = 0; i < (d.paired ? 2 : d.nmat); ++i)
+    if (!d.mat[i].wx) return false;
+  return d.M <= TM || d.x_split_pre != nullptr || tc_takes_split(d);
+}
+
 template <int NM, int EPI>
 static cudaError_t launch_t(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st) {
   // Row blocks of more than 64 rows take their input rows split once per
