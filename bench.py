@@ -389,13 +389,13 @@ class Waves:
     other, the lanes side by side on their sessions' streams (a projection of
     one wave leaves SMs idle that a kernel of another lane can use)."""
 
-    def __init__(self, Q, torch, model, utts, frames, full_prompt, lanes=1, wave=WAVE):
+    def __init__(self, Q, torch, model, utts, frames, full_prompt, lanes=1, wave=WAVE, kv_f16=False):
         self.torch = torch
         self.waves = [utts[i:i + wave] for i in range(0, len(utts), wave)]
         self.lanes = max(1, min(lanes, len(self.waves)))
         max_text = max(len(u["text"]) for u in utts)
         self.maxp = 10 + (max_text if full_prompt else 0) + frames + 1
-        self.sessions = [Q.Session(model, len(w), self.maxp) for w in self.waves]
+        self.sessions = [Q.Session(model, len(w), self.maxp, kv_f16=kv_f16) for w in self.waves]
         self.gens = [Q.Generation(s, w, frames, full_prompt=full_prompt) for s, w in zip(self.sessions, self.waves)]
         self.streams = [torch.cuda.ExternalStream(s.stream) for s in self.sessions]
         self.root = torch.cuda.current_stream()
@@ -435,7 +435,8 @@ def run_frames(args, rank, world, local, Q, W, torch, model, peak, peak_kind):
     utts, wl = workload_utts(args, rank, world, W)
     start = timed_window(args.workload, args.steps, args.warmup)
     F = start + args.steps + 1 + (1 if args.profile_step else 0)
-    wv = Waves(Q, torch, model, utts, F, args.full_prompt, lanes=args.lanes, wave=args.wave)
+    wv = Waves(Q, torch, model, utts, F, args.full_prompt, lanes=args.lanes, wave=args.wave,
+               kv_f16=args.kv == "f16")
     wv.steps(start)  # warm-up steps and the frames before the timed window (untimed)
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
@@ -558,9 +559,10 @@ def roofline_dec(ft, peak, peak_kind, ms_frame):
             "peak_kind": f"hbm_gbs ({peak_kind})"}
 
 
-def frame_roofline(B, ms_step, kv_mid, peak, peak_kind):
-    """(unique Q4 weight bytes + KV read) per frame step / step time."""
-    by = frame_weight_bytes() + B * kv_mid * KV_BYTES_PER_POS
+def frame_roofline(B, ms_step, kv_mid, peak, peak_kind, kv_elem=4):
+    """(unique Q4 weight bytes + KV read) per frame step / step time
+    (kv_elem: bytes per cached element, 4 for f32, 2 for the f16 mode)."""
+    by = frame_weight_bytes() + B * kv_mid * KV_BYTES_PER_POS * kv_elem / 4
     gbs = by / (ms_step / 1e3) / 1e9
     return {"bytes_per_step": by, "achieved_gbs": gbs, "peak_gbs": peak, "frac": gbs / peak, "peak_kind": peak_kind}
 
@@ -575,7 +577,8 @@ def run_batch1(args, rank, world, local, Q, W, torch, model, peak, peak_kind):
     r = run_frames(sub, rank, world, local, Q, W, torch, model, peak, peak_kind)
     return {"ms_per_frame": r["ms_per_step"], "frames_per_s_per_gpu": 1e3 / r["ms_per_step"],
             "frames_timed": sub.steps, "kv_len_mid": r["kv_mid"], "kernels_per_frame": r["kernels_per_frame"],
-            "frame_roofline": frame_roofline(1, r["ms_per_step"], r["kv_mid"], peak, peak_kind),
+            "frame_roofline": frame_roofline(1, r["ms_per_step"], r["kv_mid"], peak, peak_kind,
+                                             2 if args.kv == "f16" else 4),
             "roofline": roofline_dec(r["family"], peak, peak_kind, r["ms_per_step"]),
             "e2e_frames_per_s": r["e2e"]["value"] / world, "clocks": r["clocks"]}
 
@@ -597,6 +600,8 @@ def main():
     ap.add_argument("--profile-step", action="store_true",
                     help="after the timed steps, one more step inside cudaProfilerStart/Stop (for ncu "
                          "--profile-from-start off)")
+    ap.add_argument("--kv", default="f32", choices=["f32", "f16"],
+                    help="K/V cache elements: f32 (the reference's, default) or the opt-in f16 session mode")
     ap.add_argument("--full-prompt", action="store_true",
                     help="prefill the whole text (ragged KV lengths across utterances; config4/5)")
     args = ap.parse_args()
@@ -660,9 +665,12 @@ def main():
                          "tensor-core operand tiles at batch >= 16)",
                    "prompt": ("full prefill: KV lengths 9 + prompt tokens (ragged)" if args.full_prompt
                               else "generate_new: 10-row prefill, the text trailing into the frames"),
+                   "kv_cache": ("f16, opt-in (QTTS_SESSION_KV_F16; not the reference's precision)"
+                                if args.kv == "f16" else "f32, the reference's precision"),
                    "parallelism": f"{world} independent replicas, utterances sharded, no collective"},
         "ms_per_frame_batch1": (r["ms_per_step"] if not batched else (b1 or {}).get("ms_per_frame")),
-        "frame_roofline": frame_roofline(B, r["ms_per_step"] / r["waves"], r["kv_mid"], peak, peak_kind),
+        "frame_roofline": frame_roofline(B, r["ms_per_step"] / r["waves"], r["kv_mid"], peak, peak_kind,
+                                         2 if args.kv == "f16" else 4),
         "roofline": roof,
         "batch1": b1,
         "cpu_baseline": cpu,

@@ -101,6 +101,16 @@ QTTS_API size_t qtts_model_device_bytes(const qtts_model* m);
 /* ---- session: device KV caches + activations for up to max_batch utterances */
 /* gemv.rs:79-86 empty_kv_cache, as paged device KV (16 positions / page). */
 QTTS_API int qtts_session_create(qtts_model* m, int max_batch, int max_positions, qtts_session** out);
+/* Opt-in session modes (no counterpart in the reference, whose caches are
+ * f32 Vec<f32>, gemv.rs:77-86).  QTTS_SESSION_KV_F16: the talker and
+ * predictor K/V caches hold f16 (round to nearest even) instead of f32,
+ * halving their bytes and the attention's HBM traffic; every other value,
+ * the attention arithmetic included, stays f32.  Results then differ from
+ * the reference's by the cache rounding (logits within 1e-2 of the largest
+ * logit on the parity cases); qtts_session_create is _ex with flags 0. */
+#define QTTS_SESSION_KV_F16 1u
+QTTS_API int qtts_session_create_ex(qtts_model* m, int max_batch, int max_positions, unsigned flags,
+                                    qtts_session** out);
 QTTS_API int qtts_session_free(qtts_session* s);
 QTTS_API int qtts_session_reset(qtts_session* s);
 QTTS_API void* qtts_session_stream(qtts_session* s); /* cudaStream_t the session launches on */

@@ -22,17 +22,12 @@ namespace cg = cooperative_groups;
 
 namespace qtts {
 
-namespace {
-__device__ __forceinline__ const float* kv_row_c(const KvDesc& kv, int sess, int pos, int which, int h) {
-  const int page = kv.page_table ? kv.page_table[sess * kv.pages_per_sess + pos / kPageSize] : sess;
-  const size_t blk = (((size_t)page * kv.n_layers + kv.layer) * 2 + which) * kv.kv_heads + h;
-  return kv.pool + (blk * kPageSize + (pos % kPageSize)) * kHeadDim;
-}
-}  // namespace
-
-template <int G>
+// F16: the cache's element type (KvDesc::f16), fixed per instance so that the
+// position loop carries no type test.
+template <int G, bool F16>
 __global__ void __launch_bounds__(128) attn_kernel(const AttnDesc d) {
   pdl_launch_dependents();
+  const KvDesc& kv = d.kv;
   constexpr int NW = 4;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int m = blockIdx.x / d.kv_heads, h = blockIdx.x % d.kv_heads;
@@ -46,15 +41,15 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnDesc d) {
     const int sl = m / rp.rows_per_sess, r = m - sl * rp.rows_per_sess;
     const int ss = rp.sess0 + sl;
     const int ps = (rp.pos_base ? __ldcg(rp.pos_base + ss * rp.pos_stride) : rp.pos_const) + r;
-    const int kv = rp.kv_const >= 0 ? rp.kv_const + r : ps;
-    if (kv >= 0 && kv < d.kv.pages_per_sess * kPageSize) {
-      const int Lp = kv + 1, ch = (Lp + d.nsplit - 1) / d.nsplit;
+    const int kvi = rp.kv_const >= 0 ? rp.kv_const + r : ps;
+    if (kvi >= 0 && kvi < kv.pages_per_sess * kPageSize) {
+      const int Lp = kvi + 1, ch = (Lp + d.nsplit - 1) / d.nsplit;
       const int q0 = split * ch, q1 = min(Lp, q0 + ch);
       for (int pg = q0 / kPageSize; pg * kPageSize < q1; ++pg) {
         const int a = max(q0, pg * kPageSize), b = min(q1, (pg + 1) * kPageSize);
         for (int which = 0; which < 2; ++which)
-          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(kv_row_c(d.kv, ss, a, which, h)),
-                       "r"((uint32_t)((b - a) * kHeadDim * sizeof(float)))
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(kv_addr(kv, kv_at(kv, ss, a, which, h), F16)),
+                       "r"((uint32_t)((b - a) * kHeadDim * (F16 ? 2 : 4)))
                        : "memory");
       }
     }
@@ -94,8 +89,8 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnDesc d) {
     for (int u = 0; u < U; ++u) {
       const int p = pb + NW * u;
       if (p < p1) {
-        k4[u] = *reinterpret_cast<const float4*>(kv_row_c(d.kv, sess, p, 0, h) + 4 * lane);
-        v4[u] = *reinterpret_cast<const float4*>(kv_row_c(d.kv, sess, p, 1, h) + 4 * lane);
+        k4[u] = kv_load4(kv, kv_at(kv, sess, p, 0, h) + 4 * lane, F16);
+        v4[u] = kv_load4(kv, kv_at(kv, sess, p, 1, h) + 4 * lane, F16);
       } else {
         k4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
         v4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -217,18 +212,19 @@ cudaError_t launch_attention(const AttnDesc& d, cudaStream_t st) {
   o.pdl = true;
   o.cluster_y = (unsigned)d.nsplit;
   if (g_occ_query) g_occ_family = FAM_ATTN;
+  const bool f16 = d.kv.f16 != 0;
   switch (G) {
-    case 1: return launch_k(attn_kernel<1>, grid, dim3(128), 0, st, o, d);
-    case 2: return launch_k(attn_kernel<2>, grid, dim3(128), 0, st, o, d);
-    case 4: return launch_k(attn_kernel<4>, grid, dim3(128), 0, st, o, d);
+    case 1: return launch_k(f16 ? attn_kernel<1, true> : attn_kernel<1, false>, grid, dim3(128), 0, st, o, d);
+    case 2: return launch_k(f16 ? attn_kernel<2, true> : attn_kernel<2, false>, grid, dim3(128), 0, st, o, d);
+    case 4: return launch_k(f16 ? attn_kernel<4, true> : attn_kernel<4, false>, grid, dim3(128), 0, st, o, d);
     default: return cudaErrorInvalidValue;
   }
 }
 
 void attn_init_attributes() {
-  cudaFuncSetAttribute(attn_kernel<1>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  cudaFuncSetAttribute(attn_kernel<2>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  cudaFuncSetAttribute(attn_kernel<4>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  for (auto* k : {attn_kernel<1, false>, attn_kernel<2, false>, attn_kernel<4, false>, attn_kernel<1, true>,
+                  attn_kernel<2, true>, attn_kernel<4, true>})
+    cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   cudaGetLastError();
 }
 

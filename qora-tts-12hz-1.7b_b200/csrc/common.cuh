@@ -69,6 +69,30 @@ __device__ __forceinline__ void q4_word_fma(uint32_t w, const SxPack& s, float2*
 // and the 2^11 keeps lo clear of the fp16 subnormals (sm_100 f32x2 ops).
 constexpr float kSplitLoScale = 2048.0f;
 __device__ __forceinline__ uint32_t half2_bits(__half2 h) { return *reinterpret_cast<uint32_t*>(&h); }
+// ---- paged KV cache elements (KvDesc): f32, or f16 rounded to nearest even
+__device__ __forceinline__ int kv_page(const KvDesc& kv, int sess, int pos) {
+  return kv.page_table ? kv.page_table[sess * kv.pages_per_sess + pos / kPageSize] : sess;
+}
+// element index of (page, position, K = 0 / V = 1, kv head), dimension 0
+__device__ __forceinline__ size_t kv_elem(const KvDesc& kv, int page, int pos, int which, int h) {
+  const size_t blk = (((size_t)page * kv.n_layers + kv.layer) * 2 + which) * kv.kv_heads + h;
+  return (blk * kPageSize + (pos % kPageSize)) * kHeadDim;
+}
+__device__ __forceinline__ size_t kv_at(const KvDesc& kv, int sess, int pos, int which, int h) {
+  return kv_elem(kv, kv_page(kv, sess, pos), pos, which, h);
+}
+// (`f16` = kv.f16, or a constant in kernels specialised on the element type)
+__device__ __forceinline__ const void* kv_addr(const KvDesc& kv, size_t i, bool f16) {
+  return f16 ? static_cast<const void*>(reinterpret_cast<const __half*>(kv.pool) + i)
+             : static_cast<const void*>(kv.pool + i);
+}
+__device__ __forceinline__ void kv_store1(const KvDesc& kv, size_t i, float v) {
+  if (kv.f16) reinterpret_cast<__half*>(kv.pool)[i] = __float2half_rn(v);
+  else kv.pool[i] = v;
+}
+__device__ __forceinline__ float kv_load1(const KvDesc& kv, size_t i) {
+  return kv.f16 ? __half2float(reinterpret_cast<const __half*>(kv.pool)[i]) : kv.pool[i];
+}
 __device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
   const __half2 h = __floats2half2_rn(a, b);
   const float2 hf = __half22float2(h);
@@ -77,6 +101,25 @@ __device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint3
                               make_float2(kSplitLoScale, kSplitLoScale));
   lo = half2_bits(__floats2half2_rn(r.x, r.y));
 }
+// four consecutive elements (i % 4 == 0)
+__device__ __forceinline__ void kv_store4(const KvDesc& kv, size_t i, float4 v) {
+  if (kv.f16) {
+    *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(kv.pool) + i) =
+        make_uint2(half2_bits(__floats2half2_rn(v.x, v.y)), half2_bits(__floats2half2_rn(v.z, v.w)));
+  } else {
+    *reinterpret_cast<float4*>(kv.pool + i) = v;
+  }
+}
+__device__ __forceinline__ float4 kv_load4(const KvDesc& kv, size_t i, bool f16) {
+  if (f16) {
+    const uint2 u = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(kv.pool) + i);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+  }
+  return *reinterpret_cast<const float4*>(kv.pool + i);
+}
+__device__ __forceinline__ float4 kv_load4(const KvDesc& kv, size_t i) { return kv_load4(kv, i, kv.f16 != 0); }
 // Split tiles of a projection's input rows (K wide): block (row m / 128,
 // column c / 64) of 32 KB holds the hi half then the lo half, each K-major
 // core matrices of 8 rows x 16 bytes, row r and column j of the block at

@@ -530,7 +530,7 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
     // stays resident until read (small batches, long caches).  With many rows
     // the launch's cache (up to M * kv_heads * maxP positions, K and V of
     // 512 bytes each) exceeds L2 and prefetched lines evict each other first.
-    a.l2_prefetch = (double)io.M * io.kvh * s.maxP * 2.0 * kHeadDim * sizeof(float) <= kAttnPrefetchMaxBytes;
+    a.l2_prefetch = (double)io.M * io.kvh * s.maxP * 2.0 * kHeadDim * (s.kv_f16 ? 2 : 4) <= kAttnPrefetchMaxBytes;
     if (a.nsplit > 1) {
       const size_t need = (size_t)io.M * io.kvh * a.nsplit * (io.heads / io.kvh) * kAttnRec;
       if (need > s.apart_floats || (size_t)io.M * io.kvh > s.n_acounters)
@@ -593,13 +593,13 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
 static KvDesc talker_kv(Session& s, int layer) {
   KvDesc k;
   k.pool = s.kv_pool; k.page_table = s.page_table; k.pages_per_sess = s.pages_per_sess;
-  k.n_layers = s.m->d.t_layers; k.kv_heads = s.m->d.t_kv_heads; k.layer = layer;
+  k.n_layers = s.m->d.t_layers; k.kv_heads = s.m->d.t_kv_heads; k.layer = layer; k.f16 = s.kv_f16;
   return k;
 }
 static KvDesc pred_kv(Session& s, int layer) {
   KvDesc k;
   k.pool = s.pkv_pool; k.page_table = nullptr; k.pages_per_sess = 1;
-  k.n_layers = s.m->d.p_layers; k.kv_heads = s.m->d.p_kv_heads; k.layer = layer;
+  k.n_layers = s.m->d.p_layers; k.kv_heads = s.m->d.p_kv_heads; k.layer = layer; k.f16 = s.kv_f16;
   return k;
 }
 // Attention splits of the talker cache: 32 positions per split, about four
@@ -803,8 +803,9 @@ static void session_free_all(Session* s) {
   delete s;
 }
 
-static int session_create(Model* m, int maxB, int maxP, Session** out) {
+static int session_create(Model* m, int maxB, int maxP, unsigned flags, Session** out) {
   if (!m || maxB <= 0 || maxB > 4096 || maxP <= 0) return fail(QTTS_ERR_BADARG, "bad session arguments");
+  if (flags & ~(unsigned)QTTS_SESSION_KV_F16) return fail(QTTS_ERR_BADARG, "unknown session flags");
   if (maxP > m->d.t_max_pos) return fail(QTTS_ERR_RANGE, "max_positions exceeds the talker RoPE table");
   CK(cudaSetDevice(m->device));
   const qtts_dims& d = m->d;
@@ -813,6 +814,7 @@ static int session_create(Model* m, int maxB, int maxP, Session** out) {
   s->maxB = maxB;
   s->maxP = maxP;
   s->pages_per_sess = ceil_div(maxP, kPageSize);
+  s->kv_f16 = (flags & QTTS_SESSION_KV_F16) ? 1 : 0;
   int rc = QTTS_OK;
   auto A = [&](auto** p, size_t n) {
     if (rc == QTTS_OK) rc = dalloc(p, n);
@@ -820,9 +822,10 @@ static int session_create(Model* m, int maxB, int maxP, Session** out) {
   if (cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking) != cudaSuccess) rc = fail(QTTS_ERR_CUDA, "stream");
   const size_t tpage = (size_t)d.t_layers * 2 * d.t_kv_heads * kPageSize * kHeadDim;
   const size_t ppage = (size_t)d.p_layers * 2 * d.p_kv_heads * kPageSize * kHeadDim;
-  A(&s->kv_pool, tpage * maxB * s->pages_per_sess);
+  const size_t kv_div = s->kv_f16 ? 2 : 1;  // f16 elements: two per float of the allocation
+  A(&s->kv_pool, tpage * maxB * s->pages_per_sess / kv_div);
   A(&s->page_table, (size_t)maxB * s->pages_per_sess);
-  A(&s->pkv_pool, ppage * maxB);
+  A(&s->pkv_pool, ppage * maxB / kv_div);
   A(&s->slots, (size_t)maxB);
   s->rows = 10 * maxB;
   const int qmax = std::max(d.t_heads, d.p_heads) * kHeadDim;
@@ -1492,13 +1495,16 @@ int qtts_model_dims(const qtts_model* h, qtts_dims* out) {
 }
 size_t qtts_model_device_bytes(const qtts_model* h) { return h ? h->m->bytes + h->m->wx_bytes : 0; }
 
-int qtts_session_create(qtts_model* h, int max_batch, int max_positions, qtts_session** out) {
+int qtts_session_create_ex(qtts_model* h, int max_batch, int max_positions, unsigned flags, qtts_session** out) {
   if (!h || !out) return fail(QTTS_ERR_BADARG, "null argument");
   Session* s = nullptr;
-  const int rc = session_create(h->m, max_batch, max_positions, &s);
+  const int rc = session_create(h->m, max_batch, max_positions, flags, &s);
   if (rc != QTTS_OK) return rc;
   *out = new qtts_session{s};
   return QTTS_OK;
+}
+int qtts_session_create(qtts_model* h, int max_batch, int max_positions, qtts_session** out) {
+  return qtts_session_create_ex(h, max_batch, max_positions, 0u, out);
 }
 int qtts_session_free(qtts_session* h) {
   if (!h) return QTTS_OK;

@@ -51,6 +51,7 @@ struct Session {
   float* kv_pool = nullptr;   // talker [pages][layers][2][kvh][16][128]
   int* page_table = nullptr;  // [maxB][pages_per_sess]
   float* pkv_pool = nullptr;  // predictor, one page per slot
+  int kv_f16 = 0;             // both caches hold f16 elements (QTTS_SESSION_KV_F16)
   // per-slot state
   SlotState* slots = nullptr;
   // activations

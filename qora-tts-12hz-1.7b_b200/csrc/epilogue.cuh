@@ -97,12 +97,6 @@ __device__ __forceinline__ float block_sum_half(float v, float* sbuf) {
   return (sbuf[w0] + sbuf[w0 + 1]) + (sbuf[w0 + 2] + sbuf[w0 + 3]);
 }
 
-__device__ __forceinline__ float* kv_row(const KvDesc& kv, int sess, int pos, int which, int h) {
-  const int page = kv.page_table ? kv.page_table[sess * kv.pages_per_sess + pos / kPageSize] : sess;
-  const size_t blk = (((size_t)page * kv.n_layers + kv.layer) * 2 + which) * kv.kv_heads + h;
-  return kv.pool + (blk * kPageSize + (pos % kPageSize)) * kHeadDim;
-}
-
 // ---------------------------------------------------------------------------
 // QKV epilogue inputs of one thread (column tcol + tid of matrix mat, input
 // row m) gathered during the decode kernel's prologue, so the epilogue makes
@@ -138,7 +132,7 @@ __device__ __forceinline__ void qkv_pre_rest(QkvPre& q, const GemvDesc& d, int m
   q.pos = q.pos_raw + q.r;
   q.kvp = e.rp.kv_const >= 0 ? e.rp.kv_const + q.r : q.pos;
   if (col >= d.mat[mat].n) return;
-  if (mat != 0) q.page = e.kv.page_table ? e.kv.page_table[q.sess * e.kv.pages_per_sess + q.kvp / kPageSize] : q.sess;
+  if (mat != 0) q.page = kv_page(e.kv, q.sess, q.kvp);
   if (mat == 2) return;
   const int half = kHeadDim / 2, i = (col % kHeadDim) % half;
   q.rope_ok = q.pos < e.rope_rows && q.pos >= 0;
@@ -147,13 +141,13 @@ __device__ __forceinline__ void qkv_pre_rest(QkvPre& q, const GemvDesc& d, int m
     q.sn = e.rope_sin[(size_t)q.pos * half + i];
   }
 }
-// Destination of the column: q_out, or its K / V cache element (kv_row).
-__device__ __forceinline__ float* qkv_dst(const QkvPre& q, const EpiDesc& e, int mat, int col) {
-  if (mat == 0) return e.q_out + (size_t)q.m * e.ldq + col;
-  const KvDesc& kv = e.kv;
-  const int h = col / kHeadDim;
-  const size_t blk = (((size_t)q.page * kv.n_layers + kv.layer) * 2 + (mat == 2 ? 1 : 0)) * kv.kv_heads + h;
-  return kv.pool + (blk * kPageSize + (q.kvp % kPageSize)) * kHeadDim + col % kHeadDim;
+// Store of the column's value: to q_out, or to its K / V cache element.
+__device__ __forceinline__ void qkv_put(const QkvPre& q, const EpiDesc& e, int mat, int col, float v) {
+  if (mat == 0) {
+    e.q_out[(size_t)q.m * e.ldq + col] = v;
+    return;
+  }
+  kv_store1(e.kv, kv_elem(e.kv, q.page, q.kvp, mat == 2 ? 1 : 0, col / kHeadDim) + col % kHeadDim, v);
 }
 
 // ---------------------------------------------------------------------------
@@ -204,7 +198,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvDesc& d, const FrameCode
     const int h = col / kHeadDim, dd = col % kHeadDim, hl = tid / kHeadDim;
     if (MB == 1 && qp && qp->on) {  // one row, everything it needs preloaded
       if (mat == 2) {
-        if (cval) *qkv_dst(*qp, e, mat, col) = v[0][0];
+        if (cval) qkv_put(*qp, e, mat, col, v[0][0]);
         return;
       }
       const float x = cval ? v[0][0] : 0.0f;
@@ -229,7 +223,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvDesc& d, const FrameCode
         } else if (!e.rope_skip_oob && e.err_flag) {
           atomicOr(e.err_flag, kErrRopeRange);
         }
-        *qkv_dst(*qp, e, mat, col) = outv;
+        qkv_put(*qp, e, mat, col, outv);
       }
       return;
     }
@@ -240,10 +234,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvDesc& d, const FrameCode
       int sess = 0, pos = 0, kvp = 0;
       if (live) row_pos(e.rp, m, sess, pos, kvp);
       if (mat == 2) {
-        if (live && cval) {
-          KvDesc kv = e.kv;
-          kv_row(kv, sess, kvp, 1, h)[dd] = v[0][mm];
-        }
+        if (live && cval) kv_store1(e.kv, kv_at(e.kv, sess, kvp, 1, h) + dd, v[0][mm]);
         continue;
       }
       // QK-norm (talker.rs:89-99): per head of 128 = 4 warps
@@ -276,8 +267,7 @@ __device__ __forceinline__ void gemv_epilogue(const GemvDesc& d, const FrameCode
         if (mat == 0) {
           e.q_out[(size_t)m * e.ldq + col] = outv;
         } else {
-          KvDesc kv = e.kv;
-          kv_row(kv, sess, kvp, 0, h)[dd] = outv;
+          kv_store1(e.kv, kv_at(e.kv, sess, kvp, 0, h) + dd, outv);
         }
       }
     }

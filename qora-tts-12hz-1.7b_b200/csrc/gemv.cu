@@ -253,12 +253,12 @@ __global__ void __launch_bounds__(kGemvThreads) q4mv_dec_kernel(const GemvDesc d
 #pragma unroll
     for (int t = 0; t < kPw; ++t) {
       const int j = warp + t * (kGemvThreads / 32);
-      kk[t] = j < L ? *reinterpret_cast<const float4*>(kv_row(d.attn_kv, sess, j, 0, hk) + 4 * lane)
-                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      kk[t] = j < L ? kv_load4(d.attn_kv, kv_at(d.attn_kv, sess, j, 0, hk) + 4 * lane) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     float vc[kAttnInMaxPos];  // V column tid of every position (threads < 128)
 #pragma unroll
-    for (int j = 0; j < kAttnInMaxPos; ++j) vc[j] = (j < L && tid < kHeadDim) ? kv_row(d.attn_kv, sess, j, 1, hk)[tid] : 0.0f;
+    for (int j = 0; j < kAttnInMaxPos; ++j)
+      vc[j] = (j < L && tid < kHeadDim) ? kv_load1(d.attn_kv, kv_at(d.attn_kv, sess, j, 1, hk) + tid) : 0.0f;
     if (clustered) cluster_wait();
     if (EPI == EPI_QKV && qp.on) qkv_pre_rest(qp, d, mat, tcol + tid);
     const float scale = 1.0f / sqrtf((float)kHeadDim);

@@ -26,16 +26,18 @@ struct Q4Mat {
 };
 
 // Paged KV addressing.  A page holds kPageSize positions of every layer:
-//   pool[page][layer][K|V][kv_head][pos % 16][128]  (f32)
+//   pool[page][layer][K|V][kv_head][pos % 16][128]  (f32, the reference's
+//   precision; f16 elements when `f16` is set, an opt-in session mode)
 // page = page_table[sess * pages_per_sess + pos / 16] (or = sess when
 // page_table is null: one page per session, the predictor cache).
 struct KvDesc {
-  float* pool = nullptr;
+  float* pool = nullptr;  // element i at pool + i, or at (__half*)pool + i (f16)
   const int* page_table = nullptr;
   int pages_per_sess = 0;
   int n_layers = 0;
   int kv_heads = 0;
   int layer = 0;
+  int f16 = 0;
 };
 
 // Row -> (session, position) mapping shared by the QKV epilogue and the

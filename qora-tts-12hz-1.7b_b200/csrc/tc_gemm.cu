@@ -762,9 +762,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
     int p_sess = 0, p_pos = 0, p_kvp = 0, p_page = 0;
     if (lane < nrw) {
       row_pos(e.rp, m0 + rb + warp + 16 * lane, p_sess, p_pos, p_kvp);
-      p_page = (mat == 2 || mat == 1) ? (e.kv.page_table ? e.kv.page_table[p_sess * e.kv.pages_per_sess + p_kvp / kPageSize]
-                                                         : p_sess)
-                                      : 0;
+      p_page = (mat == 2 || mat == 1) ? kv_page(e.kv, p_sess, p_kvp) : 0;
     }
     float gv[4] = {0.f, 0.f, 0.f, 0.f};
     if (mat != 2) {
@@ -787,13 +785,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
       const float4 c4 = cn, s4 = sn4;
       if (jr + 1 < nrw) rope_ld(__shfl_sync(0xffffffffu, p_pos, jr + 1), cn, sn4);
       const float4 acc0 = *reinterpret_cast<const float4*>(red + (size_t)r * kRedLd + cc);
-      // the row's 16 KB block of the paged cache (kv_row with the page known)
-      auto kvp_row = [&](int which) {
-        const size_t blk = (((size_t)page * e.kv.n_layers + e.kv.layer) * 2 + which) * e.kv.kv_heads + h;
-        return e.kv.pool + (blk * kPageSize + (kvp % kPageSize)) * kHeadDim;
-      };
       if (mat == 2) {
-        *reinterpret_cast<float4*>(kvp_row(1) + cc) = acc0;
+        kv_store4(e.kv, kv_elem(e.kv, page, kvp, 1, h) + cc, acc0);
         continue;
       }
       const float vv[4] = {acc0.x, acc0.y, acc0.z, acc0.w};
@@ -815,8 +808,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_proj_kernel(const GemvDesc d, 
         if (in_range) o[j] = (dd < half) ? (x1 * cf[j] - x2 * sf[j]) : (x2 * cf[j] + x1 * sf[j]);
       }
       if (!in_range && !e.rope_skip_oob && e.err_flag && lane == 0) atomicOr(e.err_flag, kErrRopeRange);
-      float* dst = (mat == 0) ? e.q_out + (size_t)m * e.ldq + col : kvp_row(0) + cc;
-      *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+      if (mat == 0)
+        *reinterpret_cast<float4*>(e.q_out + (size_t)m * e.ldq + col) = make_float4(o[0], o[1], o[2], o[3]);
+      else
+        kv_store4(e.kv, kv_elem(e.kv, page, kvp, 0, h) + cc, make_float4(o[0], o[1], o[2], o[3]));
     }
   }
   for (int r = rb + warp; EPI != EPI_QKV && good && r < re; r += kThreads / 32) {

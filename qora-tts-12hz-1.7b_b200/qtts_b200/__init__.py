@@ -24,6 +24,7 @@ ERR_BADARG, ERR_OOM, ERR_CUDA, ERR_TIMEOUT, ERR_FORMAT, ERR_IO, ERR_STATE, ERR_N
     -1, -2, -3, -4, -5, -6, -7, -8, -9)
 IGNORE_EOS = 1
 FULL_PROMPT = 2  # benchmark mode: the whole text prefilled (qtts.h QTTS_FULL_PROMPT)
+SESSION_KV_F16 = 1  # opt-in f16 K/V caches (qtts.h QTTS_SESSION_KV_F16)
 # kernel families of the frame plan (qtts.h QTTS_FAMILY_*)
 FAMILY_Q4MV_DEC, FAMILY_Q4MV_ROWS, FAMILY_TC_PROJ, FAMILY_ATTN, FAMILY_Q4MV_BATCH = 1, 2, 3, 4, 5
 
@@ -78,6 +79,7 @@ def _load():
         "qtts_model_dims": (C.c_int, [P, C.POINTER(Dims)]),
         "qtts_model_device_bytes": (C.c_size_t, [P]),
         "qtts_session_create": (C.c_int, [P, C.c_int, C.c_int, C.POINTER(P)]),
+        "qtts_session_create_ex": (C.c_int, [P, C.c_int, C.c_int, C.c_uint, C.POINTER(P)]),
         "qtts_session_free": (C.c_int, [P]),
         "qtts_session_reset": (C.c_int, [P]),
         "qtts_session_stream": (P, [P]),
@@ -182,9 +184,12 @@ class Session:
     """The device KV caches of gemv.rs:77-86 (RawKvCache) for up to
     max_batch utterances of up to max_positions positions each."""
 
-    def __init__(self, model: Model, max_batch: int = 1, max_positions: int = 2048):
+    def __init__(self, model: Model, max_batch: int = 1, max_positions: int = 2048, kv_f16: bool = False):
+        """kv_f16: the opt-in f16 K/V caches (qtts.h QTTS_SESSION_KV_F16);
+        the default is the reference's f32."""
         h = C.c_void_p()
-        _check(lib.qtts_session_create(model.h, max_batch, max_positions, C.byref(h)))
+        flags = SESSION_KV_F16 if kv_f16 else 0
+        _check(lib.qtts_session_create_ex(model.h, max_batch, max_positions, flags, C.byref(h)))
         self.h = h
         self.model = model
         self.dims = model.dims

@@ -479,6 +479,28 @@ def test_1p7b_config4_64_utterances_teacher_forced(qtts, gpu_1p7b):
     print("near-ties tolerated:", ties)
 
 
+@pytest.mark.slow
+def test_1p7b_config4_utterances_in_256_row_wave(qtts, gpu_1p7b):
+    # config 4's 64 utterances four times over in one 256-utterance batch
+    # (config 5's wave): every projection has two 128-row blocks, takes its
+    # input rows split (by the split kernel or by their producer) and streams
+    # the expanded weight tiles; each copy must follow its utterance's
+    # oracle run
+    from qtts_b200 import workload as W
+    g = _golden_or_skip("p1p7b_config4_64")
+    utts, _ = W.config4(64, 2048)
+    F = g["codes"].shape[1]
+    s = qtts.Session(gpu_1p7b, 256, 10 + F + 1)
+    codes, frames, lg, _ = qtts.generate(s, utts * 4, F, forced=np.tile(g["codes"], (4, 1, 1)), dump_logits=True)
+    s.close()
+    ties = 0
+    for i in range(256):
+        assert frames[i] == F
+        gi = {k: (g[k][i % 64] if np.ndim(g[k]) > 0 else g[k]) for k in g}
+        ties += _check_forced(codes[i], gi, lg[i], max_ties=1)
+    print("near-ties tolerated:", ties)
+
+
 def test_wait_budget_timeout_reported_then_fresh_session_works(qtts, gpu_tiny):
     # A 1 ns budget makes the one-row GEMV's split-K cluster wait run out:
     # the root CTA records it, keeps waiting (bounded) for its peers'
