@@ -62,89 +62,204 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnDesc d) {
   const int p0 = split * chunk, p1 = min(L, p0 + chunk);
   const float scale = 1.0f / sqrtf((float)kHeadDim);  // talker.rs:305
 
-  float4 q[G];
+  // per (virtual) warp softmax state for the combine
+  constexpr int NVW = F16 ? 2 * NW : NW;
+  __shared__ float s_m[NVW][G], s_l[NVW][G];
+  __shared__ float4 s_acc[NVW][G][32];
+  if constexpr (F16) {
+    // f16 caches: a half-warp per position (lane j = lane % 16 holds
+    // dimensions 8j..8j+7, one 16-byte load per row), so a warp keeps as many
+    // bytes in flight per load as the f32 loop; the two halves are separate
+    // online-softmax streams (virtual warps vw = 2 warp + half) over
+    // positions pw + half + 8u, pw = p0 + 2 warp + 32 t.
+    const int hh = lane >> 4, j = lane & 15, vw = 2 * warp + hh;
+    float4 qa[G], qb[G];
 #pragma unroll
-  for (int g = 0; g < G; ++g)
-    q[g] = *reinterpret_cast<const float4*>(d.q + (size_t)m * d.ldq + (h * G + g) * kHeadDim + 4 * lane);
-  float mx[G], l[G];
-  float4 acc[G];
+    for (int g = 0; g < G; ++g) {
+      const float* qr = d.q + (size_t)m * d.ldq + (h * G + g) * kHeadDim + 8 * j;
+      qa[g] = *reinterpret_cast<const float4*>(qr);
+      qb[g] = *reinterpret_cast<const float4*>(qr + 4);
+    }
+    float mx[G], l[G];
+    float4 aa[G], ab[G];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    mx[g] = -INFINITY;
-    l[g] = 0.0f;
-    acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-
-  // Each warp takes U positions per step (pb, pb + NW, ...).  The U partial
-  // dot products of a lane are reduced together: two transposing butterfly
-  // rounds leave lane group j = lane / 8 with position j's sum over 16 and
-  // then 8 lanes, three more rounds finish it (6 shuffles for 4 dots instead
-  // of 20), and lane 8 j broadcasts it.  The online softmax then updates once
-  // per step: one rescale for the block's max, one exp per position.
-  constexpr int U = 4;
-  const bool hi16 = (lane & 16) != 0, hi8 = (lane & 8) != 0;
-  for (int pb = p0 + warp; pb < p1; pb += NW * U) {
-    float4 k4[U], v4[U];
+    for (int g = 0; g < G; ++g) {
+      mx[g] = -INFINITY;
+      l[g] = 0.0f;
+      aa[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+      ab[g] = aa[g];
+    }
+    constexpr int U = 4;
+    const bool b3 = (lane & 8) != 0, b2 = (lane & 4) != 0;
+    auto h8 = [](const uint4& w, float (&f)[8]) {
+      const uint32_t v[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int p = pb + NW * u;
-      if (p < p1) {
-        k4[u] = kv_load4(kv, kv_at(kv, sess, p, 0, h) + 4 * lane, F16);
-        v4[u] = kv_load4(kv, kv_at(kv, sess, p, 1, h) + 4 * lane, F16);
-      } else {
-        k4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-        v4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int t = 0; t < 4; ++t) {
+        const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&v[t]));
+        f[2 * t] = x.x;
+        f[2 * t + 1] = x.y;
+      }
+    };
+    for (int pw = p0 + 2 * warp; pw < p1; pw += 2 * NW * U) {
+      uint4 k8[U], v8[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int p = pw + hh + 2 * NW * u;
+        if (p < p1) {
+          k8[u] = *reinterpret_cast<const uint4*>(kv_addr(kv, kv_at(kv, sess, p, 0, h) + 8 * j, true));
+          v8[u] = *reinterpret_cast<const uint4*>(kv_addr(kv, kv_at(kv, sess, p, 1, h) + 8 * j, true));
+        } else {
+          k8[u] = make_uint4(0u, 0u, 0u, 0u);
+          v8[u] = k8[u];
+        }
+      }
+      // every k row converted once for all G heads, every v row once for all
+      float dp[G][U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float kf[8];
+        h8(k8[u], kf);
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+          dp[g][u] = ((qa[g].x * kf[0] + qa[g].y * kf[1]) + (qa[g].z * kf[2] + qa[g].w * kf[3])) +
+                     ((qb[g].x * kf[4] + qb[g].y * kf[5]) + (qb[g].z * kf[6] + qb[g].w * kf[7]));
+      }
+      float pe[G][U];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        // 16-lane sums of the 4 dots, transposed: after xor 8 and xor 4 the
+        // lane bits (3, 2) name the position u kept, xor 2 and xor 1 finish it
+        float a0 = b3 ? dp[g][2] : dp[g][0], a1 = b3 ? dp[g][3] : dp[g][1];
+        a0 += __shfl_xor_sync(0xffffffffu, b3 ? dp[g][0] : dp[g][2], 8);
+        a1 += __shfl_xor_sync(0xffffffffu, b3 ? dp[g][1] : dp[g][3], 8);
+        float c = b2 ? a1 : a0;
+        c += __shfl_xor_sync(0xffffffffu, b2 ? a0 : a1, 4);
+        c += __shfl_xor_sync(0xffffffffu, c, 2);
+        c += __shfl_xor_sync(0xffffffffu, c, 1);
+        float mn = mx[g];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {  // position u of this half sits at lane 16 hh + 4u
+          pe[g][u] = __shfl_sync(0xffffffffu, c, (lane & 16) + 4 * u) * scale;
+          if (pw + hh + 2 * NW * u >= p1) pe[g][u] = -INFINITY;
+          mn = fmaxf(mn, pe[g][u]);
+        }
+        // a half whose positions all lie past p1 keeps mn = -inf: no update
+        const float corr = mn == -INFINITY ? 1.0f : expf(mx[g] - mn);
+        float lsum = l[g] * corr;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          pe[g][u] = mn == -INFINITY ? 0.0f : expf(pe[g][u] - mn);  // 0 past p1
+          lsum += pe[g][u];
+        }
+        l[g] = lsum;
+        mx[g] = mn;
+        aa[g] = make_float4(aa[g].x * corr, aa[g].y * corr, aa[g].z * corr, aa[g].w * corr);
+        ab[g] = make_float4(ab[g].x * corr, ab[g].y * corr, ab[g].z * corr, ab[g].w * corr);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float vf[8];
+        h8(v8[u], vf);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float e = pe[g][u];
+          aa[g].x += e * vf[0]; aa[g].y += e * vf[1]; aa[g].z += e * vf[2]; aa[g].w += e * vf[3];
+          ab[g].x += e * vf[4]; ab[g].y += e * vf[5]; ab[g].z += e * vf[6]; ab[g].w += e * vf[7];
+        }
       }
     }
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      float dp[U];
-#pragma unroll
-      for (int u = 0; u < U; ++u) dp[u] = q[g].x * k4[u].x + q[g].y * k4[u].y + q[g].z * k4[u].z + q[g].w * k4[u].w;
-      // step 1 (xor 16): lanes < 16 keep positions 0, 1; lanes >= 16 keep 2, 3
-      float a0 = hi16 ? dp[2] : dp[0], a1 = hi16 ? dp[3] : dp[1];
-      const float b0 = hi16 ? dp[0] : dp[2], b1 = hi16 ? dp[1] : dp[3];
-      a0 += __shfl_xor_sync(0xffffffffu, b0, 16);
-      a1 += __shfl_xor_sync(0xffffffffu, b1, 16);
-      // step 2 (xor 8): lane group j = lane / 8 keeps position j
-      float c = hi8 ? a1 : a0;
-      c += __shfl_xor_sync(0xffffffffu, hi8 ? a0 : a1, 8);
-      c += __shfl_xor_sync(0xffffffffu, c, 4);
-      c += __shfl_xor_sync(0xffffffffu, c, 2);
-      c += __shfl_xor_sync(0xffffffffu, c, 1);
-      float sc[U];
-      float mn = mx[g];
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        sc[u] = __shfl_sync(0xffffffffu, c, 8 * u) * scale;
-        if (pb + NW * u >= p1) sc[u] = -INFINITY;
-        mn = fmaxf(mn, sc[u]);
+      if (j == 0) {
+        s_m[vw][g] = mx[g];
+        s_l[vw][g] = l[g];
       }
-      const float corr = expf(mx[g] - mn);
-      float lsum = l[g] * corr;
-      float4 a4 = make_float4(acc[g].x * corr, acc[g].y * corr, acc[g].z * corr, acc[g].w * corr);
-#pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const float pe = expf(sc[u] - mn);  // 0 for the positions past p1
-        lsum += pe;
-        a4.x += pe * v4[u].x; a4.y += pe * v4[u].y; a4.z += pe * v4[u].z; a4.w += pe * v4[u].w;
-      }
-      l[g] = lsum;
-      acc[g] = a4;
-      mx[g] = mn;
+      s_acc[vw][g][2 * j] = aa[g];
+      s_acc[vw][g][2 * j + 1] = ab[g];
     }
-  }
+  } else {
+    float4 q[G];
+  #pragma unroll
+    for (int g = 0; g < G; ++g)
+      q[g] = *reinterpret_cast<const float4*>(d.q + (size_t)m * d.ldq + (h * G + g) * kHeadDim + 4 * lane);
+    float mx[G], l[G];
+    float4 acc[G];
+  #pragma unroll
+    for (int g = 0; g < G; ++g) {
+      mx[g] = -INFINITY;
+      l[g] = 0.0f;
+      acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
 
-  // combine the 4 warps
-  __shared__ float s_m[NW][G], s_l[NW][G];
-  __shared__ float4 s_acc[NW][G][32];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    if (lane == 0) {
-      s_m[warp][g] = mx[g];
-      s_l[warp][g] = l[g];
+    // Each warp takes U positions per step (pb, pb + NW, ...).  The U partial
+    // dot products of a lane are reduced together: two transposing butterfly
+    // rounds leave lane group j = lane / 8 with position j's sum over 16 and
+    // then 8 lanes, three more rounds finish it (6 shuffles for 4 dots instead
+    // of 20), and lane 8 j broadcasts it.  The online softmax then updates once
+    // per step: one rescale for the block's max, one exp per position.
+    constexpr int U = 4;
+    const bool hi16 = (lane & 16) != 0, hi8 = (lane & 8) != 0;
+    for (int pb = p0 + warp; pb < p1; pb += NW * U) {
+      float4 k4[U], v4[U];
+  #pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int p = pb + NW * u;
+        if (p < p1) {
+          k4[u] = kv_load4(kv, kv_at(kv, sess, p, 0, h) + 4 * lane, F16);
+          v4[u] = kv_load4(kv, kv_at(kv, sess, p, 1, h) + 4 * lane, F16);
+        } else {
+          k4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+          v4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+  #pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float dp[U];
+  #pragma unroll
+        for (int u = 0; u < U; ++u) dp[u] = q[g].x * k4[u].x + q[g].y * k4[u].y + q[g].z * k4[u].z + q[g].w * k4[u].w;
+        // step 1 (xor 16): lanes < 16 keep positions 0, 1; lanes >= 16 keep 2, 3
+        float a0 = hi16 ? dp[2] : dp[0], a1 = hi16 ? dp[3] : dp[1];
+        const float b0 = hi16 ? dp[0] : dp[2], b1 = hi16 ? dp[1] : dp[3];
+        a0 += __shfl_xor_sync(0xffffffffu, b0, 16);
+        a1 += __shfl_xor_sync(0xffffffffu, b1, 16);
+        // step 2 (xor 8): lane group j = lane / 8 keeps position j
+        float c = hi8 ? a1 : a0;
+        c += __shfl_xor_sync(0xffffffffu, hi8 ? a0 : a1, 8);
+        c += __shfl_xor_sync(0xffffffffu, c, 4);
+        c += __shfl_xor_sync(0xffffffffu, c, 2);
+        c += __shfl_xor_sync(0xffffffffu, c, 1);
+        float sc[U];
+        float mn = mx[g];
+  #pragma unroll
+        for (int u = 0; u < U; ++u) {
+          sc[u] = __shfl_sync(0xffffffffu, c, 8 * u) * scale;
+          if (pb + NW * u >= p1) sc[u] = -INFINITY;
+          mn = fmaxf(mn, sc[u]);
+        }
+        const float corr = expf(mx[g] - mn);
+        float lsum = l[g] * corr;
+        float4 a4 = make_float4(acc[g].x * corr, acc[g].y * corr, acc[g].z * corr, acc[g].w * corr);
+  #pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const float pe = expf(sc[u] - mn);  // 0 for the positions past p1
+          lsum += pe;
+          a4.x += pe * v4[u].x; a4.y += pe * v4[u].y; a4.z += pe * v4[u].z; a4.w += pe * v4[u].w;
+        }
+        l[g] = lsum;
+        acc[g] = a4;
+        mx[g] = mn;
+      }
     }
-    s_acc[warp][g][lane] = acc[g];
+
+    // combine the 4 warps
+  #pragma unroll
+    for (int g = 0; g < G; ++g) {
+      if (lane == 0) {
+        s_m[warp][g] = mx[g];
+        s_l[warp][g] = l[g];
+      }
+      s_acc[warp][g][lane] = acc[g];
+    }
   }
   __syncthreads();
   // thread t < G*32 finalises (g = t/32, dims 4*(t%32)..)
@@ -155,10 +270,10 @@ __global__ void __launch_bounds__(128) attn_kernel(const AttnDesc d) {
   if (tid < G * 32) {
     const int g = tid / 32, ln = tid % 32;
     float M = -INFINITY;
-    for (int w = 0; w < NW; ++w) M = fmaxf(M, s_m[w][g]);
+    for (int w = 0; w < NVW; ++w) M = fmaxf(M, s_m[w][g]);
     float lt = 0.0f;
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int w = 0; w < NW; ++w) {
+    for (int w = 0; w < NVW; ++w) {
       const float f = (s_l[w][g] > 0.0f) ? expf(s_m[w][g] - M) : 0.0f;
       lt += s_l[w][g] * f;
       const float4 x = s_acc[w][g][ln];
