@@ -52,16 +52,17 @@ WAVE = 64  # utterances of one session (config 4: 64 concurrent utterances per G
 WAVE5, LANES5 = 256, 2
 # frames per utterance of each workload (the timed window sits at the middle)
 UTT_FRAMES = {"config1": 100, "config3": 2000, "config4": 500, "config5": 500}
-# DRAM bytes per algorithmic byte of tc_proj_kernel at 256 rows: ncu's
-# dram__bytes_read.sum + dram__bytes_write.sum of one launch of the gate
-# shape 2048 x 6144 x 256 (9.26 MB) over its Q4 weight and input-row bytes
-# (9.18 MB), from
-#   python bench.py --workload config2 --only 2048x6144x256
-# under `ncu --set full -k regex:tc_proj -s 10 -c 1`.  The frame's launches
-# are too large to capture with more than one pass; their traffic is this
-# ratio times their algorithmic weight bytes (their split input rows were just
-# written by the kernel before them and come from L2).
-TC_TRAFFIC_RATIO = 9.26 / 9.18
+# DRAM bytes per Q4 weight byte of the tensor-core family in a config-5
+# frame step: ncu's dram__bytes_read.sum + dram__bytes_write.sum over every
+# tc_proj_kernel and tc_xsplit_kernel launch of one step (two 256-utterance
+# waves: 24.27 GB, one pass per launch) over the family's Q4 weight bytes
+# (1.495 GB per wave), from
+#   python bench.py --no-batch1 --no-cpu-baseline --steps 3 --warmup 3 --profile-step
+# under `ncu --profile-from-start off --metrics dram__bytes_read.sum,
+# dram__bytes_write.sum,gpu__time_duration.sum`.  The projections stream the
+# expanded fp16 hi/lo operand tiles (4 bytes a weight against 0.5625 for Q4),
+# read once per step (the second row block's reads hit L2).
+TC_TRAFFIC_RATIO = 24.27 / 2 / 1.495
 
 
 def q4_bytes(k, n):
@@ -524,8 +525,9 @@ def roofline_tc(ft, peaks, ms_step, waves, B):
     return {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s",
             "frac": ach / peak if ach else None,
             "traffic": TC_TRAFFIC_RATIO * ft["weight_bytes"] / max(ft["launches"], 1),
-            "traffic_note": "per launch: the measured DRAM/algorithmic ratio of one 256-row launch (ncu, small "
-                            "case) x the family's mean Q4 weight bytes per launch",
+            "traffic_note": "per launch: the family's measured DRAM bytes per Q4 weight byte (ncu, one config-5 "
+                            "step, every launch) x its mean Q4 weight bytes per launch; the launches stream the "
+                            "expanded operand tiles (4 B per weight), hence ~8x the Q4 bytes",
             "kernel": f"tc_proj_kernel: every tcgen05 projection of one frame step ({B} rows), "
                       f"{ft['launches']} launches replayed alone in frame order",
             "us_per_launch": ft["ms"] * 1e3 / max(ft["launches"], 1), "ms_per_frame_step": ft["ms"],
@@ -537,10 +539,11 @@ def roofline_tc(ft, peaks, ms_step, waves, B):
             "algorithmic_flops_per_launch": ft["flops"] / max(ft["launches"], 1),
             "q4_weight_gbs": ft["weight_bytes"] / sec / 1e9 if sec > 0 else None,
             "peak_kind": "bf16_tflops_sustained (measured)" if "bf16_tflops_sustained" in peaks else "fallback",
-            "note": "tensor pipe executes 3 fp16 MMAs per product (hi/lo split for f32 accuracy); above 64 rows "
-                    "the Q4 weights are dequantised in the kernel and the input rows arrive split (the family's "
-                    "time includes the split kernels of the normed inputs); at <= 64 rows the expanded fp16 "
-                    "hi/lo operand tiles (4 B per weight) are copied instead"}
+            "note": "tensor pipe executes 3 fp16 MMAs per product (hi/lo split for f32 accuracy); the weights "
+                    "arrive as expanded fp16 hi/lo operand tiles (4 B per weight) by bulk copy, and above 64 rows "
+                    "the input rows arrive split by the kernel before (the family's time includes those split "
+                    "kernels); the embedding-gather and codec-head launches above 128 rows dequantise Q4 in the "
+                    "kernel"}
 
 
 def roofline_dec(ft, peak, peak_kind, ms_frame):
