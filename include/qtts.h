@@ -37,6 +37,7 @@ extern "C" {
 
 typedef struct qtts_model qtts_model;
 typedef struct qtts_session qtts_session;
+typedef struct qtts_decoder qtts_decoder;
 
 /* Model dimensions as stored in the .qora-tts headers (save.rs:49-59,92-97). */
 typedef struct {
@@ -88,6 +89,13 @@ QTTS_API int qtts_file_probe(const char* path, qtts_dims* out);
  * f16(|N(0,0.02)|), norms 1, biases N(0,0.02), RoPE tables per rope.rs:11-41
  * and loader.rs:399-408.  Replaces offline compress_model.rs:35-82. */
 QTTS_API int qtts_synth_write(const char* path, const qtts_dims* dims, uint64_t seed);
+/* flags: QTTS_SYNTH_DECODER writes a full-size synthetic speech decoder
+ * section (decoder.rs:21-108 shapes: 16 codebooks of 2048 x 256, pre-conv,
+ * 8 transformer layers of hidden 512 / 16 heads of 64 / MLP 1024 / window
+ * 72, RoPE tables; the upsample and Vocos stages written empty) instead of
+ * an empty one.  The talker and predictor bytes are the same as without. */
+#define QTTS_SYNTH_DECODER 1u
+QTTS_API int qtts_synth_write_ex(const char* path, const qtts_dims* dims, uint64_t seed, unsigned flags);
 QTTS_API void qtts_dims_1p7b(qtts_dims* out);
 QTTS_API void qtts_dims_tiny(qtts_dims* out);
 
@@ -165,6 +173,27 @@ QTTS_API int qtts_frame_kernel_count(qtts_session* s);
  * last one while the batch size, max_frames, trailing-text rows, forcing and
  * dump options are unchanged (the per-generation buffers are grow-only). */
 QTTS_API int qtts_frame_graph_captures(qtts_session* s);
+
+/* ---- speech decoder, first stage (codes -> transformer output) ------------
+ * The reference runs decode_to_audio (decoder.rs:394-513) on the CPU; its
+ * first three steps -- codebook_lookup (decoder.rs:142-187), the causal
+ * pre-conv (conv.rs:114-191) and decoder_transformer (decoder.rs:195-335) --
+ * run here on the GPU over all frames of an utterance at once.  The
+ * upsample / Vocos stages that follow stay with the caller. */
+/* save.rs:446-552 load_decoder_weights (the decoder section of a .qora-tts
+ * file), uploaded to `device`; QTTS_ERR_FORMAT if the section is empty. */
+QTTS_API int qtts_decoder_load(const char* path, int device, qtts_decoder** out);
+QTTS_API int qtts_decoder_free(qtts_decoder* d);
+QTTS_API void* qtts_decoder_stream(qtts_decoder* d); /* cudaStream_t of the decoder */
+/* codes [16][n_frames] host (codes[g][t], the reference's &[Vec<u32>]);
+ * out [1024][n_frames] host, channel-first like decoder_transformer's
+ * result.  QTTS_ERR_RANGE for a code past its codebook (the reference
+ * panics on that index). */
+QTTS_API int qtts_decode_latent(qtts_decoder* d, const uint32_t* codes, int n_frames, float* out);
+/* The same on device buffers, asynchronous on the decoder's stream; a bad
+ * code is reported by the next qtts_decoder_sync. */
+QTTS_API int qtts_decode_latent_dev(qtts_decoder* d, const uint32_t* codes, int n_frames, float* out);
+QTTS_API int qtts_decoder_sync(qtts_decoder* d);
 
 /* ---- profiling (no counterpart in the reference) -------------------------- */
 /* Kernel families of the frame plan. */

@@ -98,6 +98,10 @@ def lib():
             "oq_generate": (C.c_int, [P, u32p, C.c_int, C.c_uint32, C.c_uint32, fp, C.POINTER(Params),
                                       C.c_uint64, C.c_int, u32p, u32p, fp, fp]),
             "oq_time_frames": (C.c_double, [P, C.c_int, C.c_int, C.c_uint64]),
+            "oq_synth_write_ex": (C.c_int, [C.c_char_p, C.POINTER(Dims), C.c_uint64, C.c_uint]),
+            "oq_decoder_load": (P, [C.c_char_p, C.c_char_p, C.c_int]),
+            "oq_decoder_free": (None, [P]),
+            "oq_decode_latent": (C.c_int, [P, u32p, C.c_int, fp]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -131,6 +135,47 @@ def synth_write(path: str, dims: Dims, seed: int = 0) -> None:
     rc = lib().oq_synth_write(path.encode(), C.byref(dims), seed)
     if rc != 0:
         raise IOError(f"oracle synth_write failed for {path}")
+
+
+SYNTH_DECODER = 1
+
+
+def synth_write_with_decoder(path: str, dims: Dims, seed: int = 0) -> None:
+    """The synthetic model with a full-size speech decoder section
+    (codebooks, pre-conv, transformer, RoPE; upsample / Vocos empty)."""
+    rc = lib().oq_synth_write_ex(path.encode(), C.byref(dims), seed, SYNTH_DECODER)
+    if rc != 0:
+        raise IOError(f"oracle synth_write_ex failed for {path}")
+
+
+class Decoder:
+    """decoder.rs:142-335 + the conv.rs:114-191 pre-conv on the CPU: 16 code
+    streams of T frames -> the transformer output [1024][T]."""
+
+    def __init__(self, path: str):
+        err = C.create_string_buffer(256)
+        self.h = lib().oq_decoder_load(path.encode(), err, 256)
+        if not self.h:
+            raise IOError(f"oracle decoder load failed: {err.value.decode()}")
+
+    def decode_latent(self, codes):
+        import numpy as np
+        codes = np.ascontiguousarray(codes, dtype=np.uint32)
+        assert codes.ndim == 2 and codes.shape[0] == 16
+        T = codes.shape[1]
+        out = np.zeros((1024, T), np.float32)
+        rc = lib().oq_decode_latent(self.h, _p(codes, C.c_uint32), T, fptr(out))
+        if rc != 0:
+            raise ValueError("code index past its codebook")
+        return out
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().oq_decoder_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
 
 
 def synth_write_tied_heads(path: str, dims: Dims, seed: int = 0, period: int = 7) -> None:

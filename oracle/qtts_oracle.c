@@ -430,6 +430,11 @@ static void w_bias(wctx* c, uint64_t n) { /* write_f32_vec_io of N(0,0.02) */
   for (uint64_t i = 0; i < n; i++) { float v = (float)(gauss(&s) * 0.02); w_bytes(c, &v, 4); }
 }
 static void w_f32vec(wctx* c, const float* v, uint64_t n) { ++c->id; w_u64(c, n); w_bytes(c, v, n * 4); }
+static void w_gvec(wctx* c, uint64_t n, double mean, double sd) { /* write_f32_vec_io of mean + sd*N(0,1) */
+  uint64_t s = stream_seed(c->seed, ++c->id);
+  w_u64(c, n);
+  for (uint64_t i = 0; i < n; i++) { float v = (float)(mean + sd * gauss(&s)); w_bytes(c, &v, 4); }
+}
 static void w_empty_vec(wctx* c) { w_u64(c, 0); }
 static void w_empty_conv1d(wctx* c) { for (int i = 0; i < 6; i++) w_u32(c, 0); w_empty_vec(c); w_empty_vec(c); }
 
@@ -453,7 +458,52 @@ void oq_dims_tiny(oq_dims* d) {
   d->p_inter = 512; d->p_vocab = 2048; d->p_groups = 15; d->p_max_pos = 64; d->fmt = 1;
 }
 
-int oq_synth_write(const char* path, const oq_dims* d, uint64_t seed) {
+/* The synthetic speech decoder, decoder.rs:21-108 shapes (12 Hz tokenizer
+ * decoder): 16 codebooks of 2048 x 256, hidden 512, 16 heads of 64, MLP 1024,
+ * window 72, 8 layers, latent 1024, RoPE theta 10000 over 8192 positions;
+ * upsample and Vocos stages empty (they are not restated here).  Values:
+ * codebooks N(0,1), projections N(0,1/fan_in), biases N(0,0.02), norm weights
+ * 1 + N(0,0.1), layer scales 0.05 + N(0,0.01); save.rs:171-256 order. */
+static void w_decoder(wctx* c) {
+  const uint32_t H = OQ_DEC_HIDDEN, A = OQ_DEC_HEADS * OQ_DEC_HEAD_DIM;
+  w_u32(c, H); w_u32(c, OQ_DEC_HEADS); w_u32(c, OQ_DEC_HEAD_DIM); w_u32(c, OQ_DEC_INTER);
+  w_u32(c, OQ_DEC_WINDOW); w_u32(c, OQ_DEC_CB_DIM);
+  w_gvec(c, (uint64_t)OQ_DEC_ENTRIES * OQ_DEC_CB_DIM, 0.0, 1.0);
+  w_gvec(c, (uint64_t)OQ_DEC_CB_DIM * 512, 0.0, 1.0 / sqrt((double)OQ_DEC_CB_DIM));
+  w_u32(c, 15);
+  for (int g = 0; g < 15; g++) w_gvec(c, (uint64_t)OQ_DEC_ENTRIES * OQ_DEC_CB_DIM, 0.0, 1.0);
+  w_gvec(c, (uint64_t)OQ_DEC_CB_DIM * 512, 0.0, 1.0 / sqrt((double)OQ_DEC_CB_DIM));
+  w_u32(c, 512); w_u32(c, OQ_DEC_LATENT); w_u32(c, 3); w_u32(c, 1); w_u32(c, 0); w_u32(c, 1);
+  w_gvec(c, (uint64_t)OQ_DEC_LATENT * 512 * 3, 0.0, 1.0 / sqrt(512.0 * 3.0));
+  w_gvec(c, OQ_DEC_LATENT, 0.0, 0.02);
+  w_gvec(c, (uint64_t)OQ_DEC_LATENT * H, 0.0, 1.0 / sqrt((double)OQ_DEC_LATENT));
+  w_gvec(c, H, 0.0, 0.02);
+  w_u32(c, OQ_DEC_LAYERS);
+  for (int l = 0; l < OQ_DEC_LAYERS; l++) {
+    for (int m = 0; m < 3; m++) w_gvec(c, (uint64_t)H * A, 0.0, 1.0 / sqrt((double)H));
+    w_gvec(c, (uint64_t)A * H, 0.0, 1.0 / sqrt((double)A));
+    w_gvec(c, (uint64_t)H * OQ_DEC_INTER, 0.0, 1.0 / sqrt((double)H));
+    w_gvec(c, (uint64_t)H * OQ_DEC_INTER, 0.0, 1.0 / sqrt((double)H));
+    w_gvec(c, (uint64_t)OQ_DEC_INTER * H, 0.0, 1.0 / sqrt((double)OQ_DEC_INTER));
+    w_gvec(c, H, 1.0, 0.1); w_gvec(c, H, 1.0, 0.1);
+    w_gvec(c, H, 0.05, 0.01); w_gvec(c, H, 0.05, 0.01);
+  }
+  w_gvec(c, H, 1.0, 0.1);
+  w_gvec(c, (uint64_t)H * OQ_DEC_LATENT, 0.0, 1.0 / sqrt((double)H));
+  w_gvec(c, OQ_DEC_LATENT, 0.0, 0.02);
+  w_u32(c, 0);
+  w_empty_conv1d(c); w_u32(c, 0);
+  w_empty_vec(c); w_empty_vec(c); w_empty_conv1d(c);
+  size_t n = (size_t)OQ_DEC_ROPE_POS * (OQ_DEC_HEAD_DIM / 2);
+  float* cs = (float*)malloc(n * 4); float* sn = (float*)malloc(n * 4);
+  oq_build_rope_tables(OQ_DEC_HEAD_DIM, OQ_DEC_ROPE_POS, 10000.0, cs, sn);
+  w_f32vec(c, cs, n); w_f32vec(c, sn, n);
+  free(cs); free(sn);
+}
+
+int oq_synth_write(const char* path, const oq_dims* d, uint64_t seed) { return oq_synth_write_ex(path, d, seed, 0); }
+
+int oq_synth_write_ex(const char* path, const oq_dims* d, uint64_t seed, unsigned flags) {
   wctx c = {fopen(path, "wb"), seed, 0, 0};
   if (!c.f) return -1;
   setvbuf(c.f, NULL, _IOFBF, 1 << 23);
@@ -522,17 +572,21 @@ int oq_synth_write(const char* path, const oq_dims* d, uint64_t seed) {
     w_f32vec(&c, cs, n); w_f32vec(&c, sn, n);
     free(cs); free(sn);
   }
-  /* An empty speech-decoder section in the save.rs:171-256 layout, so that
-   * save::load_model parses the file; the decoder is out of scope. */
-  for (int i = 0; i < 6; i++) w_u32(&c, 0);
-  w_empty_vec(&c); w_empty_vec(&c); w_u32(&c, 0); w_empty_vec(&c);
-  w_empty_conv1d(&c);
-  w_empty_vec(&c); w_empty_vec(&c); w_u32(&c, 0);
-  w_empty_vec(&c); w_empty_vec(&c); w_empty_vec(&c);
-  w_u32(&c, 0);
-  w_empty_conv1d(&c); w_u32(&c, 0);
-  w_empty_vec(&c); w_empty_vec(&c); w_empty_conv1d(&c);
-  w_empty_vec(&c); w_empty_vec(&c);
+  if (flags & OQ_SYNTH_DECODER) {
+    w_decoder(&c);
+  } else {
+    /* An empty speech-decoder section in the save.rs:171-256 layout, so that
+     * save::load_model parses the file. */
+    for (int i = 0; i < 6; i++) w_u32(&c, 0);
+    w_empty_vec(&c); w_empty_vec(&c); w_u32(&c, 0); w_empty_vec(&c);
+    w_empty_conv1d(&c);
+    w_empty_vec(&c); w_empty_vec(&c); w_u32(&c, 0);
+    w_empty_vec(&c); w_empty_vec(&c); w_empty_vec(&c);
+    w_u32(&c, 0);
+    w_empty_conv1d(&c); w_u32(&c, 0);
+    w_empty_vec(&c); w_empty_vec(&c); w_empty_conv1d(&c);
+    w_empty_vec(&c); w_empty_vec(&c);
+  }
   int err = c.err;
   if (fclose(c.f) != 0) err = 1;
   return err ? -1 : 0;
@@ -603,77 +657,84 @@ static void free_layer(ol* L) {
   free(L->q_norm); free(L->k_norm); free(L->in_norm); free(L->post_norm);
 }
 
-oq_model* oq_load(const char* path, char* err, int errlen) {
-  rctx r = {fopen(path, "rb"), 0, err, errlen};
-  if (!r.f) { if (err) snprintf(err, errlen, "cannot open %s", path); return NULL; }
-  setvbuf(r.f, NULL, _IOFBF, 1 << 23);
+/* the talker and predictor sections; the stream is left at the decoder section */
+static oq_model* load_lm(rctx* r) {
   oq_model* m = (oq_model*)calloc(1, sizeof(oq_model));
   char magic[4];
-  r_bytes(&r, magic, 4);
-  if (!r.err && memcmp(magic, "QTTS", 4) != 0) r_fail(&r, "Invalid magic (expected QTTS)");
-  uint32_t ver = r_u32(&r);
-  if (!r.err && ver != 1) r_fail(&r, "unsupported version");
+  r_bytes(r, magic, 4);
+  if (!r->err && memcmp(magic, "QTTS", 4) != 0) r_fail(r, "Invalid magic (expected QTTS)");
+  uint32_t ver = r_u32(r);
+  if (!r->err && ver != 1) r_fail(r, "unsupported version");
   uint8_t fmt = 0;
-  r_bytes(&r, &fmt, 1);
+  r_bytes(r, &fmt, 1);
   oq_dims* d = &m->d;
   d->fmt = fmt;
   /* load_talker save.rs:300-351 */
-  d->t_layers = r_u32(&r); d->t_hidden = r_u32(&r); d->t_text_hidden = r_u32(&r);
-  d->t_heads = r_u32(&r); d->t_kv_heads = r_u32(&r); d->t_head_dim = r_u32(&r);
-  m->t_kv_groups = r_u32(&r);
-  m->t_nsec = r_u32(&r);
-  if (!r.err && (m->t_nsec > 3 || d->t_layers > 4096 || d->t_layers == 0))
-    r_fail(&r, "bad talker header");
-  for (int i = 0; i < m->t_nsec && !r.err; i++) d->t_sec[i] = r_u32(&r);
-  if (!r.err) {
+  d->t_layers = r_u32(r); d->t_hidden = r_u32(r); d->t_text_hidden = r_u32(r);
+  d->t_heads = r_u32(r); d->t_kv_heads = r_u32(r); d->t_head_dim = r_u32(r);
+  m->t_kv_groups = r_u32(r);
+  m->t_nsec = r_u32(r);
+  if (!r->err && (m->t_nsec > 3 || d->t_layers > 4096 || d->t_layers == 0))
+    r_fail(r, "bad talker header");
+  for (int i = 0; i < m->t_nsec && !r->err; i++) d->t_sec[i] = r_u32(r);
+  if (!r->err) {
     m->tl = (ol*)calloc(d->t_layers, sizeof(ol));
-    for (int l = 0; l < d->t_layers && !r.err; l++)
-      read_layer(&r, fmt, &m->tl[l], d->t_head_dim, d->t_hidden);
+    for (int l = 0; l < d->t_layers && !r->err; l++)
+      read_layer(r, fmt, &m->tl[l], d->t_head_dim, d->t_hidden);
   }
-  m->codec_emb = r_weight(&r, fmt);
-  m->text_emb = r_weight(&r, fmt);
-  m->fc1 = r_weight(&r, fmt);
+  m->codec_emb = r_weight(r, fmt);
+  m->text_emb = r_weight(r, fmt);
+  m->fc1 = r_weight(r, fmt);
   uint64_t l;
-  m->fc1_b = r_f32(&r, &l);
-  m->fc2 = r_weight(&r, fmt);
-  m->fc2_b = r_f32(&r, &l);
-  m->codec_head = r_weight(&r, fmt);
-  m->t_final_norm = r_f16(&r, d->t_hidden);
-  m->t_cos = r_f32(&r, &m->t_rope_len);
-  m->t_sin = r_f32(&r, &l);
-  if (!r.err) {
+  m->fc1_b = r_f32(r, &l);
+  m->fc2 = r_weight(r, fmt);
+  m->fc2_b = r_f32(r, &l);
+  m->codec_head = r_weight(r, fmt);
+  m->t_final_norm = r_f16(r, d->t_hidden);
+  m->t_cos = r_f32(r, &m->t_rope_len);
+  m->t_sin = r_f32(r, &l);
+  if (!r->err) {
     d->t_inter = m->tl[0].gate.n; d->t_vocab = m->codec_head.n;
     d->t_text_vocab = m->text_emb.k;
     d->t_max_pos = (int)(m->t_rope_len / (d->t_head_dim / 2));
   }
   /* load_predictor save.rs:353-409 */
-  d->p_layers = r_u32(&r); d->p_hidden = r_u32(&r); d->p_heads = r_u32(&r);
-  d->p_kv_heads = r_u32(&r); d->p_head_dim = r_u32(&r); m->p_kv_groups = r_u32(&r);
+  d->p_layers = r_u32(r); d->p_hidden = r_u32(r); d->p_heads = r_u32(r);
+  d->p_kv_heads = r_u32(r); d->p_head_dim = r_u32(r); m->p_kv_groups = r_u32(r);
   uint8_t hp = 0;
-  r_bytes(&r, &hp, 1);
+  r_bytes(r, &hp, 1);
   m->has_proj = hp == 1;
-  if (m->has_proj) { m->input_proj = r_weight(&r, fmt); m->input_proj_b = r_f32(&r, &l); }
-  m->n_emb = r_u32(&r);
-  if (!r.err && (m->n_emb > 64 || d->p_layers > 4096 || d->p_layers == 0)) r_fail(&r, "bad predictor header");
-  if (!r.err) {
+  if (m->has_proj) { m->input_proj = r_weight(r, fmt); m->input_proj_b = r_f32(r, &l); }
+  m->n_emb = r_u32(r);
+  if (!r->err && (m->n_emb > 64 || d->p_layers > 4096 || d->p_layers == 0)) r_fail(r, "bad predictor header");
+  if (!r->err) {
     m->p_emb = (ow*)calloc(m->n_emb, sizeof(ow));
-    for (int g = 0; g < m->n_emb; g++) m->p_emb[g] = r_weight(&r, fmt);
+    for (int g = 0; g < m->n_emb; g++) m->p_emb[g] = r_weight(r, fmt);
     m->pl = (ol*)calloc(d->p_layers, sizeof(ol));
-    for (int i = 0; i < d->p_layers && !r.err; i++) read_layer(&r, fmt, &m->pl[i], d->p_head_dim, d->p_hidden);
-    m->n_lm = r_u32(&r);
-    if (!r.err && m->n_lm > 64) r_fail(&r, "bad lm_head count");
-    if (!r.err) {
+    for (int i = 0; i < d->p_layers && !r->err; i++) read_layer(r, fmt, &m->pl[i], d->p_head_dim, d->p_hidden);
+    m->n_lm = r_u32(r);
+    if (!r->err && m->n_lm > 64) r_fail(r, "bad lm_head count");
+    if (!r->err) {
       m->lm = (ow*)calloc(m->n_lm, sizeof(ow));
-      for (int g = 0; g < m->n_lm; g++) m->lm[g] = r_weight(&r, fmt);
+      for (int g = 0; g < m->n_lm; g++) m->lm[g] = r_weight(r, fmt);
     }
-    m->p_final_norm = r_f16(&r, d->p_hidden);
-    m->p_cos = r_f32(&r, &m->p_rope_len);
-    m->p_sin = r_f32(&r, &l);
+    m->p_final_norm = r_f16(r, d->p_hidden);
+    m->p_cos = r_f32(r, &m->p_rope_len);
+    m->p_sin = r_f32(r, &l);
   }
-  fclose(r.f);
-  if (r.err) { oq_free(m); return NULL; }
+  if (r->err) { oq_free(m); return NULL; }
   d->p_inter = m->pl[0].gate.n; d->p_vocab = m->lm[0].n; d->p_groups = m->n_lm;
   d->p_max_pos = (int)(m->p_rope_len / (d->p_head_dim / 2));
+  return m;
+}
+
+
+oq_model* oq_load(const char* path, char* err, int errlen) {
+  rctx r = {fopen(path, "rb"), 0, err, errlen};
+  if (!r.f) { if (err) snprintf(err, errlen, "cannot open %s", path); return NULL; }
+  setvbuf(r.f, NULL, _IOFBF, 1 << 23);
+  oq_model* m = load_lm(&r);
+  fclose(r.f);
   return m;
 }
 
@@ -1309,4 +1370,287 @@ double oq_time_frames(const oq_model* m, int kv_len, int frames, uint64_t seed) 
   oq_kv_free(tkv); oq_kv_free(pkv);
   free(hidden); free(logits); free(res); free(sem); free(acs);
   return ((t1.tv_sec - t0.tv_sec) + 1e-9 * (t1.tv_nsec - t0.tv_nsec)) / (frames > 0 ? frames : 1);
+}
+
+/* ------------------------------------------------------------------------ */
+/* speech decoder, codes -> transformer output: decoder.rs:142-335 and the  */
+/* conv.rs:114-191 pre-conv (decode_to_audio decoder.rs:394-424, steps 1-3); */
+/* reader save.rs:446-552 (the upsample / Vocos stages are read and dropped) */
+/* ------------------------------------------------------------------------ */
+
+typedef struct { uint32_t in, out, k, stride, pad, dil; float* w; float* b; uint64_t wl, bl; } oconv;
+typedef struct { float *q, *k, *v, *o, *gate, *up, *down, *in_norm, *post_norm, *attn_scale, *mlp_scale; } odl;
+struct oq_decoder {
+  uint32_t hidden, heads, head_dim, inter, window, cb_dim, entries;
+  float* cb0; float* proj0; float* cb_rest[15]; float* proj_rest;
+  oconv pre;
+  float *in_w, *in_b, *norm, *out_w, *out_b, *rope_cos, *rope_sin;
+  uint64_t rope_len;
+  int n_layers;
+  odl* L;
+};
+
+static oconv r_conv1d(rctx* r) { /* save.rs:411-422 */
+  oconv c;
+  memset(&c, 0, sizeof(c));
+  c.in = r_u32(r); c.out = r_u32(r); c.k = r_u32(r); c.stride = r_u32(r); c.pad = r_u32(r); c.dil = r_u32(r);
+  c.w = r_f32(r, &c.wl); c.b = r_f32(r, &c.bl);
+  return c;
+}
+static void drop_vec(rctx* r) { uint64_t l; free(r_f32(r, &l)); }
+static void drop_conv(rctx* r, int hdr) { for (int i = 0; i < hdr; i++) r_u32(r); drop_vec(r); drop_vec(r); }
+static float* r_f32n(rctx* r, uint64_t expect, const char* what) {
+  uint64_t l = 0;
+  float* v = r_f32(r, &l);
+  if (!r->err && l != expect) r_fail(r, what);
+  return v;
+}
+
+void oq_decoder_free(oq_decoder* d) {
+  if (!d) return;
+  free(d->cb0); free(d->proj0); free(d->proj_rest);
+  for (int g = 0; g < 15; g++) free(d->cb_rest[g]);
+  free(d->pre.w); free(d->pre.b);
+  free(d->in_w); free(d->in_b); free(d->norm); free(d->out_w); free(d->out_b);
+  free(d->rope_cos); free(d->rope_sin);
+  if (d->L)
+    for (int l = 0; l < d->n_layers; l++) {
+      odl* L = &d->L[l];
+      free(L->q); free(L->k); free(L->v); free(L->o); free(L->gate); free(L->up); free(L->down);
+      free(L->in_norm); free(L->post_norm); free(L->attn_scale); free(L->mlp_scale);
+    }
+  free(d->L);
+  free(d);
+}
+
+oq_decoder* oq_decoder_load(const char* path, char* err, int errlen) {
+  rctx r = {fopen(path, "rb"), 0, err, errlen};
+  if (!r.f) { if (err) snprintf(err, errlen, "cannot open %s", path); return NULL; }
+  setvbuf(r.f, NULL, _IOFBF, 1 << 23);
+  oq_model* m = load_lm(&r);
+  if (!m) { fclose(r.f); return NULL; }
+  oq_free(m);
+  oq_decoder* d = (oq_decoder*)calloc(1, sizeof(oq_decoder));
+  d->hidden = r_u32(&r); d->heads = r_u32(&r); d->head_dim = r_u32(&r);
+  d->inter = r_u32(&r); d->window = r_u32(&r); d->cb_dim = r_u32(&r);
+  if (!r.err && (d->hidden == 0 || d->heads == 0 || d->head_dim == 0 || d->inter == 0 || d->cb_dim == 0))
+    r_fail(&r, "the file has no speech decoder");
+  const uint64_t A = (uint64_t)d->heads * d->head_dim, H = d->hidden;
+  uint64_t l = 0;
+  d->cb0 = r_f32(&r, &l);
+  if (!r.err && (l == 0 || l % d->cb_dim)) r_fail(&r, "codebook length");
+  d->entries = (uint32_t)(l / (d->cb_dim ? d->cb_dim : 1));
+  d->proj0 = r_f32n(&r, (uint64_t)d->cb_dim * 512, "codebook projection length");
+  uint32_t nr = r_u32(&r);
+  if (!r.err && nr != 15) r_fail(&r, "expected 15 rest codebooks");
+  for (uint32_t g = 0; g < nr && g < 15 && !r.err; g++)
+    d->cb_rest[g] = r_f32n(&r, (uint64_t)d->entries * d->cb_dim, "codebook length");
+  d->proj_rest = r_f32n(&r, (uint64_t)d->cb_dim * 512, "codebook projection length");
+  d->pre = r_conv1d(&r);
+  if (!r.err && (d->pre.in != 512 || d->pre.out != 1024 || d->pre.k == 0 || d->pre.dil == 0 ||
+                 d->pre.wl != (uint64_t)d->pre.out * d->pre.in * d->pre.k || d->pre.bl != d->pre.out))
+    r_fail(&r, "pre-conv shape");
+  d->in_w = r_f32n(&r, 1024 * H, "transformer input projection length");
+  d->in_b = r_f32n(&r, H, "transformer input bias length");
+  d->n_layers = (int)r_u32(&r);
+  if (!r.err && (d->n_layers <= 0 || d->n_layers > 64)) r_fail(&r, "bad decoder layer count");
+  if (!r.err) {
+    d->L = (odl*)calloc(d->n_layers, sizeof(odl));
+    for (int i = 0; i < d->n_layers && !r.err; i++) {
+      odl* L = &d->L[i];
+      L->q = r_f32n(&r, H * A, "q_proj length"); L->k = r_f32n(&r, H * A, "k_proj length");
+      L->v = r_f32n(&r, H * A, "v_proj length"); L->o = r_f32n(&r, A * H, "o_proj length");
+      L->gate = r_f32n(&r, H * d->inter, "gate_proj length"); L->up = r_f32n(&r, H * d->inter, "up_proj length");
+      L->down = r_f32n(&r, (uint64_t)d->inter * H, "down_proj length");
+      L->in_norm = r_f32n(&r, H, "norm length"); L->post_norm = r_f32n(&r, H, "norm length");
+      L->attn_scale = r_f32n(&r, H, "layer scale length"); L->mlp_scale = r_f32n(&r, H, "layer scale length");
+    }
+  }
+  d->norm = r_f32n(&r, H, "norm length");
+  d->out_w = r_f32n(&r, H * 1024, "transformer output projection length");
+  d->out_b = r_f32n(&r, 1024, "transformer output bias length");
+  uint32_t nu = r_u32(&r);
+  if (!r.err && nu > 4096) r_fail(&r, "bad decoder upsample count");
+  for (uint32_t i = 0; i < nu && !r.err; i++) {
+    r_u32(&r); drop_conv(&r, 5); drop_conv(&r, 3);
+    for (int j = 0; j < 7; j++) drop_vec(&r);
+  }
+  drop_conv(&r, 6);
+  uint32_t nb = r_u32(&r);
+  if (!r.err && nb > 4096) r_fail(&r, "bad vocos block count");
+  for (uint32_t i = 0; i < nb && !r.err; i++) {
+    drop_vec(&r); drop_vec(&r); drop_conv(&r, 5);
+    uint32_t nres = r_u32(&r);
+    if (!r.err && nres > 4096) r_fail(&r, "bad vocos residual count");
+    for (uint32_t j = 0; j < nres && !r.err; j++) {
+      drop_vec(&r); drop_vec(&r); drop_conv(&r, 6); drop_vec(&r); drop_vec(&r); drop_conv(&r, 6);
+    }
+  }
+  drop_vec(&r); drop_vec(&r); drop_conv(&r, 6);
+  d->rope_cos = r_f32(&r, &d->rope_len);
+  d->rope_sin = r_f32n(&r, d->rope_len, "rope table length");
+  fclose(r.f);
+  if (r.err) { oq_decoder_free(d); return NULL; }
+  return d;
+}
+
+/* decoder.rs:527-538 f32_gemv: weight [k][n], zero inputs skipped */
+static void dec_gemv(const float* in, const float* w, size_t k, size_t n, float* out) {
+  for (size_t j = 0; j < n; j++) out[j] = 0.0f;
+  for (size_t ki = 0; ki < k; ki++) {
+    float iv = in[ki];
+    if (iv == 0.0f) continue;
+    const float* wr = w + ki * n;
+    for (size_t j = 0; j < n; j++) out[j] += iv * wr[j];
+  }
+}
+/* decoder.rs:541-553 f32_gemv_bias */
+static void dec_gemv_bias(const float* in, const float* w, size_t k, size_t n, const float* bias, float* out) {
+  memcpy(out, bias, n * sizeof(float));
+  for (size_t ki = 0; ki < k; ki++) {
+    float iv = in[ki];
+    if (iv == 0.0f) continue;
+    const float* wr = w + ki * n;
+    for (size_t j = 0; j < n; j++) out[j] += iv * wr[j];
+  }
+}
+/* decoder.rs:515-525 rms_norm_f32 */
+static void dec_rms(const float* x, const float* g, size_t n, float eps, float* out) {
+  float ss = 0.0f;
+  for (size_t i = 0; i < n; i++) ss += x[i] * x[i];
+  float inv = 1.0f / sqrtf(ss / (float)n + eps);
+  for (size_t i = 0; i < n; i++) out[i] = x[i] * inv * g[i];
+}
+/* decoder.rs:556-578 apply_rope_split_half */
+static void dec_rope(float* x, int heads, int hd, int pos, const float* c, const float* s, uint64_t len) {
+  int half = hd / 2;
+  uint64_t off = (uint64_t)pos * half;
+  if (off + half > len) return;
+  for (int h = 0; h < heads; h++) {
+    float* b = x + (size_t)h * hd;
+    for (int i = 0; i < half; i++) {
+      float x0 = b[i], x1 = b[half + i], cc = c[off + i], ss = s[off + i];
+      b[i] = x0 * cc - x1 * ss;
+      b[half + i] = x1 * cc + x0 * ss;
+    }
+  }
+}
+
+int oq_decode_latent(const oq_decoder* d, const uint32_t* codes, int T, float* out) {
+  const size_t cb = d->cb_dim, H = d->hidden, A = (size_t)d->heads * d->head_dim, I = d->inter;
+  if (T <= 0) return 0;
+  for (int g = 0; g < 16; g++)
+    for (int t = 0; t < T; t++)
+      if (codes[(size_t)g * T + t] >= d->entries) return -1;
+  /* codebook_lookup decoder.rs:142-187 -> vq [512][T] */
+  float* vq = (float*)calloc((size_t)512 * T, sizeof(float));
+  float* proj = (float*)malloc(512 * sizeof(float));
+  float* se = (float*)malloc(cb * sizeof(float));
+  for (int t = 0; t < T; t++) {
+    dec_gemv(d->cb0 + (size_t)codes[t] * cb, d->proj0, cb, 512, proj);
+    for (int c = 0; c < 512; c++) vq[(size_t)c * T + t] += proj[c];
+  }
+  for (int t = 0; t < T; t++) {
+    for (size_t e = 0; e < cb; e++) se[e] = 0.0f;
+    for (int g = 0; g < 15; g++) {
+      const float* emb = d->cb_rest[g] + (size_t)codes[(size_t)(g + 1) * T + t] * cb;
+      for (size_t e = 0; e < cb; e++) se[e] += emb[e];
+    }
+    dec_gemv(se, d->proj_rest, cb, 512, proj);
+    for (int c = 0; c < 512; c++) vq[(size_t)c * T + t] += proj[c];
+  }
+  /* causal_conv1d conv.rs:114-191 (left pad (k-1)*dilation) -> [1024][T] */
+  const oconv* pc = &d->pre;
+  float* pre = (float*)malloc((size_t)pc->out * T * sizeof(float));
+  {
+    const size_t pad = (size_t)(pc->k - 1) * pc->dil, ick = (size_t)pc->in * pc->k;
+    for (uint32_t oc = 0; oc < pc->out; oc++)
+      for (int o = 0; o < T; o++) {
+        float sum = pc->b[oc];
+        for (uint32_t ic = 0; ic < pc->in; ic++) {
+          const float* wr = pc->w + oc * ick + (size_t)ic * pc->k;
+          for (uint32_t k = 0; k < pc->k; k++) {
+            size_t in_pos = (size_t)o + (size_t)k * pc->dil;
+            if (in_pos >= pad) {
+              size_t idx = in_pos - pad;
+              if (idx < (size_t)T) sum += vq[(size_t)ic * T + idx] * wr[k];
+            }
+          }
+        }
+        pre[(size_t)oc * T + o] = sum;
+      }
+  }
+  /* decoder_transformer decoder.rs:195-335 */
+  const size_t D = 1024;
+  float* xrow = (float*)malloc(D * T * sizeof(float));
+  for (size_t c = 0; c < D; c++)
+    for (int t = 0; t < T; t++) xrow[(size_t)t * D + c] = pre[c * T + t];
+  float* x = (float*)malloc(H * T * sizeof(float));
+  for (int t = 0; t < T; t++) dec_gemv_bias(xrow + (size_t)t * D, d->in_w, D, H, d->in_b, x + (size_t)t * H);
+  float* q = (float*)malloc(A * T * sizeof(float));
+  float* k = (float*)malloc(A * T * sizeof(float));
+  float* v = (float*)malloc(A * T * sizeof(float));
+  float* xn = (float*)malloc(H * sizeof(float));
+  float* ao = (float*)malloc(A * sizeof(float));
+  float* oo = (float*)malloc(H * sizeof(float));
+  float* sc = (float*)malloc((size_t)(d->window + 1) * sizeof(float));
+  float* gt = (float*)malloc(I * sizeof(float));
+  float* up = (float*)malloc(I * sizeof(float));
+  const int hd = (int)d->head_dim;
+  const float scale = 1.0f / sqrtf((float)hd);
+  for (int li = 0; li < d->n_layers; li++) {
+    const odl* L = &d->L[li];
+    for (int t = 0; t < T; t++) {
+      dec_rms(x + (size_t)t * H, L->in_norm, H, 1e-5f, xn);
+      dec_gemv(xn, L->q, H, A, q + (size_t)t * A);
+      dec_gemv(xn, L->k, H, A, k + (size_t)t * A);
+      dec_gemv(xn, L->v, H, A, v + (size_t)t * A);
+    }
+    for (int t = 0; t < T; t++) {
+      dec_rope(q + (size_t)t * A, (int)d->heads, hd, t, d->rope_cos, d->rope_sin, d->rope_len);
+      dec_rope(k + (size_t)t * A, (int)d->heads, hd, t, d->rope_cos, d->rope_sin, d->rope_len);
+    }
+    for (int t = 0; t < T; t++) {
+      int start = (t + 1 > (int)d->window) ? t + 1 - (int)d->window : 0;
+      int L_ = t + 1 - start;
+      for (size_t e = 0; e < A; e++) ao[e] = 0.0f;
+      for (int h = 0; h < (int)d->heads; h++) {
+        const float* qq = q + (size_t)t * A + (size_t)h * hd;
+        for (int s = 0; s < L_; s++) {
+          const float* kk = k + (size_t)(start + s) * A + (size_t)h * hd;
+          float dot = 0.0f;
+          for (int e = 0; e < hd; e++) dot += qq[e] * kk[e];
+          sc[s] = dot * scale;
+        }
+        oq_softmax_raw(sc, (size_t)L_);
+        for (int s = 0; s < L_; s++) {
+          const float* vv = v + (size_t)(start + s) * A + (size_t)h * hd;
+          float p = sc[s];
+          for (int e = 0; e < hd; e++) ao[(size_t)h * hd + e] += p * vv[e];
+        }
+      }
+      dec_gemv(ao, L->o, A, H, oo);
+      for (size_t j = 0; j < H; j++) x[(size_t)t * H + j] += oo[j] * L->attn_scale[j];
+    }
+    for (int t = 0; t < T; t++) {
+      dec_rms(x + (size_t)t * H, L->post_norm, H, 1e-5f, xn);
+      dec_gemv(xn, L->gate, H, I, gt);
+      dec_gemv(xn, L->up, H, I, up);
+      for (size_t j = 0; j < I; j++) {
+        float g = gt[j];
+        gt[j] = (g / (1.0f + expf(-g))) * up[j];
+      }
+      dec_gemv(gt, L->down, I, H, oo);
+      for (size_t j = 0; j < H; j++) x[(size_t)t * H + j] += oo[j] * L->mlp_scale[j];
+    }
+  }
+  float* orow = (float*)malloc(D * sizeof(float));
+  for (int t = 0; t < T; t++) {
+    dec_rms(x + (size_t)t * H, d->norm, H, 1e-5f, xn);
+    dec_gemv_bias(xn, d->out_w, H, D, d->out_b, orow);
+    for (size_t c = 0; c < D; c++) out[c * T + t] = orow[c];
+  }
+  free(vq); free(proj); free(se); free(pre); free(xrow); free(x); free(q); free(k); free(v);
+  free(xn); free(ao); free(oo); free(sc); free(gt); free(up); free(orow);
+  return 0;
 }

@@ -55,6 +55,32 @@ uint16_t oq_f2h(float f);
 
 /* -- synthetic weights in the .qora-tts layout (save.rs:23-137) -- */
 int oq_synth_write(const char* path, const oq_dims* d, uint64_t seed);
+/* flags: OQ_SYNTH_DECODER writes a full-size synthetic speech decoder
+ * (codebooks, pre-conv, transformer, RoPE; upsample / Vocos stages empty). */
+#define OQ_SYNTH_DECODER 1u
+int oq_synth_write_ex(const char* path, const oq_dims* d, uint64_t seed, unsigned flags);
+/* decoder shapes of the synthetic file (decoder.rs:21-108) */
+#define OQ_DEC_HIDDEN 512
+#define OQ_DEC_HEADS 16
+#define OQ_DEC_HEAD_DIM 64
+#define OQ_DEC_INTER 1024
+#define OQ_DEC_WINDOW 72
+#define OQ_DEC_CB_DIM 256
+#define OQ_DEC_ENTRIES 2048
+#define OQ_DEC_LAYERS 8
+#define OQ_DEC_LATENT 1024
+#define OQ_DEC_ROPE_POS 8192
+
+/* -- speech decoder, codes -> transformer output (decoder.rs:142-335 with
+ * the conv.rs:114-191 pre-conv, the first three steps of decode_to_audio
+ * decoder.rs:394-424) -- */
+typedef struct oq_decoder oq_decoder;
+oq_decoder* oq_decoder_load(const char* path, char* err, int errlen);
+void oq_decoder_free(oq_decoder* d);
+/* codes: [16][T] (codes[g][t], the reference's &[Vec<u32>]); out: the
+ * transformer output [1024][T] channel-first.  Returns 0, or -1 for a code
+ * past its codebook (the reference panics on that index). */
+int oq_decode_latent(const oq_decoder* d, const uint32_t* codes, int T, float* out);
 /* Test fixture: predictor heads written with column j == column j % period
  * (0 = the ordinary synthetic heads); applies to later oq_synth_write calls. */
 void oq_set_tie_period(int period);

@@ -140,12 +140,16 @@ bool check_layer(Reader& r, const HLayer& L, int hidden, int heads, int kvh, int
   return true;
 }
 
-// The speech-decoder section (save.rs:446-513 load_decoder_weights) is not on
-// the decode path; it is walked without reading payloads so that a file
-// save::load_model would reject is rejected here too.
-void skip_conv1d(Reader& r) {  // save.rs:411-422
-  for (int i = 0; i < 6; ++i) r.u32();
-  r.vec(4); r.vec(4);
+// The speech-decoder section (save.rs:446-552 load_decoder_weights).  Its
+// codebook / pre-conv / transformer tensors are recorded when asked for (the
+// GPU decoder stage reads them); the upsample and Vocos stages are walked
+// without reading payloads, so that a file save::load_model would reject is
+// rejected here too.
+HConv1d conv1d(Reader& r) {  // save.rs:411-422
+  HConv1d c;
+  c.in = r.u32(); c.out = r.u32(); c.k = r.u32(); c.stride = r.u32(); c.pad = r.u32(); c.dil = r.u32();
+  c.w = r.vec(4); c.b = r.vec(4);
+  return c;
 }
 void skip_conv_t1d(Reader& r) {  // save.rs:424-434
   for (int i = 0; i < 5; ++i) r.u32();
@@ -155,20 +159,27 @@ void skip_dw_conv(Reader& r) {  // save.rs:436-444
   for (int i = 0; i < 3; ++i) r.u32();
   r.vec(4); r.vec(4);
 }
-void skip_decoder(Reader& r) {
-  for (int i = 0; i < 6; ++i) r.u32();
-  r.vec(4); r.vec(4);
+void read_decoder(Reader& r, HDecoder* out) {
+  HDecoder d;
+  d.hidden = r.u32(); d.heads = r.u32(); d.head_dim = r.u32();
+  d.inter = r.u32(); d.window = r.u32(); d.cb_dim = r.u32();
+  d.cb0 = r.vec(4); d.proj0 = r.vec(4);
   uint32_t n = r.u32();
   if (!r.bad && n > 4096) r.fail("bad decoder codebook count");
-  for (uint32_t i = 0; i < n && !r.bad; ++i) r.vec(4);
-  r.vec(4);
-  skip_conv1d(r);
-  r.vec(4); r.vec(4);
+  for (uint32_t i = 0; i < n && !r.bad; ++i) d.cb_rest.push_back(r.vec(4));
+  d.proj_rest = r.vec(4);
+  d.pre_conv = conv1d(r);
+  d.in_w = r.vec(4); d.in_b = r.vec(4);
   n = r.u32();
   if (!r.bad && n > 4096) r.fail("bad decoder layer count");
-  for (uint32_t i = 0; i < n && !r.bad; ++i)
-    for (int j = 0; j < 11; ++j) r.vec(4);
-  r.vec(4); r.vec(4); r.vec(4);
+  for (uint32_t i = 0; i < n && !r.bad; ++i) {
+    HDecLayer L;
+    L.q = r.vec(4); L.k = r.vec(4); L.v = r.vec(4); L.o = r.vec(4);
+    L.gate = r.vec(4); L.up = r.vec(4); L.down = r.vec(4);
+    L.in_norm = r.vec(4); L.post_norm = r.vec(4); L.attn_scale = r.vec(4); L.mlp_scale = r.vec(4);
+    d.layers.push_back(L);
+  }
+  d.norm = r.vec(4); d.out_w = r.vec(4); d.out_b = r.vec(4);
   n = r.u32();
   if (!r.bad && n > 4096) r.fail("bad decoder upsample count");
   for (uint32_t i = 0; i < n && !r.bad; ++i) {
@@ -177,7 +188,7 @@ void skip_decoder(Reader& r) {
     skip_dw_conv(r);
     for (int j = 0; j < 7; ++j) r.vec(4);
   }
-  skip_conv1d(r);
+  conv1d(r);
   n = r.u32();
   if (!r.bad && n > 4096) r.fail("bad vocos block count");
   for (uint32_t i = 0; i < n && !r.bad; ++i) {
@@ -186,17 +197,18 @@ void skip_decoder(Reader& r) {
     const uint32_t nr = r.u32();
     if (!r.bad && nr > 4096) r.fail("bad vocos residual count");
     for (uint32_t j = 0; j < nr && !r.bad; ++j) {
-      r.vec(4); r.vec(4); skip_conv1d(r); r.vec(4); r.vec(4); skip_conv1d(r);
+      r.vec(4); r.vec(4); conv1d(r); r.vec(4); r.vec(4); conv1d(r);
     }
   }
   r.vec(4); r.vec(4);
-  skip_conv1d(r);
-  r.vec(4); r.vec(4);
+  conv1d(r);
+  d.rope_cos = r.vec(4); d.rope_sin = r.vec(4);
+  if (out && !r.bad) *out = std::move(d);
 }
 
 }  // namespace
 
-int parse_model(const char* path, HModel* out, std::string* err) {
+int parse_model(const char* path, HModel* out, std::string* err, HDecoder* dec) {
   File fh;
   fh.f = fopen(path, "rb");
   if (!fh.f) {
@@ -310,7 +322,7 @@ int parse_model(const char* path, HModel* out, std::string* err) {
     if (!r.bad && (m.p_cos.len != m.p_sin.len || m.p_cos.len % half)) r.fail("predictor rope table length mismatch");
     d.p_max_pos = r.bad ? 0 : (int)(m.p_cos.len / half);
   }
-  if (!r.bad) skip_decoder(r);
+  if (!r.bad) read_decoder(r, dec);
   if (r.bad) {
     if (err) *err = r.msg;
     return QTTS_ERR_FORMAT;
@@ -428,6 +440,17 @@ struct Writer {
     u64(v.size());
     bytes(v.data(), v.size() * 4);
   }
+  void gvec(uint64_t n, double mean, double sd) {  // write_f32_vec_io of mean + sd * N(0, 1)
+    uint64_t s = stream_seed(seed, ++id);
+    u64(n);
+    float* fb = reinterpret_cast<float*>(buf.data());
+    for (uint64_t done = 0; done < n;) {
+      const uint64_t m = n - done < buf.size() / 4 ? n - done : buf.size() / 4;
+      for (uint64_t i = 0; i < m; ++i) fb[i] = (float)(mean + sd * gauss(&s));
+      bytes(fb, m * 4);
+      done += m;
+    }
+  }
   void empty_vec() { u64(0); }
   void empty_conv1d() {
     for (int i = 0; i < 6; ++i) u32(0);
@@ -437,7 +460,8 @@ struct Writer {
 };
 
 // rope.rs:11-41 (talker, sections) and loader.rs:399-408 (predictor).
-void rope_tables(int hd, int max_pos, const int* sec, int nsec, std::vector<float>& c, std::vector<float>& s) {
+void rope_tables(int hd, int max_pos, const int* sec, int nsec, std::vector<float>& c, std::vector<float>& s,
+                 double theta = 1000000.0) {
   const int half = hd / 2;
   c.assign((size_t)max_pos * half, 0.0f);
   s.assign((size_t)max_pos * half, 0.0f);
@@ -445,7 +469,7 @@ void rope_tables(int hd, int max_pos, const int* sec, int nsec, std::vector<floa
   for (int q = 0; q < nsec; ++q) {
     for (int i = 0; i < sec[q]; ++i) {
       const int dd = off + i;
-      const double freq = 1.0 / pow(1000000.0, (double)(2 * dd) / (double)hd);
+      const double freq = 1.0 / pow(theta, (double)(2 * dd) / (double)hd);
       for (int p = 0; p < max_pos; ++p) {
         const double a = (double)p * freq;
         c[(size_t)p * half + dd] = (float)cos(a);
@@ -475,7 +499,50 @@ void dims_tiny(qtts_dims* d) {
   d->p_inter = 512; d->p_vocab = 2048; d->p_groups = 15; d->p_max_pos = 64; d->fmt = 1;
 }
 
-int synth_write(const char* path, const qtts_dims& d, uint64_t seed, std::string* err) {
+// The synthetic speech decoder (decoder.rs:21-108 shapes of the 12 Hz
+// tokenizer's decoder): 16 codebooks of 2048 x 256, hidden 512, 16 heads of 64,
+// MLP 1024, window 72, 8 layers, latent 1024, RoPE theta 10000 over 8192
+// positions.  Values: codebooks N(0, 1); projections N(0, 1/fan_in); biases
+// N(0, 0.02); norm weights 1 + N(0, 0.1); layer scales 0.05 + N(0, 0.01).
+constexpr uint32_t kDecHidden = 512, kDecHeads = 16, kDecHeadDim = 64, kDecInter = 1024, kDecWindow = 72,
+                   kDecCbDim = 256, kDecEntries = 2048, kDecLayers = 8, kDecLatent = 1024, kDecRopePos = 8192;
+void write_decoder(Writer& w) {
+  const uint32_t H = kDecHidden, A = kDecHeads * kDecHeadDim;
+  w.u32(H); w.u32(kDecHeads); w.u32(kDecHeadDim); w.u32(kDecInter); w.u32(kDecWindow); w.u32(kDecCbDim);
+  w.gvec((uint64_t)kDecEntries * kDecCbDim, 0.0, 1.0);
+  w.gvec((uint64_t)kDecCbDim * 512, 0.0, 1.0 / sqrt((double)kDecCbDim));
+  w.u32(15);
+  for (int g = 0; g < 15; ++g) w.gvec((uint64_t)kDecEntries * kDecCbDim, 0.0, 1.0);
+  w.gvec((uint64_t)kDecCbDim * 512, 0.0, 1.0 / sqrt((double)kDecCbDim));
+  // pre-conv: CausalConv1d(512 -> 1024, k = 3), weight [out][in][k]
+  w.u32(512); w.u32(kDecLatent); w.u32(3); w.u32(1); w.u32(0); w.u32(1);
+  w.gvec((uint64_t)kDecLatent * 512 * 3, 0.0, 1.0 / sqrt(512.0 * 3.0));
+  w.gvec(kDecLatent, 0.0, 0.02);
+  w.gvec((uint64_t)kDecLatent * H, 0.0, 1.0 / sqrt((double)kDecLatent));
+  w.gvec(H, 0.0, 0.02);
+  w.u32(kDecLayers);
+  for (uint32_t l = 0; l < kDecLayers; ++l) {
+    for (int m = 0; m < 3; ++m) w.gvec((uint64_t)H * A, 0.0, 1.0 / sqrt((double)H));  // q, k, v
+    w.gvec((uint64_t)A * H, 0.0, 1.0 / sqrt((double)A));                             // o
+    w.gvec((uint64_t)H * kDecInter, 0.0, 1.0 / sqrt((double)H));                     // gate
+    w.gvec((uint64_t)H * kDecInter, 0.0, 1.0 / sqrt((double)H));                     // up
+    w.gvec((uint64_t)kDecInter * H, 0.0, 1.0 / sqrt((double)kDecInter));             // down
+    w.gvec(H, 1.0, 0.1); w.gvec(H, 1.0, 0.1);                                         // norms
+    w.gvec(H, 0.05, 0.01); w.gvec(H, 0.05, 0.01);                                     // layer scales
+  }
+  w.gvec(H, 1.0, 0.1);
+  w.gvec((uint64_t)H * kDecLatent, 0.0, 1.0 / sqrt((double)H));
+  w.gvec(kDecLatent, 0.0, 0.02);
+  w.u32(0);                      // no upsample stages
+  w.empty_conv1d(); w.u32(0);    // no Vocos stages
+  w.empty_vec(); w.empty_vec(); w.empty_conv1d();
+  const int sec1[1] = {(int)kDecHeadDim / 2};
+  std::vector<float> c, s;
+  rope_tables((int)kDecHeadDim, (int)kDecRopePos, sec1, 1, c, s, 10000.0);
+  w.f32vec(c); w.f32vec(s);
+}
+
+int synth_write(const char* path, const qtts_dims& d, uint64_t seed, std::string* err, bool with_decoder) {
   if (d.t_layers <= 0 || d.p_layers <= 0 || d.t_heads % d.t_kv_heads || d.p_heads % d.p_kv_heads ||
       d.t_hidden % 32 || d.p_hidden % 32 || d.t_inter % 32 || d.p_inter % 32 || d.t_vocab % 32 || d.p_vocab % 32 ||
       (d.fmt != 0 && d.fmt != 1) || d.t_sec[0] + d.t_sec[1] + d.t_sec[2] != d.t_head_dim / 2) {
@@ -544,16 +611,20 @@ int synth_write(const char* path, const qtts_dims& d, uint64_t seed, std::string
     rope_tables(d.p_head_dim, d.p_max_pos, sec1, 1, c, s);
     w.f32vec(c); w.f32vec(s);
   }
-  // empty speech-decoder section (save.rs:171-256 layout)
-  for (int i = 0; i < 6; ++i) w.u32(0);
-  w.empty_vec(); w.empty_vec(); w.u32(0); w.empty_vec();
-  w.empty_conv1d();
-  w.empty_vec(); w.empty_vec(); w.u32(0);
-  w.empty_vec(); w.empty_vec(); w.empty_vec();
-  w.u32(0);
-  w.empty_conv1d(); w.u32(0);
-  w.empty_vec(); w.empty_vec(); w.empty_conv1d();
-  w.empty_vec(); w.empty_vec();
+  if (with_decoder) {
+    write_decoder(w);
+  } else {
+    // empty speech-decoder section (save.rs:171-256 layout)
+    for (int i = 0; i < 6; ++i) w.u32(0);
+    w.empty_vec(); w.empty_vec(); w.u32(0); w.empty_vec();
+    w.empty_conv1d();
+    w.empty_vec(); w.empty_vec(); w.u32(0);
+    w.empty_vec(); w.empty_vec(); w.empty_vec();
+    w.u32(0);
+    w.empty_conv1d(); w.u32(0);
+    w.empty_vec(); w.empty_vec(); w.empty_conv1d();
+    w.empty_vec(); w.empty_vec();
+  }
   if (fflush(fh.f) != 0) w.bad = true;
   if (w.bad) {
     if (err) *err = "write failed";

@@ -35,10 +35,33 @@ struct HModel {
   uint64_t file_size = 0;
 };
 
+// The speech decoder's codebook / pre-conv / transformer part of the decoder
+// section (save.rs:446-552 load_decoder_weights; decoder.rs:21-108 shapes):
+// payload offsets of its f32 vectors, the rest of the section walked only.
+struct HConv1d {
+  uint32_t in = 0, out = 0, k = 0, stride = 0, pad = 0, dil = 0;
+  HVec w, b;
+};
+struct HDecLayer {
+  HVec q, k, v, o, gate, up, down, in_norm, post_norm, attn_scale, mlp_scale;
+};
+struct HDecoder {
+  uint32_t hidden = 0, heads = 0, head_dim = 0, inter = 0, window = 0, cb_dim = 0;
+  HVec cb0, proj0, proj_rest;
+  std::vector<HVec> cb_rest;
+  HConv1d pre_conv;
+  HVec in_w, in_b, norm, out_w, out_b, rope_cos, rope_sin;
+  std::vector<HDecLayer> layers;
+};
+
 // Parse the talker and predictor sections, checking every length against the
-// header dimensions.  Returns QTTS_OK or QTTS_ERR_IO / QTTS_ERR_FORMAT.
-int parse_model(const char* path, HModel* out, std::string* err);
-int synth_write(const char* path, const qtts_dims& d, uint64_t seed, std::string* err);
+// header dimensions (and, with `dec`, record the decoder's tensors).  Returns
+// QTTS_OK or QTTS_ERR_IO / QTTS_ERR_FORMAT.
+int parse_model(const char* path, HModel* out, std::string* err, HDecoder* dec = nullptr);
+// with_decoder: a full-size synthetic speech decoder (codebooks, pre-conv,
+// transformer, RoPE tables; upsample and Vocos stages empty) instead of an
+// empty decoder section.
+int synth_write(const char* path, const qtts_dims& d, uint64_t seed, std::string* err, bool with_decoder = false);
 void dims_1p7b(qtts_dims* d);
 void dims_tiny(qtts_dims* d);
 

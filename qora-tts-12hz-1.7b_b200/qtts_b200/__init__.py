@@ -72,6 +72,13 @@ def _load():
         "qtts_version": (C.c_int, []),
         "qtts_file_probe": (C.c_int, [C.c_char_p, C.POINTER(Dims)]),
         "qtts_synth_write": (C.c_int, [C.c_char_p, C.POINTER(Dims), C.c_uint64]),
+        "qtts_synth_write_ex": (C.c_int, [C.c_char_p, C.POINTER(Dims), C.c_uint64, C.c_uint]),
+        "qtts_decoder_load": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(P)]),
+        "qtts_decoder_free": (C.c_int, [P]),
+        "qtts_decoder_stream": (P, [P]),
+        "qtts_decode_latent": (C.c_int, [P, C.POINTER(C.c_uint32), C.c_int, C.POINTER(C.c_float)]),
+        "qtts_decode_latent_dev": (C.c_int, [P, P, C.c_int, P]),
+        "qtts_decoder_sync": (C.c_int, [P]),
         "qtts_dims_1p7b": (None, [C.POINTER(Dims)]),
         "qtts_dims_tiny": (None, [C.POINTER(Dims)]),
         "qtts_model_load": (C.c_int, [C.c_char_p, C.c_int, C.POINTER(P)]),
@@ -148,6 +155,56 @@ def dims_tiny() -> Dims:
 def synth_write(path: str, dims: Dims, seed: int = 0) -> None:
     """Seeded synthetic model in the save.rs layout (save.rs:23-137)."""
     _check(lib.qtts_synth_write(path.encode(), C.byref(dims), seed))
+
+
+SYNTH_DECODER = 1  # qtts.h QTTS_SYNTH_DECODER
+
+
+def synth_write_with_decoder(path: str, dims: Dims, seed: int = 0) -> None:
+    """The synthetic model with a full-size speech decoder section
+    (qtts.h qtts_synth_write_ex / QTTS_SYNTH_DECODER)."""
+    _check(lib.qtts_synth_write_ex(path.encode(), C.byref(dims), seed, SYNTH_DECODER))
+
+
+class Decoder:
+    """The speech decoder's first stage on the GPU (decoder.rs:142-335 with
+    the conv.rs:114-191 pre-conv): 16 code streams of T frames -> the
+    transformer output [1024][T] (qtts.h qtts_decode_latent)."""
+
+    def __init__(self, path: str, device: int = 0):
+        h = C.c_void_p()
+        _check(lib.qtts_decoder_load(path.encode(), device, C.byref(h)))
+        self.h = h
+
+    @property
+    def stream(self) -> int:
+        return lib.qtts_decoder_stream(self.h) or 0
+
+    def decode_latent(self, codes) -> np.ndarray:
+        codes = np.ascontiguousarray(codes, dtype=np.uint32)
+        if codes.ndim != 2 or codes.shape[0] != 16:
+            raise QttsError(ERR_BADARG, f"codes must be [16][T], got {codes.shape}")
+        T = codes.shape[1]
+        out = np.empty((1024, T), np.float32)
+        _check(lib.qtts_decode_latent(self.h, codes.ctypes.data_as(C.POINTER(C.c_uint32)), T,
+                                      out.ctypes.data_as(C.POINTER(C.c_float))))
+        return out
+
+    def decode_latent_dev(self, codes_ptr: int, n_frames: int, out_ptr: int) -> None:
+        """Device buffers (codes [16][T] u32, out [1024][T] f32), async on
+        the decoder's stream; errors of the launch itself only."""
+        _check(lib.qtts_decode_latent_dev(self.h, C.c_void_p(codes_ptr), n_frames, C.c_void_p(out_ptr)))
+
+    def sync(self) -> None:
+        _check(lib.qtts_decoder_sync(self.h))
+
+    def close(self):
+        if getattr(self, "h", None) and lib is not None:  # (lib is None at interpreter exit)
+            lib.qtts_decoder_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
 
 
 def file_probe(path: str) -> Dims:

@@ -8,6 +8,8 @@ config 3: 96 prompt ids, T=0.8, top_k=50, rng seed 42, 2000 frames
 config 4: 64 utterances, prompt lengths ~U[16, 256], own voice and seed each,
           T=0.8, top_k=50, 500 frames
 config 5: 512 utterances from the config-4 generator, 64 per GPU
+decoder:  16 code streams of T frames ~U[0, 2048) (the speech decoder's
+          first stage; T = 500, an utterance of config 4/5)
 """
 from __future__ import annotations
 
@@ -15,7 +17,7 @@ import os
 
 import numpy as np
 
-from . import Dims, dims_1p7b, dims_tiny, file_probe, make_params, synth_write
+from . import Dims, dims_1p7b, dims_tiny, file_probe, make_params, synth_write, synth_write_with_decoder
 
 TEXT_VOCAB = 151936
 LANG_ENGLISH = 2050  # config.json codec_language_id.english
@@ -23,13 +25,18 @@ MODEL_DIR = os.environ.get("QTTS_MODEL_DIR", "/tmp/qtts_models")
 
 
 def model_path(kind: str = "1p7b", seed: int = 0) -> str:
-    """Path of the seeded synthetic model, written on first use."""
+    """Path of the seeded synthetic model, written on first use: "1p7b",
+    "tiny", or "decoder" (the tiny talker/predictor with a full-size speech
+    decoder section)."""
     os.makedirs(MODEL_DIR, exist_ok=True)
     path = os.path.join(MODEL_DIR, f"qtts_{kind}_seed{seed}.qora-tts")
     if not os.path.exists(path):
         d: Dims = dims_1p7b() if kind == "1p7b" else dims_tiny()
         tmp = path + f".tmp{os.getpid()}"
-        synth_write(tmp, d, seed)
+        if kind == "decoder":
+            synth_write_with_decoder(tmp, d, seed)
+        else:
+            synth_write(tmp, d, seed)
         os.replace(tmp, path)
     file_probe(path)
     return path
@@ -71,3 +78,8 @@ def config5_shard(rank: int, world: int, total: int = 512, hidden: int = 2048):
     utts, frames = config4(total, hidden)
     per = (total + world - 1) // world
     return utts[rank * per:(rank + 1) * per], frames
+
+
+def decoder_codes(T: int, seed: int = 700) -> np.ndarray:
+    """16 code streams of T frames, uniform over the 2048-entry codebooks."""
+    return np.random.default_rng(seed).integers(0, 2048, size=(16, T), dtype=np.int64).astype(np.uint32)
