@@ -1,7 +1,7 @@
 """Benchmark of the QORA-TTS 1.7B per-frame codec decode loop on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload config5|config1|config2|config3|config4] [--full-prompt]
+                    [--workload config5|config1|config2|config3|config4|decoder] [--full-prompt]
 
 One step = one frame of the hot path (code-0 sample, 15-group predictor
 expansion, frame-input fusion, 28-layer talker step, codec head) for every
@@ -22,6 +22,10 @@ timed on every rank as the line's `batch1` sub-record.
 --impl reference times the CPU oracle (a line-faithful C restatement of the
 Rust reference, which cannot be built here) on the host cores, one frame per
 step at the same cache length.
+
+--workload decoder times the speech decoder's first stage instead (16-code
+lookup, causal pre-conv, 8-layer windowed transformer; decoder.rs:142-335):
+one step = one 500-frame utterance, metric "decoder frames/sec".
 """
 from __future__ import annotations
 
@@ -45,6 +49,8 @@ METRIC = "codec frames/sec"
 PEAKS_PATH = os.path.join(REPO, "MEASURED_PEAKS.json")
 MODEL_DIR = os.environ.get("QTTS_MODEL_DIR", "/tmp/qtts_models")
 MODEL_1P7B = os.path.join(MODEL_DIR, "qtts_1p7b_seed0.qora-tts")
+DEC_T = 500  # frames of one utterance (configs 4 / 5) through the decoder's first stage
+DEC_LAYERS, DEC_WINDOW = 8, 72
 KV_BYTES_PER_POS = 28 * 8 * 128 * 2 * 4  # talker K+V read per cached position, f32
 WAVE = 64  # utterances of one session (config 4: 64 concurrent utterances per GPU)
 # config 5 (512 utterances over the GPUs): a GPU's share runs as sessions of
@@ -206,6 +212,48 @@ def _oracle_model_path():
     return MODEL_1P7B
 
 
+def _oracle_decoder_path():
+    """The synthetic model with the full-size decoder (workload "decoder"),
+    written by the oracle's own writer when absent (byte-identical to the
+    library's)."""
+    from oracle import oracle as O
+    os.makedirs(MODEL_DIR, exist_ok=True)
+    path = os.path.join(MODEL_DIR, "qtts_decoder_seed0.qora-tts")
+    if not os.path.exists(path):
+        tmp = path + f".tmp{os.getpid()}"
+        O.synth_write_with_decoder(tmp, O.dims_tiny(), 0)
+        os.replace(tmp, path)
+    return path
+
+
+def run_reference_decoder(args):
+    """--impl reference --workload decoder: the oracle's restatement of the
+    stage on one host thread (the reference's f32_gemv is single-threaded),
+    over a 50-frame sample of the 500-frame utterance per step."""
+    import numpy as np
+    from oracle import oracle as O
+    n = 50
+    codes = np.random.default_rng(700).integers(0, 2048, size=(16, DEC_T), dtype=np.int64).astype(np.uint32)
+    d = O.Decoder(_oracle_decoder_path())
+    d.decode_latent(np.ascontiguousarray(codes[:, :n]))
+    t = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        d.decode_latent(np.ascontiguousarray(codes[:, :n]))
+        t.append(time.perf_counter() - t0)
+    d.close()
+    v = n / (sum(t) / len(t))
+    line = {"metric": "decoder frames/sec", "value": v, "unit": "frames/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(t) / len(t),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"decoder: the stage over the first {n} of {DEC_T} frames per step, one CPU "
+                                   f"thread"},
+            "cpu_baseline": {"value": v, "unit": "frames/s", "cores": 1, "kind": "port",
+                             "sample": f"{n} frames per step, {args.steps} steps"},
+            "e2e": {"value": v, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
 def cpu_baseline_measure(kv_len, frames, budget_s=15.0):
     """The oracle's frame step (talker + predictor + sampler of one utterance)
     at cache length kv_len on all host cores, for a bounded sample."""
@@ -229,6 +277,9 @@ def run_reference(args, rank, world):
     """--impl reference: the oracle's frame step on the host cores, one frame
     per step, at the cache length of the GPU arm's timed window."""
     if rank != 0:
+        return
+    if args.workload == "decoder":
+        run_reference_decoder(args)
         return
     from oracle import oracle as O
     start = timed_window(args.workload, args.steps, args.warmup)
@@ -365,6 +416,93 @@ def run_config2(args, Q, torch, peak, peak_kind):
 
 # ---------------------------------------------------------------------------
 # frame workloads
+
+def decoder_flops(T, window=DEC_WINDOW):
+    """Useful FLOPs of the decoder's first stage over T frames: the GEMMs
+    (codebook projections, the 3-tap pre-conv, input projection, per layer
+    q|k|v, o, gate|up, down, output projection) and the windowed attention."""
+    gemm = 2 * (2 * 256 * 512 + 1536 * 1024 + 1024 * 512
+                + DEC_LAYERS * (512 * 3072 + 1024 * 512 + 512 * 2048 + 1024 * 512) + 512 * 1024)
+    att = sum(min(t + 1, window) for t in range(T)) * DEC_LAYERS * 16 * 64 * 2 * 2
+    return gemm * T + att
+
+
+def run_decoder(args, rank, world, local, Q, W, torch):
+    """The speech decoder's first stage (codes -> transformer output,
+    decoder.rs:142-335 with the conv.rs:114-191 pre-conv): one step = one
+    utterance of DEC_T frames, on device buffers; e2e through the public
+    qtts_decode_latent with host codes in and the host latent out."""
+    import numpy as np
+    T = DEC_T
+    if rank == 0:
+        W.model_path("decoder")
+    barrier(world)
+    dec = Q.Decoder(W.model_path("decoder"), local)
+    codes_h = W.decoder_codes(T, seed=700 + rank)
+    codes = torch.from_numpy(codes_h.astype(np.int32)).cuda()
+    out = torch.empty((1024, T), dtype=torch.float32, device="cuda")
+    st = torch.cuda.ExternalStream(dec.stream)
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        dec.decode_latent_dev(codes.data_ptr(), T, out.data_ptr())
+    dec.sync()
+    clocks = ClockSampler(local)
+    clocks.start()
+    time.sleep(0.2)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(args.steps):
+        dec.decode_latent_dev(codes.data_ptr(), T, out.data_ptr())
+    e1.record(st)
+    dec.sync()
+    torch.cuda.synchronize()
+    barrier(world)
+    clk = clocks.stop()
+    ms = reduce_over_ranks(e0.elapsed_time(e1) / args.steps, "max")
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        dec.decode_latent(codes_h)
+    e2e_s = reduce_over_ranks((time.perf_counter() - t0) / args.steps, "max")
+    dec.close()
+    flops = decoder_flops(T)
+    fp32_peak = 148 * 128 * 2 * 1.965e9 / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+        n = 50
+        od = O.Decoder(W.model_path("decoder"))
+        t0 = time.perf_counter()
+        od.decode_latent(np.ascontiguousarray(codes_h[:, :n]))
+        dt = time.perf_counter() - t0
+        od.close()
+        cpu = {"value": n / dt, "unit": "frames/s", "cores": 1, "kind": "port",
+               "sample": f"the oracle's restatement of the stage (decoder.rs:142-335, conv.rs:114-191) over "
+                         f"the first {n} frames, one thread (the reference's f32_gemv is single-threaded; its "
+                         f"conv threads by output channel)", "wall_s": dt}
+    line = {
+        "metric": "decoder frames/sec", "value": world * T / (ms / 1e3), "unit": "frames/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"decoder: speech decoder first stage (16-codebook lookup, causal pre-conv "
+                               f"512->1024, 8-layer transformer, window 72) over one utterance of {T} frames "
+                               f"per step and GPU, synthetic full-size decoder weights (157 MB f32)",
+                   "frames_per_step": T, "l2": "weights (157 MB) larger than L2, streamed every step",
+                   "parallelism": f"{world} independent replicas"},
+        "roofline": {"bound": "fp32 pipe (CUDA-core GEMMs)", "achieved": flops / (ms / 1e3) / 1e12,
+                     "peak": fp32_peak, "unit": "TFLOP/s", "frac": flops / (ms / 1e3) / 1e12 / fp32_peak,
+                     "traffic": None, "peak_kind": "nominal FP32 (148 SMs x 128 FMA x 2 x 1965 MHz)",
+                     "algorithmic_flops_per_step": flops},
+        "cpu_baseline": cpu,
+        "e2e": {"value": world * T / e2e_s, "unit": "frames/s", "h2d_bytes_per_step": 16 * T * 4,
+                "d2h_bytes_per_step": 1024 * T * 4},
+        "gpu_launches": (1 + 37 + 17 + 3 * DEC_LAYERS) * args.steps,
+        "clocks": clk,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
 
 def workload_utts(args, rank, world, W):
     if args.workload == "config1":
@@ -592,7 +730,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="config5", choices=["config1", "config2", "config3", "config4", "config5"])
+    ap.add_argument("--workload", default="config5",
+                    choices=["config1", "config2", "config3", "config4", "config5", "decoder"])
     ap.add_argument("--only", default="", help="config2: one case, KxNxM")
     ap.add_argument("--lanes", type=int, default=None,
                     help=f"frame workloads: waves run side by side (event chains); config5 {LANES5}, else 1")
@@ -632,6 +771,12 @@ def main():
     if args.workload == "config2":
         if rank == 0:
             run_config2(args, Q, torch, peak, peak_kind)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
+    if args.workload == "decoder":
+        run_decoder(args, rank, world, local, Q, W, torch)
         if world > 1:
             import torch.distributed as dist
             dist.destroy_process_group()

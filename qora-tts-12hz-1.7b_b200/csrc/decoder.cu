@@ -22,7 +22,8 @@
 //   rmsnorm, gemm   out^T = norm(x) * W_out + b_out
 //
 // Arithmetic is f32 throughout (the weights are f32 in the file).  The
-// GEMM is a CUDA-core tiled kernel (64 x 64 tiles, 4 x 4 per thread), its
+// GEMM is a CUDA-core tiled kernel (64 x 64 tiles, 4 x 4 per thread,
+// double-buffered 32-deep K steps), its
 // accumulation starting from the bias as f32_gemv_bias does; attention
 // keeps the reference's summation orders (sequential dot products, the
 // softmax sum in position order, the weighted V sum in position order).
@@ -41,7 +42,7 @@ namespace qtts {
 
 namespace {
 
-constexpr int kBM = 64, kBN = 64, kBK = 16, kGemmThreads = 256;
+constexpr int kBM = 64, kBN = 64, kBK = 32, kGemmThreads = 256;
 constexpr int kDecMaxWindow = 128;  // attention window held in shared memory
 constexpr int kDecGroups = 16;      // codebooks per frame (1 + 15)
 constexpr unsigned kDecErrCode = 1u;
@@ -60,9 +61,14 @@ struct DecGemm {
   int trans;  // store at C[n * ldc + m]
 };
 
+// One 64 x 64 output tile per CTA, 4 x 4 per thread.  K runs in 32-deep
+// steps through two shared-memory buffers: the next step's A and B tiles are
+// loaded into registers before this step's FMAs and stored into the other
+// buffer after them, so each step's global round trip overlaps the math of
+// the step before.
 __global__ void __launch_bounds__(kGemmThreads) dec_gemm_kernel(const DecGemm g) {
-  __shared__ __align__(16) float As[kBK][kBM + 4];
-  __shared__ __align__(16) float Bs[kBK][kBN];
+  __shared__ __align__(16) float As[2][kBK][kBM + 4];
+  __shared__ __align__(16) float Bs[2][kBK][kBN];
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
   float acc[4][4];
@@ -73,11 +79,13 @@ __global__ void __launch_bounds__(kGemmThreads) dec_gemm_kernel(const DecGemm g)
 #pragma unroll
     for (int i = 0; i < 4; ++i) acc[i][j] = b0;
   }
-  const int ar = tid >> 2, ac = (tid & 3) * 4;   // A tile: row ar, k chunk ac
-  const int br = tid >> 4, bc = (tid & 15) * 4;  // B tile: k row br, column chunk bc
-  for (int k0 = 0; k0 < g.K; k0 += kBK) {
-    {
-      const int m = m0 + ar, kk = k0 + ac;
+  const int ar = tid >> 3, ac = (tid & 7) * 4;   // A tile: rows ar, ar + 32; k chunk ac
+  const int br = tid >> 4, bc = (tid & 15) * 4;  // B tile: k rows br, br + 16; column chunk bc
+  float4 ra[2], rb[2];
+  auto load = [&](int k0) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int m = m0 + ar + 32 * h, kk = k0 + ac;
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
       if (m < g.M && kk < g.K) {
         long row = m;
@@ -88,28 +96,40 @@ __global__ void __launch_bounds__(kGemmThreads) dec_gemm_kernel(const DecGemm g)
         }
         if (row >= 0) v = *reinterpret_cast<const float4*>(g.A + row * g.lda + col);
       }
-      As[ac + 0][ar] = v.x;
-      As[ac + 1][ar] = v.y;
-      As[ac + 2][ar] = v.z;
-      As[ac + 3][ar] = v.w;
+      ra[h] = v;
+      const int kb = k0 + br + 16 * h, n = n0 + bc;
+      rb[h] = (kb < g.K && n < g.N) ? *reinterpret_cast<const float4*>(g.B + (long)kb * g.N + n)
+                                    : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    {
-      const int kk = k0 + br, n = n0 + bc;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (kk < g.K && n < g.N) v = *reinterpret_cast<const float4*>(g.B + (long)kk * g.N + n);
-      *reinterpret_cast<float4*>(&Bs[br][bc]) = v;
+  };
+  auto store = [&](int buf) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      As[buf][ac + 0][ar + 32 * h] = ra[h].x;
+      As[buf][ac + 1][ar + 32 * h] = ra[h].y;
+      As[buf][ac + 2][ar + 32 * h] = ra[h].z;
+      As[buf][ac + 3][ar + 32 * h] = ra[h].w;
+      *reinterpret_cast<float4*>(&Bs[buf][br + 16 * h][bc]) = rb[h];
     }
-    __syncthreads();
+  };
+  const int nk = (g.K + kBK - 1) / kBK;
+  load(0);
+  store(0);
+  __syncthreads();
+  for (int kt = 0; kt < nk; ++kt) {
+    const int buf = kt & 1;
+    if (kt + 1 < nk) load((kt + 1) * kBK);
 #pragma unroll
     for (int kk = 0; kk < kBK; ++kk) {
-      const float4 a = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
-      const float4 b = *reinterpret_cast<const float4*>(&Bs[kk][tx * 4]);
+      const float4 a = *reinterpret_cast<const float4*>(&As[buf][kk][ty * 4]);
+      const float4 b = *reinterpret_cast<const float4*>(&Bs[buf][kk][tx * 4]);
       const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
     }
+    if (kt + 1 < nk) store(buf ^ 1);
     __syncthreads();
   }
 #pragma unroll
