@@ -206,63 +206,91 @@ __global__ void dec_rope_kernel(float* QKV, int T, int heads, int hd, const floa
   b[half + e] = x1 * c + x0 * s;
 }
 
-// causal sliding-window attention (decoder.rs:258-289), a warp per (frame,
-// head): lane j scores positions j, j + 32, ... of the window (sequential
-// 64-term dot products), lane 0 runs softmax_raw (gemv.rs:434-445) over them
-// in position order, then lane d accumulates dimensions d and d + 32 over the
-// positions in order.
+// causal sliding-window attention (decoder.rs:258-289).  A CTA takes
+// kAttnFrames consecutive frames of one head and stages the K and V rows of
+// their joint window (up to kAttnFrames + window - 1 positions) in shared
+// memory with coalesced row loads; K rows are padded to 65 floats so that
+// lanes reading different rows hit different banks.  Per frame (a warp
+// each, in turn): lane j scores positions j, j + 32, ... (sequential 64-term
+// dot products), lane 0 runs softmax_raw (gemv.rs:434-445) in position
+// order, then lane d accumulates dimensions d and d + 32 over the positions
+// in order.
+constexpr int kAttnFrames = 16;
+// floats of the padded K rows, rounded up to a multiple of 4 so that the V
+// rows after them start on a 16-byte boundary
+__host__ __device__ constexpr size_t attn_k_floats(int window) {
+  return ((size_t)(kAttnFrames + window - 1) * (64 + 1) + 3) & ~(size_t)3;
+}
 template <int HD>
 __global__ void __launch_bounds__(128) dec_attn_kernel(const float* QKV, int T, int heads, int window, float* out) {
   static_assert(HD == 64, "two dimensions per lane");
-  __shared__ float s_q[4][HD];
-  __shared__ float s_p[4][kDecMaxWindow];
+  extern __shared__ float sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long item = (long)blockIdx.x * 4 + warp;
-  if (item >= (long)T * heads) return;
-  const int t = (int)(item / heads), h = (int)(item % heads);
+  const int h = blockIdx.y, t0 = blockIdx.x * kAttnFrames;
+  const int t1 = min(T, t0 + kAttnFrames);  // frames [t0, t1)
+  const int w0 = t0 + 1 > window ? t0 + 1 - window : 0;  // first position any of them sees
+  const int nw = t1 - w0;                                 // positions [w0, t1)
+  const int rows = kAttnFrames + window - 1;               // the largest joint window
+  float* sK = sm;                                         // [rows][HD + 1]
+  float* sV = sK + attn_k_floats(window);                 // [rows][HD], 16-byte aligned (float4 stores)
+  float* sP = sV + (size_t)rows * HD;                     // [4][window]
+  float* sQ = sP + 4 * window;                            // [4][HD]
   const long ld = 3L * heads * HD;
-  const float* q = QKV + (size_t)t * ld + (size_t)h * HD;
-  s_q[warp][lane] = q[lane];
-  s_q[warp][lane + 32] = q[lane + 32];
-  __syncwarp();
-  const int start = t + 1 > window ? t + 1 - window : 0, L = t + 1 - start;
+  for (int i = threadIdx.x; i < nw * (HD / 4); i += blockDim.x) {
+    const int r = i / (HD / 4), c4 = i % (HD / 4);
+    const float* row = QKV + (size_t)(w0 + r) * ld + (size_t)h * HD;
+    const float4 k = *reinterpret_cast<const float4*>(row + (size_t)heads * HD + 4 * c4);
+    const float4 v = *reinterpret_cast<const float4*>(row + (size_t)2 * heads * HD + 4 * c4);
+    float* kd = sK + (size_t)r * (HD + 1) + 4 * c4;
+    kd[0] = k.x; kd[1] = k.y; kd[2] = k.z; kd[3] = k.w;
+    *reinterpret_cast<float4*>(sV + (size_t)r * HD + 4 * c4) = v;
+  }
+  __syncthreads();
   const float scale = 1.0f / sqrtf((float)HD);
-  for (int s = lane; s < L; s += 32) {
-    const float* k = QKV + (size_t)(start + s) * ld + (size_t)heads * HD + (size_t)h * HD;
-    float dot = 0.0f;
-#pragma unroll
-    for (int e4 = 0; e4 < HD / 4; ++e4) {
-      const float4 kv = *reinterpret_cast<const float4*>(k + 4 * e4);
-      dot += s_q[warp][4 * e4] * kv.x;
-      dot += s_q[warp][4 * e4 + 1] * kv.y;
-      dot += s_q[warp][4 * e4 + 2] * kv.z;
-      dot += s_q[warp][4 * e4 + 3] * kv.w;
+  float* p = sP + warp * window;
+  float* qs = sQ + warp * HD;
+  for (int t = t0 + warp; t < t1; t += 4) {
+    const float* q = QKV + (size_t)t * ld + (size_t)h * HD;
+    qs[lane] = q[lane];
+    qs[lane + 32] = q[lane + 32];
+    __syncwarp();
+    const int start = t + 1 > window ? t + 1 - window : 0, L = t + 1 - start;
+    for (int s = lane; s < L; s += 32) {
+      const float* k = sK + (size_t)(start + s - w0) * (HD + 1);
+      float dot = 0.0f;
+#pragma unroll 16
+      for (int e = 0; e < HD; ++e) dot += qs[e] * k[e];
+      p[s] = dot * scale;
     }
-    s_p[warp][s] = dot * scale;
-  }
-  __syncwarp();
-  if (lane == 0) {
-    float mx = -INFINITY;
-    for (int s = 0; s < L; ++s) mx = fmaxf(mx, s_p[warp][s]);
-    float sum = 0.0f;
+    __syncwarp();
+    if (lane == 0) {
+      float mx = -INFINITY;
+      for (int s = 0; s < L; ++s) mx = fmaxf(mx, p[s]);
+      float sum = 0.0f;
+      for (int s = 0; s < L; ++s) {
+        const float e = expf(p[s] - mx);
+        p[s] = e;
+        sum += e;
+      }
+      const float inv = 1.0f / sum;
+      for (int s = 0; s < L; ++s) p[s] *= inv;
+    }
+    __syncwarp();
+    float a0 = 0.0f, a1 = 0.0f;
     for (int s = 0; s < L; ++s) {
-      const float e = expf(s_p[warp][s] - mx);
-      s_p[warp][s] = e;
-      sum += e;
+      const float* v = sV + (size_t)(start + s - w0) * HD;
+      const float ps = p[s];
+      a0 += ps * v[lane];
+      a1 += ps * v[lane + 32];
     }
-    const float inv = 1.0f / sum;
-    for (int s = 0; s < L; ++s) s_p[warp][s] *= inv;
+    out[(size_t)t * heads * HD + (size_t)h * HD + lane] = a0;
+    out[(size_t)t * heads * HD + (size_t)h * HD + lane + 32] = a1;
+    __syncwarp();  // qs / p are rewritten for this warp's next frame
   }
-  __syncwarp();
-  float a0 = 0.0f, a1 = 0.0f;
-  for (int s = 0; s < L; ++s) {
-    const float* v = QKV + (size_t)(start + s) * ld + (size_t)2 * heads * HD + (size_t)h * HD;
-    const float p = s_p[warp][s];
-    a0 += p * v[lane];
-    a1 += p * v[lane + 32];
-  }
-  out[(size_t)t * heads * HD + (size_t)h * HD + lane] = a0;
-  out[(size_t)t * heads * HD + (size_t)h * HD + lane + 32] = a1;
+}
+size_t attn_smem(int window) {
+  return (attn_k_floats(window) + (size_t)(kAttnFrames + window - 1) * 64 + 4 * (size_t)window + 4 * 64) *
+         sizeof(float);
 }
 
 // the MLP's silu(gate) * up (decoder.rs:307-311) on a gate|up row
@@ -400,6 +428,9 @@ int decoder_load(const char* path, int device, Decoder* D) {
   D->window = hd.window; D->cb_dim = hd.cb_dim; D->entries = (uint32_t)entries;
   D->rope_len = (long)hd.rope_cos.len;
   if (cudaStreamCreateWithFlags(&D->st, cudaStreamNonBlocking) != cudaSuccess) return fail(QTTS_ERR_CUDA, "stream");
+  if (cudaFuncSetAttribute(dec_attn_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)attn_smem((int)hd.window)) != cudaSuccess)
+    return fail(QTTS_ERR_CUDA, "decoder attention shared memory");
   if (cudaMalloc(reinterpret_cast<void**>(&D->err), 4) != cudaSuccess) return fail(QTTS_ERR_OOM, "device allocation failed");
   D->allocs.push_back(D->err);
   cudaMemset(D->err, 0, 4);
@@ -531,8 +562,9 @@ int decode_dev(Decoder& D, const uint32_t* codes, int T, float* out) {
       ok(cudaGetLastError());
     }
     ++g_kernel_launches;
-    dec_attn_kernel<64><<<(unsigned)(((long)T * D.heads + 3) / 4), 128, 0, D.st>>>(D.qkv, T, (int)D.heads,
-                                                                                  (int)D.window, D.ao);
+    dec_attn_kernel<64><<<dim3((unsigned)((T + kAttnFrames - 1) / kAttnFrames), D.heads), 128, attn_smem((int)D.window),
+                          D.st>>>(
+        D.qkv, T, (int)D.heads, (int)D.window, D.ao);
     ok(cudaGetLastError());
     plain(D.ao, A, L.wo, H, D.x, nullptr, 2, L.attn_scale);
     ok(rms(D, D.x, T, H, L.post_norm, D.xn));
