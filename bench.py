@@ -128,6 +128,13 @@ class ClockSampler:
         except Exception:
             self.proc = None
 
+    def wait_first(self, timeout_s: float = 5.0):
+        """Block until nvidia-smi has printed its first sample (it takes a
+        moment to start), so that the timed region that follows is sampled."""
+        t0 = time.time()
+        while self.proc and not self.lines and time.time() - t0 < timeout_s:
+            time.sleep(0.02)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
@@ -448,7 +455,7 @@ def run_decoder(args, rank, world, local, Q, W, torch):
     dec.sync()
     clocks = ClockSampler(local)
     clocks.start()
-    time.sleep(0.2)
+    clocks.wait_first()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
@@ -580,7 +587,7 @@ def run_frames(args, rank, world, local, Q, W, torch, model, peak, peak_kind):
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
     clocks.start()
-    time.sleep(0.2)
+    clocks.wait_first()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier(world)
     torch.cuda.synchronize()
