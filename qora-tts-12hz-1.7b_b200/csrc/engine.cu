@@ -539,7 +539,7 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
       a.counters = s.acounters;
     }
     // o on split input rows (tensor cores, > 64 rows): the attention writes them
-    if (a.nsplit == 1 && s.xs_buf2 && tc_takes_split(o)) {
+    if (a.nsplit == 1 && s.xs_buf2 && tc_takes_split_from_producer(o)) {
       a.xs_out = s.xs_buf2;
       a.err_flag = s.err_flag;
       o.x_split_pre = s.xs_buf2;
@@ -579,7 +579,7 @@ static int add_layer(Session& s, std::vector<Op>& ops, const DLayer& L, const La
     RC(plan_gemv(s, gu));
     // down on split input rows: the gate/up epilogue writes them (its own
     // input rows come split from the other buffer)
-    if (gu.tc && s.xs_buf2 && tc_takes_split(dn)) {
+    if (gu.tc && s.xs_buf2 && tc_takes_split_from_producer(dn)) {
       gu.xs_out = s.xs_buf2;
       gu.xs_out_k = io.inter;
       dn.x_split_pre = s.xs_buf2;

@@ -327,6 +327,7 @@ struct AttnDesc {
 constexpr double kAttnPrefetchMaxBytes = 48.0 * (1 << 20);
 cudaError_t launch_attention(const AttnDesc& d, cudaStream_t st);
 bool tc_takes_split(const GemvDesc& d);
+bool tc_takes_split_from_producer(const GemvDesc& d);
 bool tc_reads_expanded(const GemvDesc& d);
 size_t tc_xsplit_scratch_bytes(int M, int k);
 
