@@ -32,6 +32,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <algorithm>
 #include <vector>
 
 #include "engine.h"
@@ -45,7 +46,7 @@ namespace {
 constexpr int kBM = 64, kBN = 64, kBK = 32, kGemmThreads = 256;
 constexpr int kDecMaxWindow = 128;  // attention window held in shared memory
 constexpr int kDecGroups = 16;      // codebooks per frame (1 + 15)
-constexpr unsigned kDecErrCode = 1u;
+constexpr unsigned kDecErrCode = 1u;  // err bit of a bad code (the projection kernel sets bits 4 and 8)
 
 struct DecGemm {
   const float* A;
@@ -293,6 +294,13 @@ size_t attn_smem(int window) {
          sizeof(float);
 }
 
+// the layer-scaled residual (decoder.rs:286-288, 313-315): x += y * scale
+__global__ void dec_scale_add_kernel(float* X, const float* Y, const float* scale, int T, int n) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)T * n) return;
+  X[i] += Y[i] * scale[i % n];
+}
+
 // the MLP's silu(gate) * up (decoder.rs:307-311) on a gate|up row
 __global__ void dec_swiglu_kernel(const float* GU, int T, int I, float* Hout) {
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -317,6 +325,7 @@ cudaError_t gemm(cudaStream_t st, const DecGemm& g) {
 
 struct DecLayerDev {
   float *wqkv, *wo, *wgu, *wdown, *in_norm, *post_norm, *attn_scale, *mlp_scale;
+  Q4Mat tqkv, to, tg, tu, td;  // the same weights as tensor-core operand tiles (wx)
 };
 struct Decoder {
   int device = 0;
@@ -327,10 +336,14 @@ struct Decoder {
   float *pre_w = nullptr, *pre_b = nullptr, *in_w = nullptr, *in_b = nullptr;
   float *norm = nullptr, *out_w = nullptr, *out_b = nullptr, *rope_cos = nullptr, *rope_sin = nullptr;
   std::vector<DecLayerDev> layers;
+  bool tc = false;  // the layer projections run on the tensor cores (T >= kTcMinRows)
+  Q4Mat tin;        // input projection tiles
   // grow-only scratch for T frames
   int cap_T = 0;
   float *E0 = nullptr, *S = nullptr, *vq = nullptr, *pre = nullptr, *x = nullptr, *xn = nullptr, *qkv = nullptr,
-        *ao = nullptr, *gu = nullptr, *h = nullptr;
+        *ao = nullptr, *gu = nullptr, *h = nullptr, *tmp = nullptr;
+  uint8_t* xs = nullptr;  // split input rows of the tensor-core projections
+  size_t xs_bytes = 0;
   uint32_t* codes = nullptr;
   float* out = nullptr;
   int cap_io = 0;
@@ -340,7 +353,7 @@ struct Decoder {
     if (st) cudaStreamSynchronize(st);
     for (void* p : allocs)
       if (p) cudaFree(p);
-    cudaFree(E0); cudaFree(codes); cudaFree(out);
+    cudaFree(E0); cudaFree(xs); cudaFree(codes); cudaFree(out);
     if (st) cudaStreamDestroy(st);
   }
 };
@@ -439,6 +452,10 @@ int decoder_load(const char* path, int device, Decoder* D) {
   if (!f) return fail(QTTS_ERR_IO, std::string("cannot open ") + path);
   struct Closer { FILE* f; ~Closer() { fclose(f); } } closer{f};
   std::vector<float> a, b;
+  float wmax = 0.0f;  // largest |weight| of the projections that may take the tensor cores
+  auto track = [&](const std::vector<float>& v) {
+    for (float x : v) wmax = std::max(wmax, fabsf(x));
+  };
   DRC(read_vec(f, hd.cb0, a)); DRC(upload(*D, a, &D->cb0));
   {
     std::vector<float> all;
@@ -461,12 +478,13 @@ int decoder_load(const char* path, int device, Decoder* D) {
     DRC(upload(*D, b, &D->pre_w));
     DRC(read_vec(f, pc.b, a)); DRC(upload(*D, a, &D->pre_b));
   }
-  DRC(read_vec(f, hd.in_w, a)); DRC(upload(*D, a, &D->in_w));
+  DRC(read_vec(f, hd.in_w, a)); track(a); DRC(upload(*D, a, &D->in_w));
   DRC(read_vec(f, hd.in_b, a)); DRC(upload(*D, a, &D->in_b));
   for (auto& L : hd.layers) {
     DecLayerDev dl{};
     std::vector<float> q, k, v;
     DRC(read_vec(f, L.q, q)); DRC(read_vec(f, L.k, k)); DRC(read_vec(f, L.v, v));
+    track(q); track(k); track(v);
     b.assign(H * 3 * A, 0.0f);  // row kk: q | k | v
     for (uint64_t r = 0; r < H; ++r) {
       memcpy(&b[r * 3 * A], &q[r * A], A * 4);
@@ -474,15 +492,16 @@ int decoder_load(const char* path, int device, Decoder* D) {
       memcpy(&b[r * 3 * A + 2 * A], &v[r * A], A * 4);
     }
     DRC(upload(*D, b, &dl.wqkv));
-    DRC(read_vec(f, L.o, a)); DRC(upload(*D, a, &dl.wo));
+    DRC(read_vec(f, L.o, a)); track(a); DRC(upload(*D, a, &dl.wo));
     DRC(read_vec(f, L.gate, q)); DRC(read_vec(f, L.up, k));
+    track(q); track(k);
     b.assign(H * 2 * I, 0.0f);  // row kk: gate | up
     for (uint64_t r = 0; r < H; ++r) {
       memcpy(&b[r * 2 * I], &q[r * I], I * 4);
       memcpy(&b[r * 2 * I + I], &k[r * I], I * 4);
     }
     DRC(upload(*D, b, &dl.wgu));
-    DRC(read_vec(f, L.down, a)); DRC(upload(*D, a, &dl.wdown));
+    DRC(read_vec(f, L.down, a)); track(a); DRC(upload(*D, a, &dl.wdown));
     DRC(read_vec(f, L.in_norm, a)); DRC(upload(*D, a, &dl.in_norm));
     DRC(read_vec(f, L.post_norm, a)); DRC(upload(*D, a, &dl.post_norm));
     DRC(read_vec(f, L.attn_scale, a)); DRC(upload(*D, a, &dl.attn_scale));
@@ -494,6 +513,33 @@ int decoder_load(const char* path, int device, Decoder* D) {
   DRC(read_vec(f, hd.out_b, a)); DRC(upload(*D, a, &D->out_b));
   DRC(read_vec(f, hd.rope_cos, a)); DRC(upload(*D, a, &D->rope_cos));
   DRC(read_vec(f, hd.rope_sin, a)); DRC(upload(*D, a, &D->rope_sin));
+  // The layer projections (and the input projection) also as tensor-core
+  // operand tiles: fp16 hi + lo of each f32 weight (~22 significand bits),
+  // while every weight is inside the fp16 range
+  if (wmax < 60000.0f) {
+    auto expand = [&](const float* w, uint32_t k, uint32_t n, long ld, int col0, Q4Mat* m) {
+      uint8_t* t = nullptr;
+      if (cudaMalloc(reinterpret_cast<void**>(&t), tc_expand_bytes((int)k, (int)n)) != cudaSuccess)
+        return fail(QTTS_ERR_OOM, "device allocation failed");
+      D->allocs.push_back(t);
+      if (tc_expand_f32(w, (int)k, (int)n, ld, col0, t, D->st) != cudaSuccess)
+        return fail(QTTS_ERR_CUDA, "decoder weight expansion failed");
+      m->k = (int)k;
+      m->n = (int)n;
+      m->wx = t;
+      return (int)QTTS_OK;
+    };
+    DRC(expand(D->in_w, 1024, (uint32_t)H, (long)H, 0, &D->tin));
+    for (DecLayerDev& L : D->layers) {
+      DRC(expand(L.wqkv, (uint32_t)H, (uint32_t)(3 * A), (long)(3 * A), 0, &L.tqkv));
+      DRC(expand(L.wo, (uint32_t)A, (uint32_t)H, (long)H, 0, &L.to));
+      DRC(expand(L.wgu, (uint32_t)H, (uint32_t)I, (long)(2 * I), 0, &L.tg));
+      DRC(expand(L.wgu, (uint32_t)H, (uint32_t)I, (long)(2 * I), (int)I, &L.tu));
+      DRC(expand(L.wdown, (uint32_t)I, (uint32_t)H, (long)H, 0, &L.td));
+    }
+    if (cudaStreamSynchronize(D->st) != cudaSuccess) return fail(QTTS_ERR_CUDA, "decoder weight expansion failed");
+    D->tc = true;
+  }
   return QTTS_OK;
 }
 
@@ -501,17 +547,24 @@ int ensure_scratch(Decoder& D, int T) {
   if (T <= D.cap_T) return QTTS_OK;
   if (D.st) cudaStreamSynchronize(D.st);
   cudaFree(D.E0);
+  cudaFree(D.xs);
   D.E0 = nullptr;
+  D.xs = nullptr;
   D.cap_T = 0;
   const size_t H = D.hidden, A = (size_t)D.heads * D.head_dim, I = D.inter, cb = D.cb_dim;
-  const size_t per = 2 * cb + 512 + 1024 + 2 * H + 3 * A + A + 2 * I + I;
+  const size_t per = 2 * cb + 512 + 1024 + 2 * H + 3 * A + A + 2 * I + I + H;
+  if (D.tc) {  // the largest K of the tensor-core projections: 1024 (input, o) or the MLP width (down)
+    D.xs_bytes = tc_xsplit_scratch_bytes(T, (int)std::max<size_t>(std::max<size_t>(1024, A), I));
+    if (cudaMalloc(reinterpret_cast<void**>(&D.xs), D.xs_bytes) != cudaSuccess)
+      return fail(QTTS_ERR_OOM, "device allocation failed");
+  }
   float* base = nullptr;
   if (cudaMalloc(reinterpret_cast<void**>(&base), per * (size_t)T * 4) != cudaSuccess)
     return fail(QTTS_ERR_OOM, "device allocation failed");
   float* p = base;
   auto take = [&](size_t n) { float* r = p; p += n * (size_t)T; return r; };
   D.E0 = take(cb); D.S = take(cb); D.vq = take(512); D.pre = take(1024); D.x = take(H); D.xn = take(H);
-  D.qkv = take(3 * A); D.ao = take(A); D.gu = take(2 * I); D.h = take(I);
+  D.qkv = take(3 * A); D.ao = take(A); D.gu = take(2 * I); D.h = take(I); D.tmp = take(H);
   D.cap_T = T;
   return QTTS_OK;
 }
@@ -550,10 +603,26 @@ int decode_dev(Decoder& D, const uint32_t* codes, int T, float* out) {
     t.B = D.pre_w; t.bias = D.pre_b; t.C = D.pre; t.ldc = 1024; t.mode = 0;
     ok(gemm(D.st, t));
   }
-  plain(D.pre, 1024, D.in_w, H, D.x, D.in_b, 0, nullptr);
+  // the layer projections on the tensor cores from T >= 16 frames (the
+  // projection kernel's smallest row block); the rest stays on the CUDA cores
+  const bool tc = D.tc && T >= kTcMinRows;
+  int* tc_err = reinterpret_cast<int*>(D.err);
+  auto proj = [&](const Q4Mat* mats, int nmat, int epi, const float* X, int ldx, float* C, int ldo,
+                  const float* bias) {
+    return tc_project_expanded(mats, nmat, epi, X, ldx, T, C, ldo, bias, D.xs, D.xs_bytes, tc_err, D.st);
+  };
+  auto scale_add = [&](const float* Y, const float* scale) {
+    const long n = (long)T * H;
+    ++g_kernel_launches;
+    dec_scale_add_kernel<<<(unsigned)((n + 255) / 256), 256, 0, D.st>>>(D.x, Y, scale, T, H);
+    ok(cudaGetLastError());
+  };
+  if (tc) DRC(proj(&D.tin, 1, EPI_STORE, D.pre, 1024, D.x, H, D.in_b));
+  else plain(D.pre, 1024, D.in_w, H, D.x, D.in_b, 0, nullptr);
   for (const DecLayerDev& L : D.layers) {
     ok(rms(D, D.x, T, H, L.in_norm, D.xn));
-    plain(D.xn, H, L.wqkv, 3 * A, D.qkv, nullptr, 0, nullptr);
+    if (tc) DRC(proj(&L.tqkv, 1, EPI_STORE, D.xn, H, D.qkv, 3 * A, nullptr));
+    else plain(D.xn, H, L.wqkv, 3 * A, D.qkv, nullptr, 0, nullptr);
     {
       const long n = (long)T * D.heads * (D.head_dim / 2) * 2;
       ++g_kernel_launches;
@@ -566,16 +635,26 @@ int decode_dev(Decoder& D, const uint32_t* codes, int T, float* out) {
                           D.st>>>(
         D.qkv, T, (int)D.heads, (int)D.window, D.ao);
     ok(cudaGetLastError());
-    plain(D.ao, A, L.wo, H, D.x, nullptr, 2, L.attn_scale);
+    if (tc) {
+      DRC(proj(&L.to, 1, EPI_STORE, D.ao, A, D.tmp, H, nullptr));
+      scale_add(D.tmp, L.attn_scale);
+    } else {
+      plain(D.ao, A, L.wo, H, D.x, nullptr, 2, L.attn_scale);
+    }
     ok(rms(D, D.x, T, H, L.post_norm, D.xn));
-    plain(D.xn, H, L.wgu, 2 * I, D.gu, nullptr, 0, nullptr);
-    {
+    if (tc) {
+      const Q4Mat gu[2] = {L.tg, L.tu};  // silu(gate) * up in the projection's epilogue
+      DRC(proj(gu, 2, EPI_SWIGLU, D.xn, H, D.h, I, nullptr));
+      DRC(proj(&L.td, 1, EPI_STORE, D.h, I, D.tmp, H, nullptr));
+      scale_add(D.tmp, L.mlp_scale);
+    } else {
+      plain(D.xn, H, L.wgu, 2 * I, D.gu, nullptr, 0, nullptr);
       const long n = (long)T * I;
       ++g_kernel_launches;
       dec_swiglu_kernel<<<(unsigned)((n + 255) / 256), 256, 0, D.st>>>(D.gu, T, I, D.h);
       ok(cudaGetLastError());
+      plain(D.h, I, L.wdown, H, D.x, nullptr, 2, L.mlp_scale);
     }
-    plain(D.h, I, L.wdown, H, D.x, nullptr, 2, L.mlp_scale);
   }
   ok(rms(D, D.x, T, H, D.norm, D.xn));
   {
@@ -596,7 +675,9 @@ int check_err(Decoder& D) {
   if (h) {
     cudaMemsetAsync(D.err, 0, 4, D.st);
     cudaStreamSynchronize(D.st);
-    return fail(QTTS_ERR_RANGE, "decoder: a code index is past its codebook");
+    if (h & kDecErrCode) return fail(QTTS_ERR_RANGE, "decoder: a code index is past its codebook");
+    if (h & kErrWaitExpired) return fail(QTTS_ERR_TIMEOUT, "decoder: a bounded device wait expired");
+    return fail(QTTS_ERR_RANGE, "decoder: a tensor-core input outside the fp16 range");
   }
   return QTTS_OK;
 }

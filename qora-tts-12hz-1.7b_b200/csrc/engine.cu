@@ -1368,6 +1368,30 @@ static int gemv_plan_standalone(int k, int n, int m, GemvDesc& g) {
   return QTTS_OK;
 }
 
+int tc_project_expanded(const Q4Mat* mats, int nmat, int epi, const float* X, long ldx, int M, float* out, long ldo,
+                        const float* bias, uint8_t* xs_buf, size_t xs_bytes, int* err_flag, cudaStream_t st) {
+  if (M < kTcMinRows || nmat < 1 || nmat > 2 || (nmat == 2) != (epi == EPI_SWIGLU))
+    return fail(QTTS_ERR_BADARG, "tensor-core projection: bad shape");
+  for (int i = 0; i < nmat; ++i)
+    if (!mats[i].wx || mats[i].k % 4 || mats[i].n % 64) return fail(QTTS_ERR_BADARG, "tensor-core projection: bad weights");
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaGetLastError();
+  tc_init_attributes();
+  GemvDesc g = nmat == 2 ? gemv_base(epi, {mats[0], mats[1]}, true, M) : gemv_base(epi, {mats[0]}, false, M);
+  g.X = X; g.ldx = ldx;
+  g.epi.out = out; g.epi.ldo = ldo; g.epi.bias = bias;
+  g.err_flag = err_flag;
+  g.xs_buf = xs_buf; g.xs_bytes = xs_bytes;
+  g.cluster = 1;
+  tc_plan(sms, g);
+  // more than 128 rows must take the split rows: the other instance reads Q4 bytes
+  if (M > kTcRows && !tc_takes_split(g)) return fail(QTTS_ERR_BADARG, "tensor-core projection: split-row scratch too small");
+  const cudaError_t e = launch_gemv(g, FrameCodes{}, st);  // (checks the operands' alignment)
+  if (e != cudaSuccess) return fail(QTTS_ERR_CUDA, cudaGetErrorString(e));
+  return QTTS_OK;
+}
+
 // Scratch layout: [tile counters 16 KB][split-K partials of either kernel]
 // [split input rows of a tensor-core launch of more than 64 rows, 16-byte
 // aligned]

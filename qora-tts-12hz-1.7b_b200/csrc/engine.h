@@ -15,6 +15,13 @@ namespace qtts {
 
 void set_error(const std::string& msg);
 int fail(int code, const std::string& msg);
+// One tensor-core projection over M input rows from weights given only as
+// expanded operand tiles (Q4Mat::wx set; k, n): out[M][ldo] = X * W (+ bias)
+// for EPI_STORE, or silu(X * W0) * (X * W1) for the paired EPI_SWIGLU.  Rows
+// above 64 are split once into xs_buf (tc_xsplit_scratch_bytes(M, k)).
+// Errors of the launch; device-side ones set bits of err_flag.
+int tc_project_expanded(const Q4Mat* mats, int nmat, int epi, const float* X, long ldx, int M, float* out, long ldo,
+                        const float* bias, uint8_t* xs_buf, size_t xs_bytes, int* err_flag, cudaStream_t st);
 
 struct DLayer {
   Q4Mat q, k, v, o, gate, up, down;

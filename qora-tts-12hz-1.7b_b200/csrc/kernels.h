@@ -300,6 +300,10 @@ cudaError_t launch_tc(const GemvDesc& d, const FrameCodes& fc, cudaStream_t st);
 // expansion (one launch; the blocks are what the projection's converters write).
 size_t tc_expand_bytes(int k, int n);
 cudaError_t tc_expand(const Q4Mat& w, uint8_t* out, cudaStream_t st);
+// f32 weights w[k][ld] (columns col0 .. col0 + n) into the same operand
+// tiles, split hi + lo to ~22 significand bits (the speech decoder's
+// projections)
+cudaError_t tc_expand_f32(const float* w, int k, int n, long ld, int col0, uint8_t* out, cudaStream_t st);
 void tc_init_attributes();
 
 

@@ -1159,6 +1159,47 @@ __global__ void tc_expand_kernel(const Q4Mat w, uint8_t* out) {
   }
 }
 
+// The same expansion from f32 weights w[k][ld] (columns col0 .. col0 + n):
+// hi = fp16(w), lo = fp16((w - hi) * 2^11).  Unlike the Q4 values this split
+// is not exact: it keeps ~22 of the 24 significand bits (|w| < 65504).  A
+// thread per row and 8-column group of a block.
+__global__ void tc_expand_f32_kernel(const float* w, int k, int n, long ld, int col0, uint8_t* out) {
+  const int nt = (n + TN - 1) / TN, nks = (k + TK - 1) / TK;
+  const size_t items = (size_t)nt * nks * TK * (TN / 8);
+  for (size_t c = (size_t)blockIdx.x * blockDim.x + threadIdx.x; c < items; c += (size_t)gridDim.x * blockDim.x) {
+    const int g8 = (int)(c % (TN / 8));
+    const int brow = (int)((c / (TN / 8)) % TK);
+    const size_t blk = c / ((size_t)(TN / 8) * TK);
+    const int ks = (int)(blk % nks), t = (int)(blk / nks);
+    const int row = ks * TK + brow, cb = t * TN + g8 * 8;
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {  // half2 p holds columns p and p + 4 of the group
+      float v[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int col = cb + p + 4 * q;
+        v[q] = (row < k && col < n) ? w[(size_t)row * ld + col0 + col] : 0.0f;
+      }
+      const __half2 hh = __floats2half2_rn(v[0], v[1]);
+      const float2 hf = __half22float2(hh);
+      h[p] = h2_bits(hh);
+      l[p] = h2_bits(__floats2half2_rn((v[0] - hf.x) * kLoScale, (v[1] - hf.y) * kLoScale));
+    }
+    uint8_t* dst = out + blk * (2 * B_BYTES) + g8 * 1024 + (brow >> 3) * 128 + (brow & 7) * 16;
+    *reinterpret_cast<uint4*>(dst) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(dst + B_BYTES) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+cudaError_t tc_expand_f32(const float* w, int k, int n, long ld, int col0, uint8_t* out, cudaStream_t st) {
+  if (!w || !out || k <= 0 || n <= 0 || n % 64 || !al16(out)) return cudaErrorInvalidValue;
+  const size_t items = (size_t)((n + TN - 1) / TN) * ((k + TK - 1) / TK) * TK * (TN / 8);
+  const unsigned grid = (unsigned)std::min<size_t>((items + 255) / 256, 148 * 8);
+  tc_expand_f32_kernel<<<grid, 256, 0, st>>>(w, k, n, ld, col0, out);
+  return cudaGetLastError();
+}
+
 size_t tc_expand_bytes(int k, int n) {
   return (size_t)((n + TN - 1) / TN) * ((k + TK - 1) / TK) * (2 * B_BYTES);
 }

@@ -48,3 +48,11 @@ def test_roofline_tc_overlap_fields(bench):
     assert abs(r["achieved"] - 100.0) < 1e-9  # 1e12 FLOP in 10 ms
     assert abs(r["overlapped"]["lanes_overlap"] - 1.0) < 1e-9  # 2 waves x 10 ms over a 20 ms step
     assert r["traffic"] == pytest.approx(bench.TC_TRAFFIC_RATIO * 4e9 / 400)
+
+
+def test_decoder_launch_count(bench):
+    # CUDA cores below 16 frames: 79 kernels; tensor cores from 16 frames,
+    # with a row-split kernel before each projection above 64 frames
+    assert bench.decoder_launches(5) == 79
+    assert bench.decoder_launches(40) == 87
+    assert bench.decoder_launches(500) == 120
