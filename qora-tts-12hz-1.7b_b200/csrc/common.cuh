@@ -137,6 +137,15 @@ __device__ __forceinline__ void xs_store4(uint8_t* buf, int K, int m, int c, flo
   *reinterpret_cast<uint2*>(p) = make_uint2(h0, h1);
   *reinterpret_cast<uint2*>(p + kXsHalf) = make_uint2(l0, l1);
 }
+// One element (row m, column c) of the same tiles, split as split_pair does.
+__device__ __forceinline__ void xs_store1(uint8_t* buf, int K, int m, int c, float v) {
+  const int nks = (K + kXsK - 1) / kXsK, r = m & (kXsRows - 1), j = c & (kXsK - 1);
+  uint8_t* p = buf + ((size_t)(m / kXsRows) * nks + c / kXsK) * (2 * kXsHalf) + (r >> 3) * 1024 + (j >> 3) * 128 +
+               (r & 7) * 16 + (j & 7) * 2;
+  const __half h = __float2half_rn(v);
+  *reinterpret_cast<__half*>(p) = h;
+  *reinterpret_cast<__half*>(p + kXsHalf) = __float2half_rn(__fmul_rn(__fsub_rn(v, __half2float(h)), kSplitLoScale));
+}
 __device__ __forceinline__ bool fp16_overflow4(float4 v) {
   return fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))) > 65504.0f;
 }

@@ -35,6 +35,7 @@
 #include <algorithm>
 #include <vector>
 
+#include "common.cuh"
 #include "engine.h"
 #include "format.h"
 #include "kernels.h"
@@ -176,17 +177,34 @@ __global__ void dec_gather_kernel(const uint32_t* codes, int T, int entries, int
   }
 }
 
-// rms_norm_f32 (decoder.rs:515-525): y = x * (1 / sqrt(sum x^2 / n + eps)) * gamma, a warp per row
-__global__ void dec_rmsnorm_kernel(const float* X, int M, int n, const float* gamma, float eps, float* Y) {
+// rms_norm_f32 (decoder.rs:515-525): y = x * (1 / sqrt(sum x^2 / n + eps)) * gamma,
+// a warp per row, lane l holding columns 4l + 128 j (n % 128 == 0); with xs,
+// also written as the next projection's split operand rows (err bit 8 for a
+// value outside the fp16 range)
+__global__ void dec_rmsnorm_kernel(const float* X, int M, int n, const float* gamma, float eps, float* Y,
+                                   uint8_t* xs, int* err) {
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
   if (row >= M) return;
   const float* x = X + (size_t)row * n;
   float ss = 0.0f;
-  for (int i = lane; i < n; i += 32) ss += x[i] * x[i];
+  for (int c = 4 * lane; c < n; c += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(x + c);
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
 #pragma unroll
   for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   const float inv = 1.0f / sqrtf(ss / (float)n + eps);
-  for (int i = lane; i < n; i += 32) Y[(size_t)row * n + i] = x[i] * inv * gamma[i];
+  bool big = false;
+  for (int c = 4 * lane; c < n; c += 128) {
+    const float4 v = *reinterpret_cast<const float4*>(x + c), g = *reinterpret_cast<const float4*>(gamma + c);
+    const float4 y = make_float4(v.x * inv * g.x, v.y * inv * g.y, v.z * inv * g.z, v.w * inv * g.w);
+    *reinterpret_cast<float4*>(Y + (size_t)row * n + c) = y;
+    if (xs) {
+      xs_store4(xs, n, row, c, y);
+      big = big || fp16_overflow4(y);
+    }
+  }
+  if (big) atomicOr(err, kErrFp16Input);
 }
 
 // apply_rope_split_half (decoder.rs:556-578) on the q and k parts of a
@@ -223,7 +241,8 @@ __host__ __device__ constexpr size_t attn_k_floats(int window) {
   return ((size_t)(kAttnFrames + window - 1) * (64 + 1) + 3) & ~(size_t)3;
 }
 template <int HD>
-__global__ void __launch_bounds__(128) dec_attn_kernel(const float* QKV, int T, int heads, int window, float* out) {
+__global__ void __launch_bounds__(128) dec_attn_kernel(const float* QKV, int T, int heads, int window, float* out,
+                                                       uint8_t* xs, int* err) {
   static_assert(HD == 64, "two dimensions per lane");
   extern __shared__ float sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -286,6 +305,11 @@ __global__ void __launch_bounds__(128) dec_attn_kernel(const float* QKV, int T, 
     }
     out[(size_t)t * heads * HD + (size_t)h * HD + lane] = a0;
     out[(size_t)t * heads * HD + (size_t)h * HD + lane + 32] = a1;
+    if (xs) {  // the o projection's split operand rows
+      xs_store1(xs, heads * HD, t, h * HD + lane, a0);
+      xs_store1(xs, heads * HD, t, h * HD + lane + 32, a1);
+      if (fmaxf(fabsf(a0), fabsf(a1)) > 65504.0f) atomicOr(err, kErrFp16Input);
+    }
     __syncwarp();  // qs / p are rewritten for this warp's next frame
   }
 }
@@ -344,6 +368,7 @@ struct Decoder {
         *ao = nullptr, *gu = nullptr, *h = nullptr, *tmp = nullptr;
   uint8_t* xs = nullptr;  // split input rows of the tensor-core projections
   size_t xs_bytes = 0;
+  uint8_t *xs2a = nullptr, *xs2b = nullptr;  // the same, written by the rows' producers (alternating)
   uint32_t* codes = nullptr;
   float* out = nullptr;
   int cap_io = 0;
@@ -353,7 +378,7 @@ struct Decoder {
     if (st) cudaStreamSynchronize(st);
     for (void* p : allocs)
       if (p) cudaFree(p);
-    cudaFree(E0); cudaFree(xs); cudaFree(codes); cudaFree(out);
+    cudaFree(E0); cudaFree(xs); cudaFree(xs2a); cudaFree(xs2b); cudaFree(codes); cudaFree(out);
     if (st) cudaStreamDestroy(st);
   }
 };
@@ -548,14 +573,18 @@ int ensure_scratch(Decoder& D, int T) {
   if (D.st) cudaStreamSynchronize(D.st);
   cudaFree(D.E0);
   cudaFree(D.xs);
+  cudaFree(D.xs2a);
+  cudaFree(D.xs2b);
   D.E0 = nullptr;
-  D.xs = nullptr;
+  D.xs = D.xs2a = D.xs2b = nullptr;
   D.cap_T = 0;
   const size_t H = D.hidden, A = (size_t)D.heads * D.head_dim, I = D.inter, cb = D.cb_dim;
   const size_t per = 2 * cb + 512 + 1024 + 2 * H + 3 * A + A + 2 * I + I + H;
   if (D.tc) {  // the largest K of the tensor-core projections: 1024 (input, o) or the MLP width (down)
     D.xs_bytes = tc_xsplit_scratch_bytes(T, (int)std::max<size_t>(std::max<size_t>(1024, A), I));
-    if (cudaMalloc(reinterpret_cast<void**>(&D.xs), D.xs_bytes) != cudaSuccess)
+    if (cudaMalloc(reinterpret_cast<void**>(&D.xs), D.xs_bytes) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void**>(&D.xs2a), D.xs_bytes) != cudaSuccess ||
+        cudaMalloc(reinterpret_cast<void**>(&D.xs2b), D.xs_bytes) != cudaSuccess)
       return fail(QTTS_ERR_OOM, "device allocation failed");
   }
   float* base = nullptr;
@@ -569,9 +598,9 @@ int ensure_scratch(Decoder& D, int T) {
   return QTTS_OK;
 }
 
-cudaError_t rms(Decoder& D, const float* X, int T, int n, const float* gamma, float* Y) {
+cudaError_t rms(Decoder& D, const float* X, int T, int n, const float* gamma, float* Y, uint8_t* xs = nullptr) {
   ++g_kernel_launches;
-  dec_rmsnorm_kernel<<<(T + 7) / 8, 256, 0, D.st>>>(X, T, n, gamma, 1e-5f, Y);
+  dec_rmsnorm_kernel<<<(T + 7) / 8, 256, 0, D.st>>>(X, T, n, gamma, 1e-5f, Y, xs, reinterpret_cast<int*>(D.err));
   return cudaGetLastError();
 }
 
@@ -608,9 +637,15 @@ int decode_dev(Decoder& D, const uint32_t* codes, int T, float* out) {
   const bool tc = D.tc && T >= kTcMinRows;
   int* tc_err = reinterpret_cast<int*>(D.err);
   auto proj = [&](const Q4Mat* mats, int nmat, int epi, const float* X, int ldx, float* C, int ldo,
-                  const float* bias) {
-    return tc_project_expanded(mats, nmat, epi, X, ldx, T, C, ldo, bias, D.xs, D.xs_bytes, tc_err, D.st);
+                  const float* bias, const uint8_t* pre = nullptr, uint8_t* xs_out = nullptr) {
+    return tc_project_expanded(mats, nmat, epi, X, ldx, T, C, ldo, bias, D.xs, D.xs_bytes, pre, xs_out, tc_err,
+                               D.st);
   };
+  // above 64 frames every layer projection takes its rows split by their
+  // producer (RMSNorm, attention, the gate|up epilogue) from one of two
+  // buffers that alternate, instead of a split launch of its own
+  uint8_t* xa = (tc && T > 64) ? D.xs2a : nullptr;
+  uint8_t* xb = (tc && T > 64) ? D.xs2b : nullptr;
   auto scale_add = [&](const float* Y, const float* scale) {
     const long n = (long)T * H;
     ++g_kernel_launches;
@@ -620,8 +655,8 @@ int decode_dev(Decoder& D, const uint32_t* codes, int T, float* out) {
   if (tc) DRC(proj(&D.tin, 1, EPI_STORE, D.pre, 1024, D.x, H, D.in_b));
   else plain(D.pre, 1024, D.in_w, H, D.x, D.in_b, 0, nullptr);
   for (const DecLayerDev& L : D.layers) {
-    ok(rms(D, D.x, T, H, L.in_norm, D.xn));
-    if (tc) DRC(proj(&L.tqkv, 1, EPI_STORE, D.xn, H, D.qkv, 3 * A, nullptr));
+    ok(rms(D, D.x, T, H, L.in_norm, D.xn, xa));
+    if (tc) DRC(proj(&L.tqkv, 1, EPI_STORE, D.xn, H, D.qkv, 3 * A, nullptr, xa));
     else plain(D.xn, H, L.wqkv, 3 * A, D.qkv, nullptr, 0, nullptr);
     {
       const long n = (long)T * D.heads * (D.head_dim / 2) * 2;
@@ -633,19 +668,19 @@ int decode_dev(Decoder& D, const uint32_t* codes, int T, float* out) {
     ++g_kernel_launches;
     dec_attn_kernel<64><<<dim3((unsigned)((T + kAttnFrames - 1) / kAttnFrames), D.heads), 128, attn_smem((int)D.window),
                           D.st>>>(
-        D.qkv, T, (int)D.heads, (int)D.window, D.ao);
+        D.qkv, T, (int)D.heads, (int)D.window, D.ao, xb, tc_err);
     ok(cudaGetLastError());
     if (tc) {
-      DRC(proj(&L.to, 1, EPI_STORE, D.ao, A, D.tmp, H, nullptr));
+      DRC(proj(&L.to, 1, EPI_STORE, D.ao, A, D.tmp, H, nullptr, xb));
       scale_add(D.tmp, L.attn_scale);
     } else {
       plain(D.ao, A, L.wo, H, D.x, nullptr, 2, L.attn_scale);
     }
-    ok(rms(D, D.x, T, H, L.post_norm, D.xn));
+    ok(rms(D, D.x, T, H, L.post_norm, D.xn, xa));
     if (tc) {
       const Q4Mat gu[2] = {L.tg, L.tu};  // silu(gate) * up in the projection's epilogue
-      DRC(proj(gu, 2, EPI_SWIGLU, D.xn, H, D.h, I, nullptr));
-      DRC(proj(&L.td, 1, EPI_STORE, D.h, I, D.tmp, H, nullptr));
+      DRC(proj(gu, 2, EPI_SWIGLU, D.xn, H, D.h, I, nullptr, xa, xb));
+      DRC(proj(&L.td, 1, EPI_STORE, D.h, I, D.tmp, H, nullptr, xb));
       scale_add(D.tmp, L.mlp_scale);
     } else {
       plain(D.xn, H, L.wgu, 2 * I, D.gu, nullptr, 0, nullptr);

@@ -1369,7 +1369,8 @@ static int gemv_plan_standalone(int k, int n, int m, GemvDesc& g) {
 }
 
 int tc_project_expanded(const Q4Mat* mats, int nmat, int epi, const float* X, long ldx, int M, float* out, long ldo,
-                        const float* bias, uint8_t* xs_buf, size_t xs_bytes, int* err_flag, cudaStream_t st) {
+                        const float* bias, uint8_t* xs_buf, size_t xs_bytes, const uint8_t* x_split_pre,
+                        uint8_t* xs_out, int* err_flag, cudaStream_t st) {
   if (M < kTcMinRows || nmat < 1 || nmat > 2 || (nmat == 2) != (epi == EPI_SWIGLU))
     return fail(QTTS_ERR_BADARG, "tensor-core projection: bad shape");
   for (int i = 0; i < nmat; ++i)
@@ -1383,10 +1384,17 @@ int tc_project_expanded(const Q4Mat* mats, int nmat, int epi, const float* X, lo
   g.epi.out = out; g.epi.ldo = ldo; g.epi.bias = bias;
   g.err_flag = err_flag;
   g.xs_buf = xs_buf; g.xs_bytes = xs_bytes;
+  g.x_split_pre = x_split_pre;
+  if (xs_out) {
+    if (epi != EPI_SWIGLU) return fail(QTTS_ERR_BADARG, "tensor-core projection: split output needs SwiGLU");
+    g.xs_out = xs_out;
+    g.xs_out_k = mats[0].n;
+  }
   g.cluster = 1;
   tc_plan(sms, g);
-  // more than 128 rows must take the split rows: the other instance reads Q4 bytes
-  if (M > kTcRows && !tc_takes_split(g)) return fail(QTTS_ERR_BADARG, "tensor-core projection: split-row scratch too small");
+  // more than 128 rows must take split rows: the other instance reads Q4 bytes
+  if (M > kTcRows && !x_split_pre && !tc_takes_split(g))
+    return fail(QTTS_ERR_BADARG, "tensor-core projection: split-row scratch too small");
   const cudaError_t e = launch_gemv(g, FrameCodes{}, st);  // (checks the operands' alignment)
   if (e != cudaSuccess) return fail(QTTS_ERR_CUDA, cudaGetErrorString(e));
   return QTTS_OK;

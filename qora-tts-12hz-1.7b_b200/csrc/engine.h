@@ -20,8 +20,12 @@ int fail(int code, const std::string& msg);
 // for EPI_STORE, or silu(X * W0) * (X * W1) for the paired EPI_SWIGLU.  Rows
 // above 64 are split once into xs_buf (tc_xsplit_scratch_bytes(M, k)).
 // Errors of the launch; device-side ones set bits of err_flag.
+// x_split_pre: the input rows already split by their producer (X unused
+// then); xs_out: the EPI_SWIGLU result also written split (for a next
+// projection of K = n).
 int tc_project_expanded(const Q4Mat* mats, int nmat, int epi, const float* X, long ldx, int M, float* out, long ldo,
-                        const float* bias, uint8_t* xs_buf, size_t xs_bytes, int* err_flag, cudaStream_t st);
+                        const float* bias, uint8_t* xs_buf, size_t xs_bytes, const uint8_t* x_split_pre,
+                        uint8_t* xs_out, int* err_flag, cudaStream_t st);
 
 struct DLayer {
   Q4Mat q, k, v, o, gate, up, down;
