@@ -254,8 +254,10 @@ __global__ void __launch_bounds__(128) dec_attn_kernel(const float* QKV, int T, 
   float* sK = sm;                                         // [rows][HD + 1]
   float* sV = sK + attn_k_floats(window);                 // [rows][HD], 16-byte aligned (float4 stores)
   float* sP = sV + (size_t)rows * HD;                     // [4][window]
-  float* sQ = sP + 4 * window;                            // [4][HD]
+  float* sQ = sP + 4 * window;                            // [kAttnFrames][HD]: the block's q rows
   const long ld = 3L * heads * HD;
+  for (int i = threadIdx.x; i < (t1 - t0) * HD; i += blockDim.x)
+    sQ[i] = QKV[(size_t)(t0 + i / HD) * ld + (size_t)h * HD + i % HD];
   for (int i = threadIdx.x; i < nw * (HD / 4); i += blockDim.x) {
     const int r = i / (HD / 4), c4 = i % (HD / 4);
     const float* row = QKV + (size_t)(w0 + r) * ld + (size_t)h * HD;
@@ -268,33 +270,32 @@ __global__ void __launch_bounds__(128) dec_attn_kernel(const float* QKV, int T, 
   __syncthreads();
   const float scale = 1.0f / sqrtf((float)HD);
   float* p = sP + warp * window;
-  float* qs = sQ + warp * HD;
   for (int t = t0 + warp; t < t1; t += 4) {
-    const float* q = QKV + (size_t)t * ld + (size_t)h * HD;
-    qs[lane] = q[lane];
-    qs[lane + 32] = q[lane + 32];
-    __syncwarp();
+    const float* qs = sQ + (size_t)(t - t0) * HD;
     const int start = t + 1 > window ? t + 1 - window : 0, L = t + 1 - start;
+    float mx = -INFINITY;
     for (int s = lane; s < L; s += 32) {
       const float* k = sK + (size_t)(start + s - w0) * (HD + 1);
       float dot = 0.0f;
 #pragma unroll 16
       for (int e = 0; e < HD; ++e) dot += qs[e] * k[e];
       p[s] = dot * scale;
+      mx = fmaxf(mx, p[s]);
     }
+    // softmax_raw: the max is order-free; the exponentials in parallel; their
+    // sum in position order on lane 0, as the reference adds them
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    for (int s = lane; s < L; s += 32) p[s] = expf(p[s] - mx);
     __syncwarp();
+    float inv = 0.0f;
     if (lane == 0) {
-      float mx = -INFINITY;
-      for (int s = 0; s < L; ++s) mx = fmaxf(mx, p[s]);
       float sum = 0.0f;
-      for (int s = 0; s < L; ++s) {
-        const float e = expf(p[s] - mx);
-        p[s] = e;
-        sum += e;
-      }
-      const float inv = 1.0f / sum;
-      for (int s = 0; s < L; ++s) p[s] *= inv;
+      for (int s = 0; s < L; ++s) sum += p[s];
+      inv = 1.0f / sum;
     }
+    inv = __shfl_sync(0xffffffffu, inv, 0);
+    for (int s = lane; s < L; s += 32) p[s] *= inv;
     __syncwarp();
     float a0 = 0.0f, a1 = 0.0f;
     for (int s = 0; s < L; ++s) {
@@ -310,12 +311,12 @@ __global__ void __launch_bounds__(128) dec_attn_kernel(const float* QKV, int T, 
       xs_store1(xs, heads * HD, t, h * HD + lane + 32, a1);
       if (fmaxf(fabsf(a0), fabsf(a1)) > 65504.0f) atomicOr(err, kErrFp16Input);
     }
-    __syncwarp();  // qs / p are rewritten for this warp's next frame
+    __syncwarp();  // p is rewritten for this warp's next frame
   }
 }
 size_t attn_smem(int window) {
-  return (attn_k_floats(window) + (size_t)(kAttnFrames + window - 1) * 64 + 4 * (size_t)window + 4 * 64) *
-         sizeof(float);
+  return (attn_k_floats(window) + (size_t)(kAttnFrames + window - 1) * 64 + 4 * (size_t)window +
+          (size_t)kAttnFrames * 64) * sizeof(float);
 }
 
 // the layer-scaled residual (decoder.rs:286-288, 313-315): x += y * scale
