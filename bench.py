@@ -437,13 +437,13 @@ def decoder_flops(T, window=DEC_WINDOW):
 def decoder_launches(T, layers=DEC_LAYERS):
     """Kernels of one decode: gather, 2 codebook GEMMs, the pre-conv, then
     (from 16 frames, on the tensor cores) the input projection (after a
-    row-split kernel above 64 frames) and per layer 2 RMSNorms, RoPE,
-    attention, q|k|v, o, gate|up, down and 2 scaled residuals (the layer
-    projections' rows come split from their producers); the final RMSNorm
-    and output GEMM."""
+    row-split kernel above 64 frames) and per layer 2 RMSNorms (which also
+    apply the scaled residuals), RoPE, attention, q|k|v, o, gate|up and down
+    (the layer projections' rows come split from their producers); the final
+    RMSNorm and output GEMM."""
     if T < 16:
         return 1 + 2 + 1 + 1 + layers * 9 + 2
-    return 1 + 2 + 1 + (2 if T > 64 else 1) + layers * 10 + 2
+    return 1 + 2 + 1 + (2 if T > 64 else 1) + layers * 8 + 2
 
 
 def run_decoder(args, rank, world, local, Q, W, torch):

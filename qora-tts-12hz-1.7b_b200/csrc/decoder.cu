@@ -180,15 +180,23 @@ __global__ void dec_gather_kernel(const uint32_t* codes, int T, int entries, int
 // rms_norm_f32 (decoder.rs:515-525): y = x * (1 / sqrt(sum x^2 / n + eps)) * gamma,
 // a warp per row, lane l holding columns 4l + 128 j (n % 128 == 0); with xs,
 // also written as the next projection's split operand rows (err bit 8 for a
-// value outside the fp16 range)
-__global__ void dec_rmsnorm_kernel(const float* X, int M, int n, const float* gamma, float eps, float* Y,
-                                   uint8_t* xs, int* err) {
+// value outside the fp16 range).  With add, the layer-scaled residual that
+// precedes the norm is applied first, in place: x += add * add_scale
+// (decoder.rs:286-288, 313-315).
+__global__ void dec_rmsnorm_kernel(float* X, int M, int n, const float* gamma, float eps, float* Y, uint8_t* xs,
+                                   int* err, const float* add, const float* add_scale) {
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32, lane = threadIdx.x & 31;
   if (row >= M) return;
-  const float* x = X + (size_t)row * n;
+  float* x = X + (size_t)row * n;
   float ss = 0.0f;
   for (int c = 4 * lane; c < n; c += 128) {
-    const float4 v = *reinterpret_cast<const float4*>(x + c);
+    float4 v = *reinterpret_cast<const float4*>(x + c);
+    if (add) {
+      const float4 a = *reinterpret_cast<const float4*>(add + (size_t)row * n + c);
+      const float4 sc = *reinterpret_cast<const float4*>(add_scale + c);
+      v = make_float4(v.x + a.x * sc.x, v.y + a.y * sc.y, v.z + a.z * sc.z, v.w + a.w * sc.w);
+      *reinterpret_cast<float4*>(x + c) = v;
+    }
     ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
   }
 #pragma unroll
@@ -317,13 +325,6 @@ __global__ void __launch_bounds__(128) dec_attn_kernel(const float* QKV, int T, 
 size_t attn_smem(int window) {
   return (attn_k_floats(window) + (size_t)(kAttnFrames + window - 1) * 64 + 4 * (size_t)window +
           (size_t)kAttnFrames * 64) * sizeof(float);
-}
-
-// the layer-scaled residual (decoder.rs:286-288, 313-315): x += y * scale
-__global__ void dec_scale_add_kernel(float* X, const float* Y, const float* scale, int T, int n) {
-  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (long)T * n) return;
-  X[i] += Y[i] * scale[i % n];
 }
 
 // the MLP's silu(gate) * up (decoder.rs:307-311) on a gate|up row
@@ -599,9 +600,11 @@ int ensure_scratch(Decoder& D, int T) {
   return QTTS_OK;
 }
 
-cudaError_t rms(Decoder& D, const float* X, int T, int n, const float* gamma, float* Y, uint8_t* xs = nullptr) {
+cudaError_t rms(Decoder& D, float* X, int T, int n, const float* gamma, float* Y, uint8_t* xs = nullptr,
+               const float* add = nullptr, const float* add_scale = nullptr) {
   ++g_kernel_launches;
-  dec_rmsnorm_kernel<<<(T + 7) / 8, 256, 0, D.st>>>(X, T, n, gamma, 1e-5f, Y, xs, reinterpret_cast<int*>(D.err));
+  dec_rmsnorm_kernel<<<(T + 7) / 8, 256, 0, D.st>>>(X, T, n, gamma, 1e-5f, Y, xs, reinterpret_cast<int*>(D.err),
+                                                    add, add_scale);
   return cudaGetLastError();
 }
 
@@ -647,16 +650,14 @@ int decode_dev(Decoder& D, const uint32_t* codes, int T, float* out) {
   // buffers that alternate, instead of a split launch of its own
   uint8_t* xa = (tc && T > 64) ? D.xs2a : nullptr;
   uint8_t* xb = (tc && T > 64) ? D.xs2b : nullptr;
-  auto scale_add = [&](const float* Y, const float* scale) {
-    const long n = (long)T * H;
-    ++g_kernel_launches;
-    dec_scale_add_kernel<<<(unsigned)((n + 255) / 256), 256, 0, D.st>>>(D.x, Y, scale, T, H);
-    ok(cudaGetLastError());
-  };
+  // On the tensor-core path o and down write their products to tmp and the
+  // next RMSNorm applies the layer-scaled residual x += tmp * scale first.
+  const float* pending = nullptr;  // the layer scale of a residual not yet applied
   if (tc) DRC(proj(&D.tin, 1, EPI_STORE, D.pre, 1024, D.x, H, D.in_b));
   else plain(D.pre, 1024, D.in_w, H, D.x, D.in_b, 0, nullptr);
   for (const DecLayerDev& L : D.layers) {
-    ok(rms(D, D.x, T, H, L.in_norm, D.xn, xa));
+    ok(rms(D, D.x, T, H, L.in_norm, D.xn, xa, pending ? D.tmp : nullptr, pending));
+    pending = nullptr;
     if (tc) DRC(proj(&L.tqkv, 1, EPI_STORE, D.xn, H, D.qkv, 3 * A, nullptr, xa));
     else plain(D.xn, H, L.wqkv, 3 * A, D.qkv, nullptr, 0, nullptr);
     {
@@ -673,16 +674,17 @@ int decode_dev(Decoder& D, const uint32_t* codes, int T, float* out) {
     ok(cudaGetLastError());
     if (tc) {
       DRC(proj(&L.to, 1, EPI_STORE, D.ao, A, D.tmp, H, nullptr, xb));
-      scale_add(D.tmp, L.attn_scale);
+      pending = L.attn_scale;
     } else {
       plain(D.ao, A, L.wo, H, D.x, nullptr, 2, L.attn_scale);
     }
-    ok(rms(D, D.x, T, H, L.post_norm, D.xn, xa));
+    ok(rms(D, D.x, T, H, L.post_norm, D.xn, xa, pending ? D.tmp : nullptr, pending));
+    pending = nullptr;
     if (tc) {
       const Q4Mat gu[2] = {L.tg, L.tu};  // silu(gate) * up in the projection's epilogue
       DRC(proj(gu, 2, EPI_SWIGLU, D.xn, H, D.h, I, nullptr, xa, xb));
       DRC(proj(&L.td, 1, EPI_STORE, D.h, I, D.tmp, H, nullptr, xb));
-      scale_add(D.tmp, L.mlp_scale);
+      pending = L.mlp_scale;
     } else {
       plain(D.xn, H, L.wgu, 2 * I, D.gu, nullptr, 0, nullptr);
       const long n = (long)T * I;
@@ -692,7 +694,7 @@ int decode_dev(Decoder& D, const uint32_t* codes, int T, float* out) {
       plain(D.h, I, L.wdown, H, D.x, nullptr, 2, L.mlp_scale);
     }
   }
-  ok(rms(D, D.x, T, H, D.norm, D.xn));
+  ok(rms(D, D.x, T, H, D.norm, D.xn, nullptr, pending ? D.tmp : nullptr, pending));
   {
     DecGemm t = g;  // channel-first output [1024][T]
     t.A = D.xn; t.lda = H; t.M = T; t.K = H; t.N = 1024; t.B = D.out_w; t.bias = D.out_b;
