@@ -6,8 +6,10 @@ restatement, on the synthetic full-size decoder.
 Bar: the transformer output [1024][T] within DEC_TOL of its largest
 magnitude (f32 arithmetic throughout; the GPU's GEMMs sum in tiles with
 FMAs and its RMSNorm reduces in a tree, so the last bits differ from the
-reference's sequential sums).  Frame counts cover one frame, fewer frames
-than the 72-frame attention window, the window edge and several windows.
+reference's sequential sums; above 15 frames the layer projections run on
+the tensor cores from an fp16 hi/lo split of the f32 weights, ~22 bits).
+Frame counts cover one frame, fewer frames than the 72-frame attention
+window, the window edge, several windows, and each path boundary.
 """
 import numpy as np
 import pytest
@@ -44,8 +46,11 @@ def _rel(a, b):
     return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
 
 
-@pytest.mark.parametrize("T", [1, 5, 72, 73, 150])
+@pytest.mark.parametrize("T", [1, 5, 15, 16, 40, 72, 73, 150, 257])
 def test_decode_latent_matches_oracle(qtts, gpu_dec, orc_dec, T):
+    # 1-15 frames: CUDA-core GEMMs; from 16 the layer projections on the
+    # tensor cores (16-64: one-pass instance with in-kernel row split; above
+    # 64: rows split by their producers; 257: a ragged third row block)
     from qtts_b200 import workload as W
     codes = W.decoder_codes(T, seed=700 + T)
     got = gpu_dec.decode_latent(codes)
