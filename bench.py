@@ -440,10 +440,11 @@ def decoder_launches(T, layers=DEC_LAYERS):
     row-split kernel above 64 frames) and per layer 2 RMSNorms (which also
     apply the scaled residuals), RoPE, attention, q|k|v, o, gate|up and down
     (the layer projections' rows come split from their producers); the final
-    RMSNorm and output GEMM."""
+    RMSNorm, the output projection and (tensor cores) its transpose to
+    channel-first."""
     if T < 16:
         return 1 + 2 + 1 + 1 + layers * 9 + 2
-    return 1 + 2 + 1 + (2 if T > 64 else 1) + layers * 8 + 2
+    return 1 + 2 + 1 + (2 if T > 64 else 1) + layers * 8 + 3
 
 
 def run_decoder(args, rank, world, local, Q, W, torch):

@@ -61,6 +61,11 @@ struct DecGemm {
   long ldc;
   int mode;   // 0: C = acc; 1: C += acc; 2: C += acc * scale[n]
   int trans;  // store at C[n * ldc + m]
+  // with mode 1 and N = 512: the finished rows also as the causal 3-tap
+  // conv's split operand rows (K 1536): row m into rows m + 2 - j at columns
+  // j * 512 + n, the taps before frame 0 as zeros
+  uint8_t* conv_xs;
+  int* err;
 };
 
 // One 64 x 64 output tile per CTA, 4 x 4 per thread.  K runs in 32-deep
@@ -146,6 +151,18 @@ __global__ void __launch_bounds__(kGemmThreads) dec_gemm_kernel(const DecGemm g)
       if (g.mode == 0) *c = acc[i][j];
       else if (g.mode == 1) *c += acc[i][j];
       else *c += acc[i][j] * g.scale[n];
+      if (g.conv_xs) {
+        const float v = *c;
+#pragma unroll
+        for (int tap = 0; tap < 3; ++tap)
+          if (m + 2 - tap < g.M) xs_store1(g.conv_xs, 3 * 512, m + 2 - tap, tap * 512 + n, v);
+        if (m == 0) {  // frame 0 sees no frames before it, frame 1 one
+          xs_store1(g.conv_xs, 3 * 512, 0, n, 0.0f);
+          xs_store1(g.conv_xs, 3 * 512, 0, 512 + n, 0.0f);
+          if (g.M > 1) xs_store1(g.conv_xs, 3 * 512, 1, n, 0.0f);
+        }
+        if (fabsf(v) > 65504.0f) atomicOr(g.err, kErrFp16Input);
+      }
     }
   }
 }
@@ -327,6 +344,21 @@ size_t attn_smem(int window) {
           (size_t)kAttnFrames * 64) * sizeof(float);
 }
 
+// [T][n] -> [n][T] (the channel-first result), through a 32 x 33 tile
+__global__ void dec_transpose_kernel(const float* in, int T, int n, float* out) {
+  __shared__ float tile[32][33];
+  const int c0 = blockIdx.x * 32, t0 = blockIdx.y * 32;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int t = t0 + r, c = c0 + threadIdx.x;
+    if (t < T && c < n) tile[r][threadIdx.x] = in[(size_t)t * n + c];
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int c = c0 + r, t = t0 + threadIdx.x;
+    if (t < T && c < n) out[(size_t)c * T + t] = tile[threadIdx.x][r];
+  }
+}
+
 // the MLP's silu(gate) * up (decoder.rs:307-311) on a gate|up row
 __global__ void dec_swiglu_kernel(const float* GU, int T, int I, float* Hout) {
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -364,6 +396,7 @@ struct Decoder {
   std::vector<DecLayerDev> layers;
   bool tc = false;  // the layer projections run on the tensor cores (T >= kTcMinRows)
   Q4Mat tin;        // input projection tiles
+  Q4Mat tpre, tout; // pre-conv ([tap][in] x out) and output projection tiles
   // grow-only scratch for T frames
   int cap_T = 0;
   float *E0 = nullptr, *S = nullptr, *vq = nullptr, *pre = nullptr, *x = nullptr, *xn = nullptr, *qkv = nullptr,
@@ -557,6 +590,8 @@ int decoder_load(const char* path, int device, Decoder* D) {
       return (int)QTTS_OK;
     };
     DRC(expand(D->in_w, 1024, (uint32_t)H, (long)H, 0, &D->tin));
+    DRC(expand(D->pre_w, 3 * 512, 1024, 1024, 0, &D->tpre));
+    DRC(expand(D->out_w, (uint32_t)H, 1024, 1024, 0, &D->tout));
     for (DecLayerDev& L : D->layers) {
       DRC(expand(L.wqkv, (uint32_t)H, (uint32_t)(3 * A), (long)(3 * A), 0, &L.tqkv));
       DRC(expand(L.wo, (uint32_t)A, (uint32_t)H, (long)H, 0, &L.to));
@@ -583,7 +618,8 @@ int ensure_scratch(Decoder& D, int T) {
   const size_t H = D.hidden, A = (size_t)D.heads * D.head_dim, I = D.inter, cb = D.cb_dim;
   const size_t per = 2 * cb + 512 + 1024 + 2 * H + 3 * A + A + 2 * I + I + H;
   if (D.tc) {  // the largest K of the tensor-core projections: 1024 (input, o) or the MLP width (down)
-    D.xs_bytes = tc_xsplit_scratch_bytes(T, (int)std::max<size_t>(std::max<size_t>(1024, A), I));
+    // the largest K of the tensor-core projections: the pre-conv's 3 x 512
+    D.xs_bytes = tc_xsplit_scratch_bytes(T, (int)std::max<size_t>(std::max<size_t>(3 * 512, A), I));
     if (cudaMalloc(reinterpret_cast<void**>(&D.xs), D.xs_bytes) != cudaSuccess ||
         cudaMalloc(reinterpret_cast<void**>(&D.xs2a), D.xs_bytes) != cudaSuccess ||
         cudaMalloc(reinterpret_cast<void**>(&D.xs2b), D.xs_bytes) != cudaSuccess)
@@ -628,16 +664,9 @@ int decode_dev(Decoder& D, const uint32_t* codes, int T, float* out) {
     t.C = C; t.ldc = N; t.mode = mode; t.trans = 0;
     ok(gemm(D.st, t));
   };
-  plain(D.E0, cb, D.proj0, 512, D.vq, nullptr, 0, nullptr);
-  plain(D.S, cb, D.proj_rest, 512, D.vq, nullptr, 1, nullptr);
-  {
-    DecGemm t = g;  // causal conv: 3 taps of 512 input channels
-    t.A = D.vq; t.lda = 512; t.M = T; t.K = 3 * 512; t.N = 1024; t.taps = 3; t.cin = 512;
-    t.B = D.pre_w; t.bias = D.pre_b; t.C = D.pre; t.ldc = 1024; t.mode = 0;
-    ok(gemm(D.st, t));
-  }
-  // the layer projections on the tensor cores from T >= 16 frames (the
-  // projection kernel's smallest row block); the rest stays on the CUDA cores
+  // the pre-conv and every projection from the input projection on run on
+  // the tensor cores from T >= 16 frames (the projection kernel's smallest
+  // row block); the codebook projections stay on the CUDA cores
   const bool tc = D.tc && T >= kTcMinRows;
   int* tc_err = reinterpret_cast<int*>(D.err);
   auto proj = [&](const Q4Mat* mats, int nmat, int epi, const float* X, int ldx, float* C, int ldo,
@@ -645,6 +674,22 @@ int decode_dev(Decoder& D, const uint32_t* codes, int T, float* out) {
     return tc_project_expanded(mats, nmat, epi, X, ldx, T, C, ldo, bias, D.xs, D.xs_bytes, pre, xs_out, tc_err,
                                D.st);
   };
+  plain(D.E0, cb, D.proj0, 512, D.vq, nullptr, 0, nullptr);
+  if (tc) {
+    // the finished codebook rows go out as the causal conv's split operand
+    // rows (3 taps of 512), and the conv is a tensor-core projection
+    DecGemm t = g;
+    t.A = D.S; t.lda = cb; t.M = T; t.K = cb; t.N = 512; t.B = D.proj_rest; t.C = D.vq; t.ldc = 512; t.mode = 1;
+    t.conv_xs = D.xs2a; t.err = tc_err;
+    ok(gemm(D.st, t));
+    DRC(proj(&D.tpre, 1, EPI_STORE, D.vq, 3 * 512, D.pre, 1024, D.pre_b, D.xs2a));
+  } else {
+    plain(D.S, cb, D.proj_rest, 512, D.vq, nullptr, 1, nullptr);
+    DecGemm t = g;  // causal conv: 3 taps of 512 input channels
+    t.A = D.vq; t.lda = 512; t.M = T; t.K = 3 * 512; t.N = 1024; t.taps = 3; t.cin = 512;
+    t.B = D.pre_w; t.bias = D.pre_b; t.C = D.pre; t.ldc = 1024; t.mode = 0;
+    ok(gemm(D.st, t));
+  }
   // above 64 frames every layer projection takes its rows split by their
   // producer (RMSNorm, attention, the gate|up epilogue) from one of two
   // buffers that alternate, instead of a split launch of its own
@@ -694,8 +739,13 @@ int decode_dev(Decoder& D, const uint32_t* codes, int T, float* out) {
       plain(D.h, I, L.wdown, H, D.x, nullptr, 2, L.mlp_scale);
     }
   }
-  ok(rms(D, D.x, T, H, D.norm, D.xn, nullptr, pending ? D.tmp : nullptr, pending));
-  {
+  ok(rms(D, D.x, T, H, D.norm, D.xn, xa, pending ? D.tmp : nullptr, pending));
+  if (tc) {  // frame-major into the free pre-conv buffer, then channel-first [1024][T]
+    DRC(proj(&D.tout, 1, EPI_STORE, D.xn, H, D.pre, 1024, D.out_b, xa));
+    ++g_kernel_launches;
+    dec_transpose_kernel<<<dim3(1024 / 32, (unsigned)((T + 31) / 32)), dim3(32, 8), 0, D.st>>>(D.pre, T, 1024, out);
+    ok(cudaGetLastError());
+  } else {
     DecGemm t = g;  // channel-first output [1024][T]
     t.A = D.xn; t.lda = H; t.M = T; t.K = H; t.N = 1024; t.B = D.out_w; t.bias = D.out_b;
     t.C = out; t.ldc = T; t.mode = 0; t.trans = 1;
