@@ -260,13 +260,14 @@ __global__ void dec_rope_kernel(float* QKV, int T, int heads, int hd, const floa
 // order, then lane d accumulates dimensions d and d + 32 over the positions
 // in order.
 constexpr int kAttnFrames = 16;
+constexpr int kAttnWarps = 8;  // frames of a block taken warp by warp
 // floats of the padded K rows, rounded up to a multiple of 4 so that the V
 // rows after them start on a 16-byte boundary
 __host__ __device__ constexpr size_t attn_k_floats(int window) {
   return ((size_t)(kAttnFrames + window - 1) * (64 + 1) + 3) & ~(size_t)3;
 }
 template <int HD>
-__global__ void __launch_bounds__(128) dec_attn_kernel(const float* QKV, int T, int heads, int window, float* out,
+__global__ void __launch_bounds__(kAttnWarps * 32) dec_attn_kernel(const float* QKV, int T, int heads, int window, float* out,
                                                        uint8_t* xs, int* err) {
   static_assert(HD == 64, "two dimensions per lane");
   extern __shared__ float sm[];
@@ -278,8 +279,8 @@ __global__ void __launch_bounds__(128) dec_attn_kernel(const float* QKV, int T, 
   const int rows = kAttnFrames + window - 1;               // the largest joint window
   float* sK = sm;                                         // [rows][HD + 1]
   float* sV = sK + attn_k_floats(window);                 // [rows][HD], 16-byte aligned (float4 stores)
-  float* sP = sV + (size_t)rows * HD;                     // [4][window]
-  float* sQ = sP + 4 * window;                            // [kAttnFrames][HD]: the block's q rows
+  float* sP = sV + (size_t)rows * HD;                     // [kAttnWarps][window]
+  float* sQ = sP + kAttnWarps * window;                   // [kAttnFrames][HD]: the block's q rows
   const long ld = 3L * heads * HD;
   for (int i = threadIdx.x; i < (t1 - t0) * HD; i += blockDim.x)
     sQ[i] = QKV[(size_t)(t0 + i / HD) * ld + (size_t)h * HD + i % HD];
@@ -295,7 +296,7 @@ __global__ void __launch_bounds__(128) dec_attn_kernel(const float* QKV, int T, 
   __syncthreads();
   const float scale = 1.0f / sqrtf((float)HD);
   float* p = sP + warp * window;
-  for (int t = t0 + warp; t < t1; t += 4) {
+  for (int t = t0 + warp; t < t1; t += kAttnWarps) {
     const float* qs = sQ + (size_t)(t - t0) * HD;
     const int start = t + 1 > window ? t + 1 - window : 0, L = t + 1 - start;
     float mx = -INFINITY;
@@ -340,7 +341,7 @@ __global__ void __launch_bounds__(128) dec_attn_kernel(const float* QKV, int T, 
   }
 }
 size_t attn_smem(int window) {
-  return (attn_k_floats(window) + (size_t)(kAttnFrames + window - 1) * 64 + 4 * (size_t)window +
+  return (attn_k_floats(window) + (size_t)(kAttnFrames + window - 1) * 64 + kAttnWarps * (size_t)window +
           (size_t)kAttnFrames * 64) * sizeof(float);
 }
 
@@ -713,7 +714,8 @@ int decode_dev(Decoder& D, const uint32_t* codes, int T, float* out) {
       ok(cudaGetLastError());
     }
     ++g_kernel_launches;
-    dec_attn_kernel<64><<<dim3((unsigned)((T + kAttnFrames - 1) / kAttnFrames), D.heads), 128, attn_smem((int)D.window),
+    dec_attn_kernel<64><<<dim3((unsigned)((T + kAttnFrames - 1) / kAttnFrames), D.heads), kAttnWarps * 32,
+                          attn_smem((int)D.window),
                           D.st>>>(
         D.qkv, T, (int)D.heads, (int)D.window, D.ao, xb, tc_err);
     ok(cudaGetLastError());
