@@ -708,8 +708,7 @@ def roofline_tc(ft, peaks, ms_step, waves, B):
             "note": "tensor pipe executes 3 fp16 MMAs per product (hi/lo split for f32 accuracy); the weights "
                     "arrive as expanded fp16 hi/lo operand tiles (4 B per weight) by bulk copy, and above 64 rows "
                     "the input rows arrive split by the kernel before (the family's time includes those split "
-                    "kernels); the embedding-gather and codec-head launches above 128 rows dequantise Q4 in the "
-                    "kernel"}
+                    "kernels)"}
 
 
 def roofline_dec(ft, peak, peak_kind, ms_frame):

@@ -109,8 +109,8 @@ DLayer mk_layer(char* base, const LOff& o) {
 void gemv_init_attributes();
 void attn_init_attributes();
 
-// For batched decode the layer projections (talker and code predictor) and
-// the predictor's input_proj and group heads are expanded once into the
+// For batched decode the layer projections (talker and code predictor), the
+// codec head and the predictor's input_proj and group heads are expanded once into the
 // tensor-core operand layout (4 bytes per weight: ~6 GB for 1.7B, of the
 // GPU's 180 GB), so those launches copy operand tiles instead of
 // dequantising them; the predictor's are otherwise dequantised 15 times per
@@ -123,6 +123,7 @@ static void expand_weights(Model* m) {
     for (Q4Mat* w : {&L.q, &L.k, &L.v, &L.o, &L.gate, &L.up, &L.down}) mats.push_back(w);
   if (m->has_proj) mats.push_back(&m->input_proj);
   for (auto& w : m->lm) mats.push_back(&w);
+  mats.push_back(&m->codec_head);
   mats.erase(std::remove_if(mats.begin(), mats.end(), [](const Q4Mat* w) { return w->n % 64 != 0; }), mats.end());
   size_t total = 0;
   for (Q4Mat* w : mats) total += (tc_expand_bytes(w->k, w->n) + 255) & ~(size_t)255;

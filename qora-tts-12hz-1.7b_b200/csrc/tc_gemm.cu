@@ -981,7 +981,13 @@ __global__ void __launch_bounds__(512) tc_xsplit_kernel(const GemvDesc d, uint8_
   // producer's sums of squares of the block's rows
   float y[16];
   const bool live = m < d.M;
-  {
+  if (d.emb_idx) {  // gathered Q4 embedding rows (gemv.rs:393-396), as the STORE prologue reads them
+    const uint32_t er = live ? d.emb_idx[(size_t)m * d.emb_idx_stride] : 0u;
+    const uint8_t* prow = d.emb.packed + (size_t)er * (d.emb.n / 2);
+    const __half* srow = d.emb.scales + (size_t)er * (d.emb.n / 32);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) y[j] = (live && kk0 + j < d.k) ? q4_value(prow, srow, kk0 + j) : 0.0f;
+  } else {
     const float* xr = d.X + (size_t)(live ? m : 0) * d.ldx + kk0;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -1021,6 +1027,11 @@ __global__ void __launch_bounds__(512) tc_xsplit_kernel(const GemvDesc d, uint8_
       }
     }
   }
+  if (d.xnorm_out && live) {  // the normed rows the launch also hands on (the codec head's hidden)
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+      if (kk0 + j < d.k) d.xnorm_out[(size_t)m * d.ld_xnorm + kk0 + j] = y[j];
+  }
   float amax = 0.0f;
   uint8_t* hi = out + ((size_t)rb * nks + ks) * (2 * A_BYTES);
 #pragma unroll
@@ -1048,8 +1059,12 @@ size_t tc_xsplit_scratch_bytes(int M, int k) { return tc_xsplit_bytes(M, k); }
 // input rows (the branch of launch_t below): its producer may then write
 // them directly.
 bool tc_takes_split(const GemvDesc& d) {
-  if (!d.tc || !d.xs_buf || d.emb_idx || d.xnorm_out || !d.X || d.M <= TM / 2 ||
-      (reinterpret_cast<uintptr_t>(d.xs_buf) & 15u))
+  // gathered embedding rows: the STORE launches without a norm (input_proj);
+  // normed rows handed on: the STORE launches that keep them (codec head)
+  const bool emb = d.emb_idx != nullptr;
+  if (emb && (d.epi_kind != EPI_STORE || d.gamma || d.xnorm_out)) return false;
+  if (d.xnorm_out && (d.epi_kind != EPI_STORE || !d.gamma)) return false;
+  if (!d.tc || !d.xs_buf || (!emb && !d.X) || d.M <= TM / 2 || (reinterpret_cast<uintptr_t>(d.xs_buf) & 15u))
     return false;
   return tc_xsplit_bytes(d.M, d.k) <= d.xs_bytes;
 }
