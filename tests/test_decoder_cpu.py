@@ -162,3 +162,18 @@ def test_oracle_decoder_rejects_bad_code(oracle_mod, dec_file):
 def test_oracle_decoder_load_needs_a_decoder(oracle_mod, tiny_path):
     with pytest.raises(IOError):
         oracle_mod.Decoder(tiny_path)
+
+
+def test_truncated_decoder_section_rejected(qtts, oracle_mod, dec_file, tmp_path):
+    # cut inside the decoder's transformer weights: the reader walks the
+    # whole section (save.rs:446-552), so the file is refused as the
+    # reference's loader would refuse it, by the library and by the oracle
+    data = open(dec_file, "rb").read()
+    bad = str(tmp_path / "cut.qora-tts")
+    with open(bad, "wb") as f:
+        f.write(data[: len(data) - 60_000_000])
+    with pytest.raises(qtts.QttsError) as e:
+        qtts.file_probe(bad)
+    assert e.value.code == qtts.ERR_FORMAT
+    with pytest.raises(IOError):
+        oracle_mod.Decoder(bad)
